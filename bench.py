@@ -1,0 +1,441 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 2-bit MoE layer (qmoe-rs hot path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Default workload (configs[1] of the benchmark definition): one
+DeepSeek-V2-Lite-shaped MoE layer -- hidden 2048, 64 routed experts, top-6
+softmax gating with renormalised weights, 2 shared experts merged into one
+FFN of width 2816, expert width 1408, SwiGLU -- in decode with a batch of 32
+f32 tokens per GPU.  Expert weights are seeded N(0, 0.02) packed to qmoe-rs's
+2-bit format, the gate is f32 N(0, 0.02), activations f32 N(0, 1).
+
+A step is one forward of the layer over one batch.  The timed region replays
+K steps (CUDA graphs of the forward) back to back between CUDA events, with a
+barrier and a device synchronize on both sides, and takes the max over ranks.
+L2 is kept cold by rotating over 4 independent weight replicas (4 x 144 MB >
+126 MB L2), so every step streams its weights from HBM.
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (ROOT, os.path.join(ROOT, "qmoe-rs_b200", "python")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "MoE-layer tokens/sec at 1/2/4/8 B200; decode HBM GB/s as % of peak"
+UNIT = "tokens/s"
+
+WORKLOAD = dict(
+    name="configs[1]: DeepSeek-V2-Lite MoE layer, decode, 32 f32 tokens/GPU",
+    E=64, k=6, H=2048, I=1408, Is=2816, T=32, norm_topk=True)
+REPLICAS = 4
+KERNELS_PER_FORWARD = 5  # router, permute, gate/up, down, combine
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=1234)
+    return ap.parse_args()
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def read_profile_traffic():
+    """DRAM bytes per launch of the gate/up kernel from the committed ncu
+    summary (a line 'traffic_bytes_per_launch: N'), or None."""
+    path = os.path.join(ROOT, "profiles", "qgemv_gate_up_decode_v2lite_t32.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                break
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}),
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+def make_cfg():
+    from qmoe_b200 import MoEConfig
+    w = WORKLOAD
+    return MoEConfig(w["E"], w["k"], w["H"], w["I"], shared_intermediate_dim=w["Is"],
+                     norm_topk_prob=w["norm_topk"])
+
+
+def synth_weights(seed: int, device: str):
+    from qmoe_b200 import quantize as qz
+    w = WORKLOAD
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def mat(o, i):
+        return qz.quantize_weight(torch.randn(o, i, generator=g, device=device) * 0.02)
+
+    experts = [[mat(w["I"], w["H"]), mat(w["I"], w["H"]), mat(w["H"], w["I"])]
+               for _ in range(w["E"])]
+    shared = [mat(w["Is"], w["H"]), mat(w["Is"], w["H"]), mat(w["H"], w["Is"])]
+    gate_w = torch.randn(w["E"], w["H"], generator=g, device=device) * 0.02
+    return experts, shared, gate_w
+
+
+def algorithmic_gate_up_bytes(idx_np: np.ndarray) -> float:
+    """Bytes the gate/up kernel must move for one forward: packed gate+up rows
+    and scales of every routed expert the batch touches, the shared expert's,
+    the activations read and the SwiGLU outputs written."""
+    w = WORKLOAD
+    touched = len(np.unique(idx_np))
+    per_expert = 2 * (w["I"] * w["H"] // 4) + 2 * 4 * w["I"]
+    shared = 2 * (w["Is"] * w["H"] // 4) + 2 * 4 * w["Is"]
+    acts = 4 * w["T"] * w["H"]
+    h_out = 4 * (w["T"] * w["k"] * w["I"] + w["T"] * w["Is"])
+    return float(touched * per_expert + shared + acts + h_out)
+
+
+def algorithmic_layer_bytes(idx_np: np.ndarray) -> float:
+    w = WORKLOAD
+    touched = len(np.unique(idx_np))
+    per_expert = 3 * w["H"] * w["I"] // 4 + 4 * (2 * w["I"] + w["H"])
+    shared = 3 * w["H"] * w["Is"] // 4 + 4 * (2 * w["Is"] + w["H"])
+    gate = 4 * w["E"] * w["H"]
+    acts = 2 * 4 * w["T"] * w["H"]
+    return float(touched * per_expert + shared + gate + acts)
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle restatement of qmoe-rs's SIMD path)
+# ---------------------------------------------------------------------------
+
+def cpu_layer_inputs(seed: int):
+    experts, shared, gate_w = synth_weights(seed, "cpu")
+    ne = [[(p.numpy().reshape(-1), s.numpy()) for p, s in ex] for ex in experts]
+    ns = [(p.numpy().reshape(-1), s.numpy()) for p, s in shared]
+    return ne, ns, gate_w.numpy()
+
+
+def time_cpu_oracle(ne, ns, gw, nthreads: int, tokens: int, min_seconds: float, seed: int):
+    from oracle import oracle as qo
+    w = WORKLOAD
+    cfg = qo.MoEConfig(w["E"], w["k"], w["H"], w["I"], w["Is"], norm_topk_prob=w["norm_topk"])
+    x = np.random.default_rng(seed).standard_normal((tokens, w["H"])).astype(np.float32)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        qo.layer_forward(cfg, gw, ne, x, shared=ns, nthreads=nthreads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return n * tokens / el, n, el
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+
+def run_reference(args):
+    """qmoe-rs's CPU path on this host: the oracle restatement (qmoe-rs is
+    Rust and cannot be built here), all host threads, token-parallel."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    nthreads = os.cpu_count() or 1
+    ne, ns, gw = cpu_layer_inputs(args.seed)
+    from oracle import oracle as qo
+    w = WORKLOAD
+    cfg = qo.MoEConfig(w["E"], w["k"], w["H"], w["I"], w["Is"], norm_topk_prob=w["norm_topk"])
+    tokens = min(w["T"], nthreads)
+    x = np.random.default_rng(args.seed).standard_normal((tokens, w["H"])).astype(np.float32)
+    t0 = time.perf_counter()
+    qo.layer_forward(cfg, gw, ne, x, shared=ns, nthreads=nthreads)
+    per_step = time.perf_counter() - t0
+    budget = 240.0
+    steps = args.steps
+    warm = args.warmup
+    if (steps + warm) * per_step > budget:
+        steps = max(1, int(budget / per_step) - min(warm, 3))
+        warm = min(warm, 3)
+    for _ in range(warm):
+        qo.layer_forward(cfg, gw, ne, x, shared=ns, nthreads=nthreads)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        qo.layer_forward(cfg, gw, ne, x, shared=ns, nthreads=nthreads)
+    el = time.perf_counter() - t0
+    value = steps * tokens / el
+    sample = (f"{tokens} tokens per step ({nthreads} threads, token-parallel) of the "
+              f"{w['T']}-token batch; {steps} steps timed")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "steps_run": steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * el / steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD["name"], "T": w["T"], "E": w["E"], "top_k": w["k"],
+                   "hidden": w["H"], "intermediate": w["I"], "shared_intermediate": w["Is"]},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "qmoe-rs (Rust nightly + candle) cannot be built here; timed its C "
+                "restatement oracle/qmoe_oracle.c with the same per-token/per-expert loop "
+                "and f32x4 lane structure",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    dist = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(dev))
+    from qmoe_b200 import QMoELayer, default_context
+    ctx = default_context(local)
+    cfg = make_cfg()
+    w = WORKLOAD
+
+    layers, xs = [], []
+    for r in range(REPLICAS):
+        experts, shared, gate_w = synth_weights(args.seed + 1000 * r + 17 * rank, dev)
+        layers.append(QMoELayer(cfg, gate_w, experts, shared=shared, ctx=ctx))
+        del experts, shared
+        g = torch.Generator(device=dev).manual_seed(args.seed + 7 * r + 31 * rank)
+        xs.append(torch.randn(w["T"], w["H"], generator=g, device=dev))
+    outs = [torch.empty_like(x) for x in xs]
+    torch.cuda.synchronize()
+
+    # routing of replica 0 (for the algorithmic byte count)
+    _, idx0, _ = layers[0].forward(xs[0], return_routing=True)
+    idx_np = idx0.cpu().numpy()
+
+    # warm-up (eager), then one CUDA graph per replica
+    for i in range(max(3, args.warmup)):
+        layers[i % REPLICAS].forward(xs[i % REPLICAS])
+    torch.cuda.synchronize()
+    for L in layers:
+        L.reserve(w["T"])
+    stream = torch.cuda.Stream()
+    graphs = []
+    with torch.cuda.stream(stream):
+        for r in range(REPLICAS):
+            layers[r].forward(xs[r])  # warm on the capture stream
+        torch.cuda.current_stream().synchronize()
+        for r in range(REPLICAS):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                outs[r] = layers[r].forward(xs[r])
+            graphs.append(g)
+    torch.cuda.synchronize()
+    for i in range(max(3, args.warmup)):
+        graphs[i % REPLICAS].replay()
+    torch.cuda.synchronize()
+
+    # timed region
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record()
+        for i in range(args.steps):
+            graphs[i % REPLICAS].replay()
+        e1.record()
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    tokens = ws * w["T"] * args.steps
+    value = tokens / (ms_max / 1e3)
+
+    # live kernel timing of the dominant kernel (gate/up), eager, same inputs
+    for L in layers:
+        L.set_profiling(True)
+    stage_ms = {}
+    n_prof = 200
+    for i in range(n_prof):
+        L = layers[i % REPLICAS]
+        L.forward(xs[i % REPLICAS])
+        for k, v in L.stage_times().items():
+            stage_ms.setdefault(k, []).append(v)
+    for L in layers:
+        L.set_profiling(False)
+    stage_avg = {k: float(np.mean(v)) for k, v in stage_ms.items()}
+
+    # end to end through the C ABI with pinned host buffers
+    x_host = xs[0].cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    for _ in range(3):
+        layers[0].forward(x_host, out=out_host)
+    n_e2e = max(20, min(args.steps, 500))
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for i in range(n_e2e):
+        layers[0].forward(x_host, out=out_host)
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / n_e2e
+    e2e = {"value": w["T"] * ws / (e2e_ms / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": 4 * w["T"] * w["H"], "d2h_bytes_per_step": 4 * w["T"] * w["H"],
+           "ms_per_step": e2e_ms}
+
+    if rank == 0:
+        hbm, bf16, peak_kind = load_peaks()
+        gu_bytes = algorithmic_gate_up_bytes(idx_np)
+        gu_ms = stage_avg.get("gate_up", float("nan"))
+        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+        traffic = read_profile_traffic()
+        layer_bytes = algorithmic_layer_bytes(idx_np)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": w["name"], "T_per_gpu": w["T"], "E": w["E"],
+                       "top_k": w["k"], "hidden": w["H"], "intermediate": w["I"],
+                       "shared_intermediate": w["Is"], "activations": "f32",
+                       "parallelism": "replicas" if ws > 1 else "single",
+                       "l2": f"{REPLICAS} rotating weight replicas (> L2)",
+                       "graphs": "one CUDA graph per replica"},
+            "roofline": {"bound": "hbm", "kernel": "qgemv gate/up + SwiGLU",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": peak_kind,
+                         "traffic": traffic, "algorithmic_bytes": gu_bytes,
+                         "kernel_ms": gu_ms},
+            "layer": {"stage_ms": stage_avg, "algorithmic_bytes": layer_bytes,
+                      "achieved_gbs_per_step": layer_bytes / (ms_max / args.steps / 1e3) / 1e9},
+            "e2e": e2e,
+            "gpu_launches": KERNELS_PER_FORWARD * args.steps,
+            "clocks": clk.summary(),
+        }
+        if ws == 1:
+            ne, ns, gw = cpu_layer_inputs(args.seed)
+            v, n, el = time_cpu_oracle(ne, ns, gw, 1, w["T"], 10.0, args.seed)
+            line["cpu_baseline"] = {
+                "value": v, "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": f"{n} x full {w['T']}-token batch on 1 thread, {el:.1f} s "
+                          "(C restatement of qmoe-rs's f32x4 SIMD path)"}
+        print(json.dumps(line), flush=True)
+    for g in graphs:
+        del g
+    graphs.clear()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

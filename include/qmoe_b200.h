@@ -1,0 +1,224 @@
+/*
+ * qmoe_b200.h -- C ABI of the B200 (sm_100a) 2-bit MoE layer.
+ *
+ * Drop-in boundary for qmoe-rs's MoE hot path.  Each entry point names the
+ * qmoe-rs interface it replaces (paths relative to the qmoe-rs project root).
+ * A Rust FFI crate binds these declarations one to one; qmoe-rs's public types
+ * keep their signatures and call through them.
+ *
+ * Conventions
+ *   - Every function returns QMOE_OK (0) or a QMOE_ERR_* code; no C++
+ *     exception crosses the boundary.  qmoe_last_error() gives the calling
+ *     thread's last message.
+ *   - Plain pointers and sizes only.  `ptr_kind` says whether the data
+ *     pointers of one call are host (QMOE_PTR_HOST) or device
+ *     (QMOE_PTR_DEVICE) memory.  Host inputs are copied in and host outputs
+ *     copied back on the context's stream, and the call returns after the
+ *     copy back completes.  Device calls are asynchronous on that stream.
+ *   - Packed weights use qmoe-rs's layout verbatim (quantize.py:7-33,
+ *     src/tensor.rs:16-23): uint8 [out, in/4], four 2-bit codes per byte,
+ *     weight j of each group of four in bits 2j..2j+1, value = code - 1
+ *     (0,1,2,3 -> -1,0,+1,+2), one f32 scale per output row.
+ *   - A context, and the packed tensors and layers made from it, belong to
+ *     one device and one stream; use one per host thread.  Distinct contexts
+ *     are independent and may be used concurrently.
+ */
+#ifndef QMOE_B200_H
+#define QMOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QMOE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define QMOE_API __attribute__((visibility("default")))
+#else
+#define QMOE_API
+#endif
+
+/* status codes */
+#define QMOE_OK 0
+#define QMOE_ERR_INVALID 1     /* bad argument, shape or configuration */
+#define QMOE_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define QMOE_ERR_UNSUPPORTED 3 /* valid for qmoe-rs but not handled here */
+#define QMOE_ERR_NOMEM 4       /* device allocation failed */
+
+/* pointer kinds */
+#define QMOE_PTR_DEVICE 0
+#define QMOE_PTR_HOST 1
+
+/* activation dtypes */
+#define QMOE_DTYPE_F32 0
+#define QMOE_DTYPE_BF16 1
+
+/* scoring functions */
+#define QMOE_SCORING_SOFTMAX 0 /* qmoe-rs semantics (src/moe.rs:64-81) */
+#define QMOE_SCORING_SIGMOID 1 /* DeepSeek-V3 style; not in qmoe-rs */
+
+typedef struct qmoe_ctx qmoe_ctx;
+typedef struct qmoe_packed qmoe_packed;
+typedef struct qmoe_layer qmoe_layer;
+
+/*
+ * MoE layer configuration.  The first four fields are qmoe-rs's MoEConfig
+ * (src/moe.rs:6-11).  The rest extend it; their defaults
+ * (shared_intermediate_dim 0, scoring SOFTMAX, n_group 1, topk_group 1,
+ * norm_topk_prob 0, routed_scaling_factor 1, has_bias 0) reproduce qmoe-rs:
+ * softmax over all experts, first top_k of a stable descending sort by
+ * logit, no renormalisation.
+ */
+typedef struct qmoe_moe_config {
+    int32_t num_experts;
+    int32_t top_k;
+    int32_t hidden_dim;
+    int32_t intermediate_dim;
+    int32_t shared_intermediate_dim; /* merged shared-expert width; 0 = none */
+    int32_t scoring;                 /* QMOE_SCORING_* */
+    int32_t n_group;                 /* expert groups for group-limited top-k */
+    int32_t topk_group;              /* groups kept per token */
+    int32_t norm_topk_prob;          /* renormalise the top_k weights */
+    float routed_scaling_factor;     /* multiplies the routed weights */
+    int32_t has_bias;                /* per-expert selection bias (sigmoid) */
+    int32_t reserved;                /* must be 0 */
+} qmoe_moe_config;
+
+/* One expert's three packed projections (qmoe-rs PackedExpert,
+ * src/moe.rs:15-19).  gate/up are [I, H/4] bytes + [I] scales; down is
+ * [H, I/4] bytes + [H] scales.  The same struct carries the shared expert
+ * (src/model.rs:318-322) with I = shared_intermediate_dim. */
+typedef struct qmoe_expert_weights {
+    const uint8_t *gate_packed;
+    const float *gate_scales;
+    const uint8_t *up_packed;
+    const float *up_scales;
+    const uint8_t *down_packed;
+    const float *down_scales;
+} qmoe_expert_weights;
+
+/* ---- library --------------------------------------------------------- */
+
+/* Last error message of the calling thread ("" if none). */
+QMOE_API const char *qmoe_last_error(void);
+
+/* QMOE_ABI_VERSION of the loaded library. */
+QMOE_API int qmoe_abi_version(void);
+
+/* ---- context ---------------------------------------------------------- */
+
+/* Bind to CUDA device `device` and stream `stream` (a cudaStream_t; NULL =
+ * the legacy default stream).  Fails with QMOE_ERR_UNSUPPORTED unless the
+ * device is compute capability 10.0 (B200). */
+QMOE_API int qmoe_ctx_create(int device, void *stream, qmoe_ctx **out);
+QMOE_API int qmoe_ctx_destroy(qmoe_ctx *ctx);
+/* Replace the stream later calls run on. */
+QMOE_API int qmoe_ctx_set_stream(qmoe_ctx *ctx, void *stream);
+/* Block until the context's stream is idle; reports asynchronous errors. */
+QMOE_API int qmoe_ctx_synchronize(qmoe_ctx *ctx);
+
+/* ---- packed tensor: PackedQMoETensor (src/tensor.rs:16-121) ------------ */
+
+/* PackedQMoETensor::from_bytes (src/tensor.rs:47-53) and the data half of
+ * ::mmap_from_file (:27-43): copy `packed` ([out_features, in_features/4]
+ * bytes) and `scales` ([out_features] f32) to device memory owned by the
+ * returned handle.  in_features must be a positive multiple of 64 (rows of
+ * a multiple of 16 bytes, the width of one 128-bit load). */
+QMOE_API int qmoe_packed_create(qmoe_ctx *ctx, const uint8_t *packed, const float *scales,
+                       int64_t out_features, int64_t in_features, int ptr_kind,
+                       qmoe_packed **out);
+QMOE_API int qmoe_packed_destroy(qmoe_packed *t);
+/* Shape of the handle: PackedQMoETensor.shape (src/tensor.rs:20). */
+QMOE_API int qmoe_packed_shape(const qmoe_packed *t, int64_t *out_features,
+                      int64_t *in_features);
+
+/* PackedQMoETensor::forward_simd / forward_simd_raw (src/tensor.rs:64-95,
+ * :99-121): y[b, o] = scale[o] * sum_k (code[o,k] - 1) * x[b, k] for
+ * x [batch, in_features] f32, y [batch, out_features] f32. */
+QMOE_API int qmoe_packed_forward(qmoe_packed *t, const float *x, int64_t batch, float *y,
+                        int ptr_kind);
+
+/* ---- MoE layer: QMoELayer (src/moe.rs:23-130) + SharedExpert ----------- */
+
+/*
+ * QMoELayer::new (src/moe.rs:31-37) plus the layer's optional SharedExpert
+ * (src/model.rs:318-348).
+ *   gate_weight  [num_experts, hidden_dim] f32 (QMoELayer.gate_weight)
+ *   bias         [num_experts] f32 selection bias, or NULL (has_bias = 0)
+ *   experts      expert_count entries: experts expert_begin ..
+ *                expert_begin + expert_count - 1 (QMoELayer.experts).
+ *                A single-process layer passes expert_begin = 0 and
+ *                expert_count = num_experts; an expert-parallel rank passes
+ *                the contiguous range it owns.
+ *   shared       the shared expert, or NULL
+ * All weight pointers are of `ptr_kind`; they are copied, not retained.
+ */
+QMOE_API int qmoe_layer_create(qmoe_ctx *ctx, const qmoe_moe_config *cfg,
+                      const float *gate_weight, const float *bias,
+                      const qmoe_expert_weights *experts, int32_t expert_begin,
+                      int32_t expert_count, const qmoe_expert_weights *shared,
+                      int ptr_kind, qmoe_layer **out);
+QMOE_API int qmoe_layer_destroy(qmoe_layer *layer);
+
+/* Pre-allocate the layer's device scratch for up to max_tokens tokens per
+ * call, so later forwards allocate nothing (required before capturing a
+ * forward into a CUDA graph).  Forwards grow the scratch on demand. */
+QMOE_API int qmoe_layer_reserve(qmoe_layer *layer, int64_t max_tokens);
+
+/*
+ * The MoE block of a decoder layer without the residual: QMoELayer::forward
+ * (src/moe.rs:40-130) followed by `moe_out + SharedExpert::forward`
+ * (src/model.rs:386-389, :407-410).
+ *   x        [T, hidden_dim], dtype QMOE_DTYPE_F32 or QMOE_DTYPE_BF16
+ *   out      [T, hidden_dim], same dtype as x
+ *   topk_idx optional [T, top_k] int32: selected experts, selection order
+ *   topk_w   optional [T, top_k] f32: their combine weights
+ * Requires expert_begin = 0 and expert_count = num_experts.
+ */
+QMOE_API int qmoe_layer_forward(qmoe_layer *layer, const void *x, int dtype, int64_t T,
+                       void *out, int32_t *topk_idx, float *topk_w, int ptr_kind);
+
+/* The router alone (src/moe.rs:51-82): gate logits, scoring, top-k and
+ * combine weights for every token.  topk_idx [T, top_k] int32 and
+ * topk_w [T, top_k] f32 are required. */
+QMOE_API int qmoe_layer_route(qmoe_layer *layer, const void *x, int dtype, int64_t T,
+                     int32_t *topk_idx, float *topk_w, int ptr_kind);
+
+/*
+ * Routed experts for rows whose routing is already known (the expert half of
+ * src/moe.rs:84-129, run by an expert-parallel rank on the rows it
+ * received).  topk_idx [R, top_k] holds LOCAL expert ids in
+ * 0..expert_count-1, or -1 for a slot this rank does not own; topk_w the
+ * matching weights.  out [R, hidden_dim] = sum over valid slots, in
+ * ascending expert order, of w * expert(x).  No shared expert.
+ */
+QMOE_API int qmoe_layer_forward_routed(qmoe_layer *layer, const void *x, int dtype,
+                              int64_t R, const int32_t *topk_idx,
+                              const float *topk_w, void *out, int ptr_kind);
+
+/* SharedExpert::forward (src/model.rs:325-347) for x [T, hidden_dim];
+ * out [T, hidden_dim] in x's dtype.  With accumulate != 0, adds into out
+ * (the `moe_out + shared_out` of src/model.rs:388). */
+QMOE_API int qmoe_layer_shared_forward(qmoe_layer *layer, const void *x, int dtype,
+                              int64_t T, void *out, int accumulate, int ptr_kind);
+
+/* ---- tracing ----------------------------------------------------------- */
+
+/* Stage timing, the device-side counterpart of the Instant-based breakdown
+ * of qmoe-rs's bench harness (benches/moe_layer.rs:105-195).  While enabled,
+ * each forward records CUDA events on the context's stream around its
+ * stages: 0 router, 1 permute, 2 gate/up + SwiGLU, 3 down, 4 combine. */
+QMOE_API int qmoe_layer_set_profiling(qmoe_layer *layer, int enable);
+/* Waits for the last profiled forward and writes min(capacity, 5) stage
+ * durations in milliseconds to ms; *count receives the number written. */
+QMOE_API int qmoe_layer_stage_times(qmoe_layer *layer, float *ms, int capacity,
+                                    int *count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QMOE_B200_H */

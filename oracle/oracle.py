@@ -114,6 +114,9 @@ def lib():
         L.qo_shared_forward.restype = None
         L.qo_shared_forward.argtypes = [P, P, P, P, P, P, i64, i64, P, i64, P,
                                         ctypes.c_int, ctypes.c_int]
+        L.qo_experts_forward.restype = None
+        L.qo_experts_forward.argtypes = [ctypes.POINTER(QoConfig), P, P, P, i64, P, P, P,
+                                         ctypes.c_int]
         L.qo_dequantize.restype = None
         L.qo_dequantize.argtypes = [P, P, i64, i64, P]
         _lib = L
@@ -246,6 +249,22 @@ def moe_forward(cfg: MoEConfig, gate_w, experts, x, bias=None, nthreads: int = 1
         raise ValueError("invalid routing configuration")
     del keep
     return out, idx, w
+
+
+def experts_forward(cfg: MoEConfig, experts, x, idx, w, nthreads: int = 1):
+    """Routed experts for given routing (expert half of src/moe.rs:84-129);
+    idx [R, k] expert ids or -1, w [R, k]."""
+    x = _f32(x)
+    idx = np.ascontiguousarray(idx, dtype=np.int32)
+    w = _f32(w)
+    R = x.shape[0]
+    out = np.empty((R, cfg.hidden_dim), np.float32)
+    pp, sp, keep = _weight_tables(experts)
+    c = cfg.c(False)
+    lib().qo_experts_forward(ctypes.byref(c), pp, sp, _p(x), R, _p(idx), _p(w), _p(out),
+                             nthreads)
+    del keep
+    return out
 
 
 def shared_forward(shared, x, hidden_dim: int, shared_dim: int,

@@ -483,6 +483,56 @@ done:
     return rc;
 }
 
+/* The expert half of src/moe.rs:84-129 for rows whose routing is given:
+ * idx [R, K] holds expert ids in 0..E-1 or -1 (slot skipped), w [R, K] the
+ * weights.  out[r] = sum over valid slots in ascending expert order of
+ * w * expert(x[r]); the per-(row, expert) FFN is the reference's. */
+void qo_experts_forward(const qo_config *cfg, const uint8_t *const *w_packed,
+                        const float *const *w_scales, const float *x, int64_t R,
+                        const int32_t *idx, const float *wts, float *out,
+                        int nthreads)
+{
+    const int64_t K = cfg->top_k, H = cfg->hidden_dim, I = cfg->intermediate_dim;
+    const int rm = cfg->reduce_mode;
+    memset(out, 0, sizeof(float) * (size_t)(R * H));
+#ifdef _OPENMP
+#pragma omp parallel num_threads(nthreads > 1 ? nthreads : 1)
+#endif
+    {
+        float *g = (float *)malloc(sizeof(float) * (size_t)I);
+        float *u = (float *)malloc(sizeof(float) * (size_t)I);
+        float *act = (float *)malloc(sizeof(float) * (size_t)I);
+        float *d = (float *)malloc(sizeof(float) * (size_t)H);
+        int64_t *ord = (int64_t *)malloc(sizeof(int64_t) * (size_t)(K > 0 ? K : 1));
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+        for (int64_t r = 0; r < R; ++r) {
+            int64_t n = 0;
+            for (int64_t j = 0; j < K; ++j) {
+                if (idx[r * K + j] < 0) continue;
+                int64_t b = n - 1;
+                while (b >= 0 && idx[r * K + ord[b]] > idx[r * K + j]) {
+                    ord[b + 1] = ord[b];
+                    --b;
+                }
+                ord[b + 1] = j;
+                ++n;
+            }
+            float *o = out + r * H;
+            for (int64_t q = 0; q < n; ++q) {
+                int64_t e = idx[r * K + ord[q]];
+                float w = wts[r * K + ord[q]];
+                expert_ffn(w_packed[3 * e], w_scales[3 * e], w_packed[3 * e + 1],
+                           w_scales[3 * e + 1], w_packed[3 * e + 2], w_scales[3 * e + 2],
+                           H, I, x + r * H, act, g, u, d, rm);
+                for (int64_t h = 0; h < H; ++h) o[h] = o[h] + d[h] * w;
+            }
+        }
+        free(g); free(u); free(act); free(d); free(ord);
+    }
+}
+
 /* ---------------------------------------------------------------------- */
 /* Shared expert: src/model.rs:325-347 (batched forward_simd over T rows).  */
 /* ---------------------------------------------------------------------- */

@@ -1,0 +1,784 @@
+// api.cu -- the C ABI (include/qmoe_b200.h): contexts, device-resident packed
+// tensors and MoE layers, and the launch sequence of a forward.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "../../include/qmoe_b200.h"
+#include "kernels.h"
+
+using namespace qmoe;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define QTRY_CUDA(call)                                                            \
+    do {                                                                           \
+        cudaError_t e_ = (call);                                                   \
+        if (e_ != cudaSuccess)                                                     \
+            return fail(e_ == cudaErrorMemoryAllocation ? QMOE_ERR_NOMEM           \
+                                                        : QMOE_ERR_CUDA,           \
+                        "%s failed: %s", #call, cudaGetErrorString(e_));          \
+    } while (0)
+
+#define QTRY(call)                \
+    do {                          \
+        int r_ = (call);          \
+        if (r_ != QMOE_OK) return r_; \
+    } while (0)
+
+// Scoped switch to a context's device.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t n = 0;
+    template <class T> T *as() const { return static_cast<T *>(p); }
+};
+
+int grow(DevBuf &b, size_t bytes) {
+    if (bytes <= b.n) return QMOE_OK;
+    if (b.p) cudaFree(b.p);
+    b.p = nullptr;
+    b.n = 0;
+    size_t n = bytes < 256 ? 256 : bytes;
+    QTRY_CUDA(cudaMalloc(&b.p, n));
+    b.n = n;
+    return QMOE_OK;
+}
+
+void release(DevBuf &b) {
+    if (b.p) cudaFree(b.p);
+    b.p = nullptr;
+    b.n = 0;
+}
+
+cudaMemcpyKind kind_in(int ptr_kind) {
+    return ptr_kind == QMOE_PTR_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+}
+
+int check_ptr_kind(int k) {
+    if (k != QMOE_PTR_HOST && k != QMOE_PTR_DEVICE)
+        return fail(QMOE_ERR_INVALID, "ptr_kind must be QMOE_PTR_HOST or QMOE_PTR_DEVICE");
+    return QMOE_OK;
+}
+
+int check_dtype(int d) {
+    if (d != QMOE_DTYPE_F32 && d != QMOE_DTYPE_BF16)
+        return fail(QMOE_ERR_INVALID, "dtype must be QMOE_DTYPE_F32 or QMOE_DTYPE_BF16");
+    return QMOE_OK;
+}
+
+size_t dtype_size(int d) { return d == QMOE_DTYPE_F32 ? 4 : 2; }
+
+// Device activations and outputs are read and written with 16-byte vectors.
+int check_align(const void *p, int ptr_kind, const char *name) {
+    if (ptr_kind == QMOE_PTR_DEVICE && p && (reinterpret_cast<uintptr_t>(p) & 15u))
+        return fail(QMOE_ERR_INVALID, "device pointer %s must be 16-byte aligned", name);
+    return QMOE_OK;
+}
+
+constexpr int kDecodeTok = 5;   // tokens per work item of the decode kernels
+
+}  // namespace
+
+struct qmoe_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+};
+
+struct qmoe_packed {
+    qmoe_ctx *ctx = nullptr;
+    int64_t out_f = 0, in_f = 0;
+    uint8_t *w = nullptr;
+    float *s = nullptr;
+    DevBuf groups, ngroups, x, y;
+    int grid = 0;
+};
+
+struct qmoe_layer {
+    qmoe_ctx *ctx = nullptr;
+    qmoe_moe_config cfg{};
+    int e_begin = 0, e_count = 0;
+    bool has_shared = false;
+    float *gate_w = nullptr, *bias = nullptr;
+    uint8_t *w[3] = {nullptr, nullptr, nullptr};
+    float *s[3] = {nullptr, nullptr, nullptr};
+    uint8_t *ws[3] = {nullptr, nullptr, nullptr};
+    float *ss[3] = {nullptr, nullptr, nullptr};
+    int grid0 = 0, grid1 = 0;
+    // scratch
+    int64_t cap = -1;
+    DevBuf topk_idx, topk_w, assign_pos, pos_tok, seg_off, groups, ngroups, h, y;
+    DevBuf x_in, io_out, user_idx, user_w;
+    // tracing
+    bool profiling = false;
+    cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+};
+
+namespace {
+constexpr int kStages = 5;
+inline void mark(qmoe_layer *L, int i) {
+    if (L->profiling) cudaEventRecord(L->ev[i], L->ctx->stream);
+}
+}  // namespace
+
+extern "C" {
+
+const char *qmoe_last_error(void) { return g_err.c_str(); }
+
+int qmoe_abi_version(void) { return QMOE_ABI_VERSION; }
+
+int qmoe_ctx_create(int device, void *stream, qmoe_ctx **out) {
+    if (!out) return fail(QMOE_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    int n = 0;
+    QTRY_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n)
+        return fail(QMOE_ERR_INVALID, "device %d out of range (%d devices)", device, n);
+    cudaDeviceProp prop;
+    QTRY_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(QMOE_ERR_UNSUPPORTED,
+                    "device %d is sm_%d%d; this library is built for sm_100a (B200)",
+                    device, prop.major, prop.minor);
+    qmoe_ctx *c = new (std::nothrow) qmoe_ctx;
+    if (!c) return fail(QMOE_ERR_NOMEM, "host allocation failed");
+    c->device = device;
+    c->stream = static_cast<cudaStream_t>(stream);
+    *out = c;
+    return QMOE_OK;
+}
+
+int qmoe_ctx_destroy(qmoe_ctx *ctx) {
+    delete ctx;
+    return QMOE_OK;
+}
+
+int qmoe_ctx_set_stream(qmoe_ctx *ctx, void *stream) {
+    if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
+    ctx->stream = static_cast<cudaStream_t>(stream);
+    return QMOE_OK;
+}
+
+int qmoe_ctx_synchronize(qmoe_ctx *ctx) {
+    if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
+    DeviceGuard g(ctx->device);
+    QTRY_CUDA(cudaStreamSynchronize(ctx->stream));
+    return QMOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// packed tensor
+// ---------------------------------------------------------------------------
+
+int qmoe_packed_create(qmoe_ctx *ctx, const uint8_t *packed, const float *scales,
+                       int64_t out_features, int64_t in_features, int ptr_kind,
+                       qmoe_packed **out) {
+    if (!ctx || !packed || !scales || !out) return fail(QMOE_ERR_INVALID, "NULL argument");
+    QTRY(check_ptr_kind(ptr_kind));
+    *out = nullptr;
+    if (out_features <= 0 || in_features <= 0 || in_features % 64 != 0)
+        return fail(QMOE_ERR_INVALID,
+                    "shape (%lld, %lld): out_features must be > 0 and in_features a "
+                    "positive multiple of 64",
+                    (long long)out_features, (long long)in_features);
+    if (in_features > (1 << 20) || out_features > (1LL << 31))
+        return fail(QMOE_ERR_UNSUPPORTED, "shape too large");
+    DeviceGuard g(ctx->device);
+    qmoe_packed *t = new (std::nothrow) qmoe_packed;
+    if (!t) return fail(QMOE_ERR_NOMEM, "host allocation failed");
+    t->ctx = ctx;
+    t->out_f = out_features;
+    t->in_f = in_features;
+    const size_t wb = (size_t)out_features * (in_features / 4);
+    cudaError_t e = cudaMalloc(&t->w, wb);
+    if (e == cudaSuccess) e = cudaMalloc(&t->s, sizeof(float) * out_features);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(t->w, packed, wb, kind_in(ptr_kind), ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(t->s, scales, sizeof(float) * out_features, kind_in(ptr_kind), ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        qmoe_packed_destroy(t);
+        return fail(e == cudaErrorMemoryAllocation ? QMOE_ERR_NOMEM : QMOE_ERR_CUDA,
+                    "packed upload failed: %s", cudaGetErrorString(e));
+    }
+    t->grid = qgemv_max_grid(1, (int)in_features);
+    *out = t;
+    return QMOE_OK;
+}
+
+int qmoe_packed_destroy(qmoe_packed *t) {
+    if (!t) return QMOE_OK;
+    DeviceGuard g(t->ctx->device);
+    if (t->w) cudaFree(t->w);
+    if (t->s) cudaFree(t->s);
+    release(t->groups);
+    release(t->ngroups);
+    release(t->x);
+    release(t->y);
+    delete t;
+    return QMOE_OK;
+}
+
+int qmoe_packed_shape(const qmoe_packed *t, int64_t *out_features, int64_t *in_features) {
+    if (!t) return fail(QMOE_ERR_INVALID, "tensor is NULL");
+    if (out_features) *out_features = t->out_f;
+    if (in_features) *in_features = t->in_f;
+    return QMOE_OK;
+}
+
+int qmoe_packed_forward(qmoe_packed *t, const float *x, int64_t batch, float *y,
+                        int ptr_kind) {
+    if (!t || (!x && batch > 0) || (!y && batch > 0)) return fail(QMOE_ERR_INVALID, "NULL argument");
+    QTRY(check_ptr_kind(ptr_kind));
+    if (batch < 0) return fail(QMOE_ERR_INVALID, "batch < 0");
+    if (batch == 0) return QMOE_OK;
+    QTRY(check_align(x, ptr_kind, "x"));
+    qmoe_ctx *ctx = t->ctx;
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = ctx->stream;
+    const int64_t ngr = (batch + kDecodeTok - 1) / kDecodeTok;
+    QTRY(grow(t->groups, sizeof(int4) * ngr));
+    QTRY(grow(t->ngroups, sizeof(int32_t) * 4));
+    const float *xd = x;
+    float *yd = y;
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY(grow(t->x, sizeof(float) * batch * t->in_f));
+        QTRY(grow(t->y, sizeof(float) * batch * t->out_f));
+        QTRY_CUDA(cudaMemcpyAsync(t->x.p, x, sizeof(float) * batch * t->in_f,
+                                  cudaMemcpyHostToDevice, st));
+        xd = t->x.as<float>();
+        yd = t->y.as<float>();
+    }
+    // one shared-style segment covering all rows: groups of kDecodeTok rows
+    PermuteParams pp{};
+    pp.topk_idx = nullptr;
+    pp.T = batch;
+    pp.K = 0;
+    pp.e_begin = 0;
+    pp.e_count = 1;
+    pp.chunk = kDecodeTok;
+    pp.with_shared = 1;
+    pp.seg_off = t->ngroups.as<int32_t>() + 2;   // [2..3]: the one segment's offsets
+    pp.assign_pos = nullptr;
+    pp.pos_tok = nullptr;
+    pp.groups = t->groups.as<int4>();
+    pp.n_groups = t->ngroups.as<int32_t>();
+    QTRY_CUDA(launch_permute(pp, st));
+
+    QgemvParams q{};
+    q.groups = t->groups.as<int4>();
+    q.n_groups = t->ngroups.as<int32_t>();
+    q.rows = 0;
+    q.K = (int)t->in_f;
+    q.ws[0] = t->w;
+    q.ss[0] = t->s;
+    q.rows_s = (int)t->out_f;
+    q.K_s = (int)t->in_f;
+    q.act = xd;
+    q.act_dtype = 0;
+    q.act_ld = t->in_f;
+    q.pos_tok = nullptr;
+    q.shared_base = 0;
+    q.out = yd;
+    q.out_ld = t->out_f;
+    QTRY_CUDA(launch_qgemv(1, q, t->grid, st));
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY_CUDA(cudaMemcpyAsync(y, yd, sizeof(float) * batch * t->out_f,
+                                  cudaMemcpyDeviceToHost, st));
+        QTRY_CUDA(cudaStreamSynchronize(st));
+    }
+    return QMOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// layer
+// ---------------------------------------------------------------------------
+
+static int validate_cfg(const qmoe_moe_config *c) {
+    if (!c) return fail(QMOE_ERR_INVALID, "cfg is NULL");
+    if (c->num_experts < 1 || c->top_k < 1 || c->top_k > c->num_experts)
+        return fail(QMOE_ERR_INVALID, "need 1 <= top_k (%d) <= num_experts (%d)",
+                    c->top_k, c->num_experts);
+    if (c->top_k > 64) return fail(QMOE_ERR_UNSUPPORTED, "top_k > 64");
+    if (c->num_experts > 4096) return fail(QMOE_ERR_UNSUPPORTED, "num_experts > 4096");
+    if (c->hidden_dim <= 0 || c->hidden_dim % 64 || c->intermediate_dim <= 0 ||
+        c->intermediate_dim % 64)
+        return fail(QMOE_ERR_INVALID,
+                    "hidden_dim (%d) and intermediate_dim (%d) must be positive multiples of 64",
+                    c->hidden_dim, c->intermediate_dim);
+    if (c->shared_intermediate_dim < 0 || c->shared_intermediate_dim % 64)
+        return fail(QMOE_ERR_INVALID, "shared_intermediate_dim must be 0 or a multiple of 64");
+    if (c->scoring != QMOE_SCORING_SOFTMAX && c->scoring != QMOE_SCORING_SIGMOID)
+        return fail(QMOE_ERR_INVALID, "unknown scoring %d", c->scoring);
+    const int G = c->n_group;
+    if (G < 1 || G > 64 || c->num_experts % G)
+        return fail(QMOE_ERR_INVALID, "n_group (%d) must divide num_experts and be <= 64", G);
+    if (c->topk_group < 1 || c->topk_group > G)
+        return fail(QMOE_ERR_INVALID, "need 1 <= topk_group <= n_group");
+    if (c->top_k > c->topk_group * (c->num_experts / G))
+        return fail(QMOE_ERR_INVALID, "top_k exceeds the experts of the kept groups");
+    if (c->has_bias && c->scoring != QMOE_SCORING_SIGMOID)
+        return fail(QMOE_ERR_INVALID, "a selection bias requires sigmoid scoring");
+    if (c->reserved != 0) return fail(QMOE_ERR_INVALID, "reserved must be 0");
+    return QMOE_OK;
+}
+
+int qmoe_layer_destroy(qmoe_layer *L) {
+    if (!L) return QMOE_OK;
+    DeviceGuard g(L->ctx->device);
+    for (int m = 0; m < 3; ++m) {
+        if (L->w[m]) cudaFree(L->w[m]);
+        if (L->s[m]) cudaFree(L->s[m]);
+        if (L->ws[m]) cudaFree(L->ws[m]);
+        if (L->ss[m]) cudaFree(L->ss[m]);
+    }
+    if (L->gate_w) cudaFree(L->gate_w);
+    if (L->bias) cudaFree(L->bias);
+    for (cudaEvent_t &e : L->ev)
+        if (e) cudaEventDestroy(e);
+    DevBuf *bufs[] = {&L->topk_idx, &L->topk_w, &L->assign_pos, &L->pos_tok,
+                      &L->seg_off, &L->groups, &L->ngroups, &L->h, &L->y,
+                      &L->x_in, &L->io_out, &L->user_idx, &L->user_w};
+    for (DevBuf *b : bufs) release(*b);
+    delete L;
+    return QMOE_OK;
+}
+
+static int layer_alloc_copy(void **dst, const void *src, size_t bytes, int kind,
+                            cudaStream_t st) {
+    QTRY_CUDA(cudaMalloc(dst, bytes));
+    QTRY_CUDA(cudaMemcpyAsync(*dst, src, bytes, kind_in(kind), st));
+    return QMOE_OK;
+}
+
+static int layer_create_impl(qmoe_layer *L, const float *gate_weight, const float *bias,
+                             const qmoe_expert_weights *experts,
+                             const qmoe_expert_weights *shared, int ptr_kind) {
+    const qmoe_moe_config &c = L->cfg;
+    cudaStream_t st = L->ctx->stream;
+    const int64_t E = c.num_experts, H = c.hidden_dim, I = c.intermediate_dim;
+    QTRY(layer_alloc_copy((void **)&L->gate_w, gate_weight, sizeof(float) * E * H, ptr_kind, st));
+    if (c.has_bias)
+        QTRY(layer_alloc_copy((void **)&L->bias, bias, sizeof(float) * E, ptr_kind, st));
+    const int64_t rows[3] = {I, I, H}, kin[3] = {H, H, I};
+    const int64_t El = L->e_count;
+    for (int m = 0; m < 3; ++m) {
+        const size_t wb = (size_t)rows[m] * (kin[m] / 4);
+        QTRY_CUDA(cudaMalloc((void **)&L->w[m], wb * El));
+        QTRY_CUDA(cudaMalloc((void **)&L->s[m], sizeof(float) * rows[m] * El));
+        for (int64_t e = 0; e < El; ++e) {
+            const qmoe_expert_weights &x = experts[e];
+            const uint8_t *pk = m == 0 ? x.gate_packed : m == 1 ? x.up_packed : x.down_packed;
+            const float *sc = m == 0 ? x.gate_scales : m == 1 ? x.up_scales : x.down_scales;
+            if (!pk || !sc) return fail(QMOE_ERR_INVALID, "expert %lld has a NULL weight", (long long)e);
+            QTRY_CUDA(cudaMemcpyAsync(L->w[m] + e * wb, pk, wb, kind_in(ptr_kind), st));
+            QTRY_CUDA(cudaMemcpyAsync(L->s[m] + e * rows[m], sc, sizeof(float) * rows[m],
+                                      kind_in(ptr_kind), st));
+        }
+    }
+    if (L->has_shared) {
+        const int64_t Is = c.shared_intermediate_dim;
+        const int64_t srows[3] = {Is, Is, H}, skin[3] = {H, H, Is};
+        for (int m = 0; m < 3; ++m) {
+            const uint8_t *pk = m == 0 ? shared->gate_packed : m == 1 ? shared->up_packed : shared->down_packed;
+            const float *sc = m == 0 ? shared->gate_scales : m == 1 ? shared->up_scales : shared->down_scales;
+            if (!pk || !sc) return fail(QMOE_ERR_INVALID, "shared expert has a NULL weight");
+            QTRY(layer_alloc_copy((void **)&L->ws[m], pk, (size_t)srows[m] * (skin[m] / 4), ptr_kind, st));
+            QTRY(layer_alloc_copy((void **)&L->ss[m], sc, sizeof(float) * srows[m], ptr_kind, st));
+        }
+    }
+    QTRY_CUDA(cudaStreamSynchronize(st));
+    const int kmax0 = (int)H;
+    const int kmax1 = (int)(c.shared_intermediate_dim > I ? c.shared_intermediate_dim : I);
+    L->grid0 = qgemv_max_grid(0, kmax0);
+    L->grid1 = qgemv_max_grid(1, kmax1);
+    return QMOE_OK;
+}
+
+int qmoe_layer_create(qmoe_ctx *ctx, const qmoe_moe_config *cfg, const float *gate_weight,
+                      const float *bias, const qmoe_expert_weights *experts,
+                      int32_t expert_begin, int32_t expert_count,
+                      const qmoe_expert_weights *shared, int ptr_kind, qmoe_layer **out) {
+    if (!ctx || !out || !gate_weight) return fail(QMOE_ERR_INVALID, "NULL argument");
+    *out = nullptr;
+    QTRY(check_ptr_kind(ptr_kind));
+    QTRY(validate_cfg(cfg));
+    if (cfg->has_bias && !bias) return fail(QMOE_ERR_INVALID, "has_bias set but bias is NULL");
+    if (expert_begin < 0 || expert_count < 1 || expert_begin + expert_count > cfg->num_experts)
+        return fail(QMOE_ERR_INVALID, "expert range [%d, %d) outside [0, %d)", expert_begin,
+                    expert_begin + expert_count, cfg->num_experts);
+    if (expert_count > 768) return fail(QMOE_ERR_UNSUPPORTED, "more than 768 local experts");
+    if (!experts) return fail(QMOE_ERR_INVALID, "experts is NULL");
+    if ((cfg->shared_intermediate_dim > 0) != (shared != nullptr))
+        return fail(QMOE_ERR_INVALID,
+                    "shared must be given exactly when shared_intermediate_dim > 0");
+    DeviceGuard g(ctx->device);
+    qmoe_layer *L = new (std::nothrow) qmoe_layer;
+    if (!L) return fail(QMOE_ERR_NOMEM, "host allocation failed");
+    L->ctx = ctx;
+    L->cfg = *cfg;
+    L->e_begin = expert_begin;
+    L->e_count = expert_count;
+    L->has_shared = shared != nullptr;
+    int rc = layer_create_impl(L, gate_weight, bias, experts, shared, ptr_kind);
+    if (rc != QMOE_OK) {
+        std::string msg = g_err;
+        qmoe_layer_destroy(L);
+        g_err = msg;
+        return rc;
+    }
+    *out = L;
+    return QMOE_OK;
+}
+
+static int layer_reserve(qmoe_layer *L, int64_t T) {
+    if (T <= L->cap) return QMOE_OK;
+    const qmoe_moe_config &c = L->cfg;
+    const int64_t K = c.top_k, H = c.hidden_dim;
+    const int64_t Imax = c.shared_intermediate_dim > c.intermediate_dim ? c.shared_intermediate_dim
+                                                                        : c.intermediate_dim;
+    const int64_t TK = T * K;
+    const int64_t npos = TK + T;                 // routed + shared positions
+    const int64_t ngroups = TK + L->e_count + T + 2;
+    QTRY(grow(L->topk_idx, sizeof(int32_t) * TK));
+    QTRY(grow(L->topk_w, sizeof(float) * TK));
+    QTRY(grow(L->assign_pos, sizeof(int32_t) * TK));
+    QTRY(grow(L->pos_tok, sizeof(int32_t) * (TK + 1)));
+    QTRY(grow(L->seg_off, sizeof(int32_t) * (L->e_count + 1)));
+    QTRY(grow(L->groups, sizeof(int4) * ngroups));
+    QTRY(grow(L->ngroups, sizeof(int32_t) * 2));
+    QTRY(grow(L->h, sizeof(float) * npos * Imax));
+    QTRY(grow(L->y, sizeof(float) * npos * H));
+    L->cap = T;
+    return QMOE_OK;
+}
+
+int qmoe_layer_reserve(qmoe_layer *L, int64_t max_tokens) {
+    if (!L || max_tokens < 0) return fail(QMOE_ERR_INVALID, "bad argument");
+    DeviceGuard g(L->ctx->device);
+    return layer_reserve(L, max_tokens);
+}
+
+// Stage a host input in device memory (device inputs pass through).
+static int stage_in(DevBuf &buf, const void *src, size_t bytes, int ptr_kind,
+                    cudaStream_t st, const void **dev) {
+    if (ptr_kind == QMOE_PTR_DEVICE) {
+        *dev = src;
+        return QMOE_OK;
+    }
+    QTRY(grow(buf, bytes));
+    QTRY_CUDA(cudaMemcpyAsync(buf.p, src, bytes, cudaMemcpyHostToDevice, st));
+    *dev = buf.p;
+    return QMOE_OK;
+}
+
+static int run_router(qmoe_layer *L, const void *xd, int dtype, int64_t T) {
+    const qmoe_moe_config &c = L->cfg;
+    RouterParams rp{};
+    rp.x = xd;
+    rp.dtype = dtype;
+    rp.T = T;
+    rp.H = c.hidden_dim;
+    rp.E = c.num_experts;
+    rp.K = c.top_k;
+    rp.gate_w = L->gate_w;
+    rp.bias = L->bias;
+    rp.scoring = c.scoring;
+    rp.n_group = c.n_group;
+    rp.topk_group = c.topk_group;
+    rp.norm_topk = c.norm_topk_prob;
+    rp.routed_scale = c.routed_scaling_factor;
+    rp.topk_idx = L->topk_idx.as<int32_t>();
+    rp.topk_w = L->topk_w.as<float>();
+    mark(L, 0);
+    QTRY_CUDA(launch_router(rp, L->ctx->stream));
+    return QMOE_OK;
+}
+
+// Experts for routed assignments (topk ids relative to e_begin) plus, when
+// with_shared, the shared expert over all T rows; then the combine.
+static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
+                       const int32_t *topk_idx, const float *topk_w, int e_begin,
+                       bool with_shared, void *outd, int accumulate) {
+    const qmoe_moe_config &c = L->cfg;
+    cudaStream_t st = L->ctx->stream;
+    const int K = c.top_k;
+    const int64_t TK = T * K;
+    const int64_t Imax = c.shared_intermediate_dim > c.intermediate_dim ? c.shared_intermediate_dim
+                                                                        : c.intermediate_dim;
+    PermuteParams pp{};
+    pp.topk_idx = topk_idx;
+    pp.T = T;
+    pp.K = K;
+    pp.e_begin = e_begin;
+    pp.e_count = L->e_count;
+    pp.chunk = kDecodeTok;
+    pp.with_shared = with_shared ? 1 : 0;
+    pp.seg_off = L->seg_off.as<int32_t>();
+    pp.assign_pos = L->assign_pos.as<int32_t>();
+    pp.pos_tok = L->pos_tok.as<int32_t>();
+    pp.groups = L->groups.as<int4>();
+    pp.n_groups = L->ngroups.as<int32_t>();
+    mark(L, 1);
+    QTRY_CUDA(launch_permute(pp, st));
+
+    QgemvParams q{};
+    q.groups = L->groups.as<int4>();
+    q.n_groups = L->ngroups.as<int32_t>();
+    q.w[0] = L->w[0];
+    q.w[1] = L->w[1];
+    q.s[0] = L->s[0];
+    q.s[1] = L->s[1];
+    q.w_stride = (int64_t)c.intermediate_dim * (c.hidden_dim / 4);
+    q.s_stride = c.intermediate_dim;
+    q.rows = c.intermediate_dim;
+    q.K = c.hidden_dim;
+    if (with_shared) {
+        q.ws[0] = L->ws[0];
+        q.ws[1] = L->ws[1];
+        q.ss[0] = L->ss[0];
+        q.ss[1] = L->ss[1];
+        q.rows_s = c.shared_intermediate_dim;
+        q.K_s = c.hidden_dim;
+    }
+    q.act = xd;
+    q.act_dtype = dtype;
+    q.act_ld = c.hidden_dim;
+    q.pos_tok = L->pos_tok.as<int32_t>();
+    q.shared_base = TK;
+    q.out = L->h.as<float>();
+    q.out_ld = Imax;
+    mark(L, 2);
+    QTRY_CUDA(launch_qgemv(0, q, L->grid0, st));
+
+    QgemvParams d{};
+    d.groups = q.groups;
+    d.n_groups = q.n_groups;
+    d.w[0] = L->w[2];
+    d.s[0] = L->s[2];
+    d.w_stride = (int64_t)c.hidden_dim * (c.intermediate_dim / 4);
+    d.s_stride = c.hidden_dim;
+    d.rows = c.hidden_dim;
+    d.K = c.intermediate_dim;
+    if (with_shared) {
+        d.ws[0] = L->ws[2];
+        d.ss[0] = L->ss[2];
+        d.rows_s = c.hidden_dim;
+        d.K_s = c.shared_intermediate_dim;
+    }
+    d.act = L->h.p;
+    d.act_dtype = 0;
+    d.act_ld = Imax;
+    d.pos_tok = nullptr;
+    d.shared_base = TK;
+    d.out = L->y.as<float>();
+    d.out_ld = c.hidden_dim;
+    mark(L, 3);
+    QTRY_CUDA(launch_qgemv(1, d, L->grid1, st));
+
+    CombineParams cp{};
+    cp.y = L->y.as<float>();
+    cp.assign_pos = L->assign_pos.as<int32_t>();
+    cp.topk_idx = topk_idx;
+    cp.topk_w = topk_w;
+    cp.T = T;
+    cp.K = K;
+    cp.H = c.hidden_dim;
+    cp.y_shared = with_shared ? L->y.as<float>() + TK * c.hidden_dim : nullptr;
+    cp.accumulate = accumulate;
+    cp.out = outd;
+    cp.out_dtype = dtype;
+    mark(L, 4);
+    QTRY_CUDA(launch_combine(cp, st));
+    mark(L, 5);
+    return QMOE_OK;
+}
+
+static int finish_out(qmoe_layer *L, void *user, const void *dev, size_t bytes, int ptr_kind) {
+    if (ptr_kind == QMOE_PTR_HOST && bytes)
+        QTRY_CUDA(cudaMemcpyAsync(user, dev, bytes, cudaMemcpyDeviceToHost, L->ctx->stream));
+    return QMOE_OK;
+}
+
+int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
+                       int32_t *topk_idx, float *topk_w, int ptr_kind) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    QTRY(check_ptr_kind(ptr_kind));
+    QTRY(check_dtype(dtype));
+    if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
+    if (T > 0 && (!x || !out)) return fail(QMOE_ERR_INVALID, "NULL x or out");
+    if (L->e_begin != 0 || L->e_count != L->cfg.num_experts)
+        return fail(QMOE_ERR_INVALID,
+                    "qmoe_layer_forward needs all experts local; use the routed entry points");
+    if (T == 0) return QMOE_OK;
+    QTRY(check_align(x, ptr_kind, "x"));
+    QTRY(check_align(out, ptr_kind, "out"));
+    DeviceGuard g(L->ctx->device);
+    cudaStream_t st = L->ctx->stream;
+    QTRY(layer_reserve(L, T));
+    const qmoe_moe_config &c = L->cfg;
+    const size_t xbytes = dtype_size(dtype) * T * c.hidden_dim;
+    const void *xd;
+    QTRY(stage_in(L->x_in, x, xbytes, ptr_kind, st, &xd));
+    void *outd = out;
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY(grow(L->io_out, xbytes));
+        outd = L->io_out.p;
+    }
+    QTRY(run_router(L, xd, dtype, T));
+    QTRY(run_experts(L, xd, dtype, T, L->topk_idx.as<int32_t>(), L->topk_w.as<float>(), 0,
+                     L->has_shared, outd, 0));
+    const size_t kb = sizeof(int32_t) * T * c.top_k;
+    if (topk_idx)
+        QTRY_CUDA(cudaMemcpyAsync(topk_idx, L->topk_idx.p, kb,
+                                  ptr_kind == QMOE_PTR_HOST ? cudaMemcpyDeviceToHost
+                                                            : cudaMemcpyDeviceToDevice, st));
+    if (topk_w)
+        QTRY_CUDA(cudaMemcpyAsync(topk_w, L->topk_w.p, kb,
+                                  ptr_kind == QMOE_PTR_HOST ? cudaMemcpyDeviceToHost
+                                                            : cudaMemcpyDeviceToDevice, st));
+    QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
+    if (ptr_kind == QMOE_PTR_HOST) QTRY_CUDA(cudaStreamSynchronize(st));
+    return QMOE_OK;
+}
+
+int qmoe_layer_route(qmoe_layer *L, const void *x, int dtype, int64_t T, int32_t *topk_idx,
+                     float *topk_w, int ptr_kind) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    QTRY(check_ptr_kind(ptr_kind));
+    QTRY(check_dtype(dtype));
+    if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
+    if (T > 0 && (!x || !topk_idx || !topk_w)) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (T == 0) return QMOE_OK;
+    DeviceGuard g(L->ctx->device);
+    cudaStream_t st = L->ctx->stream;
+    QTRY(layer_reserve(L, T));
+    const qmoe_moe_config &c = L->cfg;
+    const void *xd;
+    QTRY(stage_in(L->x_in, x, dtype_size(dtype) * T * c.hidden_dim, ptr_kind, st, &xd));
+    QTRY(run_router(L, xd, dtype, T));
+    const size_t kb = sizeof(int32_t) * T * c.top_k;
+    const cudaMemcpyKind k = ptr_kind == QMOE_PTR_HOST ? cudaMemcpyDeviceToHost
+                                                       : cudaMemcpyDeviceToDevice;
+    QTRY_CUDA(cudaMemcpyAsync(topk_idx, L->topk_idx.p, kb, k, st));
+    QTRY_CUDA(cudaMemcpyAsync(topk_w, L->topk_w.p, kb, k, st));
+    if (ptr_kind == QMOE_PTR_HOST) QTRY_CUDA(cudaStreamSynchronize(st));
+    return QMOE_OK;
+}
+
+int qmoe_layer_forward_routed(qmoe_layer *L, const void *x, int dtype, int64_t R,
+                              const int32_t *topk_idx, const float *topk_w, void *out,
+                              int ptr_kind) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    QTRY(check_ptr_kind(ptr_kind));
+    QTRY(check_dtype(dtype));
+    if (R < 0) return fail(QMOE_ERR_INVALID, "R < 0");
+    if (R > 0 && (!x || !topk_idx || !topk_w || !out)) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (R == 0) return QMOE_OK;
+    QTRY(check_align(x, ptr_kind, "x"));
+    QTRY(check_align(out, ptr_kind, "out"));
+    DeviceGuard g(L->ctx->device);
+    cudaStream_t st = L->ctx->stream;
+    QTRY(layer_reserve(L, R));
+    const qmoe_moe_config &c = L->cfg;
+    const size_t xbytes = dtype_size(dtype) * R * c.hidden_dim;
+    const size_t kb = sizeof(int32_t) * R * c.top_k;
+    const void *xd, *id, *wd;
+    QTRY(stage_in(L->x_in, x, xbytes, ptr_kind, st, &xd));
+    QTRY(stage_in(L->user_idx, topk_idx, kb, ptr_kind, st, &id));
+    QTRY(stage_in(L->user_w, topk_w, kb, ptr_kind, st, &wd));
+    void *outd = out;
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY(grow(L->io_out, xbytes));
+        outd = L->io_out.p;
+    }
+    QTRY(run_experts(L, xd, dtype, R, static_cast<const int32_t *>(id),
+                     static_cast<const float *>(wd), 0, false, outd, 0));
+    QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
+    if (ptr_kind == QMOE_PTR_HOST) QTRY_CUDA(cudaStreamSynchronize(st));
+    return QMOE_OK;
+}
+
+int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
+                              int accumulate, int ptr_kind) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    QTRY(check_ptr_kind(ptr_kind));
+    QTRY(check_dtype(dtype));
+    if (!L->has_shared) return fail(QMOE_ERR_INVALID, "layer has no shared expert");
+    if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
+    if (T > 0 && (!x || !out)) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (T == 0) return QMOE_OK;
+    QTRY(check_align(x, ptr_kind, "x"));
+    QTRY(check_align(out, ptr_kind, "out"));
+    DeviceGuard g(L->ctx->device);
+    cudaStream_t st = L->ctx->stream;
+    QTRY(layer_reserve(L, T));
+    const qmoe_moe_config &c = L->cfg;
+    const size_t xbytes = dtype_size(dtype) * T * c.hidden_dim;
+    const void *xd;
+    QTRY(stage_in(L->x_in, x, xbytes, ptr_kind, st, &xd));
+    void *outd = out;
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY(grow(L->io_out, xbytes));
+        outd = L->io_out.p;
+        if (accumulate)
+            QTRY_CUDA(cudaMemcpyAsync(outd, out, xbytes, cudaMemcpyHostToDevice, st));
+    }
+    // a shared-only pass: no routed assignments (top_k slots all skipped)
+    qmoe_moe_config saved = L->cfg;
+    L->cfg.top_k = 0;
+    int rc = run_experts(L, xd, dtype, T, nullptr, nullptr, 0, true, outd, accumulate);
+    L->cfg = saved;
+    if (rc != QMOE_OK) return rc;
+    QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
+    if (ptr_kind == QMOE_PTR_HOST) QTRY_CUDA(cudaStreamSynchronize(st));
+    return QMOE_OK;
+}
+
+int qmoe_layer_set_profiling(qmoe_layer *L, int enable) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    DeviceGuard g(L->ctx->device);
+    if (enable && !L->ev[0])
+        for (cudaEvent_t &e : L->ev) QTRY_CUDA(cudaEventCreate(&e));
+    L->profiling = enable != 0;
+    return QMOE_OK;
+}
+
+int qmoe_layer_stage_times(qmoe_layer *L, float *ms, int capacity, int *count) {
+    if (!L || !ms || capacity < 0) return fail(QMOE_ERR_INVALID, "bad argument");
+    if (!L->ev[0]) return fail(QMOE_ERR_INVALID, "profiling was never enabled");
+    DeviceGuard g(L->ctx->device);
+    QTRY_CUDA(cudaEventSynchronize(L->ev[kStages]));
+    const int n = capacity < kStages ? capacity : kStages;
+    for (int i = 0; i < n; ++i) QTRY_CUDA(cudaEventElapsedTime(&ms[i], L->ev[i], L->ev[i + 1]));
+    if (count) *count = n;
+    return QMOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,84 @@
+// common.cuh -- device helpers shared by the qmoe_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#define QMOE_DEV __device__ __forceinline__
+
+namespace qmoe {
+
+constexpr int kGateChunk = 64;  // hidden-dim chunk of the pinned logit order
+
+QMOE_DEV float to_f32(float v) { return v; }
+QMOE_DEV float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Load element k of row `row` of an activation matrix stored as f32 or bf16.
+QMOE_DEV float load_act(const void *base, int dtype, int64_t idx) {
+    if (dtype == 0) return __ldg(reinterpret_cast<const float *>(base) + idx);
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(base)[idx]);
+}
+
+QMOE_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+QMOE_DEV int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Stable-descending-sort precedence: a ranks before b when its value is
+// larger, ties going to the lower index (qmoe-rs src/moe.rs:68-71 sorts an
+// index-ordered list with a stable sort).
+QMOE_DEV bool ranks_before(float va, int ia, float vb, int ib) {
+    return va > vb || (va == vb && ia < ib);
+}
+
+// Exact power of two 2^n for -149 <= n <= 127.
+QMOE_DEV float pow2i(int n) {
+    uint32_t u = n >= -126 ? (uint32_t)(n + 127) << 23 : 1u << (n + 149);
+    return __uint_as_float(u);
+}
+
+// Deterministic exp for sigmoid scoring: Cody & Waite reduction with a
+// two-float ln2, degree-7 Taylor polynomial in Horner form, scaling by 2^n.
+// Every step is one correctly rounded IEEE operation, so the CPU oracle's
+// C version of the same steps returns the same bits.
+QMOE_DEV float qexp(float x) {
+    if (!(x == x)) return x;
+    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+    if (x < -103.97208404541016f) return 0.0f;
+    float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = __fmaf_rn(n, -0.693145751953125f, x);
+    r = __fmaf_rn(n, -1.428606765330187045037746429443359375e-06f, r);
+    float p = 1.98412698412698412698e-4f;
+    p = __fmaf_rn(p, r, 1.38888888888888888889e-3f);
+    p = __fmaf_rn(p, r, 8.33333333333333333333e-3f);
+    p = __fmaf_rn(p, r, 4.16666666666666666667e-2f);
+    p = __fmaf_rn(p, r, 1.66666666666666666667e-1f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    int ni = (int)n;
+    if (ni > 127) return __fmul_rn(__fmul_rn(p, pow2i(127)), pow2i(ni - 127));
+    if (ni < -126) return __fmul_rn(__fmul_rn(p, pow2i(-126)), pow2i(ni + 126));
+    return __fmul_rn(p, pow2i(ni));
+}
+
+QMOE_DEV float qsigmoid(float x) {
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, qexp(-x)));
+}
+
+// SwiGLU exactly as qmoe-rs writes it (src/moe.rs:109-115):
+// (g * (1 / (1 + exp(-g)))) * u, each operation rounded separately.
+QMOE_DEV float swiglu(float g, float u) {
+    float s = __fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
+    return __fmul_rn(s, u);
+}
+
+}  // namespace qmoe

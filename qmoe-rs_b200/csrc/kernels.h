@@ -1,0 +1,92 @@
+// kernels.h -- launch interface of the qmoe_b200 kernels (library-internal).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qmoe {
+
+// ---- router -------------------------------------------------------------
+struct RouterParams {
+    const void *x;          // [T, H] f32 or bf16
+    int dtype;              // 0 f32, 1 bf16
+    int64_t T;
+    int H, E, K;
+    const float *gate_w;    // [E, H]
+    const float *bias;      // [E] or nullptr
+    int scoring;            // 0 softmax, 1 sigmoid
+    int n_group, topk_group;
+    int norm_topk;
+    float routed_scale;
+    int32_t *topk_idx;      // [T, K]
+    float *topk_w;          // [T, K]
+};
+size_t router_smem_bytes(int H, int E);
+cudaError_t launch_router(const RouterParams &p, cudaStream_t s);
+
+// ---- permute ------------------------------------------------------------
+// Builds per-expert segments of routed (token, slot) assignments, stable in
+// token order, and the token-group work list of the grouped kernels.
+struct PermuteParams {
+    const int32_t *topk_idx;   // [T, K]; ids outside [e_begin, e_begin+e_count) skipped
+    int64_t T;
+    int K;
+    int e_begin, e_count;
+    int chunk;                 // tokens per group descriptor
+    int with_shared;           // append groups covering all T tokens (segment e_count)
+    int32_t *seg_off;          // [e_count + 1] routed segment offsets
+    int32_t *assign_pos;       // [T, K] position of each assignment, -1 if skipped
+    int32_t *pos_tok;          // [T*K] token of each routed position
+    int4 *groups;              // (segment, pos_begin, count, 0)
+    int32_t *n_groups;         // [2]: routed groups, shared groups
+};
+size_t permute_smem_bytes(int e_count);
+cudaError_t launch_permute(const PermuteParams &p, cudaStream_t s);
+
+// ---- decode grouped GEMV (int8-limb mma.sync, in-register 2-bit unpack) --
+struct QgemvParams {
+    // work list
+    const int4 *groups;
+    const int32_t *n_groups;     // [0] routed groups, [1] shared groups
+    // routed weights, experts stacked: matrix m at w[m] + seg*w_stride
+    const uint8_t *w[2];
+    const float *s[2];
+    int64_t w_stride;            // bytes per expert matrix
+    int64_t s_stride;            // scales per expert matrix
+    int rows, K;                 // rows per matrix, reduction length
+    // shared segment weights (segment id == n_routed_segs)
+    const uint8_t *ws[2];
+    const float *ss[2];
+    int rows_s, K_s;
+    // activations: rows of f32 or bf16
+    const void *act;
+    int act_dtype;
+    int64_t act_ld;
+    const int32_t *pos_tok;      // routed position -> activation row (nullable)
+    int64_t shared_base;         // first shared position
+    // output rows by position
+    float *out;
+    int64_t out_ld;
+};
+// mode 0: gate+up matrices fused with SwiGLU (128 rows of each per item)
+// mode 1: one matrix (256 rows per item)
+cudaError_t launch_qgemv(int mode, const QgemvParams &p, int grid, cudaStream_t s);
+int qgemv_max_grid(int mode, int K_max);
+size_t qgemv_smem_bytes(int K_max);
+
+// ---- combine -----------------------------------------------------------
+struct CombineParams {
+    const float *y;              // [positions, H] expert outputs
+    const int32_t *assign_pos;   // [T, K]
+    const int32_t *topk_idx;     // [T, K] (expert order of the accumulation)
+    const float *topk_w;         // [T, K]
+    int64_t T;
+    int K, H;
+    const float *y_shared;       // [T, H] or nullptr
+    int accumulate;              // add into out instead of overwriting
+    void *out;                   // [T, H]
+    int out_dtype;
+};
+cudaError_t launch_combine(const CombineParams &p, cudaStream_t s);
+
+}  // namespace qmoe

@@ -1,0 +1,13 @@
+"""qmoe_b200: B200-native (sm_100a) 2-bit MoE layer for qmoe-rs.
+
+The compute lives in lib/libqmoe_b200.so (hand-written CUDA for sm_100a,
+C ABI in include/qmoe_b200.h); this package is the host-side binding.
+"""
+from . import capi
+from .capi import QmoeError
+from .layer import (Context, MoEConfig, PackedExpert, PackedQMoETensor, QMoELayer,
+                    default_context)
+from . import quantize
+
+__all__ = ["capi", "QmoeError", "Context", "MoEConfig", "PackedExpert",
+           "PackedQMoETensor", "QMoELayer", "default_context", "quantize"]

@@ -1,0 +1,271 @@
+"""GPU parity of the CUDA path against the CPU oracle, through the C ABI.
+
+Bars (from the project's parity contract):
+  * routing indices bit-exact (given the pinned logit order);
+  * sigmoid-scored routing weights bit-exact; softmax weights within a few
+    ulp (CUDA expf vs glibc expf);
+  * layer outputs: max-abs relative error <= 1e-4 for f32 activations,
+    <= 2e-2 for bf16 activations (oracle fed the exact bf16 -> f32 upcast).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import helpers
+from helpers import rel_err
+from oracle import oracle as qo
+from qmoe_b200 import MoEConfig, PackedQMoETensor, QMoELayer, QmoeError, capi
+from qmoe_b200 import quantize as qz
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-4
+BF16_TOL = 2e-2
+NTHREADS = max(1, min(8, os.cpu_count() or 1))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(0)
+
+
+def qo_cfg(cfg: MoEConfig) -> qo.MoEConfig:
+    return qo.MoEConfig(cfg.num_experts, cfg.top_k, cfg.hidden_dim, cfg.intermediate_dim,
+                        cfg.shared_intermediate_dim, cfg.scoring, cfg.n_group,
+                        cfg.topk_group, cfg.norm_topk_prob, cfg.routed_scaling_factor)
+
+
+def build(cfg: MoEConfig, seed=1234, bias=None, device="cuda"):
+    experts, shared, gate_w = helpers.synth_layer(
+        cfg.num_experts, cfg.hidden_dim, cfg.intermediate_dim,
+        cfg.shared_intermediate_dim, seed=seed, device=device)
+    layer = QMoELayer(cfg, gate_w, experts, shared=shared, bias=bias)
+    np_exp = helpers.to_numpy_experts(experts)
+    np_sh = helpers.to_numpy_experts([shared])[0] if shared is not None else None
+    return layer, np_exp, np_sh, gate_w.cpu().numpy()
+
+
+def oracle_layer(cfg, gate_w, np_exp, np_sh, x, bias=None):
+    return qo.layer_forward(qo_cfg(cfg), gate_w, np_exp, x, shared=np_sh, bias=bias,
+                            nthreads=NTHREADS)
+
+
+# ---------------------------------------------------------------------------
+# PackedQMoETensor::forward_simd
+# ---------------------------------------------------------------------------
+
+def test_packed_known_answer_on_gpu():
+    # src/simd.rs:57-64 on a 64-wide row: byte 0x58 then 0x55 (all code 1 = 0)
+    row = np.full(16, 0x55, np.uint8)
+    row[0] = 0b01011000
+    x = np.zeros((1, 64), np.float32)
+    x[0, :4] = [2.0, 3.0, 4.0, 5.0]
+    t = PackedQMoETensor.from_bytes(row, (1, 64), np.array([1.5], np.float32))
+    y = t.forward_simd(x)
+    assert abs(float(y[0, 0]) - 1.5) < 1e-5
+
+
+@pytest.mark.parametrize("out_f,in_f,batch", [(24, 64, 1), (300, 1408, 3), (2048, 2048, 7),
+                                              (129, 192, 33), (1408, 2048, 5)])
+def test_packed_forward_matches_oracle(out_f, in_f, batch):
+    rng = np.random.default_rng(out_f * 7 + in_f + batch)
+    packed = rng.integers(0, 256, (out_f, in_f // 4), dtype=np.uint8)  # code 3 included
+    scales = (rng.random(out_f, dtype=np.float32) * 0.05 + 0.01).astype(np.float32)
+    x = rng.standard_normal((batch, in_f)).astype(np.float32)
+    t = PackedQMoETensor.from_bytes(packed, (out_f, in_f), scales)
+    ref = qo.packed_forward(packed, scales, (out_f, in_f), x)
+    y_host = t.forward_simd(x)                        # host pointers
+    y_dev = t.forward_simd(torch.from_numpy(x).cuda())  # device pointers
+    assert rel_err(y_host, ref) <= F32_TOL
+    np.testing.assert_array_equal(y_dev.cpu().numpy(), y_host)
+
+
+def test_packed_forward_ragged_rows_and_large_values():
+    rng = np.random.default_rng(5)
+    out_f, in_f = 37, 256
+    packed = rng.integers(0, 256, (out_f, in_f // 4), dtype=np.uint8)
+    scales = rng.random(out_f, dtype=np.float32) + 0.5
+    x = (rng.standard_normal((11, in_f)) * 1e4).astype(np.float32)
+    x[3] = 0.0                                         # an all-zero row
+    x[4, 7] = 3e30                                     # one huge element
+    t = PackedQMoETensor.from_bytes(packed, (out_f, in_f), scales)
+    y = t.forward_simd(x)
+    ref = qo.packed_forward(packed, scales, (out_f, in_f), x)
+    for b in range(11):
+        assert rel_err(y[b], ref[b]) <= F32_TOL, b
+    assert np.all(y[3] == 0.0)
+
+
+def test_packed_forward_rejects_bad_shapes():
+    with pytest.raises(QmoeError) as ei:
+        PackedQMoETensor.from_bytes(np.zeros((4, 25), np.uint8), (4, 100),
+                                    np.ones(4, np.float32))
+    assert ei.value.code == capi.QMOE_ERR_INVALID
+    t = PackedQMoETensor.from_bytes(np.zeros((4, 16), np.uint8), (4, 64), np.ones(4, np.float32))
+    with pytest.raises(ValueError):
+        t.forward_simd(np.zeros((3, 65), np.float32))
+    assert t.forward_simd(np.zeros((0, 64), np.float32)).shape == (0, 4)
+
+
+# ---------------------------------------------------------------------------
+# QMoELayer::forward (+ shared expert)
+# ---------------------------------------------------------------------------
+
+def test_tiny_fixture_layer_matches_oracle(golden_dir):
+    z = np.load(os.path.join(golden_dir, "moe_tiny.npz"))
+    E, H, I, Is, T = [int(v) for v in z["dims"]]
+    np_exp = [[(z[f"e{e}_{n}_packed"].reshape(-1), z[f"e{e}_{n}_scales"])
+               for n in ("gate", "up", "down")] for e in range(E)]
+    np_sh = [(z[f"shared_{n}_packed"].reshape(-1), z[f"shared_{n}_scales"])
+             for n in ("gate", "up", "down")]
+    cfg = MoEConfig(E, 2, H, I, shared_intermediate_dim=Is)
+    layer = QMoELayer(cfg, z["gate_w"], np_exp, shared=np_sh)
+    out, idx, w = layer.forward(z["x"], return_routing=True)
+    ro, ri, rw = oracle_layer(cfg, z["gate_w"], np_exp, np_sh, z["x"])
+    np.testing.assert_array_equal(idx, ri)
+    np.testing.assert_allclose(w, rw, rtol=1e-6, atol=0)
+    assert rel_err(out, ro) <= F32_TOL
+
+
+@pytest.mark.parametrize("T", [1, 32])
+def test_v2_lite_decode_matches_oracle(T):
+    cfg = MoEConfig(64, 6, 2048, 1408, shared_intermediate_dim=2816, norm_topk_prob=(T == 32))
+    layer, np_exp, np_sh, gw = build(cfg, seed=100 + T)
+    x = torch.randn(T, 2048, generator=torch.Generator().manual_seed(T))
+    out, idx, w = layer.forward(x.cuda(), return_routing=True)
+    ro, ri, rw = oracle_layer(cfg, gw, np_exp, np_sh, x.numpy())
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=1e-6, atol=0)
+    assert rel_err(out.cpu().numpy(), ro) <= F32_TOL
+
+
+def test_host_and_device_pointers_agree_and_are_deterministic():
+    cfg = MoEConfig(8, 2, 256, 128, shared_intermediate_dim=192)
+    layer, *_ = build(cfg, seed=7)
+    x = torch.randn(13, 256, generator=torch.Generator().manual_seed(1))
+    a = layer.forward(x)                       # CPU tensor -> host pointers
+    b = layer.forward(x.cuda()).cpu()
+    c = layer.forward(x.cuda()).cpu()
+    np.testing.assert_array_equal(a.numpy(), b.numpy())
+    np.testing.assert_array_equal(b.numpy(), c.numpy())
+
+
+def test_bf16_activations_within_tolerance():
+    cfg = MoEConfig(16, 4, 512, 256, shared_intermediate_dim=256)
+    layer, np_exp, np_sh, gw = build(cfg, seed=11)
+    x = torch.randn(9, 512, generator=torch.Generator().manual_seed(3)).bfloat16()
+    out, idx, _ = layer.forward(x.cuda(), return_routing=True)
+    assert out.dtype == torch.bfloat16
+    ro, ri, _ = oracle_layer(cfg, gw, np_exp, np_sh, x.float().numpy())
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    assert rel_err(out.float().cpu().numpy(), ro) <= BF16_TOL
+
+
+def test_skewed_routing_long_segments():
+    # every token picks the same experts: segments of T tokens, many groups
+    cfg = MoEConfig(8, 2, 256, 128)
+    experts, _, gate_w = helpers.synth_layer(8, 256, 128, seed=5, device="cuda")
+    gate_w = gate_w.clone()
+    gate_w[3] += 0.5
+    gate_w[6] += 0.4
+    layer = QMoELayer(cfg, gate_w, experts)
+    x = torch.rand(37, 256, generator=torch.Generator().manual_seed(2)) + 0.5
+    out, idx, _ = layer.forward(x.cuda(), return_routing=True)
+    assert set(np.unique(idx.cpu().numpy())) == {3, 6}
+    ro, ri, _ = qo.moe_forward(qo_cfg(cfg), gate_w.cpu().numpy(),
+                               helpers.to_numpy_experts(experts), x.numpy(),
+                               nthreads=NTHREADS)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    assert rel_err(out.cpu().numpy(), ro) <= F32_TOL
+
+
+def test_sigmoid_group_limited_routing_bit_exact():
+    E, G, TG, k = 32, 8, 4, 8
+    cfg = MoEConfig(E, k, 256, 128, scoring=capi.QMOE_SCORING_SIGMOID, n_group=G,
+                    topk_group=TG, norm_topk_prob=True, routed_scaling_factor=2.5)
+    bias = (torch.randn(E, generator=torch.Generator().manual_seed(8)) * 0.05).float()
+    layer, np_exp, _, gw = build(cfg, seed=21, bias=bias.cuda())
+    x = torch.randn(19, 256, generator=torch.Generator().manual_seed(4))
+    out, idx, w = layer.forward(x.cuda(), return_routing=True)
+    ro, ri, rw = qo.moe_forward(qo_cfg(cfg), gw, np_exp, x.numpy(), bias=bias.numpy(),
+                                nthreads=NTHREADS)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_array_equal(w.cpu().numpy(), rw)
+    assert rel_err(out.cpu().numpy(), ro) <= F32_TOL
+
+
+def test_route_only_matches_oracle_bit_exact():
+    cfg = MoEConfig(64, 6, 2048, 128)
+    experts, _, gw = helpers.synth_layer(64, 2048, 128, seed=3, device="cuda")
+    layer = QMoELayer(cfg, gw, experts)
+    x = torch.randn(50, 2048, generator=torch.Generator().manual_seed(9))
+    idx, w = layer.route(x.cuda())
+    logits = qo.gate_logits(x.numpy(), gw.cpu().numpy())
+    ri, rw = qo.route(qo_cfg(cfg), logits)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=1e-6, atol=0)
+
+
+def test_forward_routed_matches_oracle():
+    cfg = MoEConfig(16, 4, 256, 192)
+    experts, _, gw = helpers.synth_layer(16, 256, 192, seed=17, device="cuda")
+    # an expert-parallel rank owning experts 4..11
+    layer = QMoELayer(cfg, gw, experts[4:12], expert_begin=4)
+    rng = np.random.default_rng(0)
+    R = 23
+    idx = np.full((R, 4), -1, np.int32)
+    for r in range(R):
+        sel = rng.choice(8, size=rng.integers(0, 5), replace=False)
+        idx[r, :len(sel)] = sel
+    w = rng.random((R, 4), dtype=np.float32)
+    x = rng.standard_normal((R, 256)).astype(np.float32)
+    out = layer.forward_routed(x, idx, w)
+    np_exp = helpers.to_numpy_experts(experts[4:12])
+    ref = qo.experts_forward(qo.MoEConfig(8, 4, 256, 192), np_exp, x, idx, w)
+    assert rel_err(out, ref) <= F32_TOL
+    assert np.all(out[np.all(idx < 0, axis=1)] == 0.0)
+
+
+def test_shared_forward_and_accumulate():
+    cfg = MoEConfig(4, 1, 128, 64, shared_intermediate_dim=320)
+    layer, _, np_sh, _ = build(cfg, seed=23)
+    x = np.random.default_rng(1).standard_normal((6, 128)).astype(np.float32)
+    ref = qo.shared_forward(np_sh, x, 128, 320)
+    s = layer.shared_forward(x)
+    assert rel_err(s, ref) <= F32_TOL
+    base = np.ones((6, 128), np.float32)
+    acc = layer.shared_forward(x, out=base.copy())
+    assert rel_err(acc - 1.0, ref) <= 1e-4
+
+
+def test_empty_batch_is_a_noop():
+    cfg = MoEConfig(4, 2, 64, 128)
+    layer, *_ = build(cfg, seed=1)
+    out = layer.forward(torch.zeros(0, 64, device="cuda"))
+    assert out.shape == (0, 64)
+
+
+def test_invalid_configs_rejected():
+    experts, _, gw = helpers.synth_layer(4, 64, 128, seed=1, device="cuda")
+    with pytest.raises(QmoeError):
+        QMoELayer(MoEConfig(4, 5, 64, 128), gw, experts)          # top_k > E
+    with pytest.raises(QmoeError):
+        QMoELayer(MoEConfig(4, 2, 64, 128, n_group=3, topk_group=1), gw, experts)
+    with pytest.raises(QmoeError):
+        QMoELayer(MoEConfig(4, 2, 64, 128, shared_intermediate_dim=64), gw, experts)
+
+
+def test_quantizer_on_device_matches_host():
+    w = torch.randn(64, 256, generator=torch.Generator().manual_seed(0)) * 0.02
+    p_cpu, s_cpu = qz.quantize_weight(w)
+    p_gpu, s_gpu = qz.quantize_weight(w.cuda())
+    np.testing.assert_allclose(s_cpu.numpy(), s_gpu.cpu().numpy(), rtol=1e-6)
+    # a scale one ulp apart may move a weight sitting exactly on a rounding
+    # boundary; anything beyond a handful of codes is a real difference
+    c_cpu = qz.unpack_codes(p_cpu, 256).numpy()
+    c_gpu = qz.unpack_codes(p_gpu.cpu(), 256).numpy()
+    assert np.count_nonzero(c_cpu != c_gpu) <= 4
