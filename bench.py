@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the CPU-baseline leg (for profiler runs)")
     return ap.parse_args()
 
 
@@ -413,7 +415,7 @@ def run_ours(args):
             "gpu_launches": KERNELS_PER_FORWARD * args.steps,
             "clocks": clk.summary(),
         }
-        if ws == 1:
+        if ws == 1 and not args.no_cpu_baseline:
             ne, ns, gw = cpu_layer_inputs(args.seed)
             v, n, el = time_cpu_oracle(ne, ns, gw, 1, w["T"], 10.0, args.seed)
             line["cpu_baseline"] = {

@@ -20,6 +20,14 @@ QMOE_DEV float load_act(const void *base, int dtype, int64_t idx) {
     return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(base)[idx]);
 }
 
+// Four consecutive activations (f32 or bf16) starting at a multiple of 4.
+QMOE_DEV float4 load_act4(const void *base, int dtype, int64_t idx) {
+    if (dtype == 0) return __ldg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(base) + idx));
+    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(reinterpret_cast<const __nv_bfloat16 *>(base) + idx));
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+
 QMOE_DEV float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -93,8 +93,6 @@ qgemv_kernel(const QgemvParams p) {
     extern __shared__ __align__(16) uint8_t sm[];
     __shared__ int s_exp[kTok];
     __shared__ long long s_sumq[kTok];
-    __shared__ float s_max[kTok];
-    __shared__ int64_t s_row[kTok];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g8 = lane >> 2, t4 = lane & 3;
@@ -136,85 +134,70 @@ qgemv_kernel(const QgemvParams p) {
             wcur[rg] = (rv[rg] && off < bpr) ? ldg_nc_v4(wr[rg] + off) : make_uint4(0, 0, 0, 0);
         }
 
-        // --- prologue: activation rows of the group -> int8 limbs in smem
-        if (tid < kTok) {
-            s_max[tid] = 0.0f;
-            s_sumq[tid] = 0;
-            int64_t row = 0;
-            if (tid < it.count) {
-                const int64_t pos = it.pos0 + tid;
-                if (p.pos_tok)
-                    row = pos < p.shared_base ? (int64_t)p.pos_tok[pos] : pos - p.shared_base;
-                else
-                    row = pos;
-            }
-            s_row[tid] = row;
-        }
-        __syncthreads();
+        // --- prologue: activation rows of the group -> int8 limbs in smem.
+        //     One warp per token: max |x| and sum(Q) by shuffle reductions.
         const int nblk = Kp >> 4;  // 16-element blocks per row (incl. padding)
-        for (int i = tid; i < it.count * (K >> 2); i += kThreads) {
-            const int c = i / (K >> 2), q = i % (K >> 2);
-            const int64_t base = s_row[c] * p.act_ld + 4 * q;
-            float m;
-            if (p.act_dtype == 0) {
-                const float4 v = __ldg(reinterpret_cast<const float4 *>(
-                    reinterpret_cast<const float *>(p.act) + base));
-                m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-            } else {
-                const __nv_bfloat16 *b = reinterpret_cast<const __nv_bfloat16 *>(p.act) + base;
-                m = fmaxf(fmaxf(fabsf(to_f32(b[0])), fabsf(to_f32(b[1]))),
-                          fmaxf(fabsf(to_f32(b[2])), fabsf(to_f32(b[3]))));
+        if (warp < it.count) {
+            const int c = warp;
+            const int64_t pos = it.pos0 + c;
+            int64_t row = pos;
+            if (p.pos_tok)
+                row = pos < p.shared_base ? (int64_t)p.pos_tok[pos] : pos - p.shared_base;
+            const int64_t base = row * p.act_ld;
+            float m = 0.0f;
+            for (int q = lane; q < (K >> 2); q += 32) {
+                const float4 v = load_act4(p.act, p.act_dtype, base + 4 * q);
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
             }
-            // non-negative floats order like their bit patterns
-            atomicMax(reinterpret_cast<int *>(&s_max[c]), __float_as_int(m));
-        }
-        __syncthreads();
-        if (tid < kTok) {
-            const float m = s_max[tid];
+            m = warp_max(m);
             int e = 0;
             if (m > 0.0f) {
                 int ex;
                 frexpf(m, &ex);          // m = f * 2^ex, f in [0.5, 1)
                 e = max(ex - 22, -120);  // m * 2^-e in [2^21, 2^22)
             }
-            s_exp[tid] = e;
-        }
-        __syncthreads();
-        for (int i = tid; i < it.count * nblk; i += kThreads) {
-            const int c = i / nblk, b = i % nblk;
-            const int k0 = b * 16;
-            const float sc = pow2i(-s_exp[c]);
-            int Q[16];
+            const float sc = pow2i(-e);
             long long sq = 0;
+            for (int b = lane; b < nblk; b += 32) {
+                int Q[16];
+                const bool in = b * 16 < K;  // K % 16 == 0: blocks are all in or out
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int k = k0 + j;
-                float v = 0.0f;
-                if (k < K) v = load_act(p.act, p.act_dtype, s_row[c] * p.act_ld + k);
-                Q[j] = __float2int_rn(v * sc);
-                sq += Q[j];
+                for (int j4 = 0; j4 < 4; ++j4) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (in) v = load_act4(p.act, p.act_dtype, base + b * 16 + 4 * j4);
+                    Q[4 * j4 + 0] = __float2int_rn(v.x * sc);
+                    Q[4 * j4 + 1] = __float2int_rn(v.y * sc);
+                    Q[4 * j4 + 2] = __float2int_rn(v.z * sc);
+                    Q[4 * j4 + 3] = __float2int_rn(v.w * sc);
+                }
+                uint32_t l0[4], l1[4], l2[4];
+#pragma unroll
+                for (int w = 0; w < 4; ++w) { l0[w] = l1[w] = l2[w] = 0u; }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int q = Q[j];
+                    sq += q;
+                    const int d0 = ((q + 128) & 255) - 128;
+                    const int q1 = (q - d0) >> 8;
+                    const int d1 = ((q1 + 128) & 255) - 128;
+                    const int d2 = (q1 - d1) >> 8;
+                    // element j -> byte (j % 4) * 4 + j / 4 of the block
+                    const int word = j & 3, sh = (j >> 2) * 8;
+                    l0[word] |= (uint32_t)(d0 & 255) << sh;
+                    l1[word] |= (uint32_t)(d1 & 255) << sh;
+                    l2[word] |= (uint32_t)(d2 & 255) << sh;
+                }
+                const int pc = swz(b) * 16;
+                *reinterpret_cast<uint4 *>(sm + (0 * kTok + c) * stride + pc) = make_uint4(l0[0], l0[1], l0[2], l0[3]);
+                *reinterpret_cast<uint4 *>(sm + (1 * kTok + c) * stride + pc) = make_uint4(l1[0], l1[1], l1[2], l1[3]);
+                *reinterpret_cast<uint4 *>(sm + (2 * kTok + c) * stride + pc) = make_uint4(l2[0], l2[1], l2[2], l2[3]);
             }
-            uint32_t l0[4], l1[4], l2[4];
 #pragma unroll
-            for (int w = 0; w < 4; ++w) { l0[w] = l1[w] = l2[w] = 0u; }
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int q = Q[j];
-                const int d0 = ((q + 128) & 255) - 128;
-                const int q1 = (q - d0) >> 8;
-                const int d1 = ((q1 + 128) & 255) - 128;
-                const int d2 = (q1 - d1) >> 8;
-                // element j -> byte (j % 4) * 4 + j / 4 of the block
-                const int word = j & 3, sh = (j >> 2) * 8;
-                l0[word] |= (uint32_t)(d0 & 255) << sh;
-                l1[word] |= (uint32_t)(d1 & 255) << sh;
-                l2[word] |= (uint32_t)(d2 & 255) << sh;
+            for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            if (lane == 0) {
+                s_exp[c] = e;
+                s_sumq[c] = sq;
             }
-            const int pc = swz(b) * 16;
-            *reinterpret_cast<uint4 *>(sm + (0 * kTok + c) * stride + pc) = make_uint4(l0[0], l0[1], l0[2], l0[3]);
-            *reinterpret_cast<uint4 *>(sm + (1 * kTok + c) * stride + pc) = make_uint4(l1[0], l1[1], l1[2], l1[3]);
-            *reinterpret_cast<uint4 *>(sm + (2 * kTok + c) * stride + pc) = make_uint4(l2[0], l2[1], l2[2], l2[3]);
-            atomicAdd(reinterpret_cast<unsigned long long *>(&s_sumq[c]), (unsigned long long)sq);
         }
         __syncthreads();
 
@@ -271,7 +254,9 @@ qgemv_kernel(const QgemvParams p) {
             const int r = tid & 127;
             const int grow = it.rb * 128 + r;
             if (grow < rows) {
-                const float sg = __ldg(sbase + grow);
+                // scales by matrix, not by this warp's matrix: threads 128..255
+                // belong to the up-projection warps but combine both
+                const float sg = __ldg((it.shared ? p.ss[0] : p.s[0] + (int64_t)it.seg * p.s_stride) + grow);
                 const float su = __ldg((it.shared ? p.ss[1] : p.s[1] + (int64_t)it.seg * p.s_stride) + grow);
                 for (int c = tid >> 7; c < it.count; c += 2) {
                     const double s2 = (double)pow2i(s_exp[c]);
