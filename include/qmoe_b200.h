@@ -205,6 +205,42 @@ QMOE_API int qmoe_layer_forward_routed(qmoe_layer *layer, const void *x, int dty
 QMOE_API int qmoe_layer_shared_forward(qmoe_layer *layer, const void *x, int dtype,
                               int64_t T, void *out, int accumulate, int ptr_kind);
 
+/* ---- allocation-free packed GEMV ---------------------------------------- */
+
+/* Limits of qmoe_packed_forward_noalloc. */
+#define QMOE_NOALLOC_MAX_BATCH 16384
+#define QMOE_NOALLOC_MAX_IN_FEATURES 8192
+
+/*
+ * y = forward_simd(x) for callers that may not allocate device memory.  It has
+ * no counterpart in qmoe-rs; it is the same product as qmoe_packed_forward
+ * for a host program that owns all device memory (for instance a server that
+ * hands its whole HBM budget to its own pool at start-up and gives a plugin
+ * only each call's buffers), or a latency-critical path where cudaMalloc's
+ * implicit device synchronisation is not allowed.
+ *
+ * All of packed ([out_features, in_features/4] bytes), scales, x
+ * ([batch, in_features] f32) and y ([batch, out_features] f32) are device
+ * pointers on `device`; packed and x must be 16-byte aligned.  The call is
+ * asynchronous on `stream` and calls no cudaMalloc, cudaFree or allocating
+ * library routine: its work list lives in one fixed array of device memory
+ * (about 52 KB) that the library holds on every GPU it is loaded on until the
+ * process exits.  Limits: batch <= QMOE_NOALLOC_MAX_BATCH, in_features a
+ * multiple of 64 and <= QMOE_NOALLOC_MAX_IN_FEATURES; larger sizes return
+ * QMOE_ERR_INVALID with a message in qmoe_last_error().
+ *
+ * The first call on a device does a one-time set-up with that device current
+ * (it looks up the array's device address and sizes the launch grid); make
+ * that first call before any stream capture.  Every call
+ * on a device uses the same array, so calls that overlap on the GPU (two
+ * streams, or two host threads) race; serialise them.  Each call rewrites
+ * everything its kernels read from the array, so nothing needs clearing.
+ */
+QMOE_API int qmoe_packed_forward_noalloc(int device, void *stream, const uint8_t *packed,
+                                         const float *scales, int64_t out_features,
+                                         int64_t in_features, const float *x,
+                                         int64_t batch, float *y);
+
 /* ---- tracing ----------------------------------------------------------- */
 
 /* Stage timing, the device-side counterpart of the Instant-based breakdown

@@ -782,3 +782,7 @@ int qmoe_layer_stage_times(qmoe_layer *L, float *ms, int capacity, int *count) {
 }
 
 }  // extern "C"
+
+namespace qmoe {
+void set_last_error_message(const char *msg) { g_err = msg ? msg : ""; }
+}  // namespace qmoe

@@ -6,6 +6,13 @@
 
 namespace qmoe {
 
+// Rows per work item of the decode kernels (qgemv.cu); a permute chunk fed to
+// them must not exceed it.
+constexpr int kQgemvTokens = 5;
+
+// Sets the message qmoe_last_error() returns on this thread (api.cu).
+void set_last_error_message(const char *msg);
+
 // ---- router -------------------------------------------------------------
 struct RouterParams {
     const void *x;          // [T, H] f32 or bf16
