@@ -246,9 +246,10 @@ QMOE_API int qmoe_packed_forward_noalloc(int device, void *stream, const uint8_t
 /* Stage timing, the device-side counterpart of the Instant-based breakdown
  * of qmoe-rs's bench harness (benches/moe_layer.rs:105-195).  While enabled,
  * each forward records CUDA events on the context's stream around its
- * stages: 0 router, 1 permute, 2 gate/up + SwiGLU, 3 down, 4 combine. */
+ * stages: 0 router, 1 permute, 2 activation limbs for gate/up, 3 gate/up +
+ * SwiGLU GEMV, 4 limbs for down, 5 down GEMV, 6 combine. */
 QMOE_API int qmoe_layer_set_profiling(qmoe_layer *layer, int enable);
-/* Waits for the last profiled forward and writes min(capacity, 5) stage
+/* Waits for the last profiled forward and writes min(capacity, 7) stage
  * durations in milliseconds to ms; *count receives the number written. */
 QMOE_API int qmoe_layer_stage_times(qmoe_layer *layer, float *ms, int capacity,
                                     int *count);

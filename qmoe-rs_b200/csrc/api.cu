@@ -104,6 +104,21 @@ int check_align(const void *p, int ptr_kind, const char *name) {
 
 constexpr int kDecodeTok = 5;   // tokens per work item of the decode kernels
 
+// A kernel whose bounded wait timed out leaves a flag in device memory; report
+// (and clear) it at the next host synchronisation point.
+int check_device_error() {
+    int *flag = qmoe::device_error_flag();
+    if (!flag) return QMOE_OK;
+    int v = 0;
+    QTRY_CUDA(cudaMemcpy(&v, flag, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v) {
+        const int z = 0;
+        cudaMemcpy(flag, &z, sizeof(int), cudaMemcpyHostToDevice);
+        return fail(QMOE_ERR_CUDA, "a device-side wait timed out; the kernel abandoned its work");
+    }
+    return QMOE_OK;
+}
+
 }  // namespace
 
 struct qmoe_ctx {
@@ -131,17 +146,23 @@ struct qmoe_layer {
     uint8_t *ws[3] = {nullptr, nullptr, nullptr};
     float *ss[3] = {nullptr, nullptr, nullptr};
     int grid0 = 0, grid1 = 0;
+    // tensor-core GEMV: TMA maps over the stacked 2-bit matrices, one CTA per SM
+    int sm_count = 0;
+    CUtensorMap tm_w[3], tm_ws[3];
+    int kp1 = 0, kp2 = 0;  // limb row strides: hidden dim / intermediate dims, padded to 256
     // scratch
     int64_t cap = -1;
     DevBuf topk_idx, topk_w, assign_pos, pos_tok, seg_off, groups, ngroups, h, y;
     DevBuf x_in, io_out, user_idx, user_w;
+    DevBuf xq1, meta1, xq2, meta2;
+    CUtensorMap tm_xq1, tm_xq2;
     // tracing
     bool profiling = false;
-    cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    cudaEvent_t ev[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
 };
 
 namespace {
-constexpr int kStages = 5;
+constexpr int kStages = 7;  // router, permute, quant1, gate_up, quant2, down, combine
 inline void mark(qmoe_layer *L, int i) {
     if (L->profiling) cudaEventRecord(L->ev[i], L->ctx->stream);
 }
@@ -189,7 +210,7 @@ int qmoe_ctx_synchronize(qmoe_ctx *ctx) {
     if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
     DeviceGuard g(ctx->device);
     QTRY_CUDA(cudaStreamSynchronize(ctx->stream));
-    return QMOE_OK;
+    return check_device_error();
 }
 
 // ---------------------------------------------------------------------------
@@ -364,7 +385,8 @@ int qmoe_layer_destroy(qmoe_layer *L) {
         if (e) cudaEventDestroy(e);
     DevBuf *bufs[] = {&L->topk_idx, &L->topk_w, &L->assign_pos, &L->pos_tok,
                       &L->seg_off, &L->groups, &L->ngroups, &L->h, &L->y,
-                      &L->x_in, &L->io_out, &L->user_idx, &L->user_w};
+                      &L->x_in, &L->io_out, &L->user_idx, &L->user_w,
+                      &L->xq1, &L->meta1, &L->xq2, &L->meta2};
     for (DevBuf *b : bufs) release(*b);
     delete L;
     return QMOE_OK;
@@ -414,6 +436,31 @@ static int layer_create_impl(qmoe_layer *L, const float *gate_weight, const floa
         }
     }
     QTRY_CUDA(cudaStreamSynchronize(st));
+    // TMA maps: rows of 64-byte boxes, 128 rows per box, 64-byte swizzle
+    for (int m = 0; m < 3; ++m) {
+        if (!make_tmap_u8(&L->tm_w[m], L->w[m], (uint64_t)(kin[m] / 4), (uint64_t)(rows[m] * El),
+                          64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+            return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for expert matrix %d", m);
+        L->tm_ws[m] = L->tm_w[m];
+    }
+    if (L->has_shared) {
+        const int64_t Is = c.shared_intermediate_dim;
+        const int64_t srows[3] = {Is, Is, H}, skin[3] = {H, H, Is};
+        for (int m = 0; m < 3; ++m)
+            if (!make_tmap_u8(&L->tm_ws[m], L->ws[m], (uint64_t)(skin[m] / 4), (uint64_t)srows[m],
+                              64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+                return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for shared matrix %d", m);
+    }
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        QTRY_CUDA(cudaDeviceGetAttribute(&L->sm_count, cudaDevAttrMultiProcessorCount, dev));
+        const int64_t Imx = c.shared_intermediate_dim > I ? c.shared_intermediate_dim : I;
+        L->kp1 = (int)((H + 255) / 256 * 256);
+        L->kp2 = (int)((Imx + 255) / 256 * 256);
+        if (qgemv_tc_smem_bytes(L->kp1, 1) > 227 * 1024 || qgemv_tc_smem_bytes(L->kp2, 1) > 227 * 1024)
+            return fail(QMOE_ERR_UNSUPPORTED, "hidden or intermediate dim too large for the GEMV tiles");
+    }
     const int kmax0 = (int)H;
     const int kmax1 = (int)(c.shared_intermediate_dim > I ? c.shared_intermediate_dim : I);
     L->grid0 = qgemv_max_grid(0, kmax0);
@@ -475,6 +522,15 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
     QTRY(grow(L->ngroups, sizeof(int32_t) * 2));
     QTRY(grow(L->h, sizeof(float) * npos * Imax));
     QTRY(grow(L->y, sizeof(float) * npos * H));
+    QTRY(grow(L->xq1, (size_t)npos * 3 * L->kp1));
+    QTRY(grow(L->xq2, (size_t)npos * 3 * L->kp2));
+    QTRY(grow(L->meta1, sizeof(longlong2) * npos));
+    QTRY(grow(L->meta2, sizeof(longlong2) * npos));
+    if (!make_tmap_u8(&L->tm_xq1, L->xq1.p, (uint64_t)L->kp1, (uint64_t)(npos * 3), 128, 16,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_u8(&L->tm_xq2, L->xq2.p, (uint64_t)L->kp2, (uint64_t)(npos * 3), 128, 16,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+        return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the limb scratch");
     L->cap = T;
     return QMOE_OK;
 }
@@ -548,59 +604,90 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     mark(L, 1);
     QTRY_CUDA(launch_permute(pp, st));
 
-    QgemvParams q{};
-    q.groups = L->groups.as<int4>();
-    q.n_groups = L->ngroups.as<int32_t>();
-    q.w[0] = L->w[0];
-    q.w[1] = L->w[1];
-    q.s[0] = L->s[0];
-    q.s[1] = L->s[1];
-    q.w_stride = (int64_t)c.intermediate_dim * (c.hidden_dim / 4);
-    q.s_stride = c.intermediate_dim;
-    q.rows = c.intermediate_dim;
-    q.K = c.hidden_dim;
-    if (with_shared) {
-        q.ws[0] = L->ws[0];
-        q.ws[1] = L->ws[1];
-        q.ss[0] = L->ss[0];
-        q.ss[1] = L->ss[1];
-        q.rows_s = c.shared_intermediate_dim;
-        q.K_s = c.hidden_dim;
-    }
-    q.act = xd;
-    q.act_dtype = dtype;
-    q.act_ld = c.hidden_dim;
-    q.pos_tok = L->pos_tok.as<int32_t>();
-    q.shared_base = TK;
-    q.out = L->h.as<float>();
-    q.out_ld = Imax;
-    mark(L, 2);
-    QTRY_CUDA(launch_qgemv(0, q, L->grid0, st));
+    const int64_t npos = TK + (with_shared ? T : 0);
+    const int32_t *n_valid = L->seg_off.as<int32_t>() + L->e_count;
+    int *err = device_error_flag();
 
-    QgemvParams d{};
-    d.groups = q.groups;
-    d.n_groups = q.n_groups;
-    d.w[0] = L->w[2];
-    d.s[0] = L->s[2];
-    d.w_stride = (int64_t)c.hidden_dim * (c.intermediate_dim / 4);
-    d.s_stride = c.hidden_dim;
-    d.rows = c.hidden_dim;
-    d.K = c.intermediate_dim;
-    if (with_shared) {
-        d.ws[0] = L->ws[2];
-        d.ss[0] = L->ss[2];
-        d.rows_s = c.hidden_dim;
-        d.K_s = c.shared_intermediate_dim;
-    }
-    d.act = L->h.p;
-    d.act_dtype = 0;
-    d.act_ld = Imax;
-    d.pos_tok = nullptr;
-    d.shared_base = TK;
-    d.out = L->y.as<float>();
-    d.out_ld = c.hidden_dim;
+    // gate/up: activations -> limbs, then the tensor-core GEMV with SwiGLU
+    QuantParams q1{};
+    q1.act = xd;
+    q1.dtype = dtype;
+    q1.act_ld = c.hidden_dim;
+    q1.pos_tok = L->pos_tok.as<int32_t>();
+    q1.shared_base = TK;
+    q1.n_valid = n_valid;
+    q1.npos = npos;
+    q1.K = c.hidden_dim;
+    q1.K_s = c.hidden_dim;
+    q1.Kp = L->kp1;
+    q1.xq = L->xq1.as<int8_t>();
+    q1.meta = L->meta1.as<longlong2>();
+    mark(L, 2);
+    QTRY_CUDA(launch_quant(q1, st));
     mark(L, 3);
-    QTRY_CUDA(launch_qgemv(1, d, L->grid1, st));
+
+    QgemvTcMaps m0;
+    m0.a0 = L->tm_w[0];
+    m0.a1 = L->tm_w[1];
+    m0.s0 = L->tm_ws[0];
+    m0.s1 = L->tm_ws[1];
+    m0.b = L->tm_xq1;
+    QgemvTcParams g0{};
+    g0.groups = L->groups.as<int4>();
+    g0.n_groups = L->ngroups.as<int32_t>();
+    g0.rows = c.intermediate_dim;
+    g0.K = c.hidden_dim;
+    g0.rows_s = with_shared ? c.shared_intermediate_dim : 0;
+    g0.K_s = c.hidden_dim;
+    g0.s[0] = L->s[0];
+    g0.s[1] = L->s[1];
+    g0.s_stride = c.intermediate_dim;
+    g0.ss[0] = L->ss[0];
+    g0.ss[1] = L->ss[1];
+    g0.meta = q1.meta;
+    g0.kp_b = L->kp1;
+    g0.b_buffers = qgemv_tc_buffers(L->kp1);
+    g0.out = L->h.as<float>();
+    g0.out_ld = Imax;
+    g0.err = err;
+    QTRY_CUDA(launch_qgemv_tc(0, m0, g0, L->sm_count, st));
+
+    // down: SwiGLU outputs -> limbs, then the tensor-core GEMV
+    QuantParams q2 = q1;
+    q2.act = L->h.p;
+    q2.dtype = 0;
+    q2.act_ld = Imax;
+    q2.pos_tok = nullptr;
+    q2.K = c.intermediate_dim;
+    q2.K_s = with_shared ? c.shared_intermediate_dim : c.intermediate_dim;
+    q2.Kp = L->kp2;
+    q2.xq = L->xq2.as<int8_t>();
+    q2.meta = L->meta2.as<longlong2>();
+    mark(L, 4);
+    QTRY_CUDA(launch_quant(q2, st));
+    mark(L, 5);
+
+    QgemvTcMaps m1;
+    m1.a0 = m1.a1 = L->tm_w[2];
+    m1.s0 = m1.s1 = L->tm_ws[2];
+    m1.b = L->tm_xq2;
+    QgemvTcParams g1{};
+    g1.groups = g0.groups;
+    g1.n_groups = g0.n_groups;
+    g1.rows = c.hidden_dim;
+    g1.K = c.intermediate_dim;
+    g1.rows_s = with_shared ? c.hidden_dim : 0;
+    g1.K_s = with_shared ? c.shared_intermediate_dim : c.intermediate_dim;
+    g1.s[0] = g1.s[1] = L->s[2];
+    g1.s_stride = c.hidden_dim;
+    g1.ss[0] = g1.ss[1] = L->ss[2];
+    g1.meta = q2.meta;
+    g1.kp_b = L->kp2;
+    g1.b_buffers = qgemv_tc_buffers(L->kp2);
+    g1.out = L->y.as<float>();
+    g1.out_ld = c.hidden_dim;
+    g1.err = err;
+    QTRY_CUDA(launch_qgemv_tc(1, m1, g1, L->sm_count, st));
 
     CombineParams cp{};
     cp.y = L->y.as<float>();
@@ -614,9 +701,9 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     cp.accumulate = accumulate;
     cp.out = outd;
     cp.out_dtype = dtype;
-    mark(L, 4);
+    mark(L, 6);
     QTRY_CUDA(launch_combine(cp, st));
-    mark(L, 5);
+    mark(L, 7);
     return QMOE_OK;
 }
 
@@ -664,7 +751,10 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
                                   ptr_kind == QMOE_PTR_HOST ? cudaMemcpyDeviceToHost
                                                             : cudaMemcpyDeviceToDevice, st));
     QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
-    if (ptr_kind == QMOE_PTR_HOST) QTRY_CUDA(cudaStreamSynchronize(st));
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY_CUDA(cudaStreamSynchronize(st));
+        QTRY(check_device_error());
+    }
     return QMOE_OK;
 }
 
@@ -688,7 +778,10 @@ int qmoe_layer_route(qmoe_layer *L, const void *x, int dtype, int64_t T, int32_t
                                                        : cudaMemcpyDeviceToDevice;
     QTRY_CUDA(cudaMemcpyAsync(topk_idx, L->topk_idx.p, kb, k, st));
     QTRY_CUDA(cudaMemcpyAsync(topk_w, L->topk_w.p, kb, k, st));
-    if (ptr_kind == QMOE_PTR_HOST) QTRY_CUDA(cudaStreamSynchronize(st));
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY_CUDA(cudaStreamSynchronize(st));
+        QTRY(check_device_error());
+    }
     return QMOE_OK;
 }
 
@@ -721,7 +814,10 @@ int qmoe_layer_forward_routed(qmoe_layer *L, const void *x, int dtype, int64_t R
     QTRY(run_experts(L, xd, dtype, R, static_cast<const int32_t *>(id),
                      static_cast<const float *>(wd), 0, false, outd, 0));
     QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
-    if (ptr_kind == QMOE_PTR_HOST) QTRY_CUDA(cudaStreamSynchronize(st));
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY_CUDA(cudaStreamSynchronize(st));
+        QTRY(check_device_error());
+    }
     return QMOE_OK;
 }
 
@@ -757,7 +853,10 @@ int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T
     L->cfg = saved;
     if (rc != QMOE_OK) return rc;
     QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
-    if (ptr_kind == QMOE_PTR_HOST) QTRY_CUDA(cudaStreamSynchronize(st));
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY_CUDA(cudaStreamSynchronize(st));
+        QTRY(check_device_error());
+    }
     return QMOE_OK;
 }
 

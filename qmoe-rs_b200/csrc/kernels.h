@@ -1,6 +1,7 @@
 // kernels.h -- launch interface of the qmoe_b200 kernels (library-internal).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -80,6 +81,54 @@ struct QgemvParams {
 cudaError_t launch_qgemv(int mode, const QgemvParams &p, int grid, cudaStream_t s);
 int qgemv_max_grid(int mode, int K_max);
 size_t qgemv_smem_bytes(int K_max);
+
+// ---- activation quantisation for the integer tensor-core GEMV -----------
+struct QuantParams {
+    const void *act;             // rows of f32 or bf16
+    int dtype;
+    int64_t act_ld;
+    const int32_t *pos_tok;      // routed position -> row (nullable: row = pos)
+    int64_t shared_base;         // positions >= this are shared rows pos - base
+    const int32_t *n_valid;      // routed positions >= *n_valid are skipped (nullable)
+    int64_t npos;                // positions (grid size)
+    int K, K_s;                  // row length of routed / shared rows
+    int Kp;                      // row stride of xq (>= both padded to 256)
+    int8_t *xq;                  // [npos][3][Kp] limbs
+    longlong2 *meta;             // [npos] (exponent, sum of Q)
+};
+cudaError_t launch_quant(const QuantParams &p, cudaStream_t s);
+
+// ---- decode grouped GEMV on tcgen05 (kind::i8, A = unpacked codes in TMEM) --
+struct QgemvTcMaps {
+    CUtensorMap a0, a1;          // routed matrices (mode 0: gate, up; mode 1: down, down)
+    CUtensorMap s0, s1;          // shared-expert matrices (copies of a0/a1 if none)
+    CUtensorMap b;               // limb rows xq [npos*3][kp_b], 128-byte swizzle
+};
+struct QgemvTcParams {
+    const int4 *groups;
+    const int32_t *n_groups;
+    int rows, K;                 // routed matrices
+    int rows_s, K_s;             // shared segment (rows_s = 0: none)
+    const float *s[2];           // routed scales, expert stride s_stride
+    int64_t s_stride;
+    const float *ss[2];          // shared scales
+    const longlong2 *meta;       // per position (exponent, sum of Q)
+    int kp_b;                    // row length of the limb rows (>= every item's padded K)
+    int b_buffers;               // limb-tile buffers (2, or 1 for very long rows)
+    float *out;
+    int64_t out_ld;
+    int *err;                    // device error word
+};
+cudaError_t launch_qgemv_tc(int mode, const QgemvTcMaps &maps, const QgemvTcParams &p, int grid,
+                            cudaStream_t s);
+size_t qgemv_tc_smem_bytes(int kp_b, int b_buffers);
+int qgemv_tc_buffers(int kp_b);
+int *device_error_flag();
+
+// Host: a 2-D uint8 tensor map over [rows][row_bytes] with the given box and
+// swizzle (CU_TENSOR_MAP_SWIZZLE_*); returns false if encoding fails.
+bool make_tmap_u8(CUtensorMap *tm, const void *base, uint64_t row_bytes, uint64_t rows,
+                  uint32_t box_bytes, uint32_t box_rows, int swizzle);
 
 // ---- combine -----------------------------------------------------------
 struct CombineParams {

@@ -1,0 +1,99 @@
+// quant.cu -- activations -> per-row fixed point, as three balanced int8 limbs.
+//
+// Feeds the integer tensor-core GEMV (qgemv_tc.cu).  For every row (one
+// routed assignment or shared-expert token, in position order):
+//   e   = exponent with max|x| * 2^-e in [2^21, 2^22)  (0 for an all-zero row)
+//   Q_k = rint(x_k * 2^-e)      (scaling by a power of two is exact)
+//   Q_k = q2 * 2^16 + q1 * 2^8 + q0 with every q in [-128, 127]
+// written as xq[row][limb][Kp] (int8) and meta[row] = (e, sum_k Q_k).
+// Inside each 16-element block the bytes are stored in the order
+// 0,4,8,12, 1,5,9,13, 2,6,10,14, 3,7,11,15: the order in which the GEMV
+// unpacks a 32-bit word of 2-bit codes ((w >> 2j) & 0x03030303 holds codes
+// j, j+4, j+8, j+12), so activation k meets the weight of column k.
+// Blocks past K up to Kp are zero.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qmoe {
+namespace {
+
+constexpr int kQuantThreads = 128;
+
+__global__ void __launch_bounds__(kQuantThreads)
+quant_kernel(const QuantParams p) {
+    const int64_t pos = blockIdx.x;
+    const bool routed = pos < p.shared_base;
+    if (routed && p.n_valid && pos >= *p.n_valid) return;  // unused routed slot
+    int64_t row = pos;
+    if (p.pos_tok) row = routed ? (int64_t)p.pos_tok[pos] : pos - p.shared_base;
+    const int64_t base = row * p.act_ld;
+    const int K = routed ? p.K : p.K_s, tid = threadIdx.x;
+    const int nblk = ((K + 255) / 256) * 16;  // blocks the GEMV reads (K padded to 256)
+    __shared__ float s_red[kQuantThreads / 32];
+    __shared__ long long s_sum[kQuantThreads / 32];
+
+    float m = 0.0f;
+    for (int q = tid; q < (K >> 2); q += kQuantThreads) {
+        const float4 v = load_act4(p.act, p.dtype, base + 4 * q);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    m = warp_max(m);
+    if ((tid & 31) == 0) s_red[tid >> 5] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
+    int e = 0;
+    if (m > 0.0f) {
+        int ex;
+        frexpf(m, &ex);
+        e = max(ex - 22, -120);
+    }
+    const float sc = pow2i(-e);
+
+    long long sq = 0;
+    int8_t *dst = p.xq + pos * 3 * (int64_t)p.Kp;
+    for (int b = tid; b < nblk; b += kQuantThreads) {
+        int Q[16];
+        const bool in = b * 16 < K;
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (in) v = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
+            Q[4 * j4 + 0] = __float2int_rn(v.x * sc);
+            Q[4 * j4 + 1] = __float2int_rn(v.y * sc);
+            Q[4 * j4 + 2] = __float2int_rn(v.z * sc);
+            Q[4 * j4 + 3] = __float2int_rn(v.w * sc);
+        }
+        uint32_t l0[4] = {0, 0, 0, 0}, l1[4] = {0, 0, 0, 0}, l2[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int q = Q[j];
+            sq += q;
+            const int d0 = ((q + 128) & 255) - 128;
+            const int q1 = (q - d0) >> 8;
+            const int d1 = ((q1 + 128) & 255) - 128;
+            const int d2 = (q1 - d1) >> 8;
+            const int word = j & 3, sh = (j >> 2) * 8;  // element j -> byte 4*(j%4) + j/4
+            l0[word] |= (uint32_t)(d0 & 255) << sh;
+            l1[word] |= (uint32_t)(d1 & 255) << sh;
+            l2[word] |= (uint32_t)(d2 & 255) << sh;
+        }
+        *reinterpret_cast<uint4 *>(dst + 0 * p.Kp + 16 * b) = make_uint4(l0[0], l0[1], l0[2], l0[3]);
+        *reinterpret_cast<uint4 *>(dst + 1 * p.Kp + 16 * b) = make_uint4(l1[0], l1[1], l1[2], l1[3]);
+        *reinterpret_cast<uint4 *>(dst + 2 * p.Kp + 16 * b) = make_uint4(l2[0], l2[1], l2[2], l2[3]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((tid & 31) == 0) s_sum[tid >> 5] = sq;
+    __syncthreads();
+    if (tid == 0) p.meta[pos] = make_longlong2(e, s_sum[0] + s_sum[1] + s_sum[2] + s_sum[3]);
+}
+
+}  // namespace
+
+cudaError_t launch_quant(const QuantParams &p, cudaStream_t s) {
+    if (p.npos == 0) return cudaSuccess;
+    quant_kernel<<<(unsigned)p.npos, kQuantThreads, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace qmoe

@@ -95,7 +95,7 @@ SIGNATURES = {
                                     ctypes.POINTER(ctypes.c_int)]),
 }
 
-STAGES = ("router", "permute", "gate_up", "down", "combine")
+STAGES = ("router", "permute", "quant_up", "gate_up", "quant_down", "down", "combine")
 
 _lib = None
 
