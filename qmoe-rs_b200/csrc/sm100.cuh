@@ -173,6 +173,20 @@ QMOE_DEV void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint3
         : "memory");
 }
 
+// Same, with the B descriptor given as its two 32-bit halves (callers step the
+// start-address field in the low half without 64-bit arithmetic) and the
+// accumulate flag as a predicate value computed once.
+QMOE_DEV void mma_i8_ts_lohi(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                             uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n .reg .b64 bd;\n setp.ne.b32 p, %5, 0;\n mov.b64 bd, {%2, %3};\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], bd, %4, {%6, %7, %8, %9}, p;\n}" ::"r"(
+            d_tmem),
+        "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
+        "r"(0u), "r"(0u)
+        : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 (bf16 operands, f32 accumulate).
 QMOE_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                           uint32_t accumulate) {
