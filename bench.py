@@ -43,7 +43,7 @@ WORKLOAD = dict(
     name="configs[1]: DeepSeek-V2-Lite MoE layer, decode, 32 f32 tokens/GPU",
     E=64, k=6, H=2048, I=1408, Is=2816, T=32, norm_topk=True)
 REPLICAS = 4
-KERNELS_PER_FORWARD = 5  # router, permute, gate/up, down, combine
+KERNELS_PER_FORWARD = 8  # router logits + select, permute, limbs x2, gate/up, down, combine
 
 
 def parse():

@@ -154,7 +154,7 @@ struct qmoe_layer {
     int64_t cap = -1;
     DevBuf topk_idx, topk_w, assign_pos, pos_tok, seg_off, groups, ngroups, h, y;
     DevBuf x_in, io_out, user_idx, user_w;
-    DevBuf xq1, meta1, xq2, meta2;
+    DevBuf xq1, meta1, xq2, meta2, router_scratch;
     CUtensorMap tm_xq1, tm_xq2;
     // tracing
     bool profiling = false;
@@ -386,7 +386,7 @@ int qmoe_layer_destroy(qmoe_layer *L) {
     DevBuf *bufs[] = {&L->topk_idx, &L->topk_w, &L->assign_pos, &L->pos_tok,
                       &L->seg_off, &L->groups, &L->ngroups, &L->h, &L->y,
                       &L->x_in, &L->io_out, &L->user_idx, &L->user_w,
-                      &L->xq1, &L->meta1, &L->xq2, &L->meta2};
+                      &L->xq1, &L->meta1, &L->xq2, &L->meta2, &L->router_scratch};
     for (DevBuf *b : bufs) release(*b);
     delete L;
     return QMOE_OK;
@@ -458,7 +458,7 @@ static int layer_create_impl(qmoe_layer *L, const float *gate_weight, const floa
         const int64_t Imx = c.shared_intermediate_dim > I ? c.shared_intermediate_dim : I;
         L->kp1 = (int)((H + 255) / 256 * 256);
         L->kp2 = (int)((Imx + 255) / 256 * 256);
-        if (qgemv_tc_smem_bytes(L->kp1, 1) > 227 * 1024 || qgemv_tc_smem_bytes(L->kp2, 1) > 227 * 1024)
+        if (qgemv_imma_smem_bytes(L->kp1, 1) > 227 * 1024 || qgemv_imma_smem_bytes(L->kp2, 1) > 227 * 1024)
             return fail(QMOE_ERR_UNSUPPORTED, "hidden or intermediate dim too large for the GEMV tiles");
     }
     const int kmax0 = (int)H;
@@ -526,6 +526,7 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
     QTRY(grow(L->xq2, (size_t)npos * 3 * L->kp2));
     QTRY(grow(L->meta1, sizeof(longlong2) * npos));
     QTRY(grow(L->meta2, sizeof(longlong2) * npos));
+    QTRY(grow(L->router_scratch, sizeof(float) * router_scratch_floats(T, c.hidden_dim, c.num_experts)));
     if (!make_tmap_u8(&L->tm_xq1, L->xq1.p, (uint64_t)L->kp1, (uint64_t)(npos * 3), 128, 16,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_tmap_u8(&L->tm_xq2, L->xq2.p, (uint64_t)L->kp2, (uint64_t)(npos * 3), 128, 16,
@@ -572,6 +573,7 @@ static int run_router(qmoe_layer *L, const void *xd, int dtype, int64_t T) {
     rp.routed_scale = c.routed_scaling_factor;
     rp.topk_idx = L->topk_idx.as<int32_t>();
     rp.topk_w = L->topk_w.as<float>();
+    rp.scratch = L->router_scratch.as<float>();
     mark(L, 0);
     QTRY_CUDA(launch_router(rp, L->ctx->stream));
     return QMOE_OK;
@@ -646,11 +648,11 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     g0.ss[1] = L->ss[1];
     g0.meta = q1.meta;
     g0.kp_b = L->kp1;
-    g0.b_buffers = qgemv_tc_buffers(L->kp1);
+    g0.b_buffers = qgemv_imma_buffers(L->kp1);
     g0.out = L->h.as<float>();
     g0.out_ld = Imax;
     g0.err = err;
-    QTRY_CUDA(launch_qgemv_tc(0, m0, g0, L->sm_count, st));
+    QTRY_CUDA(launch_qgemv_imma(0, m0, g0, L->sm_count, st));
 
     // down: SwiGLU outputs -> limbs, then the tensor-core GEMV
     QuantParams q2 = q1;
@@ -683,11 +685,11 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     g1.ss[0] = g1.ss[1] = L->ss[2];
     g1.meta = q2.meta;
     g1.kp_b = L->kp2;
-    g1.b_buffers = qgemv_tc_buffers(L->kp2);
+    g1.b_buffers = qgemv_imma_buffers(L->kp2);
     g1.out = L->y.as<float>();
     g1.out_ld = c.hidden_dim;
     g1.err = err;
-    QTRY_CUDA(launch_qgemv_tc(1, m1, g1, L->sm_count, st));
+    QTRY_CUDA(launch_qgemv_imma(1, m1, g1, L->sm_count, st));
 
     CombineParams cp{};
     cp.y = L->y.as<float>();

@@ -28,8 +28,11 @@ struct RouterParams {
     float routed_scale;
     int32_t *topk_idx;      // [T, K]
     float *topk_w;          // [T, K]
+    float *scratch;         // router_scratch_floats(T, H, E) floats
 };
 size_t router_smem_bytes(int H, int E);
+bool router_uses_partials(int64_t T, int E);
+size_t router_scratch_floats(int64_t T, int H, int E);
 cudaError_t launch_router(const RouterParams &p, cudaStream_t s);
 
 // ---- permute ------------------------------------------------------------
@@ -122,6 +125,11 @@ struct QgemvTcParams {
 cudaError_t launch_qgemv_tc(int mode, const QgemvTcMaps &maps, const QgemvTcParams &p, int grid,
                             cudaStream_t s);
 size_t qgemv_tc_smem_bytes(int kp_b, int b_buffers);
+// Same work list and operands, mma.sync m16n8k32 IMMA compute (qgemv_imma.cu).
+cudaError_t launch_qgemv_imma(int mode, const QgemvTcMaps &maps, const QgemvTcParams &p,
+                              int grid, cudaStream_t s);
+size_t qgemv_imma_smem_bytes(int kp_b, int b_buffers);
+int qgemv_imma_buffers(int kp_b);
 int qgemv_tc_buffers(int kp_b);
 int *device_error_flag();
 

@@ -1,0 +1,380 @@
+// qgemv_imma.cu -- decode-sized grouped GEMV over 2-bit packed expert weights.
+//
+// Replaces the per-assignment GEMVs of QMoELayer::forward (qmoe-rs
+// src/moe.rs:96-118 via PackedQMoETensor::forward_simd, src/tensor.rs:64-95,
+// and simd::fused_dequantize_and_dot, src/simd.rs:6-45) and the shared
+// expert's batched GEMVs (src/model.rs:325-347).
+//
+// Arithmetic: a weight is code - 1 (code in 0..3) and each activation row is
+// x ~= 2^e * Q with Q split into three int8 limbs (quant.cu), so
+//     dot(w_r, x) = 2^e * (sum_l 256^l sum_k code_rk q_lk  -  sum_k Q_k).
+// The tensor pipe forms every sum_k code_rk q_lk exactly (mma.sync
+// m16n8k32, A = s8 limbs of <= 5 positions x 3 limbs, B = u8 codes of 8
+// weight rows), the epilogue recombines the limbs in int64 and scales once.
+//
+// Why mma.sync here: with only a few positions per expert the product is a
+// stream of weights each used by <= 15 limb rows.  tcgen05.mma reads its A
+// tile (the weights, 128 rows x 32 bytes) at a fixed ~4 KB per instruction
+// whatever N is, i.e. ~37 weights per clock per SM -- below the HBM rate of
+// ~93 packed weights per clock per SM.  The warp-level m16n8k32 consumes 256
+// weights per instruction from registers, one per ~8 cycles per scheduler
+// (~120 weights per clock per SM), so the kernel can follow HBM.
+//
+// Work item = (<= 5 positions of one segment) x 256 output rows (gate+up
+// rows 128+128 in mode 0, 256 down rows in mode 1).  Persistent grid, one CTA
+// per SM, thirteen warps:
+//   warp 0      TMA: 2-bit weight tiles [128 rows x 64 B] (64-byte swizzle)
+//               into a 4-stage ring (continuous across items) and each item's
+//               limb tile [16 x Kp] (128-byte swizzle) into a 2-deep buffer;
+//   warps 1-8   compute, 32 weight rows each: 128-bit shared loads of the
+//               packed rows, unpack in registers ((w >> 2j) & 0x03030303: one
+//               shift + one mask per 4 weights), m16n8k32 IMMAs against the
+//               limb fragments; at item end the int32 accumulators go to a
+//               double-buffered tile in shared memory;
+//   warps 9-12  epilogue: limb recombination, scales, SwiGLU, stores, while
+//               the compute warps run the next item.
+// Every wait is bounded; on a time-out the kernel flags the device error
+// word, lets its TMA copies drain (again bounded) and returns.
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace qmoe {
+namespace {
+
+using namespace sm100;
+
+constexpr int kWarps = 13;
+constexpr int kThreads = kWarps * 32;
+constexpr int kCompute = 8;            // compute warps (1..8)
+constexpr int kEpiWarp0 = 9;           // first epilogue warp
+constexpr int kNS = 4;                 // weight stages in shared memory
+constexpr int kStageCodes = 256;       // codes per row per stage
+constexpr int kStageRowBytes = 64;
+constexpr int kTileBytes = 128 * kStageRowBytes;  // one 128-row weight tile
+constexpr int kBRows = 16;             // positions x limbs (15 used)
+constexpr int kBBlock = kBRows * 128;  // one 128-byte K block of the limb tile
+constexpr int kTokMax = 5;
+constexpr int kOutCols = 256;          // output rows per item
+constexpr int kAccBytes = kBRows * kOutCols * 4;  // int32 accumulator tile
+constexpr int kItemCache = 256;
+
+struct Smem {
+    uint64_t smem_full[kNS], smem_empty[kNS];
+    uint64_t bq_full[2], bq_empty[2];
+    uint64_t tile_full[2], tile_empty[2];
+    int abort;
+    int4 items[kItemCache];
+};
+
+struct Item {
+    int seg, pos0, count, rb;
+    bool shared;
+};
+
+QMOE_DEV Item decode_item(const QgemvTcParams &p, int item, int nr, int rb_r, int rb_s) {
+    Item it;
+    int g;
+    if (item < nr * rb_r) {
+        g = item / rb_r;
+        it.rb = item % rb_r;
+        it.shared = false;
+    } else {
+        const int j = item - nr * rb_r;
+        g = nr + j / rb_s;
+        it.rb = j % rb_s;
+        it.shared = true;
+    }
+    const int4 d = p.groups[g];
+    it.seg = d.x;
+    it.pos0 = d.y;
+    it.count = d.z;
+    return it;
+}
+
+QMOE_DEV void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                   uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+qgemv_imma_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
+                  const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_s1,
+                  const __grid_constant__ CUtensorMap tm_b, const QgemvTcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *wring = base;                                  // kNS x 2 weight tiles
+    uint8_t *btile = wring + kNS * 2 * kTileBytes;          // nbuf limb tiles
+    const int nbuf = p.b_buffers;
+    const int bbytes = kBRows * p.kp_b;
+    int *acc_tile = reinterpret_cast<int *>(btile + nbuf * bbytes);  // 2 x [16][256]
+    Smem *S = reinterpret_cast<Smem *>(reinterpret_cast<uint8_t *>(acc_tile) + 2 * kAccBytes);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rows_item = MODE == 0 ? 128 : 256;
+    const int rb_r = (p.rows + rows_item - 1) / rows_item;
+    const int rb_s = p.rows_s > 0 ? (p.rows_s + rows_item - 1) / rows_item : 1;
+    const int nr = p.n_groups[0], ns = p.n_groups[1];
+    const int total = nr * rb_r + ns * rb_s;
+    const int my_items = total > (int)blockIdx.x ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+
+    if (tid == 0) {
+        for (int i = 0; i < kNS; ++i) {
+            mbar_init(&S->smem_full[i], 1);
+            mbar_init(&S->smem_empty[i], kCompute);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&S->bq_full[i], 1);
+            mbar_init(&S->bq_empty[i], kCompute);
+            mbar_init(&S->tile_full[i], kCompute);
+            mbar_init(&S->tile_empty[i], 4);
+        }
+        S->abort = 0;
+        fence_mbar_init();
+    }
+    for (int i = tid; i < my_items && i < kItemCache; i += kThreads) {
+        const Item it = decode_item(p, (int)blockIdx.x + i * (int)gridDim.x, nr, rb_r, rb_s);
+        S->items[i] = make_int4(it.seg, it.pos0, it.count, it.rb | (it.shared ? (1 << 30) : 0));
+    }
+    __syncthreads();
+    volatile int *abort = &S->abort;
+
+    auto item_at = [&](int i) -> Item {
+        if (i < kItemCache) {
+            const int4 v = S->items[i];
+            Item it;
+            it.seg = v.x;
+            it.pos0 = v.y;
+            it.count = v.z;
+            it.rb = v.w & ((1 << 30) - 1);
+            it.shared = (v.w >> 30) & 1;
+            return it;
+        }
+        return decode_item(p, (int)blockIdx.x + i * (int)gridDim.x, nr, rb_r, rb_s);
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------- TMA
+        if (lane == 0) {
+            tma_prefetch_desc(&tm_a0);
+            tma_prefetch_desc(&tm_a1);
+            tma_prefetch_desc(&tm_b);
+            if (p.rows_s > 0) {
+                tma_prefetch_desc(&tm_s0);
+                tma_prefetch_desc(&tm_s1);
+            }
+            uint32_t us = 0;
+            int i = 0;
+            bool ok = true;
+            for (; ok && i < my_items; ++i) {
+                const Item it = item_at(i);
+                const int K = it.shared ? p.K_s : p.K;
+                const int nks = (K + kStageCodes - 1) / kStageCodes;
+                const int nkb = nks * 2;
+                const uint32_t b = nbuf == 2 ? (i & 1) : 0, ub = nbuf == 2 ? (i >> 1) : i;
+                if (!(ok = mbar_wait(&S->bq_empty[b], (ub & 1) ^ 1, abort, p.err))) break;
+                mbar_arrive_expect_tx(&S->bq_full[b], (uint32_t)(nkb * kBBlock));
+                for (int kb = 0; kb < nkb; ++kb)
+                    tma_load_2d(btile + b * bbytes + kb * kBBlock, &tm_b, &S->bq_full[b],
+                                kb * 128, it.pos0 * 3);
+                const CUtensorMap *t0 = it.shared ? &tm_s0 : &tm_a0;
+                const CUtensorMap *t1 = MODE == 0 ? (it.shared ? &tm_s1 : &tm_a1) : t0;
+                const int rows = it.shared ? p.rows_s : p.rows;
+                const int ybase = it.shared ? 0 : it.seg * rows;
+                const int y0 = ybase + it.rb * rows_item;
+                const int y1 = MODE == 0 ? y0 : y0 + 128;
+                for (int ks = 0; ks < nks; ++ks, ++us) {
+                    const uint32_t s = us % kNS;
+                    if (!(ok = mbar_wait(&S->smem_empty[s], ((us / kNS) & 1) ^ 1, abort, p.err)))
+                        break;
+                    mbar_arrive_expect_tx(&S->smem_full[s], 2 * kTileBytes);
+                    uint8_t *dst = wring + s * 2 * kTileBytes;
+                    tma_load_2d(dst, t0, &S->smem_full[s], ks * kStageRowBytes, y0);
+                    tma_load_2d(dst + kTileBytes, t1, &S->smem_full[s], ks * kStageRowBytes, y1);
+                }
+            }
+            if (!ok) {
+                for (uint32_t u = us > kNS ? us - kNS : 0; u < us; ++u)
+                    for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
+                        if (mbar_try_wait(&S->smem_full[u % kNS], (u / kNS) & 1)) break;
+                for (int j = i - nbuf < 0 ? 0 : i - nbuf; j <= i && j < my_items; ++j) {
+                    const uint32_t b = nbuf == 2 ? (j & 1) : 0, ub = nbuf == 2 ? (j >> 1) : j;
+                    for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
+                        if (mbar_try_wait(&S->bq_full[b], ub & 1)) break;
+                }
+            }
+        }
+    } else if (warp <= kCompute) {
+        // --------------------------------------------------------- compute
+        const int cw = warp - 1;                    // 0..7
+        const int tile = cw >> 2;                   // weight tile (gate/up, or down half)
+        const int wrow = (cw & 3) * 32;             // first row of this warp in the tile
+        const int g8 = lane >> 2, t4 = lane & 3;
+        uint32_t us = 0;
+        bool ok = true;
+        for (int i = 0; ok && i < my_items; ++i) {
+            const Item it = item_at(i);
+            const int K = it.shared ? p.K_s : p.K;
+            const int nks = (K + kStageCodes - 1) / kStageCodes;
+            const uint32_t b = nbuf == 2 ? (i & 1) : 0, ub = nbuf == 2 ? (i >> 1) : i;
+            if (!(ok = mbar_wait_warp(&S->bq_full[b], ub & 1, abort, p.err))) break;
+            const uint8_t *lt = btile + b * bbytes;
+            // limb rows g8 (atom 0) and g8 + 8 (atom 1) of the 128-byte-swizzled tile
+            const uint8_t *lrow_lo = lt + g8 * 128;
+            const uint8_t *lrow_hi = lt + 1024 + g8 * 128;
+            // two accumulators per row group (the two IMMAs of a 16-code word
+            // go to different ones), so a warp keeps 8 independent chains
+            int acc[4][4], acc2[4][4];
+#pragma unroll
+            for (int rg = 0; rg < 4; ++rg)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[rg][j] = acc2[rg][j] = 0;
+
+            for (int ks = 0; ks < nks; ++ks, ++us) {
+                const uint32_t s = us % kNS;
+                if (!(ok = mbar_wait_warp(&S->smem_full[s], (us / kNS) & 1, abort, p.err))) break;
+                // packed rows wrow + 8 rg + g8, chunk t4 (64 codes), 64-byte swizzle
+                uint4 w[4];
+                const uint8_t *wt = wring + s * 2 * kTileBytes + tile * kTileBytes;
+#pragma unroll
+                for (int rg = 0; rg < 4; ++rg) {
+                    const int r = wrow + rg * 8 + g8;
+                    w[rg] = *reinterpret_cast<const uint4 *>(wt + r * kStageRowBytes +
+                                                             16 * (t4 ^ ((r >> 1) & 3)));
+                }
+                // limb fragments of the stage: 16-element K blocks ks*16 + 4 t4 + q
+                uint4 alo[4], ahi[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int kb = ks * 2 + (t4 >> 1);        // 128-byte block
+                    const int c = ((t4 & 1) << 2) | q;        // 16-byte chunk within it
+                    const int off = kb * kBBlock + 16 * (c ^ g8);
+                    alo[q] = *reinterpret_cast<const uint4 *>(lrow_lo + off);
+                    ahi[q] = *reinterpret_cast<const uint4 *>(lrow_hi + off);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S->smem_empty[s]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                    for (int rg = 0; rg < 4; ++rg) {
+                        const uint32_t wq = q == 0 ? w[rg].x : q == 1 ? w[rg].y : q == 2 ? w[rg].z : w[rg].w;
+                        imma(acc[rg], alo[q].x, ahi[q].x, alo[q].y, ahi[q].y, wq & 0x03030303u,
+                             (wq >> 2) & 0x03030303u);
+                        imma(acc2[rg], alo[q].z, ahi[q].z, alo[q].w, ahi[q].w, (wq >> 4) & 0x03030303u,
+                             (wq >> 6) & 0x03030303u);
+                    }
+                }
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S->bq_empty[b]);
+#pragma unroll
+            for (int rg = 0; rg < 4; ++rg)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[rg][j] += acc2[rg][j];
+
+            // accumulators -> tile [16 limb rows][256 cols]
+            const uint32_t tb = i & 1;
+            if (!(ok = mbar_wait_warp(&S->tile_empty[tb], ((i >> 1) & 1) ^ 1, abort, p.err))) break;
+            int *ct = acc_tile + tb * (kAccBytes / 4);
+#pragma unroll
+            for (int rg = 0; rg < 4; ++rg) {
+                const int col = tile * 128 + wrow + rg * 8 + 2 * t4;
+                *reinterpret_cast<int2 *>(ct + g8 * kOutCols + col) = make_int2(acc[rg][0], acc[rg][1]);
+                *reinterpret_cast<int2 *>(ct + (g8 + 8) * kOutCols + col) = make_int2(acc[rg][2], acc[rg][3]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S->tile_full[tb]);
+        }
+    } else {
+        // -------------------------------------------------------- epilogue
+        const int r = (warp - kEpiWarp0) * 32 + lane;   // 0..127
+        bool ok = true;
+        for (int i = 0; ok && i < my_items; ++i) {
+            const Item it = item_at(i);
+            const int rows = it.shared ? p.rows_s : p.rows;
+            const float *sc0 = it.shared ? p.ss[0] : p.s[0] + (int64_t)it.seg * p.s_stride;
+            const float *sc1 = MODE == 0 ? (it.shared ? p.ss[1] : p.s[1] + (int64_t)it.seg * p.s_stride)
+                                         : sc0;
+            const int row0 = it.rb * rows_item + r;
+            const int row1 = MODE == 0 ? row0 : row0 + 128;
+            const float s0 = row0 < rows ? __ldg(sc0 + row0) : 0.0f;
+            const float s1 = row1 < rows ? __ldg(sc1 + row1) : 0.0f;
+            longlong2 mt[kTokMax];
+#pragma unroll
+            for (int c = 0; c < kTokMax; ++c)
+                mt[c] = c < it.count ? p.meta[it.pos0 + c] : make_longlong2(0, 0);
+
+            const uint32_t tb = i & 1;
+            if (!(ok = mbar_wait_warp(&S->tile_full[tb], (i >> 1) & 1, abort, p.err))) break;
+            const int *ct = acc_tile + tb * (kAccBytes / 4);
+            int v0[kBRows - 1], v1[kBRows - 1];
+#pragma unroll
+            for (int n = 0; n < kBRows - 1; ++n) {
+                v0[n] = ct[n * kOutCols + r];
+                v1[n] = ct[n * kOutCols + 128 + r];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S->tile_empty[tb]);
+#pragma unroll
+            for (int c = 0; c < kTokMax; ++c) {
+                if (c >= it.count) break;
+                const int64_t pos = it.pos0 + c;
+                const double s2 = (double)pow2i((int)mt[c].x);
+                // limb rows of position c are 3c + l
+                const long long a0 = (long long)v0[3 * c + 2] * 65536LL +
+                                     (long long)v0[3 * c + 1] * 256LL + (long long)v0[3 * c] - mt[c].y;
+                const long long a1 = (long long)v1[3 * c + 2] * 65536LL +
+                                     (long long)v1[3 * c + 1] * 256LL + (long long)v1[3 * c] - mt[c].y;
+                const float f0 = __fmul_rn((float)((double)a0 * s2), s0);
+                const float f1 = __fmul_rn((float)((double)a1 * s2), s1);
+                float *o = p.out + pos * p.out_ld;
+                if (MODE == 0) {
+                    if (row0 < rows) o[row0] = swiglu(f0, f1);
+                } else {
+                    if (row0 < rows) o[row0] = f0;
+                    if (row1 < rows) o[row1] = f1;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+}  // namespace
+
+size_t qgemv_imma_smem_bytes(int kp_b, int b_buffers) {
+    return 1024 + (size_t)kNS * 2 * kTileBytes + (size_t)b_buffers * kBRows * kp_b +
+           2 * (size_t)kAccBytes + sizeof(Smem);
+}
+
+int qgemv_imma_buffers(int kp_b) {
+    return qgemv_imma_smem_bytes(kp_b, 2) <= 227 * 1024 ? 2 : 1;
+}
+
+cudaError_t launch_qgemv_imma(int mode, const QgemvTcMaps &maps, const QgemvTcParams &p, int grid,
+                              cudaStream_t s) {
+    const size_t smem = qgemv_imma_smem_bytes(p.kp_b, p.b_buffers);
+    static size_t smem_set[2] = {0, 0};
+    if (smem > smem_set[mode]) {
+        cudaError_t e = mode == 0
+            ? cudaFuncSetAttribute(qgemv_imma_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+            : cudaFuncSetAttribute(qgemv_imma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        smem_set[mode] = smem;
+    }
+    if (mode == 0)
+        qgemv_imma_kernel<0><<<grid, kThreads, smem, s>>>(maps.a0, maps.a1, maps.s0, maps.s1, maps.b, p);
+    else
+        qgemv_imma_kernel<1><<<grid, kThreads, smem, s>>>(maps.a0, maps.a1, maps.s0, maps.s1, maps.b, p);
+    return cudaGetLastError();
+}
+
+}  // namespace qmoe

@@ -1,15 +1,20 @@
 // router.cu -- gate logits, scoring, top-k selection and combine weights.
 //
 // Replaces the router half of QMoELayer::forward (qmoe-rs src/moe.rs:51-82).
-// One CTA routes one token.
 //
 // Logit order (pinned; qmoe-rs delegates the gate matmul to candle, whose
 // order is not observable): the hidden dim is cut into 64-wide chunks; the
 // partial of chunk c is an fmaf chain over its 64 products starting from 0;
-// the logit is ((0 + p_0) + p_1) + ... in chunk order.  All chains run in
-// parallel, one per thread; a second pass adds the partials of each expert
-// in order.  The CPU oracle computes the same operations in the same order,
-// so the logits, and the routing built from them, agree bit for bit.
+// the logit is ((0 + p_0) + p_1) + ... in chunk order.  The CPU oracle
+// computes the same operations in the same order, so the logits, and the
+// routing built from them, agree bit for bit.  Two ways to get there:
+//   few tokens   router_partials_kernel: one thread per (token, expert,
+//                chunk) chain, all chains in parallel; the selection kernel
+//                adds each expert's partials in chunk order;
+//   many tokens  router_logits_kernel: 64x64 (token x expert) tiles staged
+//                in shared memory chunk by chunk, each thread owning 4x4
+//                logits and running the same chains and chunk sums.
+// Then router_select_kernel, one CTA per token, scores and selects.
 //
 // Selection: stable descending order with ties to the lower expert index
 // (src/moe.rs:68-71), computed as a rank per expert.  Softmax weights use
@@ -23,20 +28,17 @@ namespace qmoe {
 namespace {
 
 constexpr int kRouterThreads = 256;
-constexpr int kChunkBatch = 32;              // chunks per partials pass
-constexpr int kXStride = kGateChunk + 1;     // padded chunk stride in smem
 
 struct RouterSmem {
     // offsets in floats within the dynamic buffer
     int xs, part, logit, choice, ex, gscore, misc;
 };
 
-__host__ __device__ inline RouterSmem router_layout(int H, int E) {
-    int nc = (H + kGateChunk - 1) / kGateChunk;
+__host__ __device__ inline RouterSmem router_layout(int E) {
     RouterSmem L;
     L.xs = 0;
-    L.part = L.xs + nc * kXStride;
-    L.logit = L.part + E * kChunkBatch;
+    L.part = 0;                              // 8 floats of warp maxima
+    L.logit = L.part + 8;
     L.choice = L.logit + E;
     L.ex = L.choice + E;
     L.gscore = L.ex + E;
@@ -44,11 +46,98 @@ __host__ __device__ inline RouterSmem router_layout(int H, int E) {
     return L;
 }
 
+// One thread per (token, expert, chunk): partial[t][e][c] = fmaf chain.
+__global__ void __launch_bounds__(256)
+router_partials_kernel(const RouterParams p) {
+    const int nc = (p.H + kGateChunk - 1) / kGateChunk;
+    const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    if (i >= p.T * p.E * nc) return;
+    const int c = (int)(i % nc);
+    const int64_t te = i / nc;
+    const int e = (int)(te % p.E);
+    const int64_t t = te / p.E;
+    const int k0 = c * kGateChunk, k1 = min(p.H, k0 + kGateChunk);
+    const float *w = p.gate_w + (int64_t)e * p.H;
+    float acc = 0.0f;
+    if (k1 - k0 == kGateChunk) {
+#pragma unroll 4
+        for (int j = 0; j < kGateChunk; j += 4) {
+            const float4 xv = load_act4(p.x, p.dtype, t * p.H + k0 + j);
+            const float4 wv = __ldg(reinterpret_cast<const float4 *>(w + k0 + j));
+            acc = __fmaf_rn(xv.x, wv.x, acc);
+            acc = __fmaf_rn(xv.y, wv.y, acc);
+            acc = __fmaf_rn(xv.z, wv.z, acc);
+            acc = __fmaf_rn(xv.w, wv.w, acc);
+        }
+    } else {
+        for (int k = k0; k < k1; ++k)
+            acc = __fmaf_rn(load_act(p.x, p.dtype, t * p.H + k), __ldg(w + k), acc);
+    }
+    p.scratch[i] = acc;
+}
+
+// Tiled logits: CTA = 64 tokens x 64 experts, thread = 4 x 4 logits.
+constexpr int kTileT = 64, kTileE = 64;
+__global__ void __launch_bounds__(256)
+router_logits_kernel(const RouterParams p) {
+    __shared__ float xs[kGateChunk][kTileT + 1];
+    __shared__ float ws[kGateChunk][kTileE + 1];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int64_t t0 = (int64_t)blockIdx.x * kTileT;
+    const int e0 = blockIdx.y * kTileE;
+    float tot[4][4], acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) tot[a][b] = 0.0f;
+    for (int k0 = 0; k0 < p.H; k0 += kGateChunk) {
+        const int kn = min(kGateChunk, p.H - k0);
+        for (int i = tid; i < kTileT * kGateChunk; i += 256) {
+            const int rr = i / kGateChunk, k = i % kGateChunk;
+            const int64_t t = t0 + rr;
+            xs[k][rr] = (t < p.T && k < kn) ? load_act(p.x, p.dtype, t * p.H + k0 + k) : 0.0f;
+            const int e = e0 + rr;
+            ws[k][rr] = (e < p.E && k < kn) ? __ldg(p.gate_w + (int64_t)e * p.H + k0 + k) : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+        for (int k = 0; k < kn; ++k) {
+            float xa[4], wb[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) xa[a] = xs[k][ty * 4 + a];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) wb[b] = ws[k][tx * 4 + b];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = __fmaf_rn(xa[a], wb[b], acc[a][b]);
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) tot[a][b] = __fadd_rn(tot[a][b], acc[a][b]);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int64_t t = t0 + ty * 4 + a;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int e = e0 + tx * 4 + b;
+            if (t < p.T && e < p.E) p.scratch[t * p.E + e] = tot[a][b];
+        }
+    }
+}
+
+// Scoring and selection, one CTA per token; logits from the partials
+// (summed here in chunk order) or from router_logits_kernel.
 __global__ void __launch_bounds__(kRouterThreads)
-router_kernel(const RouterParams p) {
+router_select_kernel(const RouterParams p, int from_partials) {
     extern __shared__ float smem[];
-    const RouterSmem L = router_layout(p.H, p.E);
-    float *xs = smem + L.xs;
+    const RouterSmem L = router_layout(p.E);
     float *part = smem + L.part;
     float *logit = smem + L.logit;
     float *choice = smem + L.choice;
@@ -60,50 +149,19 @@ router_kernel(const RouterParams p) {
 
     const int t = blockIdx.x;
     const int tid = threadIdx.x;
-    const int H = p.H, E = p.E, K = p.K;
-    const int nc = (H + kGateChunk - 1) / kGateChunk;
-
-    // 1. token row -> smem (f32), chunk-padded
-    for (int k = tid; k < nc * kGateChunk; k += kRouterThreads) {
-        float v = k < H ? load_act(p.x, p.dtype, (int64_t)t * H + k) : 0.0f;
-        xs[(k / kGateChunk) * kXStride + (k % kGateChunk)] = v;
-    }
-    for (int e = tid; e < E; e += kRouterThreads) logit[e] = 0.0f;
-    __syncthreads();
-
-    // 2. chunk partials, 32 chunks per pass, then ordered per-expert sums
-    for (int c0 = 0; c0 < nc; c0 += kChunkBatch) {
-        const int cb = min(kChunkBatch, nc - c0);
-        for (int i = tid; i < E * cb; i += kRouterThreads) {
-            const int e = i / cb, c = c0 + i % cb;
-            const int k0 = c * kGateChunk;
-            const int k1 = min(H, k0 + kGateChunk);
-            const float *w = p.gate_w + (int64_t)e * H;
-            const float *xc = xs + c * kXStride;
-            float acc = 0.0f;
-            if (k1 - k0 == kGateChunk && (H % 4) == 0) {
-                const float4 *w4 = reinterpret_cast<const float4 *>(w + k0);
-#pragma unroll 4
-                for (int j = 0; j < kGateChunk / 4; ++j) {
-                    float4 wv = __ldg(w4 + j);
-                    acc = __fmaf_rn(xc[4 * j + 0], wv.x, acc);
-                    acc = __fmaf_rn(xc[4 * j + 1], wv.y, acc);
-                    acc = __fmaf_rn(xc[4 * j + 2], wv.z, acc);
-                    acc = __fmaf_rn(xc[4 * j + 3], wv.w, acc);
-                }
-            } else {
-                for (int k = k0; k < k1; ++k) acc = __fmaf_rn(xc[k - k0], __ldg(w + k), acc);
-            }
-            part[e * kChunkBatch + (c - c0)] = acc;
-        }
-        __syncthreads();
-        for (int e = tid; e < E; e += kRouterThreads) {
-            float tot = logit[e];
-            for (int c = 0; c < cb; ++c) tot = __fadd_rn(tot, part[e * kChunkBatch + c]);
+    const int E = p.E, K = p.K;
+    const int nc = (p.H + kGateChunk - 1) / kGateChunk;
+    for (int e = tid; e < E; e += kRouterThreads) {
+        if (from_partials) {
+            const float *pp = p.scratch + ((int64_t)t * E + e) * nc;
+            float tot = 0.0f;
+            for (int c = 0; c < nc; ++c) tot = __fadd_rn(tot, pp[c]);
             logit[e] = tot;
+        } else {
+            logit[e] = p.scratch[(int64_t)t * E + e];
         }
-        __syncthreads();
     }
+    __syncthreads();
 
     // 3. scores for the selection
     const bool sigm = p.scoring == 1;
@@ -211,22 +269,46 @@ router_kernel(const RouterParams p) {
 }  // namespace
 
 size_t router_smem_bytes(int H, int E) {
-    RouterSmem L = router_layout(H, E);
+    (void)H;
+    RouterSmem L = router_layout(E);
     return (size_t)(L.misc + 4 + 256 + 64) * sizeof(float);
+}
+
+constexpr int64_t kPartialsMaxLogits = 32768;  // T * E up to which the partials path runs
+
+bool router_uses_partials(int64_t T, int E) { return T * E <= kPartialsMaxLogits; }
+
+// Enough for every token count up to T on either path (monotonic in T, so a
+// buffer reserved for a larger batch serves every smaller one).
+size_t router_scratch_floats(int64_t T, int H, int E) {
+    const int64_t nc = (H + kGateChunk - 1) / kGateChunk;
+    const int64_t logits = T * E;
+    const int64_t parts = (logits < kPartialsMaxLogits ? logits : kPartialsMaxLogits) * nc;
+    return (size_t)(parts > logits ? parts : logits);
 }
 
 cudaError_t launch_router(const RouterParams &p, cudaStream_t s) {
     if (p.T == 0) return cudaSuccess;
-    size_t smem = router_smem_bytes(p.H, p.E);
+    const bool parts = router_uses_partials(p.T, p.E);
+    if (parts) {
+        const int nc = (p.H + kGateChunk - 1) / kGateChunk;
+        const int64_t n = p.T * p.E * nc;
+        router_partials_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p);
+    } else {
+        dim3 grid((unsigned)((p.T + kTileT - 1) / kTileT), (unsigned)((p.E + kTileE - 1) / kTileE));
+        router_logits_kernel<<<grid, 256, 0, s>>>(p);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const size_t smem = router_smem_bytes(p.H, p.E);
     static size_t smem_set = 0;  // raise the opt-in limit only when needed
     if (smem > smem_set) {
-        cudaError_t e = cudaFuncSetAttribute(router_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+        e = cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
         if (e != cudaSuccess) return e;
         smem_set = smem;
     }
-    router_kernel<<<(unsigned)p.T, kRouterThreads, smem, s>>>(p);
+    router_select_kernel<<<(unsigned)p.T, kRouterThreads, smem, s>>>(p, parts ? 1 : 0);
     return cudaGetLastError();
 }
 

@@ -198,16 +198,35 @@ def test_sigmoid_group_limited_routing_bit_exact():
     assert rel_err(out.cpu().numpy(), ro) <= F32_TOL
 
 
-def test_route_only_matches_oracle_bit_exact():
+# T=50 takes the per-chunk partials path, T=700 (T*E > 32768) the tiled
+# logits path with a ragged last tile; both must give the same bits.
+@pytest.mark.parametrize("T,reserve", [(50, 0), (700, 0), (32, 4096)])
+def test_route_only_matches_oracle_bit_exact(T, reserve):
     cfg = MoEConfig(64, 6, 2048, 128)
     experts, _, gw = helpers.synth_layer(64, 2048, 128, seed=3, device="cuda")
     layer = QMoELayer(cfg, gw, experts)
-    x = torch.randn(50, 2048, generator=torch.Generator().manual_seed(9))
+    if reserve:
+        layer.reserve(reserve)                 # scratch sized for the big batch
+    x = torch.randn(T, 2048, generator=torch.Generator().manual_seed(9))
     idx, w = layer.route(x.cuda())
     logits = qo.gate_logits(x.numpy(), gw.cpu().numpy())
     ri, rw = qo.route(qo_cfg(cfg), logits)
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
     np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=1e-6, atol=0)
+
+
+@pytest.mark.parametrize("T", [19, 1100])
+def test_sigmoid_routing_both_logit_paths_bit_exact(T):
+    cfg = MoEConfig(32, 8, 256, 128, scoring=capi.QMOE_SCORING_SIGMOID, n_group=8,
+                    topk_group=4, norm_topk_prob=True, routed_scaling_factor=2.5)
+    experts, _, gw = helpers.synth_layer(32, 256, 128, seed=23, device="cuda")
+    layer = QMoELayer(cfg, gw, experts)
+    x = torch.randn(T, 256, generator=torch.Generator().manual_seed(T)).bfloat16()
+    idx, w = layer.route(x.cuda())
+    logits = qo.gate_logits(x.float().numpy(), gw.cpu().numpy())
+    ri, rw = qo.route(qo_cfg(cfg), logits)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_array_equal(w.cpu().numpy(), rw)
 
 
 def test_forward_routed_matches_oracle():
