@@ -241,13 +241,29 @@ QMOE_API int qmoe_packed_forward_noalloc(int device, void *stream, const uint8_t
                                          int64_t in_features, const float *x,
                                          int64_t batch, float *y);
 
+/* ---- expert-product path -------------------------------------------------- */
+
+/* Which kernels form the expert products of a forward.  AUTO takes the
+ * prefill GEMM for bf16 activations once the routed positions per expert
+ * (or the batch, for a shared-only pass) reach 16, and the decode GEMV
+ * otherwise.  DECODE: integer-limb GEMV, products exact, f32 or bf16
+ * activations.  PREFILL: tcgen05 bf16 GEMM with f32 accumulation and bf16
+ * SwiGLU rows, bf16 activations only (an f32 forward then fails with
+ * QMOE_ERR_UNSUPPORTED); needs hidden % 128 == 0 and intermediate dims
+ * % 64 == 0.  Replaces nothing in qmoe-rs, whose path is one. */
+#define QMOE_PATH_AUTO 0
+#define QMOE_PATH_DECODE 1
+#define QMOE_PATH_PREFILL 2
+QMOE_API int qmoe_layer_set_path(qmoe_layer *layer, int path);
+
 /* ---- tracing ----------------------------------------------------------- */
 
 /* Stage timing, the device-side counterpart of the Instant-based breakdown
  * of qmoe-rs's bench harness (benches/moe_layer.rs:105-195).  While enabled,
  * each forward records CUDA events on the context's stream around its
- * stages: 0 router, 1 permute, 2 activation limbs for gate/up, 3 gate/up +
- * SwiGLU GEMV, 4 limbs for down, 5 down GEMV, 6 combine. */
+ * stages: 0 router, 1 permute, 2 activation limbs for gate/up (prefill:
+ * the bf16 row gather), 3 gate/up + SwiGLU, 4 limbs for down (prefill:
+ * none), 5 down, 6 combine. */
 QMOE_API int qmoe_layer_set_profiling(qmoe_layer *layer, int enable);
 /* Waits for the last profiled forward and writes min(capacity, 7) stage
  * durations in milliseconds to ms; *count receives the number written. */

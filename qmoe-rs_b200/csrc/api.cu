@@ -103,6 +103,9 @@ int check_align(const void *p, int ptr_kind, const char *name) {
 }
 
 constexpr int kDecodeTok = 5;   // tokens per work item of the decode kernels
+// Auto path: the prefill GEMM once the routed positions per expert segment
+// (or the batch, for a shared-only pass) reach this many.
+constexpr int64_t kPrefillMinRows = 16;
 
 // A kernel whose bounded wait timed out leaves a flag in device memory; report
 // (and clear) it at the next host synchronisation point.
@@ -156,6 +159,13 @@ struct qmoe_layer {
     DevBuf x_in, io_out, user_idx, user_w;
     DevBuf xq1, meta1, xq2, meta2, router_scratch;
     CUtensorMap tm_xq1, tm_xq2;
+    // prefill path: gate/up maps with 64-row boxes, bf16 activation / SwiGLU
+    // rows (16-element blocks permuted) and their 128-byte-swizzled maps
+    bool prefill_ok = false;
+    int path = QMOE_PATH_AUTO;
+    CUtensorMap tm_pw[2], tm_pws[2];
+    DevBuf xg, hb;
+    CUtensorMap tm_xg, tm_hb;
     // tracing
     bool profiling = false;
     cudaEvent_t ev[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -386,7 +396,8 @@ int qmoe_layer_destroy(qmoe_layer *L) {
     DevBuf *bufs[] = {&L->topk_idx, &L->topk_w, &L->assign_pos, &L->pos_tok,
                       &L->seg_off, &L->groups, &L->ngroups, &L->h, &L->y,
                       &L->x_in, &L->io_out, &L->user_idx, &L->user_w,
-                      &L->xq1, &L->meta1, &L->xq2, &L->meta2, &L->router_scratch};
+                      &L->xq1, &L->meta1, &L->xq2, &L->meta2, &L->router_scratch,
+                      &L->xg, &L->hb};
     for (DevBuf *b : bufs) release(*b);
     delete L;
     return QMOE_OK;
@@ -450,6 +461,21 @@ static int layer_create_impl(qmoe_layer *L, const float *gate_weight, const floa
             if (!make_tmap_u8(&L->tm_ws[m], L->ws[m], (uint64_t)(skin[m] / 4), (uint64_t)srows[m],
                               64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
                 return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for shared matrix %d", m);
+    }
+    // prefill kernels: K blocks of 64 everywhere, down tiles of 128 rows
+    L->prefill_ok = H % 128 == 0 && I % 64 == 0 &&
+                    (!L->has_shared || c.shared_intermediate_dim % 64 == 0);
+    if (L->prefill_ok) {
+        for (int m = 0; m < 2; ++m) {
+            if (!make_tmap_u8(&L->tm_pw[m], L->w[m], (uint64_t)(H / 4), (uint64_t)(I * El), 64, 64,
+                              CU_TENSOR_MAP_SWIZZLE_64B))
+                return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for expert matrix %d", m);
+            L->tm_pws[m] = L->tm_pw[m];
+            if (L->has_shared &&
+                !make_tmap_u8(&L->tm_pws[m], L->ws[m], (uint64_t)(H / 4),
+                              (uint64_t)c.shared_intermediate_dim, 64, 64, CU_TENSOR_MAP_SWIZZLE_64B))
+                return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for shared matrix %d", m);
+        }
     }
     {
         int dev = 0;
@@ -527,6 +553,15 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
     QTRY(grow(L->meta1, sizeof(longlong2) * npos));
     QTRY(grow(L->meta2, sizeof(longlong2) * npos));
     QTRY(grow(L->router_scratch, sizeof(float) * router_scratch_floats(T, c.hidden_dim, c.num_experts)));
+    if (L->prefill_ok) {
+        QTRY(grow(L->xg, 2 * (size_t)npos * H));
+        QTRY(grow(L->hb, 2 * (size_t)npos * Imax));
+        if (!make_tmap_bf16(&L->tm_xg, L->xg.p, (uint64_t)H, (uint64_t)npos, 2 * (uint64_t)H, 64, 64,
+                            CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_tmap_bf16(&L->tm_hb, L->hb.p, (uint64_t)Imax, (uint64_t)npos, 2 * (uint64_t)Imax,
+                            64, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+            return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill rows");
+    }
     if (!make_tmap_u8(&L->tm_xq1, L->xq1.p, (uint64_t)L->kp1, (uint64_t)(npos * 3), 128, 16,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_tmap_u8(&L->tm_xq2, L->xq2.p, (uint64_t)L->kp2, (uint64_t)(npos * 3), 128, 16,
@@ -581,6 +616,96 @@ static int run_router(qmoe_layer *L, const void *xd, int dtype, int64_t T) {
 
 // Experts for routed assignments (topk ids relative to e_begin) plus, when
 // with_shared, the shared expert over all T rows; then the combine.
+// Weighted sum of each token's expert rows in ascending expert order, plus
+// the shared expert's row (src/moe.rs:117-125, src/model.rs:386-389).
+static int run_combine(qmoe_layer *L, int64_t T, const int32_t *topk_idx, const float *topk_w,
+                       bool with_shared, void *outd, int dtype, int accumulate) {
+    const qmoe_moe_config &c = L->cfg;
+    CombineParams cp{};
+    cp.y = L->y.as<float>();
+    cp.assign_pos = L->assign_pos.as<int32_t>();
+    cp.topk_idx = topk_idx;
+    cp.topk_w = topk_w;
+    cp.T = T;
+    cp.K = c.top_k;
+    cp.H = c.hidden_dim;
+    cp.y_shared = with_shared ? L->y.as<float>() + T * c.top_k * c.hidden_dim : nullptr;
+    cp.accumulate = accumulate;
+    cp.out = outd;
+    cp.out_dtype = dtype;
+    mark(L, 6);
+    QTRY_CUDA(launch_combine(cp, L->ctx->stream));
+    mark(L, 7);
+    return QMOE_OK;
+}
+
+// Prefill expert products: gather the bf16 rows of every position, gate/up
+// GEMM with SwiGLU into bf16 rows, down GEMM into f32 rows of y.
+static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, bool with_shared,
+                       const int32_t *n_valid, int *err) {
+    const qmoe_moe_config &c = L->cfg;
+    cudaStream_t st = L->ctx->stream;
+    const int64_t TK = T * c.top_k;
+    const int64_t Imax = c.shared_intermediate_dim > c.intermediate_dim ? c.shared_intermediate_dim
+                                                                        : c.intermediate_dim;
+    GatherParams gp{};
+    gp.x = xd;
+    gp.H = c.hidden_dim;
+    gp.pos_tok = L->pos_tok.as<int32_t>();
+    gp.n_valid = n_valid;
+    gp.shared_base = TK;
+    gp.npos = npos;
+    gp.xg = L->xg.p;
+    mark(L, 2);
+    QTRY_CUDA(launch_gather_bf16(gp, st));
+    mark(L, 3);
+
+    QgemmMaps m0;
+    m0.w0 = L->tm_pw[0];
+    m0.w1 = L->tm_pw[1];
+    m0.s0 = L->tm_pws[0];
+    m0.s1 = L->tm_pws[1];
+    m0.b = L->tm_xg;
+    QgemmParams g0{};
+    g0.groups = L->groups.as<int4>();
+    g0.n_groups = L->ngroups.as<int32_t>();
+    g0.rows = c.intermediate_dim;
+    g0.K = c.hidden_dim;
+    g0.rows_s = with_shared ? c.shared_intermediate_dim : 0;
+    g0.K_s = c.hidden_dim;
+    g0.s[0] = L->s[0];
+    g0.s[1] = L->s[1];
+    g0.s_stride = c.intermediate_dim;
+    g0.ss[0] = L->ss[0];
+    g0.ss[1] = L->ss[1];
+    g0.out = L->hb.p;
+    g0.out_ld = Imax;
+    g0.err = err;
+    QTRY_CUDA(launch_qgemm_prefill(0, m0, g0, L->sm_count, st));
+    mark(L, 4);
+    mark(L, 5);
+
+    QgemmMaps m1;
+    m1.w0 = m1.w1 = L->tm_w[2];
+    m1.s0 = m1.s1 = L->tm_ws[2];
+    m1.b = L->tm_hb;
+    QgemmParams g1{};
+    g1.groups = g0.groups;
+    g1.n_groups = g0.n_groups;
+    g1.rows = c.hidden_dim;
+    g1.K = c.intermediate_dim;
+    g1.rows_s = with_shared ? c.hidden_dim : 0;
+    g1.K_s = with_shared ? c.shared_intermediate_dim : c.intermediate_dim;
+    g1.s[0] = g1.s[1] = L->s[2];
+    g1.s_stride = c.hidden_dim;
+    g1.ss[0] = g1.ss[1] = L->ss[2];
+    g1.out = L->y.p;
+    g1.out_ld = c.hidden_dim;
+    g1.err = err;
+    QTRY_CUDA(launch_qgemm_prefill(1, m1, g1, L->sm_count, st));
+    return QMOE_OK;
+}
+
 static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
                        const int32_t *topk_idx, const float *topk_w, int e_begin,
                        bool with_shared, void *outd, int accumulate) {
@@ -590,13 +715,26 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     const int64_t TK = T * K;
     const int64_t Imax = c.shared_intermediate_dim > c.intermediate_dim ? c.shared_intermediate_dim
                                                                         : c.intermediate_dim;
+    // expert products: tcgen05 bf16 GEMM for large bf16 batches, the exact
+    // integer-limb GEMV otherwise
+    bool prefill = false;
+    if (L->path == QMOE_PATH_PREFILL) {
+        if (!L->prefill_ok || dtype != QMOE_DTYPE_BF16)
+            return fail(QMOE_ERR_UNSUPPORTED,
+                        "the prefill path needs bf16 activations, hidden %% 128 == 0 and "
+                        "intermediate dims %% 64 == 0");
+        prefill = true;
+    } else if (L->path == QMOE_PATH_AUTO && L->prefill_ok && dtype == QMOE_DTYPE_BF16) {
+        const int64_t per_seg = K > 0 ? T * K / (L->e_count > 0 ? L->e_count : 1) : T;
+        prefill = per_seg >= kPrefillMinRows;
+    }
     PermuteParams pp{};
     pp.topk_idx = topk_idx;
     pp.T = T;
     pp.K = K;
     pp.e_begin = e_begin;
     pp.e_count = L->e_count;
-    pp.chunk = kDecodeTok;
+    pp.chunk = prefill ? kPrefillTile : kDecodeTok;
     pp.with_shared = with_shared ? 1 : 0;
     pp.seg_off = L->seg_off.as<int32_t>();
     pp.assign_pos = L->assign_pos.as<int32_t>();
@@ -609,6 +747,10 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     const int64_t npos = TK + (with_shared ? T : 0);
     const int32_t *n_valid = L->seg_off.as<int32_t>() + L->e_count;
     int *err = device_error_flag();
+    if (prefill) {
+        QTRY(run_prefill(L, xd, T, npos, with_shared, n_valid, err));
+        return run_combine(L, T, topk_idx, topk_w, with_shared, outd, dtype, accumulate);
+    }
 
     // gate/up: activations -> limbs, then the tensor-core GEMV with SwiGLU
     QuantParams q1{};
@@ -691,22 +833,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     g1.err = err;
     QTRY_CUDA(launch_qgemv_imma(1, m1, g1, L->sm_count, st));
 
-    CombineParams cp{};
-    cp.y = L->y.as<float>();
-    cp.assign_pos = L->assign_pos.as<int32_t>();
-    cp.topk_idx = topk_idx;
-    cp.topk_w = topk_w;
-    cp.T = T;
-    cp.K = K;
-    cp.H = c.hidden_dim;
-    cp.y_shared = with_shared ? L->y.as<float>() + TK * c.hidden_dim : nullptr;
-    cp.accumulate = accumulate;
-    cp.out = outd;
-    cp.out_dtype = dtype;
-    mark(L, 6);
-    QTRY_CUDA(launch_combine(cp, st));
-    mark(L, 7);
-    return QMOE_OK;
+    return run_combine(L, T, topk_idx, topk_w, with_shared, outd, dtype, accumulate);
 }
 
 static int finish_out(qmoe_layer *L, void *user, const void *dev, size_t bytes, int ptr_kind) {
@@ -859,6 +986,17 @@ int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T
         QTRY_CUDA(cudaStreamSynchronize(st));
         QTRY(check_device_error());
     }
+    return QMOE_OK;
+}
+
+int qmoe_layer_set_path(qmoe_layer *L, int path) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    if (path != QMOE_PATH_AUTO && path != QMOE_PATH_DECODE && path != QMOE_PATH_PREFILL)
+        return fail(QMOE_ERR_INVALID, "unknown path %d", path);
+    if (path == QMOE_PATH_PREFILL && !L->prefill_ok)
+        return fail(QMOE_ERR_UNSUPPORTED,
+                    "the prefill path needs hidden %% 128 == 0 and intermediate dims %% 64 == 0");
+    L->path = path;
     return QMOE_OK;
 }
 

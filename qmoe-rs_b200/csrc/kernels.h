@@ -138,6 +138,48 @@ int *device_error_flag();
 bool make_tmap_u8(CUtensorMap *tm, const void *base, uint64_t row_bytes, uint64_t rows,
                   uint32_t box_bytes, uint32_t box_rows, int swizzle);
 
+// ---- prefill grouped GEMM (tcgen05 kind::f16; 2-bit -> bf16 into TMEM) ---
+// Activation and SwiGLU rows are stored with every 16-element block in the
+// order kPrefillPerm16 (position -> element), the order in which one shift
+// and one mask split a 32-bit word of packed codes into bf16 pairs.
+struct GatherParams {
+    const void *x;               // [T, H] bf16
+    int64_t H;
+    const int32_t *pos_tok;      // routed position -> token
+    const int32_t *n_valid;      // routed positions in use (device)
+    int64_t shared_base;         // first shared position; shared rows = tokens 0..T-1
+    int64_t npos;                // positions (routed slots + shared rows)
+    void *xg;                    // [npos, H] bf16, blocks permuted
+};
+cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s);
+
+struct QgemmMaps {
+    CUtensorMap w0, w1;          // routed 2-bit matrices (mode 0: gate, up; mode 1: down)
+    CUtensorMap s0, s1;          // shared-expert matrices (copies of w0/w1 if none)
+    CUtensorMap b;               // bf16 activation rows [npos][ld], 128-byte swizzle
+};
+struct QgemmParams {
+    const int4 *groups;          // (segment, first position, count <= 256)
+    const int32_t *n_groups;     // [0] routed groups, [1] shared groups
+    int rows, K;                 // routed matrices: rows per expert, reduction length
+    int rows_s, K_s;             // shared matrices (rows_s = 0: none)
+    const float *s[2];           // routed row scales, expert stride s_stride
+    int64_t s_stride;
+    const float *ss[2];          // shared row scales
+    void *out;                   // mode 0: bf16 SwiGLU rows (blocks permuted); mode 1: f32
+    int64_t out_ld;              // elements per output row
+    int *err;                    // device error word
+};
+cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmParams &p, int grid,
+                                 cudaStream_t s);
+size_t qgemm_prefill_smem_bytes();
+constexpr int kPrefillTile = 256;  // tokens per work item (group chunk)
+
+// Host: a 2-D bf16 tensor map over rows of `cols` elements, `row_stride`
+// bytes apart.
+bool make_tmap_bf16(CUtensorMap *tm, const void *base, uint64_t cols, uint64_t rows,
+                    uint64_t row_stride, uint32_t box_cols, uint32_t box_rows, int swizzle);
+
 // ---- combine -----------------------------------------------------------
 struct CombineParams {
     const float *y;              // [positions, H] expert outputs

@@ -1,0 +1,454 @@
+// qgemm_prefill.cu -- prefill-sized grouped expert products on tcgen05.
+//
+// Replaces, for large batches of bf16 activations, the per-assignment GEMVs
+// of QMoELayer::forward (qmoe-rs src/moe.rs:89-125 via
+// PackedQMoETensor::forward_simd, src/tensor.rs:64-95, and
+// simd::fused_dequantize_and_dot, src/simd.rs:6-45) and the shared expert's
+// batched GEMVs (src/model.rs:325-347).
+//
+// Arithmetic: weight = (code - 1) * scale(row) (src/simd.rs:28-31, :44).  The
+// codes minus one are exact in bf16, the bf16 activations are exact, so the
+// tensor core forms sum_k (code-1) x_k with f32 accumulation and the epilogue
+// applies the row scale in f32.  The SwiGLU rows feeding the down product
+// are rounded to bf16 (the only rounding beyond f32 accumulation order).
+//
+// Work item = one group (<= 256 positions of one expert segment) x one tile
+// of 128 output rows: in mode 0 the 128 rows are 64 gate rows and the 64
+// matching up rows, interleaved (TMEM lane 2i = gate row i, 2i+1 = up row i)
+// so that the SwiGLU pairs sit in neighbouring lanes; in mode 1 they are 128
+// down rows.  D[128 x N] += A[128 x 16] * B[N x 16]^T per instruction, with
+//   A  the dequantised weights, written by the dequant warps straight into
+//      tensor memory (32 columns per 64-element K block, 8-deep ring);
+//   B  the activation rows of the group, [N x 64] bf16 K blocks staged by
+//      TMA with 128-byte swizzle (4-deep ring, 64-row boxes);
+//   D  f32 in tensor memory columns 256..511.
+// Persistent grid, one CTA per SM, fourteen warps:
+//   warp 0      TMA producer (packed weight stages of 256 K, activation K
+//               blocks);
+//   warp 1      TMEM owner and MMA issuer (one thread);
+//   warps 2-5   dequant: one TMEM lane (weight row) per thread, 64 codes per
+//               K block: ((w >> s) & 0x00030003) | 0x43004300 is the bf16
+//               pair (128 + c_lo, 128 + c_hi), one bf16x2 FMA subtracts 129;
+//   warps 6-13  epilogue: two warps per TMEM lane quarter, alternate 32-column
+//               chunks; scales, SwiGLU (mode 0) or f32 rows (mode 1).
+// Every wait is bounded; on a time-out the kernel flags the device error
+// word, drains its copies and MMAs (again bounded), frees TMEM and returns.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace qmoe {
+namespace {
+
+using namespace sm100;
+
+constexpr int kWarps = 14;
+constexpr int kThreads = kWarps * 32;
+constexpr int kEpiWarp0 = 6;
+constexpr int kEpiWarps = 8;
+constexpr int kNW = 4;                       // packed-weight stages
+constexpr int kWStage = 8192;                // 128 rows x 64 B (256 codes per row)
+constexpr int kNB = 4;                       // activation K-block stages
+constexpr int kBBox = 64 * 128;              // one 64-row x 128 B box
+constexpr int kBStage = kPrefillTile * 128;  // 256 rows x 64 bf16
+constexpr int kNA = 8;                       // TMEM A stages (32 columns each)
+constexpr uint32_t kDCol = 256;              // accumulator columns 256..511
+constexpr uint32_t kTmemCols = 512;
+constexpr int kItemCache = 256;
+
+struct Smem {
+    uint64_t wfull[kNW], wempty[kNW];
+    uint64_t bfull[kNB], bempty[kNB];
+    uint64_t afull[kNA], aempty[kNA];
+    uint64_t dfull, dempty, drain;
+    uint32_t tmem_base;
+    int abort;
+    int4 items[kItemCache];
+};
+
+struct Item {
+    int seg, pos0, count, mt;
+    bool shared;
+};
+
+QMOE_DEV Item decode_item(const QgemmParams &p, int item, int nr, int mt_r, int mt_s) {
+    Item it;
+    int g;
+    if (item < nr * mt_r) {
+        g = item / mt_r;
+        it.mt = item % mt_r;
+        it.shared = false;
+    } else {
+        const int j = item - nr * mt_r;
+        g = nr + j / mt_s;
+        it.mt = j % mt_s;
+        it.shared = true;
+    }
+    const int4 d = p.groups[g];
+    it.seg = d.x;
+    it.pos0 = d.y;
+    it.count = d.z;
+    return it;
+}
+
+// (128 + c_lo, 128 + c_hi) - (129, 129) = (c_lo - 1, c_hi - 1), exact in bf16
+QMOE_DEV uint32_t codes_to_bf16x2(uint32_t biased) {
+    uint32_t r;
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(biased), "r"(0x3F803F80u), "r"(0xC301C301u));
+    return r;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                     const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_s1,
+                     const __grid_constant__ CUtensorMap tm_b, const QgemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *bring = base;                         // kNB x 32 KB activation stages
+    uint8_t *wring = bring + kNB * kBStage;        // kNW x 8 KB packed weights
+    Smem *S = reinterpret_cast<Smem *>(wring + kNW * kWStage);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rows_tile = MODE == 0 ? 64 : 128;    // matrix rows per item (per matrix)
+    const int mt_r = (p.rows + rows_tile - 1) / rows_tile;
+    const int mt_s = p.rows_s > 0 ? (p.rows_s + rows_tile - 1) / rows_tile : 1;
+    const int nr = p.n_groups[0], ns = p.n_groups[1];
+    const int total = nr * mt_r + ns * mt_s;
+    const int my_items =
+        total > (int)blockIdx.x ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    if (my_items == 0) return;  // uniform across the CTA, before any barrier or TMEM use
+
+    if (tid == 0) {
+        for (int i = 0; i < kNW; ++i) {
+            mbar_init(&S->wfull[i], 1);
+            mbar_init(&S->wempty[i], 4);
+        }
+        for (int i = 0; i < kNB; ++i) {
+            mbar_init(&S->bfull[i], 1);
+            mbar_init(&S->bempty[i], 1);
+        }
+        for (int i = 0; i < kNA; ++i) {
+            mbar_init(&S->afull[i], 4);
+            mbar_init(&S->aempty[i], 1);
+        }
+        mbar_init(&S->dfull, 1);
+        mbar_init(&S->dempty, kEpiWarps);
+        mbar_init(&S->drain, 1);
+        S->abort = 0;
+        fence_mbar_init();
+    }
+    for (int i = tid; i < my_items && i < kItemCache; i += kThreads) {
+        const Item it = decode_item(p, (int)blockIdx.x + i * (int)gridDim.x, nr, mt_r, mt_s);
+        S->items[i] = make_int4(it.seg, it.pos0, it.count, it.mt | (it.shared ? (1 << 30) : 0));
+    }
+    if (warp == 1) {
+        tmem_alloc(&S->tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S->tmem_base;
+    volatile int *abort = &S->abort;
+
+    auto item_at = [&](int i) -> Item {
+        if (i < kItemCache) {
+            const int4 v = S->items[i];
+            Item it;
+            it.seg = v.x;
+            it.pos0 = v.y;
+            it.count = v.z;
+            it.mt = v.w & ((1 << 30) - 1);
+            it.shared = (v.w >> 30) & 1;
+            return it;
+        }
+        return decode_item(p, (int)blockIdx.x + i * (int)gridDim.x, nr, mt_r, mt_s);
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------- TMA
+        if (lane == 0) {
+            tma_prefetch_desc(&tm_w0);
+            if (MODE == 0) tma_prefetch_desc(&tm_w1);
+            tma_prefetch_desc(&tm_b);
+            if (p.rows_s > 0) {
+                tma_prefetch_desc(&tm_s0);
+                if (MODE == 0) tma_prefetch_desc(&tm_s1);
+            }
+            uint32_t uw = 0, ub = 0;
+            bool ok = true;
+            for (int i = 0; ok && i < my_items; ++i) {
+                const Item it = item_at(i);
+                const int K = it.shared ? p.K_s : p.K;
+                const int nkb = K / 64;
+                const int nbox = (it.count + 63) / 64;
+                const CUtensorMap *m0 = it.shared ? &tm_s0 : &tm_w0;
+                const CUtensorMap *m1 = it.shared ? &tm_s1 : &tm_w1;
+                const int rows = it.shared ? p.rows_s : p.rows;
+                const int y = (it.shared ? 0 : it.seg * rows) + it.mt * rows_tile;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if ((kb & 3) == 0) {
+                        const uint32_t s = uw % kNW;
+                        if (!(ok = mbar_wait(&S->wempty[s], ((uw / kNW) & 1) ^ 1, abort, p.err)))
+                            break;
+                        mbar_arrive_expect_tx(&S->wfull[s], kWStage);
+                        uint8_t *dst = wring + s * kWStage;
+                        tma_load_2d(dst, m0, &S->wfull[s], (kb >> 2) * 64, y);
+                        if (MODE == 0) tma_load_2d(dst + kWStage / 2, m1, &S->wfull[s], (kb >> 2) * 64, y);
+                        ++uw;
+                    }
+                    const uint32_t s = ub % kNB;
+                    if (!(ok = mbar_wait(&S->bempty[s], ((ub / kNB) & 1) ^ 1, abort, p.err))) break;
+                    mbar_arrive_expect_tx(&S->bfull[s], (uint32_t)(nbox * kBBox));
+                    for (int bx = 0; bx < nbox; ++bx)
+                        tma_load_2d(bring + s * kBStage + bx * kBBox, &tm_b, &S->bfull[s], kb * 64,
+                                    it.pos0 + 64 * bx);
+                    ++ub;
+                }
+            }
+            if (!ok) {
+                // let the copies already issued land before the CTA exits
+                for (uint32_t u = uw > kNW ? uw - kNW : 0; u < uw; ++u)
+                    for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
+                        if (mbar_try_wait(&S->wfull[u % kNW], (u / kNW) & 1)) break;
+                for (uint32_t u = ub > kNB ? ub - kNB : 0; u < ub; ++u)
+                    for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
+                        if (mbar_try_wait(&S->bfull[u % kNB], (u / kNB) & 1)) break;
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------- MMA
+        if (lane == 0) {
+            uint32_t ua = 0, ub = 0;
+            bool ok = true, issued = false;
+            const uint64_t bd0 = smem_desc(smem_u32(bring), 16, 1024, 2);
+            const uint32_t bd_lo = (uint32_t)bd0, bd_hi = (uint32_t)(bd0 >> 32);
+            for (int i = 0; ok && i < my_items; ++i) {
+                const Item it = item_at(i);
+                const int K = it.shared ? p.K_s : p.K;
+                const int nkb = K / 64;
+                const int N = (it.count + 15) & ~15;
+                const uint32_t idesc = idesc_bf16(128, N);
+                if (!(ok = mbar_wait(&S->dempty, (i & 1) ^ 1, abort, p.err))) break;
+                tc_fence_after();
+                for (int kb = 0; kb < nkb; ++kb, ++ua, ++ub) {
+                    const uint32_t sa = ua % kNA, sb = ub % kNB;
+                    if (!(ok = mbar_wait(&S->afull[sa], (ua / kNA) & 1, abort, p.err))) break;
+                    if (!(ok = mbar_wait(&S->bfull[sb], (ub / kNB) & 1, abort, p.err))) break;
+                    tc_fence_after();
+                    const uint32_t lo = bd_lo + (uint32_t)((sb * kBStage) >> 4);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_bf16_ts_lohi(tmem + kDCol, tmem + sa * 32 + 8 * kk, lo + 2 * kk, bd_hi,
+                                         idesc, (kb | kk) != 0);
+                    issued = true;
+                    mma_commit(&S->aempty[sa]);
+                    mma_commit(&S->bempty[sb]);
+                }
+                if (!ok) break;
+                mma_commit(&S->dfull);
+            }
+            // every MMA issued so far completes before TMEM is freed
+            if (issued) {
+                mma_commit(&S->drain);
+                for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
+                    if (mbar_try_wait(&S->drain, 0)) break;
+            }
+        }
+    } else if (warp < kEpiWarp0) {
+        // ---------------------------------------------------------- dequant
+        const int q = warp & 3;                       // TMEM lane quarter
+        const int L = q * 32 + lane;                  // A row = TMEM lane
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        // packed row in the weight stage: mode 0 gate row L/2 (even L) or up
+        // row L/2 (odd L), each a 64-row box; mode 1 down row L
+        const int r = MODE == 0 ? (L >> 1) : L;
+        const int box_off = MODE == 0 ? (L & 1) * (kWStage / 2) : 0;
+        const int sw = (r >> 1) & 3;                  // 64-byte swizzle of row r
+        uint32_t uw = 0, ua = 0;
+        bool ok = true;
+        for (int i = 0; ok && i < my_items; ++i) {
+            const Item it = item_at(i);
+            const int K = it.shared ? p.K_s : p.K;
+            const int nkb = K / 64;
+            for (int kb = 0; kb < nkb; ++kb, ++ua) {
+                const uint32_t s = uw % kNW;
+                if ((kb & 3) == 0)
+                    if (!(ok = mbar_wait_warp(&S->wfull[s], (uw / kNW) & 1, abort, p.err))) break;
+                const uint4 v = *reinterpret_cast<const uint4 *>(wring + s * kWStage + box_off +
+                                                                 r * 64 + 16 * ((kb & 3) ^ sw));
+                if ((kb & 3) == 3 || kb == nkb - 1) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S->wempty[s]);
+                    ++uw;
+                }
+                const uint32_t sa = ua % kNA;
+                if (!(ok = mbar_wait_warp(&S->aempty[sa], ((ua / kNA) & 1) ^ 1, abort, p.err))) break;
+                tc_fence_after();
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+                uint32_t regs[32];
+#pragma unroll
+                for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+#pragma unroll
+                        for (int pp = 0; pp < 2; ++pp)
+                            regs[8 * wi + 2 * j + pp] = codes_to_bf16x2(
+                                ((w4[wi] >> (2 * j + 8 * pp)) & 0x00030003u) | 0x43004300u);
+                tmem_st_x32(tmem + lane_addr + sa * 32, regs);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S->afull[sa]);
+            }
+        }
+    } else {
+        // -------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int half = (warp - kEpiWarp0) >> 2;     // which 32-column chunks
+        const int L = q * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        bool ok = true;
+        for (int i = 0; ok && i < my_items; ++i) {
+            const Item it = item_at(i);
+            const int rows = it.shared ? p.rows_s : p.rows;
+            const int nch = (it.count + 31) / 32;
+            int row;
+            float scale;
+            if (MODE == 0) {
+                row = it.mt * 64 + (L >> 1);
+                const bool up = L & 1;
+                const float *sc = it.shared ? (up ? p.ss[1] : p.ss[0])
+                                            : (up ? p.s[1] : p.s[0]) + (int64_t)it.seg * p.s_stride;
+                scale = row < rows ? __ldg(sc + row) : 0.0f;
+            } else {
+                row = it.mt * 128 + L;
+                const float *sc = it.shared ? p.ss[0] : p.s[0] + (int64_t)it.seg * p.s_stride;
+                scale = row < rows ? __ldg(sc + row) : 0.0f;
+            }
+            if (!(ok = mbar_wait_warp(&S->dfull, i & 1, abort, p.err))) break;
+            tc_fence_after();
+            bool released = false;
+            for (int c = half; c < nch; c += 2) {
+                uint32_t v[32];
+                tmem_ld_x32(tmem + lane_addr + kDCol + 32 * c, v);
+                tmem_wait_ld();
+                if (c + 2 >= nch) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S->dempty);
+                    released = true;
+                }
+                if (MODE == 0) {
+                    // lane pair (2i, 2i+1) = (gate, up) of row i: the even lane
+                    // finishes columns 0-15 of the chunk, the odd lane 16-31
+                    const bool odd = L & 1;
+                    const int hpos = (row & ~15) | (4 * (row & 3) + 2 * ((row >> 2) & 1) + ((row >> 3) & 1));
+                    __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(p.out) + hpos;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float mine_lo = __fmul_rn(__uint_as_float(v[j]), scale);
+                        const float mine_hi = __fmul_rn(__uint_as_float(v[16 + j]), scale);
+                        const float other = __shfl_xor_sync(0xffffffffu, odd ? mine_lo : mine_hi, 1);
+                        const float g = odd ? other : mine_lo;
+                        const float u = odd ? mine_hi : other;
+                        const int n = 32 * c + (odd ? 16 : 0) + j;
+                        if (n < it.count && row < rows)
+                            o[(int64_t)(it.pos0 + n) * p.out_ld] = __float2bfloat16_rn(swiglu(g, u));
+                    }
+                } else {
+                    float *o = reinterpret_cast<float *>(p.out) + row;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int n = 32 * c + j;
+                        if (n < it.count && row < rows)
+                            o[(int64_t)(it.pos0 + n) * p.out_ld] = __fmul_rn(__uint_as_float(v[j]), scale);
+                    }
+                }
+            }
+            if (!released) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S->dempty);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// One thread per 16-element block: row of x (bf16) -> position row of xg
+// with the block permuted (position 2q / 2q+1 of word q = 2j + pp holds
+// element 4pp + j / 8 + 4pp + j).
+__global__ void __launch_bounds__(256)
+gather_bf16_kernel(const GatherParams p) {
+    const int64_t nblk = p.H / 16;
+    const int64_t total = p.npos * nblk;
+    const int32_t nvalid = *p.n_valid;
+    for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * 256) {
+        const int64_t pos = i / nblk, b = i % nblk;
+        const bool routed = pos < p.shared_base;
+        if (routed && pos >= nvalid) continue;
+        const int64_t row = routed ? (int64_t)p.pos_tok[pos] : pos - p.shared_base;
+        const uint4 *src = reinterpret_cast<const uint4 *>(
+            reinterpret_cast<const __nv_bfloat16 *>(p.x) + row * p.H + 16 * b);
+        const uint4 a = __ldg(src), c = __ldg(src + 1);
+        uint4 o0, o1;
+        o0.x = __byte_perm(a.x, c.x, 0x5410);  // e0  | e8
+        o0.y = __byte_perm(a.z, c.z, 0x5410);  // e4  | e12
+        o0.z = __byte_perm(a.x, c.x, 0x7632);  // e1  | e9
+        o0.w = __byte_perm(a.z, c.z, 0x7632);  // e5  | e13
+        o1.x = __byte_perm(a.y, c.y, 0x5410);  // e2  | e10
+        o1.y = __byte_perm(a.w, c.w, 0x5410);  // e6  | e14
+        o1.z = __byte_perm(a.y, c.y, 0x7632);  // e3  | e11
+        o1.w = __byte_perm(a.w, c.w, 0x7632);  // e7  | e15
+        uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.xg) + pos * p.H + 16 * b);
+        dst[0] = o0;
+        dst[1] = o1;
+    }
+}
+
+}  // namespace
+
+size_t qgemm_prefill_smem_bytes() {
+    return 1024 + (size_t)kNB * kBStage + (size_t)kNW * kWStage + sizeof(Smem);
+}
+
+cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmParams &p, int grid,
+                                 cudaStream_t s) {
+    const size_t smem = qgemm_prefill_smem_bytes();
+    static bool attr_set[2] = {false, false};
+    if (!attr_set[mode]) {
+        cudaError_t e = mode == 0
+            ? cudaFuncSetAttribute(qgemm_prefill_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+            : cudaFuncSetAttribute(qgemm_prefill_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_set[mode] = true;
+    }
+    if (mode == 0)
+        qgemm_prefill_kernel<0><<<grid, kThreads, smem, s>>>(maps.w0, maps.w1, maps.s0, maps.s1, maps.b, p);
+    else
+        qgemm_prefill_kernel<1><<<grid, kThreads, smem, s>>>(maps.w0, maps.w1, maps.s0, maps.s1, maps.b, p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s) {
+    if (p.npos == 0) return cudaSuccess;
+    const int64_t total = p.npos * (p.H / 16);
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    gather_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace qmoe

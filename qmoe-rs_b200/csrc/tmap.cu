@@ -41,4 +41,19 @@ bool make_tmap_u8(CUtensorMap *tm, const void *base, uint64_t row_bytes, uint64_
     return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_bf16(CUtensorMap *tm, const void *base, uint64_t cols, uint64_t rows,
+                    uint64_t row_stride, uint32_t box_cols, uint32_t box_rows, int swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {row_stride};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
+                    strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    static_cast<CUtensorMapSwizzle>(swizzle), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 }  // namespace qmoe

@@ -25,6 +25,9 @@ QMOE_DTYPE_F32 = 0
 QMOE_DTYPE_BF16 = 1
 QMOE_SCORING_SOFTMAX = 0
 QMOE_SCORING_SIGMOID = 1
+QMOE_PATH_AUTO = 0
+QMOE_PATH_DECODE = 1
+QMOE_PATH_PREFILL = 2
 QMOE_NOALLOC_MAX_BATCH = 16384
 QMOE_NOALLOC_MAX_IN_FEATURES = 8192
 
@@ -90,6 +93,7 @@ SIGNATURES = {
     "qmoe_layer_forward_routed": (_I, [_P, _P, _I, _I64, _P, _P, _P, _I]),
     "qmoe_layer_shared_forward": (_I, [_P, _P, _I, _I64, _P, _I, _I]),
     "qmoe_packed_forward_noalloc": (_I, [_I, _P, _P, _P, _I64, _I64, _P, _I64, _P]),
+    "qmoe_layer_set_path": (_I, [_P, _I]),
     "qmoe_layer_set_profiling": (_I, [_P, _I]),
     "qmoe_layer_stage_times": (_I, [_P, ctypes.POINTER(ctypes.c_float), _I,
                                     ctypes.POINTER(ctypes.c_int)]),

@@ -364,6 +364,10 @@ class QMoELayer:
     def reserve(self, max_tokens: int) -> None:
         capi.call("qmoe_layer_reserve", self._h, int(max_tokens))
 
+    def set_path(self, path: int) -> None:
+        """Expert-product kernels: capi.QMOE_PATH_AUTO / _DECODE / _PREFILL."""
+        capi.call("qmoe_layer_set_path", self._h, int(path))
+
     def set_profiling(self, enable: bool) -> None:
         capi.call("qmoe_layer_set_profiling", self._h, int(bool(enable)))
 
