@@ -165,7 +165,7 @@ struct qmoe_layer {
     int path = QMOE_PATH_AUTO;
     CUtensorMap tm_pw[2], tm_pws[2];
     DevBuf xg, hb;
-    CUtensorMap tm_xg, tm_hb;
+    CUtensorMap tm_xg, tm_hb, tm_xg2, tm_hb2;  // 256-row and 128-row boxes
     // tracing
     bool profiling = false;
     cudaEvent_t ev[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -556,10 +556,14 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
     if (L->prefill_ok) {
         QTRY(grow(L->xg, 2 * (size_t)npos * H));
         QTRY(grow(L->hb, 2 * (size_t)npos * Imax));
-        if (!make_tmap_bf16(&L->tm_xg, L->xg.p, (uint64_t)H, (uint64_t)npos, 2 * (uint64_t)H, 64, 64,
-                            CU_TENSOR_MAP_SWIZZLE_128B) ||
+        if (!make_tmap_bf16(&L->tm_xg, L->xg.p, (uint64_t)H, (uint64_t)npos, 2 * (uint64_t)H, 64,
+                            kPrefillTile, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_tmap_bf16(&L->tm_xg2, L->xg.p, (uint64_t)H, (uint64_t)npos, 2 * (uint64_t)H, 64,
+                            kPrefillTile / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
             !make_tmap_bf16(&L->tm_hb, L->hb.p, (uint64_t)Imax, (uint64_t)npos, 2 * (uint64_t)Imax,
-                            64, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+                            64, kPrefillTile, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_tmap_bf16(&L->tm_hb2, L->hb.p, (uint64_t)Imax, (uint64_t)npos, 2 * (uint64_t)Imax,
+                            64, kPrefillTile / 2, CU_TENSOR_MAP_SWIZZLE_128B))
             return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill rows");
     }
     if (!make_tmap_u8(&L->tm_xq1, L->xq1.p, (uint64_t)L->kp1, (uint64_t)(npos * 3), 128, 16,
@@ -666,6 +670,7 @@ static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, b
     m0.s0 = L->tm_pws[0];
     m0.s1 = L->tm_pws[1];
     m0.b = L->tm_xg;
+    m0.b2 = L->tm_xg2;
     QgemmParams g0{};
     g0.groups = L->groups.as<int4>();
     g0.n_groups = L->ngroups.as<int32_t>();
@@ -689,6 +694,7 @@ static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, b
     m1.w0 = m1.w1 = L->tm_w[2];
     m1.s0 = m1.s1 = L->tm_ws[2];
     m1.b = L->tm_hb;
+    m1.b2 = L->tm_hb2;
     QgemmParams g1{};
     g1.groups = g0.groups;
     g1.n_groups = g0.n_groups;

@@ -31,7 +31,7 @@ struct RouterParams {
     float *scratch;         // router_scratch_floats(T, H, E) floats
 };
 size_t router_smem_bytes(int H, int E);
-bool router_uses_partials(int64_t T, int E);
+bool router_uses_partials(int64_t T, int H, int E);
 size_t router_scratch_floats(int64_t T, int H, int E);
 cudaError_t launch_router(const RouterParams &p, cudaStream_t s);
 
@@ -156,7 +156,8 @@ cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s);
 struct QgemmMaps {
     CUtensorMap w0, w1;          // routed 2-bit matrices (mode 0: gate, up; mode 1: down)
     CUtensorMap s0, s1;          // shared-expert matrices (copies of w0/w1 if none)
-    CUtensorMap b;               // bf16 activation rows [npos][ld], 128-byte swizzle
+    CUtensorMap b;               // bf16 activation rows [npos][ld], 128-byte swizzle, 256-row box
+    CUtensorMap b2;              // the same rows, 128-row box
 };
 struct QgemmParams {
     const int4 *groups;          // (segment, first position, count <= 256)

@@ -18,19 +18,30 @@
 // so that the SwiGLU pairs sit in neighbouring lanes; in mode 1 they are 128
 // down rows.  D[128 x N] += A[128 x 16] * B[N x 16]^T per instruction, with
 //   A  the dequantised weights, written by the dequant warps straight into
-//      tensor memory (32 columns per 64-element K block, 8-deep ring);
-//   B  the activation rows of the group, [N x 64] bf16 K blocks staged by
-//      TMA with 128-byte swizzle (4-deep ring, 64-row boxes);
+//      tensor memory;
+//   B  the activation rows of the group, bf16, 128-byte swizzle, one TMA box
+//      of 128 or 256 rows per 64-element K block;
 //   D  f32 in tensor memory columns 256..511.
-// Persistent grid, one CTA per SM, fourteen warps:
-//   warp 0      TMA producer (packed weight stages of 256 K, activation K
-//               blocks);
+// The pipeline moves in stages of two K blocks (128 K): a stage owns one
+// 64-column TMEM slot for A and one 64 KB shared-memory slot for B, and has
+// one "full" barrier (four dequant-warp arrivals + the TMA transaction
+// bytes) and one "empty" barrier (the MMA commit), so the single MMA thread
+// waits once per eight MMAs.  One producer thread can issue a TMA box only
+// every few hundred cycles (the issue and the barrier round trips), so boxes
+// are as large as the 128-byte swizzle allows and few per stage.
+//
+// Persistent grid, one CTA per SM, twenty-three warps:
+//   warp 0      TMA producer of the packed weight stages (256 K each);
+//   warp 22     TMA producer of the activation K blocks;
 //   warp 1      TMEM owner and MMA issuer (one thread);
 //   warps 2-5   dequant: one TMEM lane (weight row) per thread, 64 codes per
 //               K block: ((w >> s) & 0x00030003) | 0x43004300 is the bf16
 //               pair (128 + c_lo, 128 + c_hi), one bf16x2 FMA subtracts 129;
-//   warps 6-13  epilogue: two warps per TMEM lane quarter, alternate 32-column
-//               chunks; scales, SwiGLU (mode 0) or f32 rows (mode 1).
+//               a stage's TMEM stores are waited for only after the next
+//               stage is unpacked;
+//   warps 6-21  epilogue: four warps per TMEM lane quarter, each draining
+//               at most two 32-column chunks to registers, then releasing the
+//               accumulator; scales, SwiGLU (mode 0) or f32 rows (mode 1).
 // Every wait is bounded; on a time-out the kernel flags the device error
 // word, drains its copies and MMAs (again bounded), frees TMEM and returns.
 #include <cuda_bf16.h>
@@ -44,24 +55,25 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kWarps = 14;
+constexpr int kWarps = 23;
 constexpr int kThreads = kWarps * 32;
 constexpr int kEpiWarp0 = 6;
-constexpr int kEpiWarps = 8;
-constexpr int kNW = 4;                       // packed-weight stages
+constexpr int kEpiWarps = 16;                // four per TMEM lane quarter
+constexpr int kBWarp = 22;                   // activation producer
+constexpr int kNW = 3;                       // packed-weight stages
 constexpr int kWStage = 8192;                // 128 rows x 64 B (256 codes per row)
-constexpr int kNB = 4;                       // activation K-block stages
-constexpr int kBBox = 64 * 128;              // one 64-row x 128 B box
-constexpr int kBStage = kPrefillTile * 128;  // 256 rows x 64 bf16
-constexpr int kNA = 8;                       // TMEM A stages (32 columns each)
+constexpr int kNS = 3;                       // pipeline stages (2 K blocks each)
+constexpr int kKbBytes = kPrefillTile * 128; // one K block of B: 256 rows x 128 B
+constexpr int kSBytes = 2 * kKbBytes;        // B bytes of a stage
+constexpr uint32_t kACols = 64;              // TMEM columns of A per stage
 constexpr uint32_t kDCol = 256;              // accumulator columns 256..511
 constexpr uint32_t kTmemCols = 512;
 constexpr int kItemCache = 256;
+static_assert(kNS * kACols <= kDCol, "A slots overlap the accumulator");
 
 struct Smem {
     uint64_t wfull[kNW], wempty[kNW];
-    uint64_t bfull[kNB], bempty[kNB];
-    uint64_t afull[kNA], aempty[kNA];
+    uint64_t full[kNS], empty[kNS];
     uint64_t dfull, dempty, drain;
     uint32_t tmem_base;
     int abort;
@@ -100,16 +112,56 @@ QMOE_DEV uint32_t codes_to_bf16x2(uint32_t biased) {
     return r;
 }
 
+// SiLU(g) * u in the fast-math form (|relative error| ~1e-6, far inside the
+// bf16 rounding of the result); g is clamped so 1 + exp(-g) stays finite.
+QMOE_DEV float swiglu_fast(float g, float u) {
+    return __fdividef(g, 1.0f + __expf(-fmaxf(g, -80.0f))) * u;
+}
+
+// One drained 32-column chunk: scale, then (mode 0) pair the gate/up lanes
+// and store bf16 SwiGLU rows, or (mode 1) store f32 rows.
+template <int MODE>
+QMOE_DEV void epilogue_chunk(const QgemmParams &p, const Item &it, int c, const uint32_t (&v)[32],
+                             int L, int row, int rows, float scale) {
+    if (MODE == 0) {
+        // lane pair (2i, 2i+1) = (gate, up) of row i: the even lane finishes
+        // columns 0-15 of the chunk, the odd lane 16-31
+        const bool odd = L & 1;
+        const int hpos = (row & ~15) | (4 * (row & 3) + 2 * ((row >> 2) & 1) + ((row >> 3) & 1));
+        __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(p.out) + hpos;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float mine_lo = __uint_as_float(v[j]) * scale;
+            const float mine_hi = __uint_as_float(v[16 + j]) * scale;
+            const float other = __shfl_xor_sync(0xffffffffu, odd ? mine_lo : mine_hi, 1);
+            const float g = odd ? other : mine_lo;
+            const float u = odd ? mine_hi : other;
+            const int n = 32 * c + (odd ? 16 : 0) + j;
+            if (n < it.count && row < rows)
+                o[(int64_t)(it.pos0 + n) * p.out_ld] = __float2bfloat16_rn(swiglu_fast(g, u));
+        }
+    } else {
+        float *o = reinterpret_cast<float *>(p.out) + row;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int n = 32 * c + j;
+            if (n < it.count && row < rows)
+                o[(int64_t)(it.pos0 + n) * p.out_ld] = __uint_as_float(v[j]) * scale;
+        }
+    }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_s1,
-                     const __grid_constant__ CUtensorMap tm_b, const QgemmParams p) {
+                     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b2,
+                     const QgemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *bring = base;                         // kNB x 32 KB activation stages
-    uint8_t *wring = bring + kNB * kBStage;        // kNW x 8 KB packed weights
+    uint8_t *bring = base;                         // kNS x 64 KB activation stages
+    uint8_t *wring = bring + kNS * kSBytes;        // kNW x 8 KB packed weights
     Smem *S = reinterpret_cast<Smem *>(wring + kNW * kWStage);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -127,13 +179,9 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
             mbar_init(&S->wfull[i], 1);
             mbar_init(&S->wempty[i], 4);
         }
-        for (int i = 0; i < kNB; ++i) {
-            mbar_init(&S->bfull[i], 1);
-            mbar_init(&S->bempty[i], 1);
-        }
-        for (int i = 0; i < kNA; ++i) {
-            mbar_init(&S->afull[i], 4);
-            mbar_init(&S->aempty[i], 1);
+        for (int i = 0; i < kNS; ++i) {
+            mbar_init(&S->full[i], 4 + 1);     // dequant warps + TMA bytes
+            mbar_init(&S->empty[i], 1);
         }
         mbar_init(&S->dfull, 1);
         mbar_init(&S->dempty, kEpiWarps);
@@ -170,60 +218,72 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
     };
 
     if (warp == 0) {
-        // ------------------------------------------------------------- TMA
+        // ------------------------------------------------- TMA: packed weights
         if (lane == 0) {
             tma_prefetch_desc(&tm_w0);
             if (MODE == 0) tma_prefetch_desc(&tm_w1);
-            tma_prefetch_desc(&tm_b);
             if (p.rows_s > 0) {
                 tma_prefetch_desc(&tm_s0);
                 if (MODE == 0) tma_prefetch_desc(&tm_s1);
             }
-            uint32_t uw = 0, ub = 0;
+            uint32_t uw = 0;
+            bool ok = true;
+            for (int i = 0; ok && i < my_items; ++i) {
+                const Item it = item_at(i);
+                const int K = it.shared ? p.K_s : p.K;
+                const int nws = (K / 64 + 3) / 4;             // stages of 256 codes
+                const CUtensorMap *m0 = it.shared ? &tm_s0 : &tm_w0;
+                const CUtensorMap *m1 = it.shared ? &tm_s1 : &tm_w1;
+                const int rows = it.shared ? p.rows_s : p.rows;
+                const int y = (it.shared ? 0 : it.seg * rows) + it.mt * rows_tile;
+                for (int ws = 0; ws < nws; ++ws, ++uw) {
+                    const uint32_t s = uw % kNW;
+                    if (!(ok = mbar_wait(&S->wempty[s], ((uw / kNW) & 1) ^ 1, abort, p.err))) break;
+                    mbar_arrive_expect_tx(&S->wfull[s], kWStage);
+                    uint8_t *dst = wring + s * kWStage;
+                    tma_load_2d(dst, m0, &S->wfull[s], ws * 64, y);
+                    if (MODE == 0) tma_load_2d(dst + kWStage / 2, m1, &S->wfull[s], ws * 64, y);
+                }
+            }
+            if (!ok)  // let the copies already issued land before the CTA exits
+                for (uint32_t u = uw > kNW ? uw - kNW : 0; u < uw; ++u)
+                    for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
+                        if (mbar_try_wait(&S->wfull[u % kNW], (u / kNW) & 1)) break;
+        }
+    } else if (warp == kBWarp) {
+        // ---------------------------------------------- TMA: activation rows
+        if (lane == 0) {
+            tma_prefetch_desc(&tm_b);
+            tma_prefetch_desc(&tm_b2);
+            uint32_t us = 0;
             bool ok = true;
             for (int i = 0; ok && i < my_items; ++i) {
                 const Item it = item_at(i);
                 const int K = it.shared ? p.K_s : p.K;
                 const int nkb = K / 64;
-                const int nbox = (it.count + 63) / 64;
-                const CUtensorMap *m0 = it.shared ? &tm_s0 : &tm_w0;
-                const CUtensorMap *m1 = it.shared ? &tm_s1 : &tm_w1;
-                const int rows = it.shared ? p.rows_s : p.rows;
-                const int y = (it.shared ? 0 : it.seg * rows) + it.mt * rows_tile;
-                for (int kb = 0; kb < nkb; ++kb) {
-                    if ((kb & 3) == 0) {
-                        const uint32_t s = uw % kNW;
-                        if (!(ok = mbar_wait(&S->wempty[s], ((uw / kNW) & 1) ^ 1, abort, p.err)))
-                            break;
-                        mbar_arrive_expect_tx(&S->wfull[s], kWStage);
-                        uint8_t *dst = wring + s * kWStage;
-                        tma_load_2d(dst, m0, &S->wfull[s], (kb >> 2) * 64, y);
-                        if (MODE == 0) tma_load_2d(dst + kWStage / 2, m1, &S->wfull[s], (kb >> 2) * 64, y);
-                        ++uw;
-                    }
-                    const uint32_t s = ub % kNB;
-                    if (!(ok = mbar_wait(&S->bempty[s], ((ub / kNB) & 1) ^ 1, abort, p.err))) break;
-                    mbar_arrive_expect_tx(&S->bfull[s], (uint32_t)(nbox * kBBox));
-                    for (int bx = 0; bx < nbox; ++bx)
-                        tma_load_2d(bring + s * kBStage + bx * kBBox, &tm_b, &S->bfull[s], kb * 64,
-                                    it.pos0 + 64 * bx);
-                    ++ub;
+                // one box per K block: 128 rows when they hold the group, else 256
+                const bool small = it.count <= 128;
+                const CUtensorMap *mb = small ? &tm_b2 : &tm_b;
+                const uint32_t box = small ? 128 * 128 : 256 * 128;
+                for (int kb = 0; kb < nkb; kb += 2, ++us) {
+                    const int nk = nkb - kb < 2 ? nkb - kb : 2;
+                    const uint32_t s = us % kNS;
+                    if (!(ok = mbar_wait(&S->empty[s], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
+                    mbar_arrive_expect_tx(&S->full[s], nk * box);
+                    for (int j = 0; j < nk; ++j)
+                        tma_load_2d(bring + s * kSBytes + j * kKbBytes, mb, &S->full[s],
+                                    (kb + j) * 64, it.pos0);
                 }
             }
-            if (!ok) {
-                // let the copies already issued land before the CTA exits
-                for (uint32_t u = uw > kNW ? uw - kNW : 0; u < uw; ++u)
+            if (!ok)
+                for (uint32_t u = us > kNS ? us - kNS : 0; u < us; ++u)
                     for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
-                        if (mbar_try_wait(&S->wfull[u % kNW], (u / kNW) & 1)) break;
-                for (uint32_t u = ub > kNB ? ub - kNB : 0; u < ub; ++u)
-                    for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
-                        if (mbar_try_wait(&S->bfull[u % kNB], (u / kNB) & 1)) break;
-            }
+                        if (mbar_try_wait(&S->full[u % kNS], (u / kNS) & 1)) break;
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA
         if (lane == 0) {
-            uint32_t ua = 0, ub = 0;
+            uint32_t us = 0;
             bool ok = true, issued = false;
             const uint64_t bd0 = smem_desc(smem_u32(bring), 16, 1024, 2);
             const uint32_t bd_lo = (uint32_t)bd0, bd_hi = (uint32_t)(bd0 >> 32);
@@ -235,19 +295,21 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                 const uint32_t idesc = idesc_bf16(128, N);
                 if (!(ok = mbar_wait(&S->dempty, (i & 1) ^ 1, abort, p.err))) break;
                 tc_fence_after();
-                for (int kb = 0; kb < nkb; ++kb, ++ua, ++ub) {
-                    const uint32_t sa = ua % kNA, sb = ub % kNB;
-                    if (!(ok = mbar_wait(&S->afull[sa], (ua / kNA) & 1, abort, p.err))) break;
-                    if (!(ok = mbar_wait(&S->bfull[sb], (ub / kNB) & 1, abort, p.err))) break;
+                for (int kb = 0; kb < nkb; kb += 2, ++us) {
+                    const int nk = nkb - kb < 2 ? nkb - kb : 2;
+                    const uint32_t s = us % kNS;
+                    if (!(ok = mbar_wait(&S->full[s], (us / kNS) & 1, abort, p.err))) break;
                     tc_fence_after();
-                    const uint32_t lo = bd_lo + (uint32_t)((sb * kBStage) >> 4);
+                    for (int j = 0; j < nk; ++j) {
+                        const uint32_t lo = bd_lo + (uint32_t)((s * kSBytes + j * kKbBytes) >> 4);
+                        const uint32_t a = tmem + s * kACols + 32 * j;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_bf16_ts_lohi(tmem + kDCol, tmem + sa * 32 + 8 * kk, lo + 2 * kk, bd_hi,
-                                         idesc, (kb | kk) != 0);
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_bf16_ts_lohi(tmem + kDCol, a + 8 * kk, lo + 2 * kk, bd_hi, idesc,
+                                             (kb | j | kk) != 0);
+                    }
                     issued = true;
-                    mma_commit(&S->aempty[sa]);
-                    mma_commit(&S->bempty[sb]);
+                    mma_commit(&S->empty[s]);
                 }
                 if (!ok) break;
                 mma_commit(&S->dfull);
@@ -269,47 +331,71 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
         const int r = MODE == 0 ? (L >> 1) : L;
         const int box_off = MODE == 0 ? (L & 1) * (kWStage / 2) : 0;
         const int sw = (r >> 1) & 3;                  // 64-byte swizzle of row r
-        uint32_t uw = 0, ua = 0;
+        uint32_t uw = 0, us = 0;
+        int pend = -1;                                // stage stored, not yet published
         bool ok = true;
         for (int i = 0; ok && i < my_items; ++i) {
             const Item it = item_at(i);
             const int K = it.shared ? p.K_s : p.K;
             const int nkb = K / 64;
-            for (int kb = 0; kb < nkb; ++kb, ++ua) {
-                const uint32_t s = uw % kNW;
-                if ((kb & 3) == 0)
-                    if (!(ok = mbar_wait_warp(&S->wfull[s], (uw / kNW) & 1, abort, p.err))) break;
-                const uint4 v = *reinterpret_cast<const uint4 *>(wring + s * kWStage + box_off +
-                                                                 r * 64 + 16 * ((kb & 3) ^ sw));
-                if ((kb & 3) == 3 || kb == nkb - 1) {
+            for (int kb = 0; kb < nkb; kb += 2, ++us) {
+                const int nk = nkb - kb < 2 ? nkb - kb : 2;
+                const uint32_t ws = uw % kNW;         // kb and kb+1 share a weight stage
+                if ((kb & 3) == 0) {
+                    if (!(ok = mbar_wait_warp(&S->wfull[ws], (uw / kNW) & 1, abort, p.err))) break;
+                }
+                const uint8_t *wrow = wring + ws * kWStage + box_off + r * 64;
+                const uint4 v0 = *reinterpret_cast<const uint4 *>(wrow + 16 * ((kb & 3) ^ sw));
+                const uint4 v1 = *reinterpret_cast<const uint4 *>(wrow + 16 * (((kb + 1) & 3) ^ sw));
+                if ((kb & 3) == 2 || kb + nk >= nkb) {
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&S->wempty[s]);
+                    if (lane == 0) mbar_arrive(&S->wempty[ws]);
                     ++uw;
                 }
-                const uint32_t sa = ua % kNA;
-                if (!(ok = mbar_wait_warp(&S->aempty[sa], ((ua / kNA) & 1) ^ 1, abort, p.err))) break;
+                const uint32_t s = us % kNS;
+                if (!(ok = mbar_wait_warp(&S->empty[s], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
                 tc_fence_after();
-                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-                uint32_t regs[32];
+                // publish the previous stage (its stores had this stage's
+                // unpacking to complete in), then store this one
+                if (pend >= 0) {
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S->full[pend]);
+                }
 #pragma unroll
-                for (int wi = 0; wi < 4; ++wi)
+                for (int j = 0; j < 2; ++j) {
+                    if (j < nk) {
+                        const uint4 v = j ? v1 : v0;
+                        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+                        uint32_t regs[32];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
+                        for (int wi = 0; wi < 4; ++wi)
 #pragma unroll
-                        for (int pp = 0; pp < 2; ++pp)
-                            regs[8 * wi + 2 * j + pp] = codes_to_bf16x2(
-                                ((w4[wi] >> (2 * j + 8 * pp)) & 0x00030003u) | 0x43004300u);
-                tmem_st_x32(tmem + lane_addr + sa * 32, regs);
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S->afull[sa]);
+                            for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+                                for (int pp = 0; pp < 2; ++pp)
+                                    regs[8 * wi + 2 * jj + pp] = codes_to_bf16x2(
+                                        ((w4[wi] >> (2 * jj + 8 * pp)) & 0x00030003u) | 0x43004300u);
+                        tmem_st_x32(tmem + lane_addr + s * kACols + 32 * j, regs);
+                    }
+                }
+                pend = (int)s;
             }
         }
-    } else {
+        tmem_wait_st();
+        if (ok && pend >= 0) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S->full[pend]);
+        }
+    } else if (warp < kEpiWarp0 + kEpiWarps) {
         // -------------------------------------------------------- epilogue
+        // Each warp drains its (at most two) 32-column chunks of the
+        // accumulator into registers and releases it at once, so the next
+        // item's MMAs overlap the scaling, SwiGLU and stores.
         const int q = warp & 3;
-        const int half = (warp - kEpiWarp0) >> 2;     // which 32-column chunks
+        const int slot = (warp - kEpiWarp0) >> 2;     // chunks slot, slot + 4
         const int L = q * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         bool ok = true;
@@ -332,49 +418,16 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
             }
             if (!(ok = mbar_wait_warp(&S->dfull, i & 1, abort, p.err))) break;
             tc_fence_after();
-            bool released = false;
-            for (int c = half; c < nch; c += 2) {
-                uint32_t v[32];
-                tmem_ld_x32(tmem + lane_addr + kDCol + 32 * c, v);
-                tmem_wait_ld();
-                if (c + 2 >= nch) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&S->dempty);
-                    released = true;
-                }
-                if (MODE == 0) {
-                    // lane pair (2i, 2i+1) = (gate, up) of row i: the even lane
-                    // finishes columns 0-15 of the chunk, the odd lane 16-31
-                    const bool odd = L & 1;
-                    const int hpos = (row & ~15) | (4 * (row & 3) + 2 * ((row >> 2) & 1) + ((row >> 3) & 1));
-                    __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(p.out) + hpos;
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float mine_lo = __fmul_rn(__uint_as_float(v[j]), scale);
-                        const float mine_hi = __fmul_rn(__uint_as_float(v[16 + j]), scale);
-                        const float other = __shfl_xor_sync(0xffffffffu, odd ? mine_lo : mine_hi, 1);
-                        const float g = odd ? other : mine_lo;
-                        const float u = odd ? mine_hi : other;
-                        const int n = 32 * c + (odd ? 16 : 0) + j;
-                        if (n < it.count && row < rows)
-                            o[(int64_t)(it.pos0 + n) * p.out_ld] = __float2bfloat16_rn(swiglu(g, u));
-                    }
-                } else {
-                    float *o = reinterpret_cast<float *>(p.out) + row;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int n = 32 * c + j;
-                        if (n < it.count && row < rows)
-                            o[(int64_t)(it.pos0 + n) * p.out_ld] = __fmul_rn(__uint_as_float(v[j]), scale);
-                    }
-                }
-            }
-            if (!released) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S->dempty);
-            }
+            uint32_t v0[32], v1[32];
+            const int c0 = slot, c1 = slot + 4;
+            if (c0 < nch) tmem_ld_x32(tmem + lane_addr + kDCol + 32 * c0, v0);
+            if (c1 < nch) tmem_ld_x32(tmem + lane_addr + kDCol + 32 * c1, v1);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S->dempty);
+            if (c0 < nch) epilogue_chunk<MODE>(p, it, c0, v0, L, row, rows, scale);
+            if (c1 < nch) epilogue_chunk<MODE>(p, it, c1, v1, L, row, rows, scale);
         }
     }
 
@@ -421,7 +474,7 @@ gather_bf16_kernel(const GatherParams p) {
 }  // namespace
 
 size_t qgemm_prefill_smem_bytes() {
-    return 1024 + (size_t)kNB * kBStage + (size_t)kNW * kWStage + sizeof(Smem);
+    return 1024 + (size_t)kNS * kSBytes + (size_t)kNW * kWStage + sizeof(Smem);
 }
 
 cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmParams &p, int grid,
@@ -436,9 +489,11 @@ cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmPar
         attr_set[mode] = true;
     }
     if (mode == 0)
-        qgemm_prefill_kernel<0><<<grid, kThreads, smem, s>>>(maps.w0, maps.w1, maps.s0, maps.s1, maps.b, p);
+        qgemm_prefill_kernel<0><<<grid, kThreads, smem, s>>>(maps.w0, maps.w1, maps.s0, maps.s1, maps.b,
+                                                            maps.b2, p);
     else
-        qgemm_prefill_kernel<1><<<grid, kThreads, smem, s>>>(maps.w0, maps.w1, maps.s0, maps.s1, maps.b, p);
+        qgemm_prefill_kernel<1><<<grid, kThreads, smem, s>>>(maps.w0, maps.w1, maps.s0, maps.s1, maps.b,
+                                                            maps.b2, p);
     return cudaGetLastError();
 }
 

@@ -8,12 +8,14 @@
 // the logit is ((0 + p_0) + p_1) + ... in chunk order.  The CPU oracle
 // computes the same operations in the same order, so the logits, and the
 // routing built from them, agree bit for bit.  Two ways to get there:
-//   few tokens   router_partials_kernel: one thread per (token, expert,
-//                chunk) chain, all chains in parallel; the selection kernel
-//                adds each expert's partials in chunk order;
-//   many tokens  router_logits_kernel: 64x64 (token x expert) tiles staged
-//                in shared memory chunk by chunk, each thread owning 4x4
-//                logits and running the same chains and chunk sums.
+//   partials     router_chunk_kernel: every (token, expert, chunk) chain in
+//                parallel, tiles of tokens x 64 experts x one chunk staged
+//                in shared memory; the selection kernel adds each expert's
+//                partials in chunk order;
+//   whole        router_logits_kernel, for batches whose partials would not
+//                fit the scratch: 64x64 (token x expert) tiles over all
+//                chunks, each thread owning 4x4 logits and running the same
+//                chains and chunk sums.
 // Then router_select_kernel, one CTA per token, scores and selects.
 //
 // Selection: stable descending order with ties to the lower expert index
@@ -46,65 +48,126 @@ __host__ __device__ inline RouterSmem router_layout(int E) {
     return L;
 }
 
-// One thread per (token, expert, chunk): partial[t][e][c] = fmaf chain.
+// Chunk partials, partial[c][t][e] = fmaf chain of chunk c.  CTA = 16*TT
+// tokens x 64 experts x one chunk; thread = TT tokens x 4 experts.  Every
+// chain is independent, so the grid covers tokens, experts and chunks.
+template <int TT>
 __global__ void __launch_bounds__(256)
-router_partials_kernel(const RouterParams p) {
-    const int nc = (p.H + kGateChunk - 1) / kGateChunk;
-    const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
-    if (i >= p.T * p.E * nc) return;
-    const int c = (int)(i % nc);
-    const int64_t te = i / nc;
-    const int e = (int)(te % p.E);
-    const int64_t t = te / p.E;
-    const int k0 = c * kGateChunk, k1 = min(p.H, k0 + kGateChunk);
-    const float *w = p.gate_w + (int64_t)e * p.H;
-    float acc = 0.0f;
-    if (k1 - k0 == kGateChunk) {
-#pragma unroll 4
-        for (int j = 0; j < kGateChunk; j += 4) {
-            const float4 xv = load_act4(p.x, p.dtype, t * p.H + k0 + j);
-            const float4 wv = __ldg(reinterpret_cast<const float4 *>(w + k0 + j));
-            acc = __fmaf_rn(xv.x, wv.x, acc);
-            acc = __fmaf_rn(xv.y, wv.y, acc);
-            acc = __fmaf_rn(xv.z, wv.z, acc);
-            acc = __fmaf_rn(xv.w, wv.w, acc);
-        }
-    } else {
-        for (int k = k0; k < k1; ++k)
-            acc = __fmaf_rn(load_act(p.x, p.dtype, t * p.H + k), __ldg(w + k), acc);
+router_chunk_kernel(const RouterParams p) {
+    constexpr int kT = 16 * TT;
+    __shared__ float xs[kGateChunk][kT + 1];
+    __shared__ float ws[kGateChunk][64 + 1];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int64_t t0 = (int64_t)blockIdx.x * kT;
+    const int e0 = blockIdx.y * 64;
+    const int c = blockIdx.z;
+    const int k0 = c * kGateChunk;
+    for (int i = tid; i < kT * (kGateChunk / 4); i += 256) {
+        const int rr = i / (kGateChunk / 4), k4 = i % (kGateChunk / 4);
+        const int64_t t = t0 + rr;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < p.T) v = load_act4(p.x, p.dtype, t * p.H + k0 + 4 * k4);
+        xs[4 * k4 + 0][rr] = v.x;
+        xs[4 * k4 + 1][rr] = v.y;
+        xs[4 * k4 + 2][rr] = v.z;
+        xs[4 * k4 + 3][rr] = v.w;
     }
-    p.scratch[i] = acc;
+    for (int i = tid; i < 64 * (kGateChunk / 4); i += 256) {
+        const int rr = i / (kGateChunk / 4), k4 = i % (kGateChunk / 4);
+        const int e = e0 + rr;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e < p.E) v = __ldg(reinterpret_cast<const float4 *>(p.gate_w + (int64_t)e * p.H + k0 + 4 * k4));
+        ws[4 * k4 + 0][rr] = v.x;
+        ws[4 * k4 + 1][rr] = v.y;
+        ws[4 * k4 + 2][rr] = v.z;
+        ws[4 * k4 + 3][rr] = v.w;
+    }
+    __syncthreads();
+    float acc[TT][4];
+#pragma unroll
+    for (int a = 0; a < TT; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+#pragma unroll 8
+    for (int k = 0; k < kGateChunk; ++k) {
+        float xa[TT], wb[4];
+#pragma unroll
+        for (int a = 0; a < TT; ++a) xa[a] = xs[k][ty * TT + a];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) wb[b] = ws[k][tx * 4 + b];
+#pragma unroll
+        for (int a = 0; a < TT; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acc[a][b] = __fmaf_rn(xa[a], wb[b], acc[a][b]);
+    }
+    float *part = p.scratch + (int64_t)c * p.T * p.E;
+#pragma unroll
+    for (int a = 0; a < TT; ++a) {
+        const int64_t t = t0 + ty * TT + a;
+        if (t >= p.T) continue;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int e = e0 + tx * 4 + b;
+            if (e < p.E) part[t * p.E + e] = acc[a][b];
+        }
+    }
 }
 
-// Tiled logits: CTA = 64 tokens x 64 experts, thread = 4 x 4 logits.
+// Whole logits for batches whose partials would not fit the scratch: CTA =
+// 64 tokens x 64 experts over all chunks, thread = 4 x 4 logits, each chunk
+// an fmaf chain added to the running total in chunk order.  The next
+// chunk's tiles are fetched into registers while this one is computed.
 constexpr int kTileT = 64, kTileE = 64;
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 router_logits_kernel(const RouterParams p) {
     __shared__ float xs[kGateChunk][kTileT + 1];
     __shared__ float ws[kGateChunk][kTileE + 1];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int64_t t0 = (int64_t)blockIdx.x * kTileT;
     const int e0 = blockIdx.y * kTileE;
+    const int nc = p.H / kGateChunk;
+    // this thread's loads: rows rr = (tid + 256 j) / 16, float4 k4 = tid % 16
+    float4 xv[4], wv[4];
+    auto fetch = [&](int c) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = tid + 256 * j, rr = i >> 4, k4 = i & 15;
+            const int64_t t = t0 + rr;
+            const int e = e0 + rr;
+            xv[j] = t < p.T ? load_act4(p.x, p.dtype, t * p.H + c * kGateChunk + 4 * k4)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            wv[j] = e < p.E ? __ldg(reinterpret_cast<const float4 *>(p.gate_w + (int64_t)e * p.H +
+                                                                    c * kGateChunk + 4 * k4))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
     float tot[4][4], acc[4][4];
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
         for (int b = 0; b < 4; ++b) tot[a][b] = 0.0f;
-    for (int k0 = 0; k0 < p.H; k0 += kGateChunk) {
-        const int kn = min(kGateChunk, p.H - k0);
-        for (int i = tid; i < kTileT * kGateChunk; i += 256) {
-            const int rr = i / kGateChunk, k = i % kGateChunk;
-            const int64_t t = t0 + rr;
-            xs[k][rr] = (t < p.T && k < kn) ? load_act(p.x, p.dtype, t * p.H + k0 + k) : 0.0f;
-            const int e = e0 + rr;
-            ws[k][rr] = (e < p.E && k < kn) ? __ldg(p.gate_w + (int64_t)e * p.H + k0 + k) : 0.0f;
+    fetch(0);
+    for (int c = 0; c < nc; ++c) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = tid + 256 * j, rr = i >> 4, k4 = i & 15;
+            xs[4 * k4 + 0][rr] = xv[j].x;
+            xs[4 * k4 + 1][rr] = xv[j].y;
+            xs[4 * k4 + 2][rr] = xv[j].z;
+            xs[4 * k4 + 3][rr] = xv[j].w;
+            ws[4 * k4 + 0][rr] = wv[j].x;
+            ws[4 * k4 + 1][rr] = wv[j].y;
+            ws[4 * k4 + 2][rr] = wv[j].z;
+            ws[4 * k4 + 3][rr] = wv[j].w;
         }
         __syncthreads();
+        if (c + 1 < nc) fetch(c + 1);
 #pragma unroll
         for (int a = 0; a < 4; ++a)
 #pragma unroll
             for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
-        for (int k = 0; k < kn; ++k) {
+#pragma unroll 8
+        for (int k = 0; k < kGateChunk; ++k) {
             float xa[4], wb[4];
 #pragma unroll
             for (int a = 0; a < 4; ++a) xa[a] = xs[k][ty * 4 + a];
@@ -153,9 +216,10 @@ router_select_kernel(const RouterParams p, int from_partials) {
     const int nc = (p.H + kGateChunk - 1) / kGateChunk;
     for (int e = tid; e < E; e += kRouterThreads) {
         if (from_partials) {
-            const float *pp = p.scratch + ((int64_t)t * E + e) * nc;
+            const float *pp = p.scratch + (int64_t)t * E + e;
+            const int64_t stride = (int64_t)p.T * E;
             float tot = 0.0f;
-            for (int c = 0; c < nc; ++c) tot = __fadd_rn(tot, pp[c]);
+            for (int c = 0; c < nc; ++c) tot = __fadd_rn(tot, pp[c * stride]);
             logit[e] = tot;
         } else {
             logit[e] = p.scratch[(int64_t)t * E + e];
@@ -274,26 +338,32 @@ size_t router_smem_bytes(int H, int E) {
     return (size_t)(L.misc + 4 + 256 + 64) * sizeof(float);
 }
 
-constexpr int64_t kPartialsMaxLogits = 32768;  // T * E up to which the partials path runs
+// Chunk partials (T * E * H/64 floats) up to this size; whole logits beyond.
+constexpr int64_t kPartialsMaxFloats = int64_t(32) << 20;
 
-bool router_uses_partials(int64_t T, int E) { return T * E <= kPartialsMaxLogits; }
+bool router_uses_partials(int64_t T, int H, int E) {
+    return T * E * (H / kGateChunk) <= kPartialsMaxFloats;
+}
 
 // Enough for every token count up to T on either path (monotonic in T, so a
 // buffer reserved for a larger batch serves every smaller one).
 size_t router_scratch_floats(int64_t T, int H, int E) {
-    const int64_t nc = (H + kGateChunk - 1) / kGateChunk;
+    const int64_t nc = H / kGateChunk;
     const int64_t logits = T * E;
-    const int64_t parts = (logits < kPartialsMaxLogits ? logits : kPartialsMaxLogits) * nc;
+    const int64_t parts = logits * nc <= kPartialsMaxFloats ? logits * nc : kPartialsMaxFloats;
     return (size_t)(parts > logits ? parts : logits);
 }
 
 cudaError_t launch_router(const RouterParams &p, cudaStream_t s) {
     if (p.T == 0) return cudaSuccess;
-    const bool parts = router_uses_partials(p.T, p.E);
+    const bool parts = router_uses_partials(p.T, p.H, p.E);
     if (parts) {
-        const int nc = (p.H + kGateChunk - 1) / kGateChunk;
-        const int64_t n = p.T * p.E * nc;
-        router_partials_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p);
+        const int nc = p.H / kGateChunk;
+        const int TT = p.T <= 16 ? 1 : p.T <= 32 ? 2 : 4;
+        dim3 grid((unsigned)((p.T + 16 * TT - 1) / (16 * TT)), (unsigned)((p.E + 63) / 64), (unsigned)nc);
+        if (TT == 1) router_chunk_kernel<1><<<grid, 256, 0, s>>>(p);
+        else if (TT == 2) router_chunk_kernel<2><<<grid, 256, 0, s>>>(p);
+        else router_chunk_kernel<4><<<grid, 256, 0, s>>>(p);
     } else {
         dim3 grid((unsigned)((p.T + kTileT - 1) / kTileT), (unsigned)((p.E + kTileE - 1) / kTileE));
         router_logits_kernel<<<grid, 256, 0, s>>>(p);

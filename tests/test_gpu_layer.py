@@ -198,8 +198,8 @@ def test_sigmoid_group_limited_routing_bit_exact():
     assert rel_err(out.cpu().numpy(), ro) <= F32_TOL
 
 
-# T=50 takes the per-chunk partials path, T=700 (T*E > 32768) the tiled
-# logits path with a ragged last tile; both must give the same bits.
+# Chunk-partials path at three token tilings (T=50: 64-token tiles, ragged;
+# T=32 after a large reserve; T=700: many tiles); all must give the same bits.
 @pytest.mark.parametrize("T,reserve", [(50, 0), (700, 0), (32, 4096)])
 def test_route_only_matches_oracle_bit_exact(T, reserve):
     cfg = MoEConfig(64, 6, 2048, 128)
@@ -213,6 +213,21 @@ def test_route_only_matches_oracle_bit_exact(T, reserve):
     ri, rw = qo.route(qo_cfg(cfg), logits)
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
     np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=1e-6, atol=0)
+
+
+def test_whole_logits_path_bit_exact():
+    # T * E * H/64 > 2^25 partials: the whole-logits kernel, V3-style routing
+    E, H, T = 256, 4096, 2100
+    cfg = MoEConfig(E, 8, H, 128, scoring=capi.QMOE_SCORING_SIGMOID, n_group=8,
+                    topk_group=4, norm_topk_prob=True, routed_scaling_factor=2.5)
+    experts, _, gw = helpers.synth_layer(E, H, 128, seed=29, device="cuda")
+    layer = QMoELayer(cfg, gw, experts)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(12))
+    idx, w = layer.route(x.cuda())
+    logits = qo.gate_logits(x.numpy(), gw.cpu().numpy())
+    ri, rw = qo.route(qo_cfg(cfg), logits)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_array_equal(w.cpu().numpy(), rw)
 
 
 @pytest.mark.parametrize("T", [19, 1100])
