@@ -152,6 +152,7 @@ struct qmoe_layer {
     // tensor-core GEMV: TMA maps over the stacked 2-bit matrices, one CTA per SM
     int sm_count = 0;
     CUtensorMap tm_w[3], tm_ws[3];
+    CUtensorMap tm_w3[3], tm_ws3[3];  // 3-D views: two 64-byte chunks of 128 rows per box
     int kp1 = 0, kp2 = 0;  // limb row strides: hidden dim / intermediate dims, padded to 256
     // scratch
     int64_t cap = -1;
@@ -159,6 +160,7 @@ struct qmoe_layer {
     DevBuf x_in, io_out, user_idx, user_w;
     DevBuf xq1, meta1, xq2, meta2, router_scratch;
     CUtensorMap tm_xq1, tm_xq2;
+    CUtensorMap tm_xq1_3, tm_xq2_3;   // 3-D views: 16 limb rows x every 128-byte block
     // prefill path: gate/up maps with 64-row boxes, bf16 activation / SwiGLU
     // rows (16-element blocks permuted) and their 128-byte-swizzled maps
     bool prefill_ok = false;
@@ -462,6 +464,29 @@ static int layer_create_impl(qmoe_layer *L, const float *gate_weight, const floa
                               64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
                 return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for shared matrix %d", m);
     }
+    // 3-D views of the matrices for the decode GEMV (rows of whole 64-byte
+    // chunks; a stage that reaches a ragged row end uses the 2-D map)
+    for (int m = 0; m < 3; ++m) {
+        L->tm_w3[m] = L->tm_w[m];
+        if (kin[m] / 256 >= 2 &&
+            !make_tmap_u8_3d(&L->tm_w3[m], L->w[m], 64, (uint64_t)(rows[m] * El),
+                             (uint64_t)(kin[m] / 256), (uint64_t)(kin[m] / 4), 64, 64, 128, 2,
+                             CU_TENSOR_MAP_SWIZZLE_64B))
+            return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed for expert matrix %d", m);
+        L->tm_ws3[m] = L->tm_w3[m];
+    }
+    if (L->has_shared) {
+        const int64_t Is = c.shared_intermediate_dim;
+        const int64_t srows[3] = {Is, Is, H}, skin[3] = {H, H, Is};
+        for (int m = 0; m < 3; ++m) {
+            L->tm_ws3[m] = L->tm_ws[m];
+            if (skin[m] / 256 >= 2 &&
+                !make_tmap_u8_3d(&L->tm_ws3[m], L->ws[m], 64, (uint64_t)srows[m],
+                                 (uint64_t)(skin[m] / 256), (uint64_t)(skin[m] / 4), 64, 64, 128, 2,
+                                 CU_TENSOR_MAP_SWIZZLE_64B))
+                return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed for shared matrix %d", m);
+        }
+    }
     // prefill kernels: K blocks of 64 everywhere, down tiles of 128 rows
     L->prefill_ok = H % 128 == 0 && I % 64 == 0 &&
                     (!L->has_shared || c.shared_intermediate_dim % 64 == 0);
@@ -571,6 +596,11 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
         !make_tmap_u8(&L->tm_xq2, L->xq2.p, (uint64_t)L->kp2, (uint64_t)(npos * 3), 128, 16,
                       CU_TENSOR_MAP_SWIZZLE_128B))
         return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the limb scratch");
+    if (!make_tmap_u8_3d(&L->tm_xq1_3, L->xq1.p, 128, (uint64_t)(npos * 3), (uint64_t)(L->kp1 / 128),
+                         (uint64_t)L->kp1, 128, 128, 16, 4, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_u8_3d(&L->tm_xq2_3, L->xq2.p, 128, (uint64_t)(npos * 3), (uint64_t)(L->kp2 / 128),
+                         (uint64_t)L->kp2, 128, 128, 16, 4, CU_TENSOR_MAP_SWIZZLE_128B))
+        return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed for the limb scratch");
     L->cap = T;
     return QMOE_OK;
 }
@@ -782,6 +812,11 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     m0.s0 = L->tm_ws[0];
     m0.s1 = L->tm_ws[1];
     m0.b = L->tm_xq1;
+    m0.a0_3 = L->tm_w3[0];
+    m0.a1_3 = L->tm_w3[1];
+    m0.s0_3 = L->tm_ws3[0];
+    m0.s1_3 = L->tm_ws3[1];
+    m0.b3 = L->tm_xq1_3;
     QgemvTcParams g0{};
     g0.groups = L->groups.as<int4>();
     g0.n_groups = L->ngroups.as<int32_t>();
@@ -821,6 +856,9 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     m1.a0 = m1.a1 = L->tm_w[2];
     m1.s0 = m1.s1 = L->tm_ws[2];
     m1.b = L->tm_xq2;
+    m1.a0_3 = m1.a1_3 = L->tm_w3[2];
+    m1.s0_3 = m1.s1_3 = L->tm_ws3[2];
+    m1.b3 = L->tm_xq2_3;
     QgemvTcParams g1{};
     g1.groups = g0.groups;
     g1.n_groups = g0.n_groups;

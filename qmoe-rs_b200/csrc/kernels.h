@@ -106,6 +106,10 @@ struct QgemvTcMaps {
     CUtensorMap a0, a1;          // routed matrices (mode 0: gate, up; mode 1: down, down)
     CUtensorMap s0, s1;          // shared-expert matrices (copies of a0/a1 if none)
     CUtensorMap b;               // limb rows xq [npos*3][kp_b], 128-byte swizzle
+    // 3-D views for the IMMA kernel: a matrix as [64-byte chunk][row][byte]
+    // (one box = two chunks of 128 rows), the limb rows as
+    // [128-byte block][row][byte] (one box = 16 rows x every block)
+    CUtensorMap a0_3, a1_3, s0_3, s1_3, b3;
 };
 struct QgemvTcParams {
     const int4 *groups;
@@ -137,6 +141,10 @@ int *device_error_flag();
 // swizzle (CU_TENSOR_MAP_SWIZZLE_*); returns false if encoding fails.
 bool make_tmap_u8(CUtensorMap *tm, const void *base, uint64_t row_bytes, uint64_t rows,
                   uint32_t box_bytes, uint32_t box_rows, int swizzle);
+// Host: a 3-D uint8 tensor map (extents d0..d2, byte strides of dims 1 and 2).
+bool make_tmap_u8_3d(CUtensorMap *tm, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
+                     uint64_t stride1, uint64_t stride2, uint32_t b0, uint32_t b1, uint32_t b2,
+                     int swizzle);
 
 // ---- prefill grouped GEMM (tcgen05 kind::f16; 2-bit -> bf16 into TMEM) ---
 // Activation and SwiGLU rows are stored with every 16-element block in the

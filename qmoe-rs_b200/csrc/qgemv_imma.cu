@@ -23,16 +23,25 @@
 // Work item = (<= 5 positions of one segment) x 256 output rows (gate+up
 // rows 128+128 in mode 0, 256 down rows in mode 1).  Persistent grid, one CTA
 // per SM, thirteen warps:
-//   warp 0      TMA: 2-bit weight tiles [128 rows x 64 B] (64-byte swizzle)
-//               into a 4-stage ring (continuous across items) and each item's
-//               limb tile [16 x Kp] (128-byte swizzle) into a 2-deep buffer;
-//   warps 1-8   compute, 32 weight rows each: 128-bit shared loads of the
-//               packed rows, unpack in registers ((w >> 2j) & 0x03030303: one
-//               shift + one mask per 4 weights), m16n8k32 IMMAs against the
-//               limb fragments; at item end the int32 accumulators go to a
-//               double-buffered tile in shared memory;
-//   warps 9-12  epilogue: limb recombination, scales, SwiGLU, stores, while
-//               the compute warps run the next item.
+//   warp 0      TMA: per stage of 512 codes, the 2-bit weight tiles
+//               [2 chunks x 128 rows x 64 B] (64-byte swizzle, one 3-D box per
+//               tile) and the item's limb rows for those codes [4 blocks x 16
+//               rows x 128 B] (128-byte swizzle, one 3-D box), 40 KB, into a
+//               4-stage ring continuous across items: HBM latency under load
+//               is several thousand cycles, so the bytes in flight set the
+//               rate, and a thread issues a box only every few hundred
+//               cycles, so boxes are few and large;
+//   warps 1-8   compute: two groups of four warps take the two 256-code
+//               chunks of a stage; a warp owns 32 rows of each weight tile
+//               (64 rows, so each limb fragment it loads feeds 16 IMMAs):
+//               128-bit shared loads of the packed rows, unpack in registers
+//               ((w >> 2j) & 0x03030303: one shift + one mask per 4
+//               weights), m16n8k32 IMMAs against the limb fragments; at item
+//               end each group's int32 accumulators go to its tile of a
+//               double-buffered pair in shared memory;
+//   warps 9-12  epilogue: sum of the two groups' tiles, limb recombination,
+//               scales, SwiGLU, stores, while the compute warps run the next
+//               item.
 // Every wait is bounded; on a time-out the kernel flags the device error
 // word, lets its TMA copies drain (again bounded) and returns.
 #include "common.cuh"
@@ -48,20 +57,23 @@ constexpr int kWarps = 13;
 constexpr int kThreads = kWarps * 32;
 constexpr int kCompute = 8;            // compute warps (1..8)
 constexpr int kEpiWarp0 = 9;           // first epilogue warp
-constexpr int kNS = 4;                 // weight stages in shared memory
-constexpr int kStageCodes = 256;       // codes per row per stage
-constexpr int kStageRowBytes = 64;
-constexpr int kTileBytes = 128 * kStageRowBytes;  // one 128-row weight tile
+constexpr int kNS = 4;                 // stages in shared memory
+constexpr int kStageCodes = 512;       // codes per row per stage (two 64-byte chunks)
+constexpr int kSubBytes = 128 * 64;    // one 128-row x 64-byte chunk (64-byte swizzle)
+constexpr int kTileBytes = 2 * kSubBytes;  // one 128-row weight tile of a stage
 constexpr int kBRows = 16;             // positions x limbs (15 used)
-constexpr int kBBlock = kBRows * 128;  // one 128-byte K block of the limb tile
+constexpr int kBBlock = kBRows * 128;  // one 128-byte K block of the limb rows
+constexpr int kLimbBytes = 4 * kBBlock;            // limb blocks of a stage (512 codes)
+constexpr int kStageBytes = 2 * kTileBytes + kLimbBytes;  // 40 KB
 constexpr int kTokMax = 5;
 constexpr int kOutCols = 256;          // output rows per item
-constexpr int kAccBytes = kBRows * kOutCols * 4;  // int32 accumulator tile
-constexpr int kItemCache = 256;
+constexpr int kLimbRows = 15;          // limb rows in use (5 positions x 3 limbs)
+constexpr int kTileStride = 264;       // int32 row stride of an accumulator tile (padded)
+constexpr int kAccBytes = kLimbRows * kTileStride * 4;  // one group's int32 tile
+constexpr int kItemCache = 128;
 
 struct Smem {
     uint64_t smem_full[kNS], smem_empty[kNS];
-    uint64_t bq_full[2], bq_empty[2];
     uint64_t tile_full[2], tile_empty[2];
     int abort;
     int4 items[kItemCache];
@@ -103,18 +115,13 @@ QMOE_DEV void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t 
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
-qgemv_imma_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
-                  const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_s1,
-                  const __grid_constant__ CUtensorMap tm_b, const QgemvTcParams p) {
+qgemv_imma_kernel(const __grid_constant__ QgemvTcMaps maps, const QgemvTcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *wring = base;                                  // kNS x 2 weight tiles
-    uint8_t *btile = wring + kNS * 2 * kTileBytes;          // nbuf limb tiles
-    const int nbuf = p.b_buffers;
-    const int bbytes = kBRows * p.kp_b;
-    int *acc_tile = reinterpret_cast<int *>(btile + nbuf * bbytes);  // 2 x [16][256]
-    Smem *S = reinterpret_cast<Smem *>(reinterpret_cast<uint8_t *>(acc_tile) + 2 * kAccBytes);
+    uint8_t *ring = base;                                   // kNS stages: 2 weight tiles + limbs
+    int *acc_tile = reinterpret_cast<int *>(ring + kNS * kStageBytes);  // [2 bufs][2 groups][15][264]
+    Smem *S = reinterpret_cast<Smem *>(reinterpret_cast<uint8_t *>(acc_tile) + 4 * kAccBytes);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rows_item = MODE == 0 ? 128 : 256;
@@ -130,8 +137,6 @@ qgemv_imma_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_consta
             mbar_init(&S->smem_empty[i], kCompute);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&S->bq_full[i], 1);
-            mbar_init(&S->bq_empty[i], kCompute);
             mbar_init(&S->tile_full[i], kCompute);
             mbar_init(&S->tile_empty[i], 4);
         }
@@ -161,30 +166,28 @@ qgemv_imma_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_consta
 
     if (warp == 0) {
         // ------------------------------------------------------------- TMA
+        // Per stage: one 3-D box per weight tile (two 64-byte chunks of 128
+        // rows; 2-D boxes per chunk where the stage reaches the ragged end of
+        // a row) and one 3-D box of the item's limb rows for those 512 codes.
         if (lane == 0) {
-            tma_prefetch_desc(&tm_a0);
-            tma_prefetch_desc(&tm_a1);
-            tma_prefetch_desc(&tm_b);
+            tma_prefetch_desc(&maps.a0_3);
+            tma_prefetch_desc(&maps.b3);
+            if (MODE == 0) tma_prefetch_desc(&maps.a1_3);
             if (p.rows_s > 0) {
-                tma_prefetch_desc(&tm_s0);
-                tma_prefetch_desc(&tm_s1);
+                tma_prefetch_desc(&maps.s0_3);
+                if (MODE == 0) tma_prefetch_desc(&maps.s1_3);
             }
             uint32_t us = 0;
-            int i = 0;
             bool ok = true;
-            for (; ok && i < my_items; ++i) {
+            for (int i = 0; ok && i < my_items; ++i) {
                 const Item it = item_at(i);
                 const int K = it.shared ? p.K_s : p.K;
                 const int nks = (K + kStageCodes - 1) / kStageCodes;
-                const int nkb = nks * 2;
-                const uint32_t b = nbuf == 2 ? (i & 1) : 0, ub = nbuf == 2 ? (i >> 1) : i;
-                if (!(ok = mbar_wait(&S->bq_empty[b], (ub & 1) ^ 1, abort, p.err))) break;
-                mbar_arrive_expect_tx(&S->bq_full[b], (uint32_t)(nkb * kBBlock));
-                for (int kb = 0; kb < nkb; ++kb)
-                    tma_load_2d(btile + b * bbytes + kb * kBBlock, &tm_b, &S->bq_full[b],
-                                kb * 128, it.pos0 * 3);
-                const CUtensorMap *t0 = it.shared ? &tm_s0 : &tm_a0;
-                const CUtensorMap *t1 = MODE == 0 ? (it.shared ? &tm_s1 : &tm_a1) : t0;
+                const int nfull = K >> 8;                   // complete 64-byte chunks per row
+                const CUtensorMap *t0 = it.shared ? &maps.s0 : &maps.a0;
+                const CUtensorMap *t1 = MODE == 0 ? (it.shared ? &maps.s1 : &maps.a1) : t0;
+                const CUtensorMap *t0_3 = it.shared ? &maps.s0_3 : &maps.a0_3;
+                const CUtensorMap *t1_3 = MODE == 0 ? (it.shared ? &maps.s1_3 : &maps.a1_3) : t0_3;
                 const int rows = it.shared ? p.rows_s : p.rows;
                 const int ybase = it.shared ? 0 : it.seg * rows;
                 const int y0 = ybase + it.rb * rows_item;
@@ -193,28 +196,34 @@ qgemv_imma_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_consta
                     const uint32_t s = us % kNS;
                     if (!(ok = mbar_wait(&S->smem_empty[s], ((us / kNS) & 1) ^ 1, abort, p.err)))
                         break;
-                    mbar_arrive_expect_tx(&S->smem_full[s], 2 * kTileBytes);
-                    uint8_t *dst = wring + s * 2 * kTileBytes;
-                    tma_load_2d(dst, t0, &S->smem_full[s], ks * kStageRowBytes, y0);
-                    tma_load_2d(dst + kTileBytes, t1, &S->smem_full[s], ks * kStageRowBytes, y1);
+                    mbar_arrive_expect_tx(&S->smem_full[s], kStageBytes);
+                    uint8_t *dst = ring + s * kStageBytes;
+                    if (2 * ks + 1 < nfull) {
+                        tma_load_3d(dst, t0_3, &S->smem_full[s], 0, y0, 2 * ks);
+                        tma_load_3d(dst + kTileBytes, t1_3, &S->smem_full[s], 0, y1, 2 * ks);
+                    } else {
+                        for (int sub = 0; sub < 2; ++sub) {
+                            tma_load_2d(dst + sub * kSubBytes, t0, &S->smem_full[s], (2 * ks + sub) * 64, y0);
+                            tma_load_2d(dst + kTileBytes + sub * kSubBytes, t1, &S->smem_full[s],
+                                        (2 * ks + sub) * 64, y1);
+                        }
+                    }
+                    tma_load_3d(dst + 2 * kTileBytes, &maps.b3, &S->smem_full[s], 0, it.pos0 * 3, 4 * ks);
                 }
             }
-            if (!ok) {
+            if (!ok)
                 for (uint32_t u = us > kNS ? us - kNS : 0; u < us; ++u)
                     for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
                         if (mbar_try_wait(&S->smem_full[u % kNS], (u / kNS) & 1)) break;
-                for (int j = i - nbuf < 0 ? 0 : i - nbuf; j <= i && j < my_items; ++j) {
-                    const uint32_t b = nbuf == 2 ? (j & 1) : 0, ub = nbuf == 2 ? (j >> 1) : j;
-                    for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
-                        if (mbar_try_wait(&S->bq_full[b], ub & 1)) break;
-                }
-            }
         }
     } else if (warp <= kCompute) {
         // --------------------------------------------------------- compute
+        // Two groups of four warps take the two 256-code chunks of a stage;
+        // a warp owns rows 32 wq .. 32 wq + 31 of both weight tiles (eight
+        // row groups of 8), so every limb fragment it loads feeds 16 IMMAs.
         const int cw = warp - 1;                    // 0..7
-        const int tile = cw >> 2;                   // weight tile (gate/up, or down half)
-        const int wrow = (cw & 3) * 32;             // first row of this warp in the tile
+        const int grp = cw >> 2;                    // chunk of each stage
+        const int wq = cw & 3;
         const int g8 = lane >> 2, t4 = lane & 3;
         uint32_t us = 0;
         bool ok = true;
@@ -222,73 +231,74 @@ qgemv_imma_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_consta
             const Item it = item_at(i);
             const int K = it.shared ? p.K_s : p.K;
             const int nks = (K + kStageCodes - 1) / kStageCodes;
-            const uint32_t b = nbuf == 2 ? (i & 1) : 0, ub = nbuf == 2 ? (i >> 1) : i;
-            if (!(ok = mbar_wait_warp(&S->bq_full[b], ub & 1, abort, p.err))) break;
-            const uint8_t *lt = btile + b * bbytes;
-            // limb rows g8 (atom 0) and g8 + 8 (atom 1) of the 128-byte-swizzled tile
-            const uint8_t *lrow_lo = lt + g8 * 128;
-            const uint8_t *lrow_hi = lt + 1024 + g8 * 128;
-            // two accumulators per row group (the two IMMAs of a 16-code word
-            // go to different ones), so a warp keeps 8 independent chains
-            int acc[4][4], acc2[4][4];
+            int acc[8][4];
 #pragma unroll
-            for (int rg = 0; rg < 4; ++rg)
+            for (int rg = 0; rg < 8; ++rg)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[rg][j] = acc2[rg][j] = 0;
+                for (int j = 0; j < 4; ++j) acc[rg][j] = 0;
 
+            const int nsub_all = (K + 255) / 256;        // 256-code chunks holding codes < K
             for (int ks = 0; ks < nks; ++ks, ++us) {
                 const uint32_t s = us % kNS;
                 if (!(ok = mbar_wait_warp(&S->smem_full[s], (us / kNS) & 1, abort, p.err))) break;
-                // packed rows wrow + 8 rg + g8, chunk t4 (64 codes), 64-byte swizzle
-                uint4 w[4];
-                const uint8_t *wt = wring + s * 2 * kTileBytes + tile * kTileBytes;
+                const bool live = 2 * ks + grp < nsub_all;
+                uint4 w[8], alo[4], ahi[4];
+                if (live) {
+                    // packed rows 32 wq + 8 rg + g8 of tile rg / 4, chunk t4
+                    // (64 codes), 64-byte swizzle
 #pragma unroll
-                for (int rg = 0; rg < 4; ++rg) {
-                    const int r = wrow + rg * 8 + g8;
-                    w[rg] = *reinterpret_cast<const uint4 *>(wt + r * kStageRowBytes +
-                                                             16 * (t4 ^ ((r >> 1) & 3)));
-                }
-                // limb fragments of the stage: 16-element K blocks ks*16 + 4 t4 + q
-                uint4 alo[4], ahi[4];
+                    for (int rg = 0; rg < 8; ++rg) {
+                        const uint8_t *wt = ring + s * kStageBytes + (rg >> 2) * kTileBytes + grp * kSubBytes;
+                        const int rr = wq * 32 + (rg & 3) * 8 + g8;
+                        w[rg] = *reinterpret_cast<const uint4 *>(wt + rr * 64 + 16 * (t4 ^ ((rr >> 1) & 3)));
+                    }
+                    // limb fragments of the chunk: 16-element K blocks 4 t4 + q of
+                    // 128-byte block 2 grp + t4/2 of the stage; limb rows g8
+                    // (atom 0) and g8 + 8 (atom 1), 128-byte swizzle
+                    const uint8_t *lrow_lo = ring + s * kStageBytes + 2 * kTileBytes + g8 * 128;
+                    const uint8_t *lrow_hi = lrow_lo + 1024;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int kb = ks * 2 + (t4 >> 1);        // 128-byte block
-                    const int c = ((t4 & 1) << 2) | q;        // 16-byte chunk within it
-                    const int off = kb * kBBlock + 16 * (c ^ g8);
-                    alo[q] = *reinterpret_cast<const uint4 *>(lrow_lo + off);
-                    ahi[q] = *reinterpret_cast<const uint4 *>(lrow_hi + off);
+                    for (int q = 0; q < 4; ++q) {
+                        const int kb = grp * 2 + (t4 >> 1);       // 128-byte block
+                        const int c = ((t4 & 1) << 2) | q;        // 16-byte chunk within it
+                        const int off = kb * kBBlock + 16 * (c ^ g8);
+                        alo[q] = *reinterpret_cast<const uint4 *>(lrow_lo + off);
+                        ahi[q] = *reinterpret_cast<const uint4 *>(lrow_hi + off);
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&S->smem_empty[s]);
+                if (live) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                    for (int q = 0; q < 4; ++q) {
 #pragma unroll
-                    for (int rg = 0; rg < 4; ++rg) {
-                        const uint32_t wq = q == 0 ? w[rg].x : q == 1 ? w[rg].y : q == 2 ? w[rg].z : w[rg].w;
-                        imma(acc[rg], alo[q].x, ahi[q].x, alo[q].y, ahi[q].y, wq & 0x03030303u,
-                             (wq >> 2) & 0x03030303u);
-                        imma(acc2[rg], alo[q].z, ahi[q].z, alo[q].w, ahi[q].w, (wq >> 4) & 0x03030303u,
-                             (wq >> 6) & 0x03030303u);
+                        for (int rg = 0; rg < 8; ++rg) {
+                            const uint32_t wv = q == 0 ? w[rg].x : q == 1 ? w[rg].y : q == 2 ? w[rg].z : w[rg].w;
+                            imma(acc[rg], alo[q].x, ahi[q].x, alo[q].y, ahi[q].y, wv & 0x03030303u,
+                                 (wv >> 2) & 0x03030303u);
+                        }
+#pragma unroll
+                        for (int rg = 0; rg < 8; ++rg) {
+                            const uint32_t wv = q == 0 ? w[rg].x : q == 1 ? w[rg].y : q == 2 ? w[rg].z : w[rg].w;
+                            imma(acc[rg], alo[q].z, ahi[q].z, alo[q].w, ahi[q].w, (wv >> 4) & 0x03030303u,
+                                 (wv >> 6) & 0x03030303u);
+                        }
                     }
                 }
             }
             if (!ok) break;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S->bq_empty[b]);
-#pragma unroll
-            for (int rg = 0; rg < 4; ++rg)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[rg][j] += acc2[rg][j];
 
-            // accumulators -> tile [16 limb rows][256 cols]
+            // accumulators -> this group's tile [15 limb rows][256 cols]
             const uint32_t tb = i & 1;
             if (!(ok = mbar_wait_warp(&S->tile_empty[tb], ((i >> 1) & 1) ^ 1, abort, p.err))) break;
-            int *ct = acc_tile + tb * (kAccBytes / 4);
+            int *ct = acc_tile + (tb * 2 + grp) * (kAccBytes / 4);
 #pragma unroll
-            for (int rg = 0; rg < 4; ++rg) {
-                const int col = tile * 128 + wrow + rg * 8 + 2 * t4;
-                *reinterpret_cast<int2 *>(ct + g8 * kOutCols + col) = make_int2(acc[rg][0], acc[rg][1]);
-                *reinterpret_cast<int2 *>(ct + (g8 + 8) * kOutCols + col) = make_int2(acc[rg][2], acc[rg][3]);
+            for (int rg = 0; rg < 8; ++rg) {
+                const int col = (rg >> 2) * 128 + wq * 32 + (rg & 3) * 8 + 2 * t4;
+                *reinterpret_cast<int2 *>(ct + g8 * kTileStride + col) = make_int2(acc[rg][0], acc[rg][1]);
+                if (g8 + 8 < kLimbRows)
+                    *reinterpret_cast<int2 *>(ct + (g8 + 8) * kTileStride + col) =
+                        make_int2(acc[rg][2], acc[rg][3]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S->tile_full[tb]);
@@ -314,12 +324,13 @@ qgemv_imma_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_consta
 
             const uint32_t tb = i & 1;
             if (!(ok = mbar_wait_warp(&S->tile_full[tb], (i >> 1) & 1, abort, p.err))) break;
-            const int *ct = acc_tile + tb * (kAccBytes / 4);
-            int v0[kBRows - 1], v1[kBRows - 1];
+            const int *ct0 = acc_tile + (tb * 2) * (kAccBytes / 4);   // group 0 + group 1
+            const int *ct1 = ct0 + kAccBytes / 4;
+            int v0[kLimbRows], v1[kLimbRows];
 #pragma unroll
-            for (int n = 0; n < kBRows - 1; ++n) {
-                v0[n] = ct[n * kOutCols + r];
-                v1[n] = ct[n * kOutCols + 128 + r];
+            for (int n = 0; n < kLimbRows; ++n) {
+                v0[n] = ct0[n * kTileStride + r] + ct1[n * kTileStride + r];
+                v1[n] = ct0[n * kTileStride + 128 + r] + ct1[n * kTileStride + 128 + r];
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S->tile_empty[tb]);
@@ -351,12 +362,14 @@ qgemv_imma_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_consta
 }  // namespace
 
 size_t qgemv_imma_smem_bytes(int kp_b, int b_buffers) {
-    return 1024 + (size_t)kNS * 2 * kTileBytes + (size_t)b_buffers * kBRows * kp_b +
-           2 * (size_t)kAccBytes + sizeof(Smem);
+    (void)kp_b;
+    (void)b_buffers;
+    return 1024 + (size_t)kNS * kStageBytes + 4 * (size_t)kAccBytes + sizeof(Smem);
 }
 
 int qgemv_imma_buffers(int kp_b) {
-    return qgemv_imma_smem_bytes(kp_b, 2) <= 227 * 1024 ? 2 : 1;
+    (void)kp_b;
+    return 0;
 }
 
 cudaError_t launch_qgemv_imma(int mode, const QgemvTcMaps &maps, const QgemvTcParams &p, int grid,
@@ -371,9 +384,9 @@ cudaError_t launch_qgemv_imma(int mode, const QgemvTcMaps &maps, const QgemvTcPa
         smem_set[mode] = smem;
     }
     if (mode == 0)
-        qgemv_imma_kernel<0><<<grid, kThreads, smem, s>>>(maps.a0, maps.a1, maps.s0, maps.s1, maps.b, p);
+        qgemv_imma_kernel<0><<<grid, kThreads, smem, s>>>(maps, p);
     else
-        qgemv_imma_kernel<1><<<grid, kThreads, smem, s>>>(maps.a0, maps.a1, maps.s0, maps.s1, maps.b, p);
+        qgemv_imma_kernel<1><<<grid, kThreads, smem, s>>>(maps, p);
     return cudaGetLastError();
 }
 

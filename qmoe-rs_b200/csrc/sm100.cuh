@@ -102,6 +102,15 @@ QMOE_DEV void tma_load_2d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, 
         : "memory");
 }
 
+// 3-D tiled load of the box at (x, y, z).
+QMOE_DEV void tma_load_3d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 // ---- TMEM ---------------------------------------------------------------
 // Whole-warp operations.
 QMOE_DEV void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {

@@ -41,6 +41,22 @@ bool make_tmap_u8(CUtensorMap *tm, const void *base, uint64_t row_bytes, uint64_
     return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_u8_3d(CUtensorMap *tm, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
+                     uint64_t stride1, uint64_t stride2, uint32_t b0, uint32_t b1, uint32_t b2,
+                     int swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {stride1, stride2};
+    const cuuint32_t box[3] = {b0, b1, b2};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides,
+                    box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    static_cast<CUtensorMapSwizzle>(swizzle), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 bool make_tmap_bf16(CUtensorMap *tm, const void *base, uint64_t cols, uint64_t rows,
                     uint64_t row_stride, uint32_t box_cols, uint32_t box_rows, int swizzle) {
     auto fn = encode_fn();
