@@ -44,6 +44,7 @@ WORKLOAD = dict(
     E=64, k=6, H=2048, I=1408, Is=2816, T=32, norm_topk=True)
 REPLICAS = 4
 KERNELS_PER_FORWARD = 8  # router logits + select, permute, limbs x2, gate/up, down, combine
+KERNELS_PER_PREFILL = 7  # router logits + select, permute, bf16 gather, gate/up, down, combine
 
 
 def parse():
@@ -280,6 +281,79 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def graph_stage_times(layers, xs, stream, n_prof: int = 100):
+    """Average per-stage device time (ms) of the forward from the layer's
+    stage events.  Each profiled forward is queued behind a device-side
+    sleep, so the whole forward is enqueued before the GPU reaches it and no
+    host launch gap enters the numbers."""
+    for L in layers:
+        L.set_profiling(True)
+    stage_ms = {}
+    with torch.cuda.stream(stream):
+        for i in range(n_prof):
+            r = i % len(layers)
+            torch.cuda._sleep(2_000_000)       # ~1 ms of device time
+            layers[r].forward(xs[r])
+            for k, v in layers[r].stage_times().items():
+                stage_ms.setdefault(k, []).append(v)
+    for L in layers:
+        L.set_profiling(False)
+    return {k: float(np.mean(v)) for k, v in stage_ms.items()}
+
+
+def run_prefill(layers, seed: int, dev: str, steps: int = 20):
+    """the same layer in prefill, 2048 bf16 tokens per forward
+    (tcgen05 bf16 GEMM path), CUDA graphs over the rotating replicas."""
+    w = WORKLOAD
+    T = 2048
+    g = torch.Generator(device=dev).manual_seed(seed + 99)
+    xs = [torch.randn(T, w["H"], generator=g, device=dev).bfloat16() for _ in layers]
+    for L in layers:
+        L.reserve(T)
+    stream = torch.cuda.Stream()
+    graphs = []
+    with torch.cuda.stream(stream):
+        for L, x in zip(layers, xs):
+            L.forward(x)
+        torch.cuda.current_stream().synchronize()
+        for L, x in zip(layers, xs):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                L.forward(x)
+            graphs.append(gr)
+    for i in range(3):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        graphs[i % len(graphs)].replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    del graphs
+    stages = graph_stage_times(layers, xs, stream, n_prof=20)
+    H, I, Is, K, E = w["H"], w["I"], w["Is"], w["k"], w["E"]
+    flops = 2.0 * T * K * 3 * H * I + 2.0 * T * 3 * H * Is + 2.0 * T * E * H
+    gu_flops = 2.0 * T * K * 2 * H * I + 2.0 * T * 2 * H * Is
+    dn_flops = 2.0 * T * K * H * I + 2.0 * T * H * Is
+    _, bf16, peak_kind = load_peaks()
+    gu_tf = gu_flops / (stages["gate_up"] / 1e3) / 1e12
+    return {
+        "workload": "configs[2]: same layer, prefill, 2048 bf16 tokens",
+        "value": T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "dtype": "bf16",
+        "tflops": flops / (ms / 1e3) / 1e12, "algorithmic_flops": flops,
+        "roofline": {"bound": "tensor", "kernel": "qgemm_prefill gate/up + SwiGLU",
+                     "achieved": gu_tf, "peak": bf16, "unit": "TFLOP/s",
+                     "frac": gu_tf / bf16, "peak_kind": peak_kind,
+                     "kernel_ms": stages["gate_up"],
+                     "down_tflops": dn_flops / (stages["down"] / 1e3) / 1e12},
+        "stage_ms": stages,
+        "gpu_launches_per_step": KERNELS_PER_PREFILL,
+    }
+
+
 def run_ours(args):
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -353,19 +427,9 @@ def run_ours(args):
     tokens = ws * w["T"] * args.steps
     value = tokens / (ms_max / 1e3)
 
-    # live kernel timing of the dominant kernel (gate/up), eager, same inputs
-    for L in layers:
-        L.set_profiling(True)
-    stage_ms = {}
-    n_prof = 200
-    for i in range(n_prof):
-        L = layers[i % REPLICAS]
-        L.forward(xs[i % REPLICAS])
-        for k, v in L.stage_times().items():
-            stage_ms.setdefault(k, []).append(v)
-    for L in layers:
-        L.set_profiling(False)
-    stage_avg = {k: float(np.mean(v)) for k, v in stage_ms.items()}
+    # live kernel timing: the same forward captured with stage events (event
+    # record nodes between the kernels on the launching stream), replayed
+    stage_avg = graph_stage_times(layers, xs, stream)
 
     # end to end through the C ABI with pinned host buffers
     x_host = xs[0].cpu().pin_memory()
@@ -385,6 +449,8 @@ def run_ours(args):
     e2e = {"value": w["T"] * ws / (e2e_ms / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": 4 * w["T"] * w["H"], "d2h_bytes_per_step": 4 * w["T"] * w["H"],
            "ms_per_step": e2e_ms}
+
+    prefill = run_prefill(layers, args.seed, dev) if ws == 1 else None
 
     if rank == 0:
         hbm, bf16, peak_kind = load_peaks()
@@ -412,6 +478,7 @@ def run_ours(args):
             "layer": {"stage_ms": stage_avg, "algorithmic_bytes": layer_bytes,
                       "achieved_gbs_per_step": layer_bytes / (ms_max / args.steps / 1e3) / 1e9},
             "e2e": e2e,
+            "prefill": prefill,
             "gpu_launches": KERNELS_PER_FORWARD * args.steps,
             "clocks": clk.summary(),
         }

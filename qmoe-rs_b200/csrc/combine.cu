@@ -17,6 +17,8 @@ constexpr int kMaxK = 64;
 
 __global__ void __launch_bounds__(kCombThreads)
 combine_kernel(const CombineParams p) {
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
     const int H4 = p.H >> 2;
     const int64_t i = (int64_t)blockIdx.x * kCombThreads + threadIdx.x;
     if (i >= p.T * H4) return;
@@ -86,8 +88,7 @@ cudaError_t launch_combine(const CombineParams &p, cudaStream_t s) {
     const int64_t n = p.T * (p.H / 4);
     if (n == 0) return cudaSuccess;
     const unsigned grid = (unsigned)((n + kCombThreads - 1) / kCombThreads);
-    combine_kernel<<<grid, kCombThreads, 0, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(combine_kernel, dim3(grid), dim3(kCombThreads), 0, s, p);
 }
 
 }  // namespace qmoe

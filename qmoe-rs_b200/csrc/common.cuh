@@ -5,7 +5,18 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define QMOE_DEV __device__ __forceinline__
+
+// Programmatic dependent launch.  QMOE_PDL_WAIT blocks until the preceding
+// kernel in the stream has completed and its writes are visible (a no-op
+// when the launch carries no programmatic dependency); every read of a
+// predecessor's output and every global write comes after it.
+// QMOE_PDL_TRIGGER lets the next kernel in the stream begin launching while
+// this one runs.
+#define QMOE_PDL_WAIT() asm volatile("griddepcontrol.wait;" ::: "memory")
+#define QMOE_PDL_TRIGGER() asm volatile("griddepcontrol.launch_dependents;" ::: "memory")
 
 namespace qmoe {
 
@@ -89,4 +100,24 @@ QMOE_DEV float swiglu(float g, float u) {
     return __fmul_rn(s, u);
 }
 
+}  // namespace qmoe
+
+namespace qmoe {
+// Host: launch with the programmatic-stream-serialization attribute, so the
+// kernel may start while its predecessor finishes (it waits in QMOE_PDL_WAIT).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 }  // namespace qmoe

@@ -36,6 +36,8 @@ permute_kernel(const PermuteParams p) {
     int *wpre = reinterpret_cast<int *>(bm + kWarps * E);               // [kWarps][E]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
     const int64_t T = p.T;
     const int K = p.K;
     const int64_t TK = T * K;
@@ -168,8 +170,7 @@ cudaError_t launch_permute(const PermuteParams &p, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         smem_set = smem;
     }
-    permute_kernel<<<1, kPermThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(permute_kernel, dim3(1), dim3(kPermThreads), smem, s, p);
 }
 
 }  // namespace qmoe

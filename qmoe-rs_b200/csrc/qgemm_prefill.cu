@@ -165,6 +165,8 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
     Smem *S = reinterpret_cast<Smem *>(wring + kNW * kWStage);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
     const int rows_tile = MODE == 0 ? 64 : 128;    // matrix rows per item (per matrix)
     const int mt_r = (p.rows + rows_tile - 1) / rows_tile;
     const int mt_s = p.rows_s > 0 ? (p.rows_s + rows_tile - 1) / rows_tile : 1;
@@ -446,6 +448,8 @@ __global__ void __launch_bounds__(256)
 gather_bf16_kernel(const GatherParams p) {
     const int64_t nblk = p.H / 16;
     const int64_t total = p.npos * nblk;
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
     const int32_t nvalid = *p.n_valid;
     for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * 256) {
@@ -488,13 +492,10 @@ cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmPar
         if (e != cudaSuccess) return e;
         attr_set[mode] = true;
     }
-    if (mode == 0)
-        qgemm_prefill_kernel<0><<<grid, kThreads, smem, s>>>(maps.w0, maps.w1, maps.s0, maps.s1, maps.b,
-                                                            maps.b2, p);
-    else
-        qgemm_prefill_kernel<1><<<grid, kThreads, smem, s>>>(maps.w0, maps.w1, maps.s0, maps.s1, maps.b,
-                                                            maps.b2, p);
-    return cudaGetLastError();
+    return mode == 0 ? launch_pdl(qgemm_prefill_kernel<0>, dim3(grid), dim3(kThreads), smem, s, maps.w0,
+                                  maps.w1, maps.s0, maps.s1, maps.b, maps.b2, p)
+                     : launch_pdl(qgemm_prefill_kernel<1>, dim3(grid), dim3(kThreads), smem, s, maps.w0,
+                                  maps.w1, maps.s0, maps.s1, maps.b, maps.b2, p);
 }
 
 cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s) {
@@ -502,8 +503,7 @@ cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s) {
     const int64_t total = p.npos * (p.H / 16);
     int64_t blocks = (total + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    gather_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(gather_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0, s, p);
 }
 
 }  // namespace qmoe

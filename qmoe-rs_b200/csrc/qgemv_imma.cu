@@ -124,6 +124,8 @@ qgemv_imma_kernel(const __grid_constant__ QgemvTcMaps maps, const QgemvTcParams 
     Smem *S = reinterpret_cast<Smem *>(reinterpret_cast<uint8_t *>(acc_tile) + 4 * kAccBytes);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
     const int rows_item = MODE == 0 ? 128 : 256;
     const int rb_r = (p.rows + rows_item - 1) / rows_item;
     const int rb_s = p.rows_s > 0 ? (p.rows_s + rows_item - 1) / rows_item : 1;
@@ -383,11 +385,8 @@ cudaError_t launch_qgemv_imma(int mode, const QgemvTcMaps &maps, const QgemvTcPa
         if (e != cudaSuccess) return e;
         smem_set[mode] = smem;
     }
-    if (mode == 0)
-        qgemv_imma_kernel<0><<<grid, kThreads, smem, s>>>(maps, p);
-    else
-        qgemv_imma_kernel<1><<<grid, kThreads, smem, s>>>(maps, p);
-    return cudaGetLastError();
+    return mode == 0 ? launch_pdl(qgemv_imma_kernel<0>, dim3(grid), dim3(kThreads), smem, s, maps, p)
+                     : launch_pdl(qgemv_imma_kernel<1>, dim3(grid), dim3(kThreads), smem, s, maps, p);
 }
 
 }  // namespace qmoe

@@ -22,6 +22,8 @@ constexpr int kQuantThreads = 128;
 __global__ void __launch_bounds__(kQuantThreads)
 quant_kernel(const QuantParams p) {
     const int64_t pos = blockIdx.x;
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
     const bool routed = pos < p.shared_base;
     if (routed && p.n_valid && pos >= *p.n_valid) return;  // unused routed slot
     int64_t row = pos;
@@ -92,8 +94,7 @@ quant_kernel(const QuantParams p) {
 
 cudaError_t launch_quant(const QuantParams &p, cudaStream_t s) {
     if (p.npos == 0) return cudaSuccess;
-    quant_kernel<<<(unsigned)p.npos, kQuantThreads, 0, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(quant_kernel, dim3((unsigned)p.npos), dim3(kQuantThreads), 0, s, p);
 }
 
 }  // namespace qmoe

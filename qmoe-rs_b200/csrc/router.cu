@@ -62,16 +62,7 @@ router_chunk_kernel(const RouterParams p) {
     const int e0 = blockIdx.y * 64;
     const int c = blockIdx.z;
     const int k0 = c * kGateChunk;
-    for (int i = tid; i < kT * (kGateChunk / 4); i += 256) {
-        const int rr = i / (kGateChunk / 4), k4 = i % (kGateChunk / 4);
-        const int64_t t = t0 + rr;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < p.T) v = load_act4(p.x, p.dtype, t * p.H + k0 + 4 * k4);
-        xs[4 * k4 + 0][rr] = v.x;
-        xs[4 * k4 + 1][rr] = v.y;
-        xs[4 * k4 + 2][rr] = v.z;
-        xs[4 * k4 + 3][rr] = v.w;
-    }
+    // the gate tile does not depend on the preceding kernel: stage it first
     for (int i = tid; i < 64 * (kGateChunk / 4); i += 256) {
         const int rr = i / (kGateChunk / 4), k4 = i % (kGateChunk / 4);
         const int e = e0 + rr;
@@ -81,6 +72,18 @@ router_chunk_kernel(const RouterParams p) {
         ws[4 * k4 + 1][rr] = v.y;
         ws[4 * k4 + 2][rr] = v.z;
         ws[4 * k4 + 3][rr] = v.w;
+    }
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    for (int i = tid; i < kT * (kGateChunk / 4); i += 256) {
+        const int rr = i / (kGateChunk / 4), k4 = i % (kGateChunk / 4);
+        const int64_t t = t0 + rr;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < p.T) v = load_act4(p.x, p.dtype, t * p.H + k0 + 4 * k4);
+        xs[4 * k4 + 0][rr] = v.x;
+        xs[4 * k4 + 1][rr] = v.y;
+        xs[4 * k4 + 2][rr] = v.z;
+        xs[4 * k4 + 3][rr] = v.w;
     }
     __syncthreads();
     float acc[TT][4];
@@ -126,6 +129,8 @@ router_logits_kernel(const RouterParams p) {
     const int64_t t0 = (int64_t)blockIdx.x * kTileT;
     const int e0 = blockIdx.y * kTileE;
     const int nc = p.H / kGateChunk;
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
     // this thread's loads: rows rr = (tid + 256 j) / 16, float4 k4 = tid % 16
     float4 xv[4], wv[4];
     auto fetch = [&](int c) {
@@ -214,6 +219,8 @@ router_select_kernel(const RouterParams p, int from_partials) {
     const int tid = threadIdx.x;
     const int E = p.E, K = p.K;
     const int nc = (p.H + kGateChunk - 1) / kGateChunk;
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
     for (int e = tid; e < E; e += kRouterThreads) {
         if (from_partials) {
             const float *pp = p.scratch + (int64_t)t * E + e;
@@ -361,12 +368,14 @@ cudaError_t launch_router(const RouterParams &p, cudaStream_t s) {
         const int nc = p.H / kGateChunk;
         const int TT = p.T <= 16 ? 1 : p.T <= 32 ? 2 : 4;
         dim3 grid((unsigned)((p.T + 16 * TT - 1) / (16 * TT)), (unsigned)((p.E + 63) / 64), (unsigned)nc);
-        if (TT == 1) router_chunk_kernel<1><<<grid, 256, 0, s>>>(p);
-        else if (TT == 2) router_chunk_kernel<2><<<grid, 256, 0, s>>>(p);
-        else router_chunk_kernel<4><<<grid, 256, 0, s>>>(p);
+        cudaError_t e = TT == 1 ? launch_pdl(router_chunk_kernel<1>, grid, dim3(256), 0, s, p)
+                      : TT == 2 ? launch_pdl(router_chunk_kernel<2>, grid, dim3(256), 0, s, p)
+                                : launch_pdl(router_chunk_kernel<4>, grid, dim3(256), 0, s, p);
+        if (e != cudaSuccess) return e;
     } else {
         dim3 grid((unsigned)((p.T + kTileT - 1) / kTileT), (unsigned)((p.E + kTileE - 1) / kTileE));
-        router_logits_kernel<<<grid, 256, 0, s>>>(p);
+        cudaError_t e = launch_pdl(router_logits_kernel, grid, dim3(256), 0, s, p);
+        if (e != cudaSuccess) return e;
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -378,8 +387,8 @@ cudaError_t launch_router(const RouterParams &p, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         smem_set = smem;
     }
-    router_select_kernel<<<(unsigned)p.T, kRouterThreads, smem, s>>>(p, parts ? 1 : 0);
-    return cudaGetLastError();
+    return launch_pdl(router_select_kernel, dim3((unsigned)p.T), dim3(kRouterThreads), smem, s, p,
+                      parts ? 1 : 0);
 }
 
 }  // namespace qmoe
