@@ -256,6 +256,37 @@ QMOE_API int qmoe_packed_forward_noalloc(int device, void *stream, const uint8_t
 #define QMOE_PATH_PREFILL 2
 QMOE_API int qmoe_layer_set_path(qmoe_layer *layer, int path);
 
+/* ---- expert parallelism ------------------------------------------------- */
+
+/* Device-side steps of an expert-parallel layer over `world` ranks, each
+ * holding experts_per_rank consecutive experts.  qmoe-rs has no such mode
+ * (src/moe.rs:40-130 runs every expert in one process); the host issues the
+ * exchanges (NCCL all-to-all) between these calls.  All pointers are device
+ * pointers; the calls are asynchronous on the context's stream.
+ *
+ * qmoe_ep_plan: from this rank's routing (topk_idx [T, K] global ids, -1 =
+ * none; topk_w [T, K]) the send list, destination-major with tokens in
+ * order: send_counts [world], send_tok (token of each send row), send_ids
+ * [rows, K] (local expert id on the destination, -1 for slots owned
+ * elsewhere), send_w [rows, K], and slot_pos [T, world] (send row of
+ * (token, rank), -1 if none).  capacity 0: compact rows (rows = sum of
+ * send_counts <= T * world, the buffers sized T * world); capacity C >= T:
+ * rank d's rows start at d * C, the unused ones with ids -1, token 0 and
+ * weight 0 (buffers of world * C rows), so every exchange has fixed sizes.
+ * world <= 32. */
+QMOE_API int qmoe_ep_plan(qmoe_ctx *ctx, const int32_t *topk_idx, const float *topk_w,
+                          int64_t T, int K, int experts_per_rank, int world,
+                          int64_t capacity, int32_t *send_counts, int32_t *send_tok,
+                          int32_t *send_ids, float *send_w, int32_t *slot_pos);
+/* out[i] = x[idx[i]] for n rows of H elements (f32 or bf16); H % 8 == 0. */
+QMOE_API int qmoe_gather_rows(qmoe_ctx *ctx, const void *x, int dtype, int64_t H,
+                              const int32_t *idx, int64_t n, void *out);
+/* out[t] = rows[slot_pos[t][0]] + rows[slot_pos[t][1]] + ... (ascending s,
+ * -1 skipped, f32 accumulation) for T rows of H elements in dtype; the
+ * origin-side sum of the partials returned by each rank. */
+QMOE_API int qmoe_combine_rows(qmoe_ctx *ctx, const void *rows, int dtype, int64_t H,
+                               const int32_t *slot_pos, int S, int64_t T, void *out);
+
 /* ---- tracing ----------------------------------------------------------- */
 
 /* Stage timing, the device-side counterpart of the Instant-based breakdown

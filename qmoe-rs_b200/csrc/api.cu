@@ -1033,6 +1033,64 @@ int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T
     return QMOE_OK;
 }
 
+// ---------------------------------------------------------------------------
+// expert parallelism helpers
+// ---------------------------------------------------------------------------
+
+int qmoe_ep_plan(qmoe_ctx *ctx, const int32_t *topk_idx, const float *topk_w, int64_t T, int K,
+                 int experts_per_rank, int world, int64_t capacity, int32_t *send_counts,
+                 int32_t *send_tok, int32_t *send_ids, float *send_w, int32_t *slot_pos) {
+    if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
+    if (T < 0 || K <= 0 || experts_per_rank <= 0 || world <= 0 || world > 32)
+        return fail(QMOE_ERR_INVALID, "bad plan shape (T %lld, K %d, experts_per_rank %d, world %d)",
+                    (long long)T, K, experts_per_rank, world);
+    if (capacity < 0 || (capacity > 0 && capacity < T))
+        return fail(QMOE_ERR_INVALID, "capacity %lld < T %lld", (long long)capacity, (long long)T);
+    if (!send_counts || (T > 0 && (!topk_idx || !topk_w || !send_tok || !send_ids || !send_w || !slot_pos)))
+        return fail(QMOE_ERR_INVALID, "NULL argument");
+    DeviceGuard g(ctx->device);
+    EpPlanParams p{};
+    p.topk_idx = topk_idx;
+    p.topk_w = topk_w;
+    p.T = T;
+    p.K = K;
+    p.experts_per_rank = experts_per_rank;
+    p.world = world;
+    p.capacity = capacity;
+    p.send_counts = send_counts;
+    p.send_tok = send_tok;
+    p.send_ids = send_ids;
+    p.send_w = send_w;
+    p.slot_pos = slot_pos;
+    QTRY_CUDA(launch_ep_plan(p, ctx->stream));
+    return QMOE_OK;
+}
+
+int qmoe_gather_rows(qmoe_ctx *ctx, const void *x, int dtype, int64_t H, const int32_t *idx, int64_t n,
+                     void *out) {
+    if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
+    QTRY(check_dtype(dtype));
+    if (H <= 0 || H % 8 || n < 0) return fail(QMOE_ERR_INVALID, "bad shape (H %% 8 must be 0)");
+    if (n > 0 && (!x || !idx || !out)) return fail(QMOE_ERR_INVALID, "NULL argument");
+    QTRY(check_align(x, QMOE_PTR_DEVICE, "x"));
+    QTRY(check_align(out, QMOE_PTR_DEVICE, "out"));
+    DeviceGuard g(ctx->device);
+    QTRY_CUDA(launch_gather_rows(x, dtype, H, idx, n, out, ctx->stream));
+    return QMOE_OK;
+}
+
+int qmoe_combine_rows(qmoe_ctx *ctx, const void *rows, int dtype, int64_t H, const int32_t *slot_pos,
+                      int S, int64_t T, void *out) {
+    if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
+    QTRY(check_dtype(dtype));
+    if (H <= 0 || H % 4 || S <= 0 || T < 0) return fail(QMOE_ERR_INVALID, "bad shape");
+    if (T > 0 && (!slot_pos || !out)) return fail(QMOE_ERR_INVALID, "NULL argument");
+    QTRY(check_align(out, QMOE_PTR_DEVICE, "out"));
+    DeviceGuard g(ctx->device);
+    QTRY_CUDA(launch_combine_rows(rows, dtype, H, slot_pos, S, T, out, ctx->stream));
+    return QMOE_OK;
+}
+
 int qmoe_layer_set_path(qmoe_layer *L, int path) {
     if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
     if (path != QMOE_PATH_AUTO && path != QMOE_PATH_DECODE && path != QMOE_PATH_PREFILL)

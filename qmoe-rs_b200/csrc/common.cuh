@@ -39,6 +39,18 @@ QMOE_DEV float4 load_act4(const void *base, int dtype, int64_t idx) {
                        __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
 }
 
+QMOE_DEV void store_act4(void *base, int dtype, int64_t idx, float4 v) {
+    if (dtype == 0) {
+        *reinterpret_cast<float4 *>(reinterpret_cast<float *>(base) + idx) = v;
+        return;
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t *>(&lo);
+    u.y = *reinterpret_cast<const uint32_t *>(&hi);
+    *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(base) + idx) = u;
+}
+
 QMOE_DEV float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

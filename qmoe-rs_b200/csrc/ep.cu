@@ -1,0 +1,184 @@
+// ep.cu -- device side of the expert-parallel layer (experts split over
+// ranks, contiguous blocks of experts_per_rank).
+//
+// qmoe-rs runs the whole layer in one process (src/moe.rs:40-130); across G
+// GPUs each rank routes its own tokens, sends every token once to each rank
+// that owns one of its experts, runs its experts on what it received, and
+// returns one partial sum per (token, rank).  The origin then adds the
+// partials in ascending rank order, i.e. ascending expert blocks, and the
+// shared expert last (src/model.rs:386-389).  These kernels build the send
+// lists and the return map, gather rows, and add the returned partials; the
+// exchanges themselves are NCCL all-to-alls issued by the host.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qmoe {
+namespace {
+
+constexpr int kPlanThreads = 1024;
+
+// Send list, destination-major and in token order within a destination
+// (compact: destination d's rows follow those of d-1; padded, capacity C > 0:
+// destination d's rows start at d*C and the unused rows carry ids -1, so
+// every exchange has fixed sizes and needs no count on the host):
+//   send_counts[d]          tokens sent to rank d
+//   send_tok[s]             token of send row s
+//   send_ids[s][k]          local expert id of slot k on the destination, -1
+//                           if slot k goes elsewhere
+//   send_w[s][k]            that slot's combine weight (0 if -1)
+//   slot_pos[t][d]          send row of (t, d), -1 if t sends nothing to d
+// One CTA; tokens in tiles of 1024, one per thread; per destination a block
+// scan of the "sends to d" bits gives each token its row.
+__global__ void __launch_bounds__(kPlanThreads)
+ep_plan_kernel(const EpPlanParams p) {
+    __shared__ int wsum[kPlanThreads / 32];
+    __shared__ int dcount[32];
+    __shared__ int tile_total;
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = p.world, K = p.K;
+    // padded layout: every row starts unused
+    if (p.capacity > 0)
+        for (int64_t i = tid; i < (int64_t)G * p.capacity; i += kPlanThreads) {
+            p.send_tok[i] = 0;
+            for (int k = 0; k < K; ++k) {
+                p.send_ids[i * K + k] = -1;
+                p.send_w[i * K + k] = 0.0f;
+            }
+        }
+    // pass 1: tokens per destination
+    if (tid < G) dcount[tid] = 0;
+    __syncthreads();
+    for (int64_t t = tid; t < p.T; t += kPlanThreads) {
+        uint32_t m = 0;
+        for (int k = 0; k < K; ++k) {
+            const int e = p.topk_idx[t * K + k];
+            if (e >= 0) m |= 1u << (e / p.experts_per_rank);
+        }
+        for (int d = 0; d < G; ++d)
+            if (m >> d & 1u) atomicAdd(&dcount[d], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int d = 0; d < G; ++d) p.send_counts[d] = dcount[d];
+        // destination bases (kept in dcount): exclusive prefix, or d * C
+        int run = 0;
+        for (int d = 0; d < G; ++d) {
+            const int c = dcount[d];
+            dcount[d] = p.capacity > 0 ? (int)(d * p.capacity) : run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    // pass 2: rows, in token order within each destination
+    for (int d = 0; d < G; ++d) {
+        int carry = 0;
+        for (int64_t t0 = 0; t0 < p.T; t0 += kPlanThreads) {
+            const int64_t t = t0 + tid;
+            int bit = 0;
+            if (t < p.T)
+                for (int k = 0; k < K; ++k) {
+                    const int e = p.topk_idx[t * K + k];
+                    if (e >= 0 && e / p.experts_per_rank == d) bit = 1;
+                }
+            // block exclusive scan of bit
+            const unsigned b = __ballot_sync(0xffffffffu, bit);
+            const int in_warp = __popc(b & ((1u << lane) - 1u));
+            if (lane == 0) wsum[warp] = __popc(b);
+            __syncthreads();
+            if (warp == 0) {
+                const int v = wsum[lane];
+                int s = v;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int u = __shfl_up_sync(0xffffffffu, s, o);
+                    if (lane >= o) s += u;
+                }
+                wsum[lane] = s - v;
+                if (lane == 31) tile_total = s;
+            }
+            __syncthreads();
+            if (t < p.T) {
+                int pos = -1;
+                if (bit) {
+                    pos = dcount[d] + carry + wsum[warp] + in_warp;
+                    p.send_tok[pos] = (int32_t)t;
+                    for (int k = 0; k < K; ++k) {
+                        const int e = p.topk_idx[t * K + k];
+                        const bool mine = e >= 0 && e / p.experts_per_rank == d;
+                        p.send_ids[(int64_t)pos * K + k] = mine ? e - d * p.experts_per_rank : -1;
+                        p.send_w[(int64_t)pos * K + k] = mine ? p.topk_w[t * K + k] : 0.0f;
+                    }
+                }
+                p.slot_pos[t * G + d] = pos;
+            }
+            carry += tile_total;
+            __syncthreads();
+        }
+    }
+}
+
+// out[i] = x[idx[i]] for rows of H elements (f32 or bf16), 16 bytes per thread.
+__global__ void __launch_bounds__(256)
+gather_rows_kernel(const void *x, int dtype, int64_t H, const int32_t *idx, int64_t n, void *out) {
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int64_t per_row = H * (dtype ? 2 : 4) / 16;
+    const int64_t total = n * per_row;
+    for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (int64_t)gridDim.x * 256) {
+        const int64_t r = i / per_row, c = i % per_row;
+        const uint4 *src = reinterpret_cast<const uint4 *>(x) + (int64_t)idx[r] * per_row + c;
+        reinterpret_cast<uint4 *>(out)[r * per_row + c] = __ldg(src);
+    }
+}
+
+// out[t] = sum over s ascending of rows[slot_pos[t][s]] (skipping -1), f32
+// accumulation, rows and out in `dtype`.
+__global__ void __launch_bounds__(256)
+combine_rows_kernel(const void *rows, int dtype, int64_t H, const int32_t *slot_pos, int S, int64_t T,
+                    void *out) {
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int64_t H4 = H / 4;
+    const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    if (i >= T * H4) return;
+    const int64_t t = i / H4, h = (i % H4) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < S; ++s) {
+        const int pos = slot_pos[t * S + s];
+        if (pos < 0) continue;
+        const float4 v = load_act4(rows, dtype, (int64_t)pos * H + h);
+        acc.x = __fadd_rn(acc.x, v.x);
+        acc.y = __fadd_rn(acc.y, v.y);
+        acc.z = __fadd_rn(acc.z, v.z);
+        acc.w = __fadd_rn(acc.w, v.w);
+    }
+    store_act4(out, dtype, t * H + h, acc);
+}
+
+}  // namespace
+
+cudaError_t launch_ep_plan(const EpPlanParams &p, cudaStream_t s) {
+    return launch_pdl(ep_plan_kernel, dim3(1), dim3(kPlanThreads), 0, s, p);
+}
+
+cudaError_t launch_gather_rows(const void *x, int dtype, int64_t H, const int32_t *idx, int64_t n,
+                               void *out, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    const int64_t total = n * (H * (dtype ? 2 : 4) / 16);
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    return launch_pdl(gather_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, s, x, dtype, H, idx, n,
+                      out);
+}
+
+cudaError_t launch_combine_rows(const void *rows, int dtype, int64_t H, const int32_t *slot_pos, int S,
+                                int64_t T, void *out, cudaStream_t s) {
+    const int64_t n = T * (H / 4);
+    if (n == 0) return cudaSuccess;
+    return launch_pdl(combine_rows_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, rows,
+                      dtype, H, slot_pos, S, T, out);
+}
+
+}  // namespace qmoe

@@ -189,6 +189,26 @@ constexpr int kPrefillTile = 256;  // tokens per work item (group chunk)
 bool make_tmap_bf16(CUtensorMap *tm, const void *base, uint64_t cols, uint64_t rows,
                     uint64_t row_stride, uint32_t box_cols, uint32_t box_rows, int swizzle);
 
+// ---- expert parallelism (ep.cu) -----------------------------------------
+struct EpPlanParams {
+    const int32_t *topk_idx;     // [T, K] global expert ids (-1 = none)
+    const float *topk_w;         // [T, K]
+    int64_t T;
+    int K;
+    int experts_per_rank, world; // world <= 32
+    int64_t capacity;            // 0: compact rows; > 0: rows of rank d at d * capacity (>= T)
+    int32_t *send_counts;        // [world]
+    int32_t *send_tok;           // [T * world] token of each send row
+    int32_t *send_ids;           // [T * world, K] local expert ids on the destination, -1 elsewhere
+    float *send_w;               // [T * world, K]
+    int32_t *slot_pos;           // [T, world] send row of (token, rank), -1 if none
+};
+cudaError_t launch_ep_plan(const EpPlanParams &p, cudaStream_t s);
+cudaError_t launch_gather_rows(const void *x, int dtype, int64_t H, const int32_t *idx, int64_t n,
+                               void *out, cudaStream_t s);
+cudaError_t launch_combine_rows(const void *rows, int dtype, int64_t H, const int32_t *slot_pos, int S,
+                                int64_t T, void *out, cudaStream_t s);
+
 // ---- combine -----------------------------------------------------------
 struct CombineParams {
     const float *y;              // [positions, H] expert outputs

@@ -8,6 +8,8 @@ from .capi import QmoeError
 from .layer import (Context, MoEConfig, PackedExpert, PackedQMoETensor, QMoELayer,
                     default_context)
 from . import quantize
+from .ep import ExpertParallelMoE, TorchComm
 
 __all__ = ["capi", "QmoeError", "Context", "MoEConfig", "PackedExpert",
-           "PackedQMoETensor", "QMoELayer", "default_context", "quantize"]
+           "PackedQMoETensor", "QMoELayer", "default_context", "quantize",
+           "ExpertParallelMoE", "TorchComm"]
