@@ -45,6 +45,9 @@ WORKLOAD = dict(
 REPLICAS = 4
 KERNELS_PER_FORWARD = 8  # router logits + select, permute, limbs x2, gate/up, down, combine
 KERNELS_PER_PREFILL = 7  # router logits + select, permute, bf16 gather, gate/up, down, combine
+# EP rank: router x2, plan, gather, routed experts (permute, limbs x2, GEMV x2,
+# combine), return combine, shared expert (permute, limbs x2, GEMV x2, combine)
+KERNELS_PER_EP_FORWARD = 17
 
 
 def parse():
@@ -163,19 +166,27 @@ def make_cfg():
                      norm_topk_prob=w["norm_topk"])
 
 
-def synth_weights(seed: int, device: str):
+def synth_weights(seed: int, device: str, experts=None):
+    """Seeded layer; each expert has its own generator (seed, expert id), so
+    ranks that build disjoint expert ranges agree on every expert, and all
+    ranks build the same gate and shared expert."""
     from qmoe_b200 import quantize as qz
     w = WORKLOAD
-    g = torch.Generator(device=device).manual_seed(seed)
 
-    def mat(o, i):
+    def gen(s):
+        return torch.Generator(device=device).manual_seed(s)
+
+    def mat(g, o, i):
         return qz.quantize_weight(torch.randn(o, i, generator=g, device=device) * 0.02)
 
-    experts = [[mat(w["I"], w["H"]), mat(w["I"], w["H"]), mat(w["H"], w["I"])]
-               for _ in range(w["E"])]
-    shared = [mat(w["Is"], w["H"]), mat(w["Is"], w["H"]), mat(w["H"], w["Is"])]
+    out = []
+    for e in (range(w["E"]) if experts is None else experts):
+        g = gen(seed * 1009 + 1 + e)
+        out.append([mat(g, w["I"], w["H"]), mat(g, w["I"], w["H"]), mat(g, w["H"], w["I"])])
+    g = gen(seed * 1009)
+    shared = [mat(g, w["Is"], w["H"]), mat(g, w["Is"], w["H"]), mat(g, w["H"], w["Is"])]
     gate_w = torch.randn(w["E"], w["H"], generator=g, device=device) * 0.02
-    return experts, shared, gate_w
+    return out, shared, gate_w
 
 
 def algorithmic_gate_up_bytes(idx_np: np.ndarray) -> float:
@@ -354,6 +365,112 @@ def run_prefill(layers, seed: int, dev: str, steps: int = 20):
     }
 
 
+def run_ep(args, ws, rank, local, dev, dist):
+    """N > 1: the layer expert-parallel over the N GPUs (each holds E/N
+    experts, a gate and shared-expert replica and its own 32 decode tokens),
+    NCCL all-to-all dispatch and return.  Weak scaling: tokens per GPU fixed."""
+    from qmoe_b200 import ExpertParallelMoE, default_context
+    w = WORKLOAD
+    cfg = make_cfg()
+    epr = w["E"] // ws
+    mine = range(rank * epr, (rank + 1) * epr)
+    # enough replicas that one rank's weights exceed L2 between reuses
+    per_rank_bytes = epr * (3 * w["H"] * w["I"] // 4) + 3 * w["H"] * w["Is"] // 4
+    reps = max(REPLICAS, -(-4 * 126 * 2**20 // per_rank_bytes))
+    ctx = default_context(local)
+    layers = []
+    for r in range(reps):
+        experts, shared, gate_w = synth_weights(args.seed + 1000 * r, dev, experts=mine)
+        layers.append(ExpertParallelMoE(cfg, gate_w, experts, rank, ws, shared=shared, ctx=ctx,
+                                        capacity=w["T"]))
+        del experts, shared
+    g = torch.Generator(device=dev).manual_seed(args.seed + 31 * rank)
+    xs = [torch.randn(w["T"], w["H"], generator=g, device=dev) for _ in range(reps)]
+    torch.cuda.synchronize()
+    for i in range(max(3, args.warmup)):
+        layers[i % reps].forward(xs[i % reps])
+    torch.cuda.synchronize()
+    dist.barrier()
+    # one CUDA graph per replica, the NCCL exchanges captured with the kernels
+    stream = torch.cuda.Stream()
+    graphs = []
+    with torch.cuda.stream(stream):
+        for r in range(reps):
+            layers[r].forward(xs[r])
+        torch.cuda.current_stream().synchronize()
+        for r in range(reps):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                layers[r].forward(xs[r])
+            graphs.append(gr)
+    torch.cuda.synchronize()
+    dist.barrier()
+    for i in range(max(3, args.warmup)):
+        graphs[i % reps].replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for i in range(args.steps):
+            graphs[i % reps].replay()
+        e1.record()
+        torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = ws * w["T"] * args.steps / (ms_max / 1e3)
+
+    # end to end: pinned host tokens in, host result out, every step
+    x_host = xs[0].cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    n_e2e = max(20, min(args.steps, 200))
+    for i in range(3):
+        out_host.copy_(layers[0].forward(x_host.to(dev, non_blocking=True)), non_blocking=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(n_e2e):
+        out_host.copy_(layers[0].forward(x_host.to(dev, non_blocking=True)), non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / n_e2e], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": w["name"], "T_per_gpu": w["T"], "E": w["E"],
+                       "top_k": w["k"], "hidden": w["H"], "intermediate": w["I"],
+                       "shared_intermediate": w["Is"], "activations": "f32",
+                       "parallelism": f"ep{ws}", "experts_per_gpu": epr,
+                       "exchange": "NCCL all_to_all_single, fixed-capacity rows",
+                       "l2": f"{reps} rotating weight replicas per GPU (> L2)",
+                       "graphs": "one CUDA graph per replica, NCCL exchanges captured"},
+            "roofline": None,
+            "e2e": {"value": ws * w["T"] / (e2e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": 4 * w["T"] * w["H"] * ws,
+                    "d2h_bytes_per_step": 4 * w["T"] * w["H"] * ws, "ms_per_step": e2e_ms},
+            "gpu_launches": KERNELS_PER_EP_FORWARD * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    for gr in graphs:
+        del gr
+    graphs.clear()
+    torch.cuda.synchronize()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_ours(args):
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -364,6 +481,7 @@ def run_ours(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(dev))
+        return run_ep(args, ws, rank, local, dev, dist)
     from qmoe_b200 import QMoELayer, default_context
     ctx = default_context(local)
     cfg = make_cfg()

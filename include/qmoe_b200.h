@@ -266,10 +266,11 @@ QMOE_API int qmoe_layer_set_path(qmoe_layer *layer, int path);
  *
  * qmoe_ep_plan: from this rank's routing (topk_idx [T, K] global ids, -1 =
  * none; topk_w [T, K]) the send list, destination-major with tokens in
- * order: send_counts [world], send_tok (token of each send row), send_ids
- * [rows, K] (local expert id on the destination, -1 for slots owned
- * elsewhere), send_w [rows, K], and slot_pos [T, world] (send row of
- * (token, rank), -1 if none).  capacity 0: compact rows (rows = sum of
+ * order: send_counts [world], send_tok (token of each send row), send_meta
+ * [rows, 2K] int32 (K local expert ids on the destination, -1 for slots
+ * owned elsewhere, then the bits of the K f32 weights), and slot_pos [T,
+ * world] (send row of (token, rank), -1 if none).  capacity 0: compact
+ * rows (rows = sum of
  * send_counts <= T * world, the buffers sized T * world); capacity C >= T:
  * rank d's rows start at d * C, the unused ones with ids -1, token 0 and
  * weight 0 (buffers of world * C rows), so every exchange has fixed sizes.
@@ -277,15 +278,26 @@ QMOE_API int qmoe_layer_set_path(qmoe_layer *layer, int path);
 QMOE_API int qmoe_ep_plan(qmoe_ctx *ctx, const int32_t *topk_idx, const float *topk_w,
                           int64_t T, int K, int experts_per_rank, int world,
                           int64_t capacity, int32_t *send_counts, int32_t *send_tok,
-                          int32_t *send_ids, float *send_w, int32_t *slot_pos);
+                          int32_t *send_meta, int32_t *slot_pos);
 /* out[i] = x[idx[i]] for n rows of H elements (f32 or bf16); H % 8 == 0. */
 QMOE_API int qmoe_gather_rows(qmoe_ctx *ctx, const void *x, int dtype, int64_t H,
                               const int32_t *idx, int64_t n, void *out);
 /* out[t] = rows[slot_pos[t][0]] + rows[slot_pos[t][1]] + ... (ascending s,
- * -1 skipped, f32 accumulation) for T rows of H elements in dtype; the
- * origin-side sum of the partials returned by each rank. */
+ * -1 skipped) + extra[t] (if extra is not NULL), f32 accumulation, for T
+ * rows of H elements in dtype: the origin-side sum of the partials each
+ * rank returned, then the shared expert's row. */
 QMOE_API int qmoe_combine_rows(qmoe_ctx *ctx, const void *rows, int dtype, int64_t H,
-                               const int32_t *slot_pos, int S, int64_t T, void *out);
+                               const int32_t *slot_pos, int S, int64_t T, const void *extra,
+                               void *out);
+/* One rank's experts over R received rows plus the shared expert: rows carry
+ * their routing as meta [R, 2K] int32 (local expert ids, -1 = skip, then the
+ * f32 weight bits, the layout of qmoe_ep_plan's send_meta); rows shared_row0
+ * .. R-1 also get the shared expert (the rank's own tokens, appended with
+ * ids -1).  out [R, H]: per row the weighted sum of its local experts in
+ * ascending order, plus the shared output for the shared rows.  Device
+ * pointers, asynchronous. */
+QMOE_API int qmoe_layer_forward_ep(qmoe_layer *layer, const void *x, int dtype, int64_t R,
+                                   const int32_t *meta, int64_t shared_row0, void *out);
 
 /* ---- tracing ----------------------------------------------------------- */
 

@@ -316,7 +316,7 @@ int qmoe_packed_forward(qmoe_packed *t, const float *x, int64_t batch, float *y,
     pp.e_begin = 0;
     pp.e_count = 1;
     pp.chunk = kDecodeTok;
-    pp.with_shared = 1;
+    pp.shared_count = batch;
     pp.seg_off = t->ngroups.as<int32_t>() + 2;   // [2..3]: the one segment's offsets
     pp.assign_pos = nullptr;
     pp.pos_tok = nullptr;
@@ -648,22 +648,34 @@ static int run_router(qmoe_layer *L, const void *xd, int dtype, int64_t T) {
     return QMOE_OK;
 }
 
-// Experts for routed assignments (topk ids relative to e_begin) plus, when
-// with_shared, the shared expert over all T rows; then the combine.
+// What one expert pass computes over its T rows: routed assignments
+// (topk ids relative to e_begin, row stride topk_ld, -1 = skip) and the
+// shared expert over rows shared_row0 .. shared_row0 + shared_count - 1.
+struct ExpertsArgs {
+    const int32_t *topk_idx = nullptr;
+    const float *topk_w = nullptr;
+    int topk_ld = 0;
+    int e_begin = 0;
+    int64_t shared_row0 = 0, shared_count = 0;
+};
+
 // Weighted sum of each token's expert rows in ascending expert order, plus
 // the shared expert's row (src/moe.rs:117-125, src/model.rs:386-389).
-static int run_combine(qmoe_layer *L, int64_t T, const int32_t *topk_idx, const float *topk_w,
-                       bool with_shared, void *outd, int dtype, int accumulate) {
+static int run_combine(qmoe_layer *L, int64_t T, const ExpertsArgs &a, void *outd, int dtype,
+                       int accumulate) {
     const qmoe_moe_config &c = L->cfg;
     CombineParams cp{};
     cp.y = L->y.as<float>();
     cp.assign_pos = L->assign_pos.as<int32_t>();
-    cp.topk_idx = topk_idx;
-    cp.topk_w = topk_w;
+    cp.topk_idx = a.topk_idx;
+    cp.topk_w = a.topk_w;
     cp.T = T;
     cp.K = c.top_k;
+    cp.topk_ld = a.topk_ld;
     cp.H = c.hidden_dim;
-    cp.y_shared = with_shared ? L->y.as<float>() + T * c.top_k * c.hidden_dim : nullptr;
+    cp.y_shared = a.shared_count ? L->y.as<float>() + T * c.top_k * c.hidden_dim : nullptr;
+    cp.shared_row0 = a.shared_row0;
+    cp.shared_count = a.shared_count;
     cp.accumulate = accumulate;
     cp.out = outd;
     cp.out_dtype = dtype;
@@ -675,8 +687,9 @@ static int run_combine(qmoe_layer *L, int64_t T, const int32_t *topk_idx, const 
 
 // Prefill expert products: gather the bf16 rows of every position, gate/up
 // GEMM with SwiGLU into bf16 rows, down GEMM into f32 rows of y.
-static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, bool with_shared,
+static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, const ExpertsArgs &a,
                        const int32_t *n_valid, int *err) {
+    const bool with_shared = a.shared_count > 0;
     const qmoe_moe_config &c = L->cfg;
     cudaStream_t st = L->ctx->stream;
     const int64_t TK = T * c.top_k;
@@ -688,6 +701,7 @@ static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, b
     gp.pos_tok = L->pos_tok.as<int32_t>();
     gp.n_valid = n_valid;
     gp.shared_base = TK;
+    gp.shared_row0 = a.shared_row0;
     gp.npos = npos;
     gp.xg = L->xg.p;
     mark(L, 2);
@@ -742,10 +756,10 @@ static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, b
     return QMOE_OK;
 }
 
-static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
-                       const int32_t *topk_idx, const float *topk_w, int e_begin,
-                       bool with_shared, void *outd, int accumulate) {
+static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, const ExpertsArgs &a,
+                       void *outd, int accumulate) {
     const qmoe_moe_config &c = L->cfg;
+    const bool with_shared = a.shared_count > 0;
     cudaStream_t st = L->ctx->stream;
     const int K = c.top_k;
     const int64_t TK = T * K;
@@ -765,13 +779,14 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
         prefill = per_seg >= kPrefillMinRows;
     }
     PermuteParams pp{};
-    pp.topk_idx = topk_idx;
+    pp.topk_idx = a.topk_idx;
     pp.T = T;
     pp.K = K;
-    pp.e_begin = e_begin;
+    pp.topk_ld = a.topk_ld;
+    pp.e_begin = a.e_begin;
     pp.e_count = L->e_count;
     pp.chunk = prefill ? kPrefillTile : kDecodeTok;
-    pp.with_shared = with_shared ? 1 : 0;
+    pp.shared_count = a.shared_count;
     pp.seg_off = L->seg_off.as<int32_t>();
     pp.assign_pos = L->assign_pos.as<int32_t>();
     pp.pos_tok = L->pos_tok.as<int32_t>();
@@ -780,12 +795,12 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     mark(L, 1);
     QTRY_CUDA(launch_permute(pp, st));
 
-    const int64_t npos = TK + (with_shared ? T : 0);
+    const int64_t npos = TK + a.shared_count;
     const int32_t *n_valid = L->seg_off.as<int32_t>() + L->e_count;
     int *err = device_error_flag();
     if (prefill) {
-        QTRY(run_prefill(L, xd, T, npos, with_shared, n_valid, err));
-        return run_combine(L, T, topk_idx, topk_w, with_shared, outd, dtype, accumulate);
+        QTRY(run_prefill(L, xd, T, npos, a, n_valid, err));
+        return run_combine(L, T, a, outd, dtype, accumulate);
     }
 
     // gate/up: activations -> limbs, then the tensor-core GEMV with SwiGLU
@@ -795,6 +810,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     q1.act_ld = c.hidden_dim;
     q1.pos_tok = L->pos_tok.as<int32_t>();
     q1.shared_base = TK;
+    q1.shared_row0 = a.shared_row0;
     q1.n_valid = n_valid;
     q1.npos = npos;
     q1.K = c.hidden_dim;
@@ -877,7 +893,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T,
     g1.err = err;
     QTRY_CUDA(launch_qgemv_imma(1, m1, g1, L->sm_count, st));
 
-    return run_combine(L, T, topk_idx, topk_w, with_shared, outd, dtype, accumulate);
+    return run_combine(L, T, a, outd, dtype, accumulate);
 }
 
 static int finish_out(qmoe_layer *L, void *user, const void *dev, size_t bytes, int ptr_kind) {
@@ -912,8 +928,12 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
         outd = L->io_out.p;
     }
     QTRY(run_router(L, xd, dtype, T));
-    QTRY(run_experts(L, xd, dtype, T, L->topk_idx.as<int32_t>(), L->topk_w.as<float>(), 0,
-                     L->has_shared, outd, 0));
+    ExpertsArgs a;
+    a.topk_idx = L->topk_idx.as<int32_t>();
+    a.topk_w = L->topk_w.as<float>();
+    a.topk_ld = c.top_k;
+    a.shared_count = L->has_shared ? T : 0;
+    QTRY(run_experts(L, xd, dtype, T, a, outd, 0));
     const size_t kb = sizeof(int32_t) * T * c.top_k;
     if (topk_idx)
         QTRY_CUDA(cudaMemcpyAsync(topk_idx, L->topk_idx.p, kb,
@@ -984,14 +1004,40 @@ int qmoe_layer_forward_routed(qmoe_layer *L, const void *x, int dtype, int64_t R
         QTRY(grow(L->io_out, xbytes));
         outd = L->io_out.p;
     }
-    QTRY(run_experts(L, xd, dtype, R, static_cast<const int32_t *>(id),
-                     static_cast<const float *>(wd), 0, false, outd, 0));
+    ExpertsArgs a;
+    a.topk_idx = static_cast<const int32_t *>(id);
+    a.topk_w = static_cast<const float *>(wd);
+    a.topk_ld = c.top_k;
+    QTRY(run_experts(L, xd, dtype, R, a, outd, 0));
     QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
     if (ptr_kind == QMOE_PTR_HOST) {
         QTRY_CUDA(cudaStreamSynchronize(st));
         QTRY(check_device_error());
     }
     return QMOE_OK;
+}
+
+int qmoe_layer_forward_ep(qmoe_layer *L, const void *x, int dtype, int64_t R, const int32_t *meta,
+                          int64_t shared_row0, void *out) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    QTRY(check_dtype(dtype));
+    if (R < 0 || shared_row0 < 0 || shared_row0 > R)
+        return fail(QMOE_ERR_INVALID, "bad rows (R %lld, shared_row0 %lld)", (long long)R,
+                    (long long)shared_row0);
+    if (R > 0 && (!x || !meta || !out)) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (R == 0) return QMOE_OK;
+    QTRY(check_align(x, QMOE_PTR_DEVICE, "x"));
+    QTRY(check_align(out, QMOE_PTR_DEVICE, "out"));
+    DeviceGuard g(L->ctx->device);
+    QTRY(layer_reserve(L, R));
+    const int K = L->cfg.top_k;
+    ExpertsArgs a;
+    a.topk_idx = meta;
+    a.topk_w = reinterpret_cast<const float *>(meta + K);
+    a.topk_ld = 2 * K;
+    a.shared_row0 = shared_row0;
+    a.shared_count = L->has_shared ? R - shared_row0 : 0;
+    return run_experts(L, x, dtype, R, a, out, 0);
 }
 
 int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
@@ -1022,7 +1068,9 @@ int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T
     // a shared-only pass: no routed assignments (top_k slots all skipped)
     qmoe_moe_config saved = L->cfg;
     L->cfg.top_k = 0;
-    int rc = run_experts(L, xd, dtype, T, nullptr, nullptr, 0, true, outd, accumulate);
+    ExpertsArgs a;
+    a.shared_count = T;
+    int rc = run_experts(L, xd, dtype, T, a, outd, accumulate);
     L->cfg = saved;
     if (rc != QMOE_OK) return rc;
     QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
@@ -1039,14 +1087,14 @@ int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T
 
 int qmoe_ep_plan(qmoe_ctx *ctx, const int32_t *topk_idx, const float *topk_w, int64_t T, int K,
                  int experts_per_rank, int world, int64_t capacity, int32_t *send_counts,
-                 int32_t *send_tok, int32_t *send_ids, float *send_w, int32_t *slot_pos) {
+                 int32_t *send_tok, int32_t *send_meta, int32_t *slot_pos) {
     if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
     if (T < 0 || K <= 0 || experts_per_rank <= 0 || world <= 0 || world > 32)
         return fail(QMOE_ERR_INVALID, "bad plan shape (T %lld, K %d, experts_per_rank %d, world %d)",
                     (long long)T, K, experts_per_rank, world);
     if (capacity < 0 || (capacity > 0 && capacity < T))
         return fail(QMOE_ERR_INVALID, "capacity %lld < T %lld", (long long)capacity, (long long)T);
-    if (!send_counts || (T > 0 && (!topk_idx || !topk_w || !send_tok || !send_ids || !send_w || !slot_pos)))
+    if (!send_counts || (T > 0 && (!topk_idx || !topk_w || !send_tok || !send_meta || !slot_pos)))
         return fail(QMOE_ERR_INVALID, "NULL argument");
     DeviceGuard g(ctx->device);
     EpPlanParams p{};
@@ -1059,8 +1107,7 @@ int qmoe_ep_plan(qmoe_ctx *ctx, const int32_t *topk_idx, const float *topk_w, in
     p.capacity = capacity;
     p.send_counts = send_counts;
     p.send_tok = send_tok;
-    p.send_ids = send_ids;
-    p.send_w = send_w;
+    p.send_meta = send_meta;
     p.slot_pos = slot_pos;
     QTRY_CUDA(launch_ep_plan(p, ctx->stream));
     return QMOE_OK;
@@ -1080,14 +1127,15 @@ int qmoe_gather_rows(qmoe_ctx *ctx, const void *x, int dtype, int64_t H, const i
 }
 
 int qmoe_combine_rows(qmoe_ctx *ctx, const void *rows, int dtype, int64_t H, const int32_t *slot_pos,
-                      int S, int64_t T, void *out) {
+                      int S, int64_t T, const void *extra, void *out) {
     if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
     QTRY(check_dtype(dtype));
     if (H <= 0 || H % 4 || S <= 0 || T < 0) return fail(QMOE_ERR_INVALID, "bad shape");
     if (T > 0 && (!slot_pos || !out)) return fail(QMOE_ERR_INVALID, "NULL argument");
     QTRY(check_align(out, QMOE_PTR_DEVICE, "out"));
     DeviceGuard g(ctx->device);
-    QTRY_CUDA(launch_combine_rows(rows, dtype, H, slot_pos, S, T, out, ctx->stream));
+    if (extra) QTRY(check_align(extra, QMOE_PTR_DEVICE, "extra"));
+    QTRY_CUDA(launch_combine_rows(rows, dtype, H, slot_pos, S, T, extra, out, ctx->stream));
     return QMOE_OK;
 }
 

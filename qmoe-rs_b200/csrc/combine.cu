@@ -24,16 +24,16 @@ combine_kernel(const CombineParams p) {
     if (i >= p.T * H4) return;
     const int64_t t = i / H4;
     const int h = (int)(i % H4) * 4;
-    const int K = p.K;
+    const int K = p.K, ld = p.topk_ld;
 
     // slots of this token in ascending expert order (insertion sort, K small)
     int ord[kMaxK];
     int n = 0;
     for (int j = 0; j < K; ++j) {
         if (p.assign_pos[t * K + j] < 0) continue;
-        const int e = p.topk_idx[t * K + j];
+        const int e = p.topk_idx[t * ld + j];
         int b = n - 1;
-        while (b >= 0 && p.topk_idx[t * K + ord[b]] > e) {
+        while (b >= 0 && p.topk_idx[t * ld + ord[b]] > e) {
             ord[b + 1] = ord[b];
             --b;
         }
@@ -43,7 +43,7 @@ combine_kernel(const CombineParams p) {
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
     for (int q = 0; q < n; ++q) {
         const int j = ord[q];
-        const float w = p.topk_w[t * K + j];
+        const float w = p.topk_w[t * ld + j];
         const float4 y = *reinterpret_cast<const float4 *>(
             p.y + (int64_t)p.assign_pos[t * K + j] * p.H + h);
         a0 = __fadd_rn(a0, __fmul_rn(y.x, w));
@@ -51,8 +51,8 @@ combine_kernel(const CombineParams p) {
         a2 = __fadd_rn(a2, __fmul_rn(y.z, w));
         a3 = __fadd_rn(a3, __fmul_rn(y.w, w));
     }
-    if (p.y_shared) {
-        const float4 s = *reinterpret_cast<const float4 *>(p.y_shared + t * p.H + h);
+    if (p.y_shared && t >= p.shared_row0 && t < p.shared_row0 + p.shared_count) {
+        const float4 s = *reinterpret_cast<const float4 *>(p.y_shared + (t - p.shared_row0) * p.H + h);
         a0 = __fadd_rn(a0, s.x);
         a1 = __fadd_rn(a1, s.y);
         a2 = __fadd_rn(a2, s.z);

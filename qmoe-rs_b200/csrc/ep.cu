@@ -23,9 +23,9 @@ constexpr int kPlanThreads = 1024;
 // every exchange has fixed sizes and needs no count on the host):
 //   send_counts[d]          tokens sent to rank d
 //   send_tok[s]             token of send row s
-//   send_ids[s][k]          local expert id of slot k on the destination, -1
-//                           if slot k goes elsewhere
-//   send_w[s][k]            that slot's combine weight (0 if -1)
+//   send_meta[s][k]         local expert id of slot k on the destination, -1
+//                           if slot k goes elsewhere (k < K)
+//   send_meta[s][K + k]     the bits of that slot's f32 combine weight (0 if -1)
 //   slot_pos[t][d]          send row of (t, d), -1 if t sends nothing to d
 // One CTA; tokens in tiles of 1024, one per thread; per destination a block
 // scan of the "sends to d" bits gives each token its row.
@@ -43,8 +43,8 @@ ep_plan_kernel(const EpPlanParams p) {
         for (int64_t i = tid; i < (int64_t)G * p.capacity; i += kPlanThreads) {
             p.send_tok[i] = 0;
             for (int k = 0; k < K; ++k) {
-                p.send_ids[i * K + k] = -1;
-                p.send_w[i * K + k] = 0.0f;
+                p.send_meta[i * 2 * K + k] = -1;
+                p.send_meta[i * 2 * K + K + k] = 0;
             }
         }
     // pass 1: tokens per destination
@@ -107,8 +107,9 @@ ep_plan_kernel(const EpPlanParams p) {
                     for (int k = 0; k < K; ++k) {
                         const int e = p.topk_idx[t * K + k];
                         const bool mine = e >= 0 && e / p.experts_per_rank == d;
-                        p.send_ids[(int64_t)pos * K + k] = mine ? e - d * p.experts_per_rank : -1;
-                        p.send_w[(int64_t)pos * K + k] = mine ? p.topk_w[t * K + k] : 0.0f;
+                        int32_t *m = p.send_meta + (int64_t)pos * 2 * K;
+                        m[k] = mine ? e - d * p.experts_per_rank : -1;
+                        m[K + k] = mine ? __float_as_int(p.topk_w[t * K + k]) : 0;
                     }
                 }
                 p.slot_pos[t * G + d] = pos;
@@ -133,11 +134,11 @@ gather_rows_kernel(const void *x, int dtype, int64_t H, const int32_t *idx, int6
     }
 }
 
-// out[t] = sum over s ascending of rows[slot_pos[t][s]] (skipping -1), f32
-// accumulation, rows and out in `dtype`.
+// out[t] = sum over s ascending of rows[slot_pos[t][s]] (skipping -1), then
+// + extra[t] if given; f32 accumulation, rows, extra and out in `dtype`.
 __global__ void __launch_bounds__(256)
 combine_rows_kernel(const void *rows, int dtype, int64_t H, const int32_t *slot_pos, int S, int64_t T,
-                    void *out) {
+                    const void *extra, void *out) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int64_t H4 = H / 4;
@@ -149,6 +150,13 @@ combine_rows_kernel(const void *rows, int dtype, int64_t H, const int32_t *slot_
         const int pos = slot_pos[t * S + s];
         if (pos < 0) continue;
         const float4 v = load_act4(rows, dtype, (int64_t)pos * H + h);
+        acc.x = __fadd_rn(acc.x, v.x);
+        acc.y = __fadd_rn(acc.y, v.y);
+        acc.z = __fadd_rn(acc.z, v.z);
+        acc.w = __fadd_rn(acc.w, v.w);
+    }
+    if (extra) {
+        const float4 v = load_act4(extra, dtype, t * H + h);
         acc.x = __fadd_rn(acc.x, v.x);
         acc.y = __fadd_rn(acc.y, v.y);
         acc.z = __fadd_rn(acc.z, v.z);
@@ -174,11 +182,11 @@ cudaError_t launch_gather_rows(const void *x, int dtype, int64_t H, const int32_
 }
 
 cudaError_t launch_combine_rows(const void *rows, int dtype, int64_t H, const int32_t *slot_pos, int S,
-                                int64_t T, void *out, cudaStream_t s) {
+                                int64_t T, const void *extra, void *out, cudaStream_t s) {
     const int64_t n = T * (H / 4);
     if (n == 0) return cudaSuccess;
     return launch_pdl(combine_rows_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, rows,
-                      dtype, H, slot_pos, S, T, out);
+                      dtype, H, slot_pos, S, T, extra, out);
 }
 
 }  // namespace qmoe

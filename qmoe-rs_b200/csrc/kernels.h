@@ -39,12 +39,13 @@ cudaError_t launch_router(const RouterParams &p, cudaStream_t s);
 // Builds per-expert segments of routed (token, slot) assignments, stable in
 // token order, and the token-group work list of the grouped kernels.
 struct PermuteParams {
-    const int32_t *topk_idx;   // [T, K]; ids outside [e_begin, e_begin+e_count) skipped
+    const int32_t *topk_idx;   // [T, K] (row stride topk_ld); ids outside [e_begin,
+                               // e_begin+e_count) skipped
     int64_t T;
-    int K;
+    int K, topk_ld;
     int e_begin, e_count;
     int chunk;                 // tokens per group descriptor
-    int with_shared;           // append groups covering all T tokens (segment e_count)
+    int64_t shared_count;      // append groups over this many shared positions (segment e_count)
     int32_t *seg_off;          // [e_count + 1] routed segment offsets
     int32_t *assign_pos;       // [T, K] position of each assignment, -1 if skipped
     int32_t *pos_tok;          // [T*K] token of each routed position
@@ -91,7 +92,8 @@ struct QuantParams {
     int dtype;
     int64_t act_ld;
     const int32_t *pos_tok;      // routed position -> row (nullable: row = pos)
-    int64_t shared_base;         // positions >= this are shared rows pos - base
+    int64_t shared_base;         // positions >= this are shared: row shared_row0 + pos - base
+    int64_t shared_row0;
     const int32_t *n_valid;      // routed positions >= *n_valid are skipped (nullable)
     int64_t npos;                // positions (grid size)
     int K, K_s;                  // row length of routed / shared rows
@@ -155,7 +157,8 @@ struct GatherParams {
     int64_t H;
     const int32_t *pos_tok;      // routed position -> token
     const int32_t *n_valid;      // routed positions in use (device)
-    int64_t shared_base;         // first shared position; shared rows = tokens 0..T-1
+    int64_t shared_base;         // first shared position: row shared_row0 + pos - base
+    int64_t shared_row0;
     int64_t npos;                // positions (routed slots + shared rows)
     void *xg;                    // [npos, H] bf16, blocks permuted
 };
@@ -199,25 +202,26 @@ struct EpPlanParams {
     int64_t capacity;            // 0: compact rows; > 0: rows of rank d at d * capacity (>= T)
     int32_t *send_counts;        // [world]
     int32_t *send_tok;           // [T * world] token of each send row
-    int32_t *send_ids;           // [T * world, K] local expert ids on the destination, -1 elsewhere
-    float *send_w;               // [T * world, K]
+    int32_t *send_meta;          // [rows, 2K]: local expert ids on the destination (-1
+                                 // elsewhere), then the f32 weight bits
     int32_t *slot_pos;           // [T, world] send row of (token, rank), -1 if none
 };
 cudaError_t launch_ep_plan(const EpPlanParams &p, cudaStream_t s);
 cudaError_t launch_gather_rows(const void *x, int dtype, int64_t H, const int32_t *idx, int64_t n,
                                void *out, cudaStream_t s);
 cudaError_t launch_combine_rows(const void *rows, int dtype, int64_t H, const int32_t *slot_pos, int S,
-                                int64_t T, void *out, cudaStream_t s);
+                                int64_t T, const void *extra, void *out, cudaStream_t s);
 
 // ---- combine -----------------------------------------------------------
 struct CombineParams {
     const float *y;              // [positions, H] expert outputs
     const int32_t *assign_pos;   // [T, K]
-    const int32_t *topk_idx;     // [T, K] (expert order of the accumulation)
-    const float *topk_w;         // [T, K]
+    const int32_t *topk_idx;     // [T, K] row stride topk_ld (expert order of the accumulation)
+    const float *topk_w;         // [T, K] row stride topk_ld
     int64_t T;
-    int K, H;
-    const float *y_shared;       // [T, H] or nullptr
+    int K, topk_ld, H;
+    const float *y_shared;       // [shared_count, H] for rows shared_row0.. or nullptr
+    int64_t shared_row0, shared_count;
     int accumulate;              // add into out instead of overwriting
     void *out;                   // [T, H]
     int out_dtype;

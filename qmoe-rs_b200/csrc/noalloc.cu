@@ -127,7 +127,7 @@ extern "C" int qmoe_packed_forward_noalloc(int device, void *stream, const uint8
         pp.e_begin = 0;
         pp.e_count = 1;
         pp.chunk = kQgemvTokens;
-        pp.with_shared = 1;
+        pp.shared_count = batch;
         pp.seg_off = counters + 2;
         pp.assign_pos = nullptr;
         pp.pos_tok = nullptr;

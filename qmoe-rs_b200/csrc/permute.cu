@@ -47,7 +47,7 @@ permute_kernel(const PermuteParams p) {
 
     // 1. counts
     for (int64_t a = tid; a < TK; a += kPermThreads) {
-        const int e = p.topk_idx[a] - p.e_begin;
+        const int e = p.topk_idx[(a / K) * p.topk_ld + a % K] - p.e_begin;
         if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
@@ -103,15 +103,16 @@ permute_kernel(const PermuteParams p) {
         p.seg_off[E] = carry_pos;
         p.n_groups[0] = carry_grp;
         int ns = 0;
-        if (p.with_shared) ns = (int)((T + p.chunk - 1) / p.chunk);
+        if (p.shared_count) ns = (int)((p.shared_count + p.chunk - 1) / p.chunk);
         p.n_groups[1] = ns;
     }
-    if (p.with_shared) {
-        const int ns = (int)((T + p.chunk - 1) / p.chunk);
+    if (p.shared_count) {
+        const int64_t S = p.shared_count;
+        const int ns = (int)((S + p.chunk - 1) / p.chunk);
         for (int g = tid; g < ns; g += kPermThreads) {
             const int64_t b = (int64_t)g * p.chunk;
             p.groups[carry_grp + g] =
-                make_int4(E, (int)(TK + b), (int)(T - b < p.chunk ? T - b : p.chunk), 0);
+                make_int4(E, (int)(TK + b), (int)(S - b < p.chunk ? S - b : p.chunk), 0);
         }
     }
     __syncthreads();
@@ -124,7 +125,7 @@ permute_kernel(const PermuteParams p) {
         const bool live = t < T;
         if (live) {
             for (int j = 0; j < K; ++j) {
-                const int e = p.topk_idx[t * K + j] - p.e_begin;
+                const int e = p.topk_idx[t * p.topk_ld + j] - p.e_begin;
                 if (e >= 0 && e < E) atomicOr(&bm[warp * E + e], 1u << lane);
             }
         }
@@ -141,7 +142,7 @@ permute_kernel(const PermuteParams p) {
         if (live) {
             const uint32_t below = (1u << lane) - 1u;
             for (int j = 0; j < K; ++j) {
-                const int e = p.topk_idx[t * K + j] - p.e_begin;
+                const int e = p.topk_idx[t * p.topk_ld + j] - p.e_begin;
                 int pos = -1;
                 if (e >= 0 && e < E) {
                     pos = off[e] + wpre[warp * E + e] + __popc(bm[warp * E + e] & below);

@@ -456,7 +456,7 @@ gather_bf16_kernel(const GatherParams p) {
         const int64_t pos = i / nblk, b = i % nblk;
         const bool routed = pos < p.shared_base;
         if (routed && pos >= nvalid) continue;
-        const int64_t row = routed ? (int64_t)p.pos_tok[pos] : pos - p.shared_base;
+        const int64_t row = routed ? (int64_t)p.pos_tok[pos] : p.shared_row0 + pos - p.shared_base;
         const uint4 *src = reinterpret_cast<const uint4 *>(
             reinterpret_cast<const __nv_bfloat16 *>(p.x) + row * p.H + 16 * b);
         const uint4 a = __ldg(src), c = __ldg(src + 1);

@@ -27,7 +27,7 @@ quant_kernel(const QuantParams p) {
     const bool routed = pos < p.shared_base;
     if (routed && p.n_valid && pos >= *p.n_valid) return;  // unused routed slot
     int64_t row = pos;
-    if (p.pos_tok) row = routed ? (int64_t)p.pos_tok[pos] : pos - p.shared_base;
+    if (p.pos_tok) row = routed ? (int64_t)p.pos_tok[pos] : p.shared_row0 + pos - p.shared_base;
     const int64_t base = row * p.act_ld;
     const int K = routed ? p.K : p.K_s, tid = threadIdx.x;
     const int nblk = ((K + 255) / 256) * 16;  // blocks the GEMV reads (K padded to 256)

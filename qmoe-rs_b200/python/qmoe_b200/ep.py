@@ -10,14 +10,15 @@ the batch.  One forward on every rank:
   2. plan (qmoe_ep_plan): every token goes once to each rank that owns one
      of its experts, with that rank's local expert ids and weights;
   3. dispatch: all-to-all of the token rows and of their (ids, weights);
-  4. run the local experts on what arrived (qmoe_layer_forward_routed): one
-     partial sum per received row, over this rank's experts in ascending
-     order;
+  4. run the local experts on what arrived, and the shared expert on the
+     rank's own tokens appended after them, in one pass
+     (qmoe_layer_forward_ep): one partial sum per received row, over this
+     rank's experts in ascending order;
   5. return: all-to-all of the partial rows back to their origin;
   6. combine (qmoe_combine_rows): add each token's partials in ascending
      rank order -- ascending expert blocks, the reference's expert order --
-     then add the shared expert's output (qmoe_layer_shared_forward with
-     accumulate; src/model.rs:386-389: routed sum first, then + shared).
+     then the shared expert's row (src/model.rs:386-389: routed sum first,
+     then + shared).
 
 The exchanges use fixed-size buffers (each destination gets `capacity` rows,
 unused rows carry expert ids -1 and are skipped), so a forward needs no
@@ -82,19 +83,20 @@ class ExpertParallelMoE:
         return self.layer.route(x)
 
     def plan(self, idx, w, T: int):
+        """Send list: counts [G], tokens [G*C], meta [G*C, 2K] (local ids, then
+        weight bits), slot [T, G] (send row of (token, rank))."""
         G, K, C = self.world, self.config.top_k, self.capacity
         dev = idx.device
         b = self._buf("plan", lambda: dict(
             counts=torch.empty(G, dtype=torch.int32, device=dev),
             tok=torch.empty(G * C, dtype=torch.int32, device=dev),
-            ids=torch.empty(G * C, K, dtype=torch.int32, device=dev),
-            w=torch.empty(G * C, K, dtype=torch.float32, device=dev),
+            meta=torch.empty(G * C, 2 * K, dtype=torch.int32, device=dev),
             slot=torch.empty(C, G, dtype=torch.int32, device=dev)))
         self.layer.ctx.use_current_torch_stream()
         capi.call("qmoe_ep_plan", self.layer.ctx.handle, idx.data_ptr(), w.data_ptr(), T, K,
                   self.epr, G, C, b["counts"].data_ptr(), b["tok"].data_ptr(),
-                  b["ids"].data_ptr(), b["w"].data_ptr(), b["slot"].data_ptr())
-        return b["counts"], b["tok"], b["ids"], b["w"], b["slot"][:T]
+                  b["meta"].data_ptr(), b["slot"].data_ptr())
+        return b["counts"], b["tok"], b["meta"], b["slot"][:T]
 
     def gather(self, x, tok):
         H = x.shape[1]
@@ -105,63 +107,86 @@ class ExpertParallelMoE:
                   tok.data_ptr(), tok.numel(), out.data_ptr())
         return out
 
-    def experts(self, rx, rids, rw):
-        return self.layer.forward_routed(rx, rids, rw)
+    def run_rows(self, rows, meta, R: int, shared_row0: int):
+        """Local experts over rows[:R] (routing in meta) + the shared expert
+        over rows shared_row0..R-1."""
+        H = rows.shape[1]
+        y = self._buf(("y", rows.dtype), lambda: torch.empty(rows.shape[0], H, dtype=rows.dtype,
+                                                              device=rows.device))
+        self.layer.ctx.use_current_torch_stream()
+        capi.call("qmoe_layer_forward_ep", self.layer._h, rows.data_ptr(), _dt(rows), R,
+                  meta.data_ptr(), shared_row0, y.data_ptr())
+        return y
 
-    def combine(self, back, slot, T: int, dtype):
+    def combine(self, back, slot, extra, T: int, dtype):
         H = back.shape[1]
         out = torch.empty(T, H, dtype=dtype, device=back.device)
         self.layer.ctx.use_current_torch_stream()
         capi.call("qmoe_combine_rows", self.layer.ctx.handle, back.data_ptr(), _dt(back), H,
-                  slot.data_ptr(), self.world, T, out.data_ptr())
-        return out
-
-    def shared_add(self, x, out):
-        if self.has_shared:
-            self.layer.shared_forward(x, out=out)
+                  slot.data_ptr(), self.world, T,
+                  extra.data_ptr() if extra is not None else None, out.data_ptr())
         return out
 
     # -- forward ------------------------------------------------------------
     def dispatch(self, x):
         """Steps 1-2: route, plan, gather.  Returns (state, rows, meta): the
-        send rows [world * capacity, H] and their (local ids, weight bits)
-        [world * capacity, 2K] int32, destination d's block at d * capacity."""
+        send rows [world * capacity, H] and their meta [world * capacity, 2K]
+        int32, destination d's block at d * capacity."""
         T, H = x.shape
         if T > self.capacity:
             raise ValueError(f"T {T} > capacity {self.capacity}")
         idx, w = self.route(x)
-        counts, tok, ids, wts, slot = self.plan(idx, w, T)
+        counts, tok, meta, slot = self.plan(idx, w, T)
         rows = self.gather(x, tok)
-        meta = torch.cat([ids, wts.view(torch.int32)], dim=1)
         return (x, slot, idx, w), rows, meta
 
-    def compute(self, rows, meta):
-        """Step 4: this rank's experts on the received rows (block r from rank
-        r), one partial row per received row."""
-        K = self.config.top_k
-        rids = meta[:, :K].contiguous()
-        rw = meta[:, K:].contiguous().view(torch.float32)
-        return self.experts(rows, rids, rw)
+    def recv_buffers(self, x):
+        """Receive rows [world*C + C, H] and meta [world*C + C, 2K]: the first
+        world*C rows are the all-to-all targets, the last C rows take this
+        rank's own tokens for the shared expert (their expert ids stay -1)."""
+        G, C, K = self.world, self.capacity, self.config.top_k
+        H = x.shape[1]
+        rx = self._buf(("rx", x.dtype), lambda: torch.empty(G * C + C, H, dtype=x.dtype,
+                                                              device=x.device))
 
-    def finish(self, state, back):
-        """Step 6: add each token's returned partials in ascending rank order,
-        then the shared expert."""
+        def make_meta():
+            m = torch.zeros(G * C + C, 2 * K, dtype=torch.int32, device=x.device)
+            m[:, :K] = -1
+            return m
+        return rx, self._buf("rmeta", make_meta)
+
+    def compute(self, rx, rmeta, x):
+        """Step 4: this rank's experts on the received rows rx[:world*C]
+        (block r from rank r) and the shared expert on its own tokens x.
+        Returns y: rows [:world*C] the partials to return, rows
+        [world*C : world*C + T] the shared expert's output for x."""
+        GC, T = self.world * self.capacity, x.shape[0]
+        if self.has_shared:
+            rx[GC:GC + T].copy_(x)
+            return self.run_rows(rx, rmeta, GC + T, GC)
+        return self.run_rows(rx, rmeta, GC, GC)
+
+    def finish(self, state, back, y):
+        """Step 6: each token's returned partials in ascending rank order, then
+        the shared expert's row."""
         x, slot, _, _ = state
-        out = self.combine(back, slot, x.shape[0], x.dtype)
-        return self.shared_add(x, out)
+        GC, T = self.world * self.capacity, x.shape[0]
+        extra = y[GC:GC + T] if self.has_shared else None
+        return self.combine(back, slot, extra, T, x.dtype)
 
     def forward(self, x, return_routing: bool = False):
         if self.comm is None:
             self.comm = TorchComm()
+        GC = self.world * self.capacity
         state, rows, meta = self.dispatch(x)
-        rx = self._buf(("rx", rows.dtype), lambda: torch.empty_like(rows))
-        rmeta = self._buf("rmeta", lambda: torch.empty_like(meta))
-        self.comm.all_to_all(rx, rows)
-        self.comm.all_to_all(rmeta, meta)
-        y = self.compute(rx, rmeta)
-        back = self._buf(("back", y.dtype), lambda: torch.empty_like(y))
-        self.comm.all_to_all(back, y)
-        out = self.finish(state, back)
+        rx, rmeta = self.recv_buffers(x)
+        self.comm.all_to_all(rx[:GC], rows)
+        self.comm.all_to_all(rmeta[:GC], meta)
+        y = self.compute(rx, rmeta, x)
+        back = self._buf(("back", y.dtype), lambda: torch.empty(GC, y.shape[1], dtype=y.dtype,
+                                                                device=y.device))
+        self.comm.all_to_all(back, y[:GC])
+        out = self.finish(state, back, y)
         if return_routing:
             return out, state[2], state[3]
         return out

@@ -69,19 +69,28 @@ class HostRank(ExpertParallelMoE):
     def plan(self, idx, w, T):
         c, tok, ids, ww, slot = plan_reference(idx.numpy(), w.numpy(), self.epr, self.world,
                                                self.capacity)
-        return (torch.from_numpy(c), torch.from_numpy(tok), torch.from_numpy(ids),
-                torch.from_numpy(ww), torch.from_numpy(slot))
+        meta = np.concatenate([ids, ww.view(np.int32)], axis=1)
+        return (torch.from_numpy(c), torch.from_numpy(tok), torch.from_numpy(meta),
+                torch.from_numpy(slot))
 
     def gather(self, x, tok):
         return x[tok.long()].clone()
 
-    def experts(self, rx, rids, rw):
-        cfg = qo.MoEConfig(self.epr, self.config.top_k, self.config.hidden_dim,
-                           self.config.intermediate_dim)
-        y = qo.experts_forward(cfg, self.local, rx.numpy(), rids.numpy(), rw.numpy())
-        return torch.from_numpy(np.ascontiguousarray(y, np.float32))
+    def run_rows(self, rows, meta, R, shared_row0):
+        K = self.config.top_k
+        m = meta.numpy()
+        ids = np.ascontiguousarray(m[:R, :K])
+        ww = np.ascontiguousarray(m[:R, K:]).view(np.float32)
+        cfg = qo.MoEConfig(self.epr, K, self.config.hidden_dim, self.config.intermediate_dim)
+        y = np.zeros((rows.shape[0], rows.shape[1]), np.float32)
+        y[:R] = qo.experts_forward(cfg, self.local, rows[:R].numpy(), ids, ww)
+        if self.has_shared and shared_row0 < R:
+            sh = qo.shared_forward(self.shared_np, rows[shared_row0:R].numpy(),
+                                   self.config.hidden_dim, self.config.shared_intermediate_dim)
+            y[shared_row0:R] = y[shared_row0:R] + np.asarray(sh, np.float32)
+        return torch.from_numpy(y)
 
-    def combine(self, back, slot, T, dtype):
+    def combine(self, back, slot, extra, T, dtype):
         b = back.numpy()
         s = slot.numpy()
         out = np.zeros((T, b.shape[1]), np.float32)
@@ -90,12 +99,7 @@ class HostRank(ExpertParallelMoE):
             for d in range(s.shape[1]):
                 if s[t, d] >= 0:
                     acc = acc + b[s[t, d]]
+            if extra is not None:
+                acc = acc + extra[t].numpy()
             out[t] = acc
         return torch.from_numpy(out)
-
-    def shared_add(self, x, out):
-        if self.has_shared:
-            sh = qo.shared_forward(self.shared_np, x.numpy(), self.config.hidden_dim,
-                                   self.config.shared_intermediate_dim)
-            out = out + torch.from_numpy(np.asarray(sh, np.float32))
-        return out

@@ -33,9 +33,14 @@ def exchange(blocks, G, C):
 def run_virtual(ranks, xs, G, C):
     st, rows, metas = zip(*[rk.dispatch(x) for rk, x in zip(ranks, xs)])
     rx, rm = exchange(rows, G, C), exchange(metas, G, C)
-    ys = [rk.compute(a, b) for rk, a, b in zip(ranks, rx, rm)]
-    back = exchange(ys, G, C)
-    outs = [rk.finish(s, b) for rk, s, b in zip(ranks, st, back)]
+    ys = []
+    for rk, a, b, x in zip(ranks, rx, rm, xs):
+        rbuf, mbuf = rk.recv_buffers(x)
+        rbuf[:G * C].copy_(a)
+        mbuf[:G * C].copy_(b)
+        ys.append(rk.compute(rbuf, mbuf, x).clone())
+    back = exchange([y[:G * C] for y in ys], G, C)
+    outs = [rk.finish(s, b, y) for rk, s, b, y in zip(ranks, st, back, ys)]
     idx = torch.cat([s[2] for s in st])
     return torch.cat(outs), idx
 
@@ -83,25 +88,26 @@ def test_ep_plan_kernel_matches_reference(capacity):
     dev = "cuda"
     counts = torch.empty(G, dtype=torch.int32, device=dev)
     tok = torch.full((rows,), 7777, dtype=torch.int32, device=dev)
-    ids = torch.full((rows, K), 7777, dtype=torch.int32, device=dev)
-    ww = torch.full((rows, K), 7.0, dtype=torch.float32, device=dev)
+    meta = torch.full((rows, 2 * K), 7777, dtype=torch.int32, device=dev)
     slot = torch.empty(T, G, dtype=torch.int32, device=dev)
     ti, tw = torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda()
     ctx.use_current_torch_stream()
     capi.call("qmoe_ep_plan", ctx.handle, ti.data_ptr(), tw.data_ptr(), T, K, epr, G, capacity,
-              counts.data_ptr(), tok.data_ptr(), ids.data_ptr(), ww.data_ptr(), slot.data_ptr())
+              counts.data_ptr(), tok.data_ptr(), meta.data_ptr(), slot.data_ptr())
     torch.cuda.synchronize()
     c, rtok, rids, rww, rslot = plan_reference(idx, w, epr, G, capacity)
     np.testing.assert_array_equal(counts.cpu().numpy(), c)
     np.testing.assert_array_equal(slot.cpu().numpy(), rslot)
-    n = int(c.sum()) if not capacity else rows
+    m = meta.cpu().numpy()
+    ids, ww = m[:, :K], np.ascontiguousarray(m[:, K:]).view(np.float32)
     valid = rslot[rslot >= 0]
     np.testing.assert_array_equal(tok.cpu().numpy()[valid], rtok[valid])
-    np.testing.assert_array_equal(ids.cpu().numpy()[valid], rids[valid])
-    np.testing.assert_array_equal(ww.cpu().numpy()[valid], rww[valid])
-    if capacity:
-        np.testing.assert_array_equal(ids.cpu().numpy()[:n], rids[:n])
-        np.testing.assert_array_equal(tok.cpu().numpy()[:n], rtok[:n])
+    np.testing.assert_array_equal(ids[valid], rids[valid])
+    np.testing.assert_array_equal(ww[valid], rww[valid])
+    if capacity:                                 # padded rows: ids -1, weight 0, token 0
+        np.testing.assert_array_equal(ids, rids)
+        np.testing.assert_array_equal(ww, rww)
+        np.testing.assert_array_equal(tok.cpu().numpy(), rtok)
 
 
 def test_gather_and_combine_rows():
@@ -119,7 +125,11 @@ def test_gather_and_combine_rows():
         slot = torch.tensor([[0, -1, 4], [-1, -1, -1], [2, 1, 3]], dtype=torch.int32, device="cuda")
         res = torch.empty(3, 64, dtype=dt, device="cuda")
         capi.call("qmoe_combine_rows", ctx.handle, x.data_ptr(), code, 64, slot.data_ptr(), 3, 3,
-                  res.data_ptr())
+                  None, res.data_ptr())
         xf = x.float()
         ref = torch.stack([xf[0] + xf[4], torch.zeros(64, device="cuda"), (xf[2] + xf[1]) + xf[3]])
         assert torch.equal(res, ref.to(dt))
+        extra = x[8:11].contiguous()
+        capi.call("qmoe_combine_rows", ctx.handle, x.data_ptr(), code, 64, slot.data_ptr(), 3, 3,
+                  extra.data_ptr(), res.data_ptr())
+        assert torch.equal(res, (ref + extra.float()).to(dt))
