@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU-baseline leg (for profiler runs)")
+    ap.add_argument("--ncu-case", choices=["decode", "prefill"], default=None,
+                    help="only run 3 eager forwards of one replica (configs[1] decode or "
+                         "configs[2] prefill) for an ncu capture, print nothing")
     return ap.parse_args()
 
 
@@ -78,10 +81,10 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def read_profile_traffic():
-    """DRAM bytes per launch of the gate/up kernel from the committed ncu
+def read_profile_traffic(name: str = "qgemv_gate_up_decode_v2lite_t32.txt"):
+    """DRAM bytes per launch of a gate/up kernel from its committed ncu
     summary (a line 'traffic_bytes_per_launch: N'), or None."""
-    path = os.path.join(ROOT, "profiles", "qgemv_gate_up_decode_v2lite_t32.txt")
+    path = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(path):
         return None
     for line in open(path):
@@ -358,6 +361,7 @@ def run_prefill(layers, seed: int, dev: str, steps: int = 20):
         "roofline": {"bound": "tensor", "kernel": "qgemm_prefill gate/up + SwiGLU",
                      "achieved": gu_tf, "peak": bf16, "unit": "TFLOP/s",
                      "frac": gu_tf / bf16, "peak_kind": peak_kind,
+                     "traffic": read_profile_traffic("qgemm_prefill_gate_up_v2lite_t2048.txt"),
                      "kernel_ms": stages["gate_up"],
                      "down_tflops": dn_flops / (stages["down"] / 1e3) / 1e12},
         "stage_ms": stages,
@@ -616,8 +620,28 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_ncu_case(args):
+    """A short fixed workload for ncu captures (one replica, 3 forwards)."""
+    from qmoe_b200 import QMoELayer, default_context
+    torch.cuda.set_device(0)
+    experts, shared, gate_w = synth_weights(args.seed, "cuda")
+    layer = QMoELayer(make_cfg(), gate_w, experts, shared=shared, ctx=default_context(0))
+    del experts, shared
+    g = torch.Generator(device="cuda").manual_seed(args.seed + 7)
+    if args.ncu_case == "decode":
+        x = torch.randn(WORKLOAD["T"], WORKLOAD["H"], generator=g, device="cuda")
+    else:
+        x = torch.randn(2048, WORKLOAD["H"], generator=g, device="cuda").bfloat16()
+    for _ in range(3):
+        layer.forward(x)
+    torch.cuda.synchronize()
+
+
 def main():
     args = parse()
+    if args.ncu_case:
+        run_ncu_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -822,7 +822,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     QTRY_CUDA(launch_quant(q1, st));
     mark(L, 3);
 
-    QgemvTcMaps m0;
+    DecodeMaps m0;
     m0.a0 = L->tm_w[0];
     m0.a1 = L->tm_w[1];
     m0.s0 = L->tm_ws[0];
@@ -833,7 +833,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     m0.s0_3 = L->tm_ws3[0];
     m0.s1_3 = L->tm_ws3[1];
     m0.b3 = L->tm_xq1_3;
-    QgemvTcParams g0{};
+    DecodeParams g0{};
     g0.groups = L->groups.as<int4>();
     g0.n_groups = L->ngroups.as<int32_t>();
     g0.rows = c.intermediate_dim;
@@ -868,14 +868,14 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     QTRY_CUDA(launch_quant(q2, st));
     mark(L, 5);
 
-    QgemvTcMaps m1;
+    DecodeMaps m1;
     m1.a0 = m1.a1 = L->tm_w[2];
     m1.s0 = m1.s1 = L->tm_ws[2];
     m1.b = L->tm_xq2;
     m1.a0_3 = m1.a1_3 = L->tm_w3[2];
     m1.s0_3 = m1.s1_3 = L->tm_ws3[2];
     m1.b3 = L->tm_xq2_3;
-    QgemvTcParams g1{};
+    DecodeParams g1{};
     g1.groups = g0.groups;
     g1.n_groups = g0.n_groups;
     g1.rows = c.hidden_dim;

@@ -103,8 +103,8 @@ struct QuantParams {
 };
 cudaError_t launch_quant(const QuantParams &p, cudaStream_t s);
 
-// ---- decode grouped GEMV on tcgen05 (kind::i8, A = unpacked codes in TMEM) --
-struct QgemvTcMaps {
+// ---- decode grouped GEMV (qgemv_imma.cu): work list and operands ---------
+struct DecodeMaps {
     CUtensorMap a0, a1;          // routed matrices (mode 0: gate, up; mode 1: down, down)
     CUtensorMap s0, s1;          // shared-expert matrices (copies of a0/a1 if none)
     CUtensorMap b;               // limb rows xq [npos*3][kp_b], 128-byte swizzle
@@ -113,7 +113,7 @@ struct QgemvTcMaps {
     // [128-byte block][row][byte] (one box = 16 rows x every block)
     CUtensorMap a0_3, a1_3, s0_3, s1_3, b3;
 };
-struct QgemvTcParams {
+struct DecodeParams {
     const int4 *groups;
     const int32_t *n_groups;
     int rows, K;                 // routed matrices
@@ -128,15 +128,11 @@ struct QgemvTcParams {
     int64_t out_ld;
     int *err;                    // device error word
 };
-cudaError_t launch_qgemv_tc(int mode, const QgemvTcMaps &maps, const QgemvTcParams &p, int grid,
-                            cudaStream_t s);
-size_t qgemv_tc_smem_bytes(int kp_b, int b_buffers);
-// Same work list and operands, mma.sync m16n8k32 IMMA compute (qgemv_imma.cu).
-cudaError_t launch_qgemv_imma(int mode, const QgemvTcMaps &maps, const QgemvTcParams &p,
+cudaError_t launch_qgemv_imma(int mode, const DecodeMaps &maps, const DecodeParams &p,
                               int grid, cudaStream_t s);
 size_t qgemv_imma_smem_bytes(int kp_b, int b_buffers);
 int qgemv_imma_buffers(int kp_b);
-int qgemv_tc_buffers(int kp_b);
+// Device-side error word (device_state.cu) raised by a bounded wait that gives up.
 int *device_error_flag();
 
 // Host: a 2-D uint8 tensor map over [rows][row_bytes] with the given box and

@@ -84,7 +84,7 @@ struct Item {
     bool shared;
 };
 
-QMOE_DEV Item decode_item(const QgemvTcParams &p, int item, int nr, int rb_r, int rb_s) {
+QMOE_DEV Item decode_item(const DecodeParams &p, int item, int nr, int rb_r, int rb_s) {
     Item it;
     int g;
     if (item < nr * rb_r) {
@@ -115,7 +115,7 @@ QMOE_DEV void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t 
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
-qgemv_imma_kernel(const __grid_constant__ QgemvTcMaps maps, const QgemvTcParams p) {
+qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -374,7 +374,7 @@ int qgemv_imma_buffers(int kp_b) {
     return 0;
 }
 
-cudaError_t launch_qgemv_imma(int mode, const QgemvTcMaps &maps, const QgemvTcParams &p, int grid,
+cudaError_t launch_qgemv_imma(int mode, const DecodeMaps &maps, const DecodeParams &p, int grid,
                               cudaStream_t s) {
     const size_t smem = qgemv_imma_smem_bytes(p.kp_b, p.b_buffers);
     static size_t smem_set[2] = {0, 0};

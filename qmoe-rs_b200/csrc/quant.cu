@@ -1,6 +1,6 @@
 // quant.cu -- activations -> per-row fixed point, as three balanced int8 limbs.
 //
-// Feeds the integer tensor-core GEMV (qgemv_tc.cu).  For every row (one
+// Feeds the integer tensor-core GEMV (qgemv_imma.cu).  For every row (one
 // routed assignment or shared-expert token, in position order):
 //   e   = exponent with max|x| * 2^-e in [2^21, 2^22)  (0 for an all-zero row)
 //   Q_k = rint(x_k * 2^-e)      (scaling by a power of two is exact)
