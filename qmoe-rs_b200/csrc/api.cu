@@ -159,6 +159,7 @@ struct qmoe_layer {
     DevBuf topk_idx, topk_w, assign_pos, pos_tok, seg_off, groups, ngroups, h, y;
     DevBuf x_in, io_out, user_idx, user_w;
     DevBuf xq1, meta1, xq2, meta2, router_scratch;
+    DevBuf front_counter;  // hand-off counter of the decode front kernel (kept at zero)
     CUtensorMap tm_xq1, tm_xq2;
     CUtensorMap tm_xq1_3, tm_xq2_3;   // 3-D views: 16 limb rows x every 128-byte block
     // prefill path: gate/up maps with 64-row boxes, bf16 activation / SwiGLU
@@ -399,7 +400,7 @@ int qmoe_layer_destroy(qmoe_layer *L) {
                       &L->seg_off, &L->groups, &L->ngroups, &L->h, &L->y,
                       &L->x_in, &L->io_out, &L->user_idx, &L->user_w,
                       &L->xq1, &L->meta1, &L->xq2, &L->meta2, &L->router_scratch,
-                      &L->xg, &L->hb};
+                      &L->xg, &L->hb, &L->front_counter};
     for (DevBuf *b : bufs) release(*b);
     delete L;
     return QMOE_OK;
@@ -578,6 +579,10 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
     QTRY(grow(L->meta1, sizeof(longlong2) * npos));
     QTRY(grow(L->meta2, sizeof(longlong2) * npos));
     QTRY(grow(L->router_scratch, sizeof(float) * router_scratch_floats(T, c.hidden_dim, c.num_experts)));
+    if (!L->front_counter.p) {
+        QTRY(grow(L->front_counter, sizeof(int32_t)));
+        QTRY_CUDA(cudaMemsetAsync(L->front_counter.p, 0, sizeof(int32_t), L->ctx->stream));
+    }
     if (L->prefill_ok) {
         QTRY(grow(L->xg, 2 * (size_t)npos * H));
         QTRY(grow(L->hb, 2 * (size_t)npos * Imax));
@@ -624,7 +629,7 @@ static int stage_in(DevBuf &buf, const void *src, size_t bytes, int ptr_kind,
     return QMOE_OK;
 }
 
-static int run_router(qmoe_layer *L, const void *xd, int dtype, int64_t T) {
+static RouterParams router_params(qmoe_layer *L, const void *xd, int dtype, int64_t T) {
     const qmoe_moe_config &c = L->cfg;
     RouterParams rp{};
     rp.x = xd;
@@ -643,8 +648,48 @@ static int run_router(qmoe_layer *L, const void *xd, int dtype, int64_t T) {
     rp.topk_idx = L->topk_idx.as<int32_t>();
     rp.topk_w = L->topk_w.as<float>();
     rp.scratch = L->router_scratch.as<float>();
+    return rp;
+}
+
+static int run_router(qmoe_layer *L, const void *xd, int dtype, int64_t T) {
+    const RouterParams rp = router_params(L, xd, dtype, T);
     mark(L, 0);
-    QTRY_CUDA(launch_router(rp, L->ctx->stream));
+    QTRY_CUDA(launch_router(rp, nullptr, L->ctx->stream));
+    return QMOE_OK;
+}
+
+// Expert products on the tcgen05 bf16 GEMM (large bf16 batches) or on the
+// exact integer-limb GEMV.  Fails for a forced prefill path it cannot take.
+static int choose_prefill(qmoe_layer *L, int dtype, int64_t T, int K, bool *prefill) {
+    *prefill = false;
+    if (L->path == QMOE_PATH_PREFILL) {
+        if (!L->prefill_ok || dtype != QMOE_DTYPE_BF16)
+            return fail(QMOE_ERR_UNSUPPORTED,
+                        "the prefill path needs bf16 activations, hidden %% 128 == 0 and "
+                        "intermediate dims %% 64 == 0");
+        *prefill = true;
+    } else if (L->path == QMOE_PATH_AUTO && L->prefill_ok && dtype == QMOE_DTYPE_BF16) {
+        const int64_t per_seg = K > 0 ? T * K / (L->e_count > 0 ? L->e_count : 1) : T;
+        *prefill = per_seg >= kPrefillMinRows;
+    }
+    return QMOE_OK;
+}
+
+// Small batches of a full layer: the router with the permute in the last
+// CTA of its selection kernel.
+static int run_front(qmoe_layer *L, const void *xd, int dtype, int64_t T, bool prefill) {
+    const RouterParams rp = router_params(L, xd, dtype, T);
+    FrontParams f{};
+    f.counter = L->front_counter.as<int32_t>();
+    f.chunk = prefill ? kPrefillTile : kDecodeTok;
+    f.shared_count = L->has_shared ? T : 0;
+    f.seg_off = L->seg_off.as<int32_t>();
+    f.assign_pos = L->assign_pos.as<int32_t>();
+    f.pos_tok = L->pos_tok.as<int32_t>();
+    f.groups = L->groups.as<int4>();
+    f.n_groups = L->ngroups.as<int32_t>();
+    mark(L, 0);
+    QTRY_CUDA(launch_router(rp, &f, L->ctx->stream));
     return QMOE_OK;
 }
 
@@ -657,6 +702,7 @@ struct ExpertsArgs {
     int topk_ld = 0;
     int e_begin = 0;
     int64_t shared_row0 = 0, shared_count = 0;
+    bool permuted = false;  // segments and work list already built (run_front)
 };
 
 // Weighted sum of each token's expert rows in ascending expert order, plus
@@ -768,16 +814,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     // expert products: tcgen05 bf16 GEMM for large bf16 batches, the exact
     // integer-limb GEMV otherwise
     bool prefill = false;
-    if (L->path == QMOE_PATH_PREFILL) {
-        if (!L->prefill_ok || dtype != QMOE_DTYPE_BF16)
-            return fail(QMOE_ERR_UNSUPPORTED,
-                        "the prefill path needs bf16 activations, hidden %% 128 == 0 and "
-                        "intermediate dims %% 64 == 0");
-        prefill = true;
-    } else if (L->path == QMOE_PATH_AUTO && L->prefill_ok && dtype == QMOE_DTYPE_BF16) {
-        const int64_t per_seg = K > 0 ? T * K / (L->e_count > 0 ? L->e_count : 1) : T;
-        prefill = per_seg >= kPrefillMinRows;
-    }
+    QTRY(choose_prefill(L, dtype, T, K, &prefill));
     PermuteParams pp{};
     pp.topk_idx = a.topk_idx;
     pp.T = T;
@@ -793,7 +830,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     pp.groups = L->groups.as<int4>();
     pp.n_groups = L->ngroups.as<int32_t>();
     mark(L, 1);
-    QTRY_CUDA(launch_permute(pp, st));
+    if (!a.permuted) QTRY_CUDA(launch_permute(pp, st));
 
     const int64_t npos = TK + a.shared_count;
     const int32_t *n_valid = L->seg_off.as<int32_t>() + L->e_count;
@@ -927,12 +964,19 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
         QTRY(grow(L->io_out, xbytes));
         outd = L->io_out.p;
     }
-    QTRY(run_router(L, xd, dtype, T));
     ExpertsArgs a;
     a.topk_idx = L->topk_idx.as<int32_t>();
     a.topk_w = L->topk_w.as<float>();
     a.topk_ld = c.top_k;
     a.shared_count = L->has_shared ? T : 0;
+    if (L->e_count == c.num_experts && router_tail_ok(T, c.num_experts, c.top_k)) {
+        bool prefill = false;
+        QTRY(choose_prefill(L, dtype, T, c.top_k, &prefill));
+        QTRY(run_front(L, xd, dtype, T, prefill));
+        a.permuted = true;
+    } else {
+        QTRY(run_router(L, xd, dtype, T));
+    }
     QTRY(run_experts(L, xd, dtype, T, a, outd, 0));
     const size_t kb = sizeof(int32_t) * T * c.top_k;
     if (topk_idx)

@@ -33,7 +33,21 @@ struct RouterParams {
 size_t router_smem_bytes(int H, int E);
 bool router_uses_partials(int64_t T, int H, int E);
 size_t router_scratch_floats(int64_t T, int H, int E);
-cudaError_t launch_router(const RouterParams &p, cudaStream_t s);
+// With a tail (tail->counter != nullptr), the last CTA of the selection
+// kernel also builds the expert segments and the work list (the permute),
+// for batches with router_tail_ok.
+struct FrontParams {
+    int32_t *counter;          // zero before the launch; the last CTA resets it
+    int chunk;                 // tokens per group descriptor
+    int64_t shared_count;      // shared-expert positions after the routed ones (0 or T)
+    int32_t *seg_off;          // [E + 1]
+    int32_t *assign_pos;       // [T, K]
+    int32_t *pos_tok;          // [T * K]
+    int4 *groups;
+    int32_t *n_groups;         // [2]
+};
+bool router_tail_ok(int64_t T, int E, int K);
+cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaStream_t s);
 
 // ---- permute ------------------------------------------------------------
 // Builds per-expert segments of routed (token, slot) assignments, stable in

@@ -200,10 +200,21 @@ router_logits_kernel(const RouterParams p) {
     }
 }
 
+// Permute run by the selection kernel's last CTA (small batches).
+constexpr int kTailMaxT = 64, kTailMaxE = 256, kTailMaxK = 16;
+struct TailSmem {
+    unsigned long long mask[kTailMaxE];   // tokens that picked each expert
+    int cnt[kTailMaxE], off[kTailMaxE + 1], goff[kTailMaxE + 1];
+    int sel[kTailMaxT][kTailMaxK];
+    int is_last;
+};
+
 // Scoring and selection, one CTA per token; logits from the partials
-// (summed here in chunk order) or from router_logits_kernel.
+// (summed here in chunk order) or from router_logits_kernel.  With f.counter
+// set, the last CTA to finish also builds the expert segments and the work
+// list (what permute_kernel does), saving a launch for small batches.
 __global__ void __launch_bounds__(kRouterThreads)
-router_select_kernel(const RouterParams p, int from_partials) {
+router_select_kernel(const RouterParams p, int from_partials, const FrontParams f) {
     extern __shared__ float smem[];
     const RouterSmem L = router_layout(p.E);
     float *part = smem + L.part;
@@ -335,6 +346,96 @@ router_select_kernel(const RouterParams p, int from_partials) {
             p.topk_w[(int64_t)t * K + j] = w[j];
         }
     }
+    if (!f.counter) return;
+
+    // hand-off: the last CTA to finish runs the permute
+    __shared__ TailSmem S;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) S.is_last = atomicAdd(f.counter, 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (!S.is_last) return;
+    __threadfence();
+    const int T = (int)p.T;
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int a = tid; a < T * K; a += kRouterThreads)
+        S.sel[a / K][a % K] = __ldcg(p.topk_idx + a);
+    __syncthreads();
+    // phase C: permute -- expert segments in expert order, tokens in order
+    // inside a segment (the rank of token t in expert e's segment is the
+    // number of earlier tokens in e's token mask), groups of f.chunk
+    // positions, shared groups last
+    for (int e = tid; e < E; e += kRouterThreads) S.mask[e] = 0ull;
+    __syncthreads();
+    const int TK = T * K;
+    for (int a = tid; a < TK; a += kRouterThreads) {
+        const int t = a / K;
+        atomicOr(&S.mask[S.sel[t][a - t * K]], 1ull << t);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // exclusive scans over experts of counts and of group counts, 8
+        // experts per lane
+        int c8[8], g8[8], cs = 0, gsum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            c8[j] = e < E ? __popcll(S.mask[e]) : 0;
+            g8[j] = (c8[j] + f.chunk - 1) / f.chunk;
+            cs += c8[j];
+            gsum += g8[j];
+        }
+        int ci = cs, gi = gsum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int uc = __shfl_up_sync(0xffffffffu, ci, o), ug = __shfl_up_sync(0xffffffffu, gi, o);
+            if (lane >= o) { ci += uc; gi += ug; }
+        }
+        int run = ci - cs, grun = gi - gsum;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            if (e < E) {
+                S.off[e] = run;
+                S.goff[e] = grun;
+                S.cnt[e] = c8[j];
+            }
+            run += c8[j];
+            grun += g8[j];
+        }
+        if (lane == 31) {
+            S.off[E] = run;
+            S.goff[E] = grun;
+            f.seg_off[E] = run;
+            f.n_groups[0] = grun;
+            f.n_groups[1] = (int)((f.shared_count + f.chunk - 1) / f.chunk);
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += kRouterThreads) {
+        f.seg_off[e] = S.off[e];
+        const int c = S.cnt[e];
+        for (int g = 0; g * f.chunk < c; ++g) {
+            const int b = g * f.chunk;
+            f.groups[S.goff[e] + g] = make_int4(e, S.off[e] + b, min(f.chunk, c - b), 0);
+        }
+    }
+    {
+        const int ns = (int)((f.shared_count + f.chunk - 1) / f.chunk);
+        for (int g = tid; g < ns; g += kRouterThreads) {
+            const int64_t b = (int64_t)g * f.chunk;
+            const int64_t rem = f.shared_count - b;
+            f.groups[S.goff[E] + g] = make_int4(E, (int)(TK + b), (int)(rem < f.chunk ? rem : f.chunk), 0);
+        }
+    }
+    for (int a = tid; a < TK; a += kRouterThreads) {
+        const int t = a / K, e = S.sel[t][a - t * K];
+        const int pos = S.off[e] + __popcll(S.mask[e] & ((1ull << t) - 1ull));
+        f.pos_tok[pos] = t;
+        f.assign_pos[a] = pos;
+    }
+    __syncthreads();
+    if (tid == 0) *f.counter = 0;
 }
 
 }  // namespace
@@ -361,8 +462,14 @@ size_t router_scratch_floats(int64_t T, int H, int E) {
     return (size_t)(parts > logits ? parts : logits);
 }
 
-cudaError_t launch_router(const RouterParams &p, cudaStream_t s) {
+bool router_tail_ok(int64_t T, int E, int K) {
+    return T >= 1 && T <= kTailMaxT && E <= kTailMaxE && K <= kTailMaxK;
+}
+
+cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaStream_t s) {
     if (p.T == 0) return cudaSuccess;
+    FrontParams f{};
+    if (tail) f = *tail;
     const bool parts = router_uses_partials(p.T, p.H, p.E);
     if (parts) {
         const int nc = p.H / kGateChunk;
@@ -388,7 +495,8 @@ cudaError_t launch_router(const RouterParams &p, cudaStream_t s) {
         smem_set = smem;
     }
     return launch_pdl(router_select_kernel, dim3((unsigned)p.T), dim3(kRouterThreads), smem, s, p,
-                      parts ? 1 : 0);
+                      parts ? 1 : 0, f);
 }
 
 }  // namespace qmoe
+

@@ -303,3 +303,27 @@ def test_quantizer_on_device_matches_host():
     c_cpu = qz.unpack_codes(p_cpu, 256).numpy()
     c_gpu = qz.unpack_codes(p_gpu.cpu(), 256).numpy()
     assert np.count_nonzero(c_cpu != c_gpu) <= 4
+
+
+@pytest.mark.parametrize("E,k,H,T,scoring", [
+    (64, 6, 2048, 1, capi.QMOE_SCORING_SOFTMAX),
+    (64, 6, 2048, 64, capi.QMOE_SCORING_SOFTMAX),
+    (256, 8, 512, 17, capi.QMOE_SCORING_SIGMOID),
+])
+def test_fused_front_matches_separate_router(E, k, H, T, scoring):
+    """Small batches route through the fused front kernel (partials, last-CTA
+    selection and permute); route() runs the separate router kernels.  Both
+    must give the same bits, and the layer output must match the oracle."""
+    kw = {}
+    if scoring == capi.QMOE_SCORING_SIGMOID:
+        kw = dict(scoring=scoring, n_group=8, topk_group=4, norm_topk_prob=True,
+                  routed_scaling_factor=2.5)
+    cfg = MoEConfig(E, k, H, 128, shared_intermediate_dim=128, **kw)
+    layer, np_exp, np_sh, gw = build(cfg, seed=E + T)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(T + 3))
+    out, idx, w = layer.forward(x.cuda(), return_routing=True)
+    idx2, w2 = layer.route(x.cuda())
+    assert torch.equal(idx, idx2) and torch.equal(w, w2)
+    ro, ri, rw = oracle_layer(cfg, gw, np_exp, np_sh, x.numpy())
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    assert rel_err(out.cpu().numpy(), ro) <= F32_TOL
