@@ -368,6 +368,9 @@ static int validate_cfg(const qmoe_moe_config *c) {
                     c->hidden_dim, c->intermediate_dim);
     if (c->shared_intermediate_dim < 0 || c->shared_intermediate_dim % 64)
         return fail(QMOE_ERR_INVALID, "shared_intermediate_dim must be 0 or a multiple of 64");
+    // the decode GEMV sums 64 x code x int8 limb over K in int32: K <= 65536
+    if (c->hidden_dim > 65536 || c->intermediate_dim > 65536 || c->shared_intermediate_dim > 65536)
+        return fail(QMOE_ERR_UNSUPPORTED, "hidden and intermediate dims above 65536");
     if (c->scoring != QMOE_SCORING_SOFTMAX && c->scoring != QMOE_SCORING_SIGMOID)
         return fail(QMOE_ERR_INVALID, "unknown scoring %d", c->scoring);
     const int G = c->n_group;

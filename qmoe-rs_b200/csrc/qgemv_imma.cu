@@ -9,16 +9,17 @@
 // x ~= 2^e * Q with Q split into three int8 limbs (quant.cu), so
 //     dot(w_r, x) = 2^e * (sum_l 256^l sum_k code_rk q_lk  -  sum_k Q_k).
 // The tensor pipe forms every sum_k code_rk q_lk exactly (mma.sync
-// m16n8k32, A = s8 limbs of <= 5 positions x 3 limbs, B = u8 codes of 8
-// weight rows), the epilogue recombines the limbs in int64 and scales once.
+// m16n8k32, A = u8 codes of 16 weight rows, B = s8 limbs: one n8 tile holds
+// 2 positions x 3 limbs, two tiles 5 positions), the epilogue recombines the
+// limbs in int64 and scales once.
 //
 // Why mma.sync here: with only a few positions per expert the product is a
 // stream of weights each used by <= 15 limb rows.  tcgen05.mma reads its A
 // tile (the weights, 128 rows x 32 bytes) at a fixed ~4 KB per instruction
 // whatever N is, i.e. ~37 weights per clock per SM -- below the HBM rate of
-// ~93 packed weights per clock per SM.  The warp-level m16n8k32 consumes 256
-// weights per instruction from registers, one per ~8 cycles per scheduler
-// (~120 weights per clock per SM), so the kernel can follow HBM.
+// ~93 packed weights per clock per SM.  The warp-level m16n8k32 consumes 512
+// weights per instruction from registers against one n8 limb tile, one per
+// ~8 cycles per scheduler, so the kernel can follow HBM.
 //
 // Work item = (<= 5 positions of one segment) x 256 output rows (gate+up
 // rows 128+128 in mode 0, 256 down rows in mode 1).  Persistent grid, one CTA
@@ -33,12 +34,12 @@
 //               cycles, so boxes are few and large;
 //   warps 1-8   compute: two groups of four warps take the two 256-code
 //               chunks of a stage; a warp owns 32 rows of each weight tile
-//               (64 rows, so each limb fragment it loads feeds 16 IMMAs):
-//               128-bit shared loads of the packed rows, unpack in registers
-//               ((w >> 2j) & 0x03030303: one shift + one mask per 4
-//               weights), m16n8k32 IMMAs against the limb fragments; at item
-//               end each group's int32 accumulators go to its tile of a
-//               double-buffered pair in shared memory;
+//               (four 16-row blocks): 128-bit shared loads of the packed
+//               rows, unpack in registers ((w << (6 - 2j)) & 0xC0C0C0C0: one
+//               shift + one mask per 4 weights, codes scaled by 64), m16n8k32
+//               IMMAs against one limb tile for items of <= 2 positions, two
+//               otherwise; at item end each group's int32 accumulators go to
+//               its tile of a double-buffered pair in shared memory;
 //   warps 9-12  epilogue: sum of the two groups' tiles, limb recombination,
 //               scales, SwiGLU, stores, while the compute warps run the next
 //               item.
@@ -68,7 +69,7 @@ constexpr int kStageBytes = 2 * kTileBytes + kLimbBytes;  // 40 KB
 constexpr int kTokMax = 5;
 constexpr int kOutCols = 256;          // output rows per item
 constexpr int kLimbRows = 15;          // limb rows in use (5 positions x 3 limbs)
-constexpr int kTileStride = 264;       // int32 row stride of an accumulator tile (padded)
+constexpr int kTileStride = 260;       // int32 row stride of an accumulator tile (2 x 260 = 8 mod 32 banks)
 constexpr int kAccBytes = kLimbRows * kTileStride * 4;  // one group's int32 tile
 constexpr int kItemCache = 128;
 
@@ -107,10 +108,70 @@ QMOE_DEV Item decode_item(const DecodeParams &p, int item, int nr, int rb_r, int
 QMOE_DEV void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                    uint32_t b1) {
     asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// A warp's share of one stage: rows 32 wq .. 32 wq + 31 of both weight tiles
+// (16-row blocks b = 0..3: tile b / 2, rows 32 wq + 16 (b & 1) + {g8, g8 + 8})
+// x the 256-code chunk grp, against NT n8 tiles of limb rows (8 per tile).
+// m16n8k32 with A = weight codes (u8, unpacked in registers), B = limbs (s8):
+// lane (g8, t4) holds 16 codes of rows g8 and g8 + 8 per 32-bit word, and
+// (w << (6 - 2j)) & 0xC0C0C0C0 puts code j of each byte at bits 6-7, i.e.
+// every A byte is 64 x code; the epilogue divides the exact int32 sums by 64.
+// A 32-bit word q of a 64-code chunk covers 16 consecutive codes; codes
+// {0,4,8,12} + j of it meet limb bytes 4j..4j+3 of the matching 16-byte limb
+// fragment, whose positions are permuted to that order by the limb writer.
+// The loads are done, and the stage released, before the IMMAs.
+template <int NT>
+QMOE_DEV void stage_mma(const uint8_t *stage, int grp, int wq, int g8, int t4, int (&acc)[8][4],
+                        uint64_t *empty, int lane) {
+    uint4 w[8], lo[4], hi[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const uint8_t *wt = stage + (b >> 1) * kTileBytes + grp * kSubBytes;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int rr = wq * 32 + (b & 1) * 16 + h * 8 + g8;
+            w[2 * b + h] = *reinterpret_cast<const uint4 *>(wt + rr * 64 + 16 * (t4 ^ ((rr >> 1) & 3)));
+        }
+    }
+    // limb fragments of the chunk: 16-code groups 4 t4 + q, i.e. 16-byte
+    // chunk c of 128-byte block 2 grp + t4 / 2; limb rows g8 (tile 0) and
+    // g8 + 8 (tile 1), 128-byte swizzle
+    const uint8_t *lrow = stage + 2 * kTileBytes + g8 * 128;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int kb = grp * 2 + (t4 >> 1);
+        const int c = ((t4 & 1) << 2) | q;
+        const int off = kb * kBBlock + 16 * (c ^ g8);
+        lo[q] = *reinterpret_cast<const uint4 *>(lrow + off);
+        if (NT == 2) hi[q] = *reinterpret_cast<const uint4 *>(lrow + 1024 + off);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t wl = q == 0 ? w[2 * b].x : q == 1 ? w[2 * b].y : q == 2 ? w[2 * b].z : w[2 * b].w;
+            const uint32_t wh = q == 0 ? w[2 * b + 1].x : q == 1 ? w[2 * b + 1].y
+                              : q == 2 ? w[2 * b + 1].z : w[2 * b + 1].w;
+            const uint32_t m = 0xC0C0C0C0u;
+            const uint32_t a0 = (wl << 6) & m, a1 = (wh << 6) & m, a2 = (wl << 4) & m, a3 = (wh << 4) & m;
+            const uint32_t c0 = (wl << 2) & m, c1 = (wh << 2) & m, c2 = wl & m, c3 = wh & m;
+            const uint4 l = lo[q];
+            imma(acc[b], a0, a1, a2, a3, l.x, l.y);
+            imma(acc[b], c0, c1, c2, c3, l.z, l.w);
+            if (NT == 2) {
+                const uint4 u = hi[q];
+                imma(acc[4 + b], a0, a1, a2, a3, u.x, u.y);
+                imma(acc[4 + b], c0, c1, c2, c3, u.z, u.w);
+            }
+        }
+    }
 }
 
 template <int MODE>
@@ -221,8 +282,8 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
     } else if (warp <= kCompute) {
         // --------------------------------------------------------- compute
         // Two groups of four warps take the two 256-code chunks of a stage;
-        // a warp owns rows 32 wq .. 32 wq + 31 of both weight tiles (eight
-        // row groups of 8), so every limb fragment it loads feeds 16 IMMAs.
+        // a warp owns rows 32 wq .. 32 wq + 31 of both weight tiles (four
+        // 16-row blocks), so every limb fragment it loads feeds 8 or 16 IMMAs.
         const int cw = warp - 1;                    // 0..7
         const int grp = cw >> 2;                    // chunk of each stage
         const int wq = cw & 3;
@@ -233,6 +294,8 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             const Item it = item_at(i);
             const int K = it.shared ? p.K_s : p.K;
             const int nks = (K + kStageCodes - 1) / kStageCodes;
+            // limb columns in use: 3 per position; <= 2 positions fit one n8 tile
+            const bool two = it.count > 2;
             int acc[8][4];
 #pragma unroll
             for (int rg = 0; rg < 8; ++rg)
@@ -244,63 +307,42 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                 const uint32_t s = us % kNS;
                 if (!(ok = mbar_wait_warp(&S->smem_full[s], (us / kNS) & 1, abort, p.err))) break;
                 const bool live = 2 * ks + grp < nsub_all;
-                uint4 w[8], alo[4], ahi[4];
+                const uint8_t *stage = ring + s * kStageBytes;
                 if (live) {
-                    // packed rows 32 wq + 8 rg + g8 of tile rg / 4, chunk t4
-                    // (64 codes), 64-byte swizzle
-#pragma unroll
-                    for (int rg = 0; rg < 8; ++rg) {
-                        const uint8_t *wt = ring + s * kStageBytes + (rg >> 2) * kTileBytes + grp * kSubBytes;
-                        const int rr = wq * 32 + (rg & 3) * 8 + g8;
-                        w[rg] = *reinterpret_cast<const uint4 *>(wt + rr * 64 + 16 * (t4 ^ ((rr >> 1) & 3)));
-                    }
-                    // limb fragments of the chunk: 16-element K blocks 4 t4 + q of
-                    // 128-byte block 2 grp + t4/2 of the stage; limb rows g8
-                    // (atom 0) and g8 + 8 (atom 1), 128-byte swizzle
-                    const uint8_t *lrow_lo = ring + s * kStageBytes + 2 * kTileBytes + g8 * 128;
-                    const uint8_t *lrow_hi = lrow_lo + 1024;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int kb = grp * 2 + (t4 >> 1);       // 128-byte block
-                        const int c = ((t4 & 1) << 2) | q;        // 16-byte chunk within it
-                        const int off = kb * kBBlock + 16 * (c ^ g8);
-                        alo[q] = *reinterpret_cast<const uint4 *>(lrow_lo + off);
-                        ahi[q] = *reinterpret_cast<const uint4 *>(lrow_hi + off);
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S->smem_empty[s]);
-                if (live) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-#pragma unroll
-                        for (int rg = 0; rg < 8; ++rg) {
-                            const uint32_t wv = q == 0 ? w[rg].x : q == 1 ? w[rg].y : q == 2 ? w[rg].z : w[rg].w;
-                            imma(acc[rg], alo[q].x, ahi[q].x, alo[q].y, ahi[q].y, wv & 0x03030303u,
-                                 (wv >> 2) & 0x03030303u);
-                        }
-#pragma unroll
-                        for (int rg = 0; rg < 8; ++rg) {
-                            const uint32_t wv = q == 0 ? w[rg].x : q == 1 ? w[rg].y : q == 2 ? w[rg].z : w[rg].w;
-                            imma(acc[rg], alo[q].z, ahi[q].z, alo[q].w, ahi[q].w, (wv >> 4) & 0x03030303u,
-                                 (wv >> 6) & 0x03030303u);
-                        }
-                    }
+                    if (two)
+                        stage_mma<2>(stage, grp, wq, g8, t4, acc, &S->smem_empty[s], lane);
+                    else
+                        stage_mma<1>(stage, grp, wq, g8, t4, acc, &S->smem_empty[s], lane);
+                } else {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S->smem_empty[s]);
                 }
             }
             if (!ok) break;
 
-            // accumulators -> this group's tile [15 limb rows][256 cols]
+            // accumulators -> this group's tile [15 limb rows][256 cols]:
+            // acc[b] (+ acc[4 + b], limb rows 8..15) holds rows g8 / g8 + 8 of
+            // 16-row block b, limb columns 2 t4, 2 t4 + 1
             const uint32_t tb = i & 1;
             if (!(ok = mbar_wait_warp(&S->tile_empty[tb], ((i >> 1) & 1) ^ 1, abort, p.err))) break;
             int *ct = acc_tile + (tb * 2 + grp) * (kAccBytes / 4);
 #pragma unroll
-            for (int rg = 0; rg < 8; ++rg) {
-                const int col = (rg >> 2) * 128 + wq * 32 + (rg & 3) * 8 + 2 * t4;
-                *reinterpret_cast<int2 *>(ct + g8 * kTileStride + col) = make_int2(acc[rg][0], acc[rg][1]);
-                if (g8 + 8 < kLimbRows)
-                    *reinterpret_cast<int2 *>(ct + (g8 + 8) * kTileStride + col) =
-                        make_int2(acc[rg][2], acc[rg][3]);
+            for (int b = 0; b < 4; ++b) {
+                const int col = (b >> 1) * 128 + wq * 32 + (b & 1) * 16 + g8;
+                int *c0 = ct + (2 * t4) * kTileStride + col;
+                c0[0] = acc[b][0];
+                c0[kTileStride] = acc[b][1];
+                c0[8] = acc[b][2];
+                c0[kTileStride + 8] = acc[b][3];
+                if (two) {
+                    int *c1 = c0 + 8 * kTileStride;
+                    c1[0] = acc[4 + b][0];
+                    c1[8] = acc[4 + b][2];
+                    if (2 * t4 + 9 < kLimbRows) {
+                        c1[kTileStride] = acc[4 + b][1];
+                        c1[kTileStride + 8] = acc[4 + b][3];
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S->tile_full[tb]);
@@ -331,8 +373,9 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             int v0[kLimbRows], v1[kLimbRows];
 #pragma unroll
             for (int n = 0; n < kLimbRows; ++n) {
-                v0[n] = ct0[n * kTileStride + r] + ct1[n * kTileStride + r];
-                v1[n] = ct0[n * kTileStride + 128 + r] + ct1[n * kTileStride + 128 + r];
+                // the IMMAs saw 64 x code: exact multiples of 64
+                v0[n] = (ct0[n * kTileStride + r] + ct1[n * kTileStride + r]) >> 6;
+                v1[n] = (ct0[n * kTileStride + 128 + r] + ct1[n * kTileStride + 128 + r]) >> 6;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S->tile_empty[tb]);

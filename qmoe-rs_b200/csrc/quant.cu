@@ -8,8 +8,8 @@
 // written as xq[row][limb][Kp] (int8) and meta[row] = (e, sum_k Q_k).
 // Inside each 16-element block the bytes are stored in the order
 // 0,4,8,12, 1,5,9,13, 2,6,10,14, 3,7,11,15: the order in which the GEMV
-// unpacks a 32-bit word of 2-bit codes ((w >> 2j) & 0x03030303 holds codes
-// j, j+4, j+8, j+12), so activation k meets the weight of column k.
+// unpacks a 32-bit word of 2-bit codes (bits 2j..2j+1 of its four bytes are
+// codes j, j+4, j+8, j+12), so activation k meets the weight of column k.
 // Blocks past K up to Kp are zero.
 #include "common.cuh"
 #include "kernels.h"
