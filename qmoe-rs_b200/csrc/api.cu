@@ -692,7 +692,10 @@ static int run_front(qmoe_layer *L, const void *xd, int dtype, int64_t T, bool p
     f.groups = L->groups.as<int4>();
     f.n_groups = L->ngroups.as<int32_t>();
     mark(L, 0);
-    QTRY_CUDA(launch_router(rp, &f, L->ctx->stream));
+    if (front_cluster_ok(T, rp.H, rp.E, rp.K))
+        QTRY_CUDA(launch_front_cluster(rp, f, L->ctx->stream));
+    else
+        QTRY_CUDA(launch_router(rp, &f, L->ctx->stream));
     return QMOE_OK;
 }
 

@@ -1,0 +1,634 @@
+// front.cu -- the decode front in one launch: gate logits, scoring, top-k,
+// combine weights and the permute (expert segments and the token-group work
+// list), for small batches, as one thread-block cluster.
+//
+// Replaces the router half of QMoELayer::forward (qmoe-rs src/moe.rs:51-82)
+// and the grouping of its assignments by expert (src/moe.rs:90-118), with the
+// same arithmetic as router.cu + permute.cu (bit-identical results):
+//   phase A  each CTA of the cluster owns a contiguous run of 64-wide hidden
+//            chunks and forms the chunk partials of every (token, expert) --
+//            an fmaf chain over the chunk's 64 products from 0 -- and stores
+//            each token's partials into the shared memory of the CTA that
+//            owns the token (token t belongs to CTA t % cluster size;
+//            distributed shared memory stores, which do not stall); the gate
+//            tiles are fetched before the wait on the preceding kernel;
+//   phase B  after a cluster barrier, one warp per token adds that token's
+//            partials in chunk order from its own shared memory;
+//   phase C  the same warp scores, applies the group limit and sorts the
+//            experts (bitonic network over shuffles) in the stable
+//            descending order, ties to the lower expert; the softmax sum runs
+//            in descending-logit order; the warp writes the top-k ids and
+//            weights, and the ids to CTA 0's shared memory;
+//   phase D  after a second cluster barrier, CTA 0 builds the segments and
+//            the work list (per-expert token masks, one thread per expert).
+// One launch replaces the logits kernel, the selection kernel and the
+// permute, and no partial sum goes through global memory.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qmoe {
+namespace {
+
+constexpr int kFrontThreads = 256;
+constexpr int kFrontWarps = kFrontThreads / 32;
+constexpr int kFrontMaxT = 64, kFrontMaxE = 256, kFrontMaxK = 16;
+constexpr int kFrontMaxTE = 4096;          // tokens x experts
+constexpr size_t kFrontMaxSmem = 200 * 1024;
+
+QMOE_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+QMOE_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+QMOE_DEV uint32_t dsmem_map(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+QMOE_DEV void dsmem_st_s32(uint32_t addr, int v) {
+    asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+QMOE_DEV void dsmem_st_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+QMOE_DEV void dsmem_st_v4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+
+// Shared-memory layout, in floats from the (16-byte aligned) dynamic base.
+struct FrontLayout {
+    int ep, tp;          // experts / tokens rounded up to the compute tiles
+    int ws_ld, xs_ld;    // row strides of the transposed gate and x tiles
+    int town;            // tokens owned by one CTA (at most)
+    int ws, xs, recv, warp, sel, tail;
+    int warp_floats;
+    int total;
+};
+
+__host__ __device__ inline int front_tt(int T) { return T <= 16 ? 1 : T <= 32 ? 2 : 4; }
+
+__host__ __device__ inline FrontLayout front_layout(int T, int E, int nc, int cs, int lc) {
+    FrontLayout L;
+    const int tt = front_tt(T);
+    L.ep = (E + 63) / 64 * 64;
+    L.tp = (T + 16 * tt - 1) / (16 * tt) * (16 * tt);
+    L.ws_ld = L.ep + 4;
+    L.xs_ld = L.tp + 1;
+    L.town = (T + cs - 1) / cs;
+    L.ws = 0;
+    L.xs = L.ws + lc * 64 * L.ws_ld;
+    L.recv = (L.xs + lc * 64 * L.xs_ld + 3) / 4 * 4;         // [town][nc][E] partials
+    // per warp: sorted exp [E], logits [E] (each from a 16-byte boundary),
+    // group scores [64], kept groups [64]
+    L.warp_floats = 2 * ((E + 3) / 4 * 4) + 128;
+    L.warp = L.recv + (L.town * nc * E + 3) / 4 * 4;
+    L.sel = L.warp + kFrontWarps * L.warp_floats;            // [T][K] ids (CTA 0)
+    L.tail = (L.sel + kFrontMaxT * kFrontMaxK + 3) / 4 * 4;  // TailState (CTA 0)
+    L.total = L.tail;
+    return L;
+}
+
+struct TailState {
+    uint32_t mlo[kFrontMaxE], mhi[kFrontMaxE];  // tokens 0-31 / 32-63 that picked each expert
+    int wsum[2][kFrontWarps];                    // per-warp totals of the scans
+};
+
+// Partial chains of one (16*TT tokens) x (64 experts) tile of chunk c, each
+// token's four consecutive experts stored into the owner CTA's partials
+// [t / cs][c][e] (recv_s: the local address of that array; the same offset
+// in every CTA).
+template <int TT>
+QMOE_DEV void partial_tile(const float *w, const float *x, int ws_ld, int xs_ld, int tb, int eb, int tx,
+                           int ty, int T, int E, int nc, int c, int cs, uint32_t recv_s) {
+    float acc[TT][4];
+#pragma unroll
+    for (int a = 0; a < TT; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+#pragma unroll 8
+    for (int k = 0; k < kGateChunk; ++k) {
+        const float4 wb = *reinterpret_cast<const float4 *>(w + k * ws_ld + eb + 4 * tx);
+        float xa[TT];
+#pragma unroll
+        for (int a = 0; a < TT; ++a) xa[a] = x[k * xs_ld + tb + ty * TT + a];
+#pragma unroll
+        for (int a = 0; a < TT; ++a) {
+            acc[a][0] = __fmaf_rn(xa[a], wb.x, acc[a][0]);
+            acc[a][1] = __fmaf_rn(xa[a], wb.y, acc[a][1]);
+            acc[a][2] = __fmaf_rn(xa[a], wb.z, acc[a][2]);
+            acc[a][3] = __fmaf_rn(xa[a], wb.w, acc[a][3]);
+        }
+    }
+    const int e = eb + 4 * tx;
+    if (e >= E) return;
+#pragma unroll
+    for (int a = 0; a < TT; ++a) {
+        const int t = tb + ty * TT + a;
+        if (t >= T) continue;
+        const uint32_t owner = (uint32_t)(t % cs);
+        const uint32_t addr = dsmem_map(recv_s + 4u * (uint32_t)(((t / cs) * nc + c) * E + e), owner);
+        if ((E & 3) == 0) {
+            dsmem_st_v4(addr, acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+        } else {
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                if (e + b < E) dsmem_st_f32(addr + 4u * b, acc[a][b]);
+        }
+    }
+}
+
+// Warp-wide bitonic sort of 32*N keys (value, id), element i = 32 r + lane
+// in (v[r], id[r]), into the order of ranks_before: descending value, ties
+// to the lower id.  Afterwards element i has rank i.
+template <int N>
+QMOE_DEV void warp_sort(float (&v)[N], int (&id)[N], int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32 * N; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= 32) {
+                // partners in the same lane: registers r and r ^ (j / 32)
+#pragma unroll
+                for (int r = 0; r < N; ++r) {
+                    const int pr = r ^ (j >> 5);
+                    if (pr > r) {
+                        const bool up = ((r * 32 + lane) & k) == 0;
+                        const bool hi_first = ranks_before(v[pr], id[pr], v[r], id[r]);
+                        if (hi_first == up) {
+                            const float tv = v[r];
+                            v[r] = v[pr];
+                            v[pr] = tv;
+                            const int ti = id[r];
+                            id[r] = id[pr];
+                            id[pr] = ti;
+                        }
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int r = 0; r < N; ++r) {
+                    const float pv = __shfl_xor_sync(0xffffffffu, v[r], j);
+                    const int pi = __shfl_xor_sync(0xffffffffu, id[r], j);
+                    const bool up = ((r * 32 + lane) & k) == 0;
+                    const bool lower = (lane & j) == 0;
+                    const bool partner_first = ranks_before(pv, pi, v[r], id[r]);
+                    if (lower == up ? partner_first : !partner_first) {
+                        v[r] = pv;
+                        id[r] = pi;
+                    }
+                }
+            }
+        }
+    }
+}
+
+// Scoring, group limit, top-k and combine weights of token t by one warp,
+// from its logits lg[E] (the arithmetic of router_select_kernel; the ranks
+// come from a sort instead of counting).  Lanes j < K write slot j's id and
+// weight, and the id to CTA 0's gather array at sel0.
+template <int N>
+QMOE_DEV void select_token(const RouterParams &p, int t, int lane, const float *lg, float *ex, float *gs,
+                           int *gk, uint32_t sel0) {
+    const int E = p.E, K = p.K;
+    const bool sigm = p.scoring == 1;
+    const float NEG = __int_as_float(0xff800000);
+    float v[N];
+    int id[N];
+#pragma unroll
+    for (int r = 0; r < N; ++r) {
+        const int e = r * 32 + lane;
+        id[r] = e;
+        float c = NEG;               // padding ranks after every expert (id >= E)
+        if (e < E) {
+            c = lg[e];
+            if (sigm) {
+                c = qsigmoid(c);
+                if (p.bias) c = __fadd_rn(c, p.bias[e]);
+            }
+        }
+        v[r] = c;
+    }
+    const int G = p.n_group > 1 ? p.n_group : 1;
+    if (G > 1) {
+        // group score = best (softmax) or best + second (sigmoid); keep the
+        // topk_group best groups, ties to the lower index
+        const int per = E / G;
+        float *ch = ex;              // choice by expert, until ex is needed
+#pragma unroll
+        for (int r = 0; r < N; ++r)
+            if (r * 32 + lane < E) ch[r * 32 + lane] = v[r];
+        __syncwarp();
+        for (int g = lane; g < G; g += 32) {
+            const float *c = ch + g * per;
+            int bi = 0;
+            float best = c[0];
+            for (int j = 1; j < per; ++j)
+                if (c[j] > best) {
+                    best = c[j];
+                    bi = j;
+                }
+            float second = NEG;
+            bool have2 = false;
+            for (int j = 0; j < per; ++j)
+                if (j != bi && (!have2 || c[j] > second)) {
+                    second = c[j];
+                    have2 = true;
+                }
+            gs[g] = (!sigm || per < 2) ? best : __fadd_rn(best, second);
+        }
+        __syncwarp();
+        for (int g = lane; g < G; g += 32) {
+            int r = 0;
+            for (int h = 0; h < G; ++h) r += ranks_before(gs[h], h, gs[g], g);
+            gk[g] = r < p.topk_group;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < N; ++r)
+            if (r * 32 + lane < E && !gk[(r * 32 + lane) / per]) v[r] = NEG;
+        __syncwarp();
+    }
+    warp_sort<N>(v, id, lane);
+    const int my_sel = id[0];        // rank `lane`: slot lane of the selection when lane < K
+
+    float mx = 0.0f, s = 0.0f;
+    if (!sigm) {
+        // softmax over all experts (src/moe.rs:74-79): max, then the sum of
+        // exp(l - max) in descending-logit order
+        float lv[N];
+        int lid[N];
+#pragma unroll
+        for (int r = 0; r < N; ++r) {
+            lv[r] = v[r];
+            lid[r] = id[r];
+        }
+        if (G > 1) {                 // the choice order dropped groups: sort the logits
+#pragma unroll
+            for (int r = 0; r < N; ++r) {
+                const int e = r * 32 + lane;
+                lid[r] = e;
+                lv[r] = e < E ? lg[e] : NEG;
+            }
+            warp_sort<N>(lv, lid, lane);
+        }
+        mx = __shfl_sync(0xffffffffu, lv[0], 0);
+#pragma unroll
+        for (int r = 0; r < N; ++r)
+            if (r * 32 + lane < E) ex[r * 32 + lane] = expf(__fsub_rn(lv[r], mx));
+        __syncwarp();
+        if (lane == 0) {
+            int i = 0;
+            for (; i + 4 <= E; i += 4) {
+                const float4 q = *reinterpret_cast<const float4 *>(ex + i);
+                s = __fadd_rn(s, q.x);
+                s = __fadd_rn(s, q.y);
+                s = __fadd_rn(s, q.z);
+                s = __fadd_rn(s, q.w);
+            }
+            for (; i < E; ++i) s = __fadd_rn(s, ex[i]);
+        }
+        s = __shfl_sync(0xffffffffu, s, 0);
+    }
+    float w = 0.0f;
+    if (lane < K) {
+        const float l = lg[my_sel];
+        w = sigm ? qsigmoid(l) : __fdiv_rn(expf(__fsub_rn(l, mx)), s);
+    }
+    if (p.norm_topk) {
+        float den = 0.0f;
+        for (int j = 0; j < K; ++j) den = __fadd_rn(den, __shfl_sync(0xffffffffu, w, j));
+        den = __fadd_rn(den, 1e-20f);
+        w = __fdiv_rn(w, den);
+    }
+    if (p.routed_scale != 1.0f) w = __fmul_rn(w, p.routed_scale);
+    if (lane < K) {
+        p.topk_idx[(int64_t)t * K + lane] = my_sel;
+        p.topk_w[(int64_t)t * K + lane] = w;
+        dsmem_st_s32(sel0 + 4u * (uint32_t)(t * K + lane), my_sel);
+    }
+}
+
+// The permute of all T tokens from their selections sel[T][K] (one CTA, one
+// thread per expert): expert segments in expert order, tokens in order
+// inside a segment, groups of f.chunk positions, the shared groups last.
+QMOE_DEV void permute_tail(const FrontParams &f, int T, int E, int K, const int *sel, TailState &S) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int e = tid; e < E; e += kFrontThreads) {
+        S.mlo[e] = 0u;
+        S.mhi[e] = 0u;
+    }
+    __syncthreads();
+    const int TK = T * K;
+    for (int a = tid; a < TK; a += kFrontThreads) {
+        const int t = a / K;
+        atomicOr(t < 32 ? &S.mlo[sel[a]] : &S.mhi[sel[a]], 1u << (t & 31));
+    }
+    __syncthreads();
+    const int e = tid;               // E <= kFrontThreads
+    const uint64_t mask = e < E ? ((uint64_t)S.mhi[e] << 32) | S.mlo[e] : 0ull;
+    const int cnt = __popcll(mask);
+    const int ng = (cnt + f.chunk - 1) / f.chunk;
+    int ci = cnt, gi = ng;           // inclusive warp scans
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int uc = __shfl_up_sync(0xffffffffu, ci, o), ug = __shfl_up_sync(0xffffffffu, gi, o);
+        if (lane >= o) {
+            ci += uc;
+            gi += ug;
+        }
+    }
+    if (lane == 31) {
+        S.wsum[0][warp] = ci;
+        S.wsum[1][warp] = gi;
+    }
+    __syncthreads();
+    int cb = 0, gb = 0, ct = 0, gt = 0;
+#pragma unroll
+    for (int w = 0; w < kFrontWarps; ++w) {
+        if (w < warp) {
+            cb += S.wsum[0][w];
+            gb += S.wsum[1][w];
+        }
+        ct += S.wsum[0][w];
+        gt += S.wsum[1][w];
+    }
+    if (e < E) {
+        const int off = cb + ci - cnt, goff = gb + gi - ng;
+        f.seg_off[e] = off;
+        for (int g = 0; g < ng; ++g)
+            f.groups[goff + g] = make_int4(e, off + g * f.chunk, min(f.chunk, cnt - g * f.chunk), 0);
+        uint64_t m = mask;
+        for (int r = 0; m; ++r) {
+            const int t = __ffsll((long long)m) - 1;
+            m &= m - 1ull;
+            const int pos = off + r;
+            f.pos_tok[pos] = t;
+            for (int k = 0; k < K; ++k)
+                if (sel[t * K + k] == e) f.assign_pos[t * K + k] = pos;
+        }
+    }
+    const int ns = (int)((f.shared_count + f.chunk - 1) / f.chunk);
+    if (tid == 0) {
+        f.seg_off[E] = ct;
+        f.n_groups[0] = gt;
+        f.n_groups[1] = ns;
+    }
+    for (int g = tid; g < ns; g += kFrontThreads) {
+        const int64_t b = (int64_t)g * f.chunk;
+        const int64_t rem = f.shared_count - b;
+        f.groups[gt + g] = make_int4(E, (int)(TK + b), (int)(rem < f.chunk ? rem : f.chunk), 0);
+    }
+}
+
+// One cluster of gridDim.x CTAs; CTA r owns hidden chunks [r*lc, r*lc + lc)
+// and tokens r, r + cs, ... (one per warp).
+template <int TT>
+__global__ void __launch_bounds__(kFrontThreads, 1)
+front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
+    extern __shared__ float4 front_smem4[];
+    float *sm = reinterpret_cast<float *>(front_smem4);
+    const int T = (int)p.T, E = p.E, K = p.K, H = p.H;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int cs = (int)gridDim.x;
+    const int rank = (int)cluster_ctarank();
+    const int nc = H / kGateChunk;
+    const FrontLayout L = front_layout(T, E, nc, cs, lc);
+    const int c0 = rank * lc;
+    const int nloc = max(0, min(lc, nc - c0));
+    float *ws = sm + L.ws, *xs = sm + L.xs;
+
+    // A.1 gate tiles of the local chunks, transposed to [k][expert]; loads
+    // batched four per thread before their stores
+    {
+        const int n4 = nloc * E * 16;
+        for (int i0 = 0; i0 < n4; i0 += 4 * kFrontThreads) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kFrontThreads + tid;
+                if (i < n4) {
+                    const int cl = i / (E * 16), rem = i - cl * E * 16, e = rem >> 4, k4 = rem & 15;
+                    v[u] = __ldg(reinterpret_cast<const float4 *>(p.gate_w + (int64_t)e * H +
+                                                                  (c0 + cl) * kGateChunk + 4 * k4));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kFrontThreads + tid;
+                if (i < n4) {
+                    const int cl = i / (E * 16), rem = i - cl * E * 16, e = rem >> 4, k4 = rem & 15;
+                    float *w = ws + cl * kGateChunk * L.ws_ld + e;
+                    w[(4 * k4 + 0) * L.ws_ld] = v[u].x;
+                    w[(4 * k4 + 1) * L.ws_ld] = v[u].y;
+                    w[(4 * k4 + 2) * L.ws_ld] = v[u].z;
+                    w[(4 * k4 + 3) * L.ws_ld] = v[u].w;
+                }
+            }
+        }
+    }
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    // A.2 activation tiles, transposed to [k][token]
+    {
+        const int n4 = nloc * T * 16;
+        for (int i0 = 0; i0 < n4; i0 += 4 * kFrontThreads) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kFrontThreads + tid;
+                if (i < n4) {
+                    const int cl = i / (T * 16), rem = i - cl * T * 16, t = rem >> 4, k4 = rem & 15;
+                    v[u] = load_act4(p.x, p.dtype, (int64_t)t * H + (c0 + cl) * kGateChunk + 4 * k4);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kFrontThreads + tid;
+                if (i < n4) {
+                    const int cl = i / (T * 16), rem = i - cl * T * 16, t = rem >> 4, k4 = rem & 15;
+                    float *x = xs + cl * kGateChunk * L.xs_ld + t;
+                    x[(4 * k4 + 0) * L.xs_ld] = v[u].x;
+                    x[(4 * k4 + 1) * L.xs_ld] = v[u].y;
+                    x[(4 * k4 + 2) * L.xs_ld] = v[u].z;
+                    x[(4 * k4 + 3) * L.xs_ld] = v[u].w;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    // A.3 chunk partials, pushed to the token owners
+    const uint32_t recv_s = (uint32_t)__cvta_generic_to_shared(sm + L.recv);
+    {
+        const int tx = tid & 15, ty = tid >> 4;
+        const int ntt = L.tp / (16 * TT), net = L.ep / 64;
+        for (int cl = 0; cl < nloc; ++cl)
+            for (int tile = 0; tile < ntt * net; ++tile)
+                partial_tile<TT>(ws + cl * kGateChunk * L.ws_ld, xs + cl * kGateChunk * L.xs_ld, L.ws_ld,
+                                 L.xs_ld, (tile / net) * 16 * TT, (tile % net) * 64, tx, ty, T, E, nc, c0 + cl,
+                                 cs, recv_s);
+    }
+    cluster_sync_all();  // every token's partials are in its owner
+
+    // B + C: warp w takes token t = rank + cs * w
+    const int t = rank + cs * warp;
+    if (t < T) {
+        float *wsc = sm + L.warp + warp * L.warp_floats;
+        const int e4 = (E + 3) / 4 * 4;
+        float *ex = wsc, *lg = wsc + e4, *gs = wsc + 2 * e4;
+        int *gk = reinterpret_cast<int *>(gs + 64);
+        const float *rv = sm + L.recv + warp * nc * E;   // [nc][E] of this token
+        for (int e = lane; e < E; e += 32) {
+            float tot = 0.0f;
+            int c = 0;
+            for (; c + 8 <= nc; c += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = rv[(c + j) * E + e];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) tot = __fadd_rn(tot, v[j]);
+            }
+            for (; c < nc; ++c) tot = __fadd_rn(tot, rv[c * E + e]);
+            lg[e] = tot;
+        }
+        __syncwarp();
+        const uint32_t sel0 = dsmem_map((uint32_t)__cvta_generic_to_shared(sm + L.sel), 0u);
+        if (E <= 32)
+            select_token<1>(p, t, lane, lg, ex, gs, gk, sel0);
+        else if (E <= 64)
+            select_token<2>(p, t, lane, lg, ex, gs, gk, sel0);
+        else if (E <= 128)
+            select_token<4>(p, t, lane, lg, ex, gs, gk, sel0);
+        else
+            select_token<8>(p, t, lane, lg, ex, gs, gk, sel0);
+    }
+    cluster_sync_all();  // every selection in CTA 0
+    if (rank != 0) return;
+    permute_tail(f, T, E, K, reinterpret_cast<const int *>(sm + L.sel),
+                 *reinterpret_cast<TailState *>(sm + L.tail));
+}
+
+}  // namespace
+}  // namespace qmoe
+
+namespace qmoe {
+
+// Cluster shape for a batch: cs CTAs of lc chunks each, or false when the
+// batch or the layer is outside what one cluster handles.
+static bool front_shape(int64_t T, int H, int E, int K, int max_cs, int *cs, int *lc, size_t *smem) {
+    if (T < 1 || T > kFrontMaxT || E > kFrontMaxE || K > kFrontMaxK || T * E > kFrontMaxTE ||
+        H % kGateChunk)
+        return false;
+    const int nc = H / kGateChunk;
+    int c = nc < max_cs ? nc : max_cs;
+    const int l = (nc + c - 1) / c;
+    c = (nc + l - 1) / l;                 // no CTA without a chunk
+    if (T > (int64_t)kFrontWarps * c) return false;
+    const FrontLayout L = front_layout((int)T, E, nc, c, l);
+    const size_t bytes = (size_t)L.total * 4 + sizeof(TailState);
+    if (bytes > kFrontMaxSmem) return false;
+    *cs = c;
+    *lc = l;
+    *smem = bytes;
+    return true;
+}
+
+template <int TT>
+static cudaError_t launch_front_tt(const RouterParams &p, const FrontParams &f, int cs, int lc, size_t smem,
+                                   cudaStream_t s) {
+    auto kern = front_cluster_kernel<TT>;
+    static size_t smem_set = 0;
+    static bool np_set = false;
+    if (smem > smem_set) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        smem_set = smem;
+    }
+    if (cs > 8 && !np_set) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        np_set = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)cs);
+    cfg.blockDim = dim3(kFrontThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cs;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, p, f, lc);
+}
+
+// Largest cluster (16, else 8) that the device can schedule for this
+// kernel configuration; 0 if none.
+template <int TT>
+static int front_max_cluster(size_t smem) {
+    for (int cs : {16, 8}) {
+        auto kern = front_cluster_kernel<TT>;
+        if (cs > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)cs);
+        cfg.blockDim = dim3(kFrontThreads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)cs;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) return cs;
+        cudaGetLastError();
+    }
+    return 0;
+}
+
+static int front_cluster_size(int tt) {
+    static int mc[3] = {-1, -1, -1};
+    const int ti = tt == 1 ? 0 : tt == 2 ? 1 : 2;
+    if (mc[ti] < 0)
+        mc[ti] = tt == 1 ? front_max_cluster<1>(kFrontMaxSmem)
+               : tt == 2 ? front_max_cluster<2>(kFrontMaxSmem) : front_max_cluster<4>(kFrontMaxSmem);
+    return mc[ti];
+}
+
+bool front_cluster_ok(int64_t T, int H, int E, int K) {
+    int cs, lc;
+    size_t smem;
+    if (!front_shape(T, H, E, K, 16, &cs, &lc, &smem)) return false;
+    const int mc = front_cluster_size(front_tt((int)T));
+    return mc > 0 && front_shape(T, H, E, K, mc, &cs, &lc, &smem);
+}
+
+cudaError_t launch_front_cluster(const RouterParams &p, const FrontParams &f, cudaStream_t s) {
+    const int tt = front_tt((int)p.T);
+    const int mc = front_cluster_size(tt);
+    int cs, lc;
+    size_t smem;
+    if (mc <= 0 || !front_shape(p.T, p.H, p.E, p.K, mc, &cs, &lc, &smem))
+        return cudaErrorInvalidConfiguration;
+    return tt == 1 ? launch_front_tt<1>(p, f, cs, lc, smem, s)
+         : tt == 2 ? launch_front_tt<2>(p, f, cs, lc, smem, s) : launch_front_tt<4>(p, f, cs, lc, smem, s);
+}
+
+}  // namespace qmoe

@@ -48,6 +48,11 @@ struct FrontParams {
 };
 bool router_tail_ok(int64_t T, int E, int K);
 cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaStream_t s);
+// The whole decode front (logits, selection, permute) as one thread-block
+// cluster (front.cu), for small batches: front_cluster_ok says whether this
+// batch and layer shape, and the device, allow it.
+bool front_cluster_ok(int64_t T, int H, int E, int K);
+cudaError_t launch_front_cluster(const RouterParams &p, const FrontParams &f, cudaStream_t s);
 
 // ---- permute ------------------------------------------------------------
 // Builds per-expert segments of routed (token, slot) assignments, stable in

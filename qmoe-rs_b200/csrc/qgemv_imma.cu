@@ -240,6 +240,9 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                 tma_prefetch_desc(&maps.s0_3);
                 if (MODE == 0) tma_prefetch_desc(&maps.s1_3);
             }
+            const uint64_t stream = l2_evict_first_policy();
+            uint64_t keep;
+            asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(keep));
             uint32_t us = 0;
             bool ok = true;
             for (int i = 0; ok && i < my_items; ++i) {
@@ -261,14 +264,18 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                         break;
                     mbar_arrive_expect_tx(&S->smem_full[s], kStageBytes);
                     uint8_t *dst = ring + s * kStageBytes;
+                    // routed weights: read by one group of positions (rarely
+                    // two), evict first; the shared expert's: every group
+                    const uint64_t pol = it.shared ? keep : stream;
                     if (2 * ks + 1 < nfull) {
-                        tma_load_3d(dst, t0_3, &S->smem_full[s], 0, y0, 2 * ks);
-                        tma_load_3d(dst + kTileBytes, t1_3, &S->smem_full[s], 0, y1, 2 * ks);
+                        tma_load_3d_hint(dst, t0_3, &S->smem_full[s], 0, y0, 2 * ks, pol);
+                        tma_load_3d_hint(dst + kTileBytes, t1_3, &S->smem_full[s], 0, y1, 2 * ks, pol);
                     } else {
                         for (int sub = 0; sub < 2; ++sub) {
-                            tma_load_2d(dst + sub * kSubBytes, t0, &S->smem_full[s], (2 * ks + sub) * 64, y0);
-                            tma_load_2d(dst + kTileBytes + sub * kSubBytes, t1, &S->smem_full[s],
-                                        (2 * ks + sub) * 64, y1);
+                            tma_load_2d_hint(dst + sub * kSubBytes, t0, &S->smem_full[s], (2 * ks + sub) * 64,
+                                             y0, pol);
+                            tma_load_2d_hint(dst + kTileBytes + sub * kSubBytes, t1, &S->smem_full[s],
+                                             (2 * ks + sub) * 64, y1, pol);
                         }
                     }
                     tma_load_3d(dst + 2 * kTileBytes, &maps.b3, &S->smem_full[s], 0, it.pos0 * 3, 4 * ks);

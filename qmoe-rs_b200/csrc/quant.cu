@@ -17,8 +17,43 @@
 namespace qmoe {
 namespace {
 
-constexpr int kQuantThreads = 128;
+constexpr int kQuantThreads = 256;
 
+// Limbs of one 16-element block from its Q values, in the block byte order.
+QMOE_DEV void store_block(int8_t *dst, int64_t Kp, int b, const int (&Q)[16], long long &sq) {
+    uint32_t l0[4] = {0, 0, 0, 0}, l1[4] = {0, 0, 0, 0}, l2[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int q = Q[j];
+        sq += q;
+        const int d0 = ((q + 128) & 255) - 128;
+        const int q1 = (q - d0) >> 8;
+        const int d1 = ((q1 + 128) & 255) - 128;
+        const int d2 = (q1 - d1) >> 8;
+        const int word = j & 3, sh = (j >> 2) * 8;  // element j -> byte 4*(j%4) + j/4
+        l0[word] |= (uint32_t)(d0 & 255) << sh;
+        l1[word] |= (uint32_t)(d1 & 255) << sh;
+        l2[word] |= (uint32_t)(d2 & 255) << sh;
+    }
+    *reinterpret_cast<uint4 *>(dst + 0 * Kp + 16 * b) = make_uint4(l0[0], l0[1], l0[2], l0[3]);
+    *reinterpret_cast<uint4 *>(dst + 1 * Kp + 16 * b) = make_uint4(l1[0], l1[1], l1[2], l1[3]);
+    *reinterpret_cast<uint4 *>(dst + 2 * Kp + 16 * b) = make_uint4(l2[0], l2[1], l2[2], l2[3]);
+}
+
+QMOE_DEV float block_max(float m, float *s_red) {
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = s_red[0];
+#pragma unroll
+    for (int w = 1; w < kQuantThreads / 32; ++w) m = fmaxf(m, s_red[w]);
+    return m;
+}
+
+// One CTA per position.  BPT > 0: the row is read once, each thread holding
+// BPT 16-element blocks in registers (rows up to 4096 * BPT); BPT == 0: any
+// length, the row is read twice (max, then limbs).
+template <int BPT>
 __global__ void __launch_bounds__(kQuantThreads)
 quant_kernel(const QuantParams p) {
     const int64_t pos = blockIdx.x;
@@ -33,68 +68,103 @@ quant_kernel(const QuantParams p) {
     const int nblk = ((K + 255) / 256) * 16;  // blocks the GEMV reads (K padded to 256)
     __shared__ float s_red[kQuantThreads / 32];
     __shared__ long long s_sum[kQuantThreads / 32];
-
-    float m = 0.0f;
-    for (int q = tid; q < (K >> 2); q += kQuantThreads) {
-        const float4 v = load_act4(p.act, p.dtype, base + 4 * q);
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-    m = warp_max(m);
-    if ((tid & 31) == 0) s_red[tid >> 5] = m;
-    __syncthreads();
-    m = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
-    int e = 0;
-    if (m > 0.0f) {
-        int ex;
-        frexpf(m, &ex);
-        e = max(ex - 22, -120);
-    }
-    const float sc = pow2i(-e);
-
-    long long sq = 0;
     int8_t *dst = p.xq + pos * 3 * (int64_t)p.Kp;
-    for (int b = tid; b < nblk; b += kQuantThreads) {
-        int Q[16];
-        const bool in = b * 16 < K;
+    long long sq = 0;
+
+    if (BPT > 0) {
+        float4 v[BPT > 0 ? BPT : 1][4];
+        float m = 0.0f;
 #pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (in) v = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
-            Q[4 * j4 + 0] = __float2int_rn(v.x * sc);
-            Q[4 * j4 + 1] = __float2int_rn(v.y * sc);
-            Q[4 * j4 + 2] = __float2int_rn(v.z * sc);
-            Q[4 * j4 + 3] = __float2int_rn(v.w * sc);
-        }
-        uint32_t l0[4] = {0, 0, 0, 0}, l1[4] = {0, 0, 0, 0}, l2[4] = {0, 0, 0, 0};
+        for (int i = 0; i < BPT; ++i) {
+            const int b = tid + i * kQuantThreads;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int q = Q[j];
-            sq += q;
-            const int d0 = ((q + 128) & 255) - 128;
-            const int q1 = (q - d0) >> 8;
-            const int d1 = ((q1 + 128) & 255) - 128;
-            const int d2 = (q1 - d1) >> 8;
-            const int word = j & 3, sh = (j >> 2) * 8;  // element j -> byte 4*(j%4) + j/4
-            l0[word] |= (uint32_t)(d0 & 255) << sh;
-            l1[word] |= (uint32_t)(d1 & 255) << sh;
-            l2[word] |= (uint32_t)(d2 & 255) << sh;
+            for (int j4 = 0; j4 < 4; ++j4) {
+                v[i][j4] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (b * 16 < K) v[i][j4] = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i][j4].x), fabsf(v[i][j4].y)),
+                                   fmaxf(fabsf(v[i][j4].z), fabsf(v[i][j4].w))));
+            }
         }
-        *reinterpret_cast<uint4 *>(dst + 0 * p.Kp + 16 * b) = make_uint4(l0[0], l0[1], l0[2], l0[3]);
-        *reinterpret_cast<uint4 *>(dst + 1 * p.Kp + 16 * b) = make_uint4(l1[0], l1[1], l1[2], l1[3]);
-        *reinterpret_cast<uint4 *>(dst + 2 * p.Kp + 16 * b) = make_uint4(l2[0], l2[1], l2[2], l2[3]);
+        m = block_max(m, s_red);
+        int e = 0;
+        if (m > 0.0f) {
+            int ex;
+            frexpf(m, &ex);
+            e = max(ex - 22, -120);
+        }
+        const float sc = pow2i(-e);
+#pragma unroll
+        for (int i = 0; i < BPT; ++i) {
+            const int b = tid + i * kQuantThreads;
+            if (b >= nblk) continue;
+            int Q[16];
+#pragma unroll
+            for (int j4 = 0; j4 < 4; ++j4) {
+                Q[4 * j4 + 0] = __float2int_rn(v[i][j4].x * sc);
+                Q[4 * j4 + 1] = __float2int_rn(v[i][j4].y * sc);
+                Q[4 * j4 + 2] = __float2int_rn(v[i][j4].z * sc);
+                Q[4 * j4 + 3] = __float2int_rn(v[i][j4].w * sc);
+            }
+            store_block(dst, p.Kp, b, Q, sq);
+        }
+        if (tid == 0) s_sum[0] = e;     // exponent, read after the sum's barrier
+    } else {
+        float m = 0.0f;
+        for (int q = tid; q < (K >> 2); q += kQuantThreads) {
+            const float4 v = load_act4(p.act, p.dtype, base + 4 * q);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+        m = block_max(m, s_red);
+        int e = 0;
+        if (m > 0.0f) {
+            int ex;
+            frexpf(m, &ex);
+            e = max(ex - 22, -120);
+        }
+        const float sc = pow2i(-e);
+        for (int b = tid; b < nblk; b += kQuantThreads) {
+            int Q[16];
+            const bool in = b * 16 < K;
+#pragma unroll
+            for (int j4 = 0; j4 < 4; ++j4) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (in) v = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
+                Q[4 * j4 + 0] = __float2int_rn(v.x * sc);
+                Q[4 * j4 + 1] = __float2int_rn(v.y * sc);
+                Q[4 * j4 + 2] = __float2int_rn(v.z * sc);
+                Q[4 * j4 + 3] = __float2int_rn(v.w * sc);
+            }
+            store_block(dst, p.Kp, b, Q, sq);
+        }
+        if (tid == 0) s_sum[0] = e;
     }
+    __syncthreads();
+    const long long e = s_sum[0];
+    __syncthreads();
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
     if ((tid & 31) == 0) s_sum[tid >> 5] = sq;
     __syncthreads();
-    if (tid == 0) p.meta[pos] = make_longlong2(e, s_sum[0] + s_sum[1] + s_sum[2] + s_sum[3]);
+    if (tid == 0) {
+        long long t = 0;
+#pragma unroll
+        for (int w = 0; w < kQuantThreads / 32; ++w) t += s_sum[w];
+        p.meta[pos] = make_longlong2(e, t);
+    }
 }
 
 }  // namespace
 
 cudaError_t launch_quant(const QuantParams &p, cudaStream_t s) {
     if (p.npos == 0) return cudaSuccess;
-    return launch_pdl(quant_kernel, dim3((unsigned)p.npos), dim3(kQuantThreads), 0, s, p);
+    const int kmax = p.K > p.K_s ? p.K : p.K_s;
+    const int nblk = ((kmax + 255) / 256) * 16;
+    const int bpt = (nblk + kQuantThreads - 1) / kQuantThreads;
+    const dim3 grid((unsigned)p.npos), block(kQuantThreads);
+    if (bpt <= 1) return launch_pdl(quant_kernel<1>, grid, block, 0, s, p);
+    if (bpt <= 2) return launch_pdl(quant_kernel<2>, grid, block, 0, s, p);
+    if (bpt <= 4) return launch_pdl(quant_kernel<4>, grid, block, 0, s, p);
+    return launch_pdl(quant_kernel<0>, grid, block, 0, s, p);
 }
 
 }  // namespace qmoe

@@ -111,6 +111,33 @@ QMOE_DEV void tma_load_3d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, 
         : "memory");
 }
 
+// L2 policy for streams read once: their lines are the first to go, so the
+// small tensors, the code and the reused weights of the other kernels stay.
+QMOE_DEV uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// tma_load_2d / tma_load_3d with an L2 cache policy.
+QMOE_DEV void tma_load_2d_hint(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int x, int y,
+                               uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(pol)
+        : "memory");
+}
+
+QMOE_DEV void tma_load_3d_hint(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int x, int y, int z,
+                               uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(pol)
+        : "memory");
+}
+
 // ---- TMEM ---------------------------------------------------------------
 // Whole-warp operations.
 QMOE_DEV void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {

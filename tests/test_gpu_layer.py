@@ -306,14 +306,18 @@ def test_quantizer_on_device_matches_host():
 
 
 @pytest.mark.parametrize("E,k,H,T,scoring", [
-    (64, 6, 2048, 1, capi.QMOE_SCORING_SOFTMAX),
-    (64, 6, 2048, 64, capi.QMOE_SCORING_SOFTMAX),
-    (256, 8, 512, 17, capi.QMOE_SCORING_SIGMOID),
-])
+    (64, 6, 2048, 1, capi.QMOE_SCORING_SOFTMAX),      # cluster front, 16 CTAs x 2 chunks
+    (64, 6, 2048, 32, capi.QMOE_SCORING_SOFTMAX),     # the decode benchmark's shape
+    (64, 6, 2048, 64, capi.QMOE_SCORING_SOFTMAX),     # 4 tokens per CTA of the cluster
+    (96, 4, 1024, 20, capi.QMOE_SCORING_SOFTMAX),     # experts not a multiple of 64
+    (256, 8, 512, 16, capi.QMOE_SCORING_SIGMOID),     # cluster front, group limit, 8 CTAs
+    (256, 8, 512, 17, capi.QMOE_SCORING_SIGMOID),     # too many logits for one cluster:
+])                                                    # selection kernel's last CTA permutes
 def test_fused_front_matches_separate_router(E, k, H, T, scoring):
-    """Small batches route through the fused front kernel (partials, last-CTA
-    selection and permute); route() runs the separate router kernels.  Both
-    must give the same bits, and the layer output must match the oracle."""
+    """Small batches route through a fused front (the one-cluster kernel, or
+    the selection kernel whose last CTA permutes); route() runs the separate
+    router kernels.  Both must give the same bits, and the layer output must
+    match the oracle."""
     kw = {}
     if scoring == capi.QMOE_SCORING_SIGMOID:
         kw = dict(scoring=scoring, n_group=8, topk_group=4, norm_topk_prob=True,
