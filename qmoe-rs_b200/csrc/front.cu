@@ -71,15 +71,13 @@ struct FrontLayout {
     int total;
 };
 
-__host__ __device__ inline int front_tt(int T) { return T <= 16 ? 1 : T <= 32 ? 2 : 4; }
-
+// Compute tiles: 32 tokens x 64 experts per 128 threads, 4 x 4 per thread.
 __host__ __device__ inline FrontLayout front_layout(int T, int E, int nc, int cs, int lc) {
     FrontLayout L;
-    const int tt = front_tt(T);
     L.ep = (E + 63) / 64 * 64;
-    L.tp = (T + 16 * tt - 1) / (16 * tt) * (16 * tt);
+    L.tp = (T + 31) / 32 * 32;
     L.ws_ld = L.ep + 4;
-    L.xs_ld = L.tp + 1;
+    L.xs_ld = L.tp + 4;
     L.town = (T + cs - 1) / cs;
     L.ws = 0;
     L.xs = L.ws + lc * 64 * L.ws_ld;
@@ -96,29 +94,29 @@ __host__ __device__ inline FrontLayout front_layout(int T, int E, int nc, int cs
 
 struct TailState {
     uint32_t mlo[kFrontMaxE], mhi[kFrontMaxE];  // tokens 0-31 / 32-63 that picked each expert
+    int off[kFrontMaxE];                         // segment start of each expert
     int wsum[2][kFrontWarps];                    // per-warp totals of the scans
 };
 
-// Partial chains of one (16*TT tokens) x (64 experts) tile of chunk c, each
-// token's four consecutive experts stored into the owner CTA's partials
-// [t / cs][c][e] (recv_s: the local address of that array; the same offset
-// in every CTA).
-template <int TT>
+// Partial chains of one (32 tokens) x (64 experts) tile of chunk c: thread
+// (tx, ty) of 128 owns tokens tb + 4 ty .. + 3 and experts eb + 4 tx .. + 3;
+// each token's four experts go to the owner CTA's partials [t / cs][c][e]
+// (recv_s: the local address of that array, at the same offset in every
+// CTA).
 QMOE_DEV void partial_tile(const float *w, const float *x, int ws_ld, int xs_ld, int tb, int eb, int tx,
                            int ty, int T, int E, int nc, int c, int cs, uint32_t recv_s) {
-    float acc[TT][4];
+    float acc[4][4];
 #pragma unroll
-    for (int a = 0; a < TT; ++a)
+    for (int a = 0; a < 4; ++a)
 #pragma unroll
         for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
 #pragma unroll 8
     for (int k = 0; k < kGateChunk; ++k) {
         const float4 wb = *reinterpret_cast<const float4 *>(w + k * ws_ld + eb + 4 * tx);
-        float xa[TT];
+        const float4 xv = *reinterpret_cast<const float4 *>(x + k * xs_ld + tb + 4 * ty);
+        const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-        for (int a = 0; a < TT; ++a) xa[a] = x[k * xs_ld + tb + ty * TT + a];
-#pragma unroll
-        for (int a = 0; a < TT; ++a) {
+        for (int a = 0; a < 4; ++a) {
             acc[a][0] = __fmaf_rn(xa[a], wb.x, acc[a][0]);
             acc[a][1] = __fmaf_rn(xa[a], wb.y, acc[a][1]);
             acc[a][2] = __fmaf_rn(xa[a], wb.z, acc[a][2]);
@@ -128,8 +126,8 @@ QMOE_DEV void partial_tile(const float *w, const float *x, int ws_ld, int xs_ld,
     const int e = eb + 4 * tx;
     if (e >= E) return;
 #pragma unroll
-    for (int a = 0; a < TT; ++a) {
-        const int t = tb + ty * TT + a;
+    for (int a = 0; a < 4; ++a) {
+        const int t = tb + 4 * ty + a;
         if (t >= T) continue;
         const uint32_t owner = (uint32_t)(t % cs);
         const uint32_t addr = dsmem_map(recv_s + 4u * (uint32_t)(((t / cs) * nc + c) * E + e), owner);
@@ -297,8 +295,9 @@ QMOE_DEV void select_token(const RouterParams &p, int t, int lane, const float *
     }
     float w = 0.0f;
     if (lane < K) {
+        // without a group limit slot j is rank j of the logits: its exp is ex[j]
         const float l = lg[my_sel];
-        w = sigm ? qsigmoid(l) : __fdiv_rn(expf(__fsub_rn(l, mx)), s);
+        w = sigm ? qsigmoid(l) : __fdiv_rn(G > 1 ? expf(__fsub_rn(l, mx)) : ex[lane], s);
     }
     if (p.norm_topk) {
         float den = 0.0f;
@@ -360,18 +359,19 @@ QMOE_DEV void permute_tail(const FrontParams &f, int T, int E, int K, const int 
     }
     if (e < E) {
         const int off = cb + ci - cnt, goff = gb + gi - ng;
+        S.off[e] = off;
         f.seg_off[e] = off;
         for (int g = 0; g < ng; ++g)
             f.groups[goff + g] = make_int4(e, off + g * f.chunk, min(f.chunk, cnt - g * f.chunk), 0);
-        uint64_t m = mask;
-        for (int r = 0; m; ++r) {
-            const int t = __ffsll((long long)m) - 1;
-            m &= m - 1ull;
-            const int pos = off + r;
-            f.pos_tok[pos] = t;
-            for (int k = 0; k < K; ++k)
-                if (sel[t * K + k] == e) f.assign_pos[t * K + k] = pos;
-        }
+    }
+    __syncthreads();
+    // each assignment's position: its token's rank among the expert's tokens
+    for (int a = tid; a < TK; a += kFrontThreads) {
+        const int t = a / K, ea = sel[a];
+        const uint64_t m = ((uint64_t)S.mhi[ea] << 32) | S.mlo[ea];
+        const int pos = S.off[ea] + __popcll(m & ((1ull << t) - 1ull));
+        f.pos_tok[pos] = t;
+        f.assign_pos[a] = pos;
     }
     const int ns = (int)((f.shared_count + f.chunk - 1) / f.chunk);
     if (tid == 0) {
@@ -388,7 +388,6 @@ QMOE_DEV void permute_tail(const FrontParams &f, int T, int E, int K, const int 
 
 // One cluster of gridDim.x CTAs; CTA r owns hidden chunks [r*lc, r*lc + lc)
 // and tokens r, r + cs, ... (one per warp).
-template <int TT>
 __global__ void __launch_bounds__(kFrontThreads, 1)
 front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
     extern __shared__ float4 front_smem4[];
@@ -403,7 +402,8 @@ front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
     const int nloc = max(0, min(lc, nc - c0));
     float *ws = sm + L.ws, *xs = sm + L.xs;
 
-    // A.1 gate tiles of the local chunks, transposed to [k][expert]; loads
+    // A.1 gate tiles of the local chunks, transposed to [k][expert] (lanes
+    // along experts, so the transposing stores spread over the banks); loads
     // batched four per thread before their stores
     {
         const int n4 = nloc * E * 16;
@@ -413,7 +413,7 @@ front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
             for (int u = 0; u < 4; ++u) {
                 const int i = i0 + u * kFrontThreads + tid;
                 if (i < n4) {
-                    const int cl = i / (E * 16), rem = i - cl * E * 16, e = rem >> 4, k4 = rem & 15;
+                    const int e = i % E, r = i / E, k4 = r & 15, cl = r >> 4;
                     v[u] = __ldg(reinterpret_cast<const float4 *>(p.gate_w + (int64_t)e * H +
                                                                   (c0 + cl) * kGateChunk + 4 * k4));
                 }
@@ -422,7 +422,7 @@ front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
             for (int u = 0; u < 4; ++u) {
                 const int i = i0 + u * kFrontThreads + tid;
                 if (i < n4) {
-                    const int cl = i / (E * 16), rem = i - cl * E * 16, e = rem >> 4, k4 = rem & 15;
+                    const int e = i % E, r = i / E, k4 = r & 15, cl = r >> 4;
                     float *w = ws + cl * kGateChunk * L.ws_ld + e;
                     w[(4 * k4 + 0) * L.ws_ld] = v[u].x;
                     w[(4 * k4 + 1) * L.ws_ld] = v[u].y;
@@ -443,7 +443,7 @@ front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
             for (int u = 0; u < 4; ++u) {
                 const int i = i0 + u * kFrontThreads + tid;
                 if (i < n4) {
-                    const int cl = i / (T * 16), rem = i - cl * T * 16, t = rem >> 4, k4 = rem & 15;
+                    const int t = i % T, r = i / T, k4 = r & 15, cl = r >> 4;
                     v[u] = load_act4(p.x, p.dtype, (int64_t)t * H + (c0 + cl) * kGateChunk + 4 * k4);
                 }
             }
@@ -451,7 +451,7 @@ front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
             for (int u = 0; u < 4; ++u) {
                 const int i = i0 + u * kFrontThreads + tid;
                 if (i < n4) {
-                    const int cl = i / (T * 16), rem = i - cl * T * 16, t = rem >> 4, k4 = rem & 15;
+                    const int t = i % T, r = i / T, k4 = r & 15, cl = r >> 4;
                     float *x = xs + cl * kGateChunk * L.xs_ld + t;
                     x[(4 * k4 + 0) * L.xs_ld] = v[u].x;
                     x[(4 * k4 + 1) * L.xs_ld] = v[u].y;
@@ -465,13 +465,15 @@ front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
     // A.3 chunk partials, pushed to the token owners
     const uint32_t recv_s = (uint32_t)__cvta_generic_to_shared(sm + L.recv);
     {
-        const int tx = tid & 15, ty = tid >> 4;
-        const int ntt = L.tp / (16 * TT), net = L.ep / 64;
-        for (int cl = 0; cl < nloc; ++cl)
-            for (int tile = 0; tile < ntt * net; ++tile)
-                partial_tile<TT>(ws + cl * kGateChunk * L.ws_ld, xs + cl * kGateChunk * L.xs_ld, L.ws_ld,
-                                 L.xs_ld, (tile / net) * 16 * TT, (tile % net) * 64, tx, ty, T, E, nc, c0 + cl,
-                                 cs, recv_s);
+        // the two halves of the CTA take alternate (chunk, token tile,
+        // expert tile) items
+        const int h = tid >> 7, tx = tid & 15, ty = (tid >> 4) & 7;
+        const int ntt = L.tp / 32, net = L.ep / 64, per = ntt * net;
+        for (int it = h; it < nloc * per; it += 2) {
+            const int cl = it / per, tile = it - cl * per;
+            partial_tile(ws + cl * kGateChunk * L.ws_ld, xs + cl * kGateChunk * L.xs_ld, L.ws_ld, L.xs_ld,
+                         (tile / net) * 32, (tile % net) * 64, tx, ty, T, E, nc, c0 + cl, cs, recv_s);
+        }
     }
     cluster_sync_all();  // every token's partials are in its owner
 
@@ -538,10 +540,9 @@ static bool front_shape(int64_t T, int H, int E, int K, int max_cs, int *cs, int
     return true;
 }
 
-template <int TT>
-static cudaError_t launch_front_tt(const RouterParams &p, const FrontParams &f, int cs, int lc, size_t smem,
+static cudaError_t launch_front_impl(const RouterParams &p, const FrontParams &f, int cs, int lc, size_t smem,
                                    cudaStream_t s) {
-    auto kern = front_cluster_kernel<TT>;
+    auto kern = front_cluster_kernel;
     static size_t smem_set = 0;
     static bool np_set = false;
     if (smem > smem_set) {
@@ -573,10 +574,9 @@ static cudaError_t launch_front_tt(const RouterParams &p, const FrontParams &f, 
 
 // Largest cluster (16, else 8) that the device can schedule for this
 // kernel configuration; 0 if none.
-template <int TT>
 static int front_max_cluster(size_t smem) {
     for (int cs : {16, 8}) {
-        auto kern = front_cluster_kernel<TT>;
+        auto kern = front_cluster_kernel;
         if (cs > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
             cudaGetLastError();
             continue;
@@ -603,32 +603,27 @@ static int front_max_cluster(size_t smem) {
     return 0;
 }
 
-static int front_cluster_size(int tt) {
-    static int mc[3] = {-1, -1, -1};
-    const int ti = tt == 1 ? 0 : tt == 2 ? 1 : 2;
-    if (mc[ti] < 0)
-        mc[ti] = tt == 1 ? front_max_cluster<1>(kFrontMaxSmem)
-               : tt == 2 ? front_max_cluster<2>(kFrontMaxSmem) : front_max_cluster<4>(kFrontMaxSmem);
-    return mc[ti];
+static int front_cluster_size() {
+    static int mc = -1;
+    if (mc < 0) mc = front_max_cluster(kFrontMaxSmem);
+    return mc;
 }
 
 bool front_cluster_ok(int64_t T, int H, int E, int K) {
     int cs, lc;
     size_t smem;
     if (!front_shape(T, H, E, K, 16, &cs, &lc, &smem)) return false;
-    const int mc = front_cluster_size(front_tt((int)T));
+    const int mc = front_cluster_size();
     return mc > 0 && front_shape(T, H, E, K, mc, &cs, &lc, &smem);
 }
 
 cudaError_t launch_front_cluster(const RouterParams &p, const FrontParams &f, cudaStream_t s) {
-    const int tt = front_tt((int)p.T);
-    const int mc = front_cluster_size(tt);
+    const int mc = front_cluster_size();
     int cs, lc;
     size_t smem;
     if (mc <= 0 || !front_shape(p.T, p.H, p.E, p.K, mc, &cs, &lc, &smem))
         return cudaErrorInvalidConfiguration;
-    return tt == 1 ? launch_front_tt<1>(p, f, cs, lc, smem, s)
-         : tt == 2 ? launch_front_tt<2>(p, f, cs, lc, smem, s) : launch_front_tt<4>(p, f, cs, lc, smem, s);
+    return launch_front_impl(p, f, cs, lc, smem, s);
 }
 
 }  // namespace qmoe

@@ -185,8 +185,12 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
     Smem *S = reinterpret_cast<Smem *>(reinterpret_cast<uint8_t *>(acc_tile) + 4 * kAccBytes);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    QMOE_PDL_WAIT();
-    QMOE_PDL_TRIGGER();
+    // The work list (groups, counts) and the weights are read before the
+    // wait on the preceding kernel: the list comes from a kernel at least two
+    // launches back (the permute or the front, then the limb kernel), which
+    // had completed before this grid was launched, because every kernel of
+    // the library triggers its dependents only after its own wait.  The limb
+    // rows, their metadata and every global write come after the wait.
     const int rows_item = MODE == 0 ? 128 : 256;
     const int rb_r = (p.rows + rows_item - 1) / rows_item;
     const int rb_s = p.rows_s > 0 ? (p.rows_s + rows_item - 1) / rows_item : 1;
@@ -212,6 +216,11 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
     }
     __syncthreads();
     volatile int *abort = &S->abort;
+    const bool producer = warp == 0 && lane == 0;
+    if (!producer) {
+        QMOE_PDL_WAIT();
+        QMOE_PDL_TRIGGER();
+    }
 
     auto item_at = [&](int i) -> Item {
         if (i < kItemCache) {
@@ -243,12 +252,8 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             const uint64_t stream = l2_evict_first_policy();
             uint64_t keep;
             asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(keep));
-            uint32_t us = 0;
-            bool ok = true;
-            for (int i = 0; ok && i < my_items; ++i) {
-                const Item it = item_at(i);
+            auto issue_weights = [&](const Item &it, int ks, uint32_t s) {
                 const int K = it.shared ? p.K_s : p.K;
-                const int nks = (K + kStageCodes - 1) / kStageCodes;
                 const int nfull = K >> 8;                   // complete 64-byte chunks per row
                 const CUtensorMap *t0 = it.shared ? &maps.s0 : &maps.a0;
                 const CUtensorMap *t1 = MODE == 0 ? (it.shared ? &maps.s1 : &maps.a1) : t0;
@@ -258,27 +263,57 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                 const int ybase = it.shared ? 0 : it.seg * rows;
                 const int y0 = ybase + it.rb * rows_item;
                 const int y1 = MODE == 0 ? y0 : y0 + 128;
+                uint8_t *dst = ring + s * kStageBytes;
+                // routed weights: read by one group of positions (rarely
+                // two), evict first; the shared expert's: every group
+                const uint64_t pol = it.shared ? keep : stream;
+                if (2 * ks + 1 < nfull) {
+                    tma_load_3d_hint(dst, t0_3, &S->smem_full[s], 0, y0, 2 * ks, pol);
+                    tma_load_3d_hint(dst + kTileBytes, t1_3, &S->smem_full[s], 0, y1, 2 * ks, pol);
+                } else {
+                    for (int sub = 0; sub < 2; ++sub) {
+                        tma_load_2d_hint(dst + sub * kSubBytes, t0, &S->smem_full[s], (2 * ks + sub) * 64, y0,
+                                         pol);
+                        tma_load_2d_hint(dst + kTileBytes + sub * kSubBytes, t1, &S->smem_full[s],
+                                         (2 * ks + sub) * 64, y1, pol);
+                    }
+                }
+            };
+            auto issue_limbs = [&](const Item &it, int ks, uint32_t s) {
+                tma_load_3d(ring + s * kStageBytes + 2 * kTileBytes, &maps.b3, &S->smem_full[s], 0, it.pos0 * 3,
+                            4 * ks);
+            };
+            // the first kNS stages' weights go out before the wait, their limb
+            // rows after it
+            uint32_t npre = 0;
+            int pre_i[kNS], pre_ks[kNS];
+            for (int i = 0; npre < kNS && i < my_items; ++i) {
+                const Item it = item_at(i);
+                const int nks = ((it.shared ? p.K_s : p.K) + kStageCodes - 1) / kStageCodes;
+                for (int ks = 0; npre < kNS && ks < nks; ++ks, ++npre) {
+                    mbar_arrive_expect_tx(&S->smem_full[npre], kStageBytes);
+                    issue_weights(it, ks, npre);
+                    pre_i[npre] = i;
+                    pre_ks[npre] = ks;
+                }
+            }
+            QMOE_PDL_WAIT();
+            QMOE_PDL_TRIGGER();
+            for (uint32_t u = 0; u < npre; ++u) issue_limbs(item_at(pre_i[u]), pre_ks[u], u);
+            uint32_t us = 0;
+            bool ok = true;
+            for (int i = 0; ok && i < my_items; ++i) {
+                const Item it = item_at(i);
+                const int K = it.shared ? p.K_s : p.K;
+                const int nks = (K + kStageCodes - 1) / kStageCodes;
                 for (int ks = 0; ks < nks; ++ks, ++us) {
+                    if (us < npre) continue;                // issued above
                     const uint32_t s = us % kNS;
                     if (!(ok = mbar_wait(&S->smem_empty[s], ((us / kNS) & 1) ^ 1, abort, p.err)))
                         break;
                     mbar_arrive_expect_tx(&S->smem_full[s], kStageBytes);
-                    uint8_t *dst = ring + s * kStageBytes;
-                    // routed weights: read by one group of positions (rarely
-                    // two), evict first; the shared expert's: every group
-                    const uint64_t pol = it.shared ? keep : stream;
-                    if (2 * ks + 1 < nfull) {
-                        tma_load_3d_hint(dst, t0_3, &S->smem_full[s], 0, y0, 2 * ks, pol);
-                        tma_load_3d_hint(dst + kTileBytes, t1_3, &S->smem_full[s], 0, y1, 2 * ks, pol);
-                    } else {
-                        for (int sub = 0; sub < 2; ++sub) {
-                            tma_load_2d_hint(dst + sub * kSubBytes, t0, &S->smem_full[s], (2 * ks + sub) * 64,
-                                             y0, pol);
-                            tma_load_2d_hint(dst + kTileBytes + sub * kSubBytes, t1, &S->smem_full[s],
-                                             (2 * ks + sub) * 64, y1, pol);
-                        }
-                    }
-                    tma_load_3d(dst + 2 * kTileBytes, &maps.b3, &S->smem_full[s], 0, it.pos0 * 3, 4 * ks);
+                    issue_weights(it, ks, s);
+                    issue_limbs(it, ks, s);
                 }
             }
             if (!ok)
