@@ -45,6 +45,7 @@ combine_kernel(const CombineParams p) {
             // equal ids in slot order (the reference's stable order)
             int r = 0;
             for (int i0 = 0; i0 < K; i0 += 32)
+#pragma unroll
                 for (int l = 0; l < 32; ++l) {
                     const int i = i0 + l;
                     // slot i of the other 32-block is reloaded from memory
@@ -76,14 +77,17 @@ combine_kernel(const CombineParams p) {
         if (c4 >= H4) break;
         const int h = 4 * c4;
         float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-        int q = 0;
-        for (; q + 8 <= n; q += 8) {
+        // the shared row's load is issued with the first batch
+        float4 sv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (shared) sv = *reinterpret_cast<const float4 *>(p.y_shared + (t - p.shared_row0) * p.H + h);
+        for (int q = 0; q < n; q += 8) {
             float4 y[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u)
-                y[u] = *reinterpret_cast<const float4 *>(p.y + (int64_t)s_pos[q + u] * p.H + h);
+                if (q + u < n) y[u] = *reinterpret_cast<const float4 *>(p.y + (int64_t)s_pos[q + u] * p.H + h);
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
+                if (q + u >= n) break;
                 const float w = s_w[q + u];
                 a0 = __fadd_rn(a0, __fmul_rn(y[u].x, w));
                 a1 = __fadd_rn(a1, __fmul_rn(y[u].y, w));
@@ -91,16 +95,7 @@ combine_kernel(const CombineParams p) {
                 a3 = __fadd_rn(a3, __fmul_rn(y[u].w, w));
             }
         }
-        for (; q < n; ++q) {
-            const float w = s_w[q];
-            const float4 y = *reinterpret_cast<const float4 *>(p.y + (int64_t)s_pos[q] * p.H + h);
-            a0 = __fadd_rn(a0, __fmul_rn(y.x, w));
-            a1 = __fadd_rn(a1, __fmul_rn(y.y, w));
-            a2 = __fadd_rn(a2, __fmul_rn(y.z, w));
-            a3 = __fadd_rn(a3, __fmul_rn(y.w, w));
-        }
         if (shared) {
-            const float4 sv = *reinterpret_cast<const float4 *>(p.y_shared + (t - p.shared_row0) * p.H + h);
             a0 = __fadd_rn(a0, sv.x);
             a1 = __fadd_rn(a1, sv.y);
             a2 = __fadd_rn(a2, sv.z);

@@ -18,6 +18,9 @@ namespace qmoe {
 namespace {
 
 constexpr int kQuantThreads = 256;
+constexpr int kHalf = 128;                        // threads per position
+constexpr int kPosPerCta = kQuantThreads / kHalf;  // two positions per CTA: one wave
+                                                   // beside a resident GEMV CTA
 
 // Limbs of one 16-element block from its Q values, in the block byte order.
 QMOE_DEV void store_block(int8_t *dst, int64_t Kp, int b, const int (&Q)[16], long long &sq) {
@@ -40,63 +43,87 @@ QMOE_DEV void store_block(int8_t *dst, int64_t Kp, int b, const int (&Q)[16], lo
     *reinterpret_cast<uint4 *>(dst + 2 * Kp + 16 * b) = make_uint4(l2[0], l2[1], l2[2], l2[3]);
 }
 
-QMOE_DEV float block_max(float m, float *s_red) {
+// Max over the four warps of this thread's half.
+QMOE_DEV float half_max(float m, float *s_red, int half) {
     m = warp_max(m);
     if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
     __syncthreads();
-    m = s_red[0];
+    m = s_red[half * 4];
 #pragma unroll
-    for (int w = 1; w < kQuantThreads / 32; ++w) m = fmaxf(m, s_red[w]);
+    for (int w = 1; w < 4; ++w) m = fmaxf(m, s_red[half * 4 + w]);
     return m;
 }
 
-// One CTA per position.  BPT > 0: the row is read once, each thread holding
-// BPT 16-element blocks in registers (rows up to 4096 * BPT); BPT == 0: any
-// length, the row is read twice (max, then limbs).
+QMOE_DEV int exponent_of(float m) {
+    int e = 0;
+    if (m > 0.0f) {
+        int ex;
+        frexpf(m, &ex);
+        e = max(ex - 22, -120);
+    }
+    return e;
+}
+
+QMOE_DEV void quant_block(const QuantParams &p, int64_t base, int K, int b, float sc, int8_t *dst,
+                          long long &sq) {
+    int Q[16];
+    const bool in = b * 16 < K;
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (in) v = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
+        Q[4 * j4 + 0] = __float2int_rn(v.x * sc);
+        Q[4 * j4 + 1] = __float2int_rn(v.y * sc);
+        Q[4 * j4 + 2] = __float2int_rn(v.z * sc);
+        Q[4 * j4 + 3] = __float2int_rn(v.w * sc);
+    }
+    store_block(dst, p.Kp, b, Q, sq);
+}
+
+// Two positions per CTA, one per half of 128 threads.  BPT > 0: the row is
+// read once, each thread holding BPT 16-element blocks in registers (rows up
+// to 2048 * BPT); BPT == 0: any length, the row is read twice (max, limbs).
 template <int BPT>
 __global__ void __launch_bounds__(kQuantThreads)
 quant_kernel(const QuantParams p) {
-    const int64_t pos = blockIdx.x;
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
+    const int half = threadIdx.x / kHalf, ht = threadIdx.x % kHalf;
+    const int64_t pos = (int64_t)blockIdx.x * kPosPerCta + half;
     const bool routed = pos < p.shared_base;
-    if (routed && p.n_valid && pos >= *p.n_valid) return;  // unused routed slot
+    // unused routed slots and the padding position are skipped
+    const bool active = pos < p.npos && !(routed && p.n_valid && pos >= *p.n_valid);
     int64_t row = pos;
-    if (p.pos_tok) row = routed ? (int64_t)p.pos_tok[pos] : p.shared_row0 + pos - p.shared_base;
+    if (active && p.pos_tok) row = routed ? (int64_t)p.pos_tok[pos] : p.shared_row0 + pos - p.shared_base;
     const int64_t base = row * p.act_ld;
-    const int K = routed ? p.K : p.K_s, tid = threadIdx.x;
+    const int K = routed ? p.K : p.K_s;
     const int nblk = ((K + 255) / 256) * 16;  // blocks the GEMV reads (K padded to 256)
     __shared__ float s_red[kQuantThreads / 32];
     __shared__ long long s_sum[kQuantThreads / 32];
     int8_t *dst = p.xq + pos * 3 * (int64_t)p.Kp;
     long long sq = 0;
+    int e;
 
     if (BPT > 0) {
         float4 v[BPT > 0 ? BPT : 1][4];
         float m = 0.0f;
 #pragma unroll
         for (int i = 0; i < BPT; ++i) {
-            const int b = tid + i * kQuantThreads;
+            const int b = ht + i * kHalf;
 #pragma unroll
             for (int j4 = 0; j4 < 4; ++j4) {
                 v[i][j4] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (b * 16 < K) v[i][j4] = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
+                if (active && b * 16 < K) v[i][j4] = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
                 m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i][j4].x), fabsf(v[i][j4].y)),
                                    fmaxf(fabsf(v[i][j4].z), fabsf(v[i][j4].w))));
             }
         }
-        m = block_max(m, s_red);
-        int e = 0;
-        if (m > 0.0f) {
-            int ex;
-            frexpf(m, &ex);
-            e = max(ex - 22, -120);
-        }
+        e = exponent_of(half_max(m, s_red, half));
         const float sc = pow2i(-e);
 #pragma unroll
         for (int i = 0; i < BPT; ++i) {
-            const int b = tid + i * kQuantThreads;
-            if (b >= nblk) continue;
+            const int b = ht + i * kHalf;
+            if (!active || b >= nblk) continue;
             int Q[16];
 #pragma unroll
             for (int j4 = 0; j4 < 4; ++j4) {
@@ -107,48 +134,26 @@ quant_kernel(const QuantParams p) {
             }
             store_block(dst, p.Kp, b, Q, sq);
         }
-        if (tid == 0) s_sum[0] = e;     // exponent, read after the sum's barrier
     } else {
         float m = 0.0f;
-        for (int q = tid; q < (K >> 2); q += kQuantThreads) {
-            const float4 v = load_act4(p.act, p.dtype, base + 4 * q);
-            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-        }
-        m = block_max(m, s_red);
-        int e = 0;
-        if (m > 0.0f) {
-            int ex;
-            frexpf(m, &ex);
-            e = max(ex - 22, -120);
-        }
-        const float sc = pow2i(-e);
-        for (int b = tid; b < nblk; b += kQuantThreads) {
-            int Q[16];
-            const bool in = b * 16 < K;
-#pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (in) v = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
-                Q[4 * j4 + 0] = __float2int_rn(v.x * sc);
-                Q[4 * j4 + 1] = __float2int_rn(v.y * sc);
-                Q[4 * j4 + 2] = __float2int_rn(v.z * sc);
-                Q[4 * j4 + 3] = __float2int_rn(v.w * sc);
+        if (active)
+            for (int q = ht; q < (K >> 2); q += kHalf) {
+                const float4 v = load_act4(p.act, p.dtype, base + 4 * q);
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
             }
-            store_block(dst, p.Kp, b, Q, sq);
-        }
-        if (tid == 0) s_sum[0] = e;
+        e = exponent_of(half_max(m, s_red, half));
+        const float sc = pow2i(-e);
+        if (active)
+            for (int b = ht; b < nblk; b += kHalf) quant_block(p, base, K, b, sc, dst, sq);
     }
-    __syncthreads();
-    const long long e = s_sum[0];
-    __syncthreads();
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    if ((tid & 31) == 0) s_sum[tid >> 5] = sq;
+    if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = sq;
     __syncthreads();
-    if (tid == 0) {
+    if (ht == 0 && active) {
         long long t = 0;
 #pragma unroll
-        for (int w = 0; w < kQuantThreads / 32; ++w) t += s_sum[w];
+        for (int w = 0; w < 4; ++w) t += s_sum[half * 4 + w];
         p.meta[pos] = make_longlong2(e, t);
     }
 }
@@ -159,8 +164,8 @@ cudaError_t launch_quant(const QuantParams &p, cudaStream_t s) {
     if (p.npos == 0) return cudaSuccess;
     const int kmax = p.K > p.K_s ? p.K : p.K_s;
     const int nblk = ((kmax + 255) / 256) * 16;
-    const int bpt = (nblk + kQuantThreads - 1) / kQuantThreads;
-    const dim3 grid((unsigned)p.npos), block(kQuantThreads);
+    const int bpt = (nblk + kHalf - 1) / kHalf;
+    const dim3 grid((unsigned)((p.npos + kPosPerCta - 1) / kPosPerCta)), block(kQuantThreads);
     if (bpt <= 1) return launch_pdl(quant_kernel<1>, grid, block, 0, s, p);
     if (bpt <= 2) return launch_pdl(quant_kernel<2>, grid, block, 0, s, p);
     if (bpt <= 4) return launch_pdl(quant_kernel<4>, grid, block, 0, s, p);
