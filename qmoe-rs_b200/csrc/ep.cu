@@ -120,18 +120,18 @@ ep_plan_kernel(const EpPlanParams p) {
     }
 }
 
-// out[i] = x[idx[i]] for rows of H elements (f32 or bf16), 16 bytes per thread.
+// out[r] = x[idx[r]] for rows of H elements (f32 or bf16): CTA (r, slice),
+// 16 bytes per thread.
 __global__ void __launch_bounds__(256)
 gather_rows_kernel(const void *x, int dtype, int64_t H, const int32_t *idx, int64_t n, void *out) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int64_t per_row = H * (dtype ? 2 : 4) / 16;
-    const int64_t total = n * per_row;
-    for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (int64_t)gridDim.x * 256) {
-        const int64_t r = i / per_row, c = i % per_row;
-        const uint4 *src = reinterpret_cast<const uint4 *>(x) + (int64_t)idx[r] * per_row + c;
-        reinterpret_cast<uint4 *>(out)[r * per_row + c] = __ldg(src);
-    }
+    const int64_t r = blockIdx.x;
+    const int64_t c = (int64_t)blockIdx.y * 256 + threadIdx.x;
+    if (c >= per_row) return;
+    const uint4 *src = reinterpret_cast<const uint4 *>(x) + (int64_t)idx[r] * per_row + c;
+    reinterpret_cast<uint4 *>(out)[r * per_row + c] = __ldg(src);
 }
 
 // out[t] = sum over s ascending of rows[slot_pos[t][s]] (skipping -1), then
@@ -141,10 +141,10 @@ combine_rows_kernel(const void *rows, int dtype, int64_t H, const int32_t *slot_
                     const void *extra, void *out) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
-    const int64_t H4 = H / 4;
-    const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
-    if (i >= T * H4) return;
-    const int64_t t = i / H4, h = (i % H4) * 4;
+    // CTA (token t, slice of 256 x 4 elements)
+    const int64_t t = blockIdx.x;
+    const int64_t h = ((int64_t)blockIdx.y * 256 + threadIdx.x) * 4;
+    if (h >= H) return;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int s = 0; s < S; ++s) {
         const int pos = slot_pos[t * S + s];
@@ -174,19 +174,17 @@ cudaError_t launch_ep_plan(const EpPlanParams &p, cudaStream_t s) {
 cudaError_t launch_gather_rows(const void *x, int dtype, int64_t H, const int32_t *idx, int64_t n,
                                void *out, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
-    const int64_t total = n * (H * (dtype ? 2 : 4) / 16);
-    int64_t blocks = (total + 255) / 256;
-    if (blocks > 148 * 8) blocks = 148 * 8;
-    return launch_pdl(gather_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, s, x, dtype, H, idx, n,
-                      out);
+    const int64_t per_row = H * (dtype ? 2 : 4) / 16;
+    const dim3 grid((unsigned)n, (unsigned)((per_row + 255) / 256));
+    return launch_pdl(gather_rows_kernel, grid, dim3(256), 0, s, x, dtype, H, idx, n, out);
 }
 
 cudaError_t launch_combine_rows(const void *rows, int dtype, int64_t H, const int32_t *slot_pos, int S,
                                 int64_t T, const void *extra, void *out, cudaStream_t s) {
-    const int64_t n = T * (H / 4);
-    if (n == 0) return cudaSuccess;
-    return launch_pdl(combine_rows_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, rows,
-                      dtype, H, slot_pos, S, T, extra, out);
+    if (T == 0 || H == 0) return cudaSuccess;
+    const dim3 grid((unsigned)T, (unsigned)((H / 4 + 255) / 256));
+    return launch_pdl(combine_rows_kernel, grid, dim3(256), 0, s, rows, dtype, H, slot_pos, S, T, extra,
+                      out);
 }
 
 }  // namespace qmoe

@@ -444,22 +444,25 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
 // One thread per 16-element block: row of x (bf16) -> position row of xg
 // with the block permuted (position 2q / 2q+1 of word q = 2j + pp holds
 // element 4pp + j / 8 + 4pp + j).
+constexpr int kGatherRows = 2;           // positions per CTA of the gather
+
 __global__ void __launch_bounds__(256)
 gather_bf16_kernel(const GatherParams p) {
+    // kGatherRows positions per CTA, one warp-aligned slice of threads per
+    // position, 16-element blocks along the row (no division per element)
+    constexpr int kPer = 256 / kGatherRows;
+    const int64_t pos = (int64_t)blockIdx.x * kGatherRows + threadIdx.x / kPer;
     const int64_t nblk = p.H / 16;
-    const int64_t total = p.npos * nblk;
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
-    const int32_t nvalid = *p.n_valid;
-    for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * 256) {
-        const int64_t pos = i / nblk, b = i % nblk;
-        const bool routed = pos < p.shared_base;
-        if (routed && pos >= nvalid) continue;
-        const int64_t row = routed ? (int64_t)p.pos_tok[pos] : p.shared_row0 + pos - p.shared_base;
-        const uint4 *src = reinterpret_cast<const uint4 *>(
-            reinterpret_cast<const __nv_bfloat16 *>(p.x) + row * p.H + 16 * b);
-        const uint4 a = __ldg(src), c = __ldg(src + 1);
+    if (pos >= p.npos) return;
+    const bool routed = pos < p.shared_base;
+    if (routed && pos >= *p.n_valid) return;
+    const int64_t row = routed ? (int64_t)p.pos_tok[pos] : p.shared_row0 + pos - p.shared_base;
+    const uint4 *src0 = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p.x) + row * p.H);
+    uint4 *dst0 = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.xg) + pos * p.H);
+    for (int64_t b = threadIdx.x % kPer; b < nblk; b += kPer) {
+        const uint4 a = __ldg(src0 + 2 * b), c = __ldg(src0 + 2 * b + 1);
         uint4 o0, o1;
         o0.x = __byte_perm(a.x, c.x, 0x5410);  // e0  | e8
         o0.y = __byte_perm(a.z, c.z, 0x5410);  // e4  | e12
@@ -469,9 +472,8 @@ gather_bf16_kernel(const GatherParams p) {
         o1.y = __byte_perm(a.w, c.w, 0x5410);  // e6  | e14
         o1.z = __byte_perm(a.y, c.y, 0x7632);  // e3  | e11
         o1.w = __byte_perm(a.w, c.w, 0x7632);  // e7  | e15
-        uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.xg) + pos * p.H + 16 * b);
-        dst[0] = o0;
-        dst[1] = o1;
+        dst0[2 * b] = o0;
+        dst0[2 * b + 1] = o1;
     }
 }
 
@@ -500,9 +502,7 @@ cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmPar
 
 cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s) {
     if (p.npos == 0) return cudaSuccess;
-    const int64_t total = p.npos * (p.H / 16);
-    int64_t blocks = (total + 255) / 256;
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    const int64_t blocks = (p.npos + kGatherRows - 1) / kGatherRows;
     return launch_pdl(gather_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0, s, p);
 }
 

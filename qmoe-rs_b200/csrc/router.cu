@@ -25,6 +25,7 @@
 // qexp, so scores and the selection on them are bit-exact as well.
 #include "common.cuh"
 #include "kernels.h"
+#include "select.cuh"
 
 namespace qmoe {
 namespace {
@@ -438,6 +439,56 @@ router_select_kernel(const RouterParams p, int from_partials, const FrontParams 
     if (tid == 0) *f.counter = 0;
 }
 
+// Scoring and selection with one warp per token, eight tokens per CTA (for
+// batches without the permute hand-off; E <= 256, K <= 32): the logits from
+// the partials (added in chunk order, loads issued eight at a time) or from
+// router_logits_kernel, then the warp's sort-based selection.
+constexpr int kSelWarps = 8;
+
+__host__ __device__ inline int sel_warp_floats(int E) { return 2 * ((E + 3) / 4 * 4) + 128; }
+
+__global__ void __launch_bounds__(kSelWarps * 32)
+router_select_warp_kernel(const RouterParams p, int from_partials) {
+    extern __shared__ float wsm[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int E = p.E, e4 = (E + 3) / 4 * 4;
+    float *ex = wsm + warp * sel_warp_floats(E), *lg = ex + e4, *gs = lg + e4;
+    int *gk = reinterpret_cast<int *>(gs + 64);
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int64_t t = (int64_t)blockIdx.x * kSelWarps + warp;
+    if (t >= p.T) return;                         // whole warps; no CTA barrier follows
+    const int nc = p.H / kGateChunk;
+    for (int e = lane; e < E; e += 32) {
+        if (from_partials) {
+            const float *pp = p.scratch + t * E + e;
+            const int64_t stride = p.T * E;
+            float tot = 0.0f;
+            int c = 0;
+            for (; c + 8 <= nc; c += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = pp[(c + j) * stride];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) tot = __fadd_rn(tot, v[j]);
+            }
+            for (; c < nc; ++c) tot = __fadd_rn(tot, pp[c * stride]);
+            lg[e] = tot;
+        } else {
+            lg[e] = p.scratch[t * E + e];
+        }
+    }
+    __syncwarp();
+    if (E <= 32)
+        select_token<1>(p, (int)t, lane, lg, ex, gs, gk, 0u, false);
+    else if (E <= 64)
+        select_token<2>(p, (int)t, lane, lg, ex, gs, gk, 0u, false);
+    else if (E <= 128)
+        select_token<4>(p, (int)t, lane, lg, ex, gs, gk, 0u, false);
+    else
+        select_token<8>(p, (int)t, lane, lg, ex, gs, gk, 0u, false);
+}
+
 }  // namespace
 
 size_t router_smem_bytes(int H, int E) {
@@ -486,6 +537,18 @@ cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaSt
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    if (!f.counter && p.E <= 256 && p.K <= 32) {
+        const size_t wsmem = sizeof(float) * kSelWarps * sel_warp_floats(p.E);
+        static size_t wsmem_set = 0;
+        if (wsmem > wsmem_set) {
+            e = cudaFuncSetAttribute(router_select_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)wsmem);
+            if (e != cudaSuccess) return e;
+            wsmem_set = wsmem;
+        }
+        return launch_pdl(router_select_warp_kernel, dim3((unsigned)((p.T + kSelWarps - 1) / kSelWarps)),
+                          dim3(kSelWarps * 32), wsmem, s, p, parts ? 1 : 0);
+    }
     const size_t smem = router_smem_bytes(p.H, p.E);
     static size_t smem_set = 0;  // raise the opt-in limit only when needed
     if (smem > smem_set) {
