@@ -620,6 +620,17 @@ int qmoe_layer_reserve(qmoe_layer *L, int64_t max_tokens) {
 }
 
 // Stage a host input in device memory (device inputs pass through).
+// The device address of page-locked host memory that kernels may access in
+// place, or nullptr for other memory.
+static const void *mapped_host(const void *p) {
+    cudaPointerAttributes at{};
+    if (!p || cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
+}
+
 static int stage_in(DevBuf &buf, const void *src, size_t bytes, int ptr_kind,
                     cudaStream_t st, const void **dev) {
     if (ptr_kind == QMOE_PTR_DEVICE) {
@@ -680,9 +691,11 @@ static int choose_prefill(qmoe_layer *L, int dtype, int64_t T, int K, bool *pref
 
 // Small batches of a full layer: the router with the permute in the last
 // CTA of its selection kernel.
-static int run_front(qmoe_layer *L, const void *xd, int dtype, int64_t T, bool prefill) {
+static int run_front(qmoe_layer *L, const void *xd, int dtype, int64_t T, bool prefill,
+                     void *x_copy = nullptr) {
     const RouterParams rp = router_params(L, xd, dtype, T);
     FrontParams f{};
+    f.x_copy = x_copy;
     f.counter = L->front_counter.as<int32_t>();
     f.chunk = prefill ? kPrefillTile : kDecodeTok;
     f.shared_count = L->has_shared ? T : 0;
@@ -963,22 +976,42 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
     QTRY(layer_reserve(L, T));
     const qmoe_moe_config &c = L->cfg;
     const size_t xbytes = dtype_size(dtype) * T * c.hidden_dim;
-    const void *xd;
-    QTRY(stage_in(L->x_in, x, xbytes, ptr_kind, st, &xd));
-    void *outd = out;
-    if (ptr_kind == QMOE_PTR_HOST) {
-        QTRY(grow(L->io_out, xbytes));
-        outd = L->io_out.p;
-    }
     ExpertsArgs a;
     a.topk_idx = L->topk_idx.as<int32_t>();
     a.topk_w = L->topk_w.as<float>();
     a.topk_ld = c.top_k;
     a.shared_count = L->has_shared ? T : 0;
-    if (L->e_count == c.num_experts && router_tail_ok(T, c.num_experts, c.top_k)) {
-        bool prefill = false;
-        QTRY(choose_prefill(L, dtype, T, c.top_k, &prefill));
-        QTRY(run_front(L, xd, dtype, T, prefill));
+    const bool front = L->e_count == c.num_experts && router_tail_ok(T, c.num_experts, c.top_k);
+    bool prefill = false;
+    if (front) QTRY(choose_prefill(L, dtype, T, c.top_k, &prefill));
+    // Page-locked host buffers are read and written in place by the kernels
+    // (no staging copies): x by the cluster front, which leaves a device copy
+    // for the later kernels, out by the combine.  Other host memory is
+    // staged through device buffers.
+    const void *x_mapped = ptr_kind == QMOE_PTR_HOST && front && !prefill &&
+                                   front_cluster_ok(T, c.hidden_dim, c.num_experts, c.top_k)
+                               ? mapped_host(x)
+                               : nullptr;
+    void *out_mapped = ptr_kind == QMOE_PTR_HOST ? const_cast<void *>(mapped_host(out)) : nullptr;
+    const void *xd;
+    if (x_mapped) {
+        QTRY(grow(L->x_in, xbytes));
+        xd = L->x_in.p;                         // written by the front
+    } else {
+        QTRY(stage_in(L->x_in, x, xbytes, ptr_kind, st, &xd));
+    }
+    void *outd = out;
+    if (ptr_kind == QMOE_PTR_HOST) {
+        if (out_mapped) {
+            outd = out_mapped;
+        } else {
+            QTRY(grow(L->io_out, xbytes));
+            outd = L->io_out.p;
+        }
+    }
+    if (front) {
+        QTRY(run_front(L, x_mapped ? x_mapped : xd, dtype, T, prefill,
+                       x_mapped ? const_cast<void *>(xd) : nullptr));
         a.permuted = true;
     } else {
         QTRY(run_router(L, xd, dtype, T));
@@ -993,7 +1026,7 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
         QTRY_CUDA(cudaMemcpyAsync(topk_w, L->topk_w.p, kb,
                                   ptr_kind == QMOE_PTR_HOST ? cudaMemcpyDeviceToHost
                                                             : cudaMemcpyDeviceToDevice, st));
-    QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
+    if (!out_mapped) QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
     if (ptr_kind == QMOE_PTR_HOST) {
         QTRY_CUDA(cudaStreamSynchronize(st));
         QTRY(check_device_error());

@@ -270,7 +270,11 @@ front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
                 const int i = i0 + u * kFrontThreads + tid;
                 if (i < n4) {
                     const int t = i % T, r = i / T, k4 = r & 15, cl = r >> 4;
-                    v[u] = load_act4(p.x, p.dtype, (int64_t)t * H + (c0 + cl) * kGateChunk + 4 * k4);
+                    const int64_t xi = (int64_t)t * H + (c0 + cl) * kGateChunk + 4 * k4;
+                    v[u] = load_act4(p.x, p.dtype, xi);
+                    // x may be host memory read over the bus: the CTAs'
+                    // chunks together leave a device copy for later kernels
+                    if (f.x_copy) store_act4(f.x_copy, p.dtype, xi, v[u]);
                 }
             }
 #pragma unroll

@@ -45,6 +45,7 @@ struct FrontParams {
     int32_t *pos_tok;          // [T * K]
     int4 *groups;
     int32_t *n_groups;         // [2]
+    void *x_copy;              // front cluster kernel: device copy of x to write (nullable)
 };
 bool router_tail_ok(int64_t T, int E, int K);
 cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaStream_t s);

@@ -154,6 +154,26 @@ def test_host_and_device_pointers_agree_and_are_deterministic():
     np.testing.assert_array_equal(b.numpy(), c.numpy())
 
 
+@pytest.mark.parametrize("dtype,T", [(torch.float32, 32), (torch.bfloat16, 7), (torch.float32, 64)])
+def test_pinned_host_buffers_read_in_place(dtype, T):
+    # page-locked x and out: the front reads x over the bus and leaves the
+    # device copy the later kernels use, the combine writes out in place; the
+    # result must be the device path's bits, and pageable buffers (staged
+    # copies) must agree too
+    cfg = MoEConfig(16, 4, 512, 256, shared_intermediate_dim=256)
+    layer, *_ = build(cfg, seed=23)
+    x = torch.randn(T, 512, generator=torch.Generator().manual_seed(T)).to(dtype)
+    ref = layer.forward(x.cuda()).cpu()
+    xp = x.pin_memory()
+    op = torch.empty_like(xp).pin_memory()
+    idx = layer.forward(xp, out=op, return_routing=True)[1]
+    assert torch.equal(op, ref)
+    _, ridx, _ = layer.forward(x.cuda(), return_routing=True)
+    assert torch.equal(idx, ridx.cpu())
+    pageable = layer.forward(x.clone())
+    assert torch.equal(pageable, ref)
+
+
 def test_bf16_activations_within_tolerance():
     cfg = MoEConfig(16, 4, 512, 256, shared_intermediate_dim=256)
     layer, np_exp, np_sh, gw = build(cfg, seed=11)
