@@ -109,8 +109,13 @@ constexpr int64_t kPrefillMinRows = 16;
 
 // A kernel whose bounded wait timed out leaves a flag in device memory; report
 // (and clear) it at the next host synchronisation point.
+int *error_flag() {
+    static int *flag = qmoe::device_error_flag();
+    return flag;
+}
+
 int check_device_error() {
-    int *flag = qmoe::device_error_flag();
+    int *flag = error_flag();
     if (!flag) return QMOE_OK;
     int v = 0;
     QTRY_CUDA(cudaMemcpy(&v, flag, sizeof(int), cudaMemcpyDeviceToHost));
@@ -123,6 +128,31 @@ int check_device_error() {
 }
 
 }  // namespace
+
+// Waits for the stream and reads the device error word with it: the word is
+// copied into a page-locked host int in stream order, so one wait covers
+// both (no extra synchronous copy per call).
+int sync_and_check(cudaStream_t st) {
+    static thread_local int *pinned = nullptr;
+    static thread_local bool tried = false;
+    if (!tried) {
+        tried = true;
+        if (cudaHostAlloc(reinterpret_cast<void **>(&pinned), sizeof(int), cudaHostAllocDefault) != cudaSuccess) {
+            cudaGetLastError();
+            pinned = nullptr;
+        }
+    }
+    int *flag = error_flag();
+    if (!flag || !pinned) {
+        QTRY_CUDA(cudaStreamSynchronize(st));
+        return check_device_error();
+    }
+    *pinned = 0;
+    QTRY_CUDA(cudaMemcpyAsync(pinned, flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+    QTRY_CUDA(cudaStreamSynchronize(st));
+    if (*pinned) return check_device_error();     // clears the word and reports
+    return QMOE_OK;
+}
 
 struct qmoe_ctx {
     int device = 0;
@@ -222,8 +252,7 @@ int qmoe_ctx_set_stream(qmoe_ctx *ctx, void *stream) {
 int qmoe_ctx_synchronize(qmoe_ctx *ctx) {
     if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
     DeviceGuard g(ctx->device);
-    QTRY_CUDA(cudaStreamSynchronize(ctx->stream));
-    return check_device_error();
+    return sync_and_check(ctx->stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -1028,8 +1057,7 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
                                                             : cudaMemcpyDeviceToDevice, st));
     if (!out_mapped) QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
     if (ptr_kind == QMOE_PTR_HOST) {
-        QTRY_CUDA(cudaStreamSynchronize(st));
-        QTRY(check_device_error());
+        QTRY(sync_and_check(st));
     }
     return QMOE_OK;
 }
@@ -1055,8 +1083,7 @@ int qmoe_layer_route(qmoe_layer *L, const void *x, int dtype, int64_t T, int32_t
     QTRY_CUDA(cudaMemcpyAsync(topk_idx, L->topk_idx.p, kb, k, st));
     QTRY_CUDA(cudaMemcpyAsync(topk_w, L->topk_w.p, kb, k, st));
     if (ptr_kind == QMOE_PTR_HOST) {
-        QTRY_CUDA(cudaStreamSynchronize(st));
-        QTRY(check_device_error());
+        QTRY(sync_and_check(st));
     }
     return QMOE_OK;
 }
@@ -1094,8 +1121,7 @@ int qmoe_layer_forward_routed(qmoe_layer *L, const void *x, int dtype, int64_t R
     QTRY(run_experts(L, xd, dtype, R, a, outd, 0));
     QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
     if (ptr_kind == QMOE_PTR_HOST) {
-        QTRY_CUDA(cudaStreamSynchronize(st));
-        QTRY(check_device_error());
+        QTRY(sync_and_check(st));
     }
     return QMOE_OK;
 }
@@ -1158,8 +1184,7 @@ int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T
     if (rc != QMOE_OK) return rc;
     QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
     if (ptr_kind == QMOE_PTR_HOST) {
-        QTRY_CUDA(cudaStreamSynchronize(st));
-        QTRY(check_device_error());
+        QTRY(sync_and_check(st));
     }
     return QMOE_OK;
 }
