@@ -299,6 +299,56 @@ QMOE_API int qmoe_combine_rows(qmoe_ctx *ctx, const void *rows, int dtype, int64
 QMOE_API int qmoe_layer_forward_ep(qmoe_layer *layer, const void *x, int dtype, int64_t R,
                                    const int32_t *meta, int64_t shared_row0, void *out);
 
+/* ---- expert-parallel exchange over peer memory ------------------------
+ *
+ * The dispatch and return of the expert-parallel layer as kernels that
+ * write straight into the other ranks' memory (NVLink peer stores through
+ * CUDA IPC mappings; no collective library): each rank owns one device
+ * allocation holding its receive rows, their metadata, the returned
+ * partial rows and the arrival flags; the ranks exchange the allocations'
+ * IPC handles (QMOE_EP_HANDLE_BYTES each, e.g. with an all-gather of the
+ * process group) and open each other's.  Per forward, in stream order on
+ * every rank:
+ *
+ *   qmoe_ep_dispatch     rows x[send_tok[d*C + i]] (i < send_counts[d]) and
+ *                        all C metadata rows of block d go to rank d's
+ *                        receive block `rank`; this rank's own tokens x[0..T)
+ *                        go to its own receive rows world*C ..; then each
+ *                        rank's dispatch flag is raised;
+ *   qmoe_ep_wait         waits (bounded) until every rank's flag of a phase
+ *                        is up (phase 0: dispatch, 1: return);
+ *   qmoe_ep_return       rows y[d*C + i] (the partial sums of the rows
+ *                        received from rank d) go to rank d's return block
+ *                        `rank`; then the return flags;
+ *   qmoe_ep_wait(1)      ends the forward (the flags carry a per-forward
+ *                        sequence number kept on the device, so the whole
+ *                        forward can be captured in a CUDA graph).
+ *
+ * These replace the three all-to-alls (ExpertParallelMoE over
+ * torch.distributed) with two peer-store phases; with the buffers used as
+ * qmoe_layer_forward_ep's input and qmoe_combine_rows's input.  A wait that
+ * gives up raises the device error word (reported by the next synchronising
+ * call) instead of hanging.  world <= 32; every rank must use the same
+ * world, capacity, H, K and dtype. */
+#define QMOE_EP_HANDLE_BYTES 64
+typedef struct qmoe_ep_peer qmoe_ep_peer;
+QMOE_API int qmoe_ep_peer_create(qmoe_ctx *ctx, int world, int rank, int64_t capacity,
+                                 int64_t H, int K, int dtype, qmoe_ep_peer **out);
+QMOE_API int qmoe_ep_peer_destroy(qmoe_ep_peer *p);
+/* This rank's IPC handle (QMOE_EP_HANDLE_BYTES bytes). */
+QMOE_API int qmoe_ep_peer_handle(qmoe_ep_peer *p, void *handle);
+/* All ranks' handles, world * QMOE_EP_HANDLE_BYTES bytes in rank order. */
+QMOE_API int qmoe_ep_peer_connect(qmoe_ep_peer *p, const void *handles);
+/* Device pointers of this rank's receive rows [world*C + C, H] (dtype),
+ * receive metadata [world*C + C, 2K] int32 and returned rows [world*C, H]
+ * (dtype). */
+QMOE_API int qmoe_ep_peer_buffers(qmoe_ep_peer *p, void **recv_rows, int32_t **recv_meta,
+                                  void **back_rows);
+QMOE_API int qmoe_ep_dispatch(qmoe_ep_peer *p, const void *x, int64_t T, const int32_t *send_counts,
+                              const int32_t *send_tok, const int32_t *send_meta);
+QMOE_API int qmoe_ep_wait(qmoe_ep_peer *p, int phase);
+QMOE_API int qmoe_ep_return(qmoe_ep_peer *p, const void *y);
+
 /* ---- tracing ----------------------------------------------------------- */
 
 /* Stage timing, the device-side counterpart of the Instant-based breakdown

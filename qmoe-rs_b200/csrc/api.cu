@@ -1247,6 +1247,149 @@ int qmoe_combine_rows(qmoe_ctx *ctx, const void *rows, int dtype, int64_t H, con
     return QMOE_OK;
 }
 
+// ---------------------------------------------------------------------------
+// expert-parallel exchange over peer memory
+// ---------------------------------------------------------------------------
+
+struct qmoe_ep_peer {
+    qmoe_ctx *ctx = nullptr;
+    EpPeerDev d{};
+    uint8_t *mem = nullptr;
+    cudaIpcMemHandle_t handle{};
+    bool opened[kEpMaxWorld] = {};
+};
+
+static_assert(sizeof(cudaIpcMemHandle_t) == QMOE_EP_HANDLE_BYTES, "IPC handle size");
+
+static int64_t align256(int64_t n) { return (n + 255) / 256 * 256; }
+
+int qmoe_ep_peer_create(qmoe_ctx *ctx, int world, int rank, int64_t capacity, int64_t H, int K, int dtype,
+                        qmoe_ep_peer **out) {
+    if (!ctx || !out) return fail(QMOE_ERR_INVALID, "NULL argument");
+    *out = nullptr;
+    QTRY(check_dtype(dtype));
+    if (world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world)
+        return fail(QMOE_ERR_INVALID, "rank %d / world %d (world <= %d)", rank, world, kEpMaxWorld);
+    const int64_t es = (int64_t)dtype_size(dtype);
+    if (capacity < 1 || H <= 0 || (H * es) % 16 || K < 1)
+        return fail(QMOE_ERR_INVALID, "bad exchange shape (capacity %lld, H %lld, K %d)",
+                    (long long)capacity, (long long)H, K);
+    DeviceGuard g(ctx->device);
+    qmoe_ep_peer *p = new (std::nothrow) qmoe_ep_peer;
+    if (!p) return fail(QMOE_ERR_NOMEM, "host allocation failed");
+    p->ctx = ctx;
+    EpPeerDev &d = p->d;
+    d.world = world;
+    d.rank = rank;
+    d.K = K;
+    d.C = capacity;
+    d.H = H;
+    d.esize = es;
+    const int64_t rows = (int64_t)world * capacity + capacity;
+    d.off_rows = 0;
+    d.off_meta = align256(rows * H * es);
+    d.off_back = d.off_meta + align256(rows * 2 * K * 4);
+    d.off_flags = d.off_back + align256((int64_t)world * capacity * H * es);
+    const int64_t off_local = d.off_flags + align256(2 * world * 4);
+    const int64_t bytes = off_local + 256;
+    if (cudaMalloc(&p->mem, (size_t)bytes) != cudaSuccess) {
+        cudaGetLastError();
+        delete p;
+        return fail(QMOE_ERR_NOMEM, "cudaMalloc of %lld bytes failed", (long long)bytes);
+    }
+    int rc = QMOE_OK;
+    if (cudaMemset(p->mem, 0, (size_t)bytes) != cudaSuccess ||
+        cudaIpcGetMemHandle(&p->handle, p->mem) != cudaSuccess) {
+        rc = fail(QMOE_ERR_CUDA, "exchange buffer setup: %s", cudaGetErrorString(cudaGetLastError()));
+        cudaFree(p->mem);
+        delete p;
+        return rc;
+    }
+    d.base[rank] = p->mem;
+    d.seq = reinterpret_cast<int *>(p->mem + off_local);
+    d.done = d.seq + 1;
+    d.err = error_flag();
+    *out = p;
+    return QMOE_OK;
+}
+
+int qmoe_ep_peer_destroy(qmoe_ep_peer *p) {
+    if (!p) return QMOE_OK;
+    DeviceGuard g(p->ctx->device);
+    for (int r = 0; r < p->d.world; ++r)
+        if (p->opened[r]) cudaIpcCloseMemHandle(p->d.base[r]);
+    if (p->mem) cudaFree(p->mem);
+    delete p;
+    return QMOE_OK;
+}
+
+int qmoe_ep_peer_handle(qmoe_ep_peer *p, void *handle) {
+    if (!p || !handle) return fail(QMOE_ERR_INVALID, "NULL argument");
+    std::memcpy(handle, &p->handle, QMOE_EP_HANDLE_BYTES);
+    return QMOE_OK;
+}
+
+int qmoe_ep_peer_connect(qmoe_ep_peer *p, const void *handles) {
+    if (!p || !handles) return fail(QMOE_ERR_INVALID, "NULL argument");
+    DeviceGuard g(p->ctx->device);
+    for (int r = 0; r < p->d.world; ++r) {
+        if (r == p->d.rank || p->opened[r]) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t *>(handles) + (size_t)r * QMOE_EP_HANDLE_BYTES,
+                    QMOE_EP_HANDLE_BYTES);
+        void *ptr = nullptr;
+        QTRY_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        p->d.base[r] = static_cast<uint8_t *>(ptr);
+        p->opened[r] = true;
+    }
+    return QMOE_OK;
+}
+
+int qmoe_ep_peer_buffers(qmoe_ep_peer *p, void **recv_rows, int32_t **recv_meta, void **back_rows) {
+    if (!p) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (recv_rows) *recv_rows = p->mem + p->d.off_rows;
+    if (recv_meta) *recv_meta = reinterpret_cast<int32_t *>(p->mem + p->d.off_meta);
+    if (back_rows) *back_rows = p->mem + p->d.off_back;
+    return QMOE_OK;
+}
+
+static int ep_ready(const qmoe_ep_peer *p) {
+    for (int r = 0; r < p->d.world; ++r)
+        if (!p->d.base[r]) return fail(QMOE_ERR_INVALID, "exchange not connected (rank %d)", r);
+    return QMOE_OK;
+}
+
+int qmoe_ep_dispatch(qmoe_ep_peer *p, const void *x, int64_t T, const int32_t *send_counts,
+                     const int32_t *send_tok, const int32_t *send_meta) {
+    if (!p || !send_counts || !send_tok || !send_meta || (T > 0 && !x))
+        return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (T < 0 || T > p->d.C) return fail(QMOE_ERR_INVALID, "T %lld outside 0 .. capacity %lld",
+                                         (long long)T, (long long)p->d.C);
+    QTRY(ep_ready(p));
+    if (T > 0) QTRY(check_align(x, QMOE_PTR_DEVICE, "x"));
+    DeviceGuard g(p->ctx->device);
+    QTRY_CUDA(launch_ep_dispatch(p->d, x, T, send_counts, send_tok, send_meta, p->ctx->stream));
+    return QMOE_OK;
+}
+
+int qmoe_ep_wait(qmoe_ep_peer *p, int phase) {
+    if (!p) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (phase != 0 && phase != 1) return fail(QMOE_ERR_INVALID, "phase %d (0 dispatch, 1 return)", phase);
+    QTRY(ep_ready(p));
+    DeviceGuard g(p->ctx->device);
+    QTRY_CUDA(launch_ep_wait(p->d, phase, p->ctx->stream));
+    return QMOE_OK;
+}
+
+int qmoe_ep_return(qmoe_ep_peer *p, const void *y) {
+    if (!p || !y) return fail(QMOE_ERR_INVALID, "NULL argument");
+    QTRY(ep_ready(p));
+    QTRY(check_align(y, QMOE_PTR_DEVICE, "y"));
+    DeviceGuard g(p->ctx->device);
+    QTRY_CUDA(launch_ep_return(p->d, y, p->ctx->stream));
+    return QMOE_OK;
+}
+
 int qmoe_layer_set_path(qmoe_layer *L, int path) {
     if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
     if (path != QMOE_PATH_AUTO && path != QMOE_PATH_DECODE && path != QMOE_PATH_PREFILL)

@@ -1,0 +1,158 @@
+// ep_p2p.cu -- the expert-parallel exchanges as kernels over peer memory.
+//
+// qmoe-rs runs every expert in one process (src/moe.rs:40-130); split over
+// G GPUs, each forward moves every token's row to the ranks that own its
+// experts and each rank's partial sums back (the dispatch and combine of
+// expert parallelism).  Here each rank owns one device allocation (receive
+// rows, their metadata, returned partial rows, arrival flags) that the other
+// ranks map through CUDA IPC, and the copies are plain stores into the
+// peers' memory over NVLink from the kernels that read the data -- no
+// collective library, no staging buffer, no TMA on peer memory.
+//
+// Ordering: the CTAs of a copy kernel fence their stores system-wide and
+// count themselves done; the last one raises every rank's flag for this
+// rank with a system-scope release store of the forward's sequence number.
+// A waiting rank polls its own flags with acquire loads (bounded; on time-out
+// it raises the device error word).  The sequence number lives on the device
+// (read by every kernel of a forward, advanced by the last wait), so a whole
+// forward can be replayed from a CUDA graph.  Rank d's receive buffer is
+// rewritten only in the next forward, after d has returned its partial sums
+// of this one (which it computes after reading the rows), so one flag per
+// phase suffices.
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace qmoe {
+namespace {
+
+using sm100::kErrWaitTimeout;
+using sm100::kMaxWaitProbes;
+
+constexpr int kCopyThreads = 256;
+
+QMOE_DEV void st_release_sys(int *p, int v) {
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+QMOE_DEV int ld_acquire_sys(const int *p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+QMOE_DEV int *flag_at(const EpPeerDev &d, int owner, int phase, int from) {
+    return reinterpret_cast<int *>(d.base[owner] + d.off_flags) + phase * d.world + from;
+}
+
+// Copies one row of `bytes` (a multiple of 16) with the CTA.
+QMOE_DEV void copy_row(uint8_t *dst, const uint8_t *src, int64_t bytes) {
+    const uint4 *s = reinterpret_cast<const uint4 *>(src);
+    uint4 *o = reinterpret_cast<uint4 *>(dst);
+    for (int64_t i = threadIdx.x; i < bytes / 16; i += kCopyThreads) o[i] = s[i];
+}
+
+// After this CTA's stores: fence them system-wide, count the CTA; the last
+// CTA raises flag `phase` of this rank on every rank.
+QMOE_DEV void signal_done(const EpPeerDev &d, int phase) {
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomicAdd(d.done + phase, 1) == (int)(gridDim.x * gridDim.y) - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        d.done[phase] = 0;
+    }
+    __syncthreads();
+    const int s = *d.seq + 1;
+    for (int p = threadIdx.x; p < d.world; p += kCopyThreads) st_release_sys(flag_at(d, p, phase, d.rank), s);
+}
+
+// CTA j < world*C: send row j (destination j / C, row j % C) if it is in use,
+// and its metadata row; CTA world*C + t: this rank's own token t for the
+// shared expert (metadata: no routed expert).
+__global__ void __launch_bounds__(kCopyThreads)
+ep_dispatch_kernel(const EpPeerDev d, const void *x, int64_t T, const int32_t *send_counts,
+                   const int32_t *send_tok, const int32_t *send_meta) {
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int64_t GC = (int64_t)d.world * d.C;
+    const int64_t j = blockIdx.x;
+    const int64_t rb = d.H * d.esize, mb = 2 * (int64_t)d.K * 4;
+    const uint8_t *xs = static_cast<const uint8_t *>(x);
+    if (j < GC) {
+        const int dst = (int)(j / d.C);
+        const int64_t i = j - (int64_t)dst * d.C;
+        const int64_t r = (int64_t)d.rank * d.C + i;           // row in the destination's block
+        if (i < send_counts[dst]) copy_row(d.base[dst] + d.off_rows + r * rb, xs + send_tok[j] * rb, rb);
+        int32_t *m = reinterpret_cast<int32_t *>(d.base[dst] + d.off_meta + r * mb);
+        for (int k = threadIdx.x; k < 2 * d.K; k += kCopyThreads) m[k] = send_meta[j * 2 * d.K + k];
+    } else if (j - GC < T) {
+        const int64_t t = j - GC, r = GC + t;
+        copy_row(d.base[d.rank] + d.off_rows + r * rb, xs + t * rb, rb);
+        int32_t *m = reinterpret_cast<int32_t *>(d.base[d.rank] + d.off_meta + r * mb);
+        for (int k = threadIdx.x; k < 2 * d.K; k += kCopyThreads) m[k] = k < d.K ? -1 : 0;
+    }
+    signal_done(d, 0);
+}
+
+// CTA j < world*C: the partial row j (rows received from rank j / C) goes to
+// that rank's return block.
+__global__ void __launch_bounds__(kCopyThreads)
+ep_return_kernel(const EpPeerDev d, const void *y) {
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int64_t j = blockIdx.x;
+    const int64_t rb = d.H * d.esize;
+    const int dst = (int)(j / d.C);
+    const int64_t i = j - (int64_t)dst * d.C;
+    copy_row(d.base[dst] + d.off_back + ((int64_t)d.rank * d.C + i) * rb,
+             static_cast<const uint8_t *>(y) + j * rb, rb);
+    signal_done(d, 1);
+}
+
+// Lane p waits for rank p's flag of `phase`; the return phase ends the
+// forward and advances the sequence number.
+__global__ void __launch_bounds__(32)
+ep_wait_kernel(const EpPeerDev d, int phase) {
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int s = *d.seq + 1;
+    bool ok = true;
+    for (int p = threadIdx.x; p < d.world; p += 32) {
+        const int *f = flag_at(d, d.rank, phase, p);
+        uint32_t n = 0;
+        while (ld_acquire_sys(f) < s) {
+            if (++n >= kMaxWaitProbes) {
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (!ok) atomicOr(d.err, kErrWaitTimeout);
+    __syncwarp();
+    if (phase == 1 && threadIdx.x == 0) *d.seq = s;
+}
+
+}  // namespace
+
+cudaError_t launch_ep_dispatch(const EpPeerDev &d, const void *x, int64_t T, const int32_t *send_counts,
+                               const int32_t *send_tok, const int32_t *send_meta, cudaStream_t s) {
+    const int64_t ctas = (int64_t)d.world * d.C + T;
+    return launch_pdl(ep_dispatch_kernel, dim3((unsigned)ctas), dim3(kCopyThreads), 0, s, d, x, T, send_counts,
+                      send_tok, send_meta);
+}
+
+cudaError_t launch_ep_return(const EpPeerDev &d, const void *y, cudaStream_t s) {
+    return launch_pdl(ep_return_kernel, dim3((unsigned)(d.world * d.C)), dim3(kCopyThreads), 0, s, d, y);
+}
+
+cudaError_t launch_ep_wait(const EpPeerDev &d, int phase, cudaStream_t s) {
+    return launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, s, d, phase);
+}
+
+}  // namespace qmoe

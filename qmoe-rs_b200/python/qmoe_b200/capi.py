@@ -30,6 +30,7 @@ QMOE_PATH_DECODE = 1
 QMOE_PATH_PREFILL = 2
 QMOE_NOALLOC_MAX_BATCH = 16384
 QMOE_NOALLOC_MAX_IN_FEATURES = 8192
+QMOE_EP_HANDLE_BYTES = 64
 
 
 class QmoeError(RuntimeError):
@@ -98,6 +99,14 @@ SIGNATURES = {
     "qmoe_gather_rows": (_I, [_P, _P, _I, _I64, _P, _I64, _P]),
     "qmoe_combine_rows": (_I, [_P, _P, _I, _I64, _P, _I, _I64, _P, _P]),
     "qmoe_layer_forward_ep": (_I, [_P, _P, _I, _I64, _P, _I64, _P]),
+    "qmoe_ep_peer_create": (_I, [_P, _I, _I, _I64, _I64, _I, _I, _PP]),
+    "qmoe_ep_peer_destroy": (_I, [_P]),
+    "qmoe_ep_peer_handle": (_I, [_P, _P]),
+    "qmoe_ep_peer_connect": (_I, [_P, _P]),
+    "qmoe_ep_peer_buffers": (_I, [_P, _PP, _PP, _PP]),
+    "qmoe_ep_dispatch": (_I, [_P, _P, _I64, _P, _P, _P]),
+    "qmoe_ep_wait": (_I, [_P, _I]),
+    "qmoe_ep_return": (_I, [_P, _P]),
     "qmoe_layer_set_profiling": (_I, [_P, _I]),
     "qmoe_layer_stage_times": (_I, [_P, ctypes.POINTER(ctypes.c_float), _I,
                                     ctypes.POINTER(ctypes.c_int)]),

@@ -23,6 +23,11 @@ the batch.  One forward on every rank:
 The exchanges use fixed-size buffers (each destination gets `capacity` rows,
 unused rows carry expert ids -1 and are skipped), so a forward needs no
 device-to-host read of the counts and can be captured in a CUDA graph.
+
+Two ways to move the rows: `exchange="nccl"` (all-to-alls over the process
+group) or `exchange="p2p"` (PeerExchange: steps 3 and 5 as kernels that store
+straight into the other GPUs' memory over NVLink, each followed by a bounded
+wait on the peers' arrival flags).
 """
 from __future__ import annotations
 
@@ -30,6 +35,8 @@ try:
     import torch
 except ImportError:  # pragma: no cover - the EP layer needs torch.distributed
     torch = None
+
+import ctypes
 
 from . import capi
 from .layer import MoEConfig, QMoELayer
@@ -51,6 +58,55 @@ class TorchComm:
         return out
 
 
+class PeerExchange:
+    """One rank's exchange buffers in peer memory (qmoe_ep_peer_*): receive
+    rows and metadata, returned rows, arrival flags; the ranks open each
+    other's buffers through CUDA IPC handles gathered over `group`."""
+
+    def __init__(self, ctx, world: int, rank: int, capacity: int, H: int, K: int, dtype_code: int,
+                 group=None):
+        import torch.distributed as dist
+        h = ctypes.c_void_p()
+        capi.call("qmoe_ep_peer_create", ctx.handle, world, rank, capacity, H, K, dtype_code,
+                  ctypes.byref(h))
+        self._h = h
+        mine = (ctypes.c_uint8 * capi.QMOE_EP_HANDLE_BYTES)()
+        capi.call("qmoe_ep_peer_handle", h, mine)
+        dev = torch.device("cuda", ctx.device)
+        t = torch.tensor(list(bytes(mine)), dtype=torch.uint8, device=dev)
+        allh = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allh, t, group=group)
+        blob = bytes(torch.cat(allh).cpu().tolist())
+        buf = (ctypes.c_uint8 * len(blob)).from_buffer_copy(blob)
+        capi.call("qmoe_ep_peer_connect", h, buf)
+        dist.barrier(group=group)
+        rows, meta, back = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        capi.call("qmoe_ep_peer_buffers", h, ctypes.byref(rows), ctypes.byref(meta), ctypes.byref(back))
+        self.recv_rows, self.recv_meta, self.back_rows = rows.value, meta.value, back.value
+
+    def dispatch(self, x, T: int, counts, tok, meta):
+        capi.call("qmoe_ep_dispatch", self._h, ctypes.c_void_p(x.data_ptr()), T,
+                  ctypes.c_void_p(counts.data_ptr()), ctypes.c_void_p(tok.data_ptr()),
+                  ctypes.c_void_p(meta.data_ptr()))
+
+    def wait(self, phase: int):
+        capi.call("qmoe_ep_wait", self._h, phase)
+
+    def give_back(self, y):
+        capi.call("qmoe_ep_return", self._h, ctypes.c_void_p(y.data_ptr()))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            capi.lib().qmoe_ep_peer_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class ExpertParallelMoE:
     """One rank of an expert-parallel layer.
 
@@ -61,7 +117,8 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, config: MoEConfig, gate_weight, experts, rank: int, world: int,
-                 shared=None, bias=None, ctx=None, comm=None, capacity: int = 256):
+                 shared=None, bias=None, ctx=None, comm=None, capacity: int = 256,
+                 exchange: str = "nccl", dtype=None, group=None):
         if config.num_experts % world:
             raise ValueError(f"num_experts {config.num_experts} not divisible by world {world}")
         if not 1 <= world <= 32:
@@ -77,6 +134,15 @@ class ExpertParallelMoE:
         self.comm = comm
         self.capacity = int(capacity)
         self._bufs = {}
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange must be 'nccl' or 'p2p', not {exchange!r}")
+        self.exchange = exchange
+        self.peer = None
+        if exchange == "p2p":
+            dt = capi.QMOE_DTYPE_BF16 if dtype == torch.bfloat16 else capi.QMOE_DTYPE_F32
+            self.dtype = torch.bfloat16 if dt == capi.QMOE_DTYPE_BF16 else torch.float32
+            self.peer = PeerExchange(self.layer.ctx, world, rank, self.capacity,
+                                     config.hidden_dim, config.top_k, dt, group=group)
 
     # -- device steps (C ABI); split out so tests can exercise the exchanges
     def route(self, x):
@@ -174,7 +240,41 @@ class ExpertParallelMoE:
         extra = y[GC:GC + T] if self.has_shared else None
         return self.combine(back, slot, extra, T, x.dtype)
 
+    def forward_p2p(self, x, return_routing: bool = False):
+        """The forward with the exchanges over peer memory: dispatch kernel,
+        wait, this rank's experts on the received rows (and the shared expert
+        on its own tokens), return kernel, wait, combine."""
+        if x.dtype != self.dtype:
+            raise TypeError(f"this exchange carries {self.dtype} rows, got {x.dtype}")
+        T, H = x.shape
+        if T > self.capacity:
+            raise ValueError(f"T {T} > capacity {self.capacity}")
+        G, C, K = self.world, self.capacity, self.config.top_k
+        GC = G * C
+        idx, w = self.route(x)
+        counts, tok, meta, slot = self.plan(idx, w, T)
+        ctx = self.layer.ctx
+        ctx.use_current_torch_stream()
+        self.peer.dispatch(x, T, counts, tok, meta)
+        self.peer.wait(0)
+        y = self._buf(("y", x.dtype), lambda: torch.empty(GC + C, H, dtype=x.dtype, device=x.device))
+        R = GC + T if self.has_shared else GC
+        capi.call("qmoe_layer_forward_ep", self.layer._h, ctypes.c_void_p(self.peer.recv_rows), _dt(x), R,
+                  ctypes.c_void_p(self.peer.recv_meta), GC, y.data_ptr())
+        self.peer.give_back(y)
+        self.peer.wait(1)
+        out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+        extra = y[GC:GC + T] if self.has_shared else None
+        capi.call("qmoe_combine_rows", ctx.handle, ctypes.c_void_p(self.peer.back_rows), _dt(x), H,
+                  slot.data_ptr(), G, T, extra.data_ptr() if extra is not None else None,
+                  out.data_ptr())
+        if return_routing:
+            return out, idx, w
+        return out
+
     def forward(self, x, return_routing: bool = False):
+        if getattr(self, "peer", None) is not None:
+            return self.forward_p2p(x, return_routing)
         if self.comm is None:
             self.comm = TorchComm()
         GC = self.world * self.capacity
@@ -190,6 +290,11 @@ class ExpertParallelMoE:
         if return_routing:
             return out, state[2], state[3]
         return out
+
+    def close(self):
+        if getattr(self, "peer", None) is not None:
+            self.peer.close()
+            self.peer = None
 
     def _buf(self, key, make):
         b = self._bufs.get(key)
