@@ -45,9 +45,10 @@ WORKLOAD = dict(
 REPLICAS = 4
 KERNELS_PER_FORWARD = 8  # router logits + select, permute, limbs x2, gate/up, down, combine
 KERNELS_PER_PREFILL = 7  # router logits + select, permute, bf16 gather, gate/up, down, combine
-# EP rank: router x2, plan, gather, routed experts (permute, limbs x2, GEMV x2,
-# combine), return combine, shared expert (permute, limbs x2, GEMV x2, combine)
-KERNELS_PER_EP_FORWARD = 17
+# EP rank (peer-memory exchange): router x2, plan, dispatch, wait, expert pass
+# over the received rows + own tokens (permute, limbs x2, GEMV x2, combine),
+# return, wait, combine_rows
+KERNELS_PER_EP_FORWARD = 14
 
 
 def parse():
@@ -56,6 +57,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N > 1: peer-memory kernels or NCCL all-to-alls for the EP exchanges")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU-baseline leg (for profiler runs)")
@@ -387,7 +390,8 @@ def run_ep(args, ws, rank, local, dev, dist):
     for r in range(reps):
         experts, shared, gate_w = synth_weights(args.seed + 1000 * r, dev, experts=mine)
         layers.append(ExpertParallelMoE(cfg, gate_w, experts, rank, ws, shared=shared, ctx=ctx,
-                                        capacity=w["T"]))
+                                        capacity=w["T"], exchange=args.ep_exchange,
+                                        dtype=torch.float32))
         del experts, shared
     g = torch.Generator(device=dev).manual_seed(args.seed + 31 * rank)
     xs = [torch.randn(w["T"], w["H"], generator=g, device=dev) for _ in range(reps)]
@@ -396,7 +400,8 @@ def run_ep(args, ws, rank, local, dev, dist):
         layers[i % reps].forward(xs[i % reps])
     torch.cuda.synchronize()
     dist.barrier()
-    # one CUDA graph per replica, the NCCL exchanges captured with the kernels
+    # the replicas' forwards back to back in one CUDA graph (exchanges
+    # included: the peer-memory kernels, or NCCL captured with the kernels)
     stream = torch.cuda.Stream()
     graphs = []
     with torch.cuda.stream(stream):
@@ -408,10 +413,15 @@ def run_ep(args, ws, rank, local, dev, dist):
             with torch.cuda.graph(gr, stream=stream):
                 layers[r].forward(xs[r])
             graphs.append(gr)
+        chain = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(chain, stream=stream):
+            for r in range(reps):
+                layers[r].forward(xs[r])
     torch.cuda.synchronize()
     dist.barrier()
     for i in range(max(3, args.warmup)):
         graphs[i % reps].replay()
+        chain.replay()
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
@@ -419,8 +429,10 @@ def run_ep(args, ws, rank, local, dev, dist):
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         e0.record()
-        for i in range(args.steps):
-            graphs[i % reps].replay()
+        for _ in range(args.steps // reps):
+            chain.replay()
+        for i in range(args.steps % reps):
+            graphs[i].replay()
         e1.record()
         torch.cuda.synchronize()
     dist.barrier()
@@ -457,9 +469,11 @@ def run_ep(args, ws, rank, local, dev, dist):
                        "top_k": w["k"], "hidden": w["H"], "intermediate": w["I"],
                        "shared_intermediate": w["Is"], "activations": "f32",
                        "parallelism": f"ep{ws}", "experts_per_gpu": epr,
-                       "exchange": "NCCL all_to_all_single, fixed-capacity rows",
+                       "exchange": ("peer-memory stores into the other GPUs' IPC-mapped buffers "
+                                    "(NVLink), arrival flags" if args.ep_exchange == "p2p"
+                                    else "NCCL all_to_all_single") + ", fixed-capacity rows",
                        "l2": f"{reps} rotating weight replicas per GPU (> L2)",
-                       "graphs": "one CUDA graph per replica, NCCL exchanges captured"},
+                       "graphs": f"one CUDA graph of the {reps} replicas' forwards back to back"},
             "roofline": None,
             "e2e": {"value": ws * w["T"] / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": 4 * w["T"] * w["H"] * ws,
@@ -471,7 +485,11 @@ def run_ep(args, ws, rank, local, dev, dist):
     for gr in graphs:
         del gr
     graphs.clear()
+    del chain
     torch.cuda.synchronize()
+    dist.barrier()
+    for L in layers:          # every rank is done with the others' buffers
+        L.close()
     dist.barrier()
     dist.destroy_process_group()
 

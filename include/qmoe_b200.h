@@ -13,8 +13,10 @@
  *   - Plain pointers and sizes only.  `ptr_kind` says whether the data
  *     pointers of one call are host (QMOE_PTR_HOST) or device
  *     (QMOE_PTR_DEVICE) memory.  Host inputs are copied in and host outputs
- *     copied back on the context's stream, and the call returns after the
- *     copy back completes.  Device calls are asynchronous on that stream.
+ *     copied back on the context's stream (qmoe_layer_forward reads and
+ *     writes page-locked host buffers in place instead), and the call
+ *     returns after the results are in host memory.  Device calls are
+ *     asynchronous on that stream.
  *   - Packed weights use qmoe-rs's layout verbatim (quantize.py:7-33,
  *     src/tensor.rs:16-23): uint8 [out, in/4], four 2-bit codes per byte,
  *     weight j of each group of four in bits 2j..2j+1, value = code - 1
@@ -313,16 +315,16 @@ QMOE_API int qmoe_layer_forward_ep(qmoe_layer *layer, const void *x, int dtype, 
  *   qmoe_ep_dispatch     rows x[send_tok[d*C + i]] (i < send_counts[d]) and
  *                        all C metadata rows of block d go to rank d's
  *                        receive block `rank`; this rank's own tokens x[0..T)
- *                        go to its own receive rows world*C ..; then each
- *                        rank's dispatch flag is raised;
- *   qmoe_ep_wait         waits (bounded) until every rank's flag of a phase
- *                        is up (phase 0: dispatch, 1: return);
+ *                        go to its own receive rows world*C ..; every row
+ *                        sent counts one arrival on its destination;
+ *   qmoe_ep_wait         waits (bounded) until every other rank's C rows of
+ *                        a phase have arrived (phase 0: dispatch, 1: return);
  *   qmoe_ep_return       rows y[d*C + i] (the partial sums of the rows
  *                        received from rank d) go to rank d's return block
- *                        `rank`; then the return flags;
- *   qmoe_ep_wait(1)      ends the forward (the flags carry a per-forward
- *                        sequence number kept on the device, so the whole
- *                        forward can be captured in a CUDA graph).
+ *                        `rank`, each counted on arrival;
+ *   qmoe_ep_wait(1)      ends the forward (arrivals are counted against a
+ *                        per-forward sequence number kept on the device, so
+ *                        the whole forward can be captured in a CUDA graph).
  *
  * These replace the three all-to-alls (ExpertParallelMoE over
  * torch.distributed) with two peer-store phases; with the buffers used as

@@ -1307,7 +1307,6 @@ int qmoe_ep_peer_create(qmoe_ctx *ctx, int world, int rank, int64_t capacity, in
     }
     d.base[rank] = p->mem;
     d.seq = reinterpret_cast<int *>(p->mem + off_local);
-    d.done = d.seq + 1;
     d.err = error_flag();
     *out = p;
     return QMOE_OK;

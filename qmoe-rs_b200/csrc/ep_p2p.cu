@@ -9,13 +9,15 @@
 // peers' memory over NVLink from the kernels that read the data -- no
 // collective library, no staging buffer, no TMA on peer memory.
 //
-// Ordering: the CTAs of a copy kernel fence their stores system-wide and
-// count themselves done; the last one raises every rank's flag for this
-// rank with a system-scope release store of the forward's sequence number.
-// A waiting rank polls its own flags with acquire loads (bounded; on time-out
-// it raises the device error word).  The sequence number lives on the device
-// (read by every kernel of a forward, advanced by the last wait), so a whole
-// forward can be replayed from a CUDA graph.  Rank d's receive buffer is
+// Ordering: every CTA of a copy kernel moves one row to one rank; it fences
+// its stores system-wide and adds one to that rank's arrival counter for
+// (phase, this rank) with a system-scope atomic.  A waiting rank polls its
+// own counters with acquire loads until each peer's reaches C x the
+// forward's sequence number (bounded; on time-out it raises the device error
+// word); rows a rank sends to itself are ordered by its stream and not
+// counted.  The sequence number lives on the device (read by every kernel of
+// a forward, advanced by the last wait), so a whole forward can be replayed
+// from a CUDA graph.  Rank d's receive buffer is
 // rewritten only in the next forward, after d has returned its partial sums
 // of this one (which it computes after reading the rows), so one flag per
 // phase suffices.
@@ -31,9 +33,6 @@ using sm100::kMaxWaitProbes;
 
 constexpr int kCopyThreads = 256;
 
-QMOE_DEV void st_release_sys(int *p, int v) {
-    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 QMOE_DEV int ld_acquire_sys(const int *p) {
     int v;
     asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -51,24 +50,14 @@ QMOE_DEV void copy_row(uint8_t *dst, const uint8_t *src, int64_t bytes) {
     for (int64_t i = threadIdx.x; i < bytes / 16; i += kCopyThreads) o[i] = s[i];
 }
 
-// After this CTA's stores: fence them system-wide, count the CTA; the last
-// CTA raises flag `phase` of this rank on every rank.
-QMOE_DEV void signal_done(const EpPeerDev &d, int phase) {
-    __shared__ int last;
+// After this CTA's stores to rank dst: fence them system-wide and count one
+// arrival on dst (rows a rank keeps are ordered by its own stream).
+QMOE_DEV void arrive(const EpPeerDev &d, int dst, int phase) {
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0 && dst != d.rank) {
         __threadfence_system();
-        last = atomicAdd(d.done + phase, 1) == (int)(gridDim.x * gridDim.y) - 1;
+        atomicAdd_system(flag_at(d, dst, phase, d.rank), 1);
     }
-    __syncthreads();
-    if (!last) return;
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        d.done[phase] = 0;
-    }
-    __syncthreads();
-    const int s = *d.seq + 1;
-    for (int p = threadIdx.x; p < d.world; p += kCopyThreads) st_release_sys(flag_at(d, p, phase, d.rank), s);
 }
 
 // CTA j < world*C: send row j (destination j / C, row j % C) if it is in use,
@@ -90,13 +79,13 @@ ep_dispatch_kernel(const EpPeerDev d, const void *x, int64_t T, const int32_t *s
         if (i < send_counts[dst]) copy_row(d.base[dst] + d.off_rows + r * rb, xs + send_tok[j] * rb, rb);
         int32_t *m = reinterpret_cast<int32_t *>(d.base[dst] + d.off_meta + r * mb);
         for (int k = threadIdx.x; k < 2 * d.K; k += kCopyThreads) m[k] = send_meta[j * 2 * d.K + k];
+        arrive(d, dst, 0);
     } else if (j - GC < T) {
         const int64_t t = j - GC, r = GC + t;
         copy_row(d.base[d.rank] + d.off_rows + r * rb, xs + t * rb, rb);
         int32_t *m = reinterpret_cast<int32_t *>(d.base[d.rank] + d.off_meta + r * mb);
         for (int k = threadIdx.x; k < 2 * d.K; k += kCopyThreads) m[k] = k < d.K ? -1 : 0;
     }
-    signal_done(d, 0);
 }
 
 // CTA j < world*C: the partial row j (rows received from rank j / C) goes to
@@ -111,21 +100,24 @@ ep_return_kernel(const EpPeerDev d, const void *y) {
     const int64_t i = j - (int64_t)dst * d.C;
     copy_row(d.base[dst] + d.off_back + ((int64_t)d.rank * d.C + i) * rb,
              static_cast<const uint8_t *>(y) + j * rb, rb);
-    signal_done(d, 1);
+    arrive(d, dst, 1);
 }
 
-// Lane p waits for rank p's flag of `phase`; the return phase ends the
-// forward and advances the sequence number.
+// Lane p waits until rank p's C rows of `phase` of this forward have
+// arrived; the return phase ends the forward and advances the sequence
+// number.
 __global__ void __launch_bounds__(32)
 ep_wait_kernel(const EpPeerDev d, int phase) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int s = *d.seq + 1;
+    const int want = (int)(s * d.C);
     bool ok = true;
     for (int p = threadIdx.x; p < d.world; p += 32) {
+        if (p == d.rank) continue;
         const int *f = flag_at(d, d.rank, phase, p);
         uint32_t n = 0;
-        while (ld_acquire_sys(f) < s) {
+        while (ld_acquire_sys(f) < want) {
             if (++n >= kMaxWaitProbes) {
                 ok = false;
                 break;

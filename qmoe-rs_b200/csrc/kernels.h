@@ -155,7 +155,7 @@ int qgemv_imma_buffers(int kp_b);
 // ---- expert-parallel exchange over peer memory (ep_p2p.cu) ---------------
 // Every rank's allocation has the same layout: receive rows [G*C + C][H]
 // (dtype), receive metadata [G*C + C][2K] int32, returned rows [G*C][H],
-// flags [2][G] int32; offsets below.  base[r] = rank r's allocation as this
+// arrival counters [2][G] int32; offsets below.  base[r] = rank r's allocation as this
 // GPU addresses it (its own included).
 constexpr int kEpMaxWorld = 32;
 struct EpPeerDev {
@@ -164,7 +164,6 @@ struct EpPeerDev {
     int64_t C, H, esize;
     int64_t off_rows, off_meta, off_back, off_flags;
     int *seq;                    // this rank's per-forward sequence number
-    int *done;                   // this rank's CTA counters of the two copy phases [2]
     int *err;                    // device error word
 };
 cudaError_t launch_ep_dispatch(const EpPeerDev &d, const void *x, int64_t T, const int32_t *send_counts,
