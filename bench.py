@@ -376,7 +376,8 @@ def run_prefill(layers, seed: int, dev: str, steps: int = 20):
 def run_ep(args, ws, rank, local, dev, dist):
     """N > 1: the layer expert-parallel over the N GPUs (each holds E/N
     experts, a gate and shared-expert replica and its own 32 decode tokens),
-    NCCL all-to-all dispatch and return.  Weak scaling: tokens per GPU fixed."""
+    dispatch and return by stores into the peers' memory (--ep-exchange p2p)
+    or NCCL all-to-all.  Weak scaling: tokens per GPU fixed."""
     from qmoe_b200 import ExpertParallelMoE, default_context
     w = WORKLOAD
     cfg = make_cfg()
@@ -427,7 +428,12 @@ def run_ep(args, ws, rank, local, dev, dist):
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    align = torch.zeros(1, device=dev)
     with ClockSampler(local) as clk:
+        # the start event follows a collective on the device, so every rank's
+        # clock starts when the last rank arrives (host launch skew between
+        # the ranks is not counted as exchange waiting)
+        dist.all_reduce(align)
         e0.record()
         for _ in range(args.steps // reps):
             chain.replay()
@@ -451,6 +457,7 @@ def run_ep(args, ws, rank, local, dev, dist):
     dist.barrier()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
+    dist.all_reduce(align)
     a.record()
     for i in range(n_e2e):
         out_host.copy_(layers[0].forward(x_host.to(dev, non_blocking=True)), non_blocking=True)

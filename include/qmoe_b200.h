@@ -300,6 +300,14 @@ QMOE_API int qmoe_combine_rows(qmoe_ctx *ctx, const void *rows, int dtype, int64
  * pointers, asynchronous. */
 QMOE_API int qmoe_layer_forward_ep(qmoe_layer *layer, const void *x, int dtype, int64_t R,
                                    const int32_t *meta, int64_t shared_row0, void *out);
+/* qmoe_layer_route followed by qmoe_ep_plan (capacity >= T, padded rows)
+ * on this rank's tokens, device pointers, asynchronous: for small batches
+ * one launch (the decode front cluster with the send list built in place of
+ * the permute), else the router kernels and the plan kernel. */
+QMOE_API int qmoe_layer_route_plan(qmoe_layer *layer, const void *x, int dtype, int64_t T,
+                                   int32_t *topk_idx, float *topk_w, int experts_per_rank, int world,
+                                   int64_t capacity, int32_t *send_counts, int32_t *send_tok,
+                                   int32_t *send_meta, int32_t *slot_pos);
 
 /* ---- expert-parallel exchange over peer memory ------------------------
  *

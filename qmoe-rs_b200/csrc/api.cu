@@ -1088,6 +1088,58 @@ int qmoe_layer_route(qmoe_layer *L, const void *x, int dtype, int64_t T, int32_t
     return QMOE_OK;
 }
 
+int qmoe_layer_route_plan(qmoe_layer *L, const void *x, int dtype, int64_t T, int32_t *topk_idx,
+                          float *topk_w, int experts_per_rank, int world, int64_t capacity,
+                          int32_t *send_counts, int32_t *send_tok, int32_t *send_meta, int32_t *slot_pos) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    QTRY(check_dtype(dtype));
+    const qmoe_moe_config &c = L->cfg;
+    if (T < 0 || world < 1 || world > kEpMaxWorld || experts_per_rank < 1 ||
+        experts_per_rank * world != c.num_experts)
+        return fail(QMOE_ERR_INVALID, "bad plan (T %lld, world %d, experts_per_rank %d, %d experts)",
+                    (long long)T, world, experts_per_rank, c.num_experts);
+    if (capacity < T) return fail(QMOE_ERR_INVALID, "capacity %lld < T %lld", (long long)capacity,
+                                  (long long)T);
+    if (T > 0 && (!x || !topk_idx || !topk_w || !send_counts || !send_tok || !send_meta || !slot_pos))
+        return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (T == 0) return QMOE_OK;
+    QTRY(check_align(x, QMOE_PTR_DEVICE, "x"));
+    DeviceGuard g(L->ctx->device);
+    cudaStream_t st = L->ctx->stream;
+    QTRY(layer_reserve(L, T));
+    RouterParams rp = router_params(L, x, dtype, T);
+    rp.topk_idx = topk_idx;
+    rp.topk_w = topk_w;
+    mark(L, 0);
+    if (front_cluster_ok(T, c.hidden_dim, c.num_experts, c.top_k)) {
+        FrontParams f{};
+        f.plan_world = world;
+        f.plan_epr = experts_per_rank;
+        f.plan_capacity = capacity;
+        f.send_counts = send_counts;
+        f.send_tok = send_tok;
+        f.send_meta = send_meta;
+        f.slot_pos = slot_pos;
+        QTRY_CUDA(launch_front_cluster(rp, f, st));
+        return QMOE_OK;
+    }
+    QTRY_CUDA(launch_router(rp, nullptr, st));
+    EpPlanParams p{};
+    p.topk_idx = topk_idx;
+    p.topk_w = topk_w;
+    p.T = T;
+    p.K = c.top_k;
+    p.experts_per_rank = experts_per_rank;
+    p.world = world;
+    p.capacity = capacity;
+    p.send_counts = send_counts;
+    p.send_tok = send_tok;
+    p.send_meta = send_meta;
+    p.slot_pos = slot_pos;
+    QTRY_CUDA(launch_ep_plan(p, st));
+    return QMOE_OK;
+}
+
 int qmoe_layer_forward_routed(qmoe_layer *L, const void *x, int dtype, int64_t R,
                               const int32_t *topk_idx, const float *topk_w, void *out,
                               int ptr_kind) {

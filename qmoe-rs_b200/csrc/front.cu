@@ -64,7 +64,7 @@ struct FrontLayout {
     int ep, tp;          // experts / tokens rounded up to the compute tiles
     int ws_ld, xs_ld;    // row strides of the transposed gate and x tiles
     int town;            // tokens owned by one CTA (at most)
-    int ws, xs, recv, warp, sel, tail;
+    int ws, xs, recv, warp, sel, selw, tail;
     int warp_floats;
     int total;
 };
@@ -85,13 +85,15 @@ __host__ __device__ inline FrontLayout front_layout(int T, int E, int nc, int cs
     L.warp_floats = 2 * ((E + 3) / 4 * 4) + 128;
     L.warp = L.recv + (L.town * nc * E + 3) / 4 * 4;
     L.sel = L.warp + kFrontWarps * L.warp_floats;            // [T][K] ids (CTA 0)
-    L.tail = (L.sel + kFrontMaxT * kFrontMaxK + 3) / 4 * 4;  // TailState (CTA 0)
+    L.selw = L.sel + kFrontMaxT * kFrontMaxK;                // [T][K] weight bits (CTA 0)
+    L.tail = (L.selw + kFrontMaxT * kFrontMaxK + 3) / 4 * 4; // TailState (CTA 0)
     L.total = L.tail;
     return L;
 }
 
 struct TailState {
     uint32_t mlo[kFrontMaxE], mhi[kFrontMaxE];  // tokens 0-31 / 32-63 that picked each expert
+    uint32_t dlo[kEpMaxWorld], dhi[kEpMaxWorld];  // plan: tokens sending to each rank
     int off[kFrontMaxE];                         // segment start of each expert
     int wsum[2][kFrontWarps];                    // per-warp totals of the scans
 };
@@ -209,6 +211,62 @@ QMOE_DEV void permute_tail(const FrontParams &f, int T, int E, int K, const int 
         const int64_t b = (int64_t)g * f.chunk;
         const int64_t rem = f.shared_count - b;
         f.groups[gt + g] = make_int4(E, (int)(TK + b), (int)(rem < f.chunk ? rem : f.chunk), 0);
+    }
+}
+
+// The expert-parallel send list of all T tokens (qmoe_ep_plan's padded
+// layout) from their selections sel[T][K] and weight bits selw[T][K] (one
+// CTA): rank d's rows start at d * C, tokens in order, each row's metadata
+// the local ids on d (-1 for slots owned elsewhere) and the weights' bits;
+// unused rows carry token 0, ids -1 and weight 0.
+QMOE_DEV void plan_tail(const FrontParams &f, int T, int K, const int *sel, const int *selw, TailState &S) {
+    const int tid = threadIdx.x, G = f.plan_world, epr = f.plan_epr;
+    const int64_t C = f.plan_capacity;
+    for (int d = tid; d < G; d += kFrontThreads) {
+        S.dlo[d] = 0u;
+        S.dhi[d] = 0u;
+    }
+    __syncthreads();
+    for (int a = tid; a < T * K; a += kFrontThreads) {
+        const int t = a / K, e = sel[a];
+        if (e >= 0) atomicOr(t < 32 ? &S.dlo[e / epr] : &S.dhi[e / epr], 1u << (t & 31));
+    }
+    __syncthreads();
+    for (int d = tid; d < G; d += kFrontThreads) f.send_counts[d] = __popc(S.dlo[d]) + __popc(S.dhi[d]);
+    // rows past each destination's count: unused
+    for (int64_t r = tid; r < (int64_t)G * C; r += kFrontThreads) {
+        const int d = (int)(r / C);
+        const int64_t i = r - (int64_t)d * C;
+        if (i >= __popc(S.dlo[d]) + __popc(S.dhi[d])) {
+            f.send_tok[r] = 0;
+            int32_t *m = f.send_meta + r * 2 * K;
+            for (int k = 0; k < K; ++k) {
+                m[k] = -1;
+                m[K + k] = 0;
+            }
+        }
+    }
+    // (token, destination) pairs: the row is d * C + the token's rank among
+    // the tokens sending to d
+    for (int a = tid; a < T * G; a += kFrontThreads) {
+        const int t = a / G, d = a - t * G;
+        const uint32_t lo = S.dlo[d], hi = S.dhi[d];
+        const uint32_t below = (1u << (t & 31)) - 1u;
+        const bool sends = ((t < 32 ? lo : hi) >> (t & 31)) & 1u;
+        if (!sends) {
+            f.slot_pos[a] = -1;
+            continue;
+        }
+        const int64_t r = (int64_t)d * C + (t < 32 ? __popc(lo & below) : __popc(lo) + __popc(hi & below));
+        f.send_tok[r] = t;
+        int32_t *m = f.send_meta + r * 2 * K;
+        for (int k = 0; k < K; ++k) {
+            const int e = sel[t * K + k];
+            const bool mine = e >= 0 && e / epr == d;
+            m[k] = mine ? e - d * epr : -1;
+            m[K + k] = mine ? selw[t * K + k] : 0;
+        }
+        f.slot_pos[a] = (int32_t)r;
     }
 }
 
@@ -330,19 +388,24 @@ front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
         }
         __syncwarp();
         const uint32_t sel0 = dsmem_map((uint32_t)__cvta_generic_to_shared(sm + L.sel), 0u);
+        const uint32_t selw0 = dsmem_map((uint32_t)__cvta_generic_to_shared(sm + L.selw), 0u);
         if (E <= 32)
-            select_token<1>(p, t, lane, lg, ex, gs, gk, sel0, true);
+            select_token<1>(p, t, lane, lg, ex, gs, gk, sel0, selw0, true);
         else if (E <= 64)
-            select_token<2>(p, t, lane, lg, ex, gs, gk, sel0, true);
+            select_token<2>(p, t, lane, lg, ex, gs, gk, sel0, selw0, true);
         else if (E <= 128)
-            select_token<4>(p, t, lane, lg, ex, gs, gk, sel0, true);
+            select_token<4>(p, t, lane, lg, ex, gs, gk, sel0, selw0, true);
         else
-            select_token<8>(p, t, lane, lg, ex, gs, gk, sel0, true);
+            select_token<8>(p, t, lane, lg, ex, gs, gk, sel0, selw0, true);
     }
     cluster_sync_all();  // every selection in CTA 0
     if (rank != 0) return;
-    permute_tail(f, T, E, K, reinterpret_cast<const int *>(sm + L.sel),
-                 *reinterpret_cast<TailState *>(sm + L.tail));
+    if (f.plan_world > 0)
+        plan_tail(f, T, K, reinterpret_cast<const int *>(sm + L.sel), reinterpret_cast<const int *>(sm + L.selw),
+                  *reinterpret_cast<TailState *>(sm + L.tail));
+    else
+        permute_tail(f, T, E, K, reinterpret_cast<const int *>(sm + L.sel),
+                     *reinterpret_cast<TailState *>(sm + L.tail));
 }
 
 }  // namespace

@@ -46,6 +46,11 @@ struct FrontParams {
     int4 *groups;
     int32_t *n_groups;         // [2]
     void *x_copy;              // front cluster kernel: device copy of x to write (nullable)
+    // front cluster kernel, plan_world > 0: instead of the permute, the
+    // expert-parallel send list of qmoe_ep_plan (padded layout, capacity >= T)
+    int plan_world, plan_epr;
+    int64_t plan_capacity;
+    int32_t *send_counts, *send_tok, *send_meta, *slot_pos;
 };
 bool router_tail_ok(int64_t T, int E, int K);
 cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaStream_t s);

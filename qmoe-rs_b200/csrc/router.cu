@@ -480,13 +480,13 @@ router_select_warp_kernel(const RouterParams p, int from_partials) {
     }
     __syncwarp();
     if (E <= 32)
-        select_token<1>(p, (int)t, lane, lg, ex, gs, gk, 0u, false);
+        select_token<1>(p, (int)t, lane, lg, ex, gs, gk, 0u, 0u, false);
     else if (E <= 64)
-        select_token<2>(p, (int)t, lane, lg, ex, gs, gk, 0u, false);
+        select_token<2>(p, (int)t, lane, lg, ex, gs, gk, 0u, 0u, false);
     else if (E <= 128)
-        select_token<4>(p, (int)t, lane, lg, ex, gs, gk, 0u, false);
+        select_token<4>(p, (int)t, lane, lg, ex, gs, gk, 0u, 0u, false);
     else
-        select_token<8>(p, (int)t, lane, lg, ex, gs, gk, 0u, false);
+        select_token<8>(p, (int)t, lane, lg, ex, gs, gk, 0u, 0u, false);
 }
 
 }  // namespace

@@ -60,12 +60,12 @@ QMOE_DEV void warp_sort(float (&v)[N], int (&id)[N], int lane) {
 // Scoring, group limit, top-k and combine weights of token t by one warp,
 // from its logits lg[E] (the arithmetic of router_select_kernel; the ranks
 // come from a sort instead of counting).  Lanes j < K write slot j's id and
-// weight, and, when `gather`, the id to a cluster CTA's gather array at the
-// shared::cluster address sel0.  E <= 32 N, K <= 32; ex, gs, gk: warp
+// weight, and, when `gather`, the id and the weight's bits to a cluster CTA's
+// gather arrays at the shared::cluster addresses sel0 and selw0.  E <= 32 N, K <= 32; ex, gs, gk: warp
 // scratch of E, 64 and 64 entries.
 template <int N>
 QMOE_DEV void select_token(const RouterParams &p, int t, int lane, const float *lg, float *ex, float *gs,
-                           int *gk, uint32_t sel0, bool gather) {
+                           int *gk, uint32_t sel0, uint32_t selw0, bool gather) {
     const int E = p.E, K = p.K;
     const bool sigm = p.scoring == 1;
     const float NEG = __int_as_float(0xff800000);
@@ -182,10 +182,14 @@ QMOE_DEV void select_token(const RouterParams &p, int t, int lane, const float *
     if (lane < K) {
         p.topk_idx[(int64_t)t * K + lane] = my_sel;
         p.topk_w[(int64_t)t * K + lane] = w;
-        if (gather)
+        if (gather) {
             asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(sel0 + 4u * (uint32_t)(t * K + lane)),
                          "r"(my_sel)
                          : "memory");
+            asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(selw0 + 4u * (uint32_t)(t * K + lane)),
+                         "r"(__float_as_int(w))
+                         : "memory");
+        }
     }
 }
 

@@ -164,6 +164,27 @@ class ExpertParallelMoE:
                   b["meta"].data_ptr(), b["slot"].data_ptr())
         return b["counts"], b["tok"], b["meta"], b["slot"][:T]
 
+    def route_plan(self, x):
+        """route() then plan() on this rank's tokens in one C-ABI call (one
+        kernel launch for decode-sized batches) -> (idx, w, counts, tok,
+        meta, slot)."""
+        T = x.shape[0]
+        G, K, C = self.world, self.config.top_k, self.capacity
+        dev = x.device
+        b = self._buf("plan", lambda: dict(
+            counts=torch.empty(G, dtype=torch.int32, device=dev),
+            tok=torch.empty(G * C, dtype=torch.int32, device=dev),
+            meta=torch.empty(G * C, 2 * K, dtype=torch.int32, device=dev),
+            slot=torch.empty(C, G, dtype=torch.int32, device=dev)))
+        r = self._buf("routing", lambda: dict(
+            idx=torch.empty(C, K, dtype=torch.int32, device=dev),
+            w=torch.empty(C, K, dtype=torch.float32, device=dev)))
+        self.layer.ctx.use_current_torch_stream()
+        capi.call("qmoe_layer_route_plan", self.layer._h, x.data_ptr(), _dt(x), T,
+                  r["idx"].data_ptr(), r["w"].data_ptr(), self.epr, G, C, b["counts"].data_ptr(),
+                  b["tok"].data_ptr(), b["meta"].data_ptr(), b["slot"].data_ptr())
+        return r["idx"][:T], r["w"][:T], b["counts"], b["tok"], b["meta"], b["slot"][:T]
+
     def gather(self, x, tok):
         H = x.shape[1]
         out = self._buf(("gather", x.dtype), lambda: torch.empty(
@@ -251,8 +272,7 @@ class ExpertParallelMoE:
             raise ValueError(f"T {T} > capacity {self.capacity}")
         G, C, K = self.world, self.capacity, self.config.top_k
         GC = G * C
-        idx, w = self.route(x)
-        counts, tok, meta, slot = self.plan(idx, w, T)
+        idx, w, counts, tok, meta, slot = self.route_plan(x)
         ctx = self.layer.ctx
         ctx.use_current_torch_stream()
         self.peer.dispatch(x, T, counts, tok, meta)
@@ -269,7 +289,7 @@ class ExpertParallelMoE:
                   slot.data_ptr(), G, T, extra.data_ptr() if extra is not None else None,
                   out.data_ptr())
         if return_routing:
-            return out, idx, w
+            return out, idx.clone(), w.clone()
         return out
 
     def forward(self, x, return_routing: bool = False):

@@ -133,3 +133,26 @@ def test_gather_and_combine_rows():
         capi.call("qmoe_combine_rows", ctx.handle, x.data_ptr(), code, 64, slot.data_ptr(), 3, 3,
                   extra.data_ptr(), res.data_ptr())
         assert torch.equal(res, (ref + extra.float()).to(dt))
+
+
+@pytest.mark.parametrize("G,T,dtype", [
+    (2, 1, torch.float32), (2, 33, torch.bfloat16), (8, 64, torch.float32), (4, 100, torch.float32),
+])
+def test_route_plan_matches_route_then_plan(G, T, dtype):
+    """qmoe_layer_route_plan (the front cluster building the send list for
+    T <= 64, the router and plan kernels otherwise) against qmoe_layer_route
+    followed by qmoe_ep_plan: routing and every send-list array bit-exact."""
+    E, K, H, I = 64, 6, 512, 128
+    cfg = MoEConfig(E, K, H, I)
+    experts, _, gw = helpers.synth_layer(E, H, I, 0, seed=T + G, device="cuda")
+    epr = E // G
+    C = 128
+    rank = ExpertParallelMoE(cfg, gw, experts[:epr], 0, G, capacity=C)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(T)).to(dtype).cuda()
+    idx, w, counts, tok, meta, slot = [a.clone() for a in rank.route_plan(x)]
+    ri, rw = rank.route(x)
+    rc, rt, rm, rs = rank.plan(ri, rw, T)
+    torch.cuda.synchronize()
+    for a, b in [(idx, ri), (w, rw), (counts, rc), (tok, rt), (meta, rm), (slot, rs)]:
+        assert a.shape == b.shape
+        np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
