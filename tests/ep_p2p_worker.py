@@ -5,7 +5,8 @@ Every rank builds the same seeded layer, keeps its block of experts, and
 checks its own tokens' outputs from the peer-memory exchange against the
 all-to-all exchange over the process group (the same kernels on the same
 rows: equal bits) and against the whole layer on one GPU (within the f32 /
-bf16 bars), then repeats from a CUDA graph."""
+bf16 bars), then repeats from a CUDA graph.  24 tokens per rank take the
+one-launch route+plan of the decode front, 100 the router and plan kernels."""
 import datetime
 import os
 import sys
@@ -29,14 +30,15 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
-    E, K, H, I, Is, T = 16, 4, 512, 256, 256, 24
+    E, K, H, I, Is = 16, 4, 512, 256, 256
     cfg = MoEConfig(E, K, H, I, shared_intermediate_dim=Is)
     experts, shared, gate_w = helpers.synth_layer(E, H, I, Is, seed=5, device=dev)
     epr = E // world
     mine = experts[rank * epr:(rank + 1) * epr]
     ctx = default_context(local)
     full = QMoELayer(cfg, gate_w, experts, shared=shared, ctx=ctx)
-    for dtype, tol in ((torch.float32, 1e-4), (torch.bfloat16, 2e-2)):
+    for T, dtype, tol in ((24, torch.float32, 1e-4), (24, torch.bfloat16, 2e-2),
+                          (100, torch.float32, 1e-4)):
         g = torch.Generator().manual_seed(100 + rank)
         xs = [torch.randn(T, H, generator=g).to(dtype).to(dev) for _ in range(3)]
         p2p = ExpertParallelMoE(cfg, gate_w, mine, rank, world, shared=shared, capacity=T,

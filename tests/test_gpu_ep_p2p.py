@@ -1,4 +1,4 @@
-"""Peer-memory expert-parallel exchange on 2 (and, where present, 4) GPUs:
+"""Peer-memory expert-parallel exchange on 2 (and, where present, 4 and 8) GPUs:
 child processes under torch.distributed.run, one per GPU (see
 ep_p2p_worker.py).  Skipped on boxes with fewer than two GPUs."""
 import os
@@ -19,7 +19,7 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("n", [2, 4])
+@pytest.mark.parametrize("n", [2, 4, 8])
 def test_ep_p2p_matches_all_to_all_and_one_gpu(n):
     if not torch.cuda.is_available() or torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")
