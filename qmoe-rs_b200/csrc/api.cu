@@ -191,7 +191,7 @@ struct qmoe_layer {
     DevBuf xq1, meta1, xq2, meta2, router_scratch;
     DevBuf front_counter;  // hand-off counter of the decode front kernel (kept at zero)
     CUtensorMap tm_xq1, tm_xq2;
-    CUtensorMap tm_xq1_3, tm_xq2_3;   // 3-D views: 16 limb rows x every 128-byte block
+    CUtensorMap tm_xq1_3, tm_xq2_3;   // 4-D views: 16 limb rows x 512 codes per decode stage
     // prefill path: gate/up maps with 64-row boxes, bf16 activation / SwiGLU
     // rows (16-element blocks permuted) and their 128-byte-swizzled maps
     bool prefill_ok = false;
@@ -633,11 +633,19 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
         !make_tmap_u8(&L->tm_xq2, L->xq2.p, (uint64_t)L->kp2, (uint64_t)(npos * 3), 128, 16,
                       CU_TENSOR_MAP_SWIZZLE_128B))
         return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the limb scratch");
-    if (!make_tmap_u8_3d(&L->tm_xq1_3, L->xq1.p, 128, (uint64_t)(npos * 3), (uint64_t)(L->kp1 / 128),
-                         (uint64_t)L->kp1, 128, 128, 16, 4, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap_u8_3d(&L->tm_xq2_3, L->xq2.p, 128, (uint64_t)(npos * 3), (uint64_t)(L->kp2 / 128),
-                         (uint64_t)L->kp2, 128, 128, 16, 4, CU_TENSOR_MAP_SWIZZLE_128B))
-        return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed for the limb scratch");
+    // decode GEMV stage view: (128-byte block x, block of a 256-code group,
+    // limb row, group); the box lands as [group][row][block] lines, so the
+    // 128-byte swizzle phase (2 row + block) differs for the four (row pair,
+    // block) combinations a quarter-warp reads
+    {
+        const uint64_t d1[4] = {128, 2, (uint64_t)(npos * 3), (uint64_t)(L->kp1 / 256)};
+        const uint64_t d2[4] = {128, 2, (uint64_t)(npos * 3), (uint64_t)(L->kp2 / 256)};
+        const uint64_t s1[3] = {128, (uint64_t)L->kp1, 256}, s2[3] = {128, (uint64_t)L->kp2, 256};
+        const uint32_t box[4] = {128, 2, 16, 2};
+        if (!make_tmap_u8_4d(&L->tm_xq1_3, L->xq1.p, d1, s1, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_tmap_u8_4d(&L->tm_xq2_3, L->xq2.p, d2, s2, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled (4-D) failed for the limb scratch");
+    }
     L->cap = T;
     return QMOE_OK;
 }

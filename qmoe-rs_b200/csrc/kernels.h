@@ -184,6 +184,9 @@ int *device_error_flag();
 bool make_tmap_u8(CUtensorMap *tm, const void *base, uint64_t row_bytes, uint64_t rows,
                   uint32_t box_bytes, uint32_t box_rows, int swizzle);
 // Host: a 3-D uint8 tensor map (extents d0..d2, byte strides of dims 1 and 2).
+// 4-D u8 view (strides need not grow with the dimension).
+bool make_tmap_u8_4d(CUtensorMap *tm, const void *base, const uint64_t (&dims)[4],
+                     const uint64_t (&strides)[3], const uint32_t (&box)[4], int swizzle);
 bool make_tmap_u8_3d(CUtensorMap *tm, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
                      uint64_t stride1, uint64_t stride2, uint32_t b0, uint32_t b1, uint32_t b2,
                      int swizzle);

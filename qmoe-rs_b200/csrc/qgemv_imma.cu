@@ -139,16 +139,19 @@ QMOE_DEV void stage_mma(const uint8_t *stage, int grp, int wq, int g8, int t4, i
         }
     }
     // limb fragments of the chunk: 16-code groups 4 t4 + q, i.e. 16-byte
-    // chunk c of 128-byte block 2 grp + t4 / 2; limb rows g8 (tile 0) and
-    // g8 + 8 (tile 1), 128-byte swizzle
-    const uint8_t *lrow = stage + 2 * kTileBytes + g8 * 128;
+    // chunk c of 128-byte block t4 / 2 of group grp; limb rows g8 (tile 0)
+    // and g8 + 8 (tile 1).  The stage's limbs are 128-byte lines
+    // [group][row][block] with the 128-byte swizzle (chunk ^ line % 8), so a
+    // quarter-warp (rows 2i, 2i + 1 x four t4) meets four line phases
+    // 2 row + block and two chunks each: eight distinct bank groups
+    const int line = grp * 32 + g8 * 2 + (t4 >> 1);
+    const uint8_t *lrow = stage + 2 * kTileBytes + line * 128;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        const int kb = grp * 2 + (t4 >> 1);
         const int c = ((t4 & 1) << 2) | q;
-        const int off = kb * kBBlock + 16 * (c ^ g8);
+        const int off = 16 * (c ^ (line & 7));
         lo[q] = *reinterpret_cast<const uint4 *>(lrow + off);
-        if (NT == 2) hi[q] = *reinterpret_cast<const uint4 *>(lrow + 1024 + off);
+        if (NT == 2) hi[q] = *reinterpret_cast<const uint4 *>(lrow + 16 * 128 + off);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty);
@@ -280,8 +283,8 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                 }
             };
             auto issue_limbs = [&](const Item &it, int ks, uint32_t s) {
-                tma_load_3d(ring + s * kStageBytes + 2 * kTileBytes, &maps.b3, &S->smem_full[s], 0, it.pos0 * 3,
-                            4 * ks);
+                tma_load_4d(ring + s * kStageBytes + 2 * kTileBytes, &maps.b3, &S->smem_full[s], 0, 0,
+                            it.pos0 * 3, 2 * ks);
             };
             // the first kNS stages' weights go out before the wait, their limb
             // rows after it

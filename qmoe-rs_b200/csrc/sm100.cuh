@@ -111,6 +111,15 @@ QMOE_DEV void tma_load_3d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, 
         : "memory");
 }
 
+QMOE_DEV void tma_load_4d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int x, int y, int z,
+                          int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+
 // L2 policy for streams read once: their lines are the first to go, so the
 // small tensors, the code and the reused weights of the other kernels stay.
 QMOE_DEV uint64_t l2_evict_first_policy() {

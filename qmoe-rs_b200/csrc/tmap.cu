@@ -57,6 +57,20 @@ bool make_tmap_u8_3d(CUtensorMap *tm, const void *base, uint64_t d0, uint64_t d1
     return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_u8_4d(CUtensorMap *tm, const void *base, const uint64_t (&dims)[4],
+                     const uint64_t (&strides)[3], const uint32_t (&box)[4], int swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+    const cuuint64_t st[3] = {strides[0], strides[1], strides[2]};
+    const cuuint32_t b[4] = {box[0], box[1], box[2], box[3]};
+    const cuuint32_t elem[4] = {1, 1, 1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), d, st, b, elem,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, static_cast<CUtensorMapSwizzle>(swizzle),
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 bool make_tmap_bf16(CUtensorMap *tm, const void *base, uint64_t cols, uint64_t rows,
                     uint64_t row_stride, uint32_t box_cols, uint32_t box_rows, int swizzle) {
     auto fn = encode_fn();
