@@ -190,6 +190,7 @@ struct qmoe_layer {
     DevBuf x_in, io_out, user_idx, user_w;
     DevBuf xq1, meta1, xq2, meta2, router_scratch;
     DevBuf front_counter;  // hand-off counter of the decode front kernel (kept at zero)
+    DevBuf gemv_sched;     // [2 modes][2] work counters of the decode GEMVs (kept at zero)
     CUtensorMap tm_xq1, tm_xq2;
     CUtensorMap tm_xq1_3, tm_xq2_3;   // 4-D views: 16 limb rows x 512 codes per decode stage
     // prefill path: gate/up maps with 64-row boxes, bf16 activation / SwiGLU
@@ -615,6 +616,10 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
         QTRY(grow(L->front_counter, sizeof(int32_t)));
         QTRY_CUDA(cudaMemsetAsync(L->front_counter.p, 0, sizeof(int32_t), L->ctx->stream));
     }
+    if (!L->gemv_sched.p) {
+        QTRY(grow(L->gemv_sched, 4 * sizeof(int32_t)));
+        QTRY_CUDA(cudaMemsetAsync(L->gemv_sched.p, 0, 4 * sizeof(int32_t), L->ctx->stream));
+    }
     if (L->prefill_ok) {
         QTRY(grow(L->xg, 2 * (size_t)npos * H));
         QTRY(grow(L->hb, 2 * (size_t)npos * Imax));
@@ -944,6 +949,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     g0.out = L->h.as<float>();
     g0.out_ld = Imax;
     g0.err = err;
+    g0.sched = L->gemv_sched.as<int32_t>();
     QTRY_CUDA(launch_qgemv_imma(0, m0, g0, L->sm_count, st));
 
     // down: SwiGLU outputs -> limbs, then the tensor-core GEMV
@@ -984,6 +990,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     g1.out = L->y.as<float>();
     g1.out_ld = c.hidden_dim;
     g1.err = err;
+    g1.sched = L->gemv_sched.as<int32_t>() + 2;
     QTRY_CUDA(launch_qgemv_imma(1, m1, g1, L->sm_count, st));
 
     return run_combine(L, T, a, outd, dtype, accumulate);

@@ -152,6 +152,7 @@ struct DecodeParams {
     float *out;
     int64_t out_ld;
     int *err;                    // device error word
+    int *sched;                  // [2] item counter and exit count, zero between launches
 };
 cudaError_t launch_qgemv_imma(int mode, const DecodeMaps &maps, const DecodeParams &p,
                               int grid, cudaStream_t s);

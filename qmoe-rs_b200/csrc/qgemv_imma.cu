@@ -71,19 +71,33 @@ constexpr int kOutCols = 256;          // output rows per item
 constexpr int kLimbRows = 15;          // limb rows in use (5 positions x 3 limbs)
 constexpr int kTileStride = 260;       // int32 row stride of an accumulator tile (2 x 260 = 8 mod 32 banks)
 constexpr int kAccBytes = kLimbRows * kTileStride * 4;  // one group's int32 tile
-constexpr int kItemCache = 128;
+constexpr int kQueue = 16;              // published items (> kNS + 2 items in flight)
 
 struct Smem {
     uint64_t smem_full[kNS], smem_empty[kNS];
     uint64_t tile_full[2], tile_empty[2];
     int abort;
-    int4 items[kItemCache];
+    int4 queue[kQueue];                // this CTA's items in run order; x < 0: no more
 };
 
 struct Item {
     int seg, pos0, count, rb;
     bool shared;
 };
+
+QMOE_DEV int4 pack_item(const Item &it) {
+    return make_int4(it.seg, it.pos0, it.count, it.rb | (it.shared ? (1 << 30) : 0));
+}
+
+QMOE_DEV Item unpack_item(int4 v) {
+    Item it;
+    it.seg = v.x;
+    it.pos0 = v.y;
+    it.count = v.z;
+    it.rb = v.w & ((1 << 30) - 1);
+    it.shared = (v.w >> 30) & 1;
+    return it;
+}
 
 QMOE_DEV Item decode_item(const DecodeParams &p, int item, int nr, int rb_r, int rb_s) {
     Item it;
@@ -199,7 +213,6 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
     const int rb_s = p.rows_s > 0 ? (p.rows_s + rows_item - 1) / rows_item : 1;
     const int nr = p.n_groups[0], ns = p.n_groups[1];
     const int total = nr * rb_r + ns * rb_s;
-    const int my_items = total > (int)blockIdx.x ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
     if (tid == 0) {
         for (int i = 0; i < kNS; ++i) {
@@ -213,10 +226,6 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
         S->abort = 0;
         fence_mbar_init();
     }
-    for (int i = tid; i < my_items && i < kItemCache; i += kThreads) {
-        const Item it = decode_item(p, (int)blockIdx.x + i * (int)gridDim.x, nr, rb_r, rb_s);
-        S->items[i] = make_int4(it.seg, it.pos0, it.count, it.rb | (it.shared ? (1 << 30) : 0));
-    }
     __syncthreads();
     volatile int *abort = &S->abort;
     const bool producer = warp == 0 && lane == 0;
@@ -225,20 +234,12 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
         QMOE_PDL_TRIGGER();
     }
 
-    auto item_at = [&](int i) -> Item {
-        if (i < kItemCache) {
-            const int4 v = S->items[i];
-            Item it;
-            it.seg = v.x;
-            it.pos0 = v.y;
-            it.count = v.z;
-            it.rb = v.w & ((1 << 30) - 1);
-            it.shared = (v.w >> 30) & 1;
-            return it;
-        }
-        return decode_item(p, (int)blockIdx.x + i * (int)gridDim.x, nr, rb_r, rb_s);
-    };
-
+    // Work items are numbered in descending list order (the shared expert's,
+    // the costliest, first).  A CTA runs number blockIdx.x first and then the
+    // numbers the grid's counter hands out, so CTAs that finish early take
+    // more; the TMA thread publishes each item in the queue before its first
+    // stage, and after the last an end mark that rides on the next stage's
+    // full barrier (compute warps) and then on a tile barrier (epilogue).
     if (warp == 0) {
         // ------------------------------------------------------------- TMA
         // Per stage: one 3-D box per weight tile (two 64-byte chunks of 128
@@ -286,39 +287,53 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                 tma_load_4d(ring + s * kStageBytes + 2 * kTileBytes, &maps.b3, &S->smem_full[s], 0, 0,
                             it.pos0 * 3, 2 * ks);
             };
-            // the first kNS stages' weights go out before the wait, their limb
-            // rows after it
-            uint32_t npre = 0;
-            int pre_i[kNS], pre_ks[kNS];
-            for (int i = 0; npre < kNS && i < my_items; ++i) {
-                const Item it = item_at(i);
-                const int nks = ((it.shared ? p.K_s : p.K) + kStageCodes - 1) / kStageCodes;
-                for (int ks = 0; npre < kNS && ks < nks; ++ks, ++npre) {
-                    mbar_arrive_expect_tx(&S->smem_full[npre], kStageBytes);
-                    issue_weights(it, ks, npre);
-                    pre_i[npre] = i;
-                    pre_ks[npre] = ks;
-                }
-            }
-            QMOE_PDL_WAIT();
-            QMOE_PDL_TRIGGER();
-            for (uint32_t u = 0; u < npre; ++u) issue_limbs(item_at(pre_i[u]), pre_ks[u], u);
+            // the first kNS stages' weights go out before the wait on the
+            // preceding kernel, their limb rows after it
+            Item pend_it[kNS];
+            int pend_ks[kNS];
             uint32_t us = 0;
-            bool ok = true;
-            for (int i = 0; ok && i < my_items; ++i) {
-                const Item it = item_at(i);
-                const int K = it.shared ? p.K_s : p.K;
-                const int nks = (K + kStageCodes - 1) / kStageCodes;
+            bool ok = true, waited = false;
+            auto wait_then_limbs = [&]() {
+                QMOE_PDL_WAIT();
+                QMOE_PDL_TRIGGER();
+                waited = true;
+                for (uint32_t u = 0; u < us && u < kNS; ++u) issue_limbs(pend_it[u], pend_ks[u], u);
+            };
+            // the next item's number is taken once its first stage has a free
+            // slot, so a CTA holds at most the ring's stages of work ahead
+            for (int i = 0; ok; ++i) {
+                const uint32_t s0 = us % kNS;
+                if (us >= kNS) {
+                    if (!waited) wait_then_limbs();
+                    if (!(ok = mbar_wait(&S->smem_empty[s0], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
+                }
+                const int num = i == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.sched, 1);
+                if (num >= total) {
+                    S->queue[i % kQueue] = make_int4(-1, 0, 0, 0);
+                    mbar_arrive(&S->smem_full[s0]);
+                    break;
+                }
+                const Item it = decode_item(p, total - 1 - num, nr, rb_r, rb_s);
+                S->queue[i % kQueue] = pack_item(it);
+                const int nks = ((it.shared ? p.K_s : p.K) + kStageCodes - 1) / kStageCodes;
                 for (int ks = 0; ks < nks; ++ks, ++us) {
-                    if (us < npre) continue;                // issued above
                     const uint32_t s = us % kNS;
-                    if (!(ok = mbar_wait(&S->smem_empty[s], ((us / kNS) & 1) ^ 1, abort, p.err)))
-                        break;
+                    if (ks > 0 && us >= kNS) {
+                        if (!waited) wait_then_limbs();
+                        if (!(ok = mbar_wait(&S->smem_empty[s], ((us / kNS) & 1) ^ 1, abort, p.err)))
+                            break;
+                    }
                     mbar_arrive_expect_tx(&S->smem_full[s], kStageBytes);
                     issue_weights(it, ks, s);
-                    issue_limbs(it, ks, s);
+                    if (waited) {
+                        issue_limbs(it, ks, s);
+                    } else {
+                        pend_it[s] = it;
+                        pend_ks[s] = ks;
+                    }
                 }
             }
+            if (!waited) wait_then_limbs();
             if (!ok)
                 for (uint32_t u = us > kNS ? us - kNS : 0; u < us; ++u)
                     for (uint32_t n = 0; n < kMaxWaitProbes; ++n)
@@ -335,8 +350,19 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
         const int g8 = lane >> 2, t4 = lane & 3;
         uint32_t us = 0;
         bool ok = true;
-        for (int i = 0; ok && i < my_items; ++i) {
-            const Item it = item_at(i);
+        for (int i = 0; ok; ++i) {
+            // the item's first stage, or the end mark, completes the next
+            // full barrier
+            if (!(ok = mbar_wait_warp(&S->smem_full[us % kNS], (us / kNS) & 1, abort, p.err))) break;
+            const int4 qv = S->queue[i % kQueue];
+            const uint32_t tb = i & 1;
+            if (qv.x < 0) {
+                if (!(ok = mbar_wait_warp(&S->tile_empty[tb], ((i >> 1) & 1) ^ 1, abort, p.err))) break;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S->tile_full[tb]);
+                break;
+            }
+            const Item it = unpack_item(qv);
             const int K = it.shared ? p.K_s : p.K;
             const int nks = (K + kStageCodes - 1) / kStageCodes;
             // limb columns in use: 3 per position; <= 2 positions fit one n8 tile
@@ -350,7 +376,7 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             const int nsub_all = (K + 255) / 256;        // 256-code chunks holding codes < K
             for (int ks = 0; ks < nks; ++ks, ++us) {
                 const uint32_t s = us % kNS;
-                if (!(ok = mbar_wait_warp(&S->smem_full[s], (us / kNS) & 1, abort, p.err))) break;
+                if (ks > 0 && !(ok = mbar_wait_warp(&S->smem_full[s], (us / kNS) & 1, abort, p.err))) break;
                 const bool live = 2 * ks + grp < nsub_all;
                 const uint8_t *stage = ring + s * kStageBytes;
                 if (live) {
@@ -368,7 +394,6 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             // accumulators -> this group's tile [15 limb rows][256 cols]:
             // acc[b] (+ acc[4 + b], limb rows 8..15) holds rows g8 / g8 + 8 of
             // 16-row block b, limb columns 2 t4, 2 t4 + 1
-            const uint32_t tb = i & 1;
             if (!(ok = mbar_wait_warp(&S->tile_empty[tb], ((i >> 1) & 1) ^ 1, abort, p.err))) break;
             int *ct = acc_tile + (tb * 2 + grp) * (kAccBytes / 4);
 #pragma unroll
@@ -396,8 +421,12 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
         // -------------------------------------------------------- epilogue
         const int r = (warp - kEpiWarp0) * 32 + lane;   // 0..127
         bool ok = true;
-        for (int i = 0; ok && i < my_items; ++i) {
-            const Item it = item_at(i);
+        for (int i = 0; ok; ++i) {
+            const uint32_t tb = i & 1;
+            if (!(ok = mbar_wait_warp(&S->tile_full[tb], (i >> 1) & 1, abort, p.err))) break;
+            const int4 qv = S->queue[i % kQueue];
+            if (qv.x < 0) break;
+            const Item it = unpack_item(qv);
             const int rows = it.shared ? p.rows_s : p.rows;
             const float *sc0 = it.shared ? p.ss[0] : p.s[0] + (int64_t)it.seg * p.s_stride;
             const float *sc1 = MODE == 0 ? (it.shared ? p.ss[1] : p.s[1] + (int64_t)it.seg * p.s_stride)
@@ -411,8 +440,6 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             for (int c = 0; c < kTokMax; ++c)
                 mt[c] = c < it.count ? p.meta[it.pos0 + c] : make_longlong2(0, 0);
 
-            const uint32_t tb = i & 1;
-            if (!(ok = mbar_wait_warp(&S->tile_full[tb], (i >> 1) & 1, abort, p.err))) break;
             const int *ct0 = acc_tile + (tb * 2) * (kAccBytes / 4);   // group 0 + group 1
             const int *ct1 = ct0 + kAccBytes / 4;
             int v0[kLimbRows], v1[kLimbRows];
@@ -447,6 +474,12 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
         }
     }
     __syncthreads();
+    // the last CTA out resets the grid's item counter for the next launch
+    // (every CTA's last counter read precedes its exit count)
+    if (tid == 0 && atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
+        p.sched[0] = 0;
+        p.sched[1] = 0;
+    }
 }
 
 }  // namespace
