@@ -252,10 +252,15 @@ QMOE_API int qmoe_packed_forward_noalloc(int device, void *stream, const uint8_t
  * activations.  PREFILL: tcgen05 bf16 GEMM with f32 accumulation and bf16
  * SwiGLU rows, bf16 activations only (an f32 forward then fails with
  * QMOE_ERR_UNSUPPORTED); needs hidden % 128 == 0 and intermediate dims
- * % 64 == 0.  Replaces nothing in qmoe-rs, whose path is one. */
+ * % 64 == 0.  DECODE_SPLIT: the DECODE arithmetic with the activation limbs
+ * and the final combine as kernels of their own; DECODE (and AUTO) make them
+ * inside the two GEMV kernels, launched cooperatively, where the device
+ * supports cooperative launches.  Same results bit for bit.  Replaces
+ * nothing in qmoe-rs, whose path is one. */
 #define QMOE_PATH_AUTO 0
 #define QMOE_PATH_DECODE 1
 #define QMOE_PATH_PREFILL 2
+#define QMOE_PATH_DECODE_SPLIT 3
 QMOE_API int qmoe_layer_set_path(qmoe_layer *layer, int path);
 
 /* ---- expert parallelism ------------------------------------------------- */

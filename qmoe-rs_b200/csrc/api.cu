@@ -7,6 +7,7 @@
 #include <string>
 
 #include "../../include/qmoe_b200.h"
+#include "combine.cuh"
 #include "kernels.h"
 
 using namespace qmoe;
@@ -181,6 +182,8 @@ struct qmoe_layer {
     int grid0 = 0, grid1 = 0;
     // tensor-core GEMV: TMA maps over the stacked 2-bit matrices, one CTA per SM
     int sm_count = 0;
+    bool coop = false;     // cooperative launches available: the GEMVs make their own
+                           // limb rows and the down GEMV combines
     CUtensorMap tm_w[3], tm_ws[3];
     CUtensorMap tm_w3[3], tm_ws3[3];  // 3-D views: two 64-byte chunks of 128 rows per box
     int kp1 = 0, kp2 = 0;  // limb row strides: hidden dim / intermediate dims, padded to 256
@@ -190,7 +193,7 @@ struct qmoe_layer {
     DevBuf x_in, io_out, user_idx, user_w;
     DevBuf xq1, meta1, xq2, meta2, router_scratch;
     DevBuf front_counter;  // hand-off counter of the decode front kernel (kept at zero)
-    DevBuf gemv_sched;     // [2 modes][2] work counters of the decode GEMVs (kept at zero)
+    DevBuf gemv_sched;     // [2 modes][4] work counters of the decode GEMVs (kept at zero)
     CUtensorMap tm_xq1, tm_xq2;
     CUtensorMap tm_xq1_3, tm_xq2_3;   // 4-D views: 16 limb rows x 512 codes per decode stage
     // prefill path: gate/up maps with 64-row boxes, bf16 activation / SwiGLU
@@ -540,6 +543,9 @@ static int layer_create_impl(qmoe_layer *L, const float *gate_weight, const floa
         int dev = 0;
         cudaGetDevice(&dev);
         QTRY_CUDA(cudaDeviceGetAttribute(&L->sm_count, cudaDevAttrMultiProcessorCount, dev));
+        int coop = 0;
+        QTRY_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+        L->coop = coop != 0;
         const int64_t Imx = c.shared_intermediate_dim > I ? c.shared_intermediate_dim : I;
         L->kp1 = (int)((H + 255) / 256 * 256);
         L->kp2 = (int)((Imx + 255) / 256 * 256);
@@ -617,8 +623,8 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
         QTRY_CUDA(cudaMemsetAsync(L->front_counter.p, 0, sizeof(int32_t), L->ctx->stream));
     }
     if (!L->gemv_sched.p) {
-        QTRY(grow(L->gemv_sched, 4 * sizeof(int32_t)));
-        QTRY_CUDA(cudaMemsetAsync(L->gemv_sched.p, 0, 4 * sizeof(int32_t), L->ctx->stream));
+        QTRY(grow(L->gemv_sched, 8 * sizeof(int32_t)));
+        QTRY_CUDA(cudaMemsetAsync(L->gemv_sched.p, 0, 8 * sizeof(int32_t), L->ctx->stream));
     }
     if (L->prefill_ok) {
         QTRY(grow(L->xg, 2 * (size_t)npos * H));
@@ -768,8 +774,8 @@ struct ExpertsArgs {
 
 // Weighted sum of each token's expert rows in ascending expert order, plus
 // the shared expert's row (src/moe.rs:117-125, src/model.rs:386-389).
-static int run_combine(qmoe_layer *L, int64_t T, const ExpertsArgs &a, void *outd, int dtype,
-                       int accumulate) {
+static CombineParams combine_params(qmoe_layer *L, int64_t T, const ExpertsArgs &a, void *outd, int dtype,
+                                    int accumulate) {
     const qmoe_moe_config &c = L->cfg;
     CombineParams cp{};
     cp.y = L->y.as<float>();
@@ -786,6 +792,12 @@ static int run_combine(qmoe_layer *L, int64_t T, const ExpertsArgs &a, void *out
     cp.accumulate = accumulate;
     cp.out = outd;
     cp.out_dtype = dtype;
+    return cp;
+}
+
+static int run_combine(qmoe_layer *L, int64_t T, const ExpertsArgs &a, void *outd, int dtype,
+                       int accumulate) {
+    const CombineParams cp = combine_params(L, T, a, outd, dtype, accumulate);
     mark(L, 6);
     QTRY_CUDA(launch_combine(cp, L->ctx->stream));
     mark(L, 7);
@@ -916,8 +928,11 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     q1.Kp = L->kp1;
     q1.xq = L->xq1.as<int8_t>();
     q1.meta = L->meta1.as<longlong2>();
+    // cooperative GEMVs: each makes its own limb rows in a first phase (no
+    // limb kernels) and the down GEMV ends with the combine (no combine kernel)
+    const bool coop = L->coop && L->path != QMOE_PATH_DECODE_SPLIT;
     mark(L, 2);
-    QTRY_CUDA(launch_quant(q1, st));
+    if (!coop) QTRY_CUDA(launch_quant(q1, st));
     mark(L, 3);
 
     DecodeMaps m0;
@@ -950,6 +965,10 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     g0.out_ld = Imax;
     g0.err = err;
     g0.sched = L->gemv_sched.as<int32_t>();
+    if (coop) {
+        g0.quant_in = 1;
+        g0.q = q1;
+    }
     QTRY_CUDA(launch_qgemv_imma(0, m0, g0, L->sm_count, st));
 
     // down: SwiGLU outputs -> limbs, then the tensor-core GEMV
@@ -964,7 +983,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     q2.xq = L->xq2.as<int8_t>();
     q2.meta = L->meta2.as<longlong2>();
     mark(L, 4);
-    QTRY_CUDA(launch_quant(q2, st));
+    if (!coop) QTRY_CUDA(launch_quant(q2, st));
     mark(L, 5);
 
     DecodeMaps m1;
@@ -990,7 +1009,21 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     g1.out = L->y.as<float>();
     g1.out_ld = c.hidden_dim;
     g1.err = err;
-    g1.sched = L->gemv_sched.as<int32_t>() + 2;
+    g1.sched = L->gemv_sched.as<int32_t>() + 4;
+    if (coop && c.top_k <= kCombineMaxK) {
+        g1.quant_in = 1;
+        g1.q = q2;
+        g1.combine = 1;
+        g1.c = combine_params(L, T, a, outd, dtype, accumulate);
+        mark(L, 6);
+        QTRY_CUDA(launch_qgemv_imma(1, m1, g1, L->sm_count, st));
+        mark(L, 7);
+        return QMOE_OK;
+    }
+    if (coop) {
+        g1.quant_in = 1;
+        g1.q = q2;
+    }
     QTRY_CUDA(launch_qgemv_imma(1, m1, g1, L->sm_count, st));
 
     return run_combine(L, T, a, outd, dtype, accumulate);
@@ -1458,7 +1491,8 @@ int qmoe_ep_return(qmoe_ep_peer *p, const void *y) {
 
 int qmoe_layer_set_path(qmoe_layer *L, int path) {
     if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
-    if (path != QMOE_PATH_AUTO && path != QMOE_PATH_DECODE && path != QMOE_PATH_PREFILL)
+    if (path != QMOE_PATH_AUTO && path != QMOE_PATH_DECODE && path != QMOE_PATH_PREFILL &&
+        path != QMOE_PATH_DECODE_SPLIT)
         return fail(QMOE_ERR_INVALID, "unknown path %d", path);
     if (path == QMOE_PATH_PREFILL && !L->prefill_ok)
         return fail(QMOE_ERR_UNSUPPORTED,

@@ -1,128 +1,37 @@
-// combine.cu -- weighted combine of the expert outputs plus the shared expert.
-//
-// Replaces the accumulation of QMoELayer::forward (qmoe-rs src/moe.rs:121-125:
-// output_buf[t] += down_out * weight, experts visited in ascending index
-// order) and the shared-expert add of the decoder layer (src/model.rs:386-389:
-// moe_out + shared_out).  Per output element the operations and their order
-// are the reference's: acc = 0; for each of the token's experts in ascending
-// index, acc = acc + (y * w) (two roundings, no FMA); then acc + shared.
-#include "common.cuh"
-#include "kernels.h"
+// combine.cu -- the combine kernel (arithmetic and order in combine.cuh): one
+// CTA per (token, slice of kCombThreads * kCombVec float4 columns).  Warp 0
+// puts the token's live slots in ascending expert order in shared memory;
+// then every thread issues the loads of up to eight rows before their
+// in-order sum.  The cooperative down GEMV does the same work as its last
+// phase; this kernel serves the other callers.
+#include "combine.cuh"
 
 namespace qmoe {
 namespace {
 
 constexpr int kCombThreads = 256;
 constexpr int kCombVec = 4;        // float4 columns per thread
-constexpr int kMaxK = 64;
 
-// One CTA per (token, slice of kCombThreads * kCombVec float4 columns).
-// Warp 0 puts the token's live slots in ascending expert order in shared
-// memory (rank by comparison); then every thread issues the loads of up to
-// eight rows before their in-order sum.
 __global__ void __launch_bounds__(kCombThreads)
 combine_kernel(const CombineParams p) {
-    __shared__ int s_pos[kMaxK];
-    __shared__ float s_w[kMaxK];
+    __shared__ int s_pos[kCombineMaxK];
+    __shared__ float s_w[kCombineMaxK];
     __shared__ int s_n;
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int64_t t = blockIdx.x;
-    const int K = p.K, ld = p.topk_ld, tid = threadIdx.x;
-    if (tid < 32) {
-        int n_live = 0;
-        for (int j0 = 0; j0 < K; j0 += 32) {
-            const int j = j0 + tid;
-            int pos = -1, e = 0x7fffffff;
-            float w = 0.0f;
-            if (j < K) {
-                pos = p.assign_pos[t * K + j];
-                e = p.topk_idx[t * ld + j];
-                w = p.topk_w[t * ld + j];
-            }
-            const bool live = pos >= 0;
-            // rank among this token's live slots: smaller expert ids first,
-            // equal ids in slot order (the reference's stable order)
-            int r = 0;
-            for (int i0 = 0; i0 < K; i0 += 32)
-#pragma unroll
-                for (int l = 0; l < 32; ++l) {
-                    const int i = i0 + l;
-                    // slot i of the other 32-block is reloaded from memory
-                    int ei, pi;
-                    if (i0 == j0) {
-                        ei = __shfl_sync(0xffffffffu, e, l);
-                        pi = __shfl_sync(0xffffffffu, pos, l);
-                    } else {
-                        ei = i < K ? p.topk_idx[t * ld + i] : 0x7fffffff;
-                        pi = i < K ? p.assign_pos[t * K + i] : -1;
-                    }
-                    if (i < K && pi >= 0 && (ei < e || (ei == e && i < j))) ++r;
-                }
-            if (j < K && live) {
-                s_pos[r] = pos;
-                s_w[r] = w;
-            }
-            n_live += __popc(__ballot_sync(0xffffffffu, j < K && live));
-        }
-        if (tid == 0) s_n = n_live;
+    if (threadIdx.x < 32) {
+        const int n = combine_rank(p, t, threadIdx.x, s_pos, s_w);
+        if (threadIdx.x == 0) s_n = n;
     }
     __syncthreads();
     const int n = s_n;
     const int H4 = p.H >> 2;
-    const bool shared = p.y_shared && t >= p.shared_row0 && t < p.shared_row0 + p.shared_count;
 #pragma unroll
     for (int v = 0; v < kCombVec; ++v) {
-        const int c4 = (blockIdx.y * kCombVec + v) * kCombThreads + tid;
+        const int c4 = (blockIdx.y * kCombVec + v) * kCombThreads + threadIdx.x;
         if (c4 >= H4) break;
-        const int h = 4 * c4;
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-        // the shared row's load is issued with the first batch
-        float4 sv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (shared) sv = *reinterpret_cast<const float4 *>(p.y_shared + (t - p.shared_row0) * p.H + h);
-        for (int q = 0; q < n; q += 8) {
-            float4 y[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (q + u < n) y[u] = *reinterpret_cast<const float4 *>(p.y + (int64_t)s_pos[q + u] * p.H + h);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                if (q + u >= n) break;
-                const float w = s_w[q + u];
-                a0 = __fadd_rn(a0, __fmul_rn(y[u].x, w));
-                a1 = __fadd_rn(a1, __fmul_rn(y[u].y, w));
-                a2 = __fadd_rn(a2, __fmul_rn(y[u].z, w));
-                a3 = __fadd_rn(a3, __fmul_rn(y[u].w, w));
-            }
-        }
-        if (shared) {
-            a0 = __fadd_rn(a0, sv.x);
-            a1 = __fadd_rn(a1, sv.y);
-            a2 = __fadd_rn(a2, sv.z);
-            a3 = __fadd_rn(a3, sv.w);
-        }
-        const int64_t o = t * p.H + h;
-        if (p.out_dtype == 0) {
-            float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) + o);
-            if (p.accumulate) {
-                const float4 c = *dst;
-                a0 = __fadd_rn(c.x, a0); a1 = __fadd_rn(c.y, a1);
-                a2 = __fadd_rn(c.z, a2); a3 = __fadd_rn(c.w, a3);
-            }
-            *dst = make_float4(a0, a1, a2, a3);
-        } else {
-            __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.out) + o;
-            if (p.accumulate) {
-                a0 = __fadd_rn(__bfloat162float(dst[0]), a0);
-                a1 = __fadd_rn(__bfloat162float(dst[1]), a1);
-                a2 = __fadd_rn(__bfloat162float(dst[2]), a2);
-                a3 = __fadd_rn(__bfloat162float(dst[3]), a3);
-            }
-            __nv_bfloat162 lo = __floats2bfloat162_rn(a0, a1);
-            __nv_bfloat162 hi = __floats2bfloat162_rn(a2, a3);
-            *reinterpret_cast<__nv_bfloat162 *>(dst) = lo;
-            *reinterpret_cast<__nv_bfloat162 *>(dst + 2) = hi;
-        }
+        combine_float4(p, t, 4 * c4, n, s_pos, s_w);
     }
 }
 
@@ -130,7 +39,7 @@ combine_kernel(const CombineParams p) {
 
 cudaError_t launch_combine(const CombineParams &p, cudaStream_t s) {
     if (p.T == 0 || p.H == 0) return cudaSuccess;
-    if (p.K > kMaxK) return cudaErrorInvalidValue;
+    if (p.K > kCombineMaxK) return cudaErrorInvalidValue;
     const int per_cta = kCombThreads * kCombVec;
     const dim3 grid((unsigned)p.T, (unsigned)((p.H / 4 + per_cta - 1) / per_cta));
     return launch_pdl(combine_kernel, grid, dim3(kCombThreads), 0, s, p);

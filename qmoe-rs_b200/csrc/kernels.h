@@ -128,6 +128,22 @@ struct QuantParams {
 };
 cudaError_t launch_quant(const QuantParams &p, cudaStream_t s);
 
+// ---- weighted combine (combine.cu / combine.cuh) -------------------------
+struct CombineParams {
+    const float *y;              // [positions, H] expert outputs
+    const int32_t *assign_pos;   // [T, K]
+    const int32_t *topk_idx;     // [T, K] row stride topk_ld (expert order of the accumulation)
+    const float *topk_w;         // [T, K] row stride topk_ld
+    int64_t T;
+    int K, topk_ld, H;
+    const float *y_shared;       // [shared_count, H] for rows shared_row0.. or nullptr
+    int64_t shared_row0, shared_count;
+    int accumulate;              // add into out instead of overwriting
+    void *out;                   // [T, H]
+    int out_dtype;
+};
+cudaError_t launch_combine(const CombineParams &p, cudaStream_t s);
+
 // ---- decode grouped GEMV (qgemv_imma.cu): work list and operands ---------
 struct DecodeMaps {
     CUtensorMap a0, a1;          // routed matrices (mode 0: gate, up; mode 1: down, down)
@@ -152,7 +168,13 @@ struct DecodeParams {
     float *out;
     int64_t out_ld;
     int *err;                    // device error word
-    int *sched;                  // [2] item counter and exit count, zero between launches
+    int *sched;                  // [3] item counter, exit count, grid-barrier count;
+                                 // zero between launches
+    // Cooperative launch only (both 0 otherwise):
+    int quant_in;                // 1: first make the limb rows and metadata of q
+    QuantParams q;               //    (quant.cuh) in the kernel, then a grid barrier
+    int combine;                 // mode 1: after a grid barrier, the combine of c
+    CombineParams c;             //    (combine.cuh) as the last phase
 };
 cudaError_t launch_qgemv_imma(int mode, const DecodeMaps &maps, const DecodeParams &p,
                               int grid, cudaStream_t s);
@@ -257,19 +279,6 @@ cudaError_t launch_combine_rows(const void *rows, int dtype, int64_t H, const in
                                 int64_t T, const void *extra, void *out, cudaStream_t s);
 
 // ---- combine -----------------------------------------------------------
-struct CombineParams {
-    const float *y;              // [positions, H] expert outputs
-    const int32_t *assign_pos;   // [T, K]
-    const int32_t *topk_idx;     // [T, K] row stride topk_ld (expert order of the accumulation)
-    const float *topk_w;         // [T, K] row stride topk_ld
-    int64_t T;
-    int K, topk_ld, H;
-    const float *y_shared;       // [shared_count, H] for rows shared_row0.. or nullptr
-    int64_t shared_row0, shared_count;
-    int accumulate;              // add into out instead of overwriting
-    void *out;                   // [T, H]
-    int out_dtype;
-};
-cudaError_t launch_combine(const CombineParams &p, cudaStream_t s);
+
 
 }  // namespace qmoe

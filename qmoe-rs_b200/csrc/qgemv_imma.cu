@@ -45,8 +45,10 @@
 //               item.
 // Every wait is bounded; on a time-out the kernel flags the device error
 // word, lets its TMA copies drain (again bounded) and returns.
+#include "combine.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "quant.cuh"
 #include "sm100.cuh"
 
 namespace qmoe {
@@ -77,8 +79,66 @@ struct Smem {
     uint64_t smem_full[kNS], smem_empty[kNS];
     uint64_t tile_full[2], tile_empty[2];
     int abort;
+    int grid_ok;                       // the last grid barrier was passed
     int4 queue[kQueue];                // this CTA's items in run order; x < 0: no more
+    float q_red[3][4];                 // limb phase: per row group, per warp
+    long long q_sum[3][4];
+    int c_pos[kCombineMaxK];           // combine phase: the token's rows, ranked
+    float c_w[kCombineMaxK];
+    int c_n;
 };
+
+QMOE_DEV void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+QMOE_DEV int ld_acquire_gpu(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Generic-proxy global writes of this thread become visible to (and later
+// async-proxy reads, i.e. TMA, of this thread are ordered after) the fence.
+QMOE_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Bounded wait until a grid-wide barrier count reaches `target` (every CTA of
+// the cooperative launch has counted in).  On time-out: abort, error word.
+QMOE_DEV bool grid_wait(const int *ctr, int target, volatile int *abort, int *err) {
+    for (uint32_t n = 0; n < kMaxWaitProbes; ++n) {
+        if (ld_acquire_gpu(ctr) >= target) return true;
+        if (*abort) return false;
+        __nanosleep(64);
+    }
+    *abort = 1;
+    atomicOr(err, kErrWaitTimeout);
+    return false;
+}
+
+// Limb phase of a cooperative launch: warps 1..12 as three groups of four,
+// one position per group at a time (quant.cuh), then every CTA counts in on
+// the grid barrier and the twelve warps wait for all of them.
+QMOE_DEV void limb_phase(const DecodeParams &p, Smem *S, int tid, volatile int *abort) {
+    const int g = (tid - 32) >> 7, ht = (tid - 32) & 127;
+    const int kmax = p.q.K > p.q.K_s ? p.q.K : p.q.K_s;
+    const int nblk = ((kmax + 255) / 256) * 16;
+    const int bpt = (nblk + kQuantGroup - 1) / kQuantGroup;
+    auto sync = [g] { named_bar(1 + g, kQuantGroup); };
+    for (int64_t pos = (int64_t)blockIdx.x * 3 + g; pos < p.q.npos; pos += (int64_t)gridDim.x * 3) {
+        if (bpt <= 1)
+            quant_position<1>(p.q, pos, ht, S->q_red[g], S->q_sum[g], sync);
+        else if (bpt <= 2)
+            quant_position<2>(p.q, pos, ht, S->q_red[g], S->q_sum[g], sync);
+        else
+            quant_position<0>(p.q, pos, ht, S->q_red[g], S->q_sum[g], sync);
+    }
+    fence_proxy_async_global();
+    __threadfence();
+    named_bar(4, 384);
+    if (tid == 32) {
+        atomicAdd(p.sched + 2, 1);
+        S->grid_ok = grid_wait(p.sched + 2, (int)gridDim.x, abort, p.err);
+    }
+    named_bar(4, 384);
+}
 
 struct Item {
     int seg, pos0, count, rb;
@@ -233,6 +293,7 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
         QMOE_PDL_WAIT();
         QMOE_PDL_TRIGGER();
     }
+    if (p.quant_in && warp >= 1) limb_phase(p, S, tid, abort);
 
     // Work items are numbered in descending list order (the shared expert's,
     // the costliest, first).  A CTA runs number blockIdx.x first and then the
@@ -297,6 +358,14 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                 QMOE_PDL_WAIT();
                 QMOE_PDL_TRIGGER();
                 waited = true;
+                if (p.quant_in) {
+                    // the limb rows come from every CTA's limb phase
+                    if (!grid_wait(p.sched + 2, (int)gridDim.x, abort, p.err)) {
+                        ok = false;
+                        return;
+                    }
+                    fence_proxy_async_global();
+                }
                 for (uint32_t u = 0; u < us && u < kNS; ++u) issue_limbs(pend_it[u], pend_ks[u], u);
             };
             // the next item's number is taken once its first stage has a free
@@ -305,7 +374,7 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                 const uint32_t s0 = us % kNS;
                 if (us >= kNS) {
                     if (!waited) wait_then_limbs();
-                    if (!(ok = mbar_wait(&S->smem_empty[s0], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
+                    if (!ok || !(ok = mbar_wait(&S->smem_empty[s0], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
                 }
                 const int num = i == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.sched, 1);
                 if (num >= total) {
@@ -320,7 +389,7 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                     const uint32_t s = us % kNS;
                     if (ks > 0 && us >= kNS) {
                         if (!waited) wait_then_limbs();
-                        if (!(ok = mbar_wait(&S->smem_empty[s], ((us / kNS) & 1) ^ 1, abort, p.err)))
+                        if (!ok || !(ok = mbar_wait(&S->smem_empty[s], ((us / kNS) & 1) ^ 1, abort, p.err)))
                             break;
                     }
                     mbar_arrive_expect_tx(&S->smem_full[s], kStageBytes);
@@ -438,7 +507,7 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             longlong2 mt[kTokMax];
 #pragma unroll
             for (int c = 0; c < kTokMax; ++c)
-                mt[c] = c < it.count ? p.meta[it.pos0 + c] : make_longlong2(0, 0);
+                mt[c] = c < it.count ? __ldcg(p.meta + it.pos0 + c) : make_longlong2(0, 0);
 
             const int *ct0 = acc_tile + (tb * 2) * (kAccBytes / 4);   // group 0 + group 1
             const int *ct1 = ct0 + kAccBytes / 4;
@@ -474,11 +543,40 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
         }
     }
     __syncthreads();
-    // the last CTA out resets the grid's item counter for the next launch
-    // (every CTA's last counter read precedes its exit count)
+    if (MODE == 1 && p.combine) {
+        // combine phase: every CTA's y rows are stored before it counts in;
+        // tasks are (token, 1024 columns), the ranking of a task's rows done
+        // before the wait
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) atomicAdd(p.sched + 2, 1);
+        const int H4 = p.c.H >> 2;
+        const int nch = (H4 + 255) / 256;
+        const int64_t ntask = p.c.T * nch;
+        bool first = true;
+        for (int64_t task = blockIdx.x; task < ntask; task += gridDim.x) {
+            const int64_t t = task / nch;
+            const int ch = (int)(task - t * nch);
+            if (warp == 0) {
+                const int n = combine_rank(p.c, t, lane, S->c_pos, S->c_w);
+                if (lane == 0) S->c_n = n;
+                if (first && lane == 0)
+                    S->grid_ok = grid_wait(p.sched + 2, (p.quant_in ? 2 : 1) * (int)gridDim.x, abort, p.err);
+            }
+            first = false;
+            __syncthreads();
+            if (!S->grid_ok) break;
+            const int c4 = ch * 256 + tid;
+            if (tid < 256 && c4 < H4) combine_float4(p.c, t, 4 * c4, S->c_n, S->c_pos, S->c_w);
+            __syncthreads();
+        }
+    }
+    // the last CTA out resets the grid's counters for the next launch
+    // (every CTA's last counter use precedes its exit count)
     if (tid == 0 && atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
         p.sched[0] = 0;
         p.sched[1] = 0;
+        p.sched[2] = 0;
     }
 }
 
@@ -506,8 +604,9 @@ cudaError_t launch_qgemv_imma(int mode, const DecodeMaps &maps, const DecodePara
         if (e != cudaSuccess) return e;
         smem_set[mode] = smem;
     }
-    return mode == 0 ? launch_pdl(qgemv_imma_kernel<0>, dim3(grid), dim3(kThreads), smem, s, maps, p)
-                     : launch_pdl(qgemv_imma_kernel<1>, dim3(grid), dim3(kThreads), smem, s, maps, p);
+    const bool coop = p.quant_in || p.combine;
+    return mode == 0 ? launch_pdl_coop(qgemv_imma_kernel<0>, dim3(grid), dim3(kThreads), smem, s, coop, maps, p)
+                     : launch_pdl_coop(qgemv_imma_kernel<1>, dim3(grid), dim3(kThreads), smem, s, coop, maps, p);
 }
 
 }  // namespace qmoe

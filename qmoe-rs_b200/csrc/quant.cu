@@ -1,174 +1,36 @@
-// quant.cu -- activations -> per-row fixed point, as three balanced int8 limbs.
-//
-// Feeds the integer tensor-core GEMV (qgemv_imma.cu).  For every row (one
-// routed assignment or shared-expert token, in position order):
-//   e   = exponent with max|x| * 2^-e in [2^21, 2^22)  (0 for an all-zero row)
-//   Q_k = rint(x_k * 2^-e)      (scaling by a power of two is exact)
-//   Q_k = q2 * 2^16 + q1 * 2^8 + q0 with every q in [-128, 127]
-// written as xq[row][limb][Kp] (int8) and meta[row] = (e, sum_k Q_k).
-// Inside each 16-element block the bytes are stored in the order
-// 0,4,8,12, 1,5,9,13, 2,6,10,14, 3,7,11,15: the order in which the GEMV
-// unpacks a 32-bit word of 2-bit codes (bits 2j..2j+1 of its four bytes are
-// codes j, j+4, j+8, j+12), so activation k meets the weight of column k.
-// Blocks past K up to Kp are zero.
-#include "common.cuh"
-#include "kernels.h"
+// quant.cu -- the limb kernel: every position's fixed-point limbs (format and
+// arithmetic in quant.cuh), two positions per CTA.  The decode GEMVs do the
+// same work in their first phase when they are launched cooperatively; this
+// kernel serves the other callers.
+#include "quant.cuh"
 
 namespace qmoe {
 namespace {
 
-constexpr int kQuantThreads = 256;
-constexpr int kHalf = 128;                        // threads per position
-constexpr int kPosPerCta = kQuantThreads / kHalf;  // two positions per CTA: one wave
+constexpr int kQuantThreads = 2 * kQuantGroup;     // two positions per CTA: one wave
                                                    // beside a resident GEMV CTA
 
-// Limbs of one 16-element block from its Q values, in the block byte order.
-QMOE_DEV void store_block(int8_t *dst, int64_t Kp, int b, const int (&Q)[16], long long &sq) {
-    uint32_t l0[4] = {0, 0, 0, 0}, l1[4] = {0, 0, 0, 0}, l2[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const int q = Q[j];
-        sq += q;
-        const int d0 = ((q + 128) & 255) - 128;
-        const int q1 = (q - d0) >> 8;
-        const int d1 = ((q1 + 128) & 255) - 128;
-        const int d2 = (q1 - d1) >> 8;
-        const int word = j & 3, sh = (j >> 2) * 8;  // element j -> byte 4*(j%4) + j/4
-        l0[word] |= (uint32_t)(d0 & 255) << sh;
-        l1[word] |= (uint32_t)(d1 & 255) << sh;
-        l2[word] |= (uint32_t)(d2 & 255) << sh;
-    }
-    *reinterpret_cast<uint4 *>(dst + 0 * Kp + 16 * b) = make_uint4(l0[0], l0[1], l0[2], l0[3]);
-    *reinterpret_cast<uint4 *>(dst + 1 * Kp + 16 * b) = make_uint4(l1[0], l1[1], l1[2], l1[3]);
-    *reinterpret_cast<uint4 *>(dst + 2 * Kp + 16 * b) = make_uint4(l2[0], l2[1], l2[2], l2[3]);
-}
-
-// Max over the four warps of this thread's half.
-QMOE_DEV float half_max(float m, float *s_red, int half) {
-    m = warp_max(m);
-    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
-    __syncthreads();
-    m = s_red[half * 4];
-#pragma unroll
-    for (int w = 1; w < 4; ++w) m = fmaxf(m, s_red[half * 4 + w]);
-    return m;
-}
-
-QMOE_DEV int exponent_of(float m) {
-    int e = 0;
-    if (m > 0.0f) {
-        int ex;
-        frexpf(m, &ex);
-        e = max(ex - 22, -120);
-    }
-    return e;
-}
-
-QMOE_DEV void quant_block(const QuantParams &p, int64_t base, int K, int b, float sc, int8_t *dst,
-                          long long &sq) {
-    int Q[16];
-    const bool in = b * 16 < K;
-#pragma unroll
-    for (int j4 = 0; j4 < 4; ++j4) {
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (in) v = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
-        Q[4 * j4 + 0] = __float2int_rn(v.x * sc);
-        Q[4 * j4 + 1] = __float2int_rn(v.y * sc);
-        Q[4 * j4 + 2] = __float2int_rn(v.z * sc);
-        Q[4 * j4 + 3] = __float2int_rn(v.w * sc);
-    }
-    store_block(dst, p.Kp, b, Q, sq);
-}
-
-// Two positions per CTA, one per half of 128 threads.  BPT > 0: the row is
-// read once, each thread holding BPT 16-element blocks in registers (rows up
-// to 2048 * BPT); BPT == 0: any length, the row is read twice (max, limbs).
 template <int BPT>
 __global__ void __launch_bounds__(kQuantThreads)
 quant_kernel(const QuantParams p) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
-    const int half = threadIdx.x / kHalf, ht = threadIdx.x % kHalf;
-    const int64_t pos = (int64_t)blockIdx.x * kPosPerCta + half;
-    const bool routed = pos < p.shared_base;
-    // unused routed slots and the padding position are skipped
-    const bool active = pos < p.npos && !(routed && p.n_valid && pos >= *p.n_valid);
-    int64_t row = pos;
-    if (active && p.pos_tok) row = routed ? (int64_t)p.pos_tok[pos] : p.shared_row0 + pos - p.shared_base;
-    const int64_t base = row * p.act_ld;
-    const int K = routed ? p.K : p.K_s;
-    const int nblk = ((K + 255) / 256) * 16;  // blocks the GEMV reads (K padded to 256)
-    __shared__ float s_red[kQuantThreads / 32];
-    __shared__ long long s_sum[kQuantThreads / 32];
-    int8_t *dst = p.xq + pos * 3 * (int64_t)p.Kp;
-    long long sq = 0;
-    int e;
-
-    if (BPT > 0) {
-        float4 v[BPT > 0 ? BPT : 1][4];
-        float m = 0.0f;
-#pragma unroll
-        for (int i = 0; i < BPT; ++i) {
-            const int b = ht + i * kHalf;
-#pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-                v[i][j4] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (active && b * 16 < K) v[i][j4] = load_act4(p.act, p.dtype, base + b * 16 + 4 * j4);
-                m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i][j4].x), fabsf(v[i][j4].y)),
-                                   fmaxf(fabsf(v[i][j4].z), fabsf(v[i][j4].w))));
-            }
-        }
-        e = exponent_of(half_max(m, s_red, half));
-        const float sc = pow2i(-e);
-#pragma unroll
-        for (int i = 0; i < BPT; ++i) {
-            const int b = ht + i * kHalf;
-            if (!active || b >= nblk) continue;
-            int Q[16];
-#pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-                Q[4 * j4 + 0] = __float2int_rn(v[i][j4].x * sc);
-                Q[4 * j4 + 1] = __float2int_rn(v[i][j4].y * sc);
-                Q[4 * j4 + 2] = __float2int_rn(v[i][j4].z * sc);
-                Q[4 * j4 + 3] = __float2int_rn(v[i][j4].w * sc);
-            }
-            store_block(dst, p.Kp, b, Q, sq);
-        }
-    } else {
-        float m = 0.0f;
-        if (active)
-            for (int q = ht; q < (K >> 2); q += kHalf) {
-                const float4 v = load_act4(p.act, p.dtype, base + 4 * q);
-                m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-            }
-        e = exponent_of(half_max(m, s_red, half));
-        const float sc = pow2i(-e);
-        if (active)
-            for (int b = ht; b < nblk; b += kHalf) quant_block(p, base, K, b, sc, dst, sq);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = sq;
-    __syncthreads();
-    if (ht == 0 && active) {
-        long long t = 0;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) t += s_sum[half * 4 + w];
-        p.meta[pos] = make_longlong2(e, t);
-    }
+    __shared__ float s_red[8];
+    __shared__ long long s_sum[8];
+    const int half = threadIdx.x / kQuantGroup, ht = threadIdx.x % kQuantGroup;
+    const int64_t pos = (int64_t)blockIdx.x * 2 + half;
+    quant_position<BPT>(p, pos, ht, s_red + 4 * half, s_sum + 4 * half, [] { __syncthreads(); });
 }
 
 }  // namespace
 
 cudaError_t launch_quant(const QuantParams &p, cudaStream_t s) {
     if (p.npos == 0) return cudaSuccess;
-    const int kmax = p.K > p.K_s ? p.K : p.K_s;
-    const int nblk = ((kmax + 255) / 256) * 16;
-    const int bpt = (nblk + kHalf - 1) / kHalf;
-    const dim3 grid((unsigned)((p.npos + kPosPerCta - 1) / kPosPerCta)), block(kQuantThreads);
-    if (bpt <= 1) return launch_pdl(quant_kernel<1>, grid, block, 0, s, p);
-    if (bpt <= 2) return launch_pdl(quant_kernel<2>, grid, block, 0, s, p);
-    if (bpt <= 4) return launch_pdl(quant_kernel<4>, grid, block, 0, s, p);
+    const int bpt = quant_bpt(p.K > p.K_s ? p.K : p.K_s);
+    const dim3 grid((unsigned)((p.npos + 1) / 2)), block(kQuantThreads);
+    if (bpt == 1) return launch_pdl(quant_kernel<1>, grid, block, 0, s, p);
+    if (bpt == 2) return launch_pdl(quant_kernel<2>, grid, block, 0, s, p);
+    if (bpt == 4) return launch_pdl(quant_kernel<4>, grid, block, 0, s, p);
     return launch_pdl(quant_kernel<0>, grid, block, 0, s, p);
 }
 

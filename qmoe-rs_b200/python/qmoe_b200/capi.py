@@ -28,6 +28,7 @@ QMOE_SCORING_SIGMOID = 1
 QMOE_PATH_AUTO = 0
 QMOE_PATH_DECODE = 1
 QMOE_PATH_PREFILL = 2
+QMOE_PATH_DECODE_SPLIT = 3
 QMOE_NOALLOC_MAX_BATCH = 16384
 QMOE_NOALLOC_MAX_IN_FEATURES = 8192
 QMOE_EP_HANDLE_BYTES = 64

@@ -365,7 +365,7 @@ class QMoELayer:
         capi.call("qmoe_layer_reserve", self._h, int(max_tokens))
 
     def set_path(self, path: int) -> None:
-        """Expert-product kernels: capi.QMOE_PATH_AUTO / _DECODE / _PREFILL."""
+        """Expert-product kernels: capi.QMOE_PATH_AUTO / _DECODE / _PREFILL / _DECODE_SPLIT."""
         capi.call("qmoe_layer_set_path", self._h, int(path))
 
     def set_profiling(self, enable: bool) -> None:

@@ -351,3 +351,31 @@ def test_fused_front_matches_separate_router(E, k, H, T, scoring):
     ro, ri, rw = oracle_layer(cfg, gw, np_exp, np_sh, x.numpy())
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
     assert rel_err(out.cpu().numpy(), ro) <= F32_TOL
+
+
+@pytest.mark.parametrize("E,k,H,I,Is,T,dtype", [
+    (64, 6, 2048, 1408, 2816, 32, torch.float32),   # the decode benchmark's layer
+    (64, 6, 2048, 1408, 2816, 5, torch.bfloat16),
+    (16, 4, 512, 256, 0, 300, torch.float32),       # no shared expert; router + permute kernels
+    (32, 8, 768, 320, 448, 64, torch.float32),      # rows not multiples of 256
+])
+def test_cooperative_and_split_decode_agree(E, k, H, I, Is, T, dtype):
+    """The decode path makes its activation limbs and the final combine inside
+    the two GEMV kernels (cooperative launches); DECODE_SPLIT runs them as
+    separate kernels.  Same bits, and the oracle's result within tolerance."""
+    cfg = MoEConfig(E, k, H, I, shared_intermediate_dim=Is)
+    layer, np_exp, np_sh, gw = build(cfg, seed=E + T)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(T)).to(dtype)
+    xd = x.cuda()
+    layer.set_path(capi.QMOE_PATH_DECODE)
+    a = layer.forward(xd)
+    b = layer.forward(xd)
+    layer.set_path(capi.QMOE_PATH_DECODE_SPLIT)
+    c = layer.forward(xd)
+    layer.set_path(capi.QMOE_PATH_AUTO)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b), "repeated cooperative forwards differ"
+    assert torch.equal(a, c), "cooperative and split decode forwards differ"
+    ro, _, _ = oracle_layer(cfg, gw, np_exp, np_sh, x.float().numpy())
+    tol = 2e-2 if dtype == torch.bfloat16 else F32_TOL
+    assert rel_err(a.float().cpu().numpy(), ro) <= tol
