@@ -271,7 +271,10 @@ QMOE_DEV void plan_tail(const FrontParams &f, int T, int K, const int *sel, cons
 }
 
 // One cluster of gridDim.x CTAs; CTA r owns hidden chunks [r*lc, r*lc + lc)
-// and tokens r, r + cs, ... (one per warp).
+// and tokens r, r + cs, ... (one per warp).  N: experts per lane of the
+// selection (E <= 32 N), one instantiation per size so that each holds one
+// selection's code.
+template <int N>
 __global__ void __launch_bounds__(kFrontThreads, 1)
 front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
     extern __shared__ float4 front_smem4[];
@@ -389,14 +392,7 @@ front_cluster_kernel(const RouterParams p, const FrontParams f, int lc) {
         __syncwarp();
         const uint32_t sel0 = dsmem_map((uint32_t)__cvta_generic_to_shared(sm + L.sel), 0u);
         const uint32_t selw0 = dsmem_map((uint32_t)__cvta_generic_to_shared(sm + L.selw), 0u);
-        if (E <= 32)
-            select_token<1>(p, t, lane, lg, ex, gs, gk, sel0, selw0, true);
-        else if (E <= 64)
-            select_token<2>(p, t, lane, lg, ex, gs, gk, sel0, selw0, true);
-        else if (E <= 128)
-            select_token<4>(p, t, lane, lg, ex, gs, gk, sel0, selw0, true);
-        else
-            select_token<8>(p, t, lane, lg, ex, gs, gk, sel0, selw0, true);
+        select_token<N>(p, t, lane, lg, ex, gs, gk, sel0, selw0, true);
     }
     cluster_sync_all();  // every selection in CTA 0
     if (rank != 0) return;
@@ -433,9 +429,10 @@ static bool front_shape(int64_t T, int H, int E, int K, int max_cs, int *cs, int
     return true;
 }
 
-static cudaError_t launch_front_impl(const RouterParams &p, const FrontParams &f, int cs, int lc, size_t smem,
-                                   cudaStream_t s) {
-    auto kern = front_cluster_kernel;
+template <int N>
+static cudaError_t launch_front_n(const RouterParams &p, const FrontParams &f, int cs, int lc, size_t smem,
+                                  cudaStream_t s) {
+    auto kern = front_cluster_kernel<N>;
     static size_t smem_set = 0;
     static bool np_set = false;
     if (smem > smem_set) {
@@ -469,7 +466,7 @@ static cudaError_t launch_front_impl(const RouterParams &p, const FrontParams &f
 // kernel configuration; 0 if none.
 static int front_max_cluster(size_t smem) {
     for (int cs : {16, 8}) {
-        auto kern = front_cluster_kernel;
+        auto kern = front_cluster_kernel<8>;
         if (cs > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
             cudaGetLastError();
             continue;
@@ -516,7 +513,10 @@ cudaError_t launch_front_cluster(const RouterParams &p, const FrontParams &f, cu
     size_t smem;
     if (mc <= 0 || !front_shape(p.T, p.H, p.E, p.K, mc, &cs, &lc, &smem))
         return cudaErrorInvalidConfiguration;
-    return launch_front_impl(p, f, cs, lc, smem, s);
+    if (p.E <= 32) return launch_front_n<1>(p, f, cs, lc, smem, s);
+    if (p.E <= 64) return launch_front_n<2>(p, f, cs, lc, smem, s);
+    if (p.E <= 128) return launch_front_n<4>(p, f, cs, lc, smem, s);
+    return launch_front_n<8>(p, f, cs, lc, smem, s);
 }
 
 }  // namespace qmoe
