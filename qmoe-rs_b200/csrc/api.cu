@@ -1015,8 +1015,8 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
         g1.q = q2;
         g1.combine = 1;
         g1.c = combine_params(L, T, a, outd, dtype, accumulate);
-        mark(L, 6);
         QTRY_CUDA(launch_qgemv_imma(1, m1, g1, L->sm_count, st));
+        mark(L, 6);          // down GEMV with its limb and combine phases
         mark(L, 7);
         return QMOE_OK;
     }
