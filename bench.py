@@ -43,12 +43,14 @@ WORKLOAD = dict(
     name="configs[1]: DeepSeek-V2-Lite MoE layer, decode, 32 f32 tokens/GPU",
     E=64, k=6, H=2048, I=1408, Is=2816, T=32, norm_topk=True)
 REPLICAS = 4
-KERNELS_PER_FORWARD = 6  # front cluster (logits, selection, permute), limbs x2, gate/up, down, combine
+KERNELS_PER_FORWARD = 3  # front cluster (logits, selection, permute); gate/up GEMV (x limbs
+                         # first); down GEMV (h limbs first, weighted combine last)
 KERNELS_PER_PREFILL = 7  # router logits + select, permute, bf16 gather, gate/up, down, combine
 # EP rank (peer-memory exchange): front cluster (route + send list), dispatch,
-# wait, expert pass over the received rows + own tokens (permute, limbs x2,
-# GEMV x2, combine), return, wait, combine_rows
-KERNELS_PER_EP_FORWARD = 12
+# wait, expert pass over the received rows + own tokens (permute, gate/up
+# GEMV, down GEMV whose last phase returns the partial sums to their ranks),
+# finish (wait for the returns + combine)
+KERNELS_PER_EP_FORWARD = 7
 
 
 def parse():

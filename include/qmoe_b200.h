@@ -363,6 +363,18 @@ QMOE_API int qmoe_ep_dispatch(qmoe_ep_peer *p, const void *x, int64_t T, const i
                               const int32_t *send_tok, const int32_t *send_meta);
 QMOE_API int qmoe_ep_wait(qmoe_ep_peer *p, int phase);
 QMOE_API int qmoe_ep_return(qmoe_ep_peer *p, const void *y);
+/* qmoe_layer_forward_ep on this rank's receive rows (R = world*C + own tokens,
+ * shared_row0 = world*C) followed by qmoe_ep_return, with the return folded
+ * into the expert pass where it can be: the decode path's last phase stores
+ * each received row's partial sum straight into its origin rank's return
+ * block, one arrival per (row, 1024 columns); rows past world*C (this rank's
+ * shared-expert rows) go to y.  Other paths run the return kernel. */
+QMOE_API int qmoe_layer_forward_ep_return(qmoe_layer *layer, qmoe_ep_peer *p, const void *x, int dtype,
+                                          int64_t R, const int32_t *meta, int64_t shared_row0, void *y);
+/* qmoe_ep_wait(1) and qmoe_combine_rows over the return block in one launch:
+ * out[t] = sum over ranks s ascending of the returned row slot_pos[t][s]
+ * (-1: none) + extra[t] (nullable), T <= capacity, device pointers. */
+QMOE_API int qmoe_ep_finish(qmoe_ep_peer *p, const int32_t *slot_pos, int64_t T, const void *extra, void *out);
 
 /* ---- tracing ----------------------------------------------------------- */
 

@@ -770,6 +770,9 @@ struct ExpertsArgs {
     int e_begin = 0;
     int64_t shared_row0 = 0, shared_count = 0;
     bool permuted = false;  // segments and work list already built (run_front)
+    EpPeerDev *ep_ret = nullptr;  // expert parallel: the down GEMV returns the received
+                                  // rows' partial sums straight to their origin ranks
+    bool *returned = nullptr;     // set when it did (else the caller runs the return kernel)
 };
 
 // Weighted sum of each token's expert rows in ascending expert order, plus
@@ -1015,6 +1018,13 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
         g1.q = q2;
         g1.combine = 1;
         g1.c = combine_params(L, T, a, outd, dtype, accumulate);
+        if (a.ep_ret) {
+            // one arrival per combine task: (row, 1024 columns)
+            a.ep_ret->ret_units = (int)((c.hidden_dim / 4 + 255) / 256);
+            g1.ep_ret = 1;
+            g1.ret = *a.ep_ret;
+            *a.returned = true;
+        }
         QTRY_CUDA(launch_qgemv_imma(1, m1, g1, L->sm_count, st));
         mark(L, 6);          // down GEMV with its limb and combine phases
         mark(L, 7);
@@ -1407,6 +1417,8 @@ int qmoe_ep_peer_create(qmoe_ctx *ctx, int world, int rank, int64_t capacity, in
     }
     d.base[rank] = p->mem;
     d.seq = reinterpret_cast<int *>(p->mem + off_local);
+    d.done = d.seq + 1;
+    d.ret_units = 1;
     d.err = error_flag();
     *out = p;
     return QMOE_OK;
@@ -1486,6 +1498,51 @@ int qmoe_ep_return(qmoe_ep_peer *p, const void *y) {
     QTRY(check_align(y, QMOE_PTR_DEVICE, "y"));
     DeviceGuard g(p->ctx->device);
     QTRY_CUDA(launch_ep_return(p->d, y, p->ctx->stream));
+    return QMOE_OK;
+}
+
+int qmoe_layer_forward_ep_return(qmoe_layer *L, qmoe_ep_peer *p, const void *x, int dtype, int64_t R,
+                                 const int32_t *meta, int64_t shared_row0, void *y) {
+    if (!L || !p) return fail(QMOE_ERR_INVALID, "NULL layer or exchange");
+    QTRY(check_dtype(dtype));
+    QTRY(ep_ready(p));
+    const int64_t GC = (int64_t)p->d.world * p->d.C;
+    if (R < GC || shared_row0 != GC || R > GC + p->d.C)
+        return fail(QMOE_ERR_INVALID, "rows R %lld / shared_row0 %lld do not match the exchange (%lld received)",
+                    (long long)R, (long long)shared_row0, (long long)GC);
+    if ((int64_t)dtype_size(dtype) != p->d.esize || p->d.H != L->cfg.hidden_dim || p->d.K != L->cfg.top_k)
+        return fail(QMOE_ERR_INVALID, "exchange dtype / hidden / top_k differ from the layer's");
+    if (!x || !meta || !y) return fail(QMOE_ERR_INVALID, "NULL argument");
+    QTRY(check_align(x, QMOE_PTR_DEVICE, "x"));
+    QTRY(check_align(y, QMOE_PTR_DEVICE, "y"));
+    DeviceGuard g(L->ctx->device);
+    QTRY(layer_reserve(L, R));
+    const int K = L->cfg.top_k;
+    ExpertsArgs a;
+    a.topk_idx = meta;
+    a.topk_w = reinterpret_cast<const float *>(meta + K);
+    a.topk_ld = 2 * K;
+    a.shared_row0 = shared_row0;
+    a.shared_count = L->has_shared ? R - shared_row0 : 0;
+    bool returned = false;
+    p->d.ret_units = 1;
+    a.ep_ret = &p->d;
+    a.returned = &returned;
+    QTRY(run_experts(L, x, dtype, R, a, y, 0));
+    if (!returned) QTRY_CUDA(launch_ep_return(p->d, y, p->ctx->stream));
+    return QMOE_OK;
+}
+
+int qmoe_ep_finish(qmoe_ep_peer *p, const int32_t *slot_pos, int64_t T, const void *extra, void *out) {
+    if (!p || (T > 0 && (!slot_pos || !out))) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (T < 0 || T > p->d.C) return fail(QMOE_ERR_INVALID, "T %lld outside 0 .. capacity %lld",
+                                         (long long)T, (long long)p->d.C);
+    QTRY(ep_ready(p));
+    if (T == 0) return qmoe_ep_wait(p, 1);
+    QTRY(check_align(out, QMOE_PTR_DEVICE, "out"));
+    if (extra) QTRY(check_align(extra, QMOE_PTR_DEVICE, "extra"));
+    DeviceGuard g(p->ctx->device);
+    QTRY_CUDA(launch_ep_finish(p->d, slot_pos, T, extra, out, p->ctx->stream));
     return QMOE_OK;
 }
 

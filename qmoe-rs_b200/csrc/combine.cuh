@@ -60,9 +60,10 @@ QMOE_DEV int combine_rank(const CombineParams &p, int64_t t, int lane, int *s_po
     return n_live;
 }
 
-// Output columns h .. h + 3 of token t from its n ranked rows.
+// Output columns h .. h + 3 of token t from its n ranked rows, into the row
+// at orow (p.out_dtype; nullptr: row t of p.out).
 QMOE_DEV void combine_float4(const CombineParams &p, int64_t t, int h, int n, const int *s_pos,
-                             const float *s_w) {
+                             const float *s_w, void *orow = nullptr) {
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
     const bool shared = p.y_shared && t >= p.shared_row0 && t < p.shared_row0 + p.shared_count;
     // the shared row's load is issued with the first batch
@@ -89,9 +90,10 @@ QMOE_DEV void combine_float4(const CombineParams &p, int64_t t, int h, int n, co
         a2 = __fadd_rn(a2, sv.z);
         a3 = __fadd_rn(a3, sv.w);
     }
-    const int64_t o = t * p.H + h;
+    const int64_t o = orow ? h : t * p.H + h;
+    void *ob = orow ? orow : p.out;
     if (p.out_dtype == 0) {
-        float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) + o);
+        float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(ob) + o);
         if (p.accumulate) {
             const float4 c = *dst;
             a0 = __fadd_rn(c.x, a0);
@@ -101,7 +103,7 @@ QMOE_DEV void combine_float4(const CombineParams &p, int64_t t, int h, int n, co
         }
         *dst = make_float4(a0, a1, a2, a3);
     } else {
-        __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.out) + o;
+        __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(ob) + o;
         if (p.accumulate) {
             a0 = __fadd_rn(__bfloat162float(dst[0]), a0);
             a1 = __fadd_rn(__bfloat162float(dst[1]), a1);

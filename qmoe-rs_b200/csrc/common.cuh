@@ -39,6 +39,15 @@ QMOE_DEV float4 load_act4(const void *base, int dtype, int64_t idx) {
                        __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
 }
 
+// load_act4 through L2 only, for rows other CTAs or other GPUs wrote after
+// this kernel started (the read-only path of __ldg is not coherent with them).
+QMOE_DEV float4 load_act4_cg(const void *base, int dtype, int64_t idx) {
+    if (dtype == 0) return __ldcg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(base) + idx));
+    const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(reinterpret_cast<const __nv_bfloat16 *>(base) + idx));
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+
 QMOE_DEV void store_act4(void *base, int dtype, int64_t idx, float4 v) {
     if (dtype == 0) {
         *reinterpret_cast<float4 *>(reinterpret_cast<float *>(base) + idx) = v;

@@ -111,7 +111,7 @@ ep_wait_kernel(const EpPeerDev d, int phase) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int s = *d.seq + 1;
-    const int want = (int)(s * d.C);
+    const int want = (int)(s * d.C * (phase == 1 ? d.ret_units : 1));
     bool ok = true;
     for (int p = threadIdx.x; p < d.world; p += 32) {
         if (p == d.rank) continue;
@@ -130,7 +130,75 @@ ep_wait_kernel(const EpPeerDev d, int phase) {
     if (phase == 1 && threadIdx.x == 0) *d.seq = s;
 }
 
+// CTA (token t, slice of 256 x 4 columns): lanes of warp 0 wait for every
+// peer's returned rows of this forward (bounded), then the combine_rows sum
+// (ep.cu) of t's returned partials and its shared row, read through L2.
+__global__ void __launch_bounds__(256)
+ep_finish_kernel(const EpPeerDev d, const int32_t *slot_pos, int64_t T, const void *extra, void *out) {
+    __shared__ int s_ok;
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int seq = *d.seq + 1;
+    if (threadIdx.x < 32) {
+        const int want = (int)(seq * d.C * d.ret_units);
+        bool ok = true;
+        for (int p = threadIdx.x; p < d.world; p += 32) {
+            if (p == d.rank) continue;
+            const int *f = flag_at(d, d.rank, 1, p);
+            uint32_t n = 0;
+            while (ld_acquire_sys(f) < want) {
+                if (++n >= kMaxWaitProbes) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        ok = __all_sync(0xffffffffu, ok);
+        if (threadIdx.x == 0) {
+            if (!ok) atomicOr(d.err, kErrWaitTimeout);
+            s_ok = ok;
+        }
+    }
+    __syncthreads();
+    const int dtype = d.esize == 2 ? 1 : 0;
+    const int64_t t = blockIdx.x, h = ((int64_t)blockIdx.y * 256 + threadIdx.x) * 4;
+    if (s_ok && h < d.H) {
+        const uint8_t *rows = d.base[d.rank] + d.off_back;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < d.world; ++r) {
+            const int pos = slot_pos[t * d.world + r];
+            if (pos < 0) continue;
+            const float4 v = load_act4_cg(rows, dtype, (int64_t)pos * d.H + h);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        if (extra) {
+            const float4 v = load_act4_cg(extra, dtype, t * d.H + h);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        store_act4(out, dtype, t * d.H + h, acc);
+    }
+    // the last CTA out ends the forward (every CTA read seq above)
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(d.done, 1) == (int)(gridDim.x * gridDim.y) - 1) {
+        *d.done = 0;
+        *d.seq = seq;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_ep_finish(const EpPeerDev &d, const int32_t *slot_pos, int64_t T, const void *extra,
+                             void *out, cudaStream_t s) {
+    const dim3 grid((unsigned)T, (unsigned)((d.H / 4 + 255) / 256));
+    return launch_pdl(ep_finish_kernel, grid, dim3(256), 0, s, d, slot_pos, T, extra, out);
+}
 
 cudaError_t launch_ep_dispatch(const EpPeerDev &d, const void *x, int64_t T, const int32_t *send_counts,
                                const int32_t *send_tok, const int32_t *send_meta, cudaStream_t s) {

@@ -144,6 +144,23 @@ struct CombineParams {
 };
 cudaError_t launch_combine(const CombineParams &p, cudaStream_t s);
 
+// ---- expert-parallel exchange over peer memory (ep_p2p.cu) ---------------
+// Every rank's allocation has the same layout: receive rows [G*C + C][H]
+// (dtype), receive metadata [G*C + C][2K] int32, returned rows [G*C][H],
+// arrival counters [2][G] int32; offsets below.  base[r] = rank r's allocation as this
+// GPU addresses it (its own included).
+constexpr int kEpMaxWorld = 32;
+struct EpPeerDev {
+    uint8_t *base[kEpMaxWorld];
+    int world, rank, K;
+    int64_t C, H, esize;
+    int64_t off_rows, off_meta, off_back, off_flags;
+    int *seq;                    // this rank's per-forward sequence number
+    int *done;                   // exit count of the return-side kernel (zero between launches)
+    int ret_units;               // arrivals per returned row (1, or the combine tasks per row)
+    int *err;                    // device error word
+};
+
 // ---- decode grouped GEMV (qgemv_imma.cu): work list and operands ---------
 struct DecodeMaps {
     CUtensorMap a0, a1;          // routed matrices (mode 0: gate, up; mode 1: down, down)
@@ -175,29 +192,24 @@ struct DecodeParams {
     QuantParams q;               //    (quant.cuh) in the kernel, then a grid barrier
     int combine;                 // mode 1: after a grid barrier, the combine of c
     CombineParams c;             //    (combine.cuh) as the last phase
+    int ep_ret;                  // with combine: rows r < ret.world * ret.C go straight to
+    EpPeerDev ret;               //    rank r / C's return block (peer memory), counted per task
 };
 cudaError_t launch_qgemv_imma(int mode, const DecodeMaps &maps, const DecodeParams &p,
                               int grid, cudaStream_t s);
 size_t qgemv_imma_smem_bytes(int kp_b, int b_buffers);
 int qgemv_imma_buffers(int kp_b);
-// ---- expert-parallel exchange over peer memory (ep_p2p.cu) ---------------
-// Every rank's allocation has the same layout: receive rows [G*C + C][H]
-// (dtype), receive metadata [G*C + C][2K] int32, returned rows [G*C][H],
-// arrival counters [2][G] int32; offsets below.  base[r] = rank r's allocation as this
-// GPU addresses it (its own included).
-constexpr int kEpMaxWorld = 32;
-struct EpPeerDev {
-    uint8_t *base[kEpMaxWorld];
-    int world, rank, K;
-    int64_t C, H, esize;
-    int64_t off_rows, off_meta, off_back, off_flags;
-    int *seq;                    // this rank's per-forward sequence number
-    int *err;                    // device error word
-};
+
 cudaError_t launch_ep_dispatch(const EpPeerDev &d, const void *x, int64_t T, const int32_t *send_counts,
                                const int32_t *send_tok, const int32_t *send_meta, cudaStream_t s);
 cudaError_t launch_ep_return(const EpPeerDev &d, const void *y, cudaStream_t s);
 cudaError_t launch_ep_wait(const EpPeerDev &d, int phase, cudaStream_t s);
+// Return side of a forward in one launch: wait (bounded) for every peer's
+// returned rows, then out[t] = sum over ranks s ascending of back[slot_pos[t][s]]
+// (skipping -1) + extra[t] (the combine_rows arithmetic); the last CTA out
+// advances the sequence number.
+cudaError_t launch_ep_finish(const EpPeerDev &d, const int32_t *slot_pos, int64_t T, const void *extra,
+                             void *out, cudaStream_t s);
 
 // Device-side error word (device_state.cu) raised by a bounded wait that gives up.
 int *device_error_flag();

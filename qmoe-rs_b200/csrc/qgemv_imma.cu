@@ -566,9 +566,23 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             first = false;
             __syncthreads();
             if (!S->grid_ok) break;
+            // expert parallel: a received row's partial sum goes straight to
+            // its origin rank's return block, one arrival per task
+            void *orow = nullptr;
+            int dst = -1;
+            if (p.ep_ret && t < (int64_t)p.ret.world * p.ret.C) {
+                dst = (int)(t / p.ret.C);
+                const int64_t i = t - (int64_t)dst * p.ret.C;
+                orow = p.ret.base[dst] + p.ret.off_back + ((int64_t)p.ret.rank * p.ret.C + i) * p.ret.H * p.ret.esize;
+            }
             const int c4 = ch * 256 + tid;
-            if (tid < 256 && c4 < H4) combine_float4(p.c, t, 4 * c4, S->c_n, S->c_pos, S->c_w);
+            if (tid < 256 && c4 < H4) combine_float4(p.c, t, 4 * c4, S->c_n, S->c_pos, S->c_w, orow);
             __syncthreads();
+            if (tid == 0 && dst >= 0 && dst != p.ret.rank) {
+                __threadfence_system();
+                atomicAdd_system(reinterpret_cast<int *>(p.ret.base[dst] + p.ret.off_flags) + p.ret.world + p.ret.rank,
+                                 1);
+            }
         }
     }
     // the last CTA out resets the grid's counters for the next launch

@@ -101,6 +101,8 @@ SIGNATURES = {
     "qmoe_combine_rows": (_I, [_P, _P, _I, _I64, _P, _I, _I64, _P, _P]),
     "qmoe_layer_forward_ep": (_I, [_P, _P, _I, _I64, _P, _I64, _P]),
     "qmoe_layer_route_plan": (_I, [_P, _P, _I, _I64, _P, _P, _I, _I, _I64, _P, _P, _P, _P]),
+    "qmoe_layer_forward_ep_return": (_I, [_P, _P, _P, _I, _I64, _P, _I64, _P]),
+    "qmoe_ep_finish": (_I, [_P, _P, _I64, _P, _P]),
     "qmoe_ep_peer_create": (_I, [_P, _I, _I, _I64, _I64, _I, _I, _PP]),
     "qmoe_ep_peer_destroy": (_I, [_P]),
     "qmoe_ep_peer_handle": (_I, [_P, _P]),

@@ -95,6 +95,12 @@ class PeerExchange:
     def give_back(self, y):
         capi.call("qmoe_ep_return", self._h, ctypes.c_void_p(y.data_ptr()))
 
+    def finish(self, slot, T: int, extra, out):
+        """Wait for every peer's returned rows, then out[t] = the sum of t's
+        returned partials in rank order + extra[t] (one launch)."""
+        capi.call("qmoe_ep_finish", self._h, slot.data_ptr(), T,
+                  extra.data_ptr() if extra is not None else None, out.data_ptr())
+
     def close(self):
         if getattr(self, "_h", None):
             capi.lib().qmoe_ep_peer_destroy(self._h)
@@ -279,15 +285,14 @@ class ExpertParallelMoE:
         self.peer.wait(0)
         y = self._buf(("y", x.dtype), lambda: torch.empty(GC + C, H, dtype=x.dtype, device=x.device))
         R = GC + T if self.has_shared else GC
-        capi.call("qmoe_layer_forward_ep", self.layer._h, ctypes.c_void_p(self.peer.recv_rows), _dt(x), R,
-                  ctypes.c_void_p(self.peer.recv_meta), GC, y.data_ptr())
-        self.peer.give_back(y)
-        self.peer.wait(1)
+        # the expert pass stores the received rows' partial sums straight into
+        # their origin ranks' return blocks (or runs the return kernel)
+        capi.call("qmoe_layer_forward_ep_return", self.layer._h, self.peer._h,
+                  ctypes.c_void_p(self.peer.recv_rows), _dt(x), R, ctypes.c_void_p(self.peer.recv_meta),
+                  GC, y.data_ptr())
         out = torch.empty(T, H, dtype=x.dtype, device=x.device)
         extra = y[GC:GC + T] if self.has_shared else None
-        capi.call("qmoe_combine_rows", ctx.handle, ctypes.c_void_p(self.peer.back_rows), _dt(x), H,
-                  slot.data_ptr(), G, T, extra.data_ptr() if extra is not None else None,
-                  out.data_ptr())
+        self.peer.finish(slot, T, extra, out)
         if return_routing:
             return out, idx.clone(), w.clone()
         return out
