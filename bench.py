@@ -47,10 +47,10 @@ KERNELS_PER_FORWARD = 3  # front cluster (logits, selection, permute); gate/up G
                          # first); down GEMV (h limbs first, weighted combine last)
 KERNELS_PER_PREFILL = 7  # router logits + select, permute, bf16 gather, gate/up, down, combine
 # EP rank (peer-memory exchange): front cluster (route + send list), dispatch,
-# wait, expert pass over the received rows + own tokens (permute, gate/up
-# GEMV, down GEMV whose last phase returns the partial sums to their ranks),
-# finish (wait for the returns + combine)
-KERNELS_PER_EP_FORWARD = 7
+# expert pass over the received rows + own tokens (permute after waiting for
+# the peers' rows, gate/up GEMV, down GEMV whose last phase returns the partial
+# sums to their ranks), finish (wait for the returns + combine)
+KERNELS_PER_EP_FORWARD = 6
 
 
 def parse():

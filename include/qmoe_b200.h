@@ -363,8 +363,9 @@ QMOE_API int qmoe_ep_dispatch(qmoe_ep_peer *p, const void *x, int64_t T, const i
                               const int32_t *send_tok, const int32_t *send_meta);
 QMOE_API int qmoe_ep_wait(qmoe_ep_peer *p, int phase);
 QMOE_API int qmoe_ep_return(qmoe_ep_peer *p, const void *y);
-/* qmoe_layer_forward_ep on this rank's receive rows (R = world*C + own tokens,
- * shared_row0 = world*C) followed by qmoe_ep_return, with the return folded
+/* qmoe_ep_wait(0), qmoe_layer_forward_ep on this rank's receive rows (R =
+ * world*C + own tokens, shared_row0 = world*C) and qmoe_ep_return: the wait is
+ * done by the expert pass's first kernel and the return folded
  * into the expert pass where it can be: the decode path's last phase stores
  * each received row's partial sum straight into its origin rank's return
  * block, one arrival per (row, 1024 columns); rows past world*C (this rank's

@@ -773,6 +773,7 @@ struct ExpertsArgs {
     EpPeerDev *ep_ret = nullptr;  // expert parallel: the down GEMV returns the received
                                   // rows' partial sums straight to their origin ranks
     bool *returned = nullptr;     // set when it did (else the caller runs the return kernel)
+    bool wait_dispatch = false;   // the permute first waits for the peers' rows (ep_ret's flags)
 };
 
 // Weighted sum of each token's expert rows in ascending expert order, plus
@@ -905,6 +906,10 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     pp.pos_tok = L->pos_tok.as<int32_t>();
     pp.groups = L->groups.as<int4>();
     pp.n_groups = L->ngroups.as<int32_t>();
+    if (a.wait_dispatch && a.ep_ret) {
+        pp.ep_wait = 1;
+        pp.ep = *a.ep_ret;
+    }
     mark(L, 1);
     if (!a.permuted) QTRY_CUDA(launch_permute(pp, st));
 
@@ -1528,6 +1533,7 @@ int qmoe_layer_forward_ep_return(qmoe_layer *L, qmoe_ep_peer *p, const void *x, 
     p->d.ret_units = 1;
     a.ep_ret = &p->d;
     a.returned = &returned;
+    a.wait_dispatch = true;
     QTRY(run_experts(L, x, dtype, R, a, y, 0));
     if (!returned) QTRY_CUDA(launch_ep_return(p->d, y, p->ctx->stream));
     return QMOE_OK;

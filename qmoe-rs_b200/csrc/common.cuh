@@ -39,6 +39,13 @@ QMOE_DEV float4 load_act4(const void *base, int dtype, int64_t idx) {
                        __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
 }
 
+// System-scope acquire load (a flag another GPU sets after its stores).
+QMOE_DEV int ld_acquire_sys_i32(const int *p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // load_act4 through L2 only, for rows other CTAs or other GPUs wrote after
 // this kernel started (the read-only path of __ldg is not coherent with them).
 QMOE_DEV float4 load_act4_cg(const void *base, int dtype, int64_t idx) {

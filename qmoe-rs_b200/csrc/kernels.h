@@ -60,6 +60,23 @@ cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaSt
 bool front_cluster_ok(int64_t T, int H, int E, int K);
 cudaError_t launch_front_cluster(const RouterParams &p, const FrontParams &f, cudaStream_t s);
 
+// ---- expert-parallel exchange over peer memory (ep_p2p.cu) ---------------
+// Every rank's allocation has the same layout: receive rows [G*C + C][H]
+// (dtype), receive metadata [G*C + C][2K] int32, returned rows [G*C][H],
+// arrival counters [2][G] int32; offsets below.  base[r] = rank r's allocation as this
+// GPU addresses it (its own included).
+constexpr int kEpMaxWorld = 32;
+struct EpPeerDev {
+    uint8_t *base[kEpMaxWorld];
+    int world, rank, K;
+    int64_t C, H, esize;
+    int64_t off_rows, off_meta, off_back, off_flags;
+    int *seq;                    // this rank's per-forward sequence number
+    int *done;                   // exit count of the return-side kernel (zero between launches)
+    int ret_units;               // arrivals per returned row (1, or the combine tasks per row)
+    int *err;                    // device error word
+};
+
 // ---- permute ------------------------------------------------------------
 // Builds per-expert segments of routed (token, slot) assignments, stable in
 // token order, and the token-group work list of the grouped kernels.
@@ -76,6 +93,8 @@ struct PermuteParams {
     int32_t *pos_tok;          // [T*K] token of each routed position
     int4 *groups;              // (segment, pos_begin, count, 0)
     int32_t *n_groups;         // [2]: routed groups, shared groups
+    int ep_wait;               // expert parallel: first wait (bounded) until every peer's
+    EpPeerDev ep;              //    rows of this forward have arrived (the topk rows are theirs)
 };
 size_t permute_smem_bytes(int e_count);
 cudaError_t launch_permute(const PermuteParams &p, cudaStream_t s);
@@ -143,23 +162,6 @@ struct CombineParams {
     int out_dtype;
 };
 cudaError_t launch_combine(const CombineParams &p, cudaStream_t s);
-
-// ---- expert-parallel exchange over peer memory (ep_p2p.cu) ---------------
-// Every rank's allocation has the same layout: receive rows [G*C + C][H]
-// (dtype), receive metadata [G*C + C][2K] int32, returned rows [G*C][H],
-// arrival counters [2][G] int32; offsets below.  base[r] = rank r's allocation as this
-// GPU addresses it (its own included).
-constexpr int kEpMaxWorld = 32;
-struct EpPeerDev {
-    uint8_t *base[kEpMaxWorld];
-    int world, rank, K;
-    int64_t C, H, esize;
-    int64_t off_rows, off_meta, off_back, off_flags;
-    int *seq;                    // this rank's per-forward sequence number
-    int *done;                   // exit count of the return-side kernel (zero between launches)
-    int ret_units;               // arrivals per returned row (1, or the combine tasks per row)
-    int *err;                    // device error word
-};
 
 // ---- decode grouped GEMV (qgemv_imma.cu): work list and operands ---------
 struct DecodeMaps {

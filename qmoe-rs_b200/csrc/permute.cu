@@ -16,6 +16,7 @@
 // segment offsets and the token-group work list the grouped kernels walk.
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace qmoe {
 namespace {
@@ -77,6 +78,28 @@ permute_kernel(const PermuteParams p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
+    if (p.ep_wait) {
+        // the rows and their metadata come from the peers' dispatch: wait
+        // (bounded) until each peer's C rows of this forward have arrived
+        if (warp == 0) {
+            const int want = (int)((*p.ep.seq + 1) * p.ep.C);
+            bool ok = true;
+            for (int r = lane; r < p.ep.world; r += 32) {
+                if (r == p.ep.rank) continue;
+                const int *f = reinterpret_cast<const int *>(p.ep.base[p.ep.rank] + p.ep.off_flags) + r;
+                uint32_t n = 0;
+                while (ld_acquire_sys_i32(f) < want) {
+                    if (++n >= sm100::kMaxWaitProbes) {
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            if (!__all_sync(0xffffffffu, ok) && lane == 0) atomicOr(p.ep.err, sm100::kErrWaitTimeout);
+        }
+        __syncthreads();
+    }
     const int64_t T = p.T;
     const int K = p.K;
     const int64_t TK = T * K;

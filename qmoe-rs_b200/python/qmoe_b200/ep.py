@@ -268,9 +268,11 @@ class ExpertParallelMoE:
         return self.combine(back, slot, extra, T, x.dtype)
 
     def forward_p2p(self, x, return_routing: bool = False):
-        """The forward with the exchanges over peer memory: dispatch kernel,
-        wait, this rank's experts on the received rows (and the shared expert
-        on its own tokens), return kernel, wait, combine."""
+        """The forward with the exchanges over peer memory: route and send
+        list (one kernel for decode batches), dispatch kernel, this rank's
+        experts on the received rows and the shared expert on its own tokens
+        (the first kernel waits for the peers' rows, the last returns the
+        partial sums to their ranks), finish (wait for the returns, combine)."""
         if x.dtype != self.dtype:
             raise TypeError(f"this exchange carries {self.dtype} rows, got {x.dtype}")
         T, H = x.shape
@@ -282,11 +284,11 @@ class ExpertParallelMoE:
         ctx = self.layer.ctx
         ctx.use_current_torch_stream()
         self.peer.dispatch(x, T, counts, tok, meta)
-        self.peer.wait(0)
         y = self._buf(("y", x.dtype), lambda: torch.empty(GC + C, H, dtype=x.dtype, device=x.device))
         R = GC + T if self.has_shared else GC
-        # the expert pass stores the received rows' partial sums straight into
-        # their origin ranks' return blocks (or runs the return kernel)
+        # the expert pass waits for the peers' rows in its first kernel and
+        # stores the received rows' partial sums straight into their origin
+        # ranks' return blocks (or runs the return kernel)
         capi.call("qmoe_layer_forward_ep_return", self.layer._h, self.peer._h,
                   ctypes.c_void_p(self.peer.recv_rows), _dt(x), R, ctypes.c_void_p(self.peer.recv_meta),
                   GC, y.data_ptr())
