@@ -14,8 +14,11 @@
  *     pointers of one call are host (QMOE_PTR_HOST) or device
  *     (QMOE_PTR_DEVICE) memory.  Host inputs are copied in and host outputs
  *     copied back on the context's stream (qmoe_layer_forward reads and
- *     writes page-locked host buffers in place instead), and the call
- *     returns after the results are in host memory.  Device calls are
+ *     writes page-locked host buffers in place instead, and replays the
+ *     kernel sequence it captured on the previous call when x, out, T,
+ *     dtype and path repeat and no routing is copied out; not on the
+ *     legacy default stream), and the call returns after the results are
+ *     in host memory.  Device calls are
  *     asynchronous on that stream.
  *   - Packed weights use qmoe-rs's layout verbatim (quantize.py:7-33,
  *     src/tensor.rs:16-23): uint8 [out, in/4], four 2-bit codes per byte,

@@ -205,6 +205,16 @@ struct qmoe_layer {
     CUtensorMap tm_xg, tm_hb, tm_xg2, tm_hb2;  // 256-row and 128-row boxes
     // tracing
     bool profiling = false;
+    // Host-buffer forwards that repeat with the same page-locked x and out:
+    // the kernel sequence is captured once (on the second such call) and
+    // replayed as one graph launch.
+    struct {
+        const void *x = nullptr;
+        const void *out = nullptr;
+        int64_t T = 0, cap = 0;
+        int dtype = -1, path = -1, calls = 0;
+        cudaGraphExec_t exec = nullptr;
+    } fg;
     cudaEvent_t ev[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
 };
 
@@ -436,8 +446,9 @@ int qmoe_layer_destroy(qmoe_layer *L) {
                       &L->seg_off, &L->groups, &L->ngroups, &L->h, &L->y,
                       &L->x_in, &L->io_out, &L->user_idx, &L->user_w,
                       &L->xq1, &L->meta1, &L->xq2, &L->meta2, &L->router_scratch,
-                      &L->xg, &L->hb, &L->front_counter};
+                      &L->xg, &L->hb, &L->front_counter, &L->gemv_sched};
     for (DevBuf *b : bufs) release(*b);
+    if (L->fg.exec) cudaGraphExecDestroy(L->fg.exec);
     delete L;
     return QMOE_OK;
 }
@@ -1101,14 +1112,54 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
             outd = L->io_out.p;
         }
     }
-    if (front) {
-        QTRY(run_front(L, x_mapped ? x_mapped : xd, dtype, T, prefill,
-                       x_mapped ? const_cast<void *>(xd) : nullptr));
-        a.permuted = true;
-    } else {
-        QTRY(run_router(L, xd, dtype, T));
+    auto enqueue = [&]() -> int {
+        if (front) {
+            QTRY(run_front(L, x_mapped ? x_mapped : xd, dtype, T, prefill,
+                           x_mapped ? const_cast<void *>(xd) : nullptr));
+            a.permuted = true;
+        } else {
+            QTRY(run_router(L, xd, dtype, T));
+        }
+        return run_experts(L, xd, dtype, T, a, outd, 0);
+    };
+    // whole forward in place on page-locked buffers, no routing copied out:
+    // a repeat of the last call replays its captured graph
+    if (x_mapped && out_mapped && !topk_idx && !topk_w && !L->profiling) {
+        auto &G = L->fg;
+        const bool same = G.x == x && G.out == out && G.T == T && G.dtype == dtype && G.path == L->path &&
+                          G.cap == L->cap;
+        if (!same) {
+            if (G.exec) cudaGraphExecDestroy(G.exec);
+            G.exec = nullptr;
+            G.x = x;
+            G.out = out;
+            G.T = T;
+            G.cap = L->cap;
+            G.dtype = dtype;
+            G.path = L->path;
+            G.calls = 0;
+        }
+        if (!G.exec && ++G.calls >= 2) {
+            cudaGraph_t graph = nullptr;
+            if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+                const int rc = enqueue();
+                const cudaError_t ec = cudaStreamEndCapture(st, &graph);
+                if (rc == QMOE_OK && ec == cudaSuccess && graph &&
+                    cudaGraphInstantiate(&G.exec, graph, 0) != cudaSuccess)
+                    G.exec = nullptr;
+                if (graph) cudaGraphDestroy(graph);
+                cudaGetLastError();
+                if (rc != QMOE_OK) return rc;
+            } else {
+                cudaGetLastError();   // e.g. the legacy default stream, which cannot be captured
+            }
+        }
+        if (G.exec) {
+            QTRY_CUDA(cudaGraphLaunch(G.exec, st));
+            return sync_and_check(st);
+        }
     }
-    QTRY(run_experts(L, xd, dtype, T, a, outd, 0));
+    QTRY(enqueue());
     const size_t kb = sizeof(int32_t) * T * c.top_k;
     if (topk_idx)
         QTRY_CUDA(cudaMemcpyAsync(topk_idx, L->topk_idx.p, kb,

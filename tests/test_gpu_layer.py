@@ -174,6 +174,30 @@ def test_pinned_host_buffers_read_in_place(dtype, T):
     assert torch.equal(pageable, ref)
 
 
+@pytest.mark.parametrize("dtype,T", [(torch.float32, 32), (torch.bfloat16, 5)])
+def test_repeated_pinned_forwards_replay_one_graph(dtype, T):
+    # the same page-locked x and out over several calls: the second call
+    # captures the kernel sequence, later ones replay it; new contents of x
+    # must give the device path's new results every time, and a call with
+    # another output buffer must not reuse the graph
+    cfg = MoEConfig(16, 4, 512, 256, shared_intermediate_dim=256)
+    layer, *_ = build(cfg, seed=29)
+    xp = torch.empty(T, 512, dtype=dtype).pin_memory()
+    op = torch.empty(T, 512, dtype=dtype).pin_memory()
+    op2 = torch.empty_like(op).pin_memory()
+    # a side stream (the legacy default stream cannot be captured; there the
+    # calls run without a graph)
+    with torch.cuda.stream(torch.cuda.Stream()):
+        for i in range(4):
+            x = torch.randn(T, 512, generator=torch.Generator().manual_seed(100 + i)).to(dtype)
+            xp.copy_(x)
+            ref = layer.forward(x.cuda()).cpu()
+            layer.forward(xp, out=op)
+            assert torch.equal(op, ref), f"call {i}"
+        layer.forward(xp, out=op2)
+        assert torch.equal(op2, op)
+
+
 def test_bf16_activations_within_tolerance():
     cfg = MoEConfig(16, 4, 512, 256, shared_intermediate_dim=256)
     layer, np_exp, np_sh, gw = build(cfg, seed=11)
