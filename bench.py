@@ -64,7 +64,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU-baseline leg (for profiler runs)")
-    ap.add_argument("--ncu-case", choices=["decode", "prefill"], default=None,
+    ap.add_argument("--ncu-case", choices=["decode", "prefill", "pack"], default=None,
                     help="only run 3 eager forwards of one replica (configs[1] decode or "
                          "configs[2] prefill) for an ncu capture, print nothing")
     return ap.parse_args()
@@ -318,6 +318,40 @@ def graph_stage_times(layers, xs, stream, n_prof: int = 100):
     for L in layers:
         L.set_profiling(False)
     return {k: float(np.mean(v)) for k, v in stage_ms.items()}
+
+
+PACK_ROWS = 64 * 1408      # the V2-Lite layer's 64 stacked gate matrices: [64 x 1408, 2048] f32
+
+
+def run_pack(seed: int, dev: str, steps: int = 10):
+    """The device packer (quantize.py's format producer, csrc/pack.cu) over
+    the V2-Lite layer's stacked gate weights, [64 x 1408, 2048] f32 = 738 MB
+    (> L2), scales computed.  Algorithmic bytes: the f32 read, the packed
+    bytes and the scales written."""
+    from qmoe_b200 import quantize as qz
+    H = WORKLOAD["H"]
+    g = torch.Generator(device=dev).manual_seed(seed + 313)
+    wt = torch.randn(PACK_ROWS, H, generator=g, device=dev) * 0.02
+    for _ in range(3):
+        qz.device_quantize(wt)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(steps):
+        qz.device_quantize(wt)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    nbytes = 4 * PACK_ROWS * H + PACK_ROWS * H // 4 + 4 * PACK_ROWS
+    hbm, _, peak_kind = load_peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    del wt
+    torch.cuda.empty_cache()
+    return {"workload": "V2-Lite gate weights of 64 experts, [90112, 2048] f32 -> 2-bit + row scales",
+            "ms": ms, "algorithmic_bytes": nbytes, "achieved_gbs": gbs, "peak_gbs": hbm,
+            "frac": gbs / hbm, "peak_kind": peak_kind,
+            "weights_per_s": PACK_ROWS * H / (ms / 1e3)}
 
 
 def run_prefill(layers, seed: int, dev: str, steps: int = 20):
@@ -614,6 +648,7 @@ def run_ours(args):
            "ms_per_step": e2e_ms}
 
     prefill = run_prefill(layers, args.seed, dev) if ws == 1 else None
+    pack = run_pack(args.seed, dev) if ws == 1 else None
 
     if rank == 0:
         hbm, bf16, peak_kind = load_peaks()
@@ -642,6 +677,7 @@ def run_ours(args):
                       "achieved_gbs_per_step": layer_bytes / (ms_max / args.steps / 1e3) / 1e9},
             "e2e": e2e,
             "prefill": prefill,
+            "pack": pack,
             "gpu_launches": KERNELS_PER_FORWARD * args.steps,
             "clocks": clk.summary(),
         }
@@ -665,6 +701,16 @@ def run_ncu_case(args):
     """A short fixed workload for ncu captures (one replica, 3 forwards)."""
     from qmoe_b200 import QMoELayer, default_context
     torch.cuda.set_device(0)
+    if args.ncu_case == "pack":
+        # 16 experts' stacked gate weights: 184 MB (> L2), three packs and
+        # no other launch of the packer before them
+        from qmoe_b200 import quantize as qz
+        g = torch.Generator(device="cuda").manual_seed(args.seed + 313)
+        wt = torch.randn(16 * 1408, WORKLOAD["H"], generator=g, device="cuda") * 0.02
+        for _ in range(3):
+            qz.device_quantize(wt)
+        torch.cuda.synchronize()
+        return
     experts, shared, gate_w = synth_weights(args.seed, "cuda")
     layer = QMoELayer(make_cfg(), gate_w, experts, shared=shared, ctx=default_context(0))
     del experts, shared

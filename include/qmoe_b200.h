@@ -146,6 +146,26 @@ QMOE_API int qmoe_packed_shape(const qmoe_packed *t, int64_t *out_features,
 QMOE_API int qmoe_packed_forward(qmoe_packed *t, const float *x, int64_t batch, float *y,
                         int ptr_kind);
 
+/* ---- packer: quantize.py (format producer) ----------------------------- */
+
+/*
+ * The offline quantizer of qmoe-rs on the device, bit for bit:
+ * quantize_and_pack (quantize.py:7-33) with the row scale of the packing
+ * loop (quantize.py:97-100).  w [out_features, in_features] f32, row-major
+ * -> packed [out_features, in_features/4] bytes, code = clamp(round half to
+ * even(w / scale), -1, 1) + 1, weight j of each group of four in bits
+ * 2j..2j+1.  With scales_given == 0 the scales [out_features] f32 are
+ * computed and written: max(unbiased std of the row, 1e-5)
+ * (`tensor.std(dim=1)`, `torch.clamp(scale, min=1e-5)`); otherwise they are
+ * read (`quantize_and_pack(weight, scale)`).  in_features must be a
+ * positive multiple of 4 (the reference's assertion, quantize.py:26); device
+ * w must be 16-byte aligned.  Host buffers (QMOE_PTR_HOST) are staged
+ * through the device in row chunks; the call returns when they are written.
+ */
+QMOE_API int qmoe_quantize_pack(qmoe_ctx *ctx, const float *w, int64_t out_features,
+                       int64_t in_features, float *scales, int scales_given,
+                       uint8_t *packed, int ptr_kind);
+
 /* ---- MoE layer: QMoELayer (src/moe.rs:23-130) + SharedExpert ----------- */
 
 /*

@@ -394,6 +394,71 @@ int qmoe_packed_forward(qmoe_packed *t, const float *x, int64_t batch, float *y,
 }
 
 // ---------------------------------------------------------------------------
+// packer
+// ---------------------------------------------------------------------------
+
+// Host rows go through the device in chunks of at most this many bytes of w.
+constexpr size_t kPackChunkBytes = size_t(256) << 20;
+
+static int pack_chunks(qmoe_ctx *ctx, const float *w, int64_t out_f, int64_t in_f, float *scales,
+                       int scales_given, uint8_t *packed, int sm_count, DevBuf &wd, DevBuf &sd,
+                       DevBuf &pd) {
+    cudaStream_t st = ctx->stream;
+    const size_t row_bytes = sizeof(float) * (size_t)in_f;
+    int64_t chunk = (int64_t)(kPackChunkBytes / row_bytes);
+    if (chunk < 1) chunk = 1;
+    if (chunk > out_f) chunk = out_f;
+    QTRY(grow(wd, row_bytes * chunk));
+    QTRY(grow(sd, sizeof(float) * chunk));
+    QTRY(grow(pd, (size_t)(in_f / 4) * chunk));
+    for (int64_t r0 = 0; r0 < out_f; r0 += chunk) {
+        const int64_t n = out_f - r0 < chunk ? out_f - r0 : chunk;
+        QTRY_CUDA(cudaMemcpyAsync(wd.p, w + r0 * in_f, row_bytes * n, cudaMemcpyHostToDevice, st));
+        if (scales_given)
+            QTRY_CUDA(cudaMemcpyAsync(sd.p, scales + r0, sizeof(float) * n, cudaMemcpyHostToDevice, st));
+        PackParams pp{wd.as<float>(), n, in_f, sd.as<float>(), scales_given, pd.as<uint8_t>(), error_flag()};
+        QTRY_CUDA(launch_pack_rows(pp, sm_count, st));
+        QTRY_CUDA(cudaMemcpyAsync(packed + r0 * (in_f / 4), pd.p, (size_t)(in_f / 4) * n,
+                                  cudaMemcpyDeviceToHost, st));
+        if (!scales_given)
+            QTRY_CUDA(cudaMemcpyAsync(scales + r0, sd.p, sizeof(float) * n, cudaMemcpyDeviceToHost, st));
+        // the staging buffers are reused by the next chunk
+        QTRY(sync_and_check(st));
+    }
+    return QMOE_OK;
+}
+
+int qmoe_quantize_pack(qmoe_ctx *ctx, const float *w, int64_t out_features, int64_t in_features,
+                       float *scales, int scales_given, uint8_t *packed, int ptr_kind) {
+    if (!ctx) return fail(QMOE_ERR_INVALID, "ctx is NULL");
+    QTRY(check_ptr_kind(ptr_kind));
+    if (out_features < 0) return fail(QMOE_ERR_INVALID, "out_features < 0");
+    // quantize.py:26 asserts in_features % 4 == 0
+    if (in_features <= 0 || in_features % 4)
+        return fail(QMOE_ERR_INVALID, "in_features (%lld) must be a positive multiple of 4",
+                    (long long)in_features);
+    if (out_features == 0) return QMOE_OK;
+    if (!w || !scales || !packed) return fail(QMOE_ERR_INVALID, "NULL argument");
+    QTRY(check_align(w, ptr_kind, "w"));
+    DeviceGuard g(ctx->device);
+    int sm_count = 0;
+    QTRY_CUDA(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, ctx->device));
+    if (ptr_kind == QMOE_PTR_DEVICE) {
+        PackParams pp{w, out_features, in_features, scales, scales_given, packed, error_flag()};
+        QTRY_CUDA(launch_pack_rows(pp, sm_count, ctx->stream));
+        return QMOE_OK;
+    }
+    DevBuf wd, sd, pd;
+    const int rc = pack_chunks(ctx, w, out_features, in_features, scales, scales_given, packed, sm_count,
+                               wd, sd, pd);
+    if (rc != QMOE_OK) cudaStreamSynchronize(ctx->stream);   // no copy in flight from freed memory
+    release(wd);
+    release(sd);
+    release(pd);
+    return rc;
+}
+
+// ---------------------------------------------------------------------------
 // layer
 // ---------------------------------------------------------------------------
 

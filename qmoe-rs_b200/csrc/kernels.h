@@ -163,6 +163,21 @@ struct CombineParams {
 };
 cudaError_t launch_combine(const CombineParams &p, cudaStream_t s);
 
+// 2-bit packer (pack.cu): qmoe-rs quantize.py:7-33 with the row scale of
+// :97-100.  w [out_f, in_f] f32 (16-byte aligned, in_f a multiple of 4) ->
+// packed [out_f, in_f / 4]; scales [out_f] written, or read when
+// scales_given.
+struct PackParams {
+    const float *w;
+    int64_t out_f, in_f;
+    float *scales;
+    int scales_given;
+    uint8_t *packed;
+    int *err;                    // device error word (a bounded wait that gave up)
+};
+constexpr size_t kPackStageMax = 100 * 1024;   // widest row staged in shared memory (bytes)
+cudaError_t launch_pack_rows(const PackParams &p, int sm_count, cudaStream_t s);
+
 // ---- decode grouped GEMV (qgemv_imma.cu): work list and operands ---------
 struct DecodeMaps {
     CUtensorMap a0, a1;          // routed matrices (mode 0: gate, up; mode 1: down, down)

@@ -85,6 +85,7 @@ SIGNATURES = {
     "qmoe_packed_destroy": (_I, [_P]),
     "qmoe_packed_shape": (_I, [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     "qmoe_packed_forward": (_I, [_P, _P, _I64, _P, _I]),
+    "qmoe_quantize_pack": (_I, [_P, _P, _I64, _I64, _P, _I, _P, _I]),
     "qmoe_layer_create": (_I, [_P, ctypes.POINTER(MoeConfigC), _P, _P,
                                ctypes.POINTER(ExpertWeightsC), _I32, _I32,
                                ctypes.POINTER(ExpertWeightsC), _I, _PP]),

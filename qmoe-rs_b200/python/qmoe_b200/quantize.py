@@ -10,8 +10,10 @@ quantizer writes:
   * four codes per byte, weight j of a group of four in bits 2j..2j+1
     (quantize.py:31), rows of in_features/4 bytes, row-major [out, in/4].
 
-These helpers accept CPU or CUDA torch tensors, so seeded synthetic layers of
-the full benchmark sizes can be packed on the device.
+CUDA tensors are packed by the library's device packer (csrc/pack.cu through
+qmoe_quantize_pack), bit for bit the same as quantize.py on the host; CPU
+tensors by the torch restatement below (the reference's own offline
+arithmetic, used to make host-side fixtures).
 """
 from __future__ import annotations
 
@@ -43,13 +45,40 @@ def pack_codes(codes: torch.Tensor) -> torch.Tensor:
     return packed.to(torch.uint8)
 
 
+def device_quantize(weight: torch.Tensor, scale: torch.Tensor = None, ctx=None):
+    """The device packer (qmoe_quantize_pack) on CUDA tensors, on torch's
+    current stream: (packed uint8 [out, in/4], scales f32 [out]); scales
+    computed as quantize.py:97-100 unless `scale` is given."""
+    from . import capi
+    from .layer import default_context
+    if not weight.is_cuda:
+        raise ValueError("device_quantize takes a CUDA tensor")
+    if weight.dim() != 2:
+        raise ValueError("weight must be [out_features, in_features]")
+    w = weight.float().contiguous()
+    out_f, in_f = w.shape
+    ctx = ctx or default_context(w.device.index)
+    ctx.use_current_torch_stream()
+    packed = torch.empty((out_f, in_f // 4), dtype=torch.uint8, device=w.device)
+    given = scale is not None
+    scales = (scale.to(device=w.device, dtype=torch.float32).contiguous() if given
+              else torch.empty(out_f, dtype=torch.float32, device=w.device))
+    capi.call("qmoe_quantize_pack", ctx.handle, w.data_ptr(), out_f, in_f, scales.data_ptr(),
+              int(given), packed.data_ptr(), capi.QMOE_PTR_DEVICE)
+    return packed, scales
+
+
 def quantize_and_pack(weight: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     """Same contract as qmoe-rs quantize.py:7-33."""
+    if weight.is_cuda:
+        return device_quantize(weight, scale)[0]
     return pack_codes(ternary_codes(weight, scale))
 
 
 def quantize_weight(weight: torch.Tensor):
     """weight [out, in] -> (packed uint8 [out, in/4], scales f32 [out])."""
+    if weight.is_cuda:
+        return device_quantize(weight)
     scale = row_scales(weight)
     return quantize_and_pack(weight, scale), scale
 
