@@ -28,12 +28,18 @@
 // on its x86 host (INT_MIN, +1, & 3 = 1); s = 0 gives 2 / 0 / 1 for w > 0,
 // w < 0, w = 0 as w / 0 = +inf / -inf / NaN does.
 //
-// HBM-bound byte work (4 bytes read per weight, 1/4 byte written): one CTA
-// per row at a time, rows double-buffered in shared memory by 1-D bulk
-// copies (cp.async.bulk, no multicast) completing on an mbarrier, so the next
-// row streams in while the three passes (sum, squared deviations, codes) run
-// over the current one; a grid of one wave of resident CTAs loops over the
-// rows.  Rows wider than the staging limit re-read their row through L2.
+// HBM-bound byte work (4 bytes read per weight, 1/4 byte written), rows
+// streamed into shared memory by 1-D bulk copies (cp.async.bulk, no
+// multicast) completing on mbarriers, so later rows arrive while the three
+// passes (sum, squared deviations, codes) run over the current one:
+//   * rows of up to kPackWarpRowMax floats (the V2-Lite widths): one warp per
+//     row, each warp with a ring of 3 (or 2) row buffers, warp-shuffle
+//     reductions only, one CTA of 8 warps per SM;
+//   * wider rows up to kPackStageMax bytes: one CTA per row, two rows
+//     double-buffered, CTA reductions;
+//   * wider still: one CTA per row with plain loads, the second and third
+//     passes served by L2.
+// In every form a grid of one wave of resident CTAs loops over the rows.
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
