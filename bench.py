@@ -3,18 +3,27 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Default workload (configs[1] of the benchmark definition): one
-DeepSeek-V2-Lite-shaped MoE layer -- hidden 2048, 64 routed experts, top-6
-softmax gating with renormalised weights, 2 shared experts merged into one
-FFN of width 2816, expert width 1408, SwiGLU -- in decode with a batch of 32
-f32 tokens per GPU.  Expert weights are seeded N(0, 0.02) packed to qmoe-rs's
-2-bit format, the gate is f32 N(0, 0.02), activations f32 N(0, 1).
+Headline workload (configs[3] of the benchmark definition): one
+DeepSeek-V3-shaped MoE layer -- hidden 7168, 256 routed experts, sigmoid
+scoring with 8 groups of which the best 4 are kept, top-8 experts with
+renormalised weights scaled by 2.5, one shared expert, expert intermediate
+2048, SwiGLU -- over 4096 bf16 tokens per GPU.  On N GPUs the layer is
+expert-parallel (256 / N experts per GPU, the gate and the shared expert on
+every GPU, each GPU routing its own 4096 tokens and exchanging rows with the
+others over NVLink): weak scaling, per-GPU work fixed.  Expert weights are
+seeded N(0, 0.02) packed to qmoe-rs's 2-bit format, the gate f32 N(0, 0.02),
+activations bf16 N(0, 1).
 
 A step is one forward of the layer over one batch.  The timed region replays
 K steps (CUDA graphs of the forward) back to back between CUDA events, with a
 barrier and a device synchronize on both sides, and takes the max over ranks.
-L2 is kept cold by rotating over 4 independent weight replicas (4 x 144 MB >
-126 MB L2), so every step streams its weights from HBM.
+Every step streams the layer's weights from HBM: 2.85 GB on one GPU, and at
+least 0.4 GB per GPU at N = 8, all far above the 126 MB L2.
+
+On one GPU the line also carries the decode-sized lines the metric's second
+half asks for (HBM rooflines): the same V3 layer over 32 bf16 tokens, and
+configs[1] (the DeepSeek-V2-Lite layer over 32 f32 tokens), plus configs[2]
+(V2-Lite prefill, 2048 bf16 tokens) and the device packer.
 
 Prints one JSON line (rank 0).
 """
@@ -38,35 +47,63 @@ import torch  # noqa: E402
 
 METRIC = "MoE-layer tokens/sec at 1/2/4/8 B200; decode HBM GB/s as % of peak"
 UNIT = "tokens/s"
+L2_BYTES = 126 * 2**20
 
-WORKLOAD = dict(
-    name="configs[1]: DeepSeek-V2-Lite MoE layer, decode, 32 f32 tokens/GPU",
-    E=64, k=6, H=2048, I=1408, Is=2816, T=32, norm_topk=True)
-REPLICAS = 4
-KERNELS_PER_FORWARD = 3  # front cluster (logits, selection, permute); gate/up GEMV (x limbs
-                         # first); down GEMV (h limbs first, weighted combine last)
-KERNELS_PER_PREFILL = 7  # router logits + select, permute, bf16 gather, gate/up, down, combine
-# EP rank (peer-memory exchange): front cluster (route + send list), dispatch,
-# expert pass over the received rows + own tokens (permute after waiting for
-# the peers' rows, gate/up GEMV, down GEMV whose last phase returns the partial
-# sums to their ranks), finish (wait for the returns + combine)
-KERNELS_PER_EP_FORWARD = 6
+V3 = dict(key="v3",
+          name="configs[3]: DeepSeek-V3 MoE layer (hidden 7168, 256 experts, sigmoid 8 groups / "
+               "top-4 groups / top-8, 1 shared expert, intermediate 2048), 4096 bf16 tokens per GPU, "
+               "expert-parallel over the GPUs",
+          E=256, k=8, H=7168, I=2048, Is=2048, T=4096, act="bf16", scoring=1, n_group=8,
+          topk_group=4, norm_topk=True, routed_scale=2.5)
+V2 = dict(key="v2lite",
+          name="configs[1]: DeepSeek-V2-Lite MoE layer (hidden 2048, 64 experts, softmax top-6, "
+               "2 shared experts, intermediate 1408), decode, 32 f32 tokens per GPU",
+          E=64, k=6, H=2048, I=1408, Is=2816, T=32, act="f32", scoring=0, n_group=1,
+          topk_group=1, norm_topk=True, routed_scale=1.0)
+WORKLOADS = {"v3": V3, "v2lite": V2}
+
+# kernels launched per forward (counted from the launch sequence in csrc/api.cu)
+LAUNCHES = {
+    # decode (<= 64 tokens, all experts local): front cluster (logits,
+    # selection, permute); gate/up GEMV (x limbs first); down GEMV (h limbs
+    # first, weighted combine last)
+    "decode_front": 3,
+    # decode batches the front cluster does not take (T * E > 4096): router
+    # partials, selection, permute, gate/up GEMV, down GEMV
+    "decode_router": 5,
+    # prefill: router partials or logits, selection, permute, bf16 gather,
+    # gate/up GEMM, down GEMM, combine
+    "prefill": 7,
+    # expert-parallel rank, decode: front cluster (route + send list),
+    # dispatch, permute (waits for the peers' rows), gate/up GEMV, down GEMV
+    # (returns the partial sums to their ranks), finish
+    "ep_decode": 6,
+    # expert-parallel rank, prefill: router logits, selection, plan,
+    # dispatch, permute (waits), gather, gate/up GEMM, down GEMM, combine,
+    # return, finish
+    "ep_prefill": 11,
+}
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="v3",
+                    help="headline workload: v3 = configs[3] (default), v2lite = configs[1]")
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: peer-memory kernels or NCCL all-to-alls for the EP exchanges")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU-baseline leg (for profiler runs)")
-    ap.add_argument("--ncu-case", choices=["decode", "prefill", "pack"], default=None,
-                    help="only run 3 eager forwards of one replica (configs[1] decode or "
-                         "configs[2] prefill) for an ncu capture, print nothing")
+    ap.add_argument("--no-sublines", action="store_true",
+                    help="N = 1: only the headline workload")
+    ap.add_argument("--ncu-case", choices=["decode", "prefill", "pack", "v3-prefill", "v3-decode"],
+                    default=None,
+                    help="only run 3 eager forwards of a short fixed case for an ncu capture, "
+                         "print nothing")
     return ap.parse_args()
 
 
@@ -86,9 +123,9 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def read_profile_traffic(name: str = "qgemv_gate_up_decode_v2lite_t32.txt"):
-    """DRAM bytes per launch of a gate/up kernel from its committed ncu
-    summary (a line 'traffic_bytes_per_launch: N'), or None."""
+def read_profile_traffic(name: str):
+    """DRAM bytes per launch of a kernel from its committed ncu summary (a
+    line 'traffic_bytes_per_launch: N'), or None."""
     path = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(path):
         return None
@@ -164,78 +201,147 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# workload
+# workloads
 # ---------------------------------------------------------------------------
 
-def make_cfg():
+def act_dtype(W, T=None):
+    return torch.bfloat16 if W["act"] == "bf16" else torch.float32
+
+
+def act_bytes(W):
+    return 2 if W["act"] == "bf16" else 4
+
+
+def rel_err(a, b) -> float:
+    """max |a - b| / max |b| (the max-abs relative error of the parity bar)."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    den = max(float(np.max(np.abs(b))) if b.size else 0.0, 1e-30)
+    return float(np.max(np.abs(a - b))) / den if a.size else 0.0
+
+
+def make_cfg(W):
     from qmoe_b200 import MoEConfig
-    w = WORKLOAD
-    return MoEConfig(w["E"], w["k"], w["H"], w["I"], shared_intermediate_dim=w["Is"],
-                     norm_topk_prob=w["norm_topk"])
+    return MoEConfig(W["E"], W["k"], W["H"], W["I"], shared_intermediate_dim=W["Is"],
+                     scoring=W["scoring"], n_group=W["n_group"], topk_group=W["topk_group"],
+                     norm_topk_prob=W["norm_topk"], routed_scaling_factor=W["routed_scale"])
 
 
-def synth_weights(seed: int, device: str, experts=None):
+def oracle_cfg(W):
+    from oracle import oracle as qo
+    return qo.MoEConfig(W["E"], W["k"], W["H"], W["I"], W["Is"], scoring=W["scoring"],
+                        n_group=W["n_group"], topk_group=W["topk_group"],
+                        norm_topk_prob=W["norm_topk"], routed_scaling_factor=W["routed_scale"])
+
+
+def synth_weights(W, seed: int, device: str, experts=None, packer=None):
     """Seeded layer; each expert has its own generator (seed, expert id), so
     ranks that build disjoint expert ranges agree on every expert, and all
-    ranks build the same gate and shared expert."""
+    ranks build the same gate and shared expert.  `packer` maps an f32
+    [out, in] weight to (packed, scales); default: the package quantizer
+    (the device packer for CUDA tensors)."""
     from qmoe_b200 import quantize as qz
-    w = WORKLOAD
+    pack = packer or qz.quantize_weight
 
     def gen(s):
         return torch.Generator(device=device).manual_seed(s)
 
     def mat(g, o, i):
-        return qz.quantize_weight(torch.randn(o, i, generator=g, device=device) * 0.02)
+        return pack(torch.randn(o, i, generator=g, device=device) * 0.02)
 
     out = []
-    for e in (range(w["E"]) if experts is None else experts):
+    for e in (range(W["E"]) if experts is None else experts):
         g = gen(seed * 1009 + 1 + e)
-        out.append([mat(g, w["I"], w["H"]), mat(g, w["I"], w["H"]), mat(g, w["H"], w["I"])])
+        out.append([mat(g, W["I"], W["H"]), mat(g, W["I"], W["H"]), mat(g, W["H"], W["I"])])
     g = gen(seed * 1009)
-    shared = [mat(g, w["Is"], w["H"]), mat(g, w["Is"], w["H"]), mat(g, w["H"], w["Is"])]
-    gate_w = torch.randn(w["E"], w["H"], generator=g, device=device) * 0.02
+    shared = [mat(g, W["Is"], W["H"]), mat(g, W["Is"], W["H"]), mat(g, W["H"], W["Is"])]
+    gate_w = torch.randn(W["E"], W["H"], generator=g, device=device) * 0.02
     return out, shared, gate_w
 
 
-def algorithmic_gate_up_bytes(idx_np: np.ndarray) -> float:
-    """Bytes the gate/up kernel must move for one forward: packed gate+up rows
-    and scales of every routed expert the batch touches, the shared expert's,
-    the activations read and the SwiGLU outputs written."""
-    w = WORKLOAD
-    touched = len(np.unique(idx_np))
-    per_expert = 2 * (w["I"] * w["H"] // 4) + 2 * 4 * w["I"]
-    shared = 2 * (w["Is"] * w["H"] // 4) + 2 * 4 * w["Is"]
-    acts = 4 * w["T"] * w["H"]
-    h_out = 4 * (w["T"] * w["k"] * w["I"] + w["T"] * w["Is"])
-    return float(touched * per_expert + shared + acts + h_out)
+def torch_packer(w):
+    """quantize.py's arithmetic in plain torch ops (for the reference arm's
+    inputs, so that arm runs nothing of this package's CUDA library)."""
+    from qmoe_b200 import quantize as qz
+    s = qz.row_scales(w)
+    return qz.pack_codes(qz.ternary_codes(w, s)), s
 
 
-def algorithmic_layer_bytes(idx_np: np.ndarray) -> float:
-    w = WORKLOAD
-    touched = len(np.unique(idx_np))
-    per_expert = 3 * w["H"] * w["I"] // 4 + 4 * (2 * w["I"] + w["H"])
-    shared = 3 * w["H"] * w["Is"] // 4 + 4 * (2 * w["Is"] + w["H"])
-    gate = 4 * w["E"] * w["H"]
-    acts = 2 * 4 * w["T"] * w["H"]
-    return float(touched * per_expert + shared + gate + acts)
+def synth_x(W, T, seed, dev):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return torch.randn(T, W["H"], generator=g, device=dev).to(act_dtype(W))
+
+
+def per_expert_bytes(W):
+    return 3 * W["H"] * W["I"] // 4 + 4 * (2 * W["I"] + W["H"])
+
+
+def shared_bytes(W):
+    return 3 * W["H"] * W["Is"] // 4 + 4 * (2 * W["Is"] + W["H"])
+
+
+def layer_bytes(W, T, touched):
+    """Algorithmic HBM bytes of one forward: packed rows and scales of every
+    expert the batch touches, the shared expert's, the gate, x in, out."""
+    return float(touched * per_expert_bytes(W) + shared_bytes(W) + 4 * W["E"] * W["H"]
+                 + 2 * act_bytes(W) * T * W["H"])
+
+
+def gate_up_bytes(W, T, touched):
+    """The gate/up GEMV: packed gate+up rows and scales of the touched
+    experts and the shared expert, the activations read, the f32 SwiGLU rows
+    written."""
+    pe = 2 * (W["I"] * W["H"] // 4) + 2 * 4 * W["I"]
+    sh = 2 * (W["Is"] * W["H"] // 4) + 2 * 4 * W["Is"]
+    return float(touched * pe + sh + act_bytes(W) * T * W["H"]
+                 + 4 * (T * W["k"] * W["I"] + T * W["Is"]))
+
+
+def down_bytes(W, T, touched):
+    """The down GEMV (limbs of h first, weighted combine last): packed down
+    rows and scales, the f32 SwiGLU rows read, the output written."""
+    pe = W["H"] * W["I"] // 4 + 4 * W["H"]
+    sh = W["H"] * W["Is"] // 4 + 4 * W["H"]
+    return float(touched * pe + sh + 4 * (T * W["k"] * W["I"] + T * W["Is"])
+                 + act_bytes(W) * T * W["H"])
+
+
+def layer_flops(W, T):
+    H, I, Is, K, E = W["H"], W["I"], W["Is"], W["k"], W["E"]
+    gu = 2.0 * T * K * 2 * H * I + 2.0 * T * 2 * H * Is
+    dn = 2.0 * T * K * H * I + 2.0 * T * H * Is
+    return gu, dn, gu + dn + 2.0 * T * E * H
+
+
+def headline_config(W, ws, args):
+    """The `config` object of the JSON line (identical in both arms)."""
+    return {"workload": W["name"], "T_per_gpu": W["T"], "E": W["E"], "top_k": W["k"],
+            "hidden": W["H"], "intermediate": W["I"], "shared_intermediate": W["Is"],
+            "scoring": "sigmoid" if W["scoring"] == 1 else "softmax",
+            "n_group": W["n_group"], "topk_group": W["topk_group"],
+            "norm_topk_prob": W["norm_topk"], "routed_scaling_factor": W["routed_scale"],
+            "activations": W["act"], "parallelism": f"ep{ws}" if ws > 1 else "single",
+            "experts_per_gpu": W["E"] // ws,
+            "l2": "inputs larger than L2: every step streams the layer's packed weights "
+                  "(> 126 MB per GPU) from HBM"}
 
 
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle restatement of qmoe-rs's SIMD path)
 # ---------------------------------------------------------------------------
 
-def cpu_layer_inputs(seed: int):
-    experts, shared, gate_w = synth_weights(seed, "cpu")
-    ne = [[(p.numpy().reshape(-1), s.numpy()) for p, s in ex] for ex in experts]
-    ns = [(p.numpy().reshape(-1), s.numpy()) for p, s in shared]
-    return ne, ns, gate_w.numpy()
+def to_host_experts(experts, shared):
+    ne = [[(p.cpu().numpy().reshape(-1), s.cpu().numpy()) for p, s in ex] for ex in experts]
+    ns = [(p.cpu().numpy().reshape(-1), s.cpu().numpy()) for p, s in shared]
+    return ne, ns
 
 
-def time_cpu_oracle(ne, ns, gw, nthreads: int, tokens: int, min_seconds: float, seed: int):
+def time_cpu_oracle(W, ne, ns, gw, nthreads: int, tokens: int, min_seconds: float, seed: int):
     from oracle import oracle as qo
-    w = WORKLOAD
-    cfg = qo.MoEConfig(w["E"], w["k"], w["H"], w["I"], w["Is"], norm_topk_prob=w["norm_topk"])
-    x = np.random.default_rng(seed).standard_normal((tokens, w["H"])).astype(np.float32)
+    cfg = oracle_cfg(W)
+    x = np.random.default_rng(seed).standard_normal((tokens, W["H"])).astype(np.float32)
+    if W["act"] == "bf16":     # the bf16 activations the GPU arm reads, upcast exactly
+        x = torch.from_numpy(x).bfloat16().float().numpy()
     n = 0
     t0 = time.perf_counter()
     while True:
@@ -248,31 +354,41 @@ def time_cpu_oracle(ne, ns, gw, nthreads: int, tokens: int, min_seconds: float, 
 
 
 # ---------------------------------------------------------------------------
-# arms
+# reference arm
 # ---------------------------------------------------------------------------
 
 def run_reference(args):
     """qmoe-rs's CPU path on this host: the oracle restatement (qmoe-rs is
-    Rust and cannot be built here), all host threads, token-parallel."""
+    Rust and cannot be built here), all host threads, token-parallel, on a
+    bounded sample of the headline workload's tokens per step."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
+    W = WORKLOADS[args.workload]
     nthreads = os.cpu_count() or 1
-    ne, ns, gw = cpu_layer_inputs(args.seed)
+    # inputs (not timed): the seeded layer packed by quantize.py's arithmetic
+    # in plain torch (on a CUDA device when there is one, for speed)
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    experts, shared, gate_w = synth_weights(W, args.seed, dev, packer=torch_packer)
+    ne, ns = to_host_experts(experts, shared)
+    gw = gate_w.cpu().numpy()
+    del experts, shared, gate_w
+    if dev == "cuda":
+        torch.cuda.empty_cache()
     from oracle import oracle as qo
-    w = WORKLOAD
-    cfg = qo.MoEConfig(w["E"], w["k"], w["H"], w["I"], w["Is"], norm_topk_prob=w["norm_topk"])
-    tokens = min(w["T"], nthreads)
-    x = np.random.default_rng(args.seed).standard_normal((tokens, w["H"])).astype(np.float32)
+    cfg = oracle_cfg(W)
+    tokens = min(W["T"], max(nthreads, 8))
+    x = np.random.default_rng(args.seed).standard_normal((tokens, W["H"])).astype(np.float32)
+    if W["act"] == "bf16":
+        x = torch.from_numpy(x).bfloat16().float().numpy()
     t0 = time.perf_counter()
     qo.layer_forward(cfg, gw, ne, x, shared=ns, nthreads=nthreads)
     per_step = time.perf_counter() - t0
-    budget = 240.0
-    steps = args.steps
-    warm = args.warmup
+    budget = 120.0
+    steps, warm = args.steps, args.warmup
     if (steps + warm) * per_step > budget:
-        steps = max(1, int(budget / per_step) - min(warm, 3))
-        warm = min(warm, 3)
+        warm = min(warm, 2)
+        steps = max(3, int(budget / per_step) - warm)
     for _ in range(warm):
         qo.layer_forward(cfg, gw, ne, x, shared=ns, nthreads=nthreads)
     t0 = time.perf_counter()
@@ -280,25 +396,29 @@ def run_reference(args):
         qo.layer_forward(cfg, gw, ne, x, shared=ns, nthreads=nthreads)
     el = time.perf_counter() - t0
     value = steps * tokens / el
-    sample = (f"{tokens} tokens per step ({nthreads} threads, token-parallel) of the "
-              f"{w['T']}-token batch; {steps} steps timed")
+    sample = (f"{tokens} of the {W['T']} tokens per step ({nthreads} threads, token-parallel), "
+              f"{steps} steps timed")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "steps_run": steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * el / steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD["name"], "T": w["T"], "E": w["E"], "top_k": w["k"],
-                   "hidden": w["H"], "intermediate": w["I"], "shared_intermediate": w["Is"]},
+        "vs_baseline": None, "dtype": W["act"], "data": "synthetic",
+        "config": headline_config(W, max(ws, args.gpus), args),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "note": "qmoe-rs (Rust nightly + candle) cannot be built here; timed its C "
                 "restatement oracle/qmoe_oracle.c with the same per-token/per-expert loop "
-                "and f32x4 lane structure",
+                "and f32x4 lane structure (bf16 activations upcast exactly to f32, the "
+                "reference's only input type)",
     }
     print(json.dumps(line), flush=True)
 
+
+# ---------------------------------------------------------------------------
+# timing helpers (one GPU)
+# ---------------------------------------------------------------------------
 
 def graph_stage_times(layers, xs, stream, n_prof: int = 100):
     """Average per-stage device time (ms) of the forward from the layer's
@@ -320,6 +440,130 @@ def graph_stage_times(layers, xs, stream, n_prof: int = 100):
     return {k: float(np.mean(v)) for k, v in stage_ms.items()}
 
 
+def time_graphs(layers, xs, steps: int, warmup: int, clocks_dev=None):
+    """Forwards of the replicas back to back in one CUDA graph (as
+    consecutive MoE layers of a model would run), replayed; returns (ms per
+    forward, clock summary or None, stream)."""
+    reps = len(layers)
+    T = xs[0].shape[0]
+    for L in layers:
+        L.reserve(T)
+    stream = torch.cuda.Stream()
+    graphs = []
+    with torch.cuda.stream(stream):
+        for L, x in zip(layers, xs):
+            L.forward(x)
+        torch.cuda.current_stream().synchronize()
+        for L, x in zip(layers, xs):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                L.forward(x)
+            graphs.append(g)
+        chain = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(chain, stream=stream):
+            for L, x in zip(layers, xs):
+                L.forward(x)
+    torch.cuda.synchronize()
+    for i in range(max(3, warmup)):
+        graphs[i % reps].replay()
+    chain.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(clocks_dev) if clocks_dev is not None else None
+    if clk:
+        clk.__enter__()
+    e0.record()
+    for _ in range(steps // reps):
+        chain.replay()
+    for i in range(steps % reps):
+        graphs[i].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    if clk:
+        clk.__exit__()
+    ms = e0.elapsed_time(e1) / steps
+    del graphs, chain
+    return ms, (clk.summary() if clk else None), stream
+
+
+def e2e_host(layer, x_dev, n: int):
+    """Forward through the public API with page-locked host buffers: the
+    host->device copy of x and the device->host result inside every call."""
+    x_host = x_dev.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    for _ in range(3):
+        layer.forward(x_host, out=out_host)
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n):
+        layer.forward(x_host, out=out_host)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n
+
+
+def touched_experts(layer, x):
+    _, idx, _ = layer.forward(x, return_routing=True)
+    return int(len(np.unique(idx.cpu().numpy())))
+
+
+# ---------------------------------------------------------------------------
+# sub-lines (one GPU)
+# ---------------------------------------------------------------------------
+
+def run_decode_line(W, layers, xs, steps: int):
+    """A decode-sized batch on the one-GPU layer: HBM rooflines of the two
+    expert GEMVs and of the whole forward."""
+    T = xs[0].shape[0]
+    touched = touched_experts(layers[0], xs[0])
+    ms, _, stream = time_graphs(layers, xs, steps, 5)
+    stages = graph_stage_times(layers, xs, stream, n_prof=40)
+    hbm, _, peak_kind = load_peaks()
+    gu_b, dn_b, ly_b = gate_up_bytes(W, T, touched), down_bytes(W, T, touched), layer_bytes(W, T, touched)
+    gu_ms, dn_ms = stages.get("gate_up", float("nan")), stages.get("down", float("nan"))
+    launches = LAUNCHES["decode_front"] if T * W["E"] <= 4096 and T <= 64 else LAUNCHES["decode_router"]
+    return {
+        "value": T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "T": T, "dtype": W["act"],
+        "touched_experts": touched,
+        "roofline": {"bound": "hbm", "kernel": "decode GEMV gate/up + SwiGLU (x limbs first)",
+                     "achieved": gu_b / (gu_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": gu_b / (gu_ms / 1e3) / 1e9 / hbm, "peak_kind": peak_kind,
+                     "algorithmic_bytes": gu_b, "kernel_ms": gu_ms},
+        "roofline_down": {"bound": "hbm", "kernel": "decode GEMV down (h limbs first, combine last)",
+                          "achieved": dn_b / (dn_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                          "frac": dn_b / (dn_ms / 1e3) / 1e9 / hbm, "algorithmic_bytes": dn_b,
+                          "kernel_ms": dn_ms},
+        "layer": {"algorithmic_bytes": ly_b, "achieved_gbs": ly_b / (ms / 1e3) / 1e9,
+                  "frac": ly_b / (ms / 1e3) / 1e9 / hbm},
+        "stage_ms": stages, "gpu_launches_per_step": launches,
+    }
+
+
+def run_prefill_line(W, layers, xs, steps: int):
+    """A prefill-sized bf16 batch: tensor rooflines of the two expert GEMMs
+    and the whole forward."""
+    T = xs[0].shape[0]
+    ms, _, stream = time_graphs(layers, xs, steps, 3)
+    stages = graph_stage_times(layers, xs, stream, n_prof=10)
+    gu_f, dn_f, fl = layer_flops(W, T)
+    _, bf16, peak_kind = load_peaks()
+    gu_tf = gu_f / (stages["gate_up"] / 1e3) / 1e12
+    return {
+        "value": T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "T": T, "dtype": "bf16",
+        "tflops": fl / (ms / 1e3) / 1e12, "frac_layer": fl / (ms / 1e3) / 1e12 / bf16,
+        "algorithmic_flops": fl,
+        "roofline": {"bound": "tensor", "kernel": "qgemm_prefill gate/up + SwiGLU",
+                     "achieved": gu_tf, "peak": bf16, "unit": "TFLOP/s",
+                     "frac": gu_tf / bf16, "peak_kind": peak_kind, "kernel_ms": stages["gate_up"],
+                     "down_tflops": dn_f / (stages["down"] / 1e3) / 1e12,
+                     "down_frac": dn_f / (stages["down"] / 1e3) / 1e12 / bf16},
+        "stage_ms": stages, "gpu_launches_per_step": LAUNCHES["prefill"],
+    }
+
+
 PACK_ROWS = 64 * 1408      # the V2-Lite layer's 64 stacked gate matrices: [64 x 1408, 2048] f32
 
 
@@ -329,7 +573,7 @@ def run_pack(seed: int, dev: str, steps: int = 10):
     (> L2), scales computed.  Algorithmic bytes: the f32 read, the packed
     bytes and the scales written."""
     from qmoe_b200 import quantize as qz
-    H = WORKLOAD["H"]
+    H = V2["H"]
     g = torch.Generator(device=dev).manual_seed(seed + 313)
     wt = torch.randn(PACK_ROWS, H, generator=g, device=dev) * 0.02
     for _ in range(3):
@@ -354,85 +598,168 @@ def run_pack(seed: int, dev: str, steps: int = 10):
             "weights_per_s": PACK_ROWS * H / (ms / 1e3)}
 
 
-def run_prefill(layers, seed: int, dev: str, steps: int = 20):
-    """the same layer in prefill, 2048 bf16 tokens per forward
-    (tcgen05 bf16 GEMM path), CUDA graphs over the rotating replicas."""
-    w = WORKLOAD
-    T = 2048
-    g = torch.Generator(device=dev).manual_seed(seed + 99)
-    xs = [torch.randn(T, w["H"], generator=g, device=dev).bfloat16() for _ in layers]
-    for L in layers:
-        L.reserve(T)
-    stream = torch.cuda.Stream()
-    graphs = []
-    with torch.cuda.stream(stream):
-        for L, x in zip(layers, xs):
-            L.forward(x)
-        torch.cuda.current_stream().synchronize()
-        gr = torch.cuda.CUDAGraph()      # the replicas' forwards back to back
-        with torch.cuda.graph(gr, stream=stream):
-            for L, x in zip(layers, xs):
-                L.forward(x)
-        graphs.append(gr)
-    for i in range(3):
-        graphs[0].replay()
+def build_layers(W, seed, dev, ctx, reps):
+    from qmoe_b200 import QMoELayer
+    layers = []
+    keep = None
+    for r in range(reps):
+        experts, shared, gate_w = synth_weights(W, seed + 1000 * r, dev)
+        layers.append(QMoELayer(make_cfg(W), gate_w, experts, shared=shared, ctx=ctx))
+        if r == 0:
+            keep = (experts, shared, gate_w)
+        del experts, shared, gate_w
+    return layers, keep
+
+
+def replicas_for(W, per_gpu_bytes):
+    """Replicas needed so that consecutive forwards never find their weights in L2."""
+    return max(1, -(-4 * L2_BYTES // per_gpu_bytes)) if per_gpu_bytes < 4 * L2_BYTES else 1
+
+
+# ---------------------------------------------------------------------------
+# our arm, one GPU
+# ---------------------------------------------------------------------------
+
+def run_single(args, W, dev, local):
+    from qmoe_b200 import default_context
+    ctx = default_context(local)
+    T = W["T"]
+    all_bytes = W["E"] * per_expert_bytes(W) + shared_bytes(W)
+    reps = replicas_for(W, all_bytes)
+    layers, keep = build_layers(W, args.seed, dev, ctx, reps)
+    xs = [synth_x(W, T, args.seed + 7 * r, dev) for r in range(reps)]
     torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    steps = -(-steps // len(layers)) * len(layers)
-    a.record()
-    for i in range(steps // len(layers)):
-        graphs[0].replay()
-    b.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / steps
-    del graphs
-    stages = graph_stage_times(layers, xs, stream, n_prof=20)
-    H, I, Is, K, E = w["H"], w["I"], w["Is"], w["k"], w["E"]
-    flops = 2.0 * T * K * 3 * H * I + 2.0 * T * 3 * H * Is + 2.0 * T * E * H
-    gu_flops = 2.0 * T * K * 2 * H * I + 2.0 * T * 2 * H * Is
-    dn_flops = 2.0 * T * K * H * I + 2.0 * T * H * Is
-    _, bf16, peak_kind = load_peaks()
-    gu_tf = gu_flops / (stages["gate_up"] / 1e3) / 1e12
-    return {
-        "workload": "configs[2]: same layer, prefill, 2048 bf16 tokens",
-        "value": T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "dtype": "bf16",
-        "tflops": flops / (ms / 1e3) / 1e12, "algorithmic_flops": flops,
-        "roofline": {"bound": "tensor", "kernel": "qgemm_prefill gate/up + SwiGLU",
-                     "achieved": gu_tf, "peak": bf16, "unit": "TFLOP/s",
-                     "frac": gu_tf / bf16, "peak_kind": peak_kind,
-                     "traffic": read_profile_traffic("qgemm_prefill_gate_up_v2lite_t2048.txt"),
-                     "kernel_ms": stages["gate_up"],
-                     "down_tflops": dn_flops / (stages["down"] / 1e3) / 1e12},
-        "stage_ms": stages,
-        "gpu_launches_per_step": KERNELS_PER_PREFILL,
+    prefill = W["act"] == "bf16" and T * W["k"] // W["E"] >= 16
+    touched = touched_experts(layers[0], xs[0])
+
+    ms, clocks, stream = time_graphs(layers, xs, args.steps, args.warmup, clocks_dev=local)
+    value = T / (ms / 1e3)
+    stages = graph_stage_times(layers, xs, stream, n_prof=10 if prefill else 100)
+    e2e_ms = e2e_host(layers[0], xs[0], max(10, min(args.steps, 100 if prefill else 500)))
+    hbm, bf16, peak_kind = load_peaks()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": W["act"], "data": "synthetic",
+        "config": headline_config(W, 1, args),
     }
+    if prefill:
+        gu_f, dn_f, fl = layer_flops(W, T)
+        gu_tf = gu_f / (stages["gate_up"] / 1e3) / 1e12
+        dn_tf = dn_f / (stages["down"] / 1e3) / 1e12
+        line["roofline"] = {
+            "bound": "tensor", "kernel": "qgemm_prefill gate/up + SwiGLU (tcgen05, 2-bit dequant "
+                                         "in the pipeline)",
+            "achieved": gu_tf, "peak": bf16, "unit": "TFLOP/s", "frac": gu_tf / bf16,
+            "peak_kind": peak_kind, "traffic": read_profile_traffic("qgemm_prefill_gate_up_v3.txt"),
+            "algorithmic_flops": gu_f, "kernel_ms": stages["gate_up"],
+            "down_tflops": dn_tf, "down_frac": dn_tf / bf16}
+        line["layer"] = {"algorithmic_flops": fl, "tflops": fl / (ms / 1e3) / 1e12,
+                         "frac": fl / (ms / 1e3) / 1e12 / bf16, "stage_ms": stages,
+                         "touched_experts": touched}
+        launches = LAUNCHES["prefill"]
+    else:
+        gu_b = gate_up_bytes(W, T, touched)
+        ach = gu_b / (stages["gate_up"] / 1e3) / 1e9
+        line["roofline"] = {
+            "bound": "hbm", "kernel": "decode GEMV gate/up + SwiGLU (x limbs first)",
+            "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm, "peak_kind": peak_kind,
+            "traffic": read_profile_traffic("qgemv_gate_up_decode_v2lite_t32.txt"),
+            "algorithmic_bytes": gu_b, "kernel_ms": stages["gate_up"]}
+        lb = layer_bytes(W, T, touched)
+        line["layer"] = {"algorithmic_bytes": lb, "achieved_gbs": lb / (ms / 1e3) / 1e9,
+                         "frac": lb / (ms / 1e3) / 1e9 / hbm, "stage_ms": stages,
+                         "touched_experts": touched}
+        launches = LAUNCHES["decode_front"]
+    ab = act_bytes(W) * T * W["H"]
+    line["e2e"] = {"value": T / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": ab,
+                   "d2h_bytes_per_step": ab, "ms_per_step": e2e_ms,
+                   "path": "QMoELayer.forward -> qmoe_layer_forward with page-locked host x and out"}
+    line["gpu_launches"] = launches * args.steps
+    line["clocks"] = clocks
+
+    sub = {}
+    if not args.no_sublines:
+        if W is V3:
+            # the V3 layer in decode: 32 bf16 tokens through the GEMV path
+            xd = [synth_x(W, 32, args.seed + 11, dev)]
+            sub["decode_v3"] = dict(workload="configs[3] layer, decode, 32 bf16 tokens",
+                                    **run_decode_line(W, layers[:1], xd, 200))
+        del layers, xs
+        torch.cuda.empty_cache()
+        v2_layers, _ = build_layers(V2, args.seed, dev, ctx, 4)
+        xs2 = [synth_x(V2, 32, args.seed + 7 * r, dev) for r in range(4)]
+        sub["decode_v2lite"] = dict(workload=V2["name"], **run_decode_line(V2, v2_layers, xs2, 1000))
+        xp = [synth_x(dict(V2, act="bf16"), 2048, args.seed + 99 + r, dev) for r in range(4)]
+        sub["prefill_v2lite"] = dict(workload="configs[2]: the V2-Lite layer, prefill, 2048 bf16 "
+                                              "tokens", **run_prefill_line(V2, v2_layers, xp, 20))
+        del v2_layers, xs2, xp
+        torch.cuda.empty_cache()
+        sub["pack"] = run_pack(args.seed, dev)
+    line.update(sub)
+
+    if not args.no_cpu_baseline:
+        experts, shared, gate_w = keep
+        ne, ns = to_host_experts(experts, shared)
+        gw = gate_w.cpu().numpy()
+        ntok = 8 if W is V3 else W["T"]
+        v, n, el = time_cpu_oracle(W, ne, ns, gw, 1, ntok, 10.0, args.seed)
+        line["cpu_baseline"] = {
+            "value": v, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"{n} x {ntok} tokens of the {W['T']}-token batch on 1 thread, {el:.1f} s "
+                      "(C restatement of qmoe-rs's f32x4 SIMD path)"}
+    print(json.dumps(line), flush=True)
 
 
-def run_ep(args, ws, rank, local, dev, dist):
+# ---------------------------------------------------------------------------
+# our arm, N GPUs (expert parallel)
+# ---------------------------------------------------------------------------
+
+def run_ep(args, W, ws, rank, local, dev, dist):
     """N > 1: the layer expert-parallel over the N GPUs (each holds E/N
-    experts, a gate and shared-expert replica and its own 32 decode tokens),
+    experts, a gate and shared-expert replica and its own T tokens),
     dispatch and return by stores into the peers' memory (--ep-exchange p2p)
     or NCCL all-to-all.  Weak scaling: tokens per GPU fixed."""
-    from qmoe_b200 import ExpertParallelMoE, default_context
-    w = WORKLOAD
-    cfg = make_cfg()
-    epr = w["E"] // ws
+    from qmoe_b200 import ExpertParallelMoE, QMoELayer, default_context
+    cfg = make_cfg(W)
+    T = W["T"]
+    epr = W["E"] // ws
     mine = range(rank * epr, (rank + 1) * epr)
-    # enough replicas that one rank's weights exceed L2 between reuses
-    per_rank_bytes = epr * (3 * w["H"] * w["I"] // 4) + 3 * w["H"] * w["Is"] // 4
-    reps = max(REPLICAS, -(-4 * 126 * 2**20 // per_rank_bytes))
+    per_rank_bytes = epr * per_expert_bytes(W) + shared_bytes(W)
+    reps = replicas_for(W, per_rank_bytes)
     ctx = default_context(local)
+    dt = act_dtype(W)
     layers = []
     for r in range(reps):
-        experts, shared, gate_w = synth_weights(args.seed + 1000 * r, dev, experts=mine)
+        experts, shared, gate_w = synth_weights(W, args.seed + 1000 * r, dev, experts=mine)
         layers.append(ExpertParallelMoE(cfg, gate_w, experts, rank, ws, shared=shared, ctx=ctx,
-                                        capacity=w["T"], exchange=args.ep_exchange,
-                                        dtype=torch.float32))
-        del experts, shared
-    g = torch.Generator(device=dev).manual_seed(args.seed + 31 * rank)
-    xs = [torch.randn(w["T"], w["H"], generator=g, device=dev) for _ in range(reps)]
+                                        capacity=T, exchange=args.ep_exchange, dtype=dt))
+        del experts, shared, gate_w
+    xs = [synth_x(W, T, args.seed + 31 * rank + 7 * r, dev) for r in range(reps)]
     torch.cuda.synchronize()
+
+    # parity: the first eager forward of replica 0 against the whole layer on
+    # this GPU (same seeded weights, this rank's tokens)
+    out_ep, idx_ep, _ = layers[0].forward(xs[0], return_routing=True)
+    experts, shared, gate_w = synth_weights(W, args.seed, dev)
+    full = QMoELayer(cfg, gate_w, experts, shared=shared, ctx=ctx)
+    del experts, shared
+    out_1, idx_1, _ = full.forward(xs[0], return_routing=True)
+    torch.cuda.synchronize()
+    err = rel_err(out_ep.float().cpu().numpy(), out_1.float().cpu().numpy())
+    same_idx = bool(torch.equal(idx_ep, idx_1))
+    touched_local = int(((idx_1 >= rank * epr) & (idx_1 < (rank + 1) * epr)).sum().item())
+    full.close()
+    del full, out_1, idx_1, gate_w
+    torch.cuda.empty_cache()
+    tol = 2e-2 if W["act"] == "bf16" else 1e-4
+    pr = torch.tensor([err, 0.0 if same_idx else 1.0], device=dev, dtype=torch.float64)
+    dist.all_reduce(pr, op=dist.ReduceOp.MAX)
+    parity = {"ok": bool(pr[0].item() <= tol and pr[1].item() == 0.0), "max_rel_err": float(pr[0].item()),
+              "tolerance": tol, "routing_bit_exact": bool(pr[1].item() == 0.0),
+              "against": "the whole layer on one GPU, each rank's own tokens (first eager forward)"}
+
     for i in range(max(3, args.warmup)):
         layers[i % reps].forward(xs[i % reps])
     torch.cuda.synchronize()
@@ -458,7 +785,7 @@ def run_ep(args, ws, rank, local, dev, dist):
     dist.barrier()
     for i in range(max(3, args.warmup)):
         graphs[i % reps].replay()
-        chain.replay()
+    chain.replay()
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
@@ -481,12 +808,34 @@ def run_ep(args, ws, rank, local, dev, dist):
     t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = ws * w["T"] * args.steps / (ms_max / 1e3)
+    value = ws * T * args.steps / (ms_max / 1e3)
+    for gr in graphs:
+        del gr
+    graphs.clear()
+    del chain
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    # per-stage device times of this rank's forward (all ranks in step)
+    layers[0].layer.set_profiling(True)
+    st = {}
+    with torch.cuda.stream(stream):
+        for i in range(10):
+            dist.barrier()
+            layers[0].forward(xs[0])
+            for k, v in layers[0].layer.stage_times().items():
+                st.setdefault(k, []).append(v)
+    layers[0].layer.set_profiling(False)
+    st = {k: float(np.mean(v)) for k, v in st.items()}
+    names = {"router": "route_plan_dispatch", "permute": "wait_dispatch_permute", "quant_up": "gather_or_limbs"}
+    stages = {names.get(k, k): v for k, v in st.items()}
+    torch.cuda.synchronize()
+    dist.barrier()
 
     # end to end: pinned host tokens in, host result out, every step
     x_host = xs[0].cpu().pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
-    n_e2e = max(20, min(args.steps, 200))
+    n_e2e = max(10, min(args.steps, 50 if W["act"] == "bf16" else 200))
     for i in range(3):
         out_host.copy_(layers[0].forward(x_host.to(dev, non_blocking=True)), non_blocking=True)
     torch.cuda.synchronize()
@@ -502,33 +851,47 @@ def run_ep(args, ws, rank, local, dev, dist):
     t = torch.tensor([a.elapsed_time(b) / n_e2e], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
+    # routed assignments that land on each rank (imbalance) and the rows sent
+    cnt = torch.tensor([float(touched_local)], device=dev, dtype=torch.float64)
+    allc = [torch.zeros_like(cnt) for _ in range(ws)]
+    dist.all_gather(allc, cnt)
+    per_rank = [float(c.item()) for c in allc]
     if rank == 0:
+        prefill = W["act"] == "bf16" and T * W["k"] // W["E"] >= 16
+        gu_f, dn_f, fl = layer_flops(W, T)
+        _, bf16, peak_kind = load_peaks()
+        roof = None
+        if prefill and stages.get("gate_up"):
+            # this rank's expert pass: its share of the routed flops (from the
+            # routing of its own tokens, a stand-in for what it received) and
+            # its own tokens' shared expert
+            gu_tf = gu_f / (stages["gate_up"] / 1e3) / 1e12
+            roof = {"bound": "tensor", "kernel": "qgemm_prefill gate/up + SwiGLU (rank 0)",
+                    "achieved": gu_tf, "peak": bf16, "unit": "TFLOP/s", "frac": gu_tf / bf16,
+                    "peak_kind": peak_kind, "traffic": None, "kernel_ms": stages["gate_up"],
+                    "note": "flops of one GPU's worth of tokens (the weak-scaling share)"}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": w["name"], "T_per_gpu": w["T"], "E": w["E"],
-                       "top_k": w["k"], "hidden": w["H"], "intermediate": w["I"],
-                       "shared_intermediate": w["Is"], "activations": "f32",
-                       "parallelism": f"ep{ws}", "experts_per_gpu": epr,
-                       "exchange": ("peer-memory stores into the other GPUs' IPC-mapped buffers "
-                                    "(NVLink), arrival flags" if args.ep_exchange == "p2p"
-                                    else "NCCL all_to_all_single") + ", fixed-capacity rows",
-                       "l2": f"{reps} rotating weight replicas per GPU (> L2)",
-                       "graphs": f"one CUDA graph of the {reps} replicas' forwards back to back"},
-            "roofline": None,
-            "e2e": {"value": ws * w["T"] / (e2e_ms / 1e3), "unit": UNIT,
-                    "h2d_bytes_per_step": 4 * w["T"] * w["H"] * ws,
-                    "d2h_bytes_per_step": 4 * w["T"] * w["H"] * ws, "ms_per_step": e2e_ms},
-            "gpu_launches": KERNELS_PER_EP_FORWARD * args.steps,
+            "dtype": W["act"], "data": "synthetic",
+            "config": headline_config(W, ws, args),
+            "exchange": ("peer-memory stores into the other GPUs' IPC-mapped buffers (NVLink), "
+                         "arrival flags" if args.ep_exchange == "p2p" else "NCCL all_to_all_single")
+                        + ", fixed-capacity rows",
+            "replicas": reps,
+            "roofline": roof,
+            "parity": parity,
+            "stage_ms_rank0": stages,
+            "load": {"routed_assignments_per_rank": per_rank,
+                     "imbalance_max_over_mean": max(per_rank) / max(1e-9, float(np.mean(per_rank)))},
+            "e2e": {"value": ws * T / (e2e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": act_bytes(W) * T * W["H"] * ws,
+                    "d2h_bytes_per_step": act_bytes(W) * T * W["H"] * ws, "ms_per_step": e2e_ms},
+            "gpu_launches": (LAUNCHES["ep_prefill"] if prefill else LAUNCHES["ep_decode"]) * args.steps,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
-    for gr in graphs:
-        del gr
-    graphs.clear()
-    del chain
     torch.cuda.synchronize()
     dist.barrier()
     for L in layers:          # every rank is done with the others' buffers
@@ -541,164 +904,18 @@ def run_ours(args):
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = f"cuda:{local}"
-    dist = None
+    W = WORKLOADS[args.workload]
     if ws > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device(dev))
-        return run_ep(args, ws, rank, local, dev, dist)
-    from qmoe_b200 import QMoELayer, default_context
-    ctx = default_context(local)
-    cfg = make_cfg()
-    w = WORKLOAD
-
-    layers, xs = [], []
-    for r in range(REPLICAS):
-        experts, shared, gate_w = synth_weights(args.seed + 1000 * r + 17 * rank, dev)
-        layers.append(QMoELayer(cfg, gate_w, experts, shared=shared, ctx=ctx))
-        del experts, shared
-        g = torch.Generator(device=dev).manual_seed(args.seed + 7 * r + 31 * rank)
-        xs.append(torch.randn(w["T"], w["H"], generator=g, device=dev))
-    outs = [torch.empty_like(x) for x in xs]
-    torch.cuda.synchronize()
-
-    # routing of replica 0 (for the algorithmic byte count)
-    _, idx0, _ = layers[0].forward(xs[0], return_routing=True)
-    idx_np = idx0.cpu().numpy()
-
-    # warm-up (eager), then one CUDA graph per replica
-    for i in range(max(3, args.warmup)):
-        layers[i % REPLICAS].forward(xs[i % REPLICAS])
-    torch.cuda.synchronize()
-    for L in layers:
-        L.reserve(w["T"])
-    stream = torch.cuda.Stream()
-    graphs = []
-    with torch.cuda.stream(stream):
-        for r in range(REPLICAS):
-            layers[r].forward(xs[r])  # warm on the capture stream
-        torch.cuda.current_stream().synchronize()
-        for r in range(REPLICAS):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                outs[r] = layers[r].forward(xs[r])
-            graphs.append(g)
-        # the REPLICAS forwards back to back in one graph, as consecutive MoE
-        # layers of a decode step would run: each layer's first kernels
-        # overlap the previous one's tail (programmatic dependent launch)
-        chain = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(chain, stream=stream):
-            for r in range(REPLICAS):
-                outs[r] = layers[r].forward(xs[r])
-    torch.cuda.synchronize()
-    for i in range(max(3, args.warmup)):
-        graphs[i % REPLICAS].replay()
-        chain.replay()
-    torch.cuda.synchronize()
-
-    def replay_steps(n):
-        for _ in range(n // REPLICAS):
-            chain.replay()
-        for i in range(n % REPLICAS):
-            graphs[i].replay()
-
-    # timed region
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        e0.record()
-        replay_steps(args.steps)
-        e1.record()
-        torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    tokens = ws * w["T"] * args.steps
-    value = tokens / (ms_max / 1e3)
-
-    # live kernel timing: the same forward captured with stage events (event
-    # record nodes between the kernels on the launching stream), replayed
-    stage_avg = graph_stage_times(layers, xs, stream)
-
-    # end to end through the C ABI with pinned host buffers
-    x_host = xs[0].cpu().pin_memory()
-    out_host = torch.empty_like(x_host).pin_memory()
-    for _ in range(3):
-        layers[0].forward(x_host, out=out_host)
-    n_e2e = max(20, min(args.steps, 500))
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    a.record()
-    for i in range(n_e2e):
-        layers[0].forward(x_host, out=out_host)
-    b.record()
-    torch.cuda.synchronize()
-    e2e_ms = a.elapsed_time(b) / n_e2e
-    e2e = {"value": w["T"] * ws / (e2e_ms / 1e3), "unit": UNIT,
-           "h2d_bytes_per_step": 4 * w["T"] * w["H"], "d2h_bytes_per_step": 4 * w["T"] * w["H"],
-           "ms_per_step": e2e_ms}
-
-    prefill = run_prefill(layers, args.seed, dev) if ws == 1 else None
-    pack = run_pack(args.seed, dev) if ws == 1 else None
-
-    if rank == 0:
-        hbm, bf16, peak_kind = load_peaks()
-        gu_bytes = algorithmic_gate_up_bytes(idx_np)
-        gu_ms = stage_avg.get("gate_up", float("nan"))
-        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
-        traffic = read_profile_traffic()
-        layer_bytes = algorithmic_layer_bytes(idx_np)
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": w["name"], "T_per_gpu": w["T"], "E": w["E"],
-                       "top_k": w["k"], "hidden": w["H"], "intermediate": w["I"],
-                       "shared_intermediate": w["Is"], "activations": "f32",
-                       "parallelism": "replicas" if ws > 1 else "single",
-                       "l2": f"{REPLICAS} rotating weight replicas (> L2)",
-                       "graphs": f"one CUDA graph of the {REPLICAS} replicas' forwards back to back"},
-            "roofline": {"bound": "hbm", "kernel": "qgemv gate/up + SwiGLU",
-                         "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "peak_kind": peak_kind,
-                         "traffic": traffic, "algorithmic_bytes": gu_bytes,
-                         "kernel_ms": gu_ms},
-            "layer": {"stage_ms": stage_avg, "algorithmic_bytes": layer_bytes,
-                      "achieved_gbs_per_step": layer_bytes / (ms_max / args.steps / 1e3) / 1e9},
-            "e2e": e2e,
-            "prefill": prefill,
-            "pack": pack,
-            "gpu_launches": KERNELS_PER_FORWARD * args.steps,
-            "clocks": clk.summary(),
-        }
-        if ws == 1 and not args.no_cpu_baseline:
-            ne, ns, gw = cpu_layer_inputs(args.seed)
-            v, n, el = time_cpu_oracle(ne, ns, gw, 1, w["T"], 10.0, args.seed)
-            line["cpu_baseline"] = {
-                "value": v, "unit": UNIT, "cores": 1, "kind": "port",
-                "sample": f"{n} x full {w['T']}-token batch on 1 thread, {el:.1f} s "
-                          "(C restatement of qmoe-rs's f32x4 SIMD path)"}
-        print(json.dumps(line), flush=True)
-    for g in graphs:
-        del g
-    graphs.clear()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+        return run_ep(args, W, ws, rank, local, dev, dist)
+    return run_single(args, W, dev, local)
 
 
 def run_ncu_case(args):
-    """A short fixed workload for ncu captures (one replica, 3 forwards)."""
+    """A short fixed workload for ncu captures (one layer, 3 forwards)."""
     from qmoe_b200 import QMoELayer, default_context
     torch.cuda.set_device(0)
     if args.ncu_case == "pack":
@@ -706,19 +923,25 @@ def run_ncu_case(args):
         # no other launch of the packer before them
         from qmoe_b200 import quantize as qz
         g = torch.Generator(device="cuda").manual_seed(args.seed + 313)
-        wt = torch.randn(16 * 1408, WORKLOAD["H"], generator=g, device="cuda") * 0.02
+        wt = torch.randn(16 * 1408, V2["H"], generator=g, device="cuda") * 0.02
         for _ in range(3):
             qz.device_quantize(wt)
         torch.cuda.synchronize()
         return
-    experts, shared, gate_w = synth_weights(args.seed, "cuda")
-    layer = QMoELayer(make_cfg(), gate_w, experts, shared=shared, ctx=default_context(0))
-    del experts, shared
-    g = torch.Generator(device="cuda").manual_seed(args.seed + 7)
-    if args.ncu_case == "decode":
-        x = torch.randn(WORKLOAD["T"], WORKLOAD["H"], generator=g, device="cuda")
+    if args.ncu_case.startswith("v3"):
+        # v3-prefill: 32 experts of the V3 shape (353 MB of packed weights)
+        # and 512 bf16 tokens, i.e. ~128 tokens per expert as in configs[3];
+        # v3-decode: the whole V3 layer (2.85 GB) over 32 bf16 tokens
+        W = dict(V3, E=32, n_group=8, topk_group=4) if args.ncu_case == "v3-prefill" else V3
+        T = 512 if args.ncu_case == "v3-prefill" else 32
     else:
-        x = torch.randn(2048, WORKLOAD["H"], generator=g, device="cuda").bfloat16()
+        W, T = V2, (32 if args.ncu_case == "decode" else 2048)
+        if args.ncu_case == "prefill":
+            W = dict(V2, act="bf16")
+    experts, shared, gate_w = synth_weights(W, args.seed, "cuda")
+    layer = QMoELayer(make_cfg(W), gate_w, experts, shared=shared, ctx=default_context(0))
+    del experts, shared
+    x = synth_x(W, T, args.seed + 7, "cuda")
     for _ in range(3):
         layer.forward(x)
     torch.cuda.synchronize()

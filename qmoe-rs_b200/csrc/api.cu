@@ -110,10 +110,7 @@ constexpr int64_t kPrefillMinRows = 16;
 
 // A kernel whose bounded wait timed out leaves a flag in device memory; report
 // (and clear) it at the next host synchronisation point.
-int *error_flag() {
-    static int *flag = qmoe::device_error_flag();
-    return flag;
-}
+int *error_flag() { return qmoe::device_error_flag(); }   // the current device's word
 
 int check_device_error() {
     int *flag = error_flag();
@@ -211,6 +208,7 @@ struct qmoe_layer {
     struct {
         const void *x = nullptr;
         const void *out = nullptr;
+        const void *x_in = nullptr;   // the device copy of x the captured kernels read
         int64_t T = 0, cap = 0;
         int dtype = -1, path = -1, calls = 0;
         cudaGraphExec_t exec = nullptr;
@@ -1191,8 +1189,11 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
     // a repeat of the last call replays its captured graph
     if (x_mapped && out_mapped && !topk_idx && !topk_w && !L->profiling) {
         auto &G = L->fg;
+        // every buffer the captured kernels touch is part of the key: the
+        // scratch through cap (only layer_reserve reallocates it) and the
+        // device copy of x, which other host-pointer calls may reallocate
         const bool same = G.x == x && G.out == out && G.T == T && G.dtype == dtype && G.path == L->path &&
-                          G.cap == L->cap;
+                          G.cap == L->cap && G.x_in == L->x_in.p;
         if (!same) {
             if (G.exec) cudaGraphExecDestroy(G.exec);
             G.exec = nullptr;
@@ -1200,6 +1201,7 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
             G.out = out;
             G.T = T;
             G.cap = L->cap;
+            G.x_in = L->x_in.p;
             G.dtype = dtype;
             G.path = L->path;
             G.calls = 0;

@@ -433,17 +433,12 @@ template <int N>
 static cudaError_t launch_front_n(const RouterParams &p, const FrontParams &f, int cs, int lc, size_t smem,
                                   cudaStream_t s) {
     auto kern = front_cluster_kernel<N>;
-    static size_t smem_set = 0;
-    static bool np_set = false;
-    if (smem > smem_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(kern), smem);
+    if (e != cudaSuccess) return e;
+    if (cs > 8) {
+        // per-device attribute, idempotent
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
-        smem_set = smem;
-    }
-    if (cs > 8 && !np_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-        np_set = true;
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)cs);
@@ -471,7 +466,7 @@ static int front_max_cluster(size_t smem) {
             cudaGetLastError();
             continue;
         }
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        if (ensure_dyn_smem(reinterpret_cast<const void *>(kern), smem) != cudaSuccess) {
             cudaGetLastError();
             return 0;
         }

@@ -228,8 +228,13 @@ cudaError_t launch_ep_wait(const EpPeerDev &d, int phase, cudaStream_t s);
 cudaError_t launch_ep_finish(const EpPeerDev &d, const int32_t *slot_pos, int64_t T, const void *extra,
                              void *out, cudaStream_t s);
 
-// Device-side error word (device_state.cu) raised by a bounded wait that gives up.
+// Device-side error word (device_state.cu) raised by a bounded wait that gives
+// up: its address on the current device.
 int *device_error_flag();
+
+// Host: raise `func`'s dynamic shared-memory opt-in on the current device to
+// at least `bytes` (never lowers it; remembered per kernel and device).
+cudaError_t ensure_dyn_smem(const void *func, size_t bytes);
 
 // Host: a 2-D uint8 tensor map over [rows][row_bytes] with the given box and
 // swizzle (CU_TENSOR_MAP_SWIZZLE_*); returns false if encoding fails.

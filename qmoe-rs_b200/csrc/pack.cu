@@ -312,16 +312,8 @@ cudaError_t launch_pack_rows(const PackParams &p, int sm_count, cudaStream_t s) 
         // 220 KB); CTAs per SM as the shared memory allows, at most 2
         const int depth = 24 * row_bytes <= 220 * 1024 ? 3 : 2;
         const size_t smem = (size_t)kPackWarps * depth * row_bytes;
-        static bool attr_w[64] = {};
-        int dev = 0;
-        cudaError_t e = cudaGetDevice(&dev);
+        cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(pack_rows_warp), smem);
         if (e != cudaSuccess) return e;
-        if (dev < 0 || dev >= 64 || !attr_w[dev]) {
-            e = cudaFuncSetAttribute(pack_rows_warp, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)(kPackWarps * 2 * kPackWarpRowMax * sizeof(float)));
-            if (e != cudaSuccess) return e;
-            if (dev >= 0 && dev < 64) attr_w[dev] = true;
-        }
         int64_t per_sm = (int64_t)(228 * 1024) / (int64_t)(smem + 1024 + 256);
         per_sm = per_sm > 2 ? 2 : (per_sm < 1 ? 1 : per_sm);
         const int64_t warps = (rows + kPackWarps - 1) / kPackWarps;
@@ -330,17 +322,8 @@ cudaError_t launch_pack_rows(const PackParams &p, int sm_count, cudaStream_t s) 
         return launch_pdl(pack_rows_warp, dim3((unsigned)grid), dim3(kPackThreads), smem, s, p, depth);
     }
     if (row_bytes <= kPackStageMax) {
-        // the attribute is per device: set once for each device used
-        static bool attr[64] = {};
-        int dev = 0;
-        cudaError_t e = cudaGetDevice(&dev);
+        cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(pack_rows_staged), 2 * row_bytes);
         if (e != cudaSuccess) return e;
-        if (dev < 0 || dev >= 64 || !attr[dev]) {
-            e = cudaFuncSetAttribute(pack_rows_staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)(2 * kPackStageMax));
-            if (e != cudaSuccess) return e;
-            if (dev >= 0 && dev < 64) attr[dev] = true;
-        }
         int64_t per_sm = (int64_t)(228 * 1024) / (int64_t)(2 * row_bytes + 1024 + 256);
         per_sm = per_sm > kPackCtasPerSm ? kPackCtasPerSm : (per_sm < 1 ? 1 : per_sm);
         const int64_t wave = (int64_t)sm_count * per_sm;

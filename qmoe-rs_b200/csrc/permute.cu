@@ -200,14 +200,8 @@ size_t permute_smem_bytes(int e_count) {
 
 cudaError_t launch_permute(const PermuteParams &p, cudaStream_t s) {
     size_t smem = permute_smem_bytes(p.e_count);
-    static size_t smem_set = 0;  // raise the opt-in limit only when needed
-    if (smem > smem_set) {
-        cudaError_t e = cudaFuncSetAttribute(permute_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        smem_set = smem;
-    }
+    cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(permute_kernel), smem);
+    if (e != cudaSuccess) return e;
     // without routed assignments (K = 0) only the shared groups are written
     const unsigned grid = (unsigned)(p.T > 0 && p.K > 0 ? (p.T + kPermTok - 1) / kPermTok : 1);
     return launch_pdl(permute_kernel, dim3(grid), dim3(kPermThreads), smem, s, p);

@@ -486,14 +486,9 @@ size_t qgemm_prefill_smem_bytes() {
 cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmParams &p, int grid,
                                  cudaStream_t s) {
     const size_t smem = qgemm_prefill_smem_bytes();
-    static bool attr_set[2] = {false, false};
-    if (!attr_set[mode]) {
-        cudaError_t e = mode == 0
-            ? cudaFuncSetAttribute(qgemm_prefill_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-            : cudaFuncSetAttribute(qgemm_prefill_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr_set[mode] = true;
-    }
+    cudaError_t e = mode == 0 ? ensure_dyn_smem(reinterpret_cast<const void *>(qgemm_prefill_kernel<0>), smem)
+                              : ensure_dyn_smem(reinterpret_cast<const void *>(qgemm_prefill_kernel<1>), smem);
+    if (e != cudaSuccess) return e;
     return mode == 0 ? launch_pdl(qgemm_prefill_kernel<0>, dim3(grid), dim3(kThreads), smem, s, maps.w0,
                                   maps.w1, maps.s0, maps.s1, maps.b, maps.b2, p)
                      : launch_pdl(qgemm_prefill_kernel<1>, dim3(grid), dim3(kThreads), smem, s, maps.w0,

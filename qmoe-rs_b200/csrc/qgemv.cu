@@ -303,27 +303,25 @@ int qgemv_max_grid(int mode, int K_max) {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const size_t smem = qgemv_smem_bytes(K_max);
+    // only ever raises the kernel's opt-in (a smaller K_max here must not
+    // lower the limit an earlier, wider tensor's launches rely on)
     if (mode == 0) {
-        cudaFuncSetAttribute(qgemv_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ensure_dyn_smem(reinterpret_cast<const void *>(qgemv_kernel<0>), smem);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, qgemv_kernel<0>, kThreads, smem);
     } else {
-        cudaFuncSetAttribute(qgemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ensure_dyn_smem(reinterpret_cast<const void *>(qgemv_kernel<1>), smem);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, qgemv_kernel<1>, kThreads, smem);
     }
+    cudaGetLastError();
     if (per < 1) per = 1;
     return sms * per;
 }
 
 cudaError_t launch_qgemv(int mode, const QgemvParams &p, int grid, cudaStream_t s) {
     const size_t smem = qgemv_smem_bytes(p.ws[0] && p.K_s > p.K ? p.K_s : p.K);
-    static size_t smem_set[2] = {0, 0};  // raise the opt-in limit only when needed
-    if (smem > smem_set[mode]) {
-        cudaError_t e = mode == 0
-            ? cudaFuncSetAttribute(qgemv_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-            : cudaFuncSetAttribute(qgemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        smem_set[mode] = smem;
-    }
+    cudaError_t e = mode == 0 ? ensure_dyn_smem(reinterpret_cast<const void *>(qgemv_kernel<0>), smem)
+                              : ensure_dyn_smem(reinterpret_cast<const void *>(qgemv_kernel<1>), smem);
+    if (e != cudaSuccess) return e;
     if (mode == 0)
         qgemv_kernel<0><<<grid, kThreads, smem, s>>>(p);
     else

@@ -610,14 +610,9 @@ int qgemv_imma_buffers(int kp_b) {
 cudaError_t launch_qgemv_imma(int mode, const DecodeMaps &maps, const DecodeParams &p, int grid,
                               cudaStream_t s) {
     const size_t smem = qgemv_imma_smem_bytes(p.kp_b, p.b_buffers);
-    static size_t smem_set[2] = {0, 0};
-    if (smem > smem_set[mode]) {
-        cudaError_t e = mode == 0
-            ? cudaFuncSetAttribute(qgemv_imma_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-            : cudaFuncSetAttribute(qgemv_imma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        smem_set[mode] = smem;
-    }
+    cudaError_t e = mode == 0 ? ensure_dyn_smem(reinterpret_cast<const void *>(qgemv_imma_kernel<0>), smem)
+                              : ensure_dyn_smem(reinterpret_cast<const void *>(qgemv_imma_kernel<1>), smem);
+    if (e != cudaSuccess) return e;
     const bool coop = p.quant_in || p.combine;
     return mode == 0 ? launch_pdl_coop(qgemv_imma_kernel<0>, dim3(grid), dim3(kThreads), smem, s, coop, maps, p)
                      : launch_pdl_coop(qgemv_imma_kernel<1>, dim3(grid), dim3(kThreads), smem, s, coop, maps, p);

@@ -539,24 +539,14 @@ cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaSt
     if (e != cudaSuccess) return e;
     if (!f.counter && p.E <= 256 && p.K <= 32) {
         const size_t wsmem = sizeof(float) * kSelWarps * sel_warp_floats(p.E);
-        static size_t wsmem_set = 0;
-        if (wsmem > wsmem_set) {
-            e = cudaFuncSetAttribute(router_select_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)wsmem);
-            if (e != cudaSuccess) return e;
-            wsmem_set = wsmem;
-        }
+        e = ensure_dyn_smem(reinterpret_cast<const void *>(router_select_warp_kernel), wsmem);
+        if (e != cudaSuccess) return e;
         return launch_pdl(router_select_warp_kernel, dim3((unsigned)((p.T + kSelWarps - 1) / kSelWarps)),
                           dim3(kSelWarps * 32), wsmem, s, p, parts ? 1 : 0);
     }
     const size_t smem = router_smem_bytes(p.H, p.E);
-    static size_t smem_set = 0;  // raise the opt-in limit only when needed
-    if (smem > smem_set) {
-        e = cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem);
-        if (e != cudaSuccess) return e;
-        smem_set = smem;
-    }
+    e = ensure_dyn_smem(reinterpret_cast<const void *>(router_select_kernel), smem);
+    if (e != cudaSuccess) return e;
     return launch_pdl(router_select_kernel, dim3((unsigned)p.T), dim3(kRouterThreads), smem, s, p,
                       parts ? 1 : 0, f);
 }

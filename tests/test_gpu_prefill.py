@@ -113,14 +113,21 @@ def test_prefill_v2_lite_shape_matches_oracle():
 
 def test_prefill_full_configs2_agrees_with_exact_path():
     # configs[2] at full size (2048 bf16 tokens): the prefill GEMM against
-    # the exact integer-limb path on the same input (size-independent check)
+    # the exact integer-limb path on the same input (size-independent check),
+    # and against the oracle on a seeded sample of the batch's tokens (each
+    # token's output row depends on that token alone)
     cfg = MoEConfig(64, 6, 2048, 1408, shared_intermediate_dim=2816)
-    layer, *_ = build(cfg, seed=4242)
+    layer, np_exp, np_sh, gw = build(cfg, seed=4242)
     x = torch.randn(2048, 2048, generator=torch.Generator().manual_seed(11)).bfloat16()
     out_p, idx_p, out_d, idx_d = run_both_paths(layer, x)
     np.testing.assert_array_equal(idx_p, idx_d)
     assert rel_err(out_p, out_d) <= BF16_TOL
     assert np.isfinite(out_p).all()
+    sample = np.sort(np.random.default_rng(12).choice(2048, 48, replace=False))
+    ro, ri, _ = qo.layer_forward(qo_cfg(cfg), gw, np_exp, x[sample].float().numpy(), shared=np_sh,
+                                 nthreads=NTHREADS)
+    np.testing.assert_array_equal(idx_p[sample], ri)
+    assert rel_err(out_p[sample], ro) <= BF16_TOL
 
 
 def test_prefill_auto_selects_and_is_deterministic():
