@@ -129,9 +129,12 @@ QMOE_API int qmoe_ctx_synchronize(qmoe_ctx *ctx);
 
 /* PackedQMoETensor::from_bytes (src/tensor.rs:47-53) and the data half of
  * ::mmap_from_file (:27-43): copy `packed` ([out_features, in_features/4]
- * bytes) and `scales` ([out_features] f32) to device memory owned by the
- * returned handle.  in_features must be a positive multiple of 64 (rows of
- * a multiple of 16 bytes, the width of one 128-bit load). */
+ * bytes, in_features/4 rounded down as src/tensor.rs:74 does) and `scales`
+ * ([out_features] f32) to device memory owned by the returned handle.  Any
+ * positive in_features is accepted; rows whose width is not a multiple of 64
+ * are kept padded with zero weights on the device (their activations are
+ * staged into padded rows on each forward), and the in_features % 4
+ * trailing activations of a row are never read (src/simd.rs:15). */
 QMOE_API int qmoe_packed_create(qmoe_ctx *ctx, const uint8_t *packed, const float *scales,
                        int64_t out_features, int64_t in_features, int ptr_kind,
                        qmoe_packed **out);
@@ -142,7 +145,9 @@ QMOE_API int qmoe_packed_shape(const qmoe_packed *t, int64_t *out_features,
 
 /* PackedQMoETensor::forward_simd / forward_simd_raw (src/tensor.rs:64-95,
  * :99-121): y[b, o] = scale[o] * sum_k (code[o,k] - 1) * x[b, k] for
- * x [batch, in_features] f32, y [batch, out_features] f32. */
+ * x [batch, in_features] f32, y [batch, out_features] f32, k over the first
+ * 4 * (in_features / 4) elements of a row.  Device x must be 16-byte aligned
+ * when in_features is a multiple of 64. */
 QMOE_API int qmoe_packed_forward(qmoe_packed *t, const float *x, int64_t batch, float *y,
                         int ptr_kind);
 
@@ -171,13 +176,18 @@ QMOE_API int qmoe_quantize_pack(qmoe_ctx *ctx, const float *w, int64_t out_featu
 /*
  * QMoELayer::new (src/moe.rs:31-37) plus the layer's optional SharedExpert
  * (src/model.rs:318-348).
- *   gate_weight  [num_experts, hidden_dim] f32 (QMoELayer.gate_weight)
+ *   gate_weight  [num_experts, hidden_dim] f32 (QMoELayer.gate_weight);
+ *                may be NULL when expert_count is 0
  *   bias         [num_experts] f32 selection bias, or NULL (has_bias = 0)
  *   experts      expert_count entries: experts expert_begin ..
  *                expert_begin + expert_count - 1 (QMoELayer.experts).
  *                A single-process layer passes expert_begin = 0 and
  *                expert_count = num_experts; an expert-parallel rank passes
- *                the contiguous range it owns.
+ *                the contiguous range it owns.  expert_count 0 is qmoe-rs's
+ *                empty `experts` (src/moe.rs:46-48; a flattened layer,
+ *                src/loader.rs:452-456): the forward is the shared expert
+ *                alone, or zeros without one, and the routing outputs read
+ *                -1 / 0; the routing entry points reject such a layer.
  *   shared       the shared expert, or NULL
  * All weight pointers are of `ptr_kind`; they are copied, not retained.
  */

@@ -160,6 +160,11 @@ struct qmoe_ctx {
 struct qmoe_packed {
     qmoe_ctx *ctx = nullptr;
     int64_t out_f = 0, in_f = 0;
+    // Rows whose width is not a multiple of 64 codes are stored padded to
+    // k_pad codes (padding code 1 = weight 0) and their activations staged
+    // into rows of k_pad f32 whose padding stays zero; the GEMV then runs
+    // on whole 64-code blocks.  k_pad == in_f for widths it takes directly.
+    int64_t k_pad = 0;
     uint8_t *w = nullptr;
     float *s = nullptr;
     DevBuf groups, ngroups, x, y;
@@ -274,14 +279,16 @@ int qmoe_ctx_synchronize(qmoe_ctx *ctx) {
 int qmoe_packed_create(qmoe_ctx *ctx, const uint8_t *packed, const float *scales,
                        int64_t out_features, int64_t in_features, int ptr_kind,
                        qmoe_packed **out) {
-    if (!ctx || !packed || !scales || !out) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (!ctx || !scales || !out) return fail(QMOE_ERR_INVALID, "NULL argument");
     QTRY(check_ptr_kind(ptr_kind));
     *out = nullptr;
-    if (out_features <= 0 || in_features <= 0 || in_features % 64 != 0)
-        return fail(QMOE_ERR_INVALID,
-                    "shape (%lld, %lld): out_features must be > 0 and in_features a "
-                    "positive multiple of 64",
+    // src/tensor.rs:74: a row is in_features / 4 bytes; the in_features % 4
+    // trailing activations of a row are never read (src/simd.rs:15)
+    const int64_t bpr = in_features / 4;
+    if (out_features <= 0 || in_features <= 0)
+        return fail(QMOE_ERR_INVALID, "shape (%lld, %lld): both dimensions must be > 0",
                     (long long)out_features, (long long)in_features);
+    if (bpr > 0 && !packed) return fail(QMOE_ERR_INVALID, "NULL argument");
     if (in_features > (1 << 20) || out_features > (1LL << 31))
         return fail(QMOE_ERR_UNSUPPORTED, "shape too large");
     DeviceGuard g(ctx->device);
@@ -290,10 +297,20 @@ int qmoe_packed_create(qmoe_ctx *ctx, const uint8_t *packed, const float *scales
     t->ctx = ctx;
     t->out_f = out_features;
     t->in_f = in_features;
-    const size_t wb = (size_t)out_features * (in_features / 4);
+    t->k_pad = in_features % 64 == 0 ? in_features : (4 * bpr + 63) / 64 * 64;
+    if (t->k_pad == 0) t->k_pad = 64;
+    const size_t wb = (size_t)out_features * (t->k_pad / 4);
     cudaError_t e = cudaMalloc(&t->w, wb);
     if (e == cudaSuccess) e = cudaMalloc(&t->s, sizeof(float) * out_features);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(t->w, packed, wb, kind_in(ptr_kind), ctx->stream);
+    if (e == cudaSuccess && t->k_pad == in_features) {
+        e = cudaMemcpyAsync(t->w, packed, wb, kind_in(ptr_kind), ctx->stream);
+    } else if (e == cudaSuccess) {
+        // padded rows: fill with code 1 (weight 0), then the bpr bytes of each row
+        e = cudaMemsetAsync(t->w, 0x55, wb, ctx->stream);
+        if (e == cudaSuccess && bpr > 0)
+            e = cudaMemcpy2DAsync(t->w, (size_t)(t->k_pad / 4), packed, (size_t)bpr, (size_t)bpr,
+                                  (size_t)out_features, kind_in(ptr_kind), ctx->stream);
+    }
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(t->s, scales, sizeof(float) * out_features, kind_in(ptr_kind), ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
@@ -302,7 +319,7 @@ int qmoe_packed_create(qmoe_ctx *ctx, const uint8_t *packed, const float *scales
         return fail(e == cudaErrorMemoryAllocation ? QMOE_ERR_NOMEM : QMOE_ERR_CUDA,
                     "packed upload failed: %s", cudaGetErrorString(e));
     }
-    t->grid = qgemv_max_grid(1, (int)in_features);
+    t->grid = qgemv_max_grid(1, (int)t->k_pad);
     *out = t;
     return QMOE_OK;
 }
@@ -333,7 +350,8 @@ int qmoe_packed_forward(qmoe_packed *t, const float *x, int64_t batch, float *y,
     QTRY(check_ptr_kind(ptr_kind));
     if (batch < 0) return fail(QMOE_ERR_INVALID, "batch < 0");
     if (batch == 0) return QMOE_OK;
-    QTRY(check_align(x, ptr_kind, "x"));
+    const bool padded = t->k_pad != t->in_f;
+    if (!padded) QTRY(check_align(x, ptr_kind, "x"));
     qmoe_ctx *ctx = t->ctx;
     DeviceGuard g(ctx->device);
     cudaStream_t st = ctx->stream;
@@ -342,7 +360,22 @@ int qmoe_packed_forward(qmoe_packed *t, const float *x, int64_t batch, float *y,
     QTRY(grow(t->ngroups, sizeof(int32_t) * 4));
     const float *xd = x;
     float *yd = y;
-    if (ptr_kind == QMOE_PTR_HOST) {
+    if (padded) {
+        // rows of k_pad f32: the 4 * (in/4) activations a row uses, then
+        // zeros (written once per allocation; the copies never touch them)
+        const void *before = t->x.p;
+        QTRY(grow(t->x, sizeof(float) * batch * t->k_pad));
+        if (t->x.p != before) QTRY_CUDA(cudaMemsetAsync(t->x.p, 0, t->x.n, st));
+        const int64_t used = 4 * (t->in_f / 4);
+        if (used > 0)
+            QTRY_CUDA(cudaMemcpy2DAsync(t->x.p, sizeof(float) * t->k_pad, x, sizeof(float) * t->in_f,
+                                        sizeof(float) * used, (size_t)batch, kind_in(ptr_kind), st));
+        xd = t->x.as<float>();
+        if (ptr_kind == QMOE_PTR_HOST) {
+            QTRY(grow(t->y, sizeof(float) * batch * t->out_f));
+            yd = t->y.as<float>();
+        }
+    } else if (ptr_kind == QMOE_PTR_HOST) {
         QTRY(grow(t->x, sizeof(float) * batch * t->in_f));
         QTRY(grow(t->y, sizeof(float) * batch * t->out_f));
         QTRY_CUDA(cudaMemcpyAsync(t->x.p, x, sizeof(float) * batch * t->in_f,
@@ -370,14 +403,14 @@ int qmoe_packed_forward(qmoe_packed *t, const float *x, int64_t batch, float *y,
     q.groups = t->groups.as<int4>();
     q.n_groups = t->ngroups.as<int32_t>();
     q.rows = 0;
-    q.K = (int)t->in_f;
+    q.K = (int)t->k_pad;
     q.ws[0] = t->w;
     q.ss[0] = t->s;
     q.rows_s = (int)t->out_f;
-    q.K_s = (int)t->in_f;
+    q.K_s = (int)t->k_pad;
     q.act = xd;
     q.act_dtype = 0;
-    q.act_ld = t->in_f;
+    q.act_ld = padded ? t->k_pad : t->in_f;
     q.pos_tok = nullptr;
     q.shared_base = 0;
     q.out = yd;
@@ -523,18 +556,67 @@ static int layer_alloc_copy(void **dst, const void *src, size_t bytes, int kind,
     return QMOE_OK;
 }
 
+static int shared_pass(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out, int accumulate,
+                       int ptr_kind);
+
+// A layer without routed experts: the expert-side tensor maps are made over
+// the shared expert's matrices (valid descriptors that no routed item ever
+// reads, since no routed segment exists), or left unset without a shared
+// expert (the forward then writes zeros and launches nothing).
+static int empty_layer_maps(qmoe_layer *L) {
+    const qmoe_moe_config &c = L->cfg;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    QTRY_CUDA(cudaDeviceGetAttribute(&L->sm_count, cudaDevAttrMultiProcessorCount, dev));
+    int coop = 0;
+    QTRY_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+    L->coop = coop != 0;
+    if (!L->has_shared) return QMOE_OK;
+    const int64_t H = c.hidden_dim, Is = c.shared_intermediate_dim;
+    const int64_t srows[3] = {Is, Is, H}, skin[3] = {H, H, Is};
+    for (int m = 0; m < 3; ++m) {
+        if (!make_tmap_u8(&L->tm_ws[m], L->ws[m], (uint64_t)(skin[m] / 4), (uint64_t)srows[m], 64, 128,
+                          CU_TENSOR_MAP_SWIZZLE_64B))
+            return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for shared matrix %d", m);
+        L->tm_ws3[m] = L->tm_ws[m];
+        if (skin[m] / 256 >= 2 &&
+            !make_tmap_u8_3d(&L->tm_ws3[m], L->ws[m], 64, (uint64_t)srows[m], (uint64_t)(skin[m] / 256),
+                             (uint64_t)(skin[m] / 4), 64, 64, 128, 2, CU_TENSOR_MAP_SWIZZLE_64B))
+            return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed for shared matrix %d", m);
+        L->tm_w[m] = L->tm_ws[m];
+        L->tm_w3[m] = L->tm_ws3[m];
+    }
+    L->prefill_ok = H % 128 == 0 && Is % 64 == 0;
+    if (L->prefill_ok)
+        for (int m = 0; m < 2; ++m) {
+            if (!make_tmap_u8(&L->tm_pws[m], L->ws[m], (uint64_t)(H / 4), (uint64_t)Is, 64, 64,
+                              CU_TENSOR_MAP_SWIZZLE_64B))
+                return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for shared matrix %d", m);
+            L->tm_pw[m] = L->tm_pws[m];
+        }
+    L->kp1 = (int)((H + 255) / 256 * 256);
+    L->kp2 = (int)((Is + 255) / 256 * 256);
+    if (qgemv_imma_smem_bytes(L->kp1, 1) > 227 * 1024 || qgemv_imma_smem_bytes(L->kp2, 1) > 227 * 1024)
+        return fail(QMOE_ERR_UNSUPPORTED, "hidden or shared intermediate dim too large for the GEMV tiles");
+    L->grid0 = qgemv_max_grid(0, (int)H);
+    L->grid1 = qgemv_max_grid(1, (int)Is);
+    return QMOE_OK;
+}
+
 static int layer_create_impl(qmoe_layer *L, const float *gate_weight, const float *bias,
                              const qmoe_expert_weights *experts,
                              const qmoe_expert_weights *shared, int ptr_kind) {
     const qmoe_moe_config &c = L->cfg;
     cudaStream_t st = L->ctx->stream;
     const int64_t E = c.num_experts, H = c.hidden_dim, I = c.intermediate_dim;
-    QTRY(layer_alloc_copy((void **)&L->gate_w, gate_weight, sizeof(float) * E * H, ptr_kind, st));
-    if (c.has_bias)
-        QTRY(layer_alloc_copy((void **)&L->bias, bias, sizeof(float) * E, ptr_kind, st));
-    const int64_t rows[3] = {I, I, H}, kin[3] = {H, H, I};
     const int64_t El = L->e_count;
-    for (int m = 0; m < 3; ++m) {
+    if (El > 0) {
+        QTRY(layer_alloc_copy((void **)&L->gate_w, gate_weight, sizeof(float) * E * H, ptr_kind, st));
+        if (c.has_bias)
+            QTRY(layer_alloc_copy((void **)&L->bias, bias, sizeof(float) * E, ptr_kind, st));
+    }
+    const int64_t rows[3] = {I, I, H}, kin[3] = {H, H, I};
+    for (int m = 0; m < 3 && El > 0; ++m) {
         const size_t wb = (size_t)rows[m] * (kin[m] / 4);
         QTRY_CUDA(cudaMalloc((void **)&L->w[m], wb * El));
         QTRY_CUDA(cudaMalloc((void **)&L->s[m], sizeof(float) * rows[m] * El));
@@ -560,6 +642,7 @@ static int layer_create_impl(qmoe_layer *L, const float *gate_weight, const floa
         }
     }
     QTRY_CUDA(cudaStreamSynchronize(st));
+    if (El == 0) return empty_layer_maps(L);
     // TMA maps: rows of 64-byte boxes, 128 rows per box, 64-byte swizzle
     for (int m = 0; m < 3; ++m) {
         if (!make_tmap_u8(&L->tm_w[m], L->w[m], (uint64_t)(kin[m] / 4), (uint64_t)(rows[m] * El),
@@ -637,16 +720,21 @@ int qmoe_layer_create(qmoe_ctx *ctx, const qmoe_moe_config *cfg, const float *ga
                       const float *bias, const qmoe_expert_weights *experts,
                       int32_t expert_begin, int32_t expert_count,
                       const qmoe_expert_weights *shared, int ptr_kind, qmoe_layer **out) {
-    if (!ctx || !out || !gate_weight) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (!ctx || !out) return fail(QMOE_ERR_INVALID, "NULL argument");
     *out = nullptr;
     QTRY(check_ptr_kind(ptr_kind));
     QTRY(validate_cfg(cfg));
-    if (cfg->has_bias && !bias) return fail(QMOE_ERR_INVALID, "has_bias set but bias is NULL");
-    if (expert_begin < 0 || expert_count < 1 || expert_begin + expert_count > cfg->num_experts)
+    // expert_count 0: a layer without routed experts (qmoe-rs's empty
+    // `experts`, src/moe.rs:46-48, e.g. a flattened layer loaded as its
+    // shared FFN alone, src/loader.rs:452-456); its gate is never read
+    if (expert_count > 0 && !gate_weight) return fail(QMOE_ERR_INVALID, "gate_weight is NULL");
+    if (expert_count > 0 && cfg->has_bias && !bias)
+        return fail(QMOE_ERR_INVALID, "has_bias set but bias is NULL");
+    if (expert_begin < 0 || expert_count < 0 || expert_begin + expert_count > cfg->num_experts)
         return fail(QMOE_ERR_INVALID, "expert range [%d, %d) outside [0, %d)", expert_begin,
                     expert_begin + expert_count, cfg->num_experts);
     if (expert_count > 768) return fail(QMOE_ERR_UNSUPPORTED, "more than 768 local experts");
-    if (!experts) return fail(QMOE_ERR_INVALID, "experts is NULL");
+    if (expert_count > 0 && !experts) return fail(QMOE_ERR_INVALID, "experts is NULL");
     if ((cfg->shared_intermediate_dim > 0) != (shared != nullptr))
         return fail(QMOE_ERR_INVALID,
                     "shared must be given exactly when shared_intermediate_dim > 0");
@@ -1124,6 +1212,31 @@ static int finish_out(qmoe_layer *L, void *user, const void *dev, size_t bytes, 
     return QMOE_OK;
 }
 
+// A layer without routed experts: QMoELayer::forward returns zeros
+// (src/moe.rs:46-48) and the block adds the shared expert's output
+// (src/model.rs:386-389), so the result is the shared expert alone, or zeros
+// without one.  No expert is selected: routing outputs read -1 / 0.
+static int forward_without_experts(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
+                                   int32_t *topk_idx, float *topk_w, int ptr_kind) {
+    cudaStream_t st = L->ctx->stream;
+    const size_t xbytes = dtype_size(dtype) * T * L->cfg.hidden_dim;
+    const size_t kb = sizeof(int32_t) * T * L->cfg.top_k;
+    if (ptr_kind == QMOE_PTR_HOST) {
+        if (topk_idx) std::memset(topk_idx, 0xff, kb);
+        if (topk_w) std::memset(topk_w, 0, kb);
+    } else {
+        if (topk_idx) QTRY_CUDA(cudaMemsetAsync(topk_idx, 0xff, kb, st));
+        if (topk_w) QTRY_CUDA(cudaMemsetAsync(topk_w, 0, kb, st));
+    }
+    if (L->has_shared) return shared_pass(L, x, dtype, T, out, 0, ptr_kind);
+    if (ptr_kind == QMOE_PTR_HOST) {
+        std::memset(out, 0, xbytes);
+        return QMOE_OK;
+    }
+    QTRY_CUDA(cudaMemsetAsync(out, 0, xbytes, st));
+    return QMOE_OK;
+}
+
 int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
                        int32_t *topk_idx, float *topk_w, int ptr_kind) {
     if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
@@ -1131,13 +1244,14 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
     QTRY(check_dtype(dtype));
     if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
     if (T > 0 && (!x || !out)) return fail(QMOE_ERR_INVALID, "NULL x or out");
-    if (L->e_begin != 0 || L->e_count != L->cfg.num_experts)
+    if (L->e_count > 0 && (L->e_begin != 0 || L->e_count != L->cfg.num_experts))
         return fail(QMOE_ERR_INVALID,
                     "qmoe_layer_forward needs all experts local; use the routed entry points");
     if (T == 0) return QMOE_OK;
     QTRY(check_align(x, ptr_kind, "x"));
     QTRY(check_align(out, ptr_kind, "out"));
     DeviceGuard g(L->ctx->device);
+    if (L->e_count == 0) return forward_without_experts(L, x, dtype, T, out, topk_idx, topk_w, ptr_kind);
     cudaStream_t st = L->ctx->stream;
     QTRY(layer_reserve(L, T));
     const qmoe_moe_config &c = L->cfg;
@@ -1246,6 +1360,7 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
 int qmoe_layer_route(qmoe_layer *L, const void *x, int dtype, int64_t T, int32_t *topk_idx,
                      float *topk_w, int ptr_kind) {
     if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    if (L->e_count == 0) return fail(QMOE_ERR_INVALID, "the layer has no routed experts");
     QTRY(check_ptr_kind(ptr_kind));
     QTRY(check_dtype(dtype));
     if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
@@ -1273,6 +1388,7 @@ int qmoe_layer_route_plan(qmoe_layer *L, const void *x, int dtype, int64_t T, in
                           float *topk_w, int experts_per_rank, int world, int64_t capacity,
                           int32_t *send_counts, int32_t *send_tok, int32_t *send_meta, int32_t *slot_pos) {
     if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    if (L->e_count == 0) return fail(QMOE_ERR_INVALID, "the layer has no routed experts");
     QTRY(check_dtype(dtype));
     const qmoe_moe_config &c = L->cfg;
     if (T < 0 || world < 1 || world > kEpMaxWorld || experts_per_rank < 1 ||
@@ -1325,6 +1441,7 @@ int qmoe_layer_forward_routed(qmoe_layer *L, const void *x, int dtype, int64_t R
                               const int32_t *topk_idx, const float *topk_w, void *out,
                               int ptr_kind) {
     if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    if (L->e_count == 0) return fail(QMOE_ERR_INVALID, "the layer has no routed experts");
     QTRY(check_ptr_kind(ptr_kind));
     QTRY(check_dtype(dtype));
     if (R < 0) return fail(QMOE_ERR_INVALID, "R < 0");
@@ -1362,6 +1479,7 @@ int qmoe_layer_forward_routed(qmoe_layer *L, const void *x, int dtype, int64_t R
 int qmoe_layer_forward_ep(qmoe_layer *L, const void *x, int dtype, int64_t R, const int32_t *meta,
                           int64_t shared_row0, void *out) {
     if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    if (L->e_count == 0) return fail(QMOE_ERR_INVALID, "the layer has no routed experts");
     QTRY(check_dtype(dtype));
     if (R < 0 || shared_row0 < 0 || shared_row0 > R)
         return fail(QMOE_ERR_INVALID, "bad rows (R %lld, shared_row0 %lld)", (long long)R,
@@ -1382,18 +1500,10 @@ int qmoe_layer_forward_ep(qmoe_layer *L, const void *x, int dtype, int64_t R, co
     return run_experts(L, x, dtype, R, a, out, 0);
 }
 
-int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
-                              int accumulate, int ptr_kind) {
-    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
-    QTRY(check_ptr_kind(ptr_kind));
-    QTRY(check_dtype(dtype));
-    if (!L->has_shared) return fail(QMOE_ERR_INVALID, "layer has no shared expert");
-    if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
-    if (T > 0 && (!x || !out)) return fail(QMOE_ERR_INVALID, "NULL argument");
-    if (T == 0) return QMOE_OK;
-    QTRY(check_align(x, ptr_kind, "x"));
-    QTRY(check_align(out, ptr_kind, "out"));
-    DeviceGuard g(L->ctx->device);
+// The shared expert alone over T rows (SharedExpert::forward,
+// src/model.rs:325-347), written to out or added into it.
+static int shared_pass(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out, int accumulate,
+                       int ptr_kind) {
     cudaStream_t st = L->ctx->stream;
     QTRY(layer_reserve(L, T));
     const qmoe_moe_config &c = L->cfg;
@@ -1420,6 +1530,21 @@ int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T
         QTRY(sync_and_check(st));
     }
     return QMOE_OK;
+}
+
+int qmoe_layer_shared_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
+                              int accumulate, int ptr_kind) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    QTRY(check_ptr_kind(ptr_kind));
+    QTRY(check_dtype(dtype));
+    if (!L->has_shared) return fail(QMOE_ERR_INVALID, "layer has no shared expert");
+    if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
+    if (T > 0 && (!x || !out)) return fail(QMOE_ERR_INVALID, "NULL argument");
+    if (T == 0) return QMOE_OK;
+    QTRY(check_align(x, ptr_kind, "x"));
+    QTRY(check_align(out, ptr_kind, "out"));
+    DeviceGuard g(L->ctx->device);
+    return shared_pass(L, x, dtype, T, out, accumulate, ptr_kind);
 }
 
 // ---------------------------------------------------------------------------
@@ -1627,6 +1752,7 @@ int qmoe_ep_return(qmoe_ep_peer *p, const void *y) {
 int qmoe_layer_forward_ep_return(qmoe_layer *L, qmoe_ep_peer *p, const void *x, int dtype, int64_t R,
                                  const int32_t *meta, int64_t shared_row0, void *y) {
     if (!L || !p) return fail(QMOE_ERR_INVALID, "NULL layer or exchange");
+    if (L->e_count == 0) return fail(QMOE_ERR_INVALID, "the layer has no routed experts");
     QTRY(check_dtype(dtype));
     QTRY(ep_ready(p));
     const int64_t GC = (int64_t)p->d.world * p->d.C;

@@ -39,7 +39,9 @@ int *device_error_flag() {
 }
 
 cudaError_t ensure_dyn_smem(const void *func, size_t bytes) {
-    if (bytes <= 48 * 1024) return cudaSuccess;       // below the default limit
+    // (no shortcut below 48 KB: a kernel's static shared memory counts
+    // against the default limit too, so a launch with less dynamic memory
+    // than that can still need the opt-in)
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;

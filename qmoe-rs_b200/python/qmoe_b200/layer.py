@@ -246,7 +246,9 @@ def _expert_struct(ex: PackedExpert, keep: list) -> Tuple[capi.ExpertWeightsC, i
 class QMoELayer:
     """QMoELayer (src/moe.rs:23-130) with its optional SharedExpert, resident
     on one B200.  For expert parallelism pass expert_begin / the local slice
-    of `experts`."""
+    of `experts`.  With no experts (qmoe-rs's empty `experts`, e.g. a
+    flattened layer) the forward is the shared expert alone (zeros without
+    one) and gate_weight may be None."""
 
     def __init__(self, config: MoEConfig, gate_weight, experts: Sequence[PackedExpert],
                  shared: Optional[PackedExpert] = None, bias=None,
@@ -256,10 +258,16 @@ class QMoELayer:
         self.expert_begin = int(expert_begin)
         self.expert_count = len(experts)
         keep: list = []
-        if not (torch is not None and isinstance(gate_weight, torch.Tensor)):
-            gate_weight = np.ascontiguousarray(gate_weight, dtype=np.float32)
-        gp, gkind, ga = _ptr(gate_weight)
-        keep.append(ga)
+        kinds = set()
+        gp = None
+        if gate_weight is not None:
+            if not (torch is not None and isinstance(gate_weight, torch.Tensor)):
+                gate_weight = np.ascontiguousarray(gate_weight, dtype=np.float32)
+            gp, gkind, ga = _ptr(gate_weight)
+            keep.append(ga)
+            kinds.add(gkind)
+        elif len(experts):
+            raise ValueError("a layer with routed experts needs its gate_weight")
         bp = None
         if bias is not None:
             if not (torch is not None and isinstance(bias, torch.Tensor)):
@@ -267,7 +275,6 @@ class QMoELayer:
             bp, bkind, ba = _ptr(bias)
             keep.append(ba)
         arr = (capi.ExpertWeightsC * max(1, len(experts)))()
-        kinds = {gkind}
         for i, ex in enumerate(experts):
             if not isinstance(ex, PackedExpert):
                 ex = PackedExpert.from_triple(ex)
@@ -280,9 +287,9 @@ class QMoELayer:
             s, k = _expert_struct(shared, keep)
             kinds.add(k)
             sh = ctypes.pointer(s)
-        if len(kinds) != 1:
+        if len(kinds) > 1:
             raise ValueError("all weights of a layer must be host or all device memory")
-        kind = kinds.pop()
+        kind = kinds.pop() if kinds else capi.QMOE_PTR_HOST
         if kind == capi.QMOE_PTR_DEVICE:
             self.ctx.use_current_torch_stream()
         cfg = config.to_c(bias is not None)

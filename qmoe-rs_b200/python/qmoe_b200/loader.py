@@ -16,7 +16,9 @@ Rules kept from the reference:
     (:316-318);
   * a layer without a router weight gets a uniform one, ones [E, H]
     (:410-424);
-  * a missing tensor is an error naming its key (:221-232).
+  * a missing tensor is an error naming its key (:221-232);
+  * a flattened layer becomes a layer without routed experts whose FFN is
+    the shared expert (:262-305, :452-456).
 Tensors are read on the host (only this layer's keys) and handed to
 qmoe_layer_create, which uploads them once into the stacked device layout.
 """
@@ -113,6 +115,7 @@ def load_moe_layer(path: str, layer_idx: int, config: MoEConfig,
     context's device (the drop-in for the per-layer loop of src/loader.rs:430-459)."""
     t = read_layer(path, layer_idx, config)
     if t.flattened:
-        raise ValueError(f"layer {layer_idx} is flattened (a dense FFN, no routed experts): "
-                         "read it with read_layer and run its FFN as a shared expert")
+        # src/loader.rs:452-456: no routed experts, the dense FFN as the
+        # shared expert; the layer's forward is that FFN alone
+        return QMoELayer(t.config, None, [], shared=t.shared, ctx=ctx)
     return QMoELayer(t.config, t.gate_weight, t.experts, shared=t.shared, ctx=ctx)

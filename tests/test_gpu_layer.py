@@ -100,9 +100,39 @@ def test_packed_forward_ragged_rows_and_large_values():
     assert np.all(y[3] == 0.0)
 
 
+@pytest.mark.parametrize("out_f,in_f,batch", [(40, 100, 3), (130, 1412, 5), (17, 102, 2),
+                                              (8, 4, 1), (5, 2, 2), (64, 2047, 33)])
+def test_packed_forward_ragged_widths_match_oracle(out_f, in_f, batch):
+    # src/tensor.rs:74 reads in_features / 4 bytes per row and src/simd.rs:15
+    # ignores the in_features % 4 trailing activations: any width is valid
+    rng = np.random.default_rng(out_f + in_f)
+    bpr = in_f // 4
+    packed = rng.integers(0, 256, (out_f, bpr), dtype=np.uint8)
+    scales = (rng.random(out_f, dtype=np.float32) * 0.05 + 0.01).astype(np.float32)
+    x = rng.standard_normal((batch, in_f)).astype(np.float32)
+    t = PackedQMoETensor.from_bytes(packed.reshape(-1), (out_f, in_f), scales)
+    ref = qo.packed_forward(packed, scales, (out_f, in_f), x)
+    y_host = t.forward_simd(x)
+    y_dev = t.forward_simd(torch.from_numpy(x).cuda()).cpu().numpy()
+    if bpr == 0:
+        assert np.all(y_host == 0.0) and np.all(ref == 0.0)
+    else:
+        assert rel_err(y_host, ref) <= F32_TOL
+    np.testing.assert_array_equal(y_dev, y_host)
+    # a second, larger batch reuses the padded staging rows
+    x2 = rng.standard_normal((batch + 9, in_f)).astype(np.float32)
+    ref2 = qo.packed_forward(packed, scales, (out_f, in_f), x2)
+    y2 = t.forward_simd(x2)
+    assert (rel_err(y2, ref2) if bpr else float(np.abs(y2).max())) <= F32_TOL
+
+
 def test_packed_forward_rejects_bad_shapes():
     with pytest.raises(QmoeError) as ei:
-        PackedQMoETensor.from_bytes(np.zeros((4, 25), np.uint8), (4, 100),
+        PackedQMoETensor.from_bytes(np.zeros((4, 25), np.uint8), (0, 100),
+                                    np.ones(4, np.float32))
+    assert ei.value.code == capi.QMOE_ERR_INVALID
+    with pytest.raises(QmoeError) as ei:
+        PackedQMoETensor.from_bytes(np.zeros((4, 25), np.uint8), (4, 0),
                                     np.ones(4, np.float32))
     assert ei.value.code == capi.QMOE_ERR_INVALID
     t = PackedQMoETensor.from_bytes(np.zeros((4, 16), np.uint8), (4, 64), np.ones(4, np.float32))
@@ -318,6 +348,52 @@ def test_shared_forward_and_accumulate():
     base = np.ones((6, 128), np.float32)
     acc = layer.shared_forward(x, out=base.copy())
     assert rel_err(acc - 1.0, ref) <= 1e-4
+
+
+def test_graph_replay_after_x_copy_reallocated():
+    # the cached graph of repeated page-locked forwards reads the layer's
+    # device copy of x; a host-pointer call that reallocates that copy must
+    # make the next repeat capture again instead of replaying into freed memory
+    cfg = MoEConfig(16, 4, 512, 256, shared_intermediate_dim=256)
+    layer, *_ = build(cfg, seed=31)
+    layer.reserve(1024)
+    xp = torch.randn(32, 512, generator=torch.Generator().manual_seed(1)).pin_memory()
+    op = torch.empty(32, 512).pin_memory()
+    with torch.cuda.stream(torch.cuda.Stream()):
+        ref = layer.forward(xp.cuda()).cpu()
+        for _ in range(3):                        # second call captures, third replays
+            layer.forward(xp, out=op)
+            assert torch.equal(op, ref)
+        big = torch.randn(64, 512, generator=torch.Generator().manual_seed(2))   # pageable
+        layer.forward(big)                        # grows the device copy of x
+        xp.copy_(torch.randn(32, 512, generator=torch.Generator().manual_seed(3)))
+        ref = layer.forward(xp.cuda()).cpu()
+        for _ in range(3):
+            layer.forward(xp, out=op)
+            assert torch.equal(op, ref)
+
+
+def test_layer_without_experts_is_its_shared_expert():
+    # qmoe-rs: QMoELayer::forward returns zeros for empty `experts`
+    # (src/moe.rs:46-48); the block adds the shared expert (src/model.rs:386-389)
+    H, Is = 512, 320
+    cfg = MoEConfig(8, 2, H, 256, shared_intermediate_dim=Is)
+    _, shared, _ = helpers.synth_layer(1, H, 256, Is, seed=8, device="cuda")
+    layer = QMoELayer(cfg, None, [], shared=shared)
+    np_sh = helpers.to_numpy_experts([shared])[0]
+    for dtype, T, tol in ((torch.float32, 5, F32_TOL), (torch.bfloat16, 300, BF16_TOL)):
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(T)).to(dtype)
+        out, idx, w = layer.forward(x.cuda(), return_routing=True)
+        ref = qo.shared_forward(np_sh, x.float().numpy(), H, Is)
+        assert rel_err(out.float().cpu().numpy(), ref) <= tol
+        assert torch.all(idx == -1) and torch.all(w == 0)
+        host = layer.forward(x)                    # host pointers
+        assert torch.equal(host, out.cpu())
+    bare = QMoELayer(MoEConfig(8, 2, H, 256), None, [])
+    z = bare.forward(torch.randn(7, H, device="cuda"))
+    assert torch.all(z == 0)
+    zh = bare.forward(np.ones((3, H), np.float32))
+    assert np.all(np.asarray(zh) == 0)
 
 
 def test_empty_batch_is_a_noop():

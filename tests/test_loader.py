@@ -100,8 +100,7 @@ def test_flattened_layer_is_read_as_one_ffn(tmp_path):
     save_file(d, str(f))
     t = loader.read_layer(str(f), 0, MoEConfig(E, 2, H, I))
     assert t.flattened and t.experts == [] and t.config.shared_intermediate_dim == Is
-    with pytest.raises(ValueError, match="flattened"):
-        loader.load_moe_layer(str(f), 0, MoEConfig(E, 2, H, I))
+    assert t.shared[0][0].shape == (Is, H // 4)
 
 
 @pytest.mark.gpu
@@ -120,3 +119,35 @@ def test_loaded_layer_matches_direct_construction(tmp_path):
     a = direct.forward(z["x"])
     b = loaded.forward(z["x"])
     assert np.array_equal(np.asarray(a), np.asarray(b))
+    # and the loaded layer against the oracle on the same arrays
+    from oracle import oracle as qo
+    ref, _, _ = qo.layer_forward(qo.MoEConfig(E, 2, H, I, Is), z["gate_w"], np_exp, z["x"],
+                                 shared=np_sh)
+    err = float(np.max(np.abs(np.asarray(b) - ref)) / np.max(np.abs(ref)))
+    assert err <= 1e-4
+
+
+@pytest.mark.gpu
+def test_loaded_flattened_layer_is_its_ffn(tmp_path):
+    # src/loader.rs:452-456: a flattened layer has no routed experts; the
+    # block's output is 0 (QMoELayer::forward on empty experts, src/moe.rs:46-48)
+    # plus the FFN loaded as the shared expert (src/model.rs:386-389)
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from oracle import oracle as qo
+    z, E, H, I, Is, T = tiny()
+    d = {}
+    srows = {"gate": Is, "up": Is, "down": H}
+    for n in ("gate", "up", "down"):
+        d[f"layers.0.moe.{PROJ[n]}.weight"] = packed2d(z[f"shared_{n}_packed"], srows[n])
+        d[f"layers.0.moe.{PROJ[n]}.scales"] = torch.from_numpy(z[f"shared_{n}_scales"])
+    f = tmp_path / "flat.safetensors"
+    save_file(d, str(f))
+    layer = loader.load_moe_layer(str(f), 0, MoEConfig(E, 2, H, I))
+    out, idx, w = layer.forward(z["x"], return_routing=True)
+    np_sh = [(z[f"shared_{n}_packed"].reshape(-1), z[f"shared_{n}_scales"])
+             for n in ("gate", "up", "down")]
+    ref = qo.shared_forward(np_sh, z["x"], H, Is)
+    err = float(np.max(np.abs(np.asarray(out) - ref)) / np.max(np.abs(ref)))
+    assert err <= 1e-4
+    assert np.all(np.asarray(idx) == -1) and np.all(np.asarray(w) == 0.0)
