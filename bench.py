@@ -100,7 +100,8 @@ def parse():
                     help="skip the CPU-baseline leg (for profiler runs)")
     ap.add_argument("--no-sublines", action="store_true",
                     help="N = 1: only the headline workload")
-    ap.add_argument("--ncu-case", choices=["decode", "prefill", "pack", "v3-prefill", "v3-decode"],
+    ap.add_argument("--ncu-case", choices=["decode", "prefill", "pack", "v3-prefill", "v3-decode",
+                                           "v3-route"],
                     default=None,
                     help="only run 3 eager forwards of a short fixed case for an ncu capture, "
                          "print nothing")
@@ -270,6 +271,63 @@ def torch_packer(w):
 def synth_x(W, T, seed, dev):
     g = torch.Generator(device=dev).manual_seed(seed)
     return torch.randn(T, W["H"], generator=g, device=dev).to(act_dtype(W))
+
+
+def zipf_targets(E: int, s: float = 1.1, hottest: float = 0.08):
+    """Assignment shares following Zipf(s) by popularity rank, shifted
+    (p_r ~ (r + q)^-s, the Zipf-Mandelbrot form) so the hottest expert takes
+    `hottest` of all assignments -- a token can pick an expert only once, so
+    a top-8 router caps any expert at 1/8 of the assignments, below the
+    unshifted Zipf(1.1) head over 256 experts."""
+    r = np.arange(1, E + 1, dtype=np.float64)
+    lo, hi = 0.0, 1e4
+    for _ in range(200):
+        q = 0.5 * (lo + hi)
+        p = (r + q) ** -s
+        p /= p.sum()
+        lo, hi = (q, hi) if p[0] > hottest else (lo, q)
+    return p
+
+
+def route_torch(W, logits, bias):
+    """Selection of the layer's router (sigmoid, group-limited top-k) in
+    torch ops, for calibrating the bias only (the product routes on the
+    device, bit-exact with the oracle)."""
+    E, K, G, TG = W["E"], W["k"], W["n_group"], W["topk_group"]
+    choice = torch.sigmoid(logits) + bias
+    gs = choice.view(-1, G, E // G).topk(2, dim=-1).values.sum(-1)
+    keep = torch.zeros_like(gs, dtype=torch.bool).scatter_(1, gs.topk(TG, dim=-1).indices, True)
+    masked = choice.masked_fill(~keep.repeat_interleave(E // G, dim=1), float("-inf"))
+    return masked.topk(K, dim=-1).indices
+
+
+def zipf_bias(W, gate_w, seed: int, tokens: int = 4096, iters: int = 400):
+    """a seeded per-expert selection bias under which expert
+    popularity follows the shifted Zipf(1.1) of zipf_targets over a seeded
+    permutation of the experts (hottest ~8% of assignments).  Fitted on
+    `tokens` seeded N(0, 1) tokens: start from a bias proportional to the log
+    target, then damped multiplicative corrections of the measured shares.
+    Under group-limited routing the head follows the target closely while
+    the coldest experts starve.  Returns (bias [E] f32 on the gate's device,
+    target shares in expert order)."""
+    E = W["E"]
+    dev = gate_w.device
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    perm = torch.randperm(E, generator=g)
+    target = torch.empty(E, dtype=torch.float64)
+    target[perm] = torch.from_numpy(zipf_targets(E))
+    target = target.to(dev)
+    xg = torch.Generator(device=dev).manual_seed(seed + 1)
+    x = torch.randn(tokens, W["H"], generator=xg, device=dev)
+    logits = x @ gate_w.t()
+    lp = torch.log(target).float()
+    bias = 0.05 * (lp - lp.mean())
+    for _ in range(iters):
+        idx = route_torch(W, logits, bias)
+        share = torch.bincount(idx.reshape(-1), minlength=E).double() / idx.numel()
+        bias += (0.08 * torch.log((target + 1e-5) / (share + 1e-5))).float().clamp(-0.05, 0.05)
+        bias -= bias.mean()
+    return bias.float().contiguous(), target.cpu().numpy()
 
 
 def per_expert_bytes(W):
@@ -753,6 +811,10 @@ def run_ep(args, W, ws, rank, local, dev, dist):
     full.close()
     del full, out_1, idx_1, gate_w
     torch.cuda.empty_cache()
+    # the exchange's waits are bounded (about a second): start the next
+    # forwards together, not after each rank's own set-up time
+    torch.cuda.synchronize()
+    dist.barrier()
     tol = 2e-2 if W["act"] == "bf16" else 1e-4
     pr = torch.tensor([err, 0.0 if same_idx else 1.0], device=dev, dtype=torch.float64)
     dist.all_reduce(pr, op=dist.ReduceOp.MAX)
@@ -805,6 +867,7 @@ def run_ep(args, W, ws, rank, local, dev, dist):
         e1.record()
         torch.cuda.synchronize()
     dist.barrier()
+    ctx.synchronize()        # raises if any exchange wait of the timed forwards gave up
     t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
@@ -938,12 +1001,17 @@ def run_ncu_case(args):
         W, T = V2, (32 if args.ncu_case == "decode" else 2048)
         if args.ncu_case == "prefill":
             W = dict(V2, act="bf16")
+    if args.ncu_case == "v3-route":
+        T = 4096                 # the router alone over the configs[3] batch
     experts, shared, gate_w = synth_weights(W, args.seed, "cuda")
     layer = QMoELayer(make_cfg(W), gate_w, experts, shared=shared, ctx=default_context(0))
     del experts, shared
     x = synth_x(W, T, args.seed + 7, "cuda")
     for _ in range(3):
-        layer.forward(x)
+        if args.ncu_case == "v3-route":
+            layer.route(x)
+        else:
+            layer.forward(x)
     torch.cuda.synchronize()
 
 

@@ -177,6 +177,7 @@ struct qmoe_layer {
     int e_begin = 0, e_count = 0;
     bool has_shared = false;
     float *gate_w = nullptr, *bias = nullptr;
+    float *gate_t = nullptr;   // [H][gate_t_ld(E)] transposed gate (E > 64), for large-batch logits
     uint8_t *w[3] = {nullptr, nullptr, nullptr};
     float *s[3] = {nullptr, nullptr, nullptr};
     uint8_t *ws[3] = {nullptr, nullptr, nullptr};
@@ -535,6 +536,7 @@ int qmoe_layer_destroy(qmoe_layer *L) {
         if (L->ss[m]) cudaFree(L->ss[m]);
     }
     if (L->gate_w) cudaFree(L->gate_w);
+    if (L->gate_t) cudaFree(L->gate_t);
     if (L->bias) cudaFree(L->bias);
     for (cudaEvent_t &e : L->ev)
         if (e) cudaEventDestroy(e);
@@ -612,6 +614,11 @@ static int layer_create_impl(qmoe_layer *L, const float *gate_weight, const floa
     const int64_t El = L->e_count;
     if (El > 0) {
         QTRY(layer_alloc_copy((void **)&L->gate_w, gate_weight, sizeof(float) * E * H, ptr_kind, st));
+        if (E > 64) {
+            const int ld = gate_t_ld((int)E);
+            QTRY_CUDA(cudaMalloc((void **)&L->gate_t, sizeof(float) * (size_t)ld * H));
+            QTRY_CUDA(launch_transpose_gate(L->gate_w, (int)E, (int)H, L->gate_t, ld, st));
+        }
         if (c.has_bias)
             QTRY(layer_alloc_copy((void **)&L->bias, bias, sizeof(float) * E, ptr_kind, st));
     }
@@ -863,6 +870,8 @@ static RouterParams router_params(qmoe_layer *L, const void *xd, int dtype, int6
     rp.E = c.num_experts;
     rp.K = c.top_k;
     rp.gate_w = L->gate_w;
+    rp.gate_t = L->gate_t;
+    rp.gate_t_ld = gate_t_ld(c.num_experts);
     rp.bias = L->bias;
     rp.scoring = c.scoring;
     rp.n_group = c.n_group;

@@ -46,6 +46,11 @@ QMOE_DEV int ld_acquire_sys_i32(const int *p) {
     return v;
 }
 
+// Arrival counters grow by a fixed amount per forward and wrap modulo 2^32
+// over a long run; `count` has reached `want` when the wrapped difference is
+// not negative (valid while the two are less than 2^31 apart).
+QMOE_DEV bool arrived(int count, uint32_t want) { return (int32_t)((uint32_t)count - want) >= 0; }
+
 // load_act4 through L2 only, for rows other CTAs or other GPUs wrote after
 // this kernel started (the read-only path of __ldg is not coherent with them).
 QMOE_DEV float4 load_act4_cg(const void *base, int dtype, int64_t idx) {

@@ -111,13 +111,13 @@ ep_wait_kernel(const EpPeerDev d, int phase) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int s = *d.seq + 1;
-    const int want = (int)(s * d.C * (phase == 1 ? d.ret_units : 1));
+    const uint32_t want = (uint32_t)s * (uint32_t)d.C * (uint32_t)(phase == 1 ? d.ret_units : 1);
     bool ok = true;
     for (int p = threadIdx.x; p < d.world; p += 32) {
         if (p == d.rank) continue;
         const int *f = flag_at(d, d.rank, phase, p);
         uint32_t n = 0;
-        while (ld_acquire_sys(f) < want) {
+        while (!arrived(ld_acquire_sys(f), want)) {
             if (++n >= kMaxWaitProbes) {
                 ok = false;
                 break;
@@ -140,13 +140,13 @@ ep_finish_kernel(const EpPeerDev d, const int32_t *slot_pos, int64_t T, const vo
     QMOE_PDL_TRIGGER();
     const int seq = *d.seq + 1;
     if (threadIdx.x < 32) {
-        const int want = (int)(seq * d.C * d.ret_units);
+        const uint32_t want = (uint32_t)seq * (uint32_t)d.C * (uint32_t)d.ret_units;
         bool ok = true;
         for (int p = threadIdx.x; p < d.world; p += 32) {
             if (p == d.rank) continue;
             const int *f = flag_at(d, d.rank, 1, p);
             uint32_t n = 0;
-            while (ld_acquire_sys(f) < want) {
+            while (!arrived(ld_acquire_sys(f), want)) {
                 if (++n >= kMaxWaitProbes) {
                     ok = false;
                     break;

@@ -21,6 +21,8 @@ struct RouterParams {
     int64_t T;
     int H, E, K;
     const float *gate_w;    // [E, H]
+    const float *gate_t;    // [H, gate_t_ld] f32: gate_w transposed (large-batch logits), or nullptr
+    int gate_t_ld;          // row stride of gate_t in floats (E rounded up to 4)
     const float *bias;      // [E] or nullptr
     int scoring;            // 0 softmax, 1 sigmoid
     int n_group, topk_group;
@@ -31,6 +33,10 @@ struct RouterParams {
     float *scratch;         // router_scratch_floats(T, H, E) floats
 };
 size_t router_smem_bytes(int H, int E);
+// Host: gate_t[k][e] = gate_w[e][k] for the large-batch logit kernel (ld =
+// E rounded up to 4; the padding columns are zero).
+cudaError_t launch_transpose_gate(const float *gate_w, int E, int H, float *gate_t, int ld, cudaStream_t s);
+int gate_t_ld(int E);
 bool router_uses_partials(int64_t T, int H, int E);
 size_t router_scratch_floats(int64_t T, int H, int E);
 // With a tail (tail->counter != nullptr), the last CTA of the selection

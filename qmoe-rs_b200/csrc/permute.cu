@@ -82,13 +82,13 @@ permute_kernel(const PermuteParams p) {
         // the rows and their metadata come from the peers' dispatch: wait
         // (bounded) until each peer's C rows of this forward have arrived
         if (warp == 0) {
-            const int want = (int)((*p.ep.seq + 1) * p.ep.C);
+            const uint32_t want = (uint32_t)(*p.ep.seq + 1) * (uint32_t)p.ep.C;
             bool ok = true;
             for (int r = lane; r < p.ep.world; r += 32) {
                 if (r == p.ep.rank) continue;
                 const int *f = reinterpret_cast<const int *>(p.ep.base[p.ep.rank] + p.ep.off_flags) + r;
                 uint32_t n = 0;
-                while (ld_acquire_sys_i32(f) < want) {
+                while (!arrived(ld_acquire_sys_i32(f), want)) {
                     if (++n >= sm100::kMaxWaitProbes) {
                         ok = false;
                         break;

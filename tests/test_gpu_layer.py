@@ -289,19 +289,30 @@ def test_route_only_matches_oracle_bit_exact(T, reserve):
     np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=1e-6, atol=0)
 
 
-def test_whole_logits_path_bit_exact():
-    # T * E * H/64 > 2^25 partials: the whole-logits kernel, V3-style routing
-    E, H, T = 256, 4096, 2100
-    cfg = MoEConfig(E, 8, H, 128, scoring=capi.QMOE_SCORING_SIGMOID, n_group=8,
-                    topk_group=4, norm_topk_prob=True, routed_scaling_factor=2.5)
-    experts, _, gw = helpers.synth_layer(E, H, 128, seed=29, device="cuda")
+@pytest.mark.parametrize("E,H,T,dtype,sigmoid", [
+    (256, 4096, 2100, torch.float32, True),    # V3-style routing, partials would not fit
+    (160, 1024, 3300, torch.bfloat16, False),  # a ragged 128-expert tile, ragged 64-token tile
+    (96, 512, 5500, torch.float32, False),     # 96 experts: one tile, 32 of its columns empty
+])
+def test_large_batch_logits_bit_exact(E, H, T, dtype, sigmoid):
+    # T * E >= 2^19 with E > 64: the paired-FP32 tile kernel computes whole
+    # logits; they and the routing on them must be the oracle's bits
+    if sigmoid:
+        cfg = MoEConfig(E, 8, H, 128, scoring=capi.QMOE_SCORING_SIGMOID, n_group=8,
+                        topk_group=4, norm_topk_prob=True, routed_scaling_factor=2.5)
+    else:
+        cfg = MoEConfig(E, 6, H, 128)
+    experts, _, gw = helpers.synth_layer(E, H, 128, seed=29 + E, device="cuda")
     layer = QMoELayer(cfg, gw, experts)
-    x = torch.randn(T, H, generator=torch.Generator().manual_seed(12))
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(12)).to(dtype)
     idx, w = layer.route(x.cuda())
-    logits = qo.gate_logits(x.numpy(), gw.cpu().numpy())
+    logits = qo.gate_logits(x.float().numpy(), gw.cpu().numpy())
     ri, rw = qo.route(qo_cfg(cfg), logits)
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
-    np.testing.assert_array_equal(w.cpu().numpy(), rw)
+    if sigmoid:
+        np.testing.assert_array_equal(w.cpu().numpy(), rw)
+    else:
+        np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=1e-6, atol=0)
 
 
 @pytest.mark.parametrize("T", [19, 1100])
