@@ -774,14 +774,15 @@ def run_single(args, W, dev, local):
 # our arm, N GPUs (expert parallel)
 # ---------------------------------------------------------------------------
 
-def run_ep(args, W, ws, rank, local, dev, dist):
-    """N > 1: the layer expert-parallel over the N GPUs (each holds E/N
-    experts, a gate and shared-expert replica and its own T tokens),
-    dispatch and return by stores into the peers' memory (--ep-exchange p2p)
-    or NCCL all-to-all.  Weak scaling: tokens per GPU fixed."""
+def ep_measure(args, W, T, ws, rank, local, dev, dist, bias=None, steps=None):
+    """One expert-parallel workload on N GPUs: each rank holds E/N experts, a
+    gate and shared-expert replica and its own T tokens; dispatch and return
+    by stores into the peers' memory (--ep-exchange p2p) or NCCL all-to-all.
+    Returns (ms per step (max over ranks), parity, stage times of rank 0,
+    load and exchange figures, e2e ms, clocks) -- the same on every rank."""
     from qmoe_b200 import ExpertParallelMoE, QMoELayer, default_context
+    steps = steps or args.steps
     cfg = make_cfg(W)
-    T = W["T"]
     epr = W["E"] // ws
     mine = range(rank * epr, (rank + 1) * epr)
     per_rank_bytes = epr * per_expert_bytes(W) + shared_bytes(W)
@@ -792,35 +793,38 @@ def run_ep(args, W, ws, rank, local, dev, dist):
     for r in range(reps):
         experts, shared, gate_w = synth_weights(W, args.seed + 1000 * r, dev, experts=mine)
         layers.append(ExpertParallelMoE(cfg, gate_w, experts, rank, ws, shared=shared, ctx=ctx,
-                                        capacity=T, exchange=args.ep_exchange, dtype=dt))
+                                        capacity=T, exchange=args.ep_exchange, dtype=dt, bias=bias))
         del experts, shared, gate_w
     xs = [synth_x(W, T, args.seed + 31 * rank + 7 * r, dev) for r in range(reps)]
     torch.cuda.synchronize()
+    dist.barrier()
 
     # parity: the first eager forward of replica 0 against the whole layer on
     # this GPU (same seeded weights, this rank's tokens)
     out_ep, idx_ep, _ = layers[0].forward(xs[0], return_routing=True)
     experts, shared, gate_w = synth_weights(W, args.seed, dev)
-    full = QMoELayer(cfg, gate_w, experts, shared=shared, ctx=ctx)
+    full = QMoELayer(cfg, gate_w, experts, shared=shared, ctx=ctx, bias=bias)
     del experts, shared
     out_1, idx_1, _ = full.forward(xs[0], return_routing=True)
     torch.cuda.synchronize()
     err = rel_err(out_ep.float().cpu().numpy(), out_1.float().cpu().numpy())
     same_idx = bool(torch.equal(idx_ep, idx_1))
-    touched_local = int(((idx_1 >= rank * epr) & (idx_1 < (rank + 1) * epr)).sum().item())
+    # routed assignments of this rank's tokens per owning rank
+    owner = torch.bincount((idx_1.reshape(-1).long() // epr), minlength=ws).double()
+    per_expert = torch.bincount(idx_1.reshape(-1).long(), minlength=W["E"]).double()
     full.close()
     del full, out_1, idx_1, gate_w
     torch.cuda.empty_cache()
-    # the exchange's waits are bounded (about a second): start the next
-    # forwards together, not after each rank's own set-up time
-    torch.cuda.synchronize()
-    dist.barrier()
     tol = 2e-2 if W["act"] == "bf16" else 1e-4
     pr = torch.tensor([err, 0.0 if same_idx else 1.0], device=dev, dtype=torch.float64)
     dist.all_reduce(pr, op=dist.ReduceOp.MAX)
     parity = {"ok": bool(pr[0].item() <= tol and pr[1].item() == 0.0), "max_rel_err": float(pr[0].item()),
               "tolerance": tol, "routing_bit_exact": bool(pr[1].item() == 0.0),
               "against": "the whole layer on one GPU, each rank's own tokens (first eager forward)"}
+    # the exchange's waits are bounded (about a second): start the next
+    # forwards together, not after each rank's own set-up time
+    torch.cuda.synchronize()
+    dist.barrier()
 
     for i in range(max(3, args.warmup)):
         layers[i % reps].forward(xs[i % reps])
@@ -860,9 +864,9 @@ def run_ep(args, W, ws, rank, local, dev, dist):
         # the ranks is not counted as exchange waiting)
         dist.all_reduce(align)
         e0.record()
-        for _ in range(args.steps // reps):
+        for _ in range(steps // reps):
             chain.replay()
-        for i in range(args.steps % reps):
+        for i in range(steps % reps):
             graphs[i].replay()
         e1.record()
         torch.cuda.synchronize()
@@ -870,8 +874,7 @@ def run_ep(args, W, ws, rank, local, dev, dist):
     ctx.synchronize()        # raises if any exchange wait of the timed forwards gave up
     t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = ws * T * args.steps / (ms_max / 1e3)
+    ms_max = float(t.item()) / steps
     for gr in graphs:
         del gr
     graphs.clear()
@@ -895,10 +898,15 @@ def run_ep(args, W, ws, rank, local, dev, dist):
     torch.cuda.synchronize()
     dist.barrier()
 
+    # rows this rank sent to the others (dispatch) and got back (return)
+    counts = layers[0]._bufs["plan"]["counts"].cpu().long()
+    sent_rows = int(counts.sum().item() - counts[rank].item())
+    row_bytes = act_bytes(W) * W["H"]
+
     # end to end: pinned host tokens in, host result out, every step
     x_host = xs[0].cpu().pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
-    n_e2e = max(10, min(args.steps, 50 if W["act"] == "bf16" else 200))
+    n_e2e = max(10, min(steps, 50 if W["act"] == "bf16" else 200))
     for i in range(3):
         out_host.copy_(layers[0].forward(x_host.to(dev, non_blocking=True)), non_blocking=True)
     torch.cuda.synchronize()
@@ -914,28 +922,74 @@ def run_ep(args, W, ws, rank, local, dev, dist):
     t = torch.tensor([a.elapsed_time(b) / n_e2e], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
-    # routed assignments that land on each rank (imbalance) and the rows sent
-    cnt = torch.tensor([float(touched_local)], device=dev, dtype=torch.float64)
-    allc = [torch.zeros_like(cnt) for _ in range(ws)]
-    dist.all_gather(allc, cnt)
-    per_rank = [float(c.item()) for c in allc]
+
+    # load: routed assignments landing on each rank (all ranks' tokens)
+    owner = owner.to(dev)
+    dist.all_reduce(owner)
+    per_rank = [float(v) for v in owner.cpu().tolist()]
+    per_expert = per_expert.to(dev)
+    dist.all_reduce(per_expert)
+    hottest = float(per_expert.max().item() / max(1.0, per_expert.sum().item()))
+    sr = torch.tensor([float(sent_rows)], device=dev, dtype=torch.float64)
+    allsr = [torch.zeros_like(sr) for _ in range(ws)]
+    dist.all_gather(allsr, sr)
+    sent = [float(v.item()) for v in allsr]
+    load = {"routed_assignments_per_rank": per_rank,
+            "imbalance_max_over_mean": max(per_rank) / max(1e-9, float(np.mean(per_rank))),
+            "hottest_expert_share": hottest,
+            "dispatch_rows_sent_per_rank": sent,
+            "exchange_bytes_per_rank_max": 2 * row_bytes * max(sent),
+            "exchange_bytes_note": "rows sent to other GPUs x row bytes, dispatch plus the same rows' "
+                                   "partial sums returned (activation dtype); unused padded rows cross nothing"}
+    torch.cuda.synchronize()
+    dist.barrier()
+    for L in layers:          # every rank is done with the others' buffers
+        L.close()
+    del layers, xs
+    torch.cuda.empty_cache()
+    dist.barrier()
+    return ms_max, parity, stages, load, e2e_ms, clk.summary(), reps
+
+
+def run_ep(args, W, ws, rank, local, dev, dist):
+    """N > 1: the headline workload expert-parallel over the N GPUs (weak
+    scaling: tokens per GPU fixed), then configs[4] (the V3 layer under a
+    Zipf(1.1) expert popularity, 16384 tokens over the N GPUs)."""
+    T = W["T"]
+    ms, parity, stages, load, e2e_ms, clocks, reps = ep_measure(args, W, T, ws, rank, local, dev, dist)
+    value = ws * T / (ms / 1e3)
+    zipf = None
+    if W is V3 and not args.no_sublines:
+        Tz = 16384 // ws
+        _, _, gate_w = synth_weights(dict(W, E=W["E"]), args.seed, dev, experts=[])
+        bias, target = zipf_bias(W, gate_w, args.seed + 4)
+        dist.broadcast(bias, 0)
+        del gate_w
+        zs = max(10, min(args.steps, 100))
+        zms, zpar, zst, zload, ze2e, _, _ = ep_measure(args, W, Tz, ws, rank, local, dev, dist, bias=bias,
+                                                        steps=zs)
+        zipf = {"workload": "configs[4]: the configs[3] layer, 16384 bf16 tokens over the GPUs, per-expert "
+                            "selection bias giving a shifted Zipf(1.1) popularity (hottest ~8% of "
+                            "assignments) over a seeded expert permutation",
+                "value": 16384 / (zms / 1e3), "unit": UNIT, "ms_per_step": zms, "T_per_gpu": Tz,
+                "steps": zs, "parity": zpar, "stage_ms_rank0": zst, "load": zload,
+                "target_hottest_share": float(np.max(target)),
+                "e2e_ms_per_step": ze2e}
     if rank == 0:
         prefill = W["act"] == "bf16" and T * W["k"] // W["E"] >= 16
         gu_f, dn_f, fl = layer_flops(W, T)
         _, bf16, peak_kind = load_peaks()
         roof = None
         if prefill and stages.get("gate_up"):
-            # this rank's expert pass: its share of the routed flops (from the
-            # routing of its own tokens, a stand-in for what it received) and
-            # its own tokens' shared expert
             gu_tf = gu_f / (stages["gate_up"] / 1e3) / 1e12
             roof = {"bound": "tensor", "kernel": "qgemm_prefill gate/up + SwiGLU (rank 0)",
                     "achieved": gu_tf, "peak": bf16, "unit": "TFLOP/s", "frac": gu_tf / bf16,
                     "peak_kind": peak_kind, "traffic": None, "kernel_ms": stages["gate_up"],
-                    "note": "flops of one GPU's worth of tokens (the weak-scaling share)"}
+                    "note": "flops of one GPU's worth of tokens (the weak-scaling share of the "
+                            "routed work and this rank's shared-expert rows)"}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": W["act"], "data": "synthetic",
             "config": headline_config(W, ws, args),
@@ -946,19 +1000,16 @@ def run_ep(args, W, ws, rank, local, dev, dist):
             "roofline": roof,
             "parity": parity,
             "stage_ms_rank0": stages,
-            "load": {"routed_assignments_per_rank": per_rank,
-                     "imbalance_max_over_mean": max(per_rank) / max(1e-9, float(np.mean(per_rank)))},
+            "load": load,
             "e2e": {"value": ws * T / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": act_bytes(W) * T * W["H"] * ws,
                     "d2h_bytes_per_step": act_bytes(W) * T * W["H"] * ws, "ms_per_step": e2e_ms},
             "gpu_launches": (LAUNCHES["ep_prefill"] if prefill else LAUNCHES["ep_decode"]) * args.steps,
-            "clocks": clk.summary(),
+            "clocks": clocks,
         }
+        if zipf is not None:
+            line["zipf"] = zipf
         print(json.dumps(line), flush=True)
-    torch.cuda.synchronize()
-    dist.barrier()
-    for L in layers:          # every rank is done with the others' buffers
-        L.close()
     dist.barrier()
     dist.destroy_process_group()
 

@@ -104,6 +104,9 @@ int check_align(const void *p, int ptr_kind, const char *name) {
 }
 
 constexpr int kDecodeTok = 5;   // tokens per work item of the decode kernels
+// Host outputs up to this size are stored by the kernels straight into
+// page-locked host memory; larger ones are staged and copied back.
+constexpr size_t kMappedOutMaxBytes = size_t(2) << 20;
 // Auto path: the prefill GEMM once the routed positions per expert segment
 // (or the batch, for a shared-only pass) reach this many.
 constexpr int64_t kPrefillMinRows = 16;
@@ -972,7 +975,13 @@ static CombineParams combine_params(qmoe_layer *L, int64_t T, const ExpertsArgs 
 
 static int run_combine(qmoe_layer *L, int64_t T, const ExpertsArgs &a, void *outd, int dtype,
                        int accumulate) {
-    const CombineParams cp = combine_params(L, T, a, outd, dtype, accumulate);
+    CombineParams cp = combine_params(L, T, a, outd, dtype, accumulate);
+    if (a.ep_ret) {
+        // received rows go straight back to their origin ranks
+        cp.ep_ret = 1;
+        cp.ret = *a.ep_ret;
+        *a.returned = true;
+    }
     mark(L, 6);
     QTRY_CUDA(launch_combine(cp, L->ctx->stream));
     mark(L, 7);
@@ -1195,8 +1204,8 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
         g1.combine = 1;
         g1.c = combine_params(L, T, a, outd, dtype, accumulate);
         if (a.ep_ret) {
-            // one arrival per combine task: (row, 1024 columns)
-            a.ep_ret->ret_units = (int)((c.hidden_dim / 4 + 255) / 256);
+            // one arrival per combine task: (row, 1024 columns), the
+            // exchange's fixed ret_units per row
             g1.ep_ret = 1;
             g1.ret = *a.ep_ret;
             *a.returned = true;
@@ -1281,7 +1290,13 @@ int qmoe_layer_forward(qmoe_layer *L, const void *x, int dtype, int64_t T, void 
                                    front_cluster_ok(T, c.hidden_dim, c.num_experts, c.top_k)
                                ? mapped_host(x)
                                : nullptr;
-    void *out_mapped = ptr_kind == QMOE_PTR_HOST ? const_cast<void *>(mapped_host(out)) : nullptr;
+    // Outputs of decode-sized batches are written into page-locked host
+    // memory in place by the combine (no copy launch); larger ones go to a
+    // device buffer and back with one DMA copy, which moves bulk data over
+    // the bus faster than the kernel's scattered stores do.
+    void *out_mapped = ptr_kind == QMOE_PTR_HOST && xbytes <= kMappedOutMaxBytes
+                           ? const_cast<void *>(mapped_host(out))
+                           : nullptr;
     const void *xd;
     if (x_mapped) {
         QTRY(grow(L->x_in, xbytes));
@@ -1675,7 +1690,7 @@ int qmoe_ep_peer_create(qmoe_ctx *ctx, int world, int rank, int64_t capacity, in
     d.base[rank] = p->mem;
     d.seq = reinterpret_cast<int *>(p->mem + off_local);
     d.done = d.seq + 1;
-    d.ret_units = 1;
+    d.ret_units = (int)((H / 4 + 255) / 256);   // 1024-column slices per returned row
     d.err = error_flag();
     *out = p;
     return QMOE_OK;
@@ -1783,7 +1798,6 @@ int qmoe_layer_forward_ep_return(qmoe_layer *L, qmoe_ep_peer *p, const void *x, 
     a.shared_row0 = shared_row0;
     a.shared_count = L->has_shared ? R - shared_row0 : 0;
     bool returned = false;
-    p->d.ret_units = 1;
     a.ep_ret = &p->d;
     a.returned = &returned;
     a.wait_dispatch = true;

@@ -13,7 +13,7 @@ constexpr int kCombThreads = 256;
 constexpr int kCombVec = 4;        // float4 columns per thread
 
 __global__ void __launch_bounds__(kCombThreads)
-combine_kernel(const CombineParams p) {
+combine_kernel(const CombineParams p, int vec) {
     __shared__ int s_pos[kCombineMaxK];
     __shared__ float s_w[kCombineMaxK];
     __shared__ int s_n;
@@ -27,11 +27,28 @@ combine_kernel(const CombineParams p) {
     __syncthreads();
     const int n = s_n;
     const int H4 = p.H >> 2;
-#pragma unroll
-    for (int v = 0; v < kCombVec; ++v) {
-        const int c4 = (blockIdx.y * kCombVec + v) * kCombThreads + threadIdx.x;
-        if (c4 >= H4) break;
-        combine_float4(p, t, 4 * c4, n, s_pos, s_w);
+    // expert parallel: a received row's partial sum goes to its origin
+    // rank's return block; a row without live slots is not sent at all (its
+    // origin never reads it), but still counted
+    void *orow = nullptr;
+    int dst = -1;
+    if (p.ep_ret && t < (int64_t)p.ret.world * p.ret.C) {
+        dst = (int)(t / p.ret.C);
+        const int64_t i = t - (int64_t)dst * p.ret.C;
+        orow = p.ret.base[dst] + p.ret.off_back + ((int64_t)p.ret.rank * p.ret.C + i) * p.ret.H * p.ret.esize;
+    }
+    if (dst < 0 || n > 0)
+        for (int v = 0; v < vec; ++v) {
+            const int c4 = (blockIdx.y * vec + v) * kCombThreads + threadIdx.x;
+            if (c4 >= H4) break;
+            combine_float4(p, t, 4 * c4, n, s_pos, s_w, orow);
+        }
+    if (dst >= 0 && dst != p.ret.rank) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            atomicAdd_system(reinterpret_cast<int *>(p.ret.base[dst] + p.ret.off_flags) + p.ret.world + p.ret.rank, 1);
+        }
     }
 }
 
@@ -40,9 +57,12 @@ combine_kernel(const CombineParams p) {
 cudaError_t launch_combine(const CombineParams &p, cudaStream_t s) {
     if (p.T == 0 || p.H == 0) return cudaSuccess;
     if (p.K > kCombineMaxK) return cudaErrorInvalidValue;
-    const int per_cta = kCombThreads * kCombVec;
+    // expert parallel: slices of 1024 columns, one arrival each (the
+    // exchange's fixed ret_units per row)
+    const int vec = p.ep_ret ? 1 : kCombVec;
+    const int per_cta = kCombThreads * vec;
     const dim3 grid((unsigned)p.T, (unsigned)((p.H / 4 + per_cta - 1) / per_cta));
-    return launch_pdl(combine_kernel, grid, dim3(kCombThreads), 0, s, p);
+    return launch_pdl(combine_kernel, grid, dim3(kCombThreads), 0, s, p, vec);
 }
 
 }  // namespace qmoe

@@ -15,8 +15,6 @@
 namespace qmoe {
 namespace {
 
-constexpr int kPlanThreads = 1024;
-
 // Send list, destination-major and in token order within a destination
 // (compact: destination d's rows follow those of d-1; padded, capacity C > 0:
 // destination d's rows start at d*C and the unused rows carry ids -1, so
@@ -27,96 +25,100 @@ constexpr int kPlanThreads = 1024;
 //                           if slot k goes elsewhere (k < K)
 //   send_meta[s][K + k]     the bits of that slot's f32 combine weight (0 if -1)
 //   slot_pos[t][d]          send row of (t, d), -1 if t sends nothing to d
-// One CTA; tokens in tiles of 1024, one per thread; per destination a block
-// scan of the "sends to d" bits gives each token its row.
+// One CTA per tile of 256 tokens, none waiting on another: every CTA counts
+// the destinations of all tokens (those before its tile give its base in
+// each destination, all of them the totals), a block scan of the "sends to
+// d" bits gives each token of the tile its row, and the CTAs share out the
+// unused padded rows.
+constexpr int kPlanThreads = 256;
+
+QMOE_DEV uint32_t dest_mask(const EpPlanParams &p, int64_t t) {
+    uint32_t m = 0;
+    for (int k = 0; k < p.K; ++k) {
+        const int e = p.topk_idx[t * p.K + k];
+        if (e >= 0) m |= 1u << (e / p.experts_per_rank);
+    }
+    return m;
+}
+
 __global__ void __launch_bounds__(kPlanThreads)
 ep_plan_kernel(const EpPlanParams p) {
-    __shared__ int wsum[kPlanThreads / 32];
-    __shared__ int dcount[32];
-    __shared__ int tile_total;
+    __shared__ int s_before[kEpMaxWorld], s_total[kEpMaxWorld], s_base[kEpMaxWorld];
+    __shared__ int wsum[kPlanThreads / 32][kEpMaxWorld];
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = p.world, K = p.K;
-    // padded layout: every row starts unused
-    if (p.capacity > 0)
-        for (int64_t i = tid; i < (int64_t)G * p.capacity; i += kPlanThreads) {
-            p.send_tok[i] = 0;
-            for (int k = 0; k < K; ++k) {
-                p.send_meta[i * 2 * K + k] = -1;
-                p.send_meta[i * 2 * K + K + k] = 0;
-            }
-        }
-    // pass 1: tokens per destination
-    if (tid < G) dcount[tid] = 0;
+    const int64_t t0 = (int64_t)blockIdx.x * kPlanThreads;
+    if (tid < kEpMaxWorld) {
+        s_before[tid] = 0;
+        s_total[tid] = 0;
+    }
     __syncthreads();
+    // destinations of every token: counts before this tile and in total
     for (int64_t t = tid; t < p.T; t += kPlanThreads) {
-        uint32_t m = 0;
-        for (int k = 0; k < K; ++k) {
-            const int e = p.topk_idx[t * K + k];
-            if (e >= 0) m |= 1u << (e / p.experts_per_rank);
+        uint32_t m = dest_mask(p, t);
+        const bool before = t < t0;
+        while (m) {
+            const int d = __ffs(m) - 1;
+            m &= m - 1;
+            atomicAdd(&s_total[d], 1);
+            if (before) atomicAdd(&s_before[d], 1);
         }
-        for (int d = 0; d < G; ++d)
-            if (m >> d & 1u) atomicAdd(&dcount[d], 1);
     }
     __syncthreads();
     if (tid == 0) {
-        for (int d = 0; d < G; ++d) p.send_counts[d] = dcount[d];
-        // destination bases (kept in dcount): exclusive prefix, or d * C
         int run = 0;
         for (int d = 0; d < G; ++d) {
-            const int c = dcount[d];
-            dcount[d] = p.capacity > 0 ? (int)(d * p.capacity) : run;
-            run += c;
+            s_base[d] = p.capacity > 0 ? (int)(d * p.capacity) : run;
+            run += s_total[d];
         }
+        if (blockIdx.x == 0)
+            for (int d = 0; d < G; ++d) p.send_counts[d] = s_total[d];
+    }
+    // this tile: one token per thread, per destination a block scan
+    const int64_t t = t0 + tid;
+    const uint32_t m = t < p.T ? dest_mask(p, t) : 0u;
+    for (int d = 0; d < G; ++d) {
+        const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1u);
+        if (lane == 0) wsum[warp][d] = __popc(b);
     }
     __syncthreads();
-    // pass 2: rows, in token order within each destination
     for (int d = 0; d < G; ++d) {
-        int carry = 0;
-        for (int64_t t0 = 0; t0 < p.T; t0 += kPlanThreads) {
-            const int64_t t = t0 + tid;
-            int bit = 0;
-            if (t < p.T)
+        const bool bit = t < p.T && ((m >> d) & 1u);
+        const unsigned b = __ballot_sync(0xffffffffu, bit);
+        if (t < p.T) {
+            int pos = -1;
+            if (bit) {
+                int before_warps = 0;
+                for (int w = 0; w < warp; ++w) before_warps += wsum[w][d];
+                pos = s_base[d] + s_before[d] + before_warps + __popc(b & ((1u << lane) - 1u));
+                p.send_tok[pos] = (int32_t)t;
+                int32_t *mt = p.send_meta + (int64_t)pos * 2 * K;
                 for (int k = 0; k < K; ++k) {
                     const int e = p.topk_idx[t * K + k];
-                    if (e >= 0 && e / p.experts_per_rank == d) bit = 1;
+                    const bool mine = e >= 0 && e / p.experts_per_rank == d;
+                    mt[k] = mine ? e - d * p.experts_per_rank : -1;
+                    mt[K + k] = mine ? __float_as_int(p.topk_w[t * K + k]) : 0;
                 }
-            // block exclusive scan of bit
-            const unsigned b = __ballot_sync(0xffffffffu, bit);
-            const int in_warp = __popc(b & ((1u << lane) - 1u));
-            if (lane == 0) wsum[warp] = __popc(b);
-            __syncthreads();
-            if (warp == 0) {
-                const int v = wsum[lane];
-                int s = v;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int u = __shfl_up_sync(0xffffffffu, s, o);
-                    if (lane >= o) s += u;
-                }
-                wsum[lane] = s - v;
-                if (lane == 31) tile_total = s;
             }
-            __syncthreads();
-            if (t < p.T) {
-                int pos = -1;
-                if (bit) {
-                    pos = dcount[d] + carry + wsum[warp] + in_warp;
-                    p.send_tok[pos] = (int32_t)t;
-                    for (int k = 0; k < K; ++k) {
-                        const int e = p.topk_idx[t * K + k];
-                        const bool mine = e >= 0 && e / p.experts_per_rank == d;
-                        int32_t *m = p.send_meta + (int64_t)pos * 2 * K;
-                        m[k] = mine ? e - d * p.experts_per_rank : -1;
-                        m[K + k] = mine ? __float_as_int(p.topk_w[t * K + k]) : 0;
-                    }
-                }
-                p.slot_pos[t * G + d] = pos;
-            }
-            carry += tile_total;
-            __syncthreads();
+            p.slot_pos[t * G + d] = pos;
         }
+    }
+    // padded layout: the unused rows of every destination, shared out
+    if (p.capacity > 0) {
+        const int64_t C = p.capacity;
+        const int64_t stride = (int64_t)gridDim.x * kPlanThreads;
+        for (int d = 0; d < G; ++d)
+            for (int64_t i = s_total[d] + (int64_t)blockIdx.x * kPlanThreads + tid; i < C; i += stride) {
+                const int64_t r = d * C + i;
+                p.send_tok[r] = 0;
+                int32_t *mt = p.send_meta + r * 2 * K;
+                for (int k = 0; k < K; ++k) {
+                    mt[k] = -1;
+                    mt[K + k] = 0;
+                }
+            }
     }
 }
 
@@ -168,7 +170,8 @@ combine_rows_kernel(const void *rows, int dtype, int64_t H, const int32_t *slot_
 }  // namespace
 
 cudaError_t launch_ep_plan(const EpPlanParams &p, cudaStream_t s) {
-    return launch_pdl(ep_plan_kernel, dim3(1), dim3(kPlanThreads), 0, s, p);
+    const int64_t tiles = p.T > 0 ? (p.T + kPlanThreads - 1) / kPlanThreads : 1;
+    return launch_pdl(ep_plan_kernel, dim3((unsigned)tiles), dim3(kPlanThreads), 0, s, p);
 }
 
 cudaError_t launch_gather_rows(const void *x, int dtype, int64_t H, const int32_t *idx, int64_t n,

@@ -89,18 +89,33 @@ ep_dispatch_kernel(const EpPeerDev d, const void *x, int64_t T, const int32_t *s
 }
 
 // CTA j < world*C: the partial row j (rows received from rank j / C) goes to
-// that rank's return block.
+// that rank's return block, unless no slot of the row was routed here (its
+// metadata ids all -1: the origin never reads it); either way it counts the
+// exchange's ret_units arrivals.
 __global__ void __launch_bounds__(kCopyThreads)
 ep_return_kernel(const EpPeerDev d, const void *y) {
+    __shared__ int s_live;
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int64_t j = blockIdx.x;
     const int64_t rb = d.H * d.esize;
     const int dst = (int)(j / d.C);
     const int64_t i = j - (int64_t)dst * d.C;
-    copy_row(d.base[dst] + d.off_back + ((int64_t)d.rank * d.C + i) * rb,
-             static_cast<const uint8_t *>(y) + j * rb, rb);
-    arrive(d, dst, 1);
+    if (threadIdx.x < 32) {
+        const int32_t *m = reinterpret_cast<const int32_t *>(d.base[d.rank] + d.off_meta) + j * 2 * d.K;
+        const bool live = threadIdx.x < d.K && __ldcg(m + threadIdx.x) >= 0;
+        const bool any = __any_sync(0xffffffffu, live) || d.K > 32;
+        if (threadIdx.x == 0) s_live = any;
+    }
+    __syncthreads();
+    if (s_live)
+        copy_row(d.base[dst] + d.off_back + ((int64_t)d.rank * d.C + i) * rb,
+                 static_cast<const uint8_t *>(y) + j * rb, rb);
+    __syncthreads();
+    if (threadIdx.x == 0 && dst != d.rank) {
+        __threadfence_system();
+        atomicAdd_system(flag_at(d, dst, 1, d.rank), d.ret_units);
+    }
 }
 
 // Lane p waits until rank p's C rows of `phase` of this forward have

@@ -79,7 +79,8 @@ struct EpPeerDev {
     int64_t off_rows, off_meta, off_back, off_flags;
     int *seq;                    // this rank's per-forward sequence number
     int *done;                   // exit count of the return-side kernel (zero between launches)
-    int ret_units;               // arrivals per returned row (1, or the combine tasks per row)
+    int ret_units;               // arrivals per returned row: ceil(H / 1024), fixed per exchange
+                                 // (one per 1024-column slice of the row, whichever kernel returns it)
     int *err;                    // device error word
 };
 
@@ -166,6 +167,12 @@ struct CombineParams {
     int accumulate;              // add into out instead of overwriting
     void *out;                   // [T, H]
     int out_dtype;
+    // expert parallel (combine kernel): rows t < world * C are received rows;
+    // each goes straight to its origin rank's return block (peer memory),
+    // skipped when it has no live slot, and every 1024-column slice counts
+    // one arrival there
+    int ep_ret;
+    EpPeerDev ret;
 };
 cudaError_t launch_combine(const CombineParams &p, cudaStream_t s);
 

@@ -576,7 +576,10 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
                 orow = p.ret.base[dst] + p.ret.off_back + ((int64_t)p.ret.rank * p.ret.C + i) * p.ret.H * p.ret.esize;
             }
             const int c4 = ch * 256 + tid;
-            if (tid < 256 && c4 < H4) combine_float4(p.c, t, 4 * c4, S->c_n, S->c_pos, S->c_w, orow);
+            // a received row without live slots is never read by its origin:
+            // not sent, only counted
+            if (tid < 256 && c4 < H4 && (dst < 0 || S->c_n > 0))
+                combine_float4(p.c, t, 4 * c4, S->c_n, S->c_pos, S->c_w, orow);
             __syncthreads();
             if (tid == 0 && dst >= 0 && dst != p.ret.rank) {
                 __threadfence_system();

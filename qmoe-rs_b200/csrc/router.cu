@@ -201,27 +201,29 @@ router_logits_kernel(const RouterParams p) {
     }
 }
 
-// Whole logits for large batches on the paired FP32 pipe: fma.rn.f32x2 does
-// two IEEE fused multiply-adds per lane, each rounded exactly as fmaf, so
-// every (token, expert) chain is the pinned one: per 64-wide chunk an fmaf
-// chain from 0 over k in order, the chunk added to the running total in
-// chunk order (add.rn.f32x2, two IEEE adds).
+// Whole logits for large batches: fma.rn.f32x2 does two IEEE fused
+// multiply-adds per lane, each rounded exactly as fmaf, so every (token,
+// expert) chain is the pinned one: per 64-wide chunk an fmaf chain from 0
+// over k in order, the chunk added to the running total in chunk order
+// (add.rn.f32x2, two IEEE adds).
 //
-// CTA = 128 threads (4 warps) over 64 tokens x 128 experts (WE = 2; the
-// shape is a template so a 128 x 64 variant is one argument away); thread =
-// 8 tokens x 8 experts, accumulators
-// held as 32 pairs (token t, experts e, e+1).  Per chunk the shared memory
-// holds x as [k][token] with every value twice (x_t, x_t) -- one 16-byte
-// load gives the duplicated operands of two tokens -- and the transposed
-// gate as [k][expert] (gate_t, made once per layer), so a 16-byte load
-// gives two expert pairs.  Lanes are 4 token groups x 8 expert groups: the
-// four (eight) distinct 16-byte chunks a warp-wide load touches are
-// consecutive, one wavefront, each broadcast to the lanes that share it.
-// Two stages: the next chunk's gate tile arrives by cp.async and its x tile
-// through registers (converted from bf16 when needed) while this chunk is
-// computed.
-constexpr int kGemmThreads = 128;
+// CTA = 256 threads (8 warps: 2 along tokens x 4 along experts) over 64
+// tokens x 128 experts; thread = 8 tokens x 4 experts, accumulators held as
+// 16 pairs (token t, experts e, e+1).  Per chunk the shared memory holds x as
+// [k][token] with every value twice (x_t, x_t) -- one 16-byte load gives the
+// duplicated operands of two tokens -- and the transposed gate as
+// [k][expert] (gate_t, made once per layer), so a 16-byte load gives two
+// expert pairs.  Lanes are 4 token groups x 8 expert groups: the distinct
+// 16-byte chunks a warp-wide load touches are consecutive, one wavefront,
+// each broadcast to the lanes that share it.  Two stages: the next chunk's
+// gate tile arrives by cp.async and its x tile through registers
+// (converted from bf16 when needed) while this chunk is computed.
+constexpr int kGemmThreads = 256;
 constexpr int kGemmK = kGateChunk;       // 64: one chunk per stage
+constexpr int kGemmTokens = 64, kGemmExperts = 128;
+constexpr int kGemmXFloats = kGemmK * 2 * kGemmTokens;     // duplicated x tile
+constexpr int kGemmWFloats = kGemmK * kGemmExperts;
+constexpr int kGemmStageFloats = kGemmXFloats + kGemmWFloats;
 
 QMOE_DEV unsigned long long ffma2(unsigned long long a, unsigned long long b, unsigned long long c) {
     unsigned long long d;
@@ -241,101 +243,80 @@ QMOE_DEV void cp_async16(void *smem, const void *gmem, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem), "r"(n) : "memory");
 }
 
-template <int WE>
-struct GemmShape {
-    static constexpr int kWarpsT = 4 / WE;
-    static constexpr int kTokens = 32 * kWarpsT;        // per CTA
-    static constexpr int kExperts = 64 * WE;
-    static constexpr int kXFloats = kGemmK * 2 * kTokens;   // duplicated x tile
-    static constexpr int kWFloats = kGemmK * kExperts;
-    static constexpr int kStageFloats = kXFloats + kWFloats;
-};
+size_t router_gemm_smem_bytes() { return 2 * sizeof(float) * kGemmStageFloats; }
 
-size_t router_gemm_smem_bytes(int we) {
-    return we == 2 ? 2 * sizeof(float) * GemmShape<2>::kStageFloats
-                   : 2 * sizeof(float) * GemmShape<1>::kStageFloats;
-}
-
-template <int WE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 router_gemm_kernel(const RouterParams p) {
-    using S = GemmShape<WE>;
     extern __shared__ __align__(16) float gsm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int wt = warp % S::kWarpsT, we = warp / S::kWarpsT;
+    const int wt = warp & 1, we = warp >> 1;        // 2 x 4 warps
     const int tg = lane & 3, eg = lane >> 2;
-    const int64_t t0 = (int64_t)blockIdx.x * S::kTokens;
-    const int e0 = blockIdx.y * S::kExperts;
+    const int64_t t0 = (int64_t)blockIdx.x * kGemmTokens;
+    const int e0 = blockIdx.y * kGemmExperts;
     const int nc = p.H / kGemmK;
     const int ld = p.gate_t_ld;
 
     // gate tile of chunk c into stage st: rows k, 16-byte segments of experts
     auto load_w = [&](int c, int st) {
-        float *ws = gsm + st * S::kStageFloats + S::kXFloats;
-        constexpr int kSegs = S::kExperts / 4;                   // per row
-        for (int i = tid; i < kGemmK * kSegs; i += kGemmThreads) {
+        float *ws = gsm + st * kGemmStageFloats + kGemmXFloats;
+        constexpr int kSegs = kGemmExperts / 4;                  // per row
+#pragma unroll
+        for (int q = 0; q < kGemmK * kSegs / kGemmThreads; ++q) {
+            const int i = q * kGemmThreads + tid;
             const int k = i / kSegs, sgm = i % kSegs;
             const int e = e0 + 4 * sgm;
             const bool ok = e < ld;
             const float *src = p.gate_t + (int64_t)(c * kGemmK + k) * ld + (ok ? e : 0);
-            cp_async16(ws + k * S::kExperts + 4 * sgm, src, ok);
+            cp_async16(ws + k * kGemmExperts + 4 * sgm, src, ok);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    // x tile of chunk c: thread -> (token r = tid / 2 .. in steps, half h);
-    // 32 consecutive k of one token per thread and pass
-    constexpr int kPasses = S::kTokens / (kGemmThreads / 2);     // 1 or 2
-    uint4 xr[kPasses][8];                                        // up to 32 f32 or 32 bf16 (16 regs)
+    // x tile of chunk c: thread -> token r = tid / 4, quarter h = tid % 4
+    // (16 consecutive k of that token)
+    uint4 xr[4];                                                 // 16 f32 or 16 bf16 (2 used)
+    const int xr_r = tid >> 2, xr_h = tid & 3;
     auto fetch_x = [&](int c) {
+        const int64_t t = t0 + xr_r;
+        const int64_t base = t * p.H + c * kGemmK + xr_h * 16;
 #pragma unroll
-        for (int ps = 0; ps < kPasses; ++ps) {
-            const int r = ps * (kGemmThreads / 2) + (tid >> 1), h = tid & 1;
-            const int64_t t = t0 + r;
-            const int64_t base = t * p.H + c * kGemmK + h * 32;
+        for (int q = 0; q < 4; ++q) xr[q] = make_uint4(0, 0, 0, 0);
+        if (t < p.T) {
+            if (p.dtype == 0) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const float *>(p.x) + base);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) xr[ps][q] = make_uint4(0, 0, 0, 0);
-            if (t < p.T) {
-                if (p.dtype == 0) {
-                    const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const float *>(p.x) + base);
+                for (int q = 0; q < 4; ++q) xr[q] = __ldg(src + q);
+            } else {
+                const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(p.x) + base);
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) xr[ps][q] = __ldg(src + q);
-                } else {
-                    const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(p.x) + base);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) xr[ps][q] = __ldg(src + q);
-                }
+                for (int q = 0; q < 2; ++q) xr[q] = __ldg(src + q);
             }
         }
     };
     auto store_x = [&](int st) {
-        float *xs = gsm + st * S::kStageFloats;
+        float *xs = gsm + st * kGemmStageFloats;
+        float v[16];
+        if (p.dtype == 0) {
 #pragma unroll
-        for (int ps = 0; ps < kPasses; ++ps) {
-            const int r = ps * (kGemmThreads / 2) + (tid >> 1), h = tid & 1;
-            float v[32];
-            if (p.dtype == 0) {
+            for (int q = 0; q < 4; ++q) {
+                v[4 * q + 0] = __uint_as_float(xr[q].x);
+                v[4 * q + 1] = __uint_as_float(xr[q].y);
+                v[4 * q + 2] = __uint_as_float(xr[q].z);
+                v[4 * q + 3] = __uint_as_float(xr[q].w);
+            }
+        } else {
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    v[4 * q + 0] = __uint_as_float(xr[ps][q].x);
-                    v[4 * q + 1] = __uint_as_float(xr[ps][q].y);
-                    v[4 * q + 2] = __uint_as_float(xr[ps][q].z);
-                    v[4 * q + 3] = __uint_as_float(xr[ps][q].w);
-                }
-            } else {
+            for (int q = 0; q < 2; ++q) {
+                const uint32_t u[4] = {xr[q].x, xr[q].y, xr[q].z, xr[q].w};
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t u[4] = {xr[ps][q].x, xr[ps][q].y, xr[ps][q].z, xr[ps][q].w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        v[8 * q + 2 * j] = __uint_as_float(u[j] << 16);
-                        v[8 * q + 2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
-                    }
+                for (int j = 0; j < 4; ++j) {
+                    v[8 * q + 2 * j] = __uint_as_float(u[j] << 16);
+                    v[8 * q + 2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
                 }
             }
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                *reinterpret_cast<float2 *>(xs + (h * 32 + j) * (2 * S::kTokens) + 2 * r) = make_float2(v[j], v[j]);
         }
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            *reinterpret_cast<float2 *>(xs + (xr_h * 16 + j) * (2 * kGemmTokens) + 2 * xr_r) = make_float2(v[j], v[j]);
     };
 
     // the gate is the layer's, independent of the preceding kernel
@@ -345,15 +326,16 @@ router_gemm_kernel(const RouterParams p) {
     fetch_x(0);
     store_x(0);
 
-    unsigned long long acc[8][4], tot[8][4];
+    unsigned long long acc[8][2], tot[8][2];
 #pragma unroll
     for (int a = 0; a < 8; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) tot[a][b] = 0ull;
+        for (int b = 0; b < 2; ++b) tot[a][b] = 0ull;
 
-    // this thread's operand offsets within a stage (16-byte units)
-    const int xo = wt * 16 + tg;          // + 4 j (j < 4): tokens 2 (wt*16 + tg + 4j) + {0,1}
-    const int wo = we * 16 + eg;          // + 8 j (j < 2): experts 4 (we*16 + eg + 8j) + {0..3}
+    // this thread's operand offsets within a stage (16-byte units):
+    // tokens 2 (wt*16 + tg + 4j) + {0, 1} (j < 4), experts 4 (we*8 + eg) + {0..3}
+    const int xo = wt * 16 + tg;
+    const int wo = we * 8 + eg;
 
     for (int c = 0; c < nc; ++c) {
         const int st = c & 1;
@@ -363,38 +345,34 @@ router_gemm_kernel(const RouterParams p) {
             load_w(c + 1, st ^ 1);
             fetch_x(c + 1);
         }
-        const ulonglong2 *xs = reinterpret_cast<const ulonglong2 *>(gsm + st * S::kStageFloats);
-        const ulonglong2 *ws = reinterpret_cast<const ulonglong2 *>(gsm + st * S::kStageFloats + S::kXFloats);
+        const ulonglong2 *xs = reinterpret_cast<const ulonglong2 *>(gsm + st * kGemmStageFloats);
+        const ulonglong2 *ws = reinterpret_cast<const ulonglong2 *>(gsm + st * kGemmStageFloats + kGemmXFloats);
 #pragma unroll
         for (int a = 0; a < 8; ++a)
 #pragma unroll
-            for (int b = 0; b < 4; ++b) acc[a][b] = 0ull;
-#pragma unroll 4
+            for (int b = 0; b < 2; ++b) acc[a][b] = 0ull;
+#pragma unroll 8
         for (int k = 0; k < kGemmK; ++k) {
-            ulonglong2 xv[4], wv[2];
+            ulonglong2 xv[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) xv[j] = xs[k * (S::kTokens / 2) + xo + 4 * j];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) wv[j] = ws[k * (S::kExperts / 4) + wo + 8 * j];
+            for (int j = 0; j < 4; ++j) xv[j] = xs[k * (kGemmTokens / 2) + xo + 4 * j];
+            const ulonglong2 wv = ws[k * (kGemmExperts / 4) + wo];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    acc[2 * j][2 * q] = ffma2(xv[j].x, wv[q].x, acc[2 * j][2 * q]);
-                    acc[2 * j][2 * q + 1] = ffma2(xv[j].x, wv[q].y, acc[2 * j][2 * q + 1]);
-                    acc[2 * j + 1][2 * q] = ffma2(xv[j].y, wv[q].x, acc[2 * j + 1][2 * q]);
-                    acc[2 * j + 1][2 * q + 1] = ffma2(xv[j].y, wv[q].y, acc[2 * j + 1][2 * q + 1]);
-                }
+                acc[2 * j][0] = ffma2(xv[j].x, wv.x, acc[2 * j][0]);
+                acc[2 * j][1] = ffma2(xv[j].x, wv.y, acc[2 * j][1]);
+                acc[2 * j + 1][0] = ffma2(xv[j].y, wv.x, acc[2 * j + 1][0]);
+                acc[2 * j + 1][1] = ffma2(xv[j].y, wv.y, acc[2 * j + 1][1]);
             }
         }
 #pragma unroll
         for (int a = 0; a < 8; ++a)
 #pragma unroll
-            for (int b = 0; b < 4; ++b) tot[a][b] = fadd2(tot[a][b], acc[a][b]);
+            for (int b = 0; b < 2; ++b) tot[a][b] = fadd2(tot[a][b], acc[a][b]);
         if (c + 1 < nc) store_x(st ^ 1);
     }
-    // tokens 2 (wt*16 + tg + 4j) + u -> acc row 2j + u; experts
-    // 4 (we*16 + eg + 8q) + {0,1,2,3} -> acc column pairs 2q, 2q + 1
+    // acc row 2j + u = token 2 (wt*16 + tg + 4j) + u; acc column pair hb =
+    // experts 4 (we*8 + eg) + 2 hb + {0, 1}
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
@@ -402,14 +380,12 @@ router_gemm_kernel(const RouterParams p) {
             const int64_t t = t0 + 2 * (wt * 16 + tg + 4 * j) + u;
             if (t >= p.T) continue;
 #pragma unroll
-            for (int q = 0; q < 2; ++q)
-#pragma unroll
-                for (int hb = 0; hb < 2; ++hb) {
-                    const unsigned long long v = tot[2 * j + u][2 * q + hb];
-                    const int e = e0 + 4 * (we * 16 + eg + 8 * q) + 2 * hb;
-                    if (e < p.E) p.scratch[t * p.E + e] = __uint_as_float((uint32_t)v);
-                    if (e + 1 < p.E) p.scratch[t * p.E + e + 1] = __uint_as_float((uint32_t)(v >> 32));
-                }
+            for (int hb = 0; hb < 2; ++hb) {
+                const unsigned long long v = tot[2 * j + u][hb];
+                const int e = e0 + 4 * (we * 8 + eg) + 2 * hb;
+                if (e < p.E) p.scratch[t * p.E + e] = __uint_as_float((uint32_t)v);
+                if (e + 1 < p.E) p.scratch[t * p.E + e + 1] = __uint_as_float((uint32_t)(v >> 32));
+            }
         }
 }
 
@@ -766,12 +742,12 @@ cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaSt
     const bool gemm = router_uses_gemm(p);
     const bool parts = !gemm && router_uses_partials(p.T, p.H, p.E);
     if (gemm) {
-        const size_t smem = router_gemm_smem_bytes(2);
-        cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(router_gemm_kernel<2>), smem);
+        const size_t smem = router_gemm_smem_bytes();
+        cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(router_gemm_kernel), smem);
         if (e != cudaSuccess) return e;
-        dim3 grid((unsigned)((p.T + GemmShape<2>::kTokens - 1) / GemmShape<2>::kTokens),
-                  (unsigned)((p.E + GemmShape<2>::kExperts - 1) / GemmShape<2>::kExperts));
-        e = launch_pdl(router_gemm_kernel<2>, grid, dim3(kGemmThreads), smem, s, p);
+        dim3 grid((unsigned)((p.T + kGemmTokens - 1) / kGemmTokens),
+                  (unsigned)((p.E + kGemmExperts - 1) / kGemmExperts));
+        e = launch_pdl(router_gemm_kernel, grid, dim3(kGemmThreads), smem, s, p);
         if (e != cudaSuccess) return e;
     } else if (parts) {
         const int nc = p.H / kGateChunk;
