@@ -240,6 +240,29 @@ QMOE_API int qmoe_layer_forward_routed(qmoe_layer *layer, const void *x, int dty
 QMOE_API int qmoe_layer_shared_forward(qmoe_layer *layer, const void *x, int dtype,
                               int64_t T, void *out, int accumulate, int ptr_kind);
 
+/* ---- decoder-layer MoE block (src/model.rs:359-412) ----------------------- */
+
+/* The decoder layer's post_attention_layernorm (candle_nn::layer_norm,
+ * src/model.rs:366-367): weight and bias [hidden_dim] f32, eps (1e-6 there).
+ * Copied; a later call replaces them.  Needed by qmoe_layer_forward_block. */
+QMOE_API int qmoe_layer_set_norm(qmoe_layer *layer, const float *weight, const float *bias,
+                                 float eps, int ptr_kind);
+
+/*
+ * The MoE half of DecoderLayer::forward_with_cache / forward_prefill
+ * (src/model.rs:400-412, :380-389): with x the residual stream after the
+ * attention add,
+ *     y   = post_attention_layernorm(x)
+ *     out = x + (QMoELayer::forward(y) + SharedExpert::forward(y))
+ * The normalisation runs as one kernel in a pinned order (64-wide chunk
+ * sums added in order; the CPU oracle computes the same operations); the
+ * residual add is the last operation of the combine.  x, out [T, hidden_dim]
+ * in dtype; topk_idx / topk_w optional as in qmoe_layer_forward.  A layer
+ * without routed experts gives x + shared(y) (or x).
+ */
+QMOE_API int qmoe_layer_forward_block(qmoe_layer *layer, const void *x, int dtype, int64_t T,
+                                      void *out, int32_t *topk_idx, float *topk_w, int ptr_kind);
+
 /* ---- allocation-free packed GEMV ---------------------------------------- */
 
 /* Limits of qmoe_packed_forward_noalloc. */

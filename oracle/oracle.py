@@ -13,6 +13,9 @@ qmoe-rs project root):
   moe_forward      src/moe.rs:40-130
   shared_forward   src/model.rs:325-347
   layer_forward    src/model.rs:386-389 (moe_out + shared_out)
+  layernorm        post_attention_layernorm, src/model.rs:366-367, :401-403
+                   (pinned order standing in for candle's layer_norm)
+  block_forward    the MoE half of DecoderLayer::forward_*, src/model.rs:400-412
 """
 from __future__ import annotations
 
@@ -117,6 +120,8 @@ def lib():
         L.qo_experts_forward.restype = None
         L.qo_experts_forward.argtypes = [ctypes.POINTER(QoConfig), P, P, P, i64, P, P, P,
                                          ctypes.c_int]
+        L.qo_layernorm.restype = None
+        L.qo_layernorm.argtypes = [P, P, P, ctypes.c_float, i64, i64, ctypes.c_int, P]
         L.qo_dequantize.restype = None
         L.qo_dequantize.argtypes = [P, P, i64, i64, P]
         _lib = L
@@ -285,3 +290,25 @@ def dequantize(packed, scales, shape):
     w = np.empty((out_f, in_f), np.float32)
     lib().qo_dequantize(_p(packed), _p(scales), out_f, in_f, _p(w))
     return w
+
+
+def layernorm(x, w, b, eps: float = 1e-6, round_bf16: bool = False):
+    """Pinned-order LayerNorm of the rows of x (see qo_layernorm)."""
+    x = _f32(x)
+    w, b = _f32(w), _f32(b)
+    T, H = x.shape
+    y = np.empty_like(x)
+    lib().qo_layernorm(_p(x), _p(w), _p(b), ctypes.c_float(eps), T, H, int(round_bf16), _p(y))
+    return y
+
+
+def block_forward(cfg: MoEConfig, gate_w, experts, x, ln_w, ln_b, eps: float = 1e-6, shared=None,
+                  bias=None, nthreads: int = 1, round_bf16: bool = False):
+    """The MoE half of a decoder layer (src/model.rs:400-412): y =
+    post_attention_layernorm(x); out = x + (moe(y) + shared(y)).  With
+    round_bf16 the normalised rows are rounded to bf16 first (a bf16
+    forward's router and experts read them so).  Returns (out, idx, w)."""
+    x = _f32(x)
+    y = layernorm(x, ln_w, ln_b, eps, round_bf16)
+    moe, idx, w = layer_forward(cfg, gate_w, experts, y, shared=shared, bias=bias, nthreads=nthreads)
+    return (x + moe).astype(np.float32), idx, w

@@ -588,3 +588,70 @@ void qo_dequantize(const uint8_t *packed, const float *scales, int64_t out_f,
             w[o * in_f + k] = c * scales[o];
         }
 }
+
+/* ---------------------------------------------------------------------- */
+/* Decoder-layer MoE block: post-attention LayerNorm (src/model.rs:366-367, */
+/* :400-403) and the residual add (:409-412)                                */
+/* ---------------------------------------------------------------------- */
+/*
+ * candle_nn::layer_norm(hidden, 1e-6) normalises each row with its mean and
+ * biased variance and applies weight and bias.  candle's summation order is
+ * not observable here (third-party, not vendored), so this pins one, in the
+ * same 64-wide chunks as the gate logits:
+ *   s1   = ((0 + p_0) + p_1) + ...,  p_c = sequential f32 sum of chunk c
+ *   mean = s1 / H
+ *   s2   = ((0 + q_0) + q_1) + ...,  q_c = fmaf chain of d*d over chunk c,
+ *          d = x - mean
+ *   rstd = 1 / sqrtf(s2 / H + eps)
+ *   y    = ((x - mean) * rstd) * w + b   (each operation rounded once)
+ * The CUDA kernel computes the same operations in the same order.  With
+ * round_bf16 the result is rounded to bf16 (round to nearest even), what a
+ * bf16 forward hands to its router and experts.
+ */
+static float qo_round_bf16(float v)
+{
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u) {       /* inf / nan: keep, quiet nan */
+        if (u & 0x007fffffu) u |= 0x00400000u;
+        u &= 0xffff0000u;
+    } else {
+        u += 0x7fffu + ((u >> 16) & 1u);
+        u &= 0xffff0000u;
+    }
+    float r;
+    memcpy(&r, &u, 4);
+    return r;
+}
+
+void qo_layernorm(const float *x, const float *w, const float *b, float eps, int64_t T,
+                  int64_t H, int round_bf16, float *y)
+{
+    for (int64_t t = 0; t < T; ++t) {
+        const float *xv = x + t * H;
+        float s1 = 0.0f;
+        for (int64_t c0 = 0; c0 < H; c0 += QO_GATE_CHUNK) {
+            int64_t c1 = c0 + QO_GATE_CHUNK < H ? c0 + QO_GATE_CHUNK : H;
+            float p = 0.0f;
+            for (int64_t k = c0; k < c1; ++k) p = p + xv[k];
+            s1 = s1 + p;
+        }
+        const float mean = s1 / (float)H;
+        float s2 = 0.0f;
+        for (int64_t c0 = 0; c0 < H; c0 += QO_GATE_CHUNK) {
+            int64_t c1 = c0 + QO_GATE_CHUNK < H ? c0 + QO_GATE_CHUNK : H;
+            float q = 0.0f;
+            for (int64_t k = c0; k < c1; ++k) {
+                const float d = xv[k] - mean;
+                q = fmaf(d, d, q);
+            }
+            s2 = s2 + q;
+        }
+        const float rstd = 1.0f / sqrtf(s2 / (float)H + eps);
+        for (int64_t k = 0; k < H; ++k) {
+            const float n = (xv[k] - mean) * rstd;
+            const float v = n * w[k] + b[k];
+            y[t * H + k] = round_bf16 ? qo_round_bf16(v) : v;
+        }
+    }
+}

@@ -181,6 +181,10 @@ struct qmoe_layer {
     bool has_shared = false;
     float *gate_w = nullptr, *bias = nullptr;
     float *gate_t = nullptr;   // [H][gate_t_ld(E)] transposed gate (E > 64), for large-batch logits
+    // the decoder layer's post-attention LayerNorm (qmoe_layer_set_norm)
+    float *ln_w = nullptr, *ln_b = nullptr;
+    float ln_eps = 1e-6f;
+    DevBuf xn;                 // normalised rows of a block forward
     uint8_t *w[3] = {nullptr, nullptr, nullptr};
     float *s[3] = {nullptr, nullptr, nullptr};
     uint8_t *ws[3] = {nullptr, nullptr, nullptr};
@@ -540,6 +544,9 @@ int qmoe_layer_destroy(qmoe_layer *L) {
     }
     if (L->gate_w) cudaFree(L->gate_w);
     if (L->gate_t) cudaFree(L->gate_t);
+    if (L->ln_w) cudaFree(L->ln_w);
+    if (L->ln_b) cudaFree(L->ln_b);
+    release(L->xn);
     if (L->bias) cudaFree(L->bias);
     for (cudaEvent_t &e : L->ev)
         if (e) cudaEventDestroy(e);
@@ -948,6 +955,7 @@ struct ExpertsArgs {
                                   // rows' partial sums straight to their origin ranks
     bool *returned = nullptr;     // set when it did (else the caller runs the return kernel)
     bool wait_dispatch = false;   // the permute first waits for the peers' rows (ep_ret's flags)
+    const void *residual = nullptr;  // block forward: the residual stream, added by the combine
 };
 
 // Weighted sum of each token's expert rows in ascending expert order, plus
@@ -968,6 +976,7 @@ static CombineParams combine_params(qmoe_layer *L, int64_t T, const ExpertsArgs 
     cp.shared_row0 = a.shared_row0;
     cp.shared_count = a.shared_count;
     cp.accumulate = accumulate;
+    cp.residual = a.residual;
     cp.out = outd;
     cp.out_dtype = dtype;
     return cp;
@@ -1816,6 +1825,92 @@ int qmoe_ep_finish(qmoe_ep_peer *p, const int32_t *slot_pos, int64_t T, const vo
     if (extra) QTRY(check_align(extra, QMOE_PTR_DEVICE, "extra"));
     DeviceGuard g(p->ctx->device);
     QTRY_CUDA(launch_ep_finish(p->d, slot_pos, T, extra, out, p->ctx->stream));
+    return QMOE_OK;
+}
+
+int qmoe_layer_set_norm(qmoe_layer *L, const float *weight, const float *bias, float eps, int ptr_kind) {
+    if (!L || !weight || !bias) return fail(QMOE_ERR_INVALID, "NULL argument");
+    QTRY(check_ptr_kind(ptr_kind));
+    if (!(eps >= 0.0f)) return fail(QMOE_ERR_INVALID, "eps must be >= 0");
+    DeviceGuard g(L->ctx->device);
+    const size_t nb = sizeof(float) * L->cfg.hidden_dim;
+    if (!L->ln_w) QTRY_CUDA(cudaMalloc((void **)&L->ln_w, nb));
+    if (!L->ln_b) QTRY_CUDA(cudaMalloc((void **)&L->ln_b, nb));
+    QTRY_CUDA(cudaMemcpyAsync(L->ln_w, weight, nb, kind_in(ptr_kind), L->ctx->stream));
+    QTRY_CUDA(cudaMemcpyAsync(L->ln_b, bias, nb, kind_in(ptr_kind), L->ctx->stream));
+    QTRY_CUDA(cudaStreamSynchronize(L->ctx->stream));
+    L->ln_eps = eps;
+    return QMOE_OK;
+}
+
+int qmoe_layer_forward_block(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
+                             int32_t *topk_idx, float *topk_w, int ptr_kind) {
+    if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
+    QTRY(check_ptr_kind(ptr_kind));
+    QTRY(check_dtype(dtype));
+    if (!L->ln_w) return fail(QMOE_ERR_INVALID, "no LayerNorm set (qmoe_layer_set_norm)");
+    if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
+    if (T > 0 && (!x || !out)) return fail(QMOE_ERR_INVALID, "NULL x or out");
+    if (L->e_count > 0 && (L->e_begin != 0 || L->e_count != L->cfg.num_experts))
+        return fail(QMOE_ERR_INVALID, "a block forward needs all experts local");
+    if (T == 0) return QMOE_OK;
+    QTRY(check_align(x, ptr_kind, "x"));
+    QTRY(check_align(out, ptr_kind, "out"));
+    DeviceGuard g(L->ctx->device);
+    cudaStream_t st = L->ctx->stream;
+    QTRY(layer_reserve(L, T));
+    const qmoe_moe_config &c = L->cfg;
+    const size_t xbytes = dtype_size(dtype) * T * c.hidden_dim;
+    const void *xd;
+    QTRY(stage_in(L->x_in, x, xbytes, ptr_kind, st, &xd));
+    void *outd = out;
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY(grow(L->io_out, xbytes));
+        outd = L->io_out.p;
+    }
+    // post_attention_layernorm (src/model.rs:401-403) into the block's rows
+    QTRY(grow(L->xn, xbytes));
+    NormParams np{xd, dtype, T, c.hidden_dim, L->ln_w, L->ln_b, L->ln_eps, L->xn.p};
+    QTRY_CUDA(launch_layernorm(np, st));
+    const void *xn = L->xn.p;
+    ExpertsArgs a;
+    a.residual = xd;                          // residual + (moe + shared), src/model.rs:409-412
+    const size_t kb = sizeof(int32_t) * T * c.top_k;
+    if (L->e_count == 0) {
+        // no routed experts (src/moe.rs:46-48): x + shared(LN(x)), or x
+        if (topk_idx) QTRY_CUDA(cudaMemsetAsync(L->topk_idx.p, 0xff, kb, st));
+        if (topk_w) QTRY_CUDA(cudaMemsetAsync(L->topk_w.p, 0, kb, st));
+        if (L->has_shared) {
+            qmoe_moe_config saved = L->cfg;
+            L->cfg.top_k = 0;
+            a.shared_count = T;
+            const int rc = run_experts(L, xn, dtype, T, a, outd, 0);
+            L->cfg = saved;
+            if (rc != QMOE_OK) return rc;
+        } else {
+            QTRY_CUDA(cudaMemcpyAsync(outd, xd, xbytes, cudaMemcpyDeviceToDevice, st));
+        }
+    } else {
+        a.topk_idx = L->topk_idx.as<int32_t>();
+        a.topk_w = L->topk_w.as<float>();
+        a.topk_ld = c.top_k;
+        a.shared_count = L->has_shared ? T : 0;
+        const bool front = router_tail_ok(T, c.num_experts, c.top_k);
+        bool prefill = false;
+        QTRY(choose_prefill(L, dtype, T, c.top_k, &prefill));
+        if (front) {
+            QTRY(run_front(L, xn, dtype, T, prefill));
+            a.permuted = true;
+        } else {
+            QTRY(run_router(L, xn, dtype, T));
+        }
+        QTRY(run_experts(L, xn, dtype, T, a, outd, 0));
+    }
+    const cudaMemcpyKind k = ptr_kind == QMOE_PTR_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+    if (topk_idx) QTRY_CUDA(cudaMemcpyAsync(topk_idx, L->topk_idx.p, kb, k, st));
+    if (topk_w) QTRY_CUDA(cudaMemcpyAsync(topk_w, L->topk_w.p, kb, k, st));
+    QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
+    if (ptr_kind == QMOE_PTR_HOST) QTRY(sync_and_check(st));
     return QMOE_OK;
 }
 

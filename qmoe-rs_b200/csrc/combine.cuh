@@ -90,6 +90,14 @@ QMOE_DEV void combine_float4(const CombineParams &p, int64_t t, int h, int n, co
         a2 = __fadd_rn(a2, sv.z);
         a3 = __fadd_rn(a3, sv.w);
     }
+    if (p.residual) {
+        // residual + (moe_out + shared_out) (src/model.rs:409-412)
+        const float4 r = load_act4_cg(p.residual, p.out_dtype, t * p.H + h);
+        a0 = __fadd_rn(r.x, a0);
+        a1 = __fadd_rn(r.y, a1);
+        a2 = __fadd_rn(r.z, a2);
+        a3 = __fadd_rn(r.w, a3);
+    }
     const int64_t o = orow ? h : t * p.H + h;
     void *ob = orow ? orow : p.out;
     if (p.out_dtype == 0) {

@@ -165,6 +165,8 @@ struct CombineParams {
     const float *y_shared;       // [shared_count, H] for rows shared_row0.. or nullptr
     int64_t shared_row0, shared_count;
     int accumulate;              // add into out instead of overwriting
+    const void *residual;        // [T, H] in out_dtype, added last (nullable): the decoder
+                                 // layer's residual stream (src/model.rs:409-412)
     void *out;                   // [T, H]
     int out_dtype;
     // expert parallel (combine kernel): rows t < world * C are received rows;
@@ -175,6 +177,18 @@ struct CombineParams {
     EpPeerDev ret;
 };
 cudaError_t launch_combine(const CombineParams &p, cudaStream_t s);
+
+// ---- post-attention LayerNorm (norm.cu) ----------------------------------
+struct NormParams {
+    const void *x;               // [T, H] f32 or bf16
+    int dtype;
+    int64_t T;
+    int H;                       // multiple of 64
+    const float *w, *b;          // [H]
+    float eps;
+    void *y;                     // [T, H] in x's dtype
+};
+cudaError_t launch_layernorm(const NormParams &p, cudaStream_t s);
 
 // 2-bit packer (pack.cu): qmoe-rs quantize.py:7-33 with the row scale of
 // :97-100.  w [out_f, in_f] f32 (16-byte aligned, in_f a multiple of 4) ->

@@ -368,6 +368,53 @@ class QMoELayer:
         capi.call("qmoe_layer_shared_forward", self._h, xp, dt, T, op, int(acc), kind)
         return out
 
+    def set_norm(self, weight, bias, eps: float = 1e-6) -> None:
+        """The decoder layer's post_attention_layernorm (src/model.rs:366-367):
+        weight and bias [hidden_dim] f32."""
+        keep = []
+        ptrs = []
+        kinds = set()
+        for a in (weight, bias):
+            if not (torch is not None and isinstance(a, torch.Tensor)):
+                a = np.ascontiguousarray(a, dtype=np.float32)
+            p, k, ka = _ptr(a)
+            keep.append(ka)
+            ptrs.append(p)
+            kinds.add(k)
+        if len(kinds) != 1:
+            raise ValueError("weight and bias must both be host or both device memory")
+        kind = kinds.pop()
+        if kind == capi.QMOE_PTR_DEVICE:
+            self.ctx.use_current_torch_stream()
+        capi.call("qmoe_layer_set_norm", self._h, ptrs[0], ptrs[1], float(eps), kind)
+
+    def forward_block(self, xs, return_routing: bool = False, out=None):
+        """The MoE half of a decoder layer (src/model.rs:400-412): xs + moe(LN(xs))
+        + shared(LN(xs)), with LN the post-attention LayerNorm set by set_norm."""
+        T, H = xs.shape
+        if H != self.config.hidden_dim:
+            raise ValueError(f"hidden dim {H} != {self.config.hidden_dim}")
+        dt = _dtype_code(xs)
+        if out is None:
+            out = _empty_like_kind(xs, (T, H), dt)
+        K = self.config.top_k
+        idx = w = None
+        ip = wp = None
+        if return_routing:
+            idx = _empty_aux(xs, (T, K), np.int32, torch.int32 if torch else None)
+            w = _empty_aux(xs, (T, K), np.float32, torch.float32 if torch else None)
+            ip, wp = _ptr(idx)[0], _ptr(w)[0]
+        xp, kind, keep = _ptr(xs)
+        op, okind, _ = _ptr(out)
+        if okind != kind:
+            raise ValueError("x and out must both be host or both device memory")
+        if kind == capi.QMOE_PTR_DEVICE:
+            self.ctx.use_current_torch_stream()
+        capi.call("qmoe_layer_forward_block", self._h, xp, dt, T, op, ip, wp, kind)
+        if return_routing:
+            return out, idx, w
+        return out
+
     def reserve(self, max_tokens: int) -> None:
         capi.call("qmoe_layer_reserve", self._h, int(max_tokens))
 

@@ -245,3 +245,21 @@ def test_softmax_renorm_flag():
 def test_invalid_routing_rejected():
     with pytest.raises(ValueError):
         qo.route(qo.MoEConfig(4, 5, 64, 128), np.zeros((1, 4), np.float32))
+
+
+def test_oracle_layernorm_against_float64_reference():
+    # the pinned-order LayerNorm of the oracle (post_attention_layernorm,
+    # src/model.rs:366-367) is a LayerNorm: within f32 rounding of torch's
+    # float64 result; its bf16 rounding is round-to-nearest-even
+    import torch
+    rng = np.random.default_rng(3)
+    for H in (64, 512, 7168):
+        x = (rng.standard_normal((7, H)) * 3 + 1.5).astype(np.float32)
+        w = rng.standard_normal(H).astype(np.float32)
+        b = rng.standard_normal(H).astype(np.float32)
+        y = qo.layernorm(x, w, b, 1e-6)
+        ref = torch.nn.functional.layer_norm(torch.from_numpy(x).double(), (H,), torch.from_numpy(w).double(),
+                                             torch.from_numpy(b).double(), eps=1e-6).numpy()
+        assert np.max(np.abs(y - ref)) <= 2e-5 * max(1.0, np.max(np.abs(ref)))
+        yb = qo.layernorm(x, w, b, 1e-6, round_bf16=True)
+        assert np.array_equal(yb, torch.from_numpy(y).bfloat16().float().numpy())
