@@ -263,6 +263,24 @@ QMOE_API int qmoe_layer_set_norm(qmoe_layer *layer, const float *weight, const f
 QMOE_API int qmoe_layer_forward_block(qmoe_layer *layer, const void *x, int dtype, int64_t T,
                                       void *out, int32_t *topk_idx, float *topk_w, int ptr_kind);
 
+/*
+ * Consecutive blocks: the layer loop of DeepSeekCoderV2::forward_next /
+ * forward_prefill (src/model.rs:447-453, :481-489) over the MoE halves of
+ * the decoder layers, the attention halves left out:
+ *     out = block_{n-1}( ... block_1(block_0(x)) ... )
+ * with block_l = qmoe_layer_forward_block of layers[l] (each with its
+ * LayerNorm set; all on one context and of one hidden_dim).  The first call
+ * for a given x, out, T and dtype captures the whole launch sequence into one
+ * CUDA graph; repeats replay it (one graph launch for all layers; not on the
+ * legacy default stream, which cannot be captured).  Intermediate rows live
+ * in two buffers the chain owns.
+ */
+typedef struct qmoe_chain qmoe_chain;
+QMOE_API int qmoe_chain_create(qmoe_layer *const *layers, int n_layers, qmoe_chain **out);
+QMOE_API int qmoe_chain_destroy(qmoe_chain *chain);
+QMOE_API int qmoe_chain_forward(qmoe_chain *chain, const void *x, int dtype, int64_t T, void *out,
+                                int ptr_kind);
+
 /* ---- allocation-free packed GEMV ---------------------------------------- */
 
 /* Limits of qmoe_packed_forward_noalloc. */

@@ -5,6 +5,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../../include/qmoe_b200.h"
 #include "combine.cuh"
@@ -1843,16 +1844,70 @@ int qmoe_layer_set_norm(qmoe_layer *L, const float *weight, const float *bias, f
     return QMOE_OK;
 }
 
-int qmoe_layer_forward_block(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
-                             int32_t *topk_idx, float *topk_w, int ptr_kind) {
+// The block's device work on the layer's stream: LayerNorm of xd into the
+// layer's rows, the router and experts on them, the combine adding the
+// residual xd into outd.  Needs layer_reserve(L, T) and L->xn grown to the
+// rows' bytes; allocates nothing itself (so a chain of blocks can be
+// captured into a CUDA graph).
+static int block_enqueue(qmoe_layer *L, const void *xd, int dtype, int64_t T, void *outd, bool want_routing) {
+    cudaStream_t st = L->ctx->stream;
+    const qmoe_moe_config &c = L->cfg;
+    const size_t xbytes = dtype_size(dtype) * T * c.hidden_dim;
+    // post_attention_layernorm (src/model.rs:401-403) into the block's rows
+    NormParams np{xd, dtype, T, c.hidden_dim, L->ln_w, L->ln_b, L->ln_eps, L->xn.p};
+    QTRY_CUDA(launch_layernorm(np, st));
+    const void *xn = L->xn.p;
+    ExpertsArgs a;
+    a.residual = xd;                          // residual + (moe + shared), src/model.rs:409-412
+    if (L->e_count == 0) {
+        // no routed experts (src/moe.rs:46-48): x + shared(LN(x)), or x
+        const size_t kb = sizeof(int32_t) * T * c.top_k;
+        if (want_routing) {
+            QTRY_CUDA(cudaMemsetAsync(L->topk_idx.p, 0xff, kb, st));
+            QTRY_CUDA(cudaMemsetAsync(L->topk_w.p, 0, kb, st));
+        }
+        if (L->has_shared) {
+            qmoe_moe_config saved = L->cfg;
+            L->cfg.top_k = 0;
+            a.shared_count = T;
+            const int rc = run_experts(L, xn, dtype, T, a, outd, 0);
+            L->cfg = saved;
+            return rc;
+        }
+        QTRY_CUDA(cudaMemcpyAsync(outd, xd, xbytes, cudaMemcpyDeviceToDevice, st));
+        return QMOE_OK;
+    }
+    a.topk_idx = L->topk_idx.as<int32_t>();
+    a.topk_w = L->topk_w.as<float>();
+    a.topk_ld = c.top_k;
+    a.shared_count = L->has_shared ? T : 0;
+    const bool front = router_tail_ok(T, c.num_experts, c.top_k);
+    bool prefill = false;
+    QTRY(choose_prefill(L, dtype, T, c.top_k, &prefill));
+    if (front) {
+        QTRY(run_front(L, xn, dtype, T, prefill));
+        a.permuted = true;
+    } else {
+        QTRY(run_router(L, xn, dtype, T));
+    }
+    return run_experts(L, xn, dtype, T, a, outd, 0);
+}
+
+static int check_block_layer(const qmoe_layer *L) {
     if (!L) return fail(QMOE_ERR_INVALID, "layer is NULL");
-    QTRY(check_ptr_kind(ptr_kind));
-    QTRY(check_dtype(dtype));
     if (!L->ln_w) return fail(QMOE_ERR_INVALID, "no LayerNorm set (qmoe_layer_set_norm)");
-    if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
-    if (T > 0 && (!x || !out)) return fail(QMOE_ERR_INVALID, "NULL x or out");
     if (L->e_count > 0 && (L->e_begin != 0 || L->e_count != L->cfg.num_experts))
         return fail(QMOE_ERR_INVALID, "a block forward needs all experts local");
+    return QMOE_OK;
+}
+
+int qmoe_layer_forward_block(qmoe_layer *L, const void *x, int dtype, int64_t T, void *out,
+                             int32_t *topk_idx, float *topk_w, int ptr_kind) {
+    QTRY(check_block_layer(L));
+    QTRY(check_ptr_kind(ptr_kind));
+    QTRY(check_dtype(dtype));
+    if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
+    if (T > 0 && (!x || !out)) return fail(QMOE_ERR_INVALID, "NULL x or out");
     if (T == 0) return QMOE_OK;
     QTRY(check_align(x, ptr_kind, "x"));
     QTRY(check_align(out, ptr_kind, "out"));
@@ -1868,49 +1923,159 @@ int qmoe_layer_forward_block(qmoe_layer *L, const void *x, int dtype, int64_t T,
         QTRY(grow(L->io_out, xbytes));
         outd = L->io_out.p;
     }
-    // post_attention_layernorm (src/model.rs:401-403) into the block's rows
     QTRY(grow(L->xn, xbytes));
-    NormParams np{xd, dtype, T, c.hidden_dim, L->ln_w, L->ln_b, L->ln_eps, L->xn.p};
-    QTRY_CUDA(launch_layernorm(np, st));
-    const void *xn = L->xn.p;
-    ExpertsArgs a;
-    a.residual = xd;                          // residual + (moe + shared), src/model.rs:409-412
+    QTRY(block_enqueue(L, xd, dtype, T, outd, topk_idx || topk_w));
     const size_t kb = sizeof(int32_t) * T * c.top_k;
-    if (L->e_count == 0) {
-        // no routed experts (src/moe.rs:46-48): x + shared(LN(x)), or x
-        if (topk_idx) QTRY_CUDA(cudaMemsetAsync(L->topk_idx.p, 0xff, kb, st));
-        if (topk_w) QTRY_CUDA(cudaMemsetAsync(L->topk_w.p, 0, kb, st));
-        if (L->has_shared) {
-            qmoe_moe_config saved = L->cfg;
-            L->cfg.top_k = 0;
-            a.shared_count = T;
-            const int rc = run_experts(L, xn, dtype, T, a, outd, 0);
-            L->cfg = saved;
-            if (rc != QMOE_OK) return rc;
-        } else {
-            QTRY_CUDA(cudaMemcpyAsync(outd, xd, xbytes, cudaMemcpyDeviceToDevice, st));
-        }
-    } else {
-        a.topk_idx = L->topk_idx.as<int32_t>();
-        a.topk_w = L->topk_w.as<float>();
-        a.topk_ld = c.top_k;
-        a.shared_count = L->has_shared ? T : 0;
-        const bool front = router_tail_ok(T, c.num_experts, c.top_k);
-        bool prefill = false;
-        QTRY(choose_prefill(L, dtype, T, c.top_k, &prefill));
-        if (front) {
-            QTRY(run_front(L, xn, dtype, T, prefill));
-            a.permuted = true;
-        } else {
-            QTRY(run_router(L, xn, dtype, T));
-        }
-        QTRY(run_experts(L, xn, dtype, T, a, outd, 0));
-    }
     const cudaMemcpyKind k = ptr_kind == QMOE_PTR_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
     if (topk_idx) QTRY_CUDA(cudaMemcpyAsync(topk_idx, L->topk_idx.p, kb, k, st));
     if (topk_w) QTRY_CUDA(cudaMemcpyAsync(topk_w, L->topk_w.p, kb, k, st));
     QTRY(finish_out(L, out, outd, xbytes, ptr_kind));
     if (ptr_kind == QMOE_PTR_HOST) QTRY(sync_and_check(st));
+    return QMOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// chain of blocks
+// ---------------------------------------------------------------------------
+
+struct qmoe_chain {
+    qmoe_ctx *ctx = nullptr;
+    std::vector<qmoe_layer *> layers;
+    int64_t H = 0;
+    DevBuf ping[2], in, out;
+    // the captured launch sequence and what it was captured for: the input
+    // and output rows, T, dtype, and every buffer of every layer it touches
+    struct Key {
+        const void *xd = nullptr, *outd = nullptr;
+        int64_t T = -1;
+        int dtype = -1;
+        std::vector<const void *> bufs;
+        std::vector<int64_t> caps;
+        std::vector<int> paths;
+    } key;
+    cudaGraphExec_t exec = nullptr;
+};
+
+static void chain_key(const qmoe_chain *C, const void *xd, const void *outd, int64_t T, int dtype,
+                      qmoe_chain::Key &k) {
+    k.xd = xd;
+    k.outd = outd;
+    k.T = T;
+    k.dtype = dtype;
+    k.bufs.clear();
+    k.caps.clear();
+    k.paths.clear();
+    k.bufs.push_back(C->ping[0].p);
+    k.bufs.push_back(C->ping[1].p);
+    for (const qmoe_layer *L : C->layers) {
+        k.bufs.push_back(L->xn.p);
+        k.caps.push_back(L->cap);
+        k.paths.push_back(L->path);
+    }
+}
+
+static bool same_key(const qmoe_chain::Key &a, const qmoe_chain::Key &b) {
+    return a.xd == b.xd && a.outd == b.outd && a.T == b.T && a.dtype == b.dtype && a.bufs == b.bufs &&
+           a.caps == b.caps && a.paths == b.paths;
+}
+
+int qmoe_chain_create(qmoe_layer *const *layers, int n_layers, qmoe_chain **out) {
+    if (!layers || !out || n_layers < 1) return fail(QMOE_ERR_INVALID, "need at least one layer");
+    *out = nullptr;
+    for (int l = 0; l < n_layers; ++l) {
+        QTRY(check_block_layer(layers[l]));
+        if (layers[l]->ctx != layers[0]->ctx)
+            return fail(QMOE_ERR_INVALID, "the layers of a chain must share one context");
+        if (layers[l]->cfg.hidden_dim != layers[0]->cfg.hidden_dim)
+            return fail(QMOE_ERR_INVALID, "the layers of a chain must share hidden_dim");
+    }
+    qmoe_chain *C = new (std::nothrow) qmoe_chain;
+    if (!C) return fail(QMOE_ERR_NOMEM, "host allocation failed");
+    C->ctx = layers[0]->ctx;
+    C->layers.assign(layers, layers + n_layers);
+    C->H = layers[0]->cfg.hidden_dim;
+    *out = C;
+    return QMOE_OK;
+}
+
+int qmoe_chain_destroy(qmoe_chain *C) {
+    if (!C) return QMOE_OK;
+    DeviceGuard g(C->ctx->device);
+    if (C->exec) cudaGraphExecDestroy(C->exec);
+    for (DevBuf *b : {&C->ping[0], &C->ping[1], &C->in, &C->out}) release(*b);
+    delete C;
+    return QMOE_OK;
+}
+
+int qmoe_chain_forward(qmoe_chain *C, const void *x, int dtype, int64_t T, void *out, int ptr_kind) {
+    if (!C) return fail(QMOE_ERR_INVALID, "chain is NULL");
+    QTRY(check_ptr_kind(ptr_kind));
+    QTRY(check_dtype(dtype));
+    if (T < 0) return fail(QMOE_ERR_INVALID, "T < 0");
+    if (T > 0 && (!x || !out)) return fail(QMOE_ERR_INVALID, "NULL x or out");
+    if (T == 0) return QMOE_OK;
+    QTRY(check_align(x, ptr_kind, "x"));
+    QTRY(check_align(out, ptr_kind, "out"));
+    DeviceGuard g(C->ctx->device);
+    cudaStream_t st = C->ctx->stream;
+    const size_t xbytes = dtype_size(dtype) * T * C->H;
+    // every buffer of the sequence exists before it is enqueued or captured
+    const int n = (int)C->layers.size();
+    for (qmoe_layer *L : C->layers) {
+        QTRY(layer_reserve(L, T));
+        QTRY(grow(L->xn, xbytes));
+    }
+    if (n > 1) QTRY(grow(C->ping[0], xbytes));
+    if (n > 2) QTRY(grow(C->ping[1], xbytes));
+    const void *xd = x;
+    void *outd = out;
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY(grow(C->in, xbytes));
+        QTRY(grow(C->out, xbytes));
+        QTRY_CUDA(cudaMemcpyAsync(C->in.p, x, xbytes, cudaMemcpyHostToDevice, st));
+        xd = C->in.p;
+        outd = C->out.p;
+    }
+    auto enqueue = [&]() -> int {
+        const void *cur = xd;
+        for (int l = 0; l < n; ++l) {
+            void *dst = l == n - 1 ? outd : C->ping[l & 1].p;
+            QTRY(block_enqueue(C->layers[l], cur, dtype, T, dst, false));
+            cur = dst;
+        }
+        return QMOE_OK;
+    };
+    bool profiling = false;
+    for (const qmoe_layer *L : C->layers) profiling |= L->profiling;
+    qmoe_chain::Key k;
+    chain_key(C, xd, outd, T, dtype, k);
+    if (!profiling && !(C->exec && same_key(k, C->key))) {
+        if (C->exec) cudaGraphExecDestroy(C->exec);
+        C->exec = nullptr;
+        cudaGraph_t graph = nullptr;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int rc = enqueue();
+            const cudaError_t ec = cudaStreamEndCapture(st, &graph);
+            if (rc == QMOE_OK && ec == cudaSuccess && graph &&
+                cudaGraphInstantiate(&C->exec, graph, 0) != cudaSuccess)
+                C->exec = nullptr;
+            if (graph) cudaGraphDestroy(graph);
+            cudaGetLastError();
+            if (rc != QMOE_OK) return rc;
+            if (C->exec) C->key = k;
+        } else {
+            cudaGetLastError();   // e.g. the legacy default stream, which cannot be captured
+        }
+    }
+    if (C->exec && !profiling) {
+        QTRY_CUDA(cudaGraphLaunch(C->exec, st));
+    } else {
+        QTRY(enqueue());
+    }
+    if (ptr_kind == QMOE_PTR_HOST) {
+        QTRY_CUDA(cudaMemcpyAsync(out, outd, xbytes, cudaMemcpyDeviceToHost, st));
+        QTRY(sync_and_check(st));
+    }
     return QMOE_OK;
 }
 

@@ -5,11 +5,11 @@ C ABI in include/qmoe_b200.h); this package is the host-side binding.
 """
 from . import capi
 from .capi import QmoeError
-from .layer import (Context, MoEConfig, PackedExpert, PackedQMoETensor, QMoELayer,
+from .layer import (BlockChain, Context, MoEConfig, PackedExpert, PackedQMoETensor, QMoELayer,
                     default_context)
 from . import quantize
 from .ep import ExpertParallelMoE, TorchComm
 
-__all__ = ["capi", "QmoeError", "Context", "MoEConfig", "PackedExpert",
+__all__ = ["capi", "QmoeError", "BlockChain", "Context", "MoEConfig", "PackedExpert",
            "PackedQMoETensor", "QMoELayer", "default_context", "quantize",
            "ExpertParallelMoE", "TorchComm"]

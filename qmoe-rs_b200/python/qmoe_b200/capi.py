@@ -99,6 +99,9 @@ SIGNATURES = {
     "qmoe_layer_set_path": (_I, [_P, _I]),
     "qmoe_layer_set_norm": (_I, [_P, _P, _P, ctypes.c_float, _I]),
     "qmoe_layer_forward_block": (_I, [_P, _P, _I, _I64, _P, _P, _P, _I]),
+    "qmoe_chain_create": (_I, [ctypes.POINTER(_P), _I, _PP]),
+    "qmoe_chain_destroy": (_I, [_P]),
+    "qmoe_chain_forward": (_I, [_P, _P, _I, _I64, _P, _I]),
     "qmoe_ep_plan": (_I, [_P, _P, _P, _I64, _I, _I, _I, _I64, _P, _P, _P, _P]),
     "qmoe_gather_rows": (_I, [_P, _P, _I, _I64, _P, _I64, _P]),
     "qmoe_combine_rows": (_I, [_P, _P, _I, _I64, _P, _I, _I64, _P, _P]),

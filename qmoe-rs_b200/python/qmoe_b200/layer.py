@@ -446,3 +446,46 @@ class QMoELayer:
             self.close()
         except Exception:
             pass
+
+
+class BlockChain:
+    """The layer loop of DeepSeekCoderV2::forward_next (src/model.rs:481-489)
+    over the MoE halves of consecutive decoder layers (attention left out):
+    x -> block_0 -> block_1 -> ..., each block a QMoELayer with its
+    post-attention LayerNorm set.  Repeated calls with the same buffers replay
+    one captured CUDA graph of all the layers' launches."""
+
+    def __init__(self, layers: Sequence["QMoELayer"]):
+        if not layers:
+            raise ValueError("a chain needs at least one layer")
+        self.layers = list(layers)
+        self.ctx = self.layers[0].ctx
+        arr = (ctypes.c_void_p * len(self.layers))(*[L.handle.value for L in self.layers])
+        h = ctypes.c_void_p()
+        capi.call("qmoe_chain_create", arr, len(self.layers), ctypes.byref(h))
+        self._h = h
+
+    def forward(self, xs, out=None):
+        T, H = xs.shape
+        dt = _dtype_code(xs)
+        if out is None:
+            out = _empty_like_kind(xs, (T, H), dt)
+        xp, kind, keep = _ptr(xs)
+        op, okind, _ = _ptr(out)
+        if okind != kind:
+            raise ValueError("x and out must both be host or both device memory")
+        if kind == capi.QMOE_PTR_DEVICE:
+            self.ctx.use_current_torch_stream()
+        capi.call("qmoe_chain_forward", self._h, xp, dt, T, op, kind)
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            capi.lib().qmoe_chain_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

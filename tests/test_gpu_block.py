@@ -76,3 +76,47 @@ def test_block_without_experts_adds_the_shared_ffn():
     bare = QMoELayer(MoEConfig(8, 2, H, 128), None, [])
     bare.set_norm(w, b)
     assert torch.equal(bare.forward_block(x.cuda()).cpu(), x)
+
+
+@pytest.mark.parametrize("dtype,T", [(torch.float32, 8), (torch.bfloat16, 256)])
+def test_chain_of_blocks_matches_blockwise_and_oracle(dtype, T):
+    # the layer loop of forward_next (src/model.rs:481-489) over MoE blocks:
+    # the chain's captured graph gives the bits of the blocks called one by
+    # one, on every repeat with new inputs in the same buffers
+    from qmoe_b200 import BlockChain
+    E, K, H, I, Is = 16, 4, 512, 256, 256
+    cfg = MoEConfig(E, K, H, I, shared_intermediate_dim=Is)
+    layers, params = [], []
+    for l in range(3):
+        experts, shared, gw = helpers.synth_layer(E, H, I, Is, seed=50 + l, device="cuda")
+        L = QMoELayer(cfg, gw, experts, shared=shared)
+        w, b = ln_params(H, 60 + l)
+        L.set_norm(w, b)
+        layers.append(L)
+        params.append((gw.cpu().numpy(), helpers.to_numpy_experts(experts),
+                       helpers.to_numpy_experts([shared])[0], w, b))
+    chain = BlockChain(layers)
+    xbuf = torch.empty(T, H, dtype=dtype, device="cuda")
+    obuf = torch.empty(T, H, dtype=dtype, device="cuda")
+    with torch.cuda.stream(torch.cuda.Stream()):
+        for i in range(3):
+            xbuf.copy_(torch.randn(T, H, generator=torch.Generator().manual_seed(70 + i)).to(dtype))
+            chain.forward(xbuf, out=obuf)
+            ref = xbuf
+            for L in layers:
+                ref = L.forward_block(ref)
+            torch.cuda.synchronize()
+            assert torch.equal(obuf, ref), f"call {i}"
+    # two blocks against the oracle
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(5)).to(dtype)
+    two = BlockChain(layers[:2]).forward(x.cuda())
+    y = x.float().numpy()
+    for gw, ne, ns, w, b in params[:2]:
+        y, _, _ = qo.block_forward(qo.MoEConfig(E, K, H, I, Is), gw, ne, y, w, b, 1e-6, shared=ns,
+                                   nthreads=NTHREADS, round_bf16=dtype == torch.bfloat16)
+        if dtype == torch.bfloat16:
+            y = torch.from_numpy(y).bfloat16().float().numpy()     # the block's bf16 output
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    assert rel_err(two.float().cpu().numpy(), y) <= tol
+    host = BlockChain(layers).forward(x)                           # host pointers
+    assert torch.equal(host, chain.forward(x.cuda()).cpu())
