@@ -69,7 +69,8 @@ LAUNCHES = {
     # first, weighted combine last)
     "decode_front": 3,
     # decode batches the front cluster does not take (T * E > 4096): router
-    # partials, selection, permute, gate/up GEMV, down GEMV
+    # partials, their ordered sums, selection with the permute in its last
+    # CTA, gate/up GEMV, down GEMV
     "decode_router": 5,
     # prefill: router partials or logits, selection, permute, bf16 gather,
     # gate/up GEMM, down GEMM, combine

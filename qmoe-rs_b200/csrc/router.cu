@@ -389,6 +389,32 @@ router_gemm_kernel(const RouterParams p) {
         }
 }
 
+// Whole logits from the chunk partials, one thread per (token, expert): the
+// ordered chunk sum, loads issued sixteen at a time, written over the slot
+// of chunk 0 that only this thread reads.  For batches too small to give the
+// one-warp-per-token selection enough warps to sum its partials quickly.
+__global__ void __launch_bounds__(256)
+router_sum_kernel(const RouterParams p) {
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    const int64_t n = p.T * p.E;
+    if (i >= n) return;
+    const int nc = p.H / kGateChunk;
+    const float *pp = p.scratch + i;
+    float tot = 0.0f;
+    int c = 0;
+    for (; c + 16 <= nc; c += 16) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __ldcg(pp + (c + j) * n);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) tot = __fadd_rn(tot, v[j]);
+    }
+    for (; c < nc; ++c) tot = __fadd_rn(tot, __ldcg(pp + c * n));
+    p.scratch[i] = tot;
+}
+
 __global__ void transpose_gate_kernel(const float *w, int E, int H, float *wt, int ld) {
     __shared__ float tile[32][33];
     const int e0 = blockIdx.y * 32, k0 = blockIdx.x * 32;
@@ -764,18 +790,26 @@ cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaSt
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    // few tokens and many chunks: the partials are summed by one thread per
+    // logit first (a warp or CTA per token would read them nearly serially)
+    bool from_parts = parts;
+    if (parts && p.T < 256 && p.H / kGateChunk >= 16) {
+        e = launch_pdl(router_sum_kernel, dim3((unsigned)((p.T * p.E + 255) / 256)), dim3(256), 0, s, p);
+        if (e != cudaSuccess) return e;
+        from_parts = false;
+    }
     if (!f.counter && p.E <= 256 && p.K <= 32) {
         const size_t wsmem = sizeof(float) * kSelWarps * sel_warp_floats(p.E);
         e = ensure_dyn_smem(reinterpret_cast<const void *>(router_select_warp_kernel), wsmem);
         if (e != cudaSuccess) return e;
         return launch_pdl(router_select_warp_kernel, dim3((unsigned)((p.T + kSelWarps - 1) / kSelWarps)),
-                          dim3(kSelWarps * 32), wsmem, s, p, parts ? 1 : 0);
+                          dim3(kSelWarps * 32), wsmem, s, p, from_parts ? 1 : 0);
     }
     const size_t smem = router_smem_bytes(p.H, p.E);
     e = ensure_dyn_smem(reinterpret_cast<const void *>(router_select_kernel), smem);
     if (e != cudaSuccess) return e;
     return launch_pdl(router_select_kernel, dim3((unsigned)p.T), dim3(kRouterThreads), smem, s, p,
-                      parts ? 1 : 0, f);
+                      from_parts ? 1 : 0, f);
 }
 
 }  // namespace qmoe
