@@ -1214,8 +1214,8 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
         g1.combine = 1;
         g1.c = combine_params(L, T, a, outd, dtype, accumulate);
         if (a.ep_ret) {
-            // one arrival per combine task: (row, 1024 columns), the
-            // exchange's fixed ret_units per row
+            // the combine tasks signal each destination once it has all
+            // its rows (ep_signal.cuh)
             g1.ep_ret = 1;
             g1.ret = *a.ep_ret;
             *a.returned = true;
@@ -1683,7 +1683,7 @@ int qmoe_ep_peer_create(qmoe_ctx *ctx, int world, int rank, int64_t capacity, in
     d.off_back = d.off_meta + align256(rows * 2 * K * 4);
     d.off_flags = d.off_back + align256((int64_t)world * capacity * H * es);
     const int64_t off_local = d.off_flags + align256(2 * world * 4);
-    const int64_t bytes = off_local + 256;
+    const int64_t bytes = off_local + 256 + 2 * kEpMaxWorld * 4;
     if (cudaMalloc(&p->mem, (size_t)bytes) != cudaSuccess) {
         cudaGetLastError();
         delete p;
@@ -1700,7 +1700,7 @@ int qmoe_ep_peer_create(qmoe_ctx *ctx, int world, int rank, int64_t capacity, in
     d.base[rank] = p->mem;
     d.seq = reinterpret_cast<int *>(p->mem + off_local);
     d.done = d.seq + 1;
-    d.ret_units = (int)((H / 4 + 255) / 256);   // 1024-column slices per returned row
+    d.cnt = reinterpret_cast<int *>(p->mem + off_local + 256);
     d.err = error_flag();
     *out = p;
     return QMOE_OK;

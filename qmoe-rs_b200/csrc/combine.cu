@@ -5,6 +5,7 @@
 // in-order sum.  The cooperative down GEMV does the same work as its last
 // phase; this kernel serves the other callers.
 #include "combine.cuh"
+#include "ep_signal.cuh"
 
 namespace qmoe {
 namespace {
@@ -45,10 +46,7 @@ combine_kernel(const CombineParams p, int vec) {
         }
     if (dst >= 0 && dst != p.ret.rank) {
         __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence_system();
-            atomicAdd_system(reinterpret_cast<int *>(p.ret.base[dst] + p.ret.off_flags) + p.ret.world + p.ret.rank, 1);
-        }
+        if (threadIdx.x == 0) ep_signal(p.ret, dst, 1, (int)(p.ret.C * gridDim.y));
     }
 }
 
@@ -57,8 +55,8 @@ combine_kernel(const CombineParams p, int vec) {
 cudaError_t launch_combine(const CombineParams &p, cudaStream_t s) {
     if (p.T == 0 || p.H == 0) return cudaSuccess;
     if (p.K > kCombineMaxK) return cudaErrorInvalidValue;
-    // expert parallel: slices of 1024 columns, one arrival each (the
-    // exchange's fixed ret_units per row)
+    // expert parallel: slices of 1024 columns (more CTAs in flight for the
+    // NVLink stores)
     const int vec = p.ep_ret ? 1 : kCombVec;
     const int per_cta = kCombThreads * vec;
     const dim3 grid((unsigned)p.T, (unsigned)((p.H / 4 + per_cta - 1) / per_cta));

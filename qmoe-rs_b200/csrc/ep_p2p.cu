@@ -22,6 +22,7 @@
 // of this one (which it computes after reading the rows), so one flag per
 // phase suffices.
 #include "common.cuh"
+#include "ep_signal.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
 
@@ -39,9 +40,7 @@ QMOE_DEV int ld_acquire_sys(const int *p) {
     return v;
 }
 
-QMOE_DEV int *flag_at(const EpPeerDev &d, int owner, int phase, int from) {
-    return reinterpret_cast<int *>(d.base[owner] + d.off_flags) + phase * d.world + from;
-}
+QMOE_DEV int *flag_at(const EpPeerDev &d, int owner, int phase, int from) { return ep_flag(d, owner, phase, from); }
 
 // Copies one row of `bytes` (a multiple of 16) with the CTA.
 QMOE_DEV void copy_row(uint8_t *dst, const uint8_t *src, int64_t bytes) {
@@ -50,14 +49,12 @@ QMOE_DEV void copy_row(uint8_t *dst, const uint8_t *src, int64_t bytes) {
     for (int64_t i = threadIdx.x; i < bytes / 16; i += kCopyThreads) o[i] = s[i];
 }
 
-// After this CTA's stores to rank dst: fence them system-wide and count one
-// arrival on dst (rows a rank keeps are ordered by its own stream).
-QMOE_DEV void arrive(const EpPeerDev &d, int dst, int phase) {
+// After this CTA's stores to rank dst: count the CTA towards dst's signal
+// (rows a rank keeps are ordered by its own stream); `units` CTAs write to
+// each destination.
+QMOE_DEV void arrive(const EpPeerDev &d, int dst, int phase, int units) {
     __syncthreads();
-    if (threadIdx.x == 0 && dst != d.rank) {
-        __threadfence_system();
-        atomicAdd_system(flag_at(d, dst, phase, d.rank), 1);
-    }
+    if (threadIdx.x == 0 && dst != d.rank) ep_signal(d, dst, phase, units);
 }
 
 // CTA j < world*C: send row j (destination j / C, row j % C) if it is in use,
@@ -79,7 +76,7 @@ ep_dispatch_kernel(const EpPeerDev d, const void *x, int64_t T, const int32_t *s
         if (i < send_counts[dst]) copy_row(d.base[dst] + d.off_rows + r * rb, xs + send_tok[j] * rb, rb);
         int32_t *m = reinterpret_cast<int32_t *>(d.base[dst] + d.off_meta + r * mb);
         for (int k = threadIdx.x; k < 2 * d.K; k += kCopyThreads) m[k] = send_meta[j * 2 * d.K + k];
-        arrive(d, dst, 0);
+        arrive(d, dst, 0, (int)d.C);
     } else if (j - GC < T) {
         const int64_t t = j - GC, r = GC + t;
         copy_row(d.base[d.rank] + d.off_rows + r * rb, xs + t * rb, rb);
@@ -111,11 +108,7 @@ ep_return_kernel(const EpPeerDev d, const void *y) {
     if (s_live)
         copy_row(d.base[dst] + d.off_back + ((int64_t)d.rank * d.C + i) * rb,
                  static_cast<const uint8_t *>(y) + j * rb, rb);
-    __syncthreads();
-    if (threadIdx.x == 0 && dst != d.rank) {
-        __threadfence_system();
-        atomicAdd_system(flag_at(d, dst, 1, d.rank), d.ret_units);
-    }
+    arrive(d, dst, 1, (int)d.C);
 }
 
 // Lane p waits until rank p's C rows of `phase` of this forward have
@@ -126,7 +119,7 @@ ep_wait_kernel(const EpPeerDev d, int phase) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int s = *d.seq + 1;
-    const uint32_t want = (uint32_t)s * (uint32_t)d.C * (uint32_t)(phase == 1 ? d.ret_units : 1);
+    const uint32_t want = (uint32_t)s;           // forwards whose phase arrived
     bool ok = true;
     for (int p = threadIdx.x; p < d.world; p += 32) {
         if (p == d.rank) continue;
@@ -155,7 +148,7 @@ ep_finish_kernel(const EpPeerDev d, const int32_t *slot_pos, int64_t T, const vo
     QMOE_PDL_TRIGGER();
     const int seq = *d.seq + 1;
     if (threadIdx.x < 32) {
-        const uint32_t want = (uint32_t)seq * (uint32_t)d.C * (uint32_t)d.ret_units;
+        const uint32_t want = (uint32_t)seq;
         bool ok = true;
         for (int p = threadIdx.x; p < d.world; p += 32) {
             if (p == d.rank) continue;

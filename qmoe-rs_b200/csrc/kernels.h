@@ -79,8 +79,8 @@ struct EpPeerDev {
     int64_t off_rows, off_meta, off_back, off_flags;
     int *seq;                    // this rank's per-forward sequence number
     int *done;                   // exit count of the return-side kernel (zero between launches)
-    int ret_units;               // arrivals per returned row: ceil(H / 1024), fixed per exchange
-                                 // (one per 1024-column slice of the row, whichever kernel returns it)
+    int *cnt;                    // [2][kEpMaxWorld] units done per (phase, destination)
+                                 // within one launch (zero between launches; ep_signal.cuh)
     int *err;                    // device error word
 };
 

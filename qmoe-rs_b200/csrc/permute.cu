@@ -82,7 +82,7 @@ permute_kernel(const PermuteParams p) {
         // the rows and their metadata come from the peers' dispatch: wait
         // (bounded) until each peer's C rows of this forward have arrived
         if (warp == 0) {
-            const uint32_t want = (uint32_t)(*p.ep.seq + 1) * (uint32_t)p.ep.C;
+            const uint32_t want = (uint32_t)(*p.ep.seq + 1);   // forwards whose dispatch arrived
             bool ok = true;
             for (int r = lane; r < p.ep.world; r += 32) {
                 if (r == p.ep.rank) continue;

@@ -46,6 +46,7 @@
 // Every wait is bounded; on a time-out the kernel flags the device error
 // word, lets its TMA copies drain (again bounded) and returns.
 #include "combine.cuh"
+#include "ep_signal.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "quant.cuh"
@@ -581,11 +582,7 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             if (tid < 256 && c4 < H4 && (dst < 0 || S->c_n > 0))
                 combine_float4(p.c, t, 4 * c4, S->c_n, S->c_pos, S->c_w, orow);
             __syncthreads();
-            if (tid == 0 && dst >= 0 && dst != p.ret.rank) {
-                __threadfence_system();
-                atomicAdd_system(reinterpret_cast<int *>(p.ret.base[dst] + p.ret.off_flags) + p.ret.world + p.ret.rank,
-                                 1);
-            }
+            if (tid == 0 && dst >= 0 && dst != p.ret.rank) ep_signal(p.ret, dst, 1, (int)(p.ret.C * nch));
         }
     }
     // the last CTA out resets the grid's counters for the next launch
