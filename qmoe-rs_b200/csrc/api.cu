@@ -584,8 +584,11 @@ static int empty_layer_maps(qmoe_layer *L) {
     int coop = 0;
     QTRY_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
     L->coop = coop != 0;
-    if (!L->has_shared) return QMOE_OK;
     const int64_t H = c.hidden_dim, Is = c.shared_intermediate_dim;
+    const int64_t Imx = Is > c.intermediate_dim ? Is : c.intermediate_dim;
+    L->kp1 = (int)((H + 255) / 256 * 256);       // limb strides (the scratch is laid out even
+    L->kp2 = (int)((Imx + 255) / 256 * 256);     // when no kernel will read it)
+    if (!L->has_shared) return QMOE_OK;
     const int64_t srows[3] = {Is, Is, H}, skin[3] = {H, H, Is};
     for (int m = 0; m < 3; ++m) {
         if (!make_tmap_u8(&L->tm_ws[m], L->ws[m], (uint64_t)(skin[m] / 4), (uint64_t)srows[m], 64, 128,
@@ -607,8 +610,6 @@ static int empty_layer_maps(qmoe_layer *L) {
                 return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for shared matrix %d", m);
             L->tm_pw[m] = L->tm_pws[m];
         }
-    L->kp1 = (int)((H + 255) / 256 * 256);
-    L->kp2 = (int)((Is + 255) / 256 * 256);
     if (qgemv_imma_smem_bytes(L->kp1, 1) > 227 * 1024 || qgemv_imma_smem_bytes(L->kp2, 1) > 227 * 1024)
         return fail(QMOE_ERR_UNSUPPORTED, "hidden or shared intermediate dim too large for the GEMV tiles");
     L->grid0 = qgemv_max_grid(0, (int)H);

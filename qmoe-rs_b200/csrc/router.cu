@@ -207,21 +207,23 @@ router_logits_kernel(const RouterParams p) {
 // over k in order, the chunk added to the running total in chunk order
 // (add.rn.f32x2, two IEEE adds).
 //
-// CTA = 256 threads (8 warps: 2 along tokens x 4 along experts) over 64
-// tokens x 128 experts; thread = 8 tokens x 4 experts, accumulators held as
-// 16 pairs (token t, experts e, e+1).  Per chunk the shared memory holds x as
-// [k][token] with every value twice (x_t, x_t) -- one 16-byte load gives the
-// duplicated operands of two tokens -- and the transposed gate as
-// [k][expert] (gate_t, made once per layer), so a 16-byte load gives two
-// expert pairs.  Lanes are 4 token groups x 8 expert groups: the distinct
-// 16-byte chunks a warp-wide load touches are consecutive, one wavefront,
-// each broadcast to the lanes that share it.  Two stages: the next chunk's
-// gate tile arrives by cp.async and its x tile through registers
-// (converted from bf16 when needed) while this chunk is computed.
-constexpr int kGemmThreads = 256;
+// The loop is bound by shared-memory wavefronts: a warp-wide 16-byte load
+// takes four of them whatever the broadcast, one per eight lanes.  So each
+// thread owns an 8 x 8 tile (8 tokens x 8 experts, 32 accumulator pairs)
+// and reads per k two 16-byte loads of x and two of the gate -- 16
+// wavefronts per warp for 64 FMAs per lane, which keeps pace with the FP32
+// pipe at four warps per SM -- and duplicates each x value into the pair
+// operand (x, x) with a register move.  CTA = 128 threads (2 x 2 warps)
+// over 64 tokens x 128 experts; per chunk the shared memory holds x as
+// [k][token] and the transposed gate (gate_t, made once per layer) as
+// [k][expert].  Lanes are 4 token groups x 8 expert groups, so the eight
+// lanes of a load phase read consecutive 16-byte chunks.  Two stages: the
+// next chunk's gate tile arrives by cp.async and its x tile through
+// registers (converted from bf16 when needed) while this chunk is computed.
+constexpr int kGemmThreads = 128;
 constexpr int kGemmK = kGateChunk;       // 64: one chunk per stage
 constexpr int kGemmTokens = 64, kGemmExperts = 128;
-constexpr int kGemmXFloats = kGemmK * 2 * kGemmTokens;     // duplicated x tile
+constexpr int kGemmXFloats = kGemmK * kGemmTokens;
 constexpr int kGemmWFloats = kGemmK * kGemmExperts;
 constexpr int kGemmStageFloats = kGemmXFloats + kGemmWFloats;
 
@@ -237,6 +239,12 @@ QMOE_DEV unsigned long long fadd2(unsigned long long a, unsigned long long b) {
     return d;
 }
 
+QMOE_DEV unsigned long long dup2(float v) {
+    unsigned long long d;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(d) : "f"(v));
+    return d;
+}
+
 QMOE_DEV void cp_async16(void *smem, const void *gmem, bool valid) {
     const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
     const int n = valid ? 16 : 0;                 // 0: fill the 16 bytes with zeros
@@ -249,7 +257,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 router_gemm_kernel(const RouterParams p) {
     extern __shared__ __align__(16) float gsm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int wt = warp & 1, we = warp >> 1;        // 2 x 4 warps
+    const int wt = warp & 1, we = warp >> 1;        // 2 x 2 warps
     const int tg = lane & 3, eg = lane >> 2;
     const int64_t t0 = (int64_t)blockIdx.x * kGemmTokens;
     const int e0 = blockIdx.y * kGemmExperts;
@@ -271,33 +279,33 @@ router_gemm_kernel(const RouterParams p) {
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    // x tile of chunk c: thread -> token r = tid / 4, quarter h = tid % 4
-    // (16 consecutive k of that token)
-    uint4 xr[4];                                                 // 16 f32 or 16 bf16 (2 used)
-    const int xr_r = tid >> 2, xr_h = tid & 3;
+    // x tile of chunk c: thread -> token r = tid / 2, half h = tid % 2 (32
+    // consecutive k of that token)
+    uint4 xr[8];                                                 // 32 f32 or 32 bf16 (4 used)
+    const int xr_r = tid >> 1, xr_h = tid & 1;
     auto fetch_x = [&](int c) {
         const int64_t t = t0 + xr_r;
-        const int64_t base = t * p.H + c * kGemmK + xr_h * 16;
+        const int64_t base = t * p.H + c * kGemmK + xr_h * 32;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) xr[q] = make_uint4(0, 0, 0, 0);
+        for (int q = 0; q < 8; ++q) xr[q] = make_uint4(0, 0, 0, 0);
         if (t < p.T) {
             if (p.dtype == 0) {
                 const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const float *>(p.x) + base);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) xr[q] = __ldg(src + q);
+                for (int q = 0; q < 8; ++q) xr[q] = __ldg(src + q);
             } else {
                 const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(p.x) + base);
 #pragma unroll
-                for (int q = 0; q < 2; ++q) xr[q] = __ldg(src + q);
+                for (int q = 0; q < 4; ++q) xr[q] = __ldg(src + q);
             }
         }
     };
     auto store_x = [&](int st) {
         float *xs = gsm + st * kGemmStageFloats;
-        float v[16];
+        float v[32];
         if (p.dtype == 0) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < 8; ++q) {
                 v[4 * q + 0] = __uint_as_float(xr[q].x);
                 v[4 * q + 1] = __uint_as_float(xr[q].y);
                 v[4 * q + 2] = __uint_as_float(xr[q].z);
@@ -305,7 +313,7 @@ router_gemm_kernel(const RouterParams p) {
             }
         } else {
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
+            for (int q = 0; q < 4; ++q) {
                 const uint32_t u[4] = {xr[q].x, xr[q].y, xr[q].z, xr[q].w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -315,8 +323,7 @@ router_gemm_kernel(const RouterParams p) {
             }
         }
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            *reinterpret_cast<float2 *>(xs + (xr_h * 16 + j) * (2 * kGemmTokens) + 2 * xr_r) = make_float2(v[j], v[j]);
+        for (int j = 0; j < 32; ++j) xs[(xr_h * 32 + j) * kGemmTokens + xr_r] = v[j];
     };
 
     // the gate is the layer's, independent of the preceding kernel
@@ -326,16 +333,16 @@ router_gemm_kernel(const RouterParams p) {
     fetch_x(0);
     store_x(0);
 
-    unsigned long long acc[8][2], tot[8][2];
+    unsigned long long acc[8][4], tot[8][4];
 #pragma unroll
     for (int a = 0; a < 8; ++a)
 #pragma unroll
-        for (int b = 0; b < 2; ++b) tot[a][b] = 0ull;
+        for (int b = 0; b < 4; ++b) tot[a][b] = 0ull;
 
-    // this thread's operand offsets within a stage (16-byte units):
-    // tokens 2 (wt*16 + tg + 4j) + {0, 1} (j < 4), experts 4 (we*8 + eg) + {0..3}
-    const int xo = wt * 16 + tg;
-    const int wo = we * 8 + eg;
+    // this thread's tokens: 4 tg + 16 j + u (j < 2, u < 4) in the warp's 32;
+    // experts: 4 eg + 32 q + v (q < 2, v < 4) in the warp's 64
+    const int xo = wt * 8 + tg;          // float4 index in an x row (+ 4 j)
+    const int wo = we * 16 + eg;         // float4 index in a gate row (+ 8 q)
 
     for (int c = 0; c < nc; ++c) {
         const int st = c & 1;
@@ -345,48 +352,48 @@ router_gemm_kernel(const RouterParams p) {
             load_w(c + 1, st ^ 1);
             fetch_x(c + 1);
         }
-        const ulonglong2 *xs = reinterpret_cast<const ulonglong2 *>(gsm + st * kGemmStageFloats);
+        const float4 *xs = reinterpret_cast<const float4 *>(gsm + st * kGemmStageFloats);
         const ulonglong2 *ws = reinterpret_cast<const ulonglong2 *>(gsm + st * kGemmStageFloats + kGemmXFloats);
 #pragma unroll
         for (int a = 0; a < 8; ++a)
 #pragma unroll
-            for (int b = 0; b < 2; ++b) acc[a][b] = 0ull;
-#pragma unroll 8
+            for (int b = 0; b < 4; ++b) acc[a][b] = 0ull;
+#pragma unroll 4
         for (int k = 0; k < kGemmK; ++k) {
-            ulonglong2 xv[4];
+            const float4 x0 = xs[k * (kGemmTokens / 4) + xo];
+            const float4 x1 = xs[k * (kGemmTokens / 4) + xo + 4];
+            const ulonglong2 w0 = ws[k * (kGemmExperts / 4) + wo];
+            const ulonglong2 w1 = ws[k * (kGemmExperts / 4) + wo + 8];
+            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) xv[j] = xs[k * (kGemmTokens / 2) + xo + 4 * j];
-            const ulonglong2 wv = ws[k * (kGemmExperts / 4) + wo];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                acc[2 * j][0] = ffma2(xv[j].x, wv.x, acc[2 * j][0]);
-                acc[2 * j][1] = ffma2(xv[j].x, wv.y, acc[2 * j][1]);
-                acc[2 * j + 1][0] = ffma2(xv[j].y, wv.x, acc[2 * j + 1][0]);
-                acc[2 * j + 1][1] = ffma2(xv[j].y, wv.y, acc[2 * j + 1][1]);
+            for (int a = 0; a < 8; ++a) {
+                const unsigned long long xx = dup2(xv[a]);
+                acc[a][0] = ffma2(xx, w0.x, acc[a][0]);
+                acc[a][1] = ffma2(xx, w0.y, acc[a][1]);
+                acc[a][2] = ffma2(xx, w1.x, acc[a][2]);
+                acc[a][3] = ffma2(xx, w1.y, acc[a][3]);
             }
         }
 #pragma unroll
         for (int a = 0; a < 8; ++a)
 #pragma unroll
-            for (int b = 0; b < 2; ++b) tot[a][b] = fadd2(tot[a][b], acc[a][b]);
+            for (int b = 0; b < 4; ++b) tot[a][b] = fadd2(tot[a][b], acc[a][b]);
         if (c + 1 < nc) store_x(st ^ 1);
     }
-    // acc row 2j + u = token 2 (wt*16 + tg + 4j) + u; acc column pair hb =
-    // experts 4 (we*8 + eg) + 2 hb + {0, 1}
+    // acc row a = token 4 (wt*8 + tg) + 16 (a / 4) + a % 4; column pair b =
+    // experts 4 (we*16 + eg) + 32 (b / 2) + 2 (b % 2) + {0, 1}
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int a = 0; a < 8; ++a) {
+        const int64_t t = t0 + 4 * (wt * 8 + tg) + 16 * (a >> 2) + (a & 3);
+        if (t >= p.T) continue;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int64_t t = t0 + 2 * (wt * 16 + tg + 4 * j) + u;
-            if (t >= p.T) continue;
-#pragma unroll
-            for (int hb = 0; hb < 2; ++hb) {
-                const unsigned long long v = tot[2 * j + u][hb];
-                const int e = e0 + 4 * (we * 8 + eg) + 2 * hb;
-                if (e < p.E) p.scratch[t * p.E + e] = __uint_as_float((uint32_t)v);
-                if (e + 1 < p.E) p.scratch[t * p.E + e + 1] = __uint_as_float((uint32_t)(v >> 32));
-            }
+        for (int b = 0; b < 4; ++b) {
+            const unsigned long long v = tot[a][b];
+            const int e = e0 + 4 * (we * 16 + eg) + 32 * (b >> 1) + 2 * (b & 1);
+            if (e < p.E) p.scratch[t * p.E + e] = __uint_as_float((uint32_t)v);
+            if (e + 1 < p.E) p.scratch[t * p.E + e + 1] = __uint_as_float((uint32_t)(v >> 32));
         }
+    }
 }
 
 // Whole logits from the chunk partials, one thread per (token, expert): the
