@@ -125,14 +125,14 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def read_profile_traffic(name: str):
+def read_profile_traffic(name: str, key: str = "traffic_bytes_per_launch"):
     """DRAM bytes per launch of a kernel from its committed ncu summary (a
-    line 'traffic_bytes_per_launch: N'), or None."""
+    line '<key>: N'), or None."""
     path = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(path):
         return None
     for line in open(path):
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith(key + ":"):
             try:
                 return float(line.split(":", 1)[1].strip())
             except ValueError:
@@ -584,13 +584,14 @@ def run_decode_line(W, layers, xs, steps: int):
     gu_b, dn_b, ly_b = gate_up_bytes(W, T, touched), down_bytes(W, T, touched), layer_bytes(W, T, touched)
     gu_ms, dn_ms = stages.get("gate_up", float("nan")), stages.get("down", float("nan"))
     launches = LAUNCHES["decode_front"] if T * W["E"] <= 4096 and T <= 64 else LAUNCHES["decode_router"]
+    traffic = read_profile_traffic("qgemv_decode_v3_t32.txt" if W is V3 else "qgemv_gate_up_decode_v2lite_t32.txt")
     return {
         "value": T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "T": T, "dtype": W["act"],
         "touched_experts": touched,
         "roofline": {"bound": "hbm", "kernel": "decode GEMV gate/up + SwiGLU (x limbs first)",
                      "achieved": gu_b / (gu_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
                      "frac": gu_b / (gu_ms / 1e3) / 1e9 / hbm, "peak_kind": peak_kind,
-                     "algorithmic_bytes": gu_b, "kernel_ms": gu_ms},
+                     "traffic": traffic, "algorithmic_bytes": gu_b, "kernel_ms": gu_ms},
         "roofline_down": {"bound": "hbm", "kernel": "decode GEMV down (h limbs first, combine last)",
                           "achieved": dn_b / (dn_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
                           "frac": dn_b / (dn_ms / 1e3) / 1e9 / hbm, "algorithmic_bytes": dn_b,
@@ -711,7 +712,10 @@ def run_single(args, W, dev, local):
             "bound": "tensor", "kernel": "qgemm_prefill gate/up + SwiGLU (tcgen05, 2-bit dequant "
                                          "in the pipeline)",
             "achieved": gu_tf, "peak": bf16, "unit": "TFLOP/s", "frac": gu_tf / bf16,
-            "peak_kind": peak_kind, "traffic": read_profile_traffic("qgemm_prefill_gate_up_v3.txt"),
+            "peak_kind": peak_kind,
+            "traffic": read_profile_traffic("qgemm_prefill_gate_up_v3.txt", "traffic_bytes_per_launch_full_v3"),
+            "traffic_note": "ncu DRAM bytes of a 32-expert, 512-token V3-shaped launch, scaled by the "
+                            "items of the full launch (8704 / 1088)",
             "algorithmic_flops": gu_f, "kernel_ms": stages["gate_up"],
             "down_tflops": dn_tf, "down_frac": dn_tf / bf16}
         line["layer"] = {"algorithmic_flops": fl, "tflops": fl / (ms / 1e3) / 1e12,
