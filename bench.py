@@ -102,7 +102,7 @@ def parse():
     ap.add_argument("--no-sublines", action="store_true",
                     help="N = 1: only the headline workload")
     ap.add_argument("--ncu-case", choices=["decode", "prefill", "pack", "v3-prefill", "v3-decode",
-                                           "v3-route"],
+                                           "v3-route", "v3"],
                     default=None,
                     help="only run 3 eager forwards of a short fixed case for an ncu capture, "
                          "print nothing")
@@ -1051,8 +1051,9 @@ def run_ncu_case(args):
         # v3-prefill: 32 experts of the V3 shape (353 MB of packed weights)
         # and 512 bf16 tokens, i.e. ~128 tokens per expert as in configs[3];
         # v3-decode: the whole V3 layer (2.85 GB) over 32 bf16 tokens
+        # v3: the whole configs[3] forward (4096 tokens), for the launch list
         W = dict(V3, E=32, n_group=8, topk_group=4) if args.ncu_case == "v3-prefill" else V3
-        T = 512 if args.ncu_case == "v3-prefill" else 32
+        T = {"v3-prefill": 512, "v3": 4096}.get(args.ncu_case, 32)
     else:
         W, T = V2, (32 if args.ncu_case == "decode" else 2048)
         if args.ncu_case == "prefill":
