@@ -22,16 +22,11 @@
 //   B  the activation rows of the group, bf16, 128-byte swizzle, one TMA box
 //      of 128 or 256 rows per 64-element K block;
 //   D  f32 in tensor memory columns 256..511.
-// The pipeline moves in stages of two K blocks (128 K): a stage uses one of
-// four 64-column TMEM slots for A and one of three 64 KB shared-memory slots
-// for B.  The two rings have their own barriers -- A: "afull" (four
-// dequant-warp arrivals) and "aempty" (MMA commit); B: "full" (the TMA
-// transaction bytes) and "empty" (MMA commit) -- so the dequant warps can run
-// up to three stages ahead of the MMAs while the activation ring stays
-// within shared memory, and the single MMA thread waits once per eight MMAs.
-// (Measured at V3 shape with one shared ring of three: the MMA thread spent
-// ~19 % of its time waiting for a stage, the dequant warps publishing a
-// stage only after unpacking the next.)  One producer thread can issue a TMA box only
+// The pipeline moves in stages of two K blocks (128 K): a stage owns one
+// 64-column TMEM slot for A and one 64 KB shared-memory slot for B, and has
+// one "full" barrier (four dequant-warp arrivals + the TMA transaction
+// bytes) and one "empty" barrier (the MMA commit), so the single MMA thread
+// waits once per eight MMAs.  One producer thread can issue a TMA box only
 // every few hundred cycles (the issue and the barrier round trips), so boxes
 // are as large as the 128-byte swizzle allows and few per stage.
 //
@@ -67,20 +62,18 @@ constexpr int kEpiWarps = 16;                // four per TMEM lane quarter
 constexpr int kBWarp = 22;                   // activation producer
 constexpr int kNW = 3;                       // packed-weight stages
 constexpr int kWStage = 8192;                // 128 rows x 64 B (256 codes per row)
-constexpr int kNS = 3;                       // activation (B) stages in shared memory (2 K blocks each)
-constexpr int kNA = 4;                       // dequantised-weight (A) slots in tensor memory
+constexpr int kNS = 3;                       // pipeline stages (2 K blocks each)
 constexpr int kKbBytes = kPrefillTile * 128; // one K block of B: 256 rows x 128 B
 constexpr int kSBytes = 2 * kKbBytes;        // B bytes of a stage
 constexpr uint32_t kACols = 64;              // TMEM columns of A per stage
 constexpr uint32_t kDCol = 256;              // accumulator columns 256..511
 constexpr uint32_t kTmemCols = 512;
 constexpr int kItemCache = 256;
-static_assert(kNA * kACols <= kDCol, "A slots overlap the accumulator");
+static_assert(kNS * kACols <= kDCol, "A slots overlap the accumulator");
 
 struct Smem {
     uint64_t wfull[kNW], wempty[kNW];
-    uint64_t full[kNS], empty[kNS];        // activation stages: TMA bytes / MMA commit
-    uint64_t afull[kNA], aempty[kNA];      // weight slots: 4 dequant warps / MMA commit
+    uint64_t full[kNS], empty[kNS];
     uint64_t dfull, dempty, drain;
     uint32_t tmem_base;
     int abort;
@@ -189,12 +182,8 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
             mbar_init(&S->wempty[i], 4);
         }
         for (int i = 0; i < kNS; ++i) {
-            mbar_init(&S->full[i], 1);         // TMA bytes
+            mbar_init(&S->full[i], 4 + 1);     // dequant warps + TMA bytes
             mbar_init(&S->empty[i], 1);
-        }
-        for (int i = 0; i < kNA; ++i) {
-            mbar_init(&S->afull[i], 4);        // dequant warps
-            mbar_init(&S->aempty[i], 1);
         }
         mbar_init(&S->dfull, 1);
         mbar_init(&S->dempty, kEpiWarps);
@@ -310,13 +299,12 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                 tc_fence_after();
                 for (int kb = 0; kb < nkb; kb += 2, ++us) {
                     const int nk = nkb - kb < 2 ? nkb - kb : 2;
-                    const uint32_t s = us % kNS, sa = us % kNA;
+                    const uint32_t s = us % kNS;
                     if (!(ok = mbar_wait(&S->full[s], (us / kNS) & 1, abort, p.err))) break;
-                    if (!(ok = mbar_wait(&S->afull[sa], (us / kNA) & 1, abort, p.err))) break;
                     tc_fence_after();
                     for (int j = 0; j < nk; ++j) {
                         const uint32_t lo = bd_lo + (uint32_t)((s * kSBytes + j * kKbBytes) >> 4);
-                        const uint32_t a = tmem + sa * kACols + 32 * j;
+                        const uint32_t a = tmem + s * kACols + 32 * j;
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
                             mma_bf16_ts_lohi(tmem + kDCol, a + 8 * kk, lo + 2 * kk, bd_hi, idesc,
@@ -324,7 +312,6 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                     }
                     issued = true;
                     mma_commit(&S->empty[s]);
-                    mma_commit(&S->aempty[sa]);
                 }
                 if (!ok) break;
                 mma_commit(&S->dfull);
@@ -367,8 +354,8 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                     if (lane == 0) mbar_arrive(&S->wempty[ws]);
                     ++uw;
                 }
-                const uint32_t s = us % kNA;       // this stage's weight slot
-                if (!(ok = mbar_wait_warp(&S->aempty[s], ((us / kNA) & 1) ^ 1, abort, p.err))) break;
+                const uint32_t s = us % kNS;
+                if (!(ok = mbar_wait_warp(&S->empty[s], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
                 tc_fence_after();
                 // publish the previous stage (its stores had this stage's
                 // unpacking to complete in), then store this one
@@ -376,7 +363,7 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&S->afull[pend]);
+                    if (lane == 0) mbar_arrive(&S->full[pend]);
                 }
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
@@ -402,7 +389,7 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
         if (ok && pend >= 0) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&S->afull[pend]);
+            if (lane == 0) mbar_arrive(&S->full[pend]);
         }
     } else if (warp < kEpiWarp0 + kEpiWarps) {
         // -------------------------------------------------------- epilogue
