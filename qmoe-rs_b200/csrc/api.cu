@@ -214,6 +214,7 @@ struct qmoe_layer {
     CUtensorMap tm_pw[2], tm_pws[2];
     DevBuf xg, hb;
     CUtensorMap tm_xg, tm_hb, tm_xg2, tm_hb2;  // 256-row and 128-row boxes
+    CUtensorMap tm_xg3, tm_hb3;                // 192-row boxes
     // tracing
     bool profiling = false;
     // Host-buffer forwards that repeat with the same page-locked x and out:
@@ -817,7 +818,11 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
             !make_tmap_bf16(&L->tm_hb, L->hb.p, (uint64_t)Imax, (uint64_t)npos, 2 * (uint64_t)Imax,
                             64, kPrefillTile, CU_TENSOR_MAP_SWIZZLE_128B) ||
             !make_tmap_bf16(&L->tm_hb2, L->hb.p, (uint64_t)Imax, (uint64_t)npos, 2 * (uint64_t)Imax,
-                            64, kPrefillTile / 2, CU_TENSOR_MAP_SWIZZLE_128B))
+                            64, kPrefillTile / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_tmap_bf16(&L->tm_xg3, L->xg.p, (uint64_t)H, (uint64_t)npos, 2 * (uint64_t)H, 64,
+                            kPrefillTile * 3 / 4, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_tmap_bf16(&L->tm_hb3, L->hb.p, (uint64_t)Imax, (uint64_t)npos, 2 * (uint64_t)Imax,
+                            64, kPrefillTile * 3 / 4, CU_TENSOR_MAP_SWIZZLE_128B))
             return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill rows");
     }
     if (!make_tmap_u8(&L->tm_xq1, L->xq1.p, (uint64_t)L->kp1, (uint64_t)(npos * 3), 128, 16,
@@ -1029,6 +1034,7 @@ static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, c
     m0.s1 = L->tm_pws[1];
     m0.b = L->tm_xg;
     m0.b2 = L->tm_xg2;
+    m0.b3 = L->tm_xg3;
     QgemmParams g0{};
     g0.groups = L->groups.as<int4>();
     g0.n_groups = L->ngroups.as<int32_t>();
@@ -1053,6 +1059,7 @@ static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, c
     m1.s0 = m1.s1 = L->tm_ws[2];
     m1.b = L->tm_hb;
     m1.b2 = L->tm_hb2;
+    m1.b3 = L->tm_hb3;
     QgemmParams g1{};
     g1.groups = g0.groups;
     g1.n_groups = g0.n_groups;

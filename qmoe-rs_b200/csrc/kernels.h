@@ -296,6 +296,7 @@ struct QgemmMaps {
     CUtensorMap s0, s1;          // shared-expert matrices (copies of w0/w1 if none)
     CUtensorMap b;               // bf16 activation rows [npos][ld], 128-byte swizzle, 256-row box
     CUtensorMap b2;              // the same rows, 128-row box
+    CUtensorMap b3;              // the same rows, 192-row box
 };
 struct QgemmParams {
     const int4 *groups;          // (segment, first position, count <= 256)

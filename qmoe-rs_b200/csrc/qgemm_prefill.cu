@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_s1,
                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b2,
-                     const QgemmParams p) {
+                     const __grid_constant__ CUtensorMap tm_b3, const QgemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -257,16 +257,17 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
         if (lane == 0) {
             tma_prefetch_desc(&tm_b);
             tma_prefetch_desc(&tm_b2);
+            tma_prefetch_desc(&tm_b3);
             uint32_t us = 0;
             bool ok = true;
             for (int i = 0; ok && i < my_items; ++i) {
                 const Item it = item_at(i);
                 const int K = it.shared ? p.K_s : p.K;
                 const int nkb = K / 64;
-                // one box per K block: 128 rows when they hold the group, else 256
-                const bool small = it.count <= 128;
-                const CUtensorMap *mb = small ? &tm_b2 : &tm_b;
-                const uint32_t box = small ? 128 * 128 : 256 * 128;
+                // one box per K block, the smallest of 128 / 192 / 256 rows that
+                // holds the group (the MMAs read N = count rounded to 16 rows)
+                const CUtensorMap *mb = it.count <= 128 ? &tm_b2 : it.count <= 192 ? &tm_b3 : &tm_b;
+                const uint32_t box = (it.count <= 128 ? 128 : it.count <= 192 ? 192 : 256) * 128;
                 for (int kb = 0; kb < nkb; kb += 2, ++us) {
                     const int nk = nkb - kb < 2 ? nkb - kb : 2;
                     const uint32_t s = us % kNS;
@@ -490,9 +491,9 @@ cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmPar
                               : ensure_dyn_smem(reinterpret_cast<const void *>(qgemm_prefill_kernel<1>), smem);
     if (e != cudaSuccess) return e;
     return mode == 0 ? launch_pdl(qgemm_prefill_kernel<0>, dim3(grid), dim3(kThreads), smem, s, maps.w0,
-                                  maps.w1, maps.s0, maps.s1, maps.b, maps.b2, p)
+                                  maps.w1, maps.s0, maps.s1, maps.b, maps.b2, maps.b3, p)
                      : launch_pdl(qgemm_prefill_kernel<1>, dim3(grid), dim3(kThreads), smem, s, maps.w0,
-                                  maps.w1, maps.s0, maps.s1, maps.b, maps.b2, p);
+                                  maps.w1, maps.s0, maps.s1, maps.b, maps.b2, maps.b3, p);
 }
 
 cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s) {
