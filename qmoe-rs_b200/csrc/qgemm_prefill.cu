@@ -442,39 +442,57 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
     }
 }
 
-// One thread per 16-element block: row of x (bf16) -> position row of xg
-// with the block permuted (position 2q / 2q+1 of word q = 2j + pp holds
-// element 4pp + j / 8 + 4pp + j).
-constexpr int kGatherRows = 2;           // positions per CTA of the gather
+// Row of x (bf16) -> position row of xg with each 16-element block permuted
+// (position 2q / 2q+1 of word q = 2j + pp holds element 4pp + j / 8 + 4pp +
+// j).  One warp per position row, grid-stride over the rows; a lane moves
+// the 32-byte blocks lane, lane + 32, ... with two blocks' loads in flight
+// before their stores.
+constexpr int kGatherWarps = 8;
 
-__global__ void __launch_bounds__(256)
+QMOE_DEV void permute_block(const uint4 &a, const uint4 &c, uint4 &o0, uint4 &o1) {
+    o0.x = __byte_perm(a.x, c.x, 0x5410);  // e0  | e8
+    o0.y = __byte_perm(a.z, c.z, 0x5410);  // e4  | e12
+    o0.z = __byte_perm(a.x, c.x, 0x7632);  // e1  | e9
+    o0.w = __byte_perm(a.z, c.z, 0x7632);  // e5  | e13
+    o1.x = __byte_perm(a.y, c.y, 0x5410);  // e2  | e10
+    o1.y = __byte_perm(a.w, c.w, 0x5410);  // e6  | e14
+    o1.z = __byte_perm(a.y, c.y, 0x7632);  // e3  | e11
+    o1.w = __byte_perm(a.w, c.w, 0x7632);  // e7  | e15
+}
+
+__global__ void __launch_bounds__(kGatherWarps * 32)
 gather_bf16_kernel(const GatherParams p) {
-    // kGatherRows positions per CTA, one warp-aligned slice of threads per
-    // position, 16-element blocks along the row (no division per element)
-    constexpr int kPer = 256 / kGatherRows;
-    const int64_t pos = (int64_t)blockIdx.x * kGatherRows + threadIdx.x / kPer;
-    const int64_t nblk = p.H / 16;
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
-    if (pos >= p.npos) return;
-    const bool routed = pos < p.shared_base;
-    if (routed && pos >= *p.n_valid) return;
-    const int64_t row = routed ? (int64_t)p.pos_tok[pos] : p.shared_row0 + pos - p.shared_base;
-    const uint4 *src0 = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p.x) + row * p.H);
-    uint4 *dst0 = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.xg) + pos * p.H);
-    for (int64_t b = threadIdx.x % kPer; b < nblk; b += kPer) {
-        const uint4 a = __ldg(src0 + 2 * b), c = __ldg(src0 + 2 * b + 1);
-        uint4 o0, o1;
-        o0.x = __byte_perm(a.x, c.x, 0x5410);  // e0  | e8
-        o0.y = __byte_perm(a.z, c.z, 0x5410);  // e4  | e12
-        o0.z = __byte_perm(a.x, c.x, 0x7632);  // e1  | e9
-        o0.w = __byte_perm(a.z, c.z, 0x7632);  // e5  | e13
-        o1.x = __byte_perm(a.y, c.y, 0x5410);  // e2  | e10
-        o1.y = __byte_perm(a.w, c.w, 0x5410);  // e6  | e14
-        o1.z = __byte_perm(a.y, c.y, 0x7632);  // e3  | e11
-        o1.w = __byte_perm(a.w, c.w, 0x7632);  // e7  | e15
-        dst0[2 * b] = o0;
-        dst0[2 * b + 1] = o1;
+    const int lane = threadIdx.x & 31;
+    const int64_t nblk = p.H / 16;
+    const int64_t nvalid = *p.n_valid;
+    const int64_t warps = (int64_t)gridDim.x * kGatherWarps;
+    for (int64_t pos = (int64_t)blockIdx.x * kGatherWarps + (threadIdx.x >> 5); pos < p.npos; pos += warps) {
+        const bool routed = pos < p.shared_base;
+        if (routed && pos >= nvalid) continue;
+        const int64_t row = routed ? (int64_t)p.pos_tok[pos] : p.shared_row0 + pos - p.shared_base;
+        const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p.x) + row * p.H);
+        uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.xg) + pos * p.H);
+        int64_t b = lane;
+        for (; b + 32 < nblk; b += 64) {
+            const uint4 a0 = __ldg(src + 2 * b), c0 = __ldg(src + 2 * b + 1);
+            const uint4 a1 = __ldg(src + 2 * (b + 32)), c1 = __ldg(src + 2 * (b + 32) + 1);
+            uint4 o0, o1;
+            permute_block(a0, c0, o0, o1);
+            dst[2 * b] = o0;
+            dst[2 * b + 1] = o1;
+            permute_block(a1, c1, o0, o1);
+            dst[2 * (b + 32)] = o0;
+            dst[2 * (b + 32) + 1] = o1;
+        }
+        if (b < nblk) {
+            const uint4 a0 = __ldg(src + 2 * b), c0 = __ldg(src + 2 * b + 1);
+            uint4 o0, o1;
+            permute_block(a0, c0, o0, o1);
+            dst[2 * b] = o0;
+            dst[2 * b + 1] = o1;
+        }
     }
 }
 
@@ -498,8 +516,14 @@ cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmPar
 
 cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s) {
     if (p.npos == 0) return cudaSuccess;
-    const int64_t blocks = (p.npos + kGatherRows - 1) / kGatherRows;
-    return launch_pdl(gather_bf16_kernel, dim3((unsigned)blocks), dim3(256), 0, s, p);
+    // enough warps for every SM (8 CTAs of 8 warps each), at most one per row
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t need = (p.npos + kGatherWarps - 1) / kGatherWarps;
+    const int64_t cap = (int64_t)sms * 8;
+    return launch_pdl(gather_bf16_kernel, dim3((unsigned)(need < cap ? need : cap)), dim3(kGatherWarps * 32), 0,
+                      s, p);
 }
 
 }  // namespace qmoe

@@ -89,3 +89,35 @@ def test_v3_decode_matches_oracle(v3, dtype, T):
     np.testing.assert_array_equal(w.cpu().numpy(), rw)
     tol = F32_TOL if dtype == torch.float32 else BF16_TOL
     assert rel_err(out.float().cpu().numpy(), ro) <= tol
+
+
+def test_v3_zipf_biased_routing_matches_oracle(v3):
+    # configs[4]'s router: a per-expert selection bias fitted so expert
+    # popularity follows a Zipf(1.1) head (hottest ~8 % of assignments);
+    # sampled tokens of a 2048-token batch against the oracle with the same
+    # bias, routing bit-exact
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    import bench
+    layer0, np_exp, np_sh, gw, ocfg = v3
+    W = bench.V3
+    bias, target = bench.zipf_bias(W, torch.from_numpy(gw).cuda(), seed=99)
+    cfg = MoEConfig(E, K, H, I, shared_intermediate_dim=IS, scoring=capi.QMOE_SCORING_SIGMOID,
+                    n_group=8, topk_group=4, norm_topk_prob=True, routed_scaling_factor=2.5)
+    layer = QMoELayer(cfg, gw, np_exp, shared=np_sh, bias=bias.cpu().numpy())
+    T = 2048
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(61)).bfloat16()
+    out, idx, w = layer.forward(x.cuda(), return_routing=True)
+    torch.cuda.synchronize()
+    share = np.bincount(idx.cpu().numpy().reshape(-1), minlength=E) / (T * K)
+    assert 0.05 <= share.max() <= 0.11, share.max()
+    assert int(np.argmax(share)) == int(np.argmax(target))
+    sample = np.sort(np.random.default_rng(8).choice(T, 32, replace=False))
+    ro, ri, rw = qo.layer_forward(ocfg, gw, np_exp, x[sample].float().numpy(), shared=np_sh,
+                                  bias=bias.cpu().numpy(), nthreads=NTHREADS)
+    np.testing.assert_array_equal(idx.cpu().numpy()[sample], ri)
+    np.testing.assert_array_equal(w.cpu().numpy()[sample], rw)
+    assert rel_err(out.float().cpu().numpy()[sample], ro) <= BF16_TOL
+    layer.close()
