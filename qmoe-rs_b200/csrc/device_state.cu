@@ -38,6 +38,20 @@ int *device_error_flag() {
     return static_cast<int *>(p);
 }
 
+int device_sm_count() {
+    static std::atomic<int> cached[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev >= 0 && dev < kMaxDevices) {
+        const int c = cached[dev].load(std::memory_order_relaxed);
+        if (c > 0) return c;
+    }
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    if (dev >= 0 && dev < kMaxDevices) cached[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
 cudaError_t ensure_dyn_smem(const void *func, size_t bytes) {
     // (no shortcut below 48 KB: a kernel's static shared memory counts
     // against the default limit too, so a launch with less dynamic memory

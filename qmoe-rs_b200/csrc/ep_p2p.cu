@@ -9,13 +9,12 @@
 // peers' memory over NVLink from the kernels that read the data -- no
 // collective library, no staging buffer, no TMA on peer memory.
 //
-// Ordering: every CTA of a copy kernel moves one row to one rank; it fences
-// its stores system-wide and adds one to that rank's arrival counter for
-// (phase, this rank) with a system-scope atomic.  A waiting rank polls its
-// own counters with acquire loads until each peer's reaches C x the
-// forward's sequence number (bounded; on time-out it raises the device error
-// word); rows a rank sends to itself are ordered by its stream and not
-// counted.  The sequence number lives on the device (read by every kernel of
+// Ordering: the CTAs of a copy kernel stride over the rows (any destination);
+// each fences its stores system-wide once, and the last CTA raises every
+// peer's flag for (phase, this rank) (ep_signal.cuh).  A waiting rank polls
+// its own flags with acquire loads until each peer's reaches the forward's
+// sequence number (bounded; on time-out it raises the device error word);
+// rows a rank sends to itself are ordered by its stream.  The sequence number lives on the device (read by every kernel of
 // a forward, advanced by the last wait), so a whole forward can be replayed
 // from a CUDA graph.  Rank d's receive buffer is
 // rewritten only in the next forward, after d has returned its partial sums
@@ -42,73 +41,84 @@ QMOE_DEV int ld_acquire_sys(const int *p) {
 
 QMOE_DEV int *flag_at(const EpPeerDev &d, int owner, int phase, int from) { return ep_flag(d, owner, phase, from); }
 
-// Copies one row of `bytes` (a multiple of 16) with the CTA.
+// Copies one row of `bytes` (a multiple of 16) with the CTA, four 16-byte
+// loads in flight per thread before their stores.
 QMOE_DEV void copy_row(uint8_t *dst, const uint8_t *src, int64_t bytes) {
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *o = reinterpret_cast<uint4 *>(dst);
-    for (int64_t i = threadIdx.x; i < bytes / 16; i += kCopyThreads) o[i] = s[i];
+    const int64_t n = bytes / 16;
+    for (int64_t i0 = threadIdx.x; i0 < n; i0 += 4 * kCopyThreads) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (i0 + u * kCopyThreads < n) v[u] = __ldg(s + i0 + u * kCopyThreads);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (i0 + u * kCopyThreads < n) o[i0 + u * kCopyThreads] = v[u];
+    }
 }
 
-// After this CTA's stores to rank dst: count the CTA towards dst's signal
-// (rows a rank keeps are ordered by its own stream); `units` CTAs write to
-// each destination.
-QMOE_DEV void arrive(const EpPeerDev &d, int dst, int phase, int units) {
+// After all of this CTA's stores: count it towards the phase's signal.
+QMOE_DEV void arrive(const EpPeerDev &d, int phase) {
     __syncthreads();
-    if (threadIdx.x == 0 && dst != d.rank) ep_signal(d, dst, phase, units);
+    if (threadIdx.x == 0) ep_signal_all(d, phase, (int)gridDim.x);
 }
 
-// CTA j < world*C: send row j (destination j / C, row j % C) if it is in use,
-// and its metadata row; CTA world*C + t: this rank's own token t for the
-// shared expert (metadata: no routed expert).
+// Row j < world*C: send row j (destination j / C, row j % C) if it is in use,
+// and its metadata row; row world*C + t: this rank's own token t for the
+// shared expert (metadata: no routed expert).  CTAs stride over the rows.
 __global__ void __launch_bounds__(kCopyThreads)
 ep_dispatch_kernel(const EpPeerDev d, const void *x, int64_t T, const int32_t *send_counts,
                    const int32_t *send_tok, const int32_t *send_meta) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
     const int64_t GC = (int64_t)d.world * d.C;
-    const int64_t j = blockIdx.x;
     const int64_t rb = d.H * d.esize, mb = 2 * (int64_t)d.K * 4;
     const uint8_t *xs = static_cast<const uint8_t *>(x);
-    if (j < GC) {
-        const int dst = (int)(j / d.C);
-        const int64_t i = j - (int64_t)dst * d.C;
-        const int64_t r = (int64_t)d.rank * d.C + i;           // row in the destination's block
-        if (i < send_counts[dst]) copy_row(d.base[dst] + d.off_rows + r * rb, xs + send_tok[j] * rb, rb);
-        int32_t *m = reinterpret_cast<int32_t *>(d.base[dst] + d.off_meta + r * mb);
-        for (int k = threadIdx.x; k < 2 * d.K; k += kCopyThreads) m[k] = send_meta[j * 2 * d.K + k];
-        arrive(d, dst, 0, (int)d.C);
-    } else if (j - GC < T) {
-        const int64_t t = j - GC, r = GC + t;
-        copy_row(d.base[d.rank] + d.off_rows + r * rb, xs + t * rb, rb);
-        int32_t *m = reinterpret_cast<int32_t *>(d.base[d.rank] + d.off_meta + r * mb);
-        for (int k = threadIdx.x; k < 2 * d.K; k += kCopyThreads) m[k] = k < d.K ? -1 : 0;
+    for (int64_t j = blockIdx.x; j < GC + T; j += gridDim.x) {
+        if (j < GC) {
+            const int dst = (int)(j / d.C);
+            const int64_t i = j - (int64_t)dst * d.C;
+            const int64_t r = (int64_t)d.rank * d.C + i;           // row in the destination's block
+            if (i < send_counts[dst]) copy_row(d.base[dst] + d.off_rows + r * rb, xs + send_tok[j] * rb, rb);
+            int32_t *m = reinterpret_cast<int32_t *>(d.base[dst] + d.off_meta + r * mb);
+            for (int k = threadIdx.x; k < 2 * d.K; k += kCopyThreads) m[k] = send_meta[j * 2 * d.K + k];
+        } else {
+            const int64_t t = j - GC, r = GC + t;
+            copy_row(d.base[d.rank] + d.off_rows + r * rb, xs + t * rb, rb);
+            int32_t *m = reinterpret_cast<int32_t *>(d.base[d.rank] + d.off_meta + r * mb);
+            for (int k = threadIdx.x; k < 2 * d.K; k += kCopyThreads) m[k] = k < d.K ? -1 : 0;
+        }
     }
+    arrive(d, 0);
 }
 
-// CTA j < world*C: the partial row j (rows received from rank j / C) goes to
+// Row j < world*C: the partial row j (rows received from rank j / C) goes to
 // that rank's return block, unless no slot of the row was routed here (its
-// metadata ids all -1: the origin never reads it); either way it counts the
-// exchange's ret_units arrivals.
+// metadata ids all -1: the origin never reads it).  CTAs stride over the
+// rows.
 __global__ void __launch_bounds__(kCopyThreads)
 ep_return_kernel(const EpPeerDev d, const void *y) {
     __shared__ int s_live;
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
-    const int64_t j = blockIdx.x;
     const int64_t rb = d.H * d.esize;
-    const int dst = (int)(j / d.C);
-    const int64_t i = j - (int64_t)dst * d.C;
-    if (threadIdx.x < 32) {
-        const int32_t *m = reinterpret_cast<const int32_t *>(d.base[d.rank] + d.off_meta) + j * 2 * d.K;
-        const bool live = threadIdx.x < d.K && __ldcg(m + threadIdx.x) >= 0;
-        const bool any = __any_sync(0xffffffffu, live) || d.K > 32;
-        if (threadIdx.x == 0) s_live = any;
+    for (int64_t j = blockIdx.x; j < (int64_t)d.world * d.C; j += gridDim.x) {
+        const int dst = (int)(j / d.C);
+        const int64_t i = j - (int64_t)dst * d.C;
+        if (threadIdx.x < 32) {
+            const int32_t *m = reinterpret_cast<const int32_t *>(d.base[d.rank] + d.off_meta) + j * 2 * d.K;
+            const bool live = threadIdx.x < d.K && __ldcg(m + threadIdx.x) >= 0;
+            const bool any = __any_sync(0xffffffffu, live) || d.K > 32;
+            if (threadIdx.x == 0) s_live = any;
+        }
+        __syncthreads();
+        if (s_live)
+            copy_row(d.base[dst] + d.off_back + ((int64_t)d.rank * d.C + i) * rb,
+                     static_cast<const uint8_t *>(y) + j * rb, rb);
+        __syncthreads();                           // s_live is rewritten next row
     }
-    __syncthreads();
-    if (s_live)
-        copy_row(d.base[dst] + d.off_back + ((int64_t)d.rank * d.C + i) * rb,
-                 static_cast<const uint8_t *>(y) + j * rb, rb);
-    arrive(d, dst, 1, (int)d.C);
+    arrive(d, 1);
 }
 
 // Lane p waits until rank p's C rows of `phase` of this forward have
@@ -210,13 +220,16 @@ cudaError_t launch_ep_finish(const EpPeerDev &d, const int32_t *slot_pos, int64_
 
 cudaError_t launch_ep_dispatch(const EpPeerDev &d, const void *x, int64_t T, const int32_t *send_counts,
                                const int32_t *send_tok, const int32_t *send_meta, cudaStream_t s) {
-    const int64_t ctas = (int64_t)d.world * d.C + T;
-    return launch_pdl(ep_dispatch_kernel, dim3((unsigned)ctas), dim3(kCopyThreads), 0, s, d, x, T, send_counts,
-                      send_tok, send_meta);
+    const int64_t rows = (int64_t)d.world * d.C + T;
+    const int grid = (int)std::min<int64_t>(rows, (int64_t)device_sm_count() * kEpCopyCtasPerSm);
+    return launch_pdl(ep_dispatch_kernel, dim3((unsigned)std::max(grid, 1)), dim3(kCopyThreads), 0, s, d, x, T,
+                      send_counts, send_tok, send_meta);
 }
 
 cudaError_t launch_ep_return(const EpPeerDev &d, const void *y, cudaStream_t s) {
-    return launch_pdl(ep_return_kernel, dim3((unsigned)(d.world * d.C)), dim3(kCopyThreads), 0, s, d, y);
+    const int64_t rows = (int64_t)d.world * d.C;
+    const int grid = (int)std::min<int64_t>(rows, (int64_t)device_sm_count() * kEpCopyCtasPerSm);
+    return launch_pdl(ep_return_kernel, dim3((unsigned)std::max(grid, 1)), dim3(kCopyThreads), 0, s, d, y);
 }
 
 cudaError_t launch_ep_wait(const EpPeerDev &d, int phase, cudaStream_t s) {

@@ -79,8 +79,8 @@ struct EpPeerDev {
     int64_t off_rows, off_meta, off_back, off_flags;
     int *seq;                    // this rank's per-forward sequence number
     int *done;                   // exit count of the return-side kernel (zero between launches)
-    int *cnt;                    // [2][kEpMaxWorld] units done per (phase, destination)
-                                 // within one launch (zero between launches; ep_signal.cuh)
+    int *cnt;                    // [2][kEpMaxWorld]; [phase][0]: CTAs of one launch done
+                                 // (zero between launches; ep_signal.cuh)
     int *err;                    // device error word
 };
 
@@ -258,6 +258,13 @@ cudaError_t launch_ep_finish(const EpPeerDev &d, const int32_t *slot_pos, int64_
 // Device-side error word (device_state.cu) raised by a bounded wait that gives
 // up: its address on the current device.
 int *device_error_flag();
+
+// Host: the current device's SM count (cached per device; 148 if the query
+// fails).
+int device_sm_count();
+// CTAs per SM of the grid-stride copy and return kernels of the expert-
+// parallel exchange (each CTA fences its peer stores once).
+constexpr int kEpCopyCtasPerSm = 4;
 
 // Host: raise `func`'s dynamic shared-memory opt-in on the current device to
 // at least `bytes` (never lowers it; remembered per kernel and device).

@@ -568,7 +568,7 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             __syncthreads();
             if (!S->grid_ok) break;
             // expert parallel: a received row's partial sum goes straight to
-            // its origin rank's return block, one arrival per task
+            // its origin rank's return block
             void *orow = nullptr;
             int dst = -1;
             if (p.ep_ret && t < (int64_t)p.ret.world * p.ret.C) {
@@ -578,12 +578,13 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
             }
             const int c4 = ch * 256 + tid;
             // a received row without live slots is never read by its origin:
-            // not sent, only counted
+            // not sent
             if (tid < 256 && c4 < H4 && (dst < 0 || S->c_n > 0))
                 combine_float4(p.c, t, 4 * c4, S->c_n, S->c_pos, S->c_w, orow);
             __syncthreads();
-            if (tid == 0 && dst >= 0 && dst != p.ret.rank) ep_signal(p.ret, dst, 1, (int)(p.ret.C * nch));
         }
+        // every CTA counts in once, after all of its stores into peer memory
+        if (p.ep_ret && tid == 0) ep_signal_all(p.ret, 1, (int)gridDim.x);
     }
     // the last CTA out resets the grid's counters for the next launch
     // (every CTA's last counter use precedes its exit count)
