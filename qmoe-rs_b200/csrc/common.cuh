@@ -51,6 +51,16 @@ QMOE_DEV int ld_acquire_sys_i32(const int *p) {
 // not negative (valid while the two are less than 2^31 apart).
 QMOE_DEV bool arrived(int count, uint32_t want) { return (int32_t)((uint32_t)count - want) >= 0; }
 
+// Group g of a segment of c positions cut into ceil(c / chunk) groups of
+// near-equal size (each at most chunk): (first position, count).  Even
+// groups keep the GEMMs' tiles full (300 rows as 150 + 150, not 256 + 44).
+QMOE_DEV int2 split_group(int64_t c, int chunk, int g) {
+    const int64_t ng = (c + chunk - 1) / chunk;
+    const int64_t sz = (c + ng - 1) / ng;
+    const int64_t b = (int64_t)g * sz;
+    return make_int2((int)b, (int)(c - b < sz ? c - b : sz));
+}
+
 // load_act4 through L2 only, for rows other CTAs or other GPUs wrote after
 // this kernel started (the read-only path of __ldg is not coherent with them).
 QMOE_DEV float4 load_act4_cg(const void *base, int dtype, int64_t idx) {

@@ -143,7 +143,8 @@ QMOE_DEV void partial_tile(const float *w, const float *x, int ws_ld, int xs_ld,
 
 // The permute of all T tokens from their selections sel[T][K] (one CTA, one
 // thread per expert): expert segments in expert order, tokens in order
-// inside a segment, groups of f.chunk positions, the shared groups last.
+// inside a segment, groups of at most f.chunk positions (split_group), the
+// shared groups last.
 QMOE_DEV void permute_tail(const FrontParams &f, int T, int E, int K, const int *sel, TailState &S) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int e = tid; e < E; e += kFrontThreads) {
@@ -189,8 +190,10 @@ QMOE_DEV void permute_tail(const FrontParams &f, int T, int E, int K, const int 
         const int off = cb + ci - cnt, goff = gb + gi - ng;
         S.off[e] = off;
         f.seg_off[e] = off;
-        for (int g = 0; g < ng; ++g)
-            f.groups[goff + g] = make_int4(e, off + g * f.chunk, min(f.chunk, cnt - g * f.chunk), 0);
+        for (int g = 0; g < ng; ++g) {
+            const int2 sg = split_group(cnt, f.chunk, g);
+            f.groups[goff + g] = make_int4(e, off + sg.x, sg.y, 0);
+        }
     }
     __syncthreads();
     // each assignment's position: its token's rank among the expert's tokens
@@ -208,9 +211,8 @@ QMOE_DEV void permute_tail(const FrontParams &f, int T, int E, int K, const int 
         f.n_groups[1] = ns;
     }
     for (int g = tid; g < ns; g += kFrontThreads) {
-        const int64_t b = (int64_t)g * f.chunk;
-        const int64_t rem = f.shared_count - b;
-        f.groups[gt + g] = make_int4(E, (int)(TK + b), (int)(rem < f.chunk ? rem : f.chunk), 0);
+        const int2 sg = split_group(f.shared_count, f.chunk, g);
+        f.groups[gt + g] = make_int4(E, TK + sg.x, sg.y, 0);
     }
 }
 

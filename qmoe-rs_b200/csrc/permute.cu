@@ -142,8 +142,8 @@ permute_kernel(const PermuteParams p) {
             p.seg_off[e] = off[e];
             const int c = tot[e];
             for (int g = 0; g * p.chunk < c; ++g) {
-                const int b = g * p.chunk;
-                p.groups[goff[e] + g] = make_int4(e, off[e] + b, min(p.chunk, c - b), 0);
+                const int2 sg = split_group(c, p.chunk, g);
+                p.groups[goff[e] + g] = make_int4(e, off[e] + sg.x, sg.y, 0);
             }
         }
         const int ns = p.shared_count ? (int)((p.shared_count + p.chunk - 1) / p.chunk) : 0;
@@ -153,9 +153,8 @@ permute_kernel(const PermuteParams p) {
             p.n_groups[1] = ns;
         }
         for (int g = tid; g < ns; g += kPermThreads) {
-            const int64_t b = (int64_t)g * p.chunk;
-            const int64_t rem = p.shared_count - b;
-            p.groups[totals.y + g] = make_int4(E, (int)(TK + b), (int)(rem < p.chunk ? rem : p.chunk), 0);
+            const int2 sg = split_group(p.shared_count, p.chunk, g);
+            p.groups[totals.y + g] = make_int4(E, (int)(TK + sg.x), sg.y, 0);
         }
     }
 

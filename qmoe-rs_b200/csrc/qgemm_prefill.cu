@@ -268,6 +268,14 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                 // holds the group (the MMAs read N = count rounded to 16 rows)
                 const CUtensorMap *mb = it.count <= 128 ? &tm_b2 : it.count <= 192 ? &tm_b3 : &tm_b;
                 const uint32_t box = (it.count <= 128 ? 128 : it.count <= 192 ? 192 : 256) * 128;
+                if (it.count > kPrefillTile) {
+                    // a group larger than the stage slots: nothing is loaded,
+                    // every role gives up at its next wait
+                    atomicOr(p.err, kErrBadGroup);
+                    *abort = 1;
+                    ok = false;
+                    break;
+                }
                 for (int kb = 0; kb < nkb; kb += 2, ++us) {
                     const int nk = nkb - kb < 2 ? nkb - kb : 2;
                     const uint32_t s = us % kNS;

@@ -652,16 +652,15 @@ router_select_kernel(const RouterParams p, int from_partials, const FrontParams 
         f.seg_off[e] = S.off[e];
         const int c = S.cnt[e];
         for (int g = 0; g * f.chunk < c; ++g) {
-            const int b = g * f.chunk;
-            f.groups[S.goff[e] + g] = make_int4(e, S.off[e] + b, min(f.chunk, c - b), 0);
+            const int2 sg = split_group(c, f.chunk, g);
+            f.groups[S.goff[e] + g] = make_int4(e, S.off[e] + sg.x, sg.y, 0);
         }
     }
     {
         const int ns = (int)((f.shared_count + f.chunk - 1) / f.chunk);
         for (int g = tid; g < ns; g += kRouterThreads) {
-            const int64_t b = (int64_t)g * f.chunk;
-            const int64_t rem = f.shared_count - b;
-            f.groups[S.goff[E] + g] = make_int4(E, (int)(TK + b), (int)(rem < f.chunk ? rem : f.chunk), 0);
+            const int2 sg = split_group(f.shared_count, f.chunk, g);
+            f.groups[S.goff[E] + g] = make_int4(E, (int)(TK + sg.x), sg.y, 0);
         }
     }
     for (int a = tid; a < TK; a += kRouterThreads) {

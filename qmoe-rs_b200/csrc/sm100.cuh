@@ -13,6 +13,7 @@ namespace sm100 {
 // Device-side failure flag: set by a kernel whose bounded wait ran out; the
 // host reads it back (qmoe_ctx_synchronize and every host-pointer call).
 constexpr int kErrWaitTimeout = 1;
+constexpr int kErrBadGroup = 2;      // a work item larger than the kernel was configured for
 
 // One bounded wait = this many failed try_wait probes (each try_wait itself
 // suspends for up to a hardware-chosen time), on the order of a second.
