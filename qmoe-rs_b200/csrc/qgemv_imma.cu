@@ -124,10 +124,15 @@ QMOE_DEV void limb_phase(const DecodeParams &p, Smem *S, int tid, volatile int *
     const int bpt = (nblk + kQuantGroup - 1) / kQuantGroup;
     auto sync = [g] { named_bar(1 + g, kQuantGroup); };
     for (int64_t pos = (int64_t)blockIdx.x * 3 + g; pos < p.q.npos; pos += (int64_t)gridDim.x * 3) {
+        // rows of up to 1024 float4 (the V3 hidden size) stay in registers:
+        // every load in flight at once instead of two passes of dependent
+        // loads
         if (bpt <= 1)
             quant_position<1>(p.q, pos, ht, S->q_red[g], S->q_sum[g], sync);
         else if (bpt <= 2)
             quant_position<2>(p.q, pos, ht, S->q_red[g], S->q_sum[g], sync);
+        else if (bpt <= 4)
+            quant_position<4>(p.q, pos, ht, S->q_red[g], S->q_sum[g], sync);
         else
             quant_position<0>(p.q, pos, ht, S->q_red[g], S->q_sum[g], sync);
     }
@@ -545,12 +550,15 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
     }
     __syncthreads();
     if (MODE == 1 && p.combine) {
-        // combine phase: every CTA's y rows are stored before it counts in;
-        // tasks are (token, 1024 columns), the ranking of a task's rows done
-        // before the wait
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) atomicAdd(p.sched + 2, 1);
+        // combine phase: every CTA's y rows are stored before it counts in
+        // (the barrier above orders them before thread 0's fence, which
+        // makes them visible device-wide before its count: one fence per
+        // CTA, not one per warp); tasks are (token, 1024 columns), the
+        // ranking of a task's rows done before the wait
+        if (tid == 0) {
+            __threadfence();
+            atomicAdd(p.sched + 2, 1);
+        }
         const int H4 = p.c.H >> 2;
         const int nch = (H4 + 255) / 256;
         const int64_t ntask = p.c.T * nch;

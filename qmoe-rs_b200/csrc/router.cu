@@ -396,27 +396,136 @@ router_gemm_kernel(const RouterParams p) {
     }
 }
 
+// Chunk partials for layers that keep the transposed gate (E > 64), small
+// batches: CTA = 32 tokens x 128 experts x one chunk, 128 threads; warp w
+// owns experts 32w..32w+31, lane (tg = lane % 4, eg = lane / 4) 8 tokens x 4
+// experts, i.e. 16 accumulator pairs of fma.rn.f32x2 (each lane two IEEE
+// fused multiply-adds, rounded as fmaf: the chain of every (token, expert)
+// over the chunk's 64 k in order, from 0).  Per k a warp reads two 16-byte
+// loads of x and one of the gate: 12 shared-memory wavefronts for 32 FMAs
+// per lane, against 10 for 8 in router_chunk_kernel.
+constexpr int kChunkTTok = 32, kChunkTExp = 128, kChunkTThreads = 128;
+
+__global__ void __launch_bounds__(kChunkTThreads)
+router_chunk_t_kernel(const RouterParams p) {
+    __shared__ __align__(16) float xs[kGateChunk][kChunkTTok];
+    __shared__ __align__(16) float ws[kGateChunk][kChunkTExp];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t t0 = (int64_t)blockIdx.x * kChunkTTok;
+    const int e0 = blockIdx.y * kChunkTExp;
+    const int c = blockIdx.z;
+    const int ld = p.gate_t_ld;
+    // gate rows k of the chunk, experts e0 .. e0+127 (zero past ld): the
+    // layer's, independent of the preceding kernel
+    constexpr int kSegs = kChunkTExp / 4;
+#pragma unroll
+    for (int q = 0; q < kGateChunk * kSegs / kChunkTThreads; ++q) {
+        const int i = q * kChunkTThreads + tid;
+        const int k = i / kSegs, sgm = i % kSegs;
+        const int e = e0 + 4 * sgm;
+        const bool ok = e < ld;
+        cp_async16(&ws[k][4 * sgm], p.gate_t + (int64_t)(c * kGateChunk + k) * ld + (ok ? e : 0), ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    {
+        // x: warp w stores k = 16w .. 16w+15 of token lane (no bank conflicts)
+        const int r = lane, kq = warp * 16;
+        const int64_t t = t0 + r;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+        if (t < p.T) {
+            const int64_t base = t * p.H + (int64_t)c * kGateChunk + kq;
+            if (p.dtype == 0) {
+                const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(p.x) + base);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 a = __ldg(src + q);
+                    v[4 * q] = a.x;
+                    v[4 * q + 1] = a.y;
+                    v[4 * q + 2] = a.z;
+                    v[4 * q + 3] = a.w;
+                }
+            } else {
+                const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(p.x) + base);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const uint4 a = __ldg(src + q);
+                    const uint32_t u[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        v[8 * q + 2 * j] = __uint_as_float(u[j] << 16);
+                        v[8 * q + 2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xs[kq + j][r] = v[j];
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    const int tg = lane & 3, eg = lane >> 2;
+    const float4 *xs4 = reinterpret_cast<const float4 *>(&xs[0][0]);
+    const ulonglong2 *ws2 = reinterpret_cast<const ulonglong2 *>(&ws[0][0]);
+    const int xo = 2 * tg, wo = warp * 8 + eg;     // float4 index in an x row / a gate row
+    unsigned long long acc[8][2];
+#pragma unroll
+    for (int a = 0; a < 8; ++a) acc[a][0] = acc[a][1] = 0ull;
+#pragma unroll 8
+    for (int k = 0; k < kGateChunk; ++k) {
+        const float4 x0 = xs4[k * (kChunkTTok / 4) + xo];
+        const float4 x1 = xs4[k * (kChunkTTok / 4) + xo + 1];
+        const ulonglong2 w = ws2[k * (kChunkTExp / 4) + wo];
+        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+            const unsigned long long xx = dup2(xv[a]);
+            acc[a][0] = ffma2(xx, w.x, acc[a][0]);
+            acc[a][1] = ffma2(xx, w.y, acc[a][1]);
+        }
+    }
+    // acc[a] = token 8 tg + a, experts 4 (8 warp + eg) + {0, 1, 2, 3}
+    float *part = p.scratch + (int64_t)c * p.T * p.E;
+    const int e = e0 + 4 * wo;
+#pragma unroll
+    for (int a = 0; a < 8; ++a) {
+        const int64_t t = t0 + 8 * tg + a;
+        if (t >= p.T) continue;
+        const float v[4] = {__uint_as_float((uint32_t)acc[a][0]), __uint_as_float((uint32_t)(acc[a][0] >> 32)),
+                            __uint_as_float((uint32_t)acc[a][1]), __uint_as_float((uint32_t)(acc[a][1] >> 32))};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (e + j < p.E) part[t * p.E + e + j] = v[j];
+    }
+}
+
 // Whole logits from the chunk partials, one thread per (token, expert): the
-// ordered chunk sum, loads issued sixteen at a time, written over the slot
-// of chunk 0 that only this thread reads.  For batches too small to give the
-// one-warp-per-token selection enough warps to sum its partials quickly.
-__global__ void __launch_bounds__(256)
+// ordered chunk sum, loads issued thirty-two at a time, written over the
+// slot of chunk 0 that only this thread reads.  For batches too small to
+// give the one-warp-per-token selection enough warps to sum its partials
+// quickly.
+constexpr int kSumThreads = 128;
+
+__global__ void __launch_bounds__(kSumThreads)
 router_sum_kernel(const RouterParams p) {
     QMOE_PDL_WAIT();
     QMOE_PDL_TRIGGER();
-    const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    const int64_t i = (int64_t)blockIdx.x * kSumThreads + threadIdx.x;
     const int64_t n = p.T * p.E;
     if (i >= n) return;
     const int nc = p.H / kGateChunk;
     const float *pp = p.scratch + i;
     float tot = 0.0f;
     int c = 0;
-    for (; c + 16 <= nc; c += 16) {
-        float v[16];
+    for (; c + 32 <= nc; c += 32) {
+        float v[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = __ldcg(pp + (c + j) * n);
+        for (int j = 0; j < 32; ++j) v[j] = __ldcg(pp + (c + j) * n);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) tot = __fadd_rn(tot, v[j]);
+        for (int j = 0; j < 32; ++j) tot = __fadd_rn(tot, v[j]);
     }
     for (; c < nc; ++c) tot = __fadd_rn(tot, __ldcg(pp + c * n));
     p.scratch[i] = tot;
@@ -444,6 +553,101 @@ struct TailSmem {
     int sel[kTailMaxT][kTailMaxK];
     int is_last;
 };
+
+// With f.counter set: the last CTA of the selection kernel to finish builds
+// the expert segments and the work list from every token's selection (what
+// permute_kernel does), saving a launch for small batches.  Called by every
+// thread of every CTA after its own selections are stored.
+QMOE_DEV void permute_tail(const RouterParams &p, const FrontParams &f) {
+    if (!f.counter) return;
+    __shared__ TailSmem S;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int E = p.E, K = p.K;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) S.is_last = atomicAdd(f.counter, 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (!S.is_last) return;
+    __threadfence();
+    const int T = (int)p.T;
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int a = tid; a < T * K; a += nthr) S.sel[a / K][a % K] = __ldcg(p.topk_idx + a);
+    __syncthreads();
+    // expert segments in expert order, tokens in order inside a segment (the
+    // rank of token t in expert e's segment is the number of earlier tokens
+    // in e's token mask), groups of at most f.chunk positions, shared groups
+    // last
+    for (int e = tid; e < E; e += nthr) S.mask[e] = 0ull;
+    __syncthreads();
+    const int TK = T * K;
+    for (int a = tid; a < TK; a += nthr) {
+        const int t = a / K;
+        atomicOr(&S.mask[S.sel[t][a - t * K]], 1ull << t);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // exclusive scans over experts of counts and of group counts, 8
+        // experts per lane
+        int c8[8], g8[8], cs = 0, gsum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            c8[j] = e < E ? __popcll(S.mask[e]) : 0;
+            g8[j] = (c8[j] + f.chunk - 1) / f.chunk;
+            cs += c8[j];
+            gsum += g8[j];
+        }
+        int ci = cs, gi = gsum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int uc = __shfl_up_sync(0xffffffffu, ci, o), ug = __shfl_up_sync(0xffffffffu, gi, o);
+            if (lane >= o) { ci += uc; gi += ug; }
+        }
+        int run = ci - cs, grun = gi - gsum;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            if (e < E) {
+                S.off[e] = run;
+                S.goff[e] = grun;
+                S.cnt[e] = c8[j];
+            }
+            run += c8[j];
+            grun += g8[j];
+        }
+        if (lane == 31) {
+            S.off[E] = run;
+            S.goff[E] = grun;
+            f.seg_off[E] = run;
+            f.n_groups[0] = grun;
+            f.n_groups[1] = (int)((f.shared_count + f.chunk - 1) / f.chunk);
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += nthr) {
+        f.seg_off[e] = S.off[e];
+        const int c = S.cnt[e];
+        for (int g = 0; g * f.chunk < c; ++g) {
+            const int2 sg = split_group(c, f.chunk, g);
+            f.groups[S.goff[e] + g] = make_int4(e, S.off[e] + sg.x, sg.y, 0);
+        }
+    }
+    {
+        const int ns = (int)((f.shared_count + f.chunk - 1) / f.chunk);
+        for (int g = tid; g < ns; g += nthr) {
+            const int2 sg = split_group(f.shared_count, f.chunk, g);
+            f.groups[S.goff[E] + g] = make_int4(E, (int)(TK + sg.x), sg.y, 0);
+        }
+    }
+    for (int a = tid; a < TK; a += nthr) {
+        const int t = a / K, e = S.sel[t][a - t * K];
+        const int pos = S.off[e] + __popcll(S.mask[e] & ((1ull << t) - 1ull));
+        f.pos_tok[pos] = t;
+        f.assign_pos[a] = pos;
+    }
+    __syncthreads();
+    if (tid == 0) *f.counter = 0;
+}
 
 // Scoring and selection, one CTA per token; logits from the partials
 // (summed here in chunk order) or from router_logits_kernel.  With f.counter
@@ -582,116 +786,22 @@ router_select_kernel(const RouterParams p, int from_partials, const FrontParams 
             p.topk_w[(int64_t)t * K + j] = w[j];
         }
     }
-    if (!f.counter) return;
-
-    // hand-off: the last CTA to finish runs the permute
-    __shared__ TailSmem S;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) S.is_last = atomicAdd(f.counter, 1) == (int)gridDim.x - 1;
-    __syncthreads();
-    if (!S.is_last) return;
-    __threadfence();
-    const int T = (int)p.T;
-    const int lane = tid & 31, warp = tid >> 5;
-    for (int a = tid; a < T * K; a += kRouterThreads)
-        S.sel[a / K][a % K] = __ldcg(p.topk_idx + a);
-    __syncthreads();
-    // phase C: permute -- expert segments in expert order, tokens in order
-    // inside a segment (the rank of token t in expert e's segment is the
-    // number of earlier tokens in e's token mask), groups of f.chunk
-    // positions, shared groups last
-    for (int e = tid; e < E; e += kRouterThreads) S.mask[e] = 0ull;
-    __syncthreads();
-    const int TK = T * K;
-    for (int a = tid; a < TK; a += kRouterThreads) {
-        const int t = a / K;
-        atomicOr(&S.mask[S.sel[t][a - t * K]], 1ull << t);
-    }
-    __syncthreads();
-    if (warp == 0) {
-        // exclusive scans over experts of counts and of group counts, 8
-        // experts per lane
-        int c8[8], g8[8], cs = 0, gsum = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = lane * 8 + j;
-            c8[j] = e < E ? __popcll(S.mask[e]) : 0;
-            g8[j] = (c8[j] + f.chunk - 1) / f.chunk;
-            cs += c8[j];
-            gsum += g8[j];
-        }
-        int ci = cs, gi = gsum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int uc = __shfl_up_sync(0xffffffffu, ci, o), ug = __shfl_up_sync(0xffffffffu, gi, o);
-            if (lane >= o) { ci += uc; gi += ug; }
-        }
-        int run = ci - cs, grun = gi - gsum;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = lane * 8 + j;
-            if (e < E) {
-                S.off[e] = run;
-                S.goff[e] = grun;
-                S.cnt[e] = c8[j];
-            }
-            run += c8[j];
-            grun += g8[j];
-        }
-        if (lane == 31) {
-            S.off[E] = run;
-            S.goff[E] = grun;
-            f.seg_off[E] = run;
-            f.n_groups[0] = grun;
-            f.n_groups[1] = (int)((f.shared_count + f.chunk - 1) / f.chunk);
-        }
-    }
-    __syncthreads();
-    for (int e = tid; e < E; e += kRouterThreads) {
-        f.seg_off[e] = S.off[e];
-        const int c = S.cnt[e];
-        for (int g = 0; g * f.chunk < c; ++g) {
-            const int2 sg = split_group(c, f.chunk, g);
-            f.groups[S.goff[e] + g] = make_int4(e, S.off[e] + sg.x, sg.y, 0);
-        }
-    }
-    {
-        const int ns = (int)((f.shared_count + f.chunk - 1) / f.chunk);
-        for (int g = tid; g < ns; g += kRouterThreads) {
-            const int2 sg = split_group(f.shared_count, f.chunk, g);
-            f.groups[S.goff[E] + g] = make_int4(E, (int)(TK + sg.x), sg.y, 0);
-        }
-    }
-    for (int a = tid; a < TK; a += kRouterThreads) {
-        const int t = a / K, e = S.sel[t][a - t * K];
-        const int pos = S.off[e] + __popcll(S.mask[e] & ((1ull << t) - 1ull));
-        f.pos_tok[pos] = t;
-        f.assign_pos[a] = pos;
-    }
-    __syncthreads();
-    if (tid == 0) *f.counter = 0;
+    permute_tail(p, f);
 }
 
-// Scoring and selection with one warp per token, eight tokens per CTA (for
-// batches without the permute hand-off; E <= 256, K <= 32): the logits from
-// the partials (added in chunk order, loads issued eight at a time) or from
-// router_logits_kernel, then the warp's sort-based selection.
+// Scoring and selection with one warp per token, eight tokens per CTA (E <=
+// 256, K <= 32): the logits from the partials (added in chunk order, loads
+// issued eight at a time) or from the other logit kernels, then the warp's
+// sort-based selection; with f.counter set the last CTA then runs the
+// permute.
 constexpr int kSelWarps = 8;
 
 __host__ __device__ inline int sel_warp_floats(int E) { return 2 * ((E + 3) / 4 * 4) + 128; }
 
-__global__ void __launch_bounds__(kSelWarps * 32)
-router_select_warp_kernel(const RouterParams p, int from_partials) {
-    extern __shared__ float wsm[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int E = p.E, e4 = (E + 3) / 4 * 4;
-    float *ex = wsm + warp * sel_warp_floats(E), *lg = ex + e4, *gs = lg + e4;
-    int *gk = reinterpret_cast<int *>(gs + 64);
-    QMOE_PDL_WAIT();
-    QMOE_PDL_TRIGGER();
-    const int64_t t = (int64_t)blockIdx.x * kSelWarps + warp;
-    if (t >= p.T) return;                         // whole warps; no CTA barrier follows
+// One warp: token t's logits into lg, then its selection.
+QMOE_DEV void select_warp_token(const RouterParams &p, int from_partials, int64_t t, int lane, float *lg,
+                                float *ex, float *gs, int *gk) {
+    const int E = p.E;
     const int nc = p.H / kGateChunk;
     for (int e = lane; e < E; e += 32) {
         if (from_partials) {
@@ -721,6 +831,20 @@ router_select_warp_kernel(const RouterParams p, int from_partials) {
         select_token<4>(p, (int)t, lane, lg, ex, gs, gk, 0u, 0u, false);
     else
         select_token<8>(p, (int)t, lane, lg, ex, gs, gk, 0u, 0u, false);
+}
+
+__global__ void __launch_bounds__(kSelWarps * 32)
+router_select_warp_kernel(const RouterParams p, int from_partials, const FrontParams f) {
+    extern __shared__ float wsm[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int E = p.E, e4 = (E + 3) / 4 * 4;
+    float *ex = wsm + warp * sel_warp_floats(E), *lg = ex + e4, *gs = lg + e4;
+    int *gk = reinterpret_cast<int *>(gs + 64);
+    QMOE_PDL_WAIT();
+    QMOE_PDL_TRIGGER();
+    const int64_t t = (int64_t)blockIdx.x * kSelWarps + warp;
+    if (t < p.T) select_warp_token(p, from_partials, t, lane, lg, ex, gs, gk);
+    permute_tail(p, f);
 }
 
 }  // namespace
@@ -781,6 +905,11 @@ cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaSt
                   (unsigned)((p.E + kGemmExperts - 1) / kGemmExperts));
         e = launch_pdl(router_gemm_kernel, grid, dim3(kGemmThreads), smem, s, p);
         if (e != cudaSuccess) return e;
+    } else if (parts && p.gate_t && p.E > 64 && p.T <= 64) {
+        dim3 grid((unsigned)((p.T + kChunkTTok - 1) / kChunkTTok), (unsigned)((p.E + kChunkTExp - 1) / kChunkTExp),
+                  (unsigned)(p.H / kGateChunk));
+        cudaError_t e = launch_pdl(router_chunk_t_kernel, grid, dim3(kChunkTThreads), 0, s, p);
+        if (e != cudaSuccess) return e;
     } else if (parts) {
         const int nc = p.H / kGateChunk;
         const int TT = p.T <= 16 ? 1 : p.T <= 32 ? 2 : 4;
@@ -800,16 +929,20 @@ cudaError_t launch_router(const RouterParams &p, const FrontParams *tail, cudaSt
     // logit first (a warp or CTA per token would read them nearly serially)
     bool from_parts = parts;
     if (parts && p.T < 256 && p.H / kGateChunk >= 16) {
-        e = launch_pdl(router_sum_kernel, dim3((unsigned)((p.T * p.E + 255) / 256)), dim3(256), 0, s, p);
+        e = launch_pdl(router_sum_kernel, dim3((unsigned)((p.T * p.E + kSumThreads - 1) / kSumThreads)),
+                       dim3(kSumThreads), 0, s, p);
         if (e != cudaSuccess) return e;
         from_parts = false;
     }
+    // (with the permute hand-off the CTA-per-token selection is faster for
+    // these few tokens: the warp selection of 8 of 256 experts measured
+    // 55 us against 19 us at 32 tokens)
     if (!f.counter && p.E <= 256 && p.K <= 32) {
         const size_t wsmem = sizeof(float) * kSelWarps * sel_warp_floats(p.E);
         e = ensure_dyn_smem(reinterpret_cast<const void *>(router_select_warp_kernel), wsmem);
         if (e != cudaSuccess) return e;
         return launch_pdl(router_select_warp_kernel, dim3((unsigned)((p.T + kSelWarps - 1) / kSelWarps)),
-                          dim3(kSelWarps * 32), wsmem, s, p, from_parts ? 1 : 0);
+                          dim3(kSelWarps * 32), wsmem, s, p, from_parts ? 1 : 0, f);
     }
     const size_t smem = router_smem_bytes(p.H, p.E);
     e = ensure_dyn_smem(reinterpret_cast<const void *>(router_select_kernel), smem);
