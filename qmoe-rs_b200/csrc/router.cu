@@ -707,10 +707,13 @@ router_select_kernel(const RouterParams p, int from_partials, const FrontParams 
             const float *c = choice + g * per;
             int bi = 0;
             float best = c[0];
+            // (unrolled: the loads run ahead of the compare chain)
+#pragma unroll 8
             for (int j = 1; j < per; ++j)
                 if (c[j] > best) { best = c[j]; bi = j; }
             float second = NEG;
             bool have2 = false;
+#pragma unroll 8
             for (int j = 0; j < per; ++j)
                 if (j != bi && (!have2 || c[j] > second)) { second = c[j]; have2 = true; }
             gscore[g] = (!sigm || per < 2) ? best : __fadd_rn(best, second);
@@ -727,10 +730,12 @@ router_select_kernel(const RouterParams p, int from_partials, const FrontParams 
         __syncthreads();
     }
 
-    // 5. rank of every expert; the first K ranks are the selection
+    // 5. rank of every expert (a count: any order of the terms); the first
+    //    K ranks are the selection
     for (int e = tid; e < E; e += kRouterThreads) {
         const float v = choice[e];
         int r = 0;
+#pragma unroll 16
         for (int j = 0; j < E; ++j) r += ranks_before(choice[j], j, v, e);
         if (r < K) sel[r] = e;
     }
@@ -753,6 +758,7 @@ router_select_kernel(const RouterParams p, int from_partials, const FrontParams 
         for (int e = tid; e < E; e += kRouterThreads) {
             const float v = logit[e];
             int r = 0;
+#pragma unroll 16
             for (int j = 0; j < E; ++j) r += ranks_before(logit[j], j, v, e);
             ex[r] = expf(__fsub_rn(v, mx));
         }
@@ -765,14 +771,18 @@ router_select_kernel(const RouterParams p, int from_partials, const FrontParams 
     }
     __syncthreads();
 
-    // 6. combine weights
+    // 6. combine weights: slot j's by thread j, then the ordered sums by
+    //    thread 0
+    float *wsel = choice;                          // free after the ranking
+    if (tid < K) {
+        const float mx = misc[0], s = misc[1];
+        const int e = sel[tid];
+        wsel[tid] = sigm ? qsigmoid(logit[e]) : __fdiv_rn(expf(__fsub_rn(logit[e], mx)), s);
+    }
+    __syncthreads();
     if (tid == 0) {
         float w[64];
-        const float mx = misc[0], s = misc[1];
-        for (int j = 0; j < K; ++j) {
-            const int e = sel[j];
-            w[j] = sigm ? qsigmoid(logit[e]) : __fdiv_rn(expf(__fsub_rn(logit[e], mx)), s);
-        }
+        for (int j = 0; j < K; ++j) w[j] = wsel[j];
         if (p.norm_topk) {
             float den = 0.0f;
             for (int j = 0; j < K; ++j) den = __fadd_rn(den, w[j]);
