@@ -811,18 +811,18 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
     if (L->prefill_ok) {
         QTRY(grow(L->xg, 2 * (size_t)npos * H));
         QTRY(grow(L->hb, 2 * (size_t)npos * Imax));
-        if (!make_tmap_bf16(&L->tm_xg, L->xg.p, (uint64_t)H, (uint64_t)npos, 2 * (uint64_t)H, 64,
-                            kPrefillTile, CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !make_tmap_bf16(&L->tm_xg2, L->xg.p, (uint64_t)H, (uint64_t)npos, 2 * (uint64_t)H, 64,
-                            kPrefillTile / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !make_tmap_bf16(&L->tm_hb, L->hb.p, (uint64_t)Imax, (uint64_t)npos, 2 * (uint64_t)Imax,
-                            64, kPrefillTile, CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !make_tmap_bf16(&L->tm_hb2, L->hb.p, (uint64_t)Imax, (uint64_t)npos, 2 * (uint64_t)Imax,
-                            64, kPrefillTile / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !make_tmap_bf16(&L->tm_xg3, L->xg.p, (uint64_t)H, (uint64_t)npos, 2 * (uint64_t)H, 64,
-                            kPrefillTile * 3 / 4, CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !make_tmap_bf16(&L->tm_hb3, L->hb.p, (uint64_t)Imax, (uint64_t)npos, 2 * (uint64_t)Imax,
-                            64, kPrefillTile * 3 / 4, CU_TENSOR_MAP_SWIZZLE_128B))
+        // 3-D views [K block of 128 bytes][row][K block index]: one box =
+        // two K blocks of 128, 192 or 256 rows, i.e. one copy per GEMM stage
+        auto rows3d = [&](CUtensorMap *tm, void *base, uint64_t cols, uint32_t box_rows) {
+            return make_tmap_u8_3d(tm, base, 128, (uint64_t)npos, cols / 64, 2 * cols, 128, 128, box_rows, 2,
+                                   CU_TENSOR_MAP_SWIZZLE_128B);
+        };
+        if (!rows3d(&L->tm_xg, L->xg.p, (uint64_t)H, kPrefillTile) ||
+            !rows3d(&L->tm_xg2, L->xg.p, (uint64_t)H, kPrefillTile / 2) ||
+            !rows3d(&L->tm_xg3, L->xg.p, (uint64_t)H, kPrefillTile * 3 / 4) ||
+            !rows3d(&L->tm_hb, L->hb.p, (uint64_t)Imax, kPrefillTile) ||
+            !rows3d(&L->tm_hb2, L->hb.p, (uint64_t)Imax, kPrefillTile / 2) ||
+            !rows3d(&L->tm_hb3, L->hb.p, (uint64_t)Imax, kPrefillTile * 3 / 4))
             return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill rows");
     }
     if (!make_tmap_u8(&L->tm_xq1, L->xq1.p, (uint64_t)L->kp1, (uint64_t)(npos * 3), 128, 16,

@@ -19,8 +19,10 @@
 // down rows.  D[128 x N] += A[128 x 16] * B[N x 16]^T per instruction, with
 //   A  the dequantised weights, written by the dequant warps straight into
 //      tensor memory;
-//   B  the activation rows of the group, bf16, 128-byte swizzle, one TMA box
-//      of 128 or 256 rows per 64-element K block;
+//   B  the activation rows of the group, bf16, 128-byte swizzle, one 3-D TMA
+//      box per stage: two 64-element K blocks of 128, 192 or 256 rows (the
+//      fewer boxes, the faster the activation ring refills: with one 2-D box
+//      per K block the MMA thread waited for activations ~30 % of its time);
 //   D  f32 in tensor memory columns 256..511.
 // The pipeline moves in stages of two K blocks (128 K): a stage owns one
 // 64-column TMEM slot for A and one 64 KB shared-memory slot for B, and has
@@ -104,6 +106,9 @@ QMOE_DEV Item decode_item(const QgemmParams &p, int item, int nr, int mt_r, int 
     it.count = d.z;
     return it;
 }
+
+// Rows of the activation box of a group of `count` positions.
+QMOE_DEV int box_rows(int count) { return count <= 128 ? 128 : count <= 192 ? 192 : 256; }
 
 // (128 + c_lo, 128 + c_hi) - (129, 129) = (c_lo - 1, c_hi - 1), exact in bf16
 QMOE_DEV uint32_t codes_to_bf16x2(uint32_t biased) {
@@ -264,10 +269,12 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                 const Item it = item_at(i);
                 const int K = it.shared ? p.K_s : p.K;
                 const int nkb = K / 64;
-                // one box per K block, the smallest of 128 / 192 / 256 rows that
-                // holds the group (the MMAs read N = count rounded to 16 rows)
+                // one box per stage (two K blocks), the smallest of 128 / 192 /
+                // 256 rows that holds the group (the MMAs read N = count
+                // rounded to 16 rows); a stage with one K block left gets the
+                // second zero-filled (past the last K block) and unused
                 const CUtensorMap *mb = it.count <= 128 ? &tm_b2 : it.count <= 192 ? &tm_b3 : &tm_b;
-                const uint32_t box = (it.count <= 128 ? 128 : it.count <= 192 ? 192 : 256) * 128;
+                const uint32_t box = (uint32_t)box_rows(it.count) * 128;
                 if (it.count > kPrefillTile) {
                     // a group larger than the stage slots: nothing is loaded,
                     // every role gives up at its next wait
@@ -277,13 +284,10 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                     break;
                 }
                 for (int kb = 0; kb < nkb; kb += 2, ++us) {
-                    const int nk = nkb - kb < 2 ? nkb - kb : 2;
                     const uint32_t s = us % kNS;
                     if (!(ok = mbar_wait(&S->empty[s], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
-                    mbar_arrive_expect_tx(&S->full[s], nk * box);
-                    for (int j = 0; j < nk; ++j)
-                        tma_load_2d(bring + s * kSBytes + j * kKbBytes, mb, &S->full[s],
-                                    (kb + j) * 64, it.pos0);
+                    mbar_arrive_expect_tx(&S->full[s], 2 * box);
+                    tma_load_3d(bring + s * kSBytes, mb, &S->full[s], 0, it.pos0, kb);
                 }
             }
             if (!ok)
@@ -304,6 +308,7 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                 const int nkb = K / 64;
                 const int N = (it.count + 15) & ~15;
                 const uint32_t idesc = idesc_bf16(128, N);
+                const int box = box_rows(it.count) * 128;   // bytes of one K block of B
                 if (!(ok = mbar_wait(&S->dempty, (i & 1) ^ 1, abort, p.err))) break;
                 tc_fence_after();
                 for (int kb = 0; kb < nkb; kb += 2, ++us) {
@@ -312,7 +317,7 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                     if (!(ok = mbar_wait(&S->full[s], (us / kNS) & 1, abort, p.err))) break;
                     tc_fence_after();
                     for (int j = 0; j < nk; ++j) {
-                        const uint32_t lo = bd_lo + (uint32_t)((s * kSBytes + j * kKbBytes) >> 4);
+                        const uint32_t lo = bd_lo + (uint32_t)((s * kSBytes + j * box) >> 4);
                         const uint32_t a = tmem + s * kACols + 32 * j;
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
