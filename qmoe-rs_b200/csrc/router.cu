@@ -649,6 +649,28 @@ QMOE_DEV void permute_tail(const RouterParams &p, const FrontParams &f) {
     if (tid == 0) *f.counter = 0;
 }
 
+// Warp: the value at the first index (lane) of the largest non-NaN value
+// among the lanes other than `skip` -- the result of the scan
+// `best = v[first]; for later j: if (v[j] > best) best = v[j]` when the
+// first considered value is not NaN; its lane in *idx.
+QMOE_DEV float first_max(float v, int ln, int skip, int *idx) {
+    const float NEG = __int_as_float(0xff800000);
+    const bool out = ln == skip || v != v;
+    float bv = out ? NEG : v;
+    int bi = out ? 64 + ln : ln;                   // excluded lanes lose every tie
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    *idx = bi;
+    return bv;
+}
+
 // Scoring and selection, one CTA per token; logits from the partials
 // (summed here in chunk order) or from router_logits_kernel.  With f.counter
 // set, the last CTA to finish also builds the expert segments and the work
@@ -703,20 +725,37 @@ router_select_kernel(const RouterParams p, int from_partials, const FrontParams 
     const float NEG = __int_as_float(0xff800000);
     if (G > 1) {
         const int per = E / G;
-        for (int g = tid; g < G; g += kRouterThreads) {
-            const float *c = choice + g * per;
-            int bi = 0;
-            float best = c[0];
-            // (unrolled: the loads run ahead of the compare chain)
-#pragma unroll 8
-            for (int j = 1; j < per; ++j)
-                if (c[j] > best) { best = c[j]; bi = j; }
-            float second = NEG;
-            bool have2 = false;
-#pragma unroll 8
-            for (int j = 0; j < per; ++j)
-                if (j != bi && (!have2 || c[j] > second)) { second = c[j]; have2 = true; }
-            gscore[g] = (!sigm || per < 2) ? best : __fadd_rn(best, second);
+        if (per == 32 && G <= kRouterThreads / 32) {
+            // warp g, lane j: expert g*32 + j; the scans below as shuffle
+            // reductions with the same results
+            const int wg = tid >> 5, ln = tid & 31;
+            if (wg < G) {
+                const float v = choice[wg * 32 + ln];
+                const float c0 = __shfl_sync(0xffffffffu, v, 0);
+                float best = c0;
+                int bi = 0;
+                if (c0 == c0) best = first_max(v, ln, -1, &bi);   // else NaN first: never replaced
+                float second = NEG;
+                if (sigm) {
+                    const float cj0 = __shfl_sync(0xffffffffu, v, bi == 0 ? 1 : 0);
+                    int si;
+                    second = cj0 == cj0 ? first_max(v, ln, bi, &si) : cj0;
+                }
+                if (ln == 0) gscore[wg] = !sigm ? best : __fadd_rn(best, second);
+            }
+        } else {
+            for (int g = tid; g < G; g += kRouterThreads) {
+                const float *c = choice + g * per;
+                int bi = 0;
+                float best = c[0];
+                for (int j = 1; j < per; ++j)
+                    if (c[j] > best) { best = c[j]; bi = j; }
+                float second = NEG;
+                bool have2 = false;
+                for (int j = 0; j < per; ++j)
+                    if (j != bi && (!have2 || c[j] > second)) { second = c[j]; have2 = true; }
+                gscore[g] = (!sigm || per < 2) ? best : __fadd_rn(best, second);
+            }
         }
         __syncthreads();
         for (int g = tid; g < G; g += kRouterThreads) {
@@ -731,12 +770,42 @@ router_select_kernel(const RouterParams p, int from_partials, const FrontParams 
     }
 
     // 5. rank of every expert (a count: any order of the terms); the first
-    //    K ranks are the selection
+    //    K ranks are the selection.  When at least K experts of the kept
+    //    groups score above -inf and no score is NaN, the K best are kept
+    //    experts that every dropped expert (-inf) ranks after, so only kept
+    //    experts are ranked, against kept experts alone.
+    int n_real = 0, n_nan = 0;
     for (int e = tid; e < E; e += kRouterThreads) {
         const float v = choice[e];
+        n_real += v > NEG;
+        n_nan += v != v;
+    }
+    {
+        __shared__ int s_cnt[2];
+        if (tid < 2) s_cnt[tid] = 0;
+        __syncthreads();
+        if (n_real) atomicAdd(&s_cnt[0], n_real);
+        if (n_nan) atomicAdd(&s_cnt[1], n_nan);
+        __syncthreads();
+        n_real = s_cnt[0];
+        n_nan = s_cnt[1];
+    }
+    const bool kept_only = G > 1 && n_nan == 0 && n_real >= K;
+    const int per = E / G;
+    for (int e = tid; e < E; e += kRouterThreads) {
+        const float v = choice[e];
+        if (kept_only && !(v > NEG)) continue;     // ranks after the K best
         int r = 0;
+        if (kept_only) {
+            for (int g = 0; g < G; ++g) {
+                if (!gkeep[g]) continue;
+#pragma unroll 8
+                for (int j = g * per; j < (g + 1) * per; ++j) r += ranks_before(choice[j], j, v, e);
+            }
+        } else {
 #pragma unroll 16
-        for (int j = 0; j < E; ++j) r += ranks_before(choice[j], j, v, e);
+            for (int j = 0; j < E; ++j) r += ranks_before(choice[j], j, v, e);
+        }
         if (r < K) sel[r] = e;
     }
 
