@@ -329,6 +329,36 @@ def test_sigmoid_routing_both_logit_paths_bit_exact(T):
     np.testing.assert_array_equal(w.cpu().numpy(), rw)
 
 
+@pytest.mark.parametrize("case", ["sigmoid", "sigmoid_minus_inf_bias", "softmax_groups"])
+def test_small_batch_selection_with_permute_matches_oracle(case):
+    # 32 tokens of 256 experts: the CTA-per-token selection with the permute
+    # in its last CTA -- group scores by warp reductions, ranks over the kept
+    # groups, or over every expert when fewer than k kept experts score above
+    # -inf (the -inf bias case: five finite experts, ties broken by index)
+    E, H, I = 256, 512, 128
+    bias = None
+    if case == "softmax_groups":
+        cfg = MoEConfig(E, 6, H, I, n_group=8, topk_group=3)
+    else:
+        cfg = MoEConfig(E, 8, H, I, scoring=capi.QMOE_SCORING_SIGMOID, n_group=8, topk_group=4,
+                        norm_topk_prob=True, routed_scaling_factor=2.5)
+        bias = (torch.randn(E, generator=torch.Generator().manual_seed(77)) * 0.05).float()
+        if case == "sigmoid_minus_inf_bias":
+            bias[:] = float("-inf")
+            bias[[3, 40, 41, 200, 201]] = 0.0
+    layer, np_exp, _, gw = build(cfg, seed=31, bias=None if bias is None else bias.cuda())
+    x = torch.randn(32, H, generator=torch.Generator().manual_seed(5))
+    out, idx, w = layer.forward(x.cuda(), return_routing=True)
+    ro, ri, rw = qo.moe_forward(qo_cfg(cfg), gw, np_exp, x.numpy(),
+                                bias=None if bias is None else bias.numpy(), nthreads=NTHREADS)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    if case == "softmax_groups":
+        np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=1e-6, atol=0)
+    else:
+        np.testing.assert_array_equal(w.cpu().numpy(), rw)
+    assert rel_err(out.cpu().numpy(), ro) <= F32_TOL
+
+
 def test_forward_routed_matches_oracle():
     cfg = MoEConfig(16, 4, 256, 192)
     experts, _, gw = helpers.synth_layer(16, 256, 192, seed=17, device="cuda")
