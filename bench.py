@@ -980,6 +980,15 @@ def run_ep(args, W, ws, rank, local, dev, dist):
                 "steps": zs, "parity": zpar, "stage_ms_rank0": zst, "load": zload,
                 "target_hottest_share": float(np.max(target)),
                 "e2e_ms_per_step": ze2e}
+    dec = None
+    if W is V3 and not args.no_sublines:
+        # configs[1] in decode, expert parallel: 32 f32 tokens per GPU
+        ds = max(50, min(10 * args.steps, 500))
+        dms, dpar, dst, dload, de2e, _, _ = ep_measure(args, V2, 32, ws, rank, local, dev, dist, steps=ds)
+        dec = {"workload": "configs[1] layer (V2-Lite), decode, 32 f32 tokens per GPU, expert parallel "
+                           "(weak scaling)",
+               "value": ws * 32 / (dms / 1e3), "unit": UNIT, "ms_per_step": dms, "steps": ds,
+               "parity": dpar, "stage_ms_rank0": dst, "load": dload, "e2e_ms_per_step": de2e}
     if rank == 0:
         prefill = W["act"] == "bf16" and T * W["k"] // W["E"] >= 16
         gu_f, dn_f, fl = layer_flops(W, T)
@@ -1014,6 +1023,8 @@ def run_ep(args, W, ws, rank, local, dev, dist):
         }
         if zipf is not None:
             line["zipf"] = zipf
+        if dec is not None:
+            line["decode_v2lite_ep"] = dec
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
