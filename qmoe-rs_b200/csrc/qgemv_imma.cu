@@ -268,12 +268,15 @@ qgemv_imma_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p)
     Smem *S = reinterpret_cast<Smem *>(reinterpret_cast<uint8_t *>(acc_tile) + 4 * kAccBytes);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // The work list (groups, counts) and the weights are read before the
-    // wait on the preceding kernel: the list comes from a kernel at least two
-    // launches back (the permute or the front, then the limb kernel), which
-    // had completed before this grid was launched, because every kernel of
-    // the library triggers its dependents only after its own wait.  The limb
-    // rows, their metadata and every global write come after the wait.
+    // Separate-limb launches read the work list (groups, counts) and issue
+    // the first weights before the wait on the preceding kernel: the list
+    // comes from a kernel two launches back (the permute or the front, then
+    // the limb kernel), which had completed before this grid was launched,
+    // because every kernel of the library triggers its dependents only after
+    // its own wait.  A cooperative launch (limbs or combine inside) follows
+    // the kernel that builds the list, so it waits for that grid first.  The
+    // limb rows, their metadata and every global write come after the wait.
+    if (p.quant_in || p.combine) QMOE_PDL_WAIT();
     const int rows_item = MODE == 0 ? 128 : 256;
     const int rb_r = (p.rows + rows_item - 1) / rows_item;
     const int rb_s = p.rows_s > 0 ? (p.rows_s + rows_item - 1) / rows_item : 1;
