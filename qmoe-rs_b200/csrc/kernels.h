@@ -171,8 +171,8 @@ struct CombineParams {
     int out_dtype;
     // expert parallel (combine kernel): rows t < world * C are received rows;
     // each goes straight to its origin rank's return block (peer memory),
-    // skipped when it has no live slot, and every 1024-column slice counts
-    // one arrival there
+    // skipped when it has no live slot; every CTA signals once after its
+    // stores (ep_signal.cuh)
     int ep_ret;
     EpPeerDev ret;
 };
@@ -237,7 +237,7 @@ struct DecodeParams {
     int combine;                 // mode 1: after a grid barrier, the combine of c
     CombineParams c;             //    (combine.cuh) as the last phase
     int ep_ret;                  // with combine: rows r < ret.world * ret.C go straight to
-    EpPeerDev ret;               //    rank r / C's return block (peer memory), counted per task
+    EpPeerDev ret;               //    rank r / C's return block (peer memory), one signal per CTA
 };
 cudaError_t launch_qgemv_imma(int mode, const DecodeMaps &maps, const DecodeParams &p,
                               int grid, cudaStream_t s);
