@@ -1,5 +1,7 @@
 """Loader upload: one MoE layer's packed tensors from a qmoe-rs safetensors
-file into a device-resident QMoELayer (qmoe-rs src/loader.rs:204-359).
+file into a device-resident QMoELayer (qmoe-rs src/loader.rs:204-359), and
+the decoder layers' MoE blocks of a whole file as a chain
+(src/loader.rs:373-459 builds the model from the same keys).
 
 Key layout (the one quantize.py writes and src/loader.rs reads):
   layers.{l}.moe.gate.weight                          [E, H] router, f32
@@ -21,16 +23,29 @@ Rules kept from the reference:
     the shared expert (:262-305, :452-456).
 Tensors are read on the host (only this layer's keys) and handed to
 qmoe_layer_create, which uploads them once into the stacked device layout.
+
+Model-level helpers (the MoE part of what the reference's model loader
+reads):
+  * moe_config_from_tensors -- deduce_config (src/loader.rs:77-184): experts
+    and hidden size from a router weight's shape, the expert width from a
+    per-expert gate_proj's packed shape, top_k 6, layers = last index + 1;
+  * moe_config_from_json -- parse_config_json (:186-201) with its defaults;
+  * read_norm / load_block / load_block_chain -- the decoder layer's
+    post_attention_layernorm (src/model.rs:366-367: eps 1e-6, weight and bias
+    from layers.{l}.post_attention_layernorm, ones and zeros when the file has
+    none, which is what the reference's VarBuilder creates) set on each
+    layer, and the layers chained as forward_next's loop (src/model.rs:481-489).
 """
 from __future__ import annotations
 
 import dataclasses
-from typing import List, NamedTuple, Optional, Tuple
+import json
+from typing import List, NamedTuple, Optional, Sequence, Tuple
 
 import torch
 from safetensors import safe_open
 
-from .layer import Context, MoEConfig, QMoELayer
+from .layer import BlockChain, Context, MoEConfig, QMoELayer
 
 _PROJS = ("gate_proj", "up_proj", "down_proj")
 
@@ -119,3 +134,111 @@ def load_moe_layer(path: str, layer_idx: int, config: MoEConfig,
         # shared expert; the layer's forward is that FFN alone
         return QMoELayer(t.config, None, [], shared=t.shared, ctx=ctx)
     return QMoELayer(t.config, t.gate_weight, t.experts, shared=t.shared, ctx=ctx)
+
+
+# ---------------------------------------------------------------------------
+# model-level: configuration, post-attention LayerNorm, block chains
+# ---------------------------------------------------------------------------
+
+def layer_count(path: str) -> int:
+    """Layers of a file: the largest `layers.{l}.` index + 1 (src/loader.rs:95-106)."""
+    last = -1
+    with safe_open(path, framework="pt", device="cpu") as f:
+        for name in f.keys():
+            if name.startswith("layers."):
+                idx = name.split(".")[1]
+                if idx.isdigit():
+                    last = max(last, int(idx))
+    return last + 1
+
+
+def moe_config_from_tensors(path: str) -> MoEConfig:
+    """The MoE configuration deduce_config (src/loader.rs:77-184) reads from
+    tensor shapes: num_experts and hidden_dim from a `moe.gate.weight`, then
+    intermediate_dim and hidden_dim (4 x the packed bytes per row) from a
+    per-expert `gate_proj.weight`; top_k is 6.  Where the reference takes the
+    first matching name of the file's unordered key list, the per-expert
+    projections of the lowest layer are used (a flattened layer's
+    `moe.gate_proj.weight` is not an expert's)."""
+    E = H = I = None
+    with safe_open(path, framework="pt", device="cpu") as f:
+        names = sorted(f.keys())
+        for n in names:
+            if n.endswith("moe.gate.weight"):
+                shp = f.get_slice(n).get_shape()
+                if len(shp) == 2:
+                    E, H = int(shp[0]), int(shp[1])
+                    break
+        experts = [n for n in names if ".moe.experts." in n and n.endswith(".gate_proj.weight")]
+        if experts:
+            shp = f.get_slice(experts[0]).get_shape()
+            if len(shp) == 2:
+                I, H = int(shp[0]), 4 * int(shp[1])
+    if E is None or H is None or I is None:
+        raise KeyError("the file has no router weight or no per-expert gate_proj to deduce the "
+                       "MoE configuration from")
+    return MoEConfig(E, 6, H, I)
+
+
+def moe_config_from_json(path: str) -> Tuple[MoEConfig, int]:
+    """(MoE configuration, layers) from a config.json as parse_config_json
+    (src/loader.rs:186-201) reads it, with its defaults: hidden_size 2048,
+    num_layers | num_hidden_layers 27, num_experts | num_local_experts 64,
+    top_k | num_experts_per_tok 6, intermediate_dim | intermediate_size 1408,
+    hidden_dim = hidden_size."""
+    with open(path) as fh:
+        c = json.load(fh)
+
+    def first(*keys, default):
+        for k in keys:
+            if c.get(k) is not None:
+                return c[k]
+        return default
+
+    hidden = int(first("hidden_size", default=2048))
+    cfg = MoEConfig(int(first("num_experts", "num_local_experts", default=64)),
+                    int(first("top_k", "num_experts_per_tok", default=6)),
+                    int(first("hidden_dim", default=hidden)),
+                    int(first("intermediate_dim", "intermediate_size", default=1408)))
+    return cfg, int(first("num_layers", "num_hidden_layers", default=27))
+
+
+def read_norm(path: str, layer_idx: int, hidden: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(weight, bias) [hidden] f32 of layer `layer_idx`'s post_attention_layernorm;
+    ones and zeros when the file has none (the values the reference's
+    VarBuilder gives a LayerNorm missing from the file)."""
+    pre = f"layers.{layer_idx}.post_attention_layernorm"
+    with safe_open(path, framework="pt", device="cpu") as f:
+        names = set(f.keys())
+        w = (f.get_tensor(pre + ".weight").to(torch.float32).reshape(-1) if pre + ".weight" in names
+             else torch.ones(hidden, dtype=torch.float32))
+        b = (f.get_tensor(pre + ".bias").to(torch.float32).reshape(-1) if pre + ".bias" in names
+             else torch.zeros(hidden, dtype=torch.float32))
+    for t, k in ((w, "weight"), (b, "bias")):
+        if t.numel() != hidden:
+            raise ValueError(f"{pre}.{k}: {t.numel()} values for hidden size {hidden}")
+    return w.contiguous(), b.contiguous()
+
+
+NORM_EPS = 1e-6        # candle_nn::layer_norm(hidden, 1e-6, ...) (src/model.rs:367)
+
+
+def load_block(path: str, layer_idx: int, config: MoEConfig,
+               ctx: Optional[Context] = None) -> QMoELayer:
+    """Layer `layer_idx`'s MoE block: the MoE layer with its post-attention
+    LayerNorm set, ready for forward_block (src/model.rs:400-412)."""
+    layer = load_moe_layer(path, layer_idx, config, ctx=ctx)
+    w, b = read_norm(path, layer_idx, config.hidden_dim)
+    layer.set_norm(w, b, NORM_EPS)
+    return layer
+
+
+def load_block_chain(path: str, config: MoEConfig, layers: Optional[Sequence[int]] = None,
+                     ctx: Optional[Context] = None) -> BlockChain:
+    """The MoE blocks of `layers` (default: every layer of the file, in
+    order) chained as forward_next's layer loop (src/model.rs:481-489);
+    flattened layers take part as their FFN."""
+    idx = list(layers) if layers is not None else list(range(layer_count(path)))
+    if not idx:
+        raise ValueError("no layers to chain")
+    return BlockChain([load_block(path, l, config, ctx=ctx) for l in idx])
