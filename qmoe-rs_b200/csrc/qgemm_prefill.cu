@@ -20,17 +20,16 @@
 //   A  the dequantised weights, written by the dequant warps straight into
 //      tensor memory;
 //   B  the activation rows of the group, bf16, 128-byte swizzle, one 3-D TMA
-//      box per stage: two 64-element K blocks of 128, 192 or 256 rows (the
-//      fewer boxes, the faster the activation ring refills: with one 2-D box
-//      per K block the MMA thread waited for activations ~30 % of its time);
+//      box per stage: the stage's 64-element K blocks of 128, 192 or 256 rows;
 //   D  f32 in tensor memory columns 256..511.
-// The pipeline moves in stages of two K blocks (128 K): a stage owns one
-// 64-column TMEM slot for A and one 64 KB shared-memory slot for B, and has
-// one "full" barrier (four dequant-warp arrivals + the TMA transaction
-// bytes) and one "empty" barrier (the MMA commit), so the single MMA thread
-// waits once per eight MMAs.  One producer thread can issue a TMA box only
-// every few hundred cycles (the issue and the barrier round trips), so boxes
-// are as large as the 128-byte swizzle allows and few per stage.
+// The pipeline moves in stages of KBS K blocks (Geo below: 4 K blocks in 2
+// stages for groups of up to 192 rows, 2 in 3 for up to 256): a stage owns a
+// 32 x KBS-column TMEM slot for A and a shared-memory slot for B, and has one
+// "full" barrier (four dequant-warp arrivals + the TMA transaction bytes)
+// and one "empty" barrier (the MMA commit), so the single MMA thread waits
+// once per 4 x KBS MMAs -- and each of those waits costs it ~0.5k cycles
+// (a thread with MMAs in flight sees barrier phases late), which is why the
+// stages are as large as the ring and the tensor memory allow.
 //
 // Persistent grid, one CTA per SM, twenty-three warps:
 //   warp 0      TMA producer of the packed weight stages (256 K each);
