@@ -732,7 +732,7 @@ def run_single(args, W, dev, local):
             "peak_kind": tpeak_kind, "peak_burst": burst, "frac_of_burst": gu_tf / burst,
             "traffic": read_profile_traffic("qgemm_prefill_gate_up_v3.txt", "traffic_bytes_per_launch_full_v3"),
             "traffic_note": "ncu DRAM bytes of a 32-expert, 512-token V3-shaped launch, scaled by the "
-                            "items of the full launch (8896 / 1120)",
+                            "items of the full launch (8704 / 1088)",
             "algorithmic_flops": gu_f, "kernel_ms": stages["gate_up"],
             "down_tflops": dn_tf, "down_frac": dn_tf / bf16, "down_frac_of_burst": dn_tf / burst}
         line["layer"] = {"algorithmic_flops": fl, "tflops": fl / (ms / 1e3) / 1e12,

@@ -213,9 +213,8 @@ struct qmoe_layer {
     int path = QMOE_PATH_AUTO;
     CUtensorMap tm_pw[2], tm_pws[2];
     DevBuf xg, hb;
-    // activation / SwiGLU rows as 3-D views for the prefill GEMM:
-    // [K blocks per box - 2][box rows 256, 128, 192]
-    CUtensorMap tm_xgd[3][3], tm_hbd[3][3];
+    CUtensorMap tm_xg, tm_hb, tm_xg2, tm_hb2;  // 256-row and 128-row boxes
+    CUtensorMap tm_xg3, tm_hb3;                // 192-row boxes
     // tracing
     bool profiling = false;
     // Host-buffer forwards that repeat with the same page-locked x and out:
@@ -813,18 +812,18 @@ static int layer_reserve(qmoe_layer *L, int64_t T) {
         QTRY(grow(L->xg, 2 * (size_t)npos * H));
         QTRY(grow(L->hb, 2 * (size_t)npos * Imax));
         // 3-D views [K block of 128 bytes][row][K block index]: one box =
-        // 2, 3 or 4 K blocks of 256, 128 or 192 rows, i.e. one copy per GEMM
-        // stage
-        auto rows3d = [&](CUtensorMap *tm, void *base, uint64_t cols, uint32_t box_rows, uint32_t kbs) {
-            return make_tmap_u8_3d(tm, base, 128, (uint64_t)npos, cols / 64, 2 * cols, 128, 128, box_rows, kbs,
+        // two K blocks of 128, 192 or 256 rows, i.e. one copy per GEMM stage
+        auto rows3d = [&](CUtensorMap *tm, void *base, uint64_t cols, uint32_t box_rows) {
+            return make_tmap_u8_3d(tm, base, 128, (uint64_t)npos, cols / 64, 2 * cols, 128, 128, box_rows, 2,
                                    CU_TENSOR_MAP_SWIZZLE_128B);
         };
-        const uint32_t heights[3] = {kPrefillTile, kPrefillTile / 2, kPrefillTile * 3 / 4};
-        for (int d = 0; d < 3; ++d)
-            for (int h = 0; h < 3; ++h)
-                if (!rows3d(&L->tm_xgd[d][h], L->xg.p, (uint64_t)H, heights[h], (uint32_t)(d + 2)) ||
-                    !rows3d(&L->tm_hbd[d][h], L->hb.p, (uint64_t)Imax, heights[h], (uint32_t)(d + 2)))
-                    return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill rows");
+        if (!rows3d(&L->tm_xg, L->xg.p, (uint64_t)H, kPrefillTile) ||
+            !rows3d(&L->tm_xg2, L->xg.p, (uint64_t)H, kPrefillTile / 2) ||
+            !rows3d(&L->tm_xg3, L->xg.p, (uint64_t)H, kPrefillTile * 3 / 4) ||
+            !rows3d(&L->tm_hb, L->hb.p, (uint64_t)Imax, kPrefillTile) ||
+            !rows3d(&L->tm_hb2, L->hb.p, (uint64_t)Imax, kPrefillTile / 2) ||
+            !rows3d(&L->tm_hb3, L->hb.p, (uint64_t)Imax, kPrefillTile * 3 / 4))
+            return fail(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill rows");
     }
     if (!make_tmap_u8(&L->tm_xq1, L->xq1.p, (uint64_t)L->kp1, (uint64_t)(npos * 3), 128, 16,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -926,15 +925,6 @@ static int choose_prefill(qmoe_layer *L, int dtype, int64_t T, int K, bool *pref
     return QMOE_OK;
 }
 
-// Group chunk of the prefill path over T rows: 192-row groups (the GEMM's
-// 4-K-block stages) when the experts average at most 160 positions, else 256.
-// A function of (layer, T) only, so the permute (or the front) and the GEMMs
-// of one forward agree.
-static int prefill_chunk(const qmoe_layer *L, int64_t T) {
-    const int64_t e = L->e_count > 0 ? L->e_count : 1;
-    return T * L->cfg.top_k <= 160 * e ? kPrefillTileSmall : kPrefillTile;
-}
-
 // Small batches of a full layer: the router with the permute in the last
 // CTA of its selection kernel.
 static int run_front(qmoe_layer *L, const void *xd, int dtype, int64_t T, bool prefill,
@@ -943,7 +933,7 @@ static int run_front(qmoe_layer *L, const void *xd, int dtype, int64_t T, bool p
     FrontParams f{};
     f.x_copy = x_copy;
     f.counter = L->front_counter.as<int32_t>();
-    f.chunk = prefill ? prefill_chunk(L, T) : kDecodeTok;
+    f.chunk = prefill ? kPrefillTile : kDecodeTok;
     f.shared_count = L->has_shared ? T : 0;
     f.seg_off = L->seg_off.as<int32_t>();
     f.assign_pos = L->assign_pos.as<int32_t>();
@@ -1042,15 +1032,12 @@ static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, c
     m0.w1 = L->tm_pw[1];
     m0.s0 = L->tm_pws[0];
     m0.s1 = L->tm_pws[1];
-    const int rows_max = prefill_chunk(L, T);
-    const int dk = qgemm_prefill_kblocks(rows_max) - 2;
-    m0.b = L->tm_xgd[dk][0];
-    m0.b2 = L->tm_xgd[dk][1];
-    m0.b3 = L->tm_xgd[dk][2];
+    m0.b = L->tm_xg;
+    m0.b2 = L->tm_xg2;
+    m0.b3 = L->tm_xg3;
     QgemmParams g0{};
     g0.groups = L->groups.as<int4>();
     g0.n_groups = L->ngroups.as<int32_t>();
-    g0.rows_max = rows_max;
     g0.rows = c.intermediate_dim;
     g0.K = c.hidden_dim;
     g0.rows_s = with_shared ? c.shared_intermediate_dim : 0;
@@ -1070,13 +1057,12 @@ static int run_prefill(qmoe_layer *L, const void *xd, int64_t T, int64_t npos, c
     QgemmMaps m1;
     m1.w0 = m1.w1 = L->tm_w[2];
     m1.s0 = m1.s1 = L->tm_ws[2];
-    m1.b = L->tm_hbd[dk][0];
-    m1.b2 = L->tm_hbd[dk][1];
-    m1.b3 = L->tm_hbd[dk][2];
+    m1.b = L->tm_hb;
+    m1.b2 = L->tm_hb2;
+    m1.b3 = L->tm_hb3;
     QgemmParams g1{};
     g1.groups = g0.groups;
     g1.n_groups = g0.n_groups;
-    g1.rows_max = rows_max;
     g1.rows = c.hidden_dim;
     g1.K = c.intermediate_dim;
     g1.rows_s = with_shared ? c.hidden_dim : 0;
@@ -1111,7 +1097,7 @@ static int run_experts(qmoe_layer *L, const void *xd, int dtype, int64_t T, cons
     pp.topk_ld = a.topk_ld;
     pp.e_begin = a.e_begin;
     pp.e_count = L->e_count;
-    pp.chunk = prefill ? prefill_chunk(L, T) : kDecodeTok;
+    pp.chunk = prefill ? kPrefillTile : kDecodeTok;
     pp.shared_count = a.shared_count;
     pp.seg_off = L->seg_off.as<int32_t>();
     pp.assign_pos = L->assign_pos.as<int32_t>();

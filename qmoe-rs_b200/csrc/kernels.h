@@ -301,16 +301,13 @@ cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s);
 struct QgemmMaps {
     CUtensorMap w0, w1;          // routed 2-bit matrices (mode 0: gate, up; mode 1: down)
     CUtensorMap s0, s1;          // shared-expert matrices (copies of w0/w1 if none)
-    // bf16 activation rows [npos][ld], 128-byte swizzle, as 3-D views whose
-    // box is qgemm_prefill_kblocks(rows_max) K blocks deep:
-    CUtensorMap b;               // 256-row box
-    CUtensorMap b2;              // 128-row box
-    CUtensorMap b3;              // 192-row box
+    CUtensorMap b;               // bf16 activation rows [npos][ld], 128-byte swizzle, 256-row box
+    CUtensorMap b2;              // the same rows, 128-row box
+    CUtensorMap b3;              // the same rows, 192-row box
 };
 struct QgemmParams {
-    const int4 *groups;          // (segment, first position, count <= rows_max)
+    const int4 *groups;          // (segment, first position, count <= 256)
     const int32_t *n_groups;     // [0] routed groups, [1] shared groups
-    int rows_max;                // the permute's group chunk: 192 or 256
     int rows, K;                 // routed matrices: rows per expert, reduction length
     int rows_s, K_s;             // shared matrices (rows_s = 0: none)
     const float *s[2];           // routed row scales, expert stride s_stride
@@ -323,12 +320,7 @@ struct QgemmParams {
 cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmParams &p, int grid,
                                  cudaStream_t s);
 size_t qgemm_prefill_smem_bytes();
-constexpr int kPrefillTile = 256;       // tokens per work item (group chunk), at most
-constexpr int kPrefillTileSmall = 192;  // the chunk for ~128 rows per expert (one GPU)
-constexpr int kPrefillKblocksLarge = 2; // K blocks per GEMM stage for chunks above 192
-// K blocks per stage of the prefill GEMM for groups of up to rows_max rows
-// (the depth of its activation tensor maps' boxes).
-int qgemm_prefill_kblocks(int rows_max);
+constexpr int kPrefillTile = 256;  // tokens per work item (group chunk)
 
 // Host: a 2-D bf16 tensor map over rows of `cols` elements, `row_stride`
 // bytes apart.

@@ -20,16 +20,17 @@
 //   A  the dequantised weights, written by the dequant warps straight into
 //      tensor memory;
 //   B  the activation rows of the group, bf16, 128-byte swizzle, one 3-D TMA
-//      box per stage: the stage's 64-element K blocks of 128, 192 or 256 rows;
+//      box per stage: two 64-element K blocks of 128, 192 or 256 rows (the
+//      fewer boxes, the faster the activation ring refills: with one 2-D box
+//      per K block the MMA thread waited for activations ~30 % of its time);
 //   D  f32 in tensor memory columns 256..511.
-// The pipeline moves in stages of KBS K blocks (Geo below: 4 K blocks in 2
-// stages for groups of up to 192 rows, 2 in 3 for up to 256): a stage owns a
-// 32 x KBS-column TMEM slot for A and a shared-memory slot for B, and has one
-// "full" barrier (four dequant-warp arrivals + the TMA transaction bytes)
-// and one "empty" barrier (the MMA commit), so the single MMA thread waits
-// once per 4 x KBS MMAs -- and each of those waits costs it ~0.5k cycles
-// (a thread with MMAs in flight sees barrier phases late), which is why the
-// stages are as large as the ring and the tensor memory allow.
+// The pipeline moves in stages of two K blocks (128 K): a stage owns one
+// 64-column TMEM slot for A and one 64 KB shared-memory slot for B, and has
+// one "full" barrier (four dequant-warp arrivals + the TMA transaction
+// bytes) and one "empty" barrier (the MMA commit), so the single MMA thread
+// waits once per eight MMAs.  One producer thread can issue a TMA box only
+// every few hundred cycles (the issue and the barrier round trips), so boxes
+// are as large as the 128-byte swizzle allows and few per stage.
 //
 // Persistent grid, one CTA per SM, twenty-three warps:
 //   warp 0      TMA producer of the packed weight stages (256 K each);
@@ -63,35 +64,18 @@ constexpr int kEpiWarps = 16;                // four per TMEM lane quarter
 constexpr int kBWarp = 22;                   // activation producer
 constexpr int kNW = 3;                       // packed-weight stages
 constexpr int kWStage = 8192;                // 128 rows x 64 B (256 codes per row)
-constexpr int kRingBytes = 3 * 2 * kPrefillTile * 128;   // 192 KB of activation stages
-constexpr int kNSMax = 3;                    // pipeline stages, at most
+constexpr int kNS = 3;                       // pipeline stages (2 K blocks each)
+constexpr int kKbBytes = kPrefillTile * 128; // one K block of B: 256 rows x 128 B
+constexpr int kSBytes = 2 * kKbBytes;        // B bytes of a stage
+constexpr uint32_t kACols = 64;              // TMEM columns of A per stage
 constexpr uint32_t kDCol = 256;              // accumulator columns 256..511
 constexpr uint32_t kTmemCols = 512;
 constexpr int kItemCache = 256;
-
-// Stage geometry of a kernel instance: KBS K blocks (64 K each) per stage.
-// The MMA thread, with MMAs of its own in flight, observes each stage's
-// barrier ~0.5k cycles late (measured), whatever the stage's size, so the
-// fewer, larger stages the better: 4 K blocks x 2 stages for groups of up to
-// 192 rows (gate/up 7 % faster than 2 x 3 at ~128 rows per group); for up to
-// 256 rows 2 x 3 (3 x 2 measured slower there: the ring's 192 KB and the 256
-// TMEM columns beside the accumulator bound the choice).  With two stages a stage is published
-// as soon as it is stored; with three the previous stage is published after
-// this one is unpacked.
-template <int KBS>
-struct Geo {
-    static constexpr int kNS = KBS == 2 ? 3 : 2;
-    static constexpr int kRowsMax = KBS == 4 ? kPrefillTileSmall : kPrefillTile;
-    static constexpr int kSBytes = KBS * kRowsMax * 128;     // B bytes of a stage
-    static constexpr uint32_t kACols = KBS * 32;              // TMEM columns of A per stage
-    static_assert(kNS * kSBytes <= kRingBytes, "activation stages exceed the ring");
-    static_assert(kNS * kACols <= kDCol, "A slots overlap the accumulator");
-    static_assert(kNS <= kNSMax, "barrier arrays too small");
-};
+static_assert(kNS * kACols <= kDCol, "A slots overlap the accumulator");
 
 struct Smem {
     uint64_t wfull[kNW], wempty[kNW];
-    uint64_t full[kNSMax], empty[kNSMax];
+    uint64_t full[kNS], empty[kNS];
     uint64_t dfull, dempty, drain;
     uint32_t tmem_base;
     int abort;
@@ -172,7 +156,7 @@ QMOE_DEV void epilogue_chunk(const QgemmParams &p, const Item &it, int c, const 
     }
 }
 
-template <int MODE, int KBS>
+template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_s1,
@@ -181,11 +165,8 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr int kNS = Geo<KBS>::kNS;
-    constexpr int kSBytes = Geo<KBS>::kSBytes;
-    constexpr uint32_t kACols = Geo<KBS>::kACols;
-    uint8_t *bring = base;                         // kNS activation stages
-    uint8_t *wring = bring + kRingBytes;           // kNW x 8 KB packed weights
+    uint8_t *bring = base;                         // kNS x 64 KB activation stages
+    uint8_t *wring = bring + kNS * kSBytes;        // kNW x 8 KB packed weights
     Smem *S = reinterpret_cast<Smem *>(wring + kNW * kWStage);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -294,7 +275,7 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                 // second zero-filled (past the last K block) and unused
                 const CUtensorMap *mb = it.count <= 128 ? &tm_b2 : it.count <= 192 ? &tm_b3 : &tm_b;
                 const uint32_t box = (uint32_t)box_rows(it.count) * 128;
-                if (it.count > Geo<KBS>::kRowsMax) {
+                if (it.count > kPrefillTile) {
                     // a group larger than the stage slots: nothing is loaded,
                     // every role gives up at its next wait
                     atomicOr(p.err, kErrBadGroup);
@@ -302,10 +283,10 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                     ok = false;
                     break;
                 }
-                for (int kb = 0; kb < nkb; kb += KBS, ++us) {
+                for (int kb = 0; kb < nkb; kb += 2, ++us) {
                     const uint32_t s = us % kNS;
                     if (!(ok = mbar_wait(&S->empty[s], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
-                    mbar_arrive_expect_tx(&S->full[s], KBS * box);
+                    mbar_arrive_expect_tx(&S->full[s], 2 * box);
                     tma_load_3d(bring + s * kSBytes, mb, &S->full[s], 0, it.pos0, kb);
                 }
             }
@@ -330,8 +311,8 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
                 const int box = box_rows(it.count) * 128;   // bytes of one K block of B
                 if (!(ok = mbar_wait(&S->dempty, (i & 1) ^ 1, abort, p.err))) break;
                 tc_fence_after();
-                for (int kb = 0; kb < nkb; kb += KBS, ++us) {
-                    const int nk = nkb - kb < KBS ? nkb - kb : KBS;
+                for (int kb = 0; kb < nkb; kb += 2, ++us) {
+                    const int nk = nkb - kb < 2 ? nkb - kb : 2;
                     const uint32_t s = us % kNS;
                     if (!(ok = mbar_wait(&S->full[s], (us / kNS) & 1, abort, p.err))) break;
                     tc_fence_after();
@@ -366,141 +347,63 @@ qgemm_prefill_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_con
         const int r = MODE == 0 ? (L >> 1) : L;
         const int box_off = MODE == 0 ? (L & 1) * (kWStage / 2) : 0;
         const int sw = (r >> 1) & 3;                  // 64-byte swizzle of row r
-        if constexpr (KBS == 2) {
-            // two K blocks per stage, three stages (the original loop)
-            uint32_t uw = 0, us = 0;
-            int pend = -1;                                // stage stored, not yet published
-            bool ok = true;
-            for (int i = 0; ok && i < my_items; ++i) {
-                const Item it = item_at(i);
-                const int K = it.shared ? p.K_s : p.K;
-                const int nkb = K / 64;
-                for (int kb = 0; kb < nkb; kb += 2, ++us) {
-                    const int nk = nkb - kb < 2 ? nkb - kb : 2;
-                    const uint32_t ws = uw % kNW;         // kb and kb+1 share a weight stage
-                    if ((kb & 3) == 0) {
-                        if (!(ok = mbar_wait_warp(&S->wfull[ws], (uw / kNW) & 1, abort, p.err))) break;
-                    }
-                    const uint8_t *wrow = wring + ws * kWStage + box_off + r * 64;
-                    const uint4 v0 = *reinterpret_cast<const uint4 *>(wrow + 16 * ((kb & 3) ^ sw));
-                    const uint4 v1 = *reinterpret_cast<const uint4 *>(wrow + 16 * (((kb + 1) & 3) ^ sw));
-                    if ((kb & 3) == 2 || kb + nk >= nkb) {
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&S->wempty[ws]);
-                        ++uw;
-                    }
-                    const uint32_t s = us % kNS;
-                    if (!(ok = mbar_wait_warp(&S->empty[s], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
-                    tc_fence_after();
-                    // publish the previous stage (its stores had this stage's
-                    // unpacking to complete in), then store this one
-                    if (pend >= 0) {
-                        tmem_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&S->full[pend]);
-                    }
-    #pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        if (j < nk) {
-                            const uint4 v = j ? v1 : v0;
-                            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-                            uint32_t regs[32];
-    #pragma unroll
-                            for (int wi = 0; wi < 4; ++wi)
-    #pragma unroll
-                                for (int jj = 0; jj < 4; ++jj)
-    #pragma unroll
-                                    for (int pp = 0; pp < 2; ++pp)
-                                        regs[8 * wi + 2 * jj + pp] = codes_to_bf16x2(
-                                            ((w4[wi] >> (2 * jj + 8 * pp)) & 0x00030003u) | 0x43004300u);
-                            tmem_st_x32(tmem + lane_addr + s * kACols + 32 * j, regs);
-                        }
-                    }
-                    pend = (int)s;
+        uint32_t uw = 0, us = 0;
+        int pend = -1;                                // stage stored, not yet published
+        bool ok = true;
+        for (int i = 0; ok && i < my_items; ++i) {
+            const Item it = item_at(i);
+            const int K = it.shared ? p.K_s : p.K;
+            const int nkb = K / 64;
+            for (int kb = 0; kb < nkb; kb += 2, ++us) {
+                const int nk = nkb - kb < 2 ? nkb - kb : 2;
+                const uint32_t ws = uw % kNW;         // kb and kb+1 share a weight stage
+                if ((kb & 3) == 0) {
+                    if (!(ok = mbar_wait_warp(&S->wfull[ws], (uw / kNW) & 1, abort, p.err))) break;
                 }
-            }
-            tmem_wait_st();
-            if (ok && pend >= 0) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S->full[pend]);
-            }
-        } else {
-            uint32_t uw = 0, us = 0;
-            int pend = -1;                                // stage stored, not yet published
-            bool ok = true;
-            for (int i = 0; ok && i < my_items; ++i) {
-                const Item it = item_at(i);
-                const int K = it.shared ? p.K_s : p.K;
-                const int nkb = K / 64;
-                for (int kb = 0; kb < nkb; kb += KBS, ++us) {
-                    const int nk = nkb - kb < KBS ? nkb - kb : KBS;
-                    // this stage's packed codes into registers, K block by K block
-                    // (a weight stage holds 4 K blocks; it is released after its last)
-                    uint4 v[KBS];
-    #pragma unroll
-                    for (int j = 0; j < KBS; ++j) {
-                        if (j < nk) {
-                            const int kbj = kb + j;
-                            const uint32_t ws = uw % kNW;
-                            if ((kbj & 3) == 0) {
-                                if (!(ok = mbar_wait_warp(&S->wfull[ws], (uw / kNW) & 1, abort, p.err))) break;
-                            }
-                            const uint8_t *wrow = wring + ws * kWStage + box_off + r * 64;
-                            v[j] = *reinterpret_cast<const uint4 *>(wrow + 16 * ((kbj & 3) ^ sw));
-                            if ((kbj & 3) == 3 || kbj == nkb - 1) {
-                                __syncwarp();
-                                if (lane == 0) mbar_arrive(&S->wempty[ws]);
-                                ++uw;
-                            }
-                        }
-                    }
-                    if (!ok) break;
-                    const uint32_t s = us % kNS;
-                    if (!(ok = mbar_wait_warp(&S->empty[s], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
-                    tc_fence_after();
-                    // three stages: publish the previous stage (its stores had this
-                    // stage's unpacking to complete in), then store this one
-                    if (kNS >= 3 && pend >= 0) {
-                        tmem_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&S->full[pend]);
-                    }
-    #pragma unroll
-                    for (int j = 0; j < KBS; ++j) {
-                        if (j < nk) {
-                            const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-                            uint32_t regs[32];
-    #pragma unroll
-                            for (int wi = 0; wi < 4; ++wi)
-    #pragma unroll
-                                for (int jj = 0; jj < 4; ++jj)
-    #pragma unroll
-                                    for (int pp = 0; pp < 2; ++pp)
-                                        regs[8 * wi + 2 * jj + pp] = codes_to_bf16x2(
-                                            ((w4[wi] >> (2 * jj + 8 * pp)) & 0x00030003u) | 0x43004300u);
-                            tmem_st_x32(tmem + lane_addr + s * kACols + 32 * j, regs);
-                        }
-                    }
-                    if (kNS >= 3) {
-                        pend = (int)s;
-                    } else {
-                        // two stages: publish at once
-                        tmem_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&S->full[s]);
+                const uint8_t *wrow = wring + ws * kWStage + box_off + r * 64;
+                const uint4 v0 = *reinterpret_cast<const uint4 *>(wrow + 16 * ((kb & 3) ^ sw));
+                const uint4 v1 = *reinterpret_cast<const uint4 *>(wrow + 16 * (((kb + 1) & 3) ^ sw));
+                if ((kb & 3) == 2 || kb + nk >= nkb) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S->wempty[ws]);
+                    ++uw;
+                }
+                const uint32_t s = us % kNS;
+                if (!(ok = mbar_wait_warp(&S->empty[s], ((us / kNS) & 1) ^ 1, abort, p.err))) break;
+                tc_fence_after();
+                // publish the previous stage (its stores had this stage's
+                // unpacking to complete in), then store this one
+                if (pend >= 0) {
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S->full[pend]);
+                }
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    if (j < nk) {
+                        const uint4 v = j ? v1 : v0;
+                        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+                        uint32_t regs[32];
+#pragma unroll
+                        for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+                            for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+                                for (int pp = 0; pp < 2; ++pp)
+                                    regs[8 * wi + 2 * jj + pp] = codes_to_bf16x2(
+                                        ((w4[wi] >> (2 * jj + 8 * pp)) & 0x00030003u) | 0x43004300u);
+                        tmem_st_x32(tmem + lane_addr + s * kACols + 32 * j, regs);
                     }
                 }
+                pend = (int)s;
             }
-            tmem_wait_st();
-            if (ok && pend >= 0) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S->full[pend]);
-            }
+        }
+        tmem_wait_st();
+        if (ok && pend >= 0) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S->full[pend]);
         }
     } else if (warp < kEpiWarp0 + kEpiWarps) {
         // -------------------------------------------------------- epilogue
@@ -609,27 +512,19 @@ gather_bf16_kernel(const GatherParams p) {
 }  // namespace
 
 size_t qgemm_prefill_smem_bytes() {
-    return 1024 + (size_t)kRingBytes + (size_t)kNW * kWStage + sizeof(Smem);
+    return 1024 + (size_t)kNS * kSBytes + (size_t)kNW * kWStage + sizeof(Smem);
 }
-
-template <int MODE, int KBS>
-static cudaError_t launch_instance(const QgemmMaps &maps, const QgemmParams &p, int grid, cudaStream_t s) {
-    const size_t smem = qgemm_prefill_smem_bytes();
-    const cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(qgemm_prefill_kernel<MODE, KBS>), smem);
-    if (e != cudaSuccess) return e;
-    return launch_pdl(qgemm_prefill_kernel<MODE, KBS>, dim3(grid), dim3(kThreads), smem, s, maps.w0, maps.w1,
-                      maps.s0, maps.s1, maps.b, maps.b2, maps.b3, p);
-}
-
-int qgemm_prefill_kblocks(int rows_max) { return rows_max <= kPrefillTileSmall ? 4 : kPrefillKblocksLarge; }
 
 cudaError_t launch_qgemm_prefill(int mode, const QgemmMaps &maps, const QgemmParams &p, int grid,
                                  cudaStream_t s) {
-    if (p.rows_max <= 0 || p.rows_max > kPrefillTile) return cudaErrorInvalidValue;
-    const int kbs = qgemm_prefill_kblocks(p.rows_max);
-    static_assert(kPrefillKblocksLarge == 2, "the launcher instantiates 4 and 2 K blocks per stage");
-    if (mode == 0) return kbs == 4 ? launch_instance<0, 4>(maps, p, grid, s) : launch_instance<0, 2>(maps, p, grid, s);
-    return kbs == 4 ? launch_instance<1, 4>(maps, p, grid, s) : launch_instance<1, 2>(maps, p, grid, s);
+    const size_t smem = qgemm_prefill_smem_bytes();
+    cudaError_t e = mode == 0 ? ensure_dyn_smem(reinterpret_cast<const void *>(qgemm_prefill_kernel<0>), smem)
+                              : ensure_dyn_smem(reinterpret_cast<const void *>(qgemm_prefill_kernel<1>), smem);
+    if (e != cudaSuccess) return e;
+    return mode == 0 ? launch_pdl(qgemm_prefill_kernel<0>, dim3(grid), dim3(kThreads), smem, s, maps.w0,
+                                  maps.w1, maps.s0, maps.s1, maps.b, maps.b2, maps.b3, p)
+                     : launch_pdl(qgemm_prefill_kernel<1>, dim3(grid), dim3(kThreads), smem, s, maps.w0,
+                                  maps.w1, maps.s0, maps.s1, maps.b, maps.b2, maps.b3, p);
 }
 
 cudaError_t launch_gather_bf16(const GatherParams &p, cudaStream_t s) {
