@@ -23,6 +23,9 @@
 //            the work list (per-expert token masks, one thread per expert).
 // One launch replaces the logits kernel, the selection kernel and the
 // permute, and no partial sum goes through global memory.
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "select.cuh"
@@ -490,9 +493,20 @@ static int front_max_cluster(size_t smem) {
     return 0;
 }
 
+// Per device (the kernel attributes and the occupancy query are per device).
 static int front_cluster_size() {
-    static int mc = -1;
-    if (mc < 0) mc = front_max_cluster(kFrontMaxSmem);
+    static std::mutex mu;
+    static std::map<int, int> known;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = known.find(dev);
+    if (it != known.end()) return it->second;
+    const int mc = front_max_cluster(kFrontMaxSmem);
+    known[dev] = mc;
     return mc;
 }
 
